@@ -1,0 +1,164 @@
+"""Seeded synthetic inputs: random-init Qwen2-architecture weights and GEMV cases.
+
+No checkpoints or datasets exist on this machine, so every workload runs on
+weights drawn here from a fixed seed.  Each tensor gets its own numpy PCG64
+stream keyed by (seed, tensor index), so a tensor can be regenerated alone and
+the same seed gives the same bits on every machine with the same numpy.
+
+Weights follow the shapes of the dqm-mini-llama engine
+(include/dqm_llama/model.h:38-51): linears are [out_features, in_features],
+stored as ggml blocks (34-byte Q8_0 / 18-byte Q4_0, row-major, 32 values per
+block along in_features).  Linear weights and the token embedding are drawn
+N(0, 0.02); norm weights are 1 + N(0, 0.02); QKV biases N(0, 0.02).
+
+Q8_0 quantization is delegated to a caller-supplied function (the device
+quantizer in the product, the oracle on CPU) because it must match the
+reference's QuantizeToQ80 bit for bit.  Q4_0 model weights use the ggml
+convention (scale = signed absmax / -8, q = trunc(x/d + 8.5) clipped to 15),
+which is what GGUF files carry; the forward pass reads any valid Q4_0 block.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, List, Optional
+
+import numpy as np
+
+Q80, Q40 = 1, 2
+BLOCK_BYTES = {Q80: 34, Q40: 18}
+
+QWEN2_0_5B = dict(name="qwen2-0.5b", vocab=151936, dim=896, hidden=4864, n_layers=24,
+                  n_heads=14, n_kv_heads=2, rope_theta=1e6, eps=1e-6, bias=True, tied=True)
+QWEN2_7B = dict(name="qwen2-7b", vocab=152064, dim=3584, hidden=18944, n_layers=28,
+                n_heads=28, n_kv_heads=4, rope_theta=1e6, eps=1e-6, bias=True, tied=False)
+# Small Qwen2-style shape for fast parity cases (same GQA ratio, head_dim 64).
+QWEN2_MINI = dict(name="qwen2-mini", vocab=1024, dim=256, hidden=704, n_layers=2,
+                  n_heads=4, n_kv_heads=2, rope_theta=1e6, eps=1e-6, bias=True, tied=True)
+
+_FIELDS = ("attention_norm", "wq", "wk", "wv", "bq", "bk", "bv", "wo", "ffn_norm",
+           "w_gate", "w_up", "w_down")
+
+
+def rng_for(seed: int, index: int) -> np.random.Generator:
+    return np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, index])))
+
+
+def normal(seed: int, index: int, shape, std: float = 0.02) -> np.ndarray:
+    x = rng_for(seed, index).standard_normal(shape, dtype=np.float32)
+    return x * np.float32(std)
+
+
+def quantize_q40_ggml(src: np.ndarray) -> np.ndarray:
+    """ggml's Q4_0 rule, vectorised: d = m / -8 where m is the signed value of
+    largest magnitude; id = 1/d; q = min(15, trunc(x*id + 8.5)); the stored
+    scale is d rounded to fp16 (round-to-nearest-even).  Rows must be a
+    multiple of 32 long."""
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    rows, cols = src.reshape(-1, src.shape[-1]).shape
+    assert cols % 32 == 0, "ggml Q4_0 synthesis expects in_features % 32 == 0"
+    blk = src.reshape(-1, 32)
+    idx = np.abs(blk).argmax(axis=1)
+    m = blk[np.arange(blk.shape[0]), idx]
+    d = m / np.float32(-8.0)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d != 0, np.float32(1.0) / d, np.float32(0.0)).astype(np.float32)
+    q = np.trunc(blk * inv[:, None] + np.float32(8.5)).astype(np.int32)
+    q = np.minimum(q, 15).astype(np.uint8)
+    packed = (q[:, :16] | (q[:, 16:] << 4)).astype(np.uint8)
+    out = np.empty((blk.shape[0], 18), dtype=np.uint8)
+    out[:, :2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = packed
+    return out.reshape(-1)
+
+
+@dataclass
+class SynthLayer:
+    attention_norm: np.ndarray
+    wq: np.ndarray
+    wk: np.ndarray
+    wv: np.ndarray
+    bq: Optional[np.ndarray]
+    bk: Optional[np.ndarray]
+    bv: Optional[np.ndarray]
+    wo: np.ndarray
+    ffn_norm: np.ndarray
+    w_gate: np.ndarray
+    w_up: np.ndarray
+    w_down: np.ndarray
+
+
+@dataclass
+class SynthModel:
+    cfg: dict
+    qtype: int
+    token_embd: np.ndarray          # blocks [vocab, dim]
+    final_norm: np.ndarray          # f32 [dim]
+    lm_head: Optional[np.ndarray]   # blocks [vocab, dim]; None when tied
+    layers: List[SynthLayer] = field(default_factory=list)
+
+    @property
+    def head_dim(self) -> int:
+        return self.cfg["dim"] // self.cfg["n_heads"]
+
+
+def make_model(cfg: dict, qtype: int, seed: int,
+               quantize_q80: Optional[Callable[[np.ndarray], np.ndarray]] = None,
+               n_layers: Optional[int] = None) -> SynthModel:
+    """Draw a whole model.  ``quantize_q80`` maps a 2-D float32 array to its
+    Q8_0 blocks (uint8); it is required when qtype is Q8_0."""
+    cfg = dict(cfg)
+    if n_layers is not None:
+        cfg["n_layers"] = n_layers
+    if qtype == Q80:
+        if quantize_q80 is None:
+            raise ValueError("make_model: a Q8_0 quantizer is required")
+        quant = quantize_q80
+    else:
+        quant = quantize_q40_ggml
+    dim, hid = cfg["dim"], cfg["hidden"]
+    hd = dim // cfg["n_heads"]
+    qd, kvd = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    token_embd = quant(normal(seed, 0, (cfg["vocab"], dim)))
+    final_norm = np.float32(1.0) + normal(seed, 1, (dim,))
+    lm_head = None if cfg["tied"] else quant(normal(seed, 2, (cfg["vocab"], dim)))
+    layers = []
+    for li in range(cfg["n_layers"]):
+        base = 16 + 16 * li
+        shapes = {"wq": (qd, dim), "wk": (kvd, dim), "wv": (kvd, dim), "wo": (dim, qd),
+                  "w_gate": (hid, dim), "w_up": (hid, dim), "w_down": (dim, hid)}
+        vals = {}
+        for fi, name in enumerate(_FIELDS):
+            idx = base + fi
+            if name in shapes:
+                vals[name] = quant(normal(seed, idx, shapes[name]))
+            elif name in ("attention_norm", "ffn_norm"):
+                vals[name] = np.float32(1.0) + normal(seed, idx, (dim,))
+            else:  # biases
+                n = qd if name == "bq" else kvd
+                vals[name] = normal(seed, idx, (n,)) if cfg["bias"] else None
+        layers.append(SynthLayer(**vals))
+    return SynthModel(cfg=cfg, qtype=qtype, token_embd=token_embd, final_norm=final_norm,
+                      lm_head=lm_head, layers=layers)
+
+
+def prompt_tokens(vocab: int, n: int, seed: int) -> np.ndarray:
+    """n token ids drawn uniformly from [0, vocab)."""
+    return rng_for(seed, 999).integers(0, vocab, size=n, dtype=np.int64).astype(np.int32)
+
+
+def gemv_case(out_features: int, in_features: int, seed: int, qtype: int = Q80):
+    """Standalone GEMV inputs: int8 values uniform in [-127, 127] (Q4_0: nibbles
+    uniform in [0, 15]), fp16 scales uniform in [1e-4, 1e-2], x ~ N(0, 1).
+    Returns (blocks uint8, x float32)."""
+    g = rng_for(seed, 7000 + qtype)
+    nb = (in_features + 31) // 32
+    n = out_features * nb
+    d = g.uniform(1e-4, 1e-2, size=n).astype(np.float16).view(np.uint8).reshape(n, 2)
+    if qtype == Q80:
+        qs = g.integers(-127, 128, size=(n, 32), dtype=np.int16).astype(np.int8).view(np.uint8)
+        blocks = np.concatenate([d, qs], axis=1)
+    else:
+        qs = g.integers(0, 256, size=(n, 16), dtype=np.int16).astype(np.uint8)
+        blocks = np.concatenate([d, qs], axis=1)
+    x = g.standard_normal(in_features, dtype=np.float32)
+    return np.ascontiguousarray(blocks.reshape(-1)), x
