@@ -1,0 +1,396 @@
+"""Benchmark: batch-1 decode of the Qwen2-0.5B-architecture Q8_0 model on B200.
+
+Workload (one "step" = one decoded token at batch 1): the Qwen2-0.5B shape
+(24 layers, dim 896, FFN 4864, 14/2 heads, vocab 151936, tied embeddings),
+random-init N(0, 0.02) weights quantized to Q8_0, 32 random prompt ids, then
+greedy decoding at positions 32..95 (64 decode positions, cycled so a timed
+run can hold any number of steps).  Synthetic weights: no checkpoint exists
+here.  Each step streams ~525 MB of weights, more than the 126 MB L2, so no
+flush is needed between steps.
+
+Reported (one JSON line on rank 0):
+  value      decode tok/s with weights resident, tokens chosen by the device
+             argmax, the step graph replayed back to back (CUDA events);
+  e2e        the same through the C ABI entry point ForwardToken with host
+             buffers: token/pos uploaded, 151936 logits downloaded and argmaxed
+             on the host every step, as the reference engine does;
+  roofline   the dominant kernel (the Q8_0 GEMV) timed live at the lm_head
+             shape 151936 x 896 (145.25 MB per launch, two rotating copies);
+  cpu_baseline  the reference's own CPU path (compiled from its sources) on
+             this host's cores, a bounded sample of decode steps.
+With --impl reference only the reference arm runs and prints its line.
+Under torchrun every rank runs an independent replica (the 0.5B model does
+not shard); value = tokens of all ranks / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+import __graft_entry__ as ge  # noqa: E402
+
+N_PROMPT = 32
+N_DECODE_POS = 64
+MODEL_SEED = 20261201
+PROMPT_SEED = 1
+LM_HEAD_BYTES = 151936 * 28 * 34 + 896 * 4 + 151936 * 4  # blocks + x + logits
+METRIC = "decode tok/s, Qwen2-0.5B Q8_0, batch 1"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during a timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def build_model(pkg, torch, n_layers=None):
+    S = pkg.synth
+    w = S.make_model(S.QWEN2_0_5B, S.Q80, MODEL_SEED, n_layers=n_layers,
+                     quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+    torch.cuda.synchronize()
+    return w
+
+
+def time_decode(pkg, torch, ctx, first_token, steps: int, warmup: int):
+    """Device-resident greedy decode: positions cycle through 32..95."""
+    stream = torch.cuda.ExternalStream(ctx.stream_handle)
+
+    def run(n):
+        done = 0
+        while done < n:
+            chunk = min(N_DECODE_POS, n - done)
+            ctx.decode_enqueue(first_token, N_PROMPT, chunk)
+            done += chunk
+
+    run(warmup)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    run(steps)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / 1000.0
+
+
+def time_e2e(ctx, first_token, steps: int):
+    """ForwardToken through the C ABI with host buffers; host argmax picks the
+    next token, like the reference's CPU sampler after ComputeLogitsDevice."""
+    logits = np.empty(151936, np.float32)
+    tok = first_token
+    for i in range(4):  # warm-up
+        ctx.ForwardToken(tok, N_PROMPT + i, logits)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        ctx.ForwardToken(tok, N_PROMPT + (i % N_DECODE_POS), logits)
+        tok = int(np.argmax(logits))
+    return time.perf_counter() - t0
+
+
+def time_gemv(pkg, torch, w, launches: int = 40):
+    """Packed Q8_0 GEMV at the lm_head shape, two rotating weight copies
+    (290 MB > L2), CUDA events on the launching stream."""
+    blocks = torch.from_numpy(w.token_embd).cuda()
+    packs = [pkg.pack_weight(pkg.Q80, blocks, 151936, 896) for _ in range(2)]
+    x = torch.randn(896, device="cuda")
+    y = torch.empty(151936, device="cuda")
+    for i in range(6):
+        pkg.gemv_packed(pkg.Q80, x, packs[i % 2], 151936, y=y)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(launches):
+        pkg.gemv_packed(pkg.Q80, x, packs[i % 2], 151936, y=y)
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / 1000.0 / launches
+
+
+def gemv_sweep(pkg, torch, S):
+    """Config 2 shapes: GB/s per standalone launch, rotating copies > L2."""
+    out = {}
+    for o, i in ((896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896)):
+        blocks, x = S.gemv_case(o, i, 7)
+        bd = torch.from_numpy(blocks).cuda()
+        nbytes = blocks.nbytes + 4 * (i + o)
+        copies = max(2, int(300e6 // blocks.nbytes) + 1)
+        packs = [pkg.pack_weight(pkg.Q80, bd, o, i) for _ in range(copies)]
+        xd = torch.from_numpy(x).cuda()
+        y = torch.empty(o, device="cuda")
+        for p in packs[:4]:
+            pkg.gemv_packed(pkg.Q80, xd, p, o, y=y)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(copies, 20)
+        s.record()
+        for k in range(n):
+            pkg.gemv_packed(pkg.Q80, xd, packs[k % copies], o, y=y)
+        e.record()
+        e.synchronize()
+        dt = s.elapsed_time(e) / 1000.0 / n
+        out[f"{o}x{i}"] = {"us": round(dt * 1e6, 2), "GB_s": round(nbytes / dt / 1e9, 1)}
+        del packs
+    return out
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the lm_head GEMV from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "gemv_q8_0_lm_head_151936x896.md")
+    try:
+        for ln in open(path):
+            if ln.startswith("dram_bytes_per_launch:"):
+                return int(float(ln.split(":")[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+def reference_decode(w, steps: int, warmup: int, threads: int):
+    """The reference's CPU decode (oracle/_ref) on this host: returns s/token."""
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        return None, "reference library missing"
+    rm = orc.RefModel(w, N_PROMPT + N_DECODE_POS, threads=threads)
+    S = ge.load_package().synth
+    prompt = S.prompt_tokens(w.cfg["vocab"], N_PROMPT, PROMPT_SEED)
+    logits = rm.forward_batch(prompt[:1], 0)  # one prompt token is enough context
+    tok = int(np.argmax(logits))
+    for i in range(warmup):
+        logits = rm.forward_batch([tok], 1 + i)
+        tok = int(np.argmax(logits))
+    t0 = time.perf_counter()
+    for i in range(steps):
+        logits = rm.forward_batch([tok], 1 + warmup + i)
+        tok = int(np.argmax(logits))
+    dt = time.perf_counter() - t0
+    return dt / steps, "ok"
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    pkg = ge.load_package()
+    S = pkg.synth
+    orc = ge.load_oracle()
+    if not orc.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdqmref.so not built"}))
+        return
+    threads = os.cpu_count() or 1
+    w = S.make_model(S.QWEN2_0_5B, S.Q80, MODEL_SEED,
+                     quantize_q80=lambda a: orc.quantize_q80(a, use_ref=True))
+    steps = max(1, min(args.steps, 16))
+    warm = max(1, min(args.warmup, 2))
+    spt, _ = reference_decode(w, steps, warm, threads)
+    v = 1.0 / spt
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": round(spt * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic random-init weights, random prompt ids",
+        "config": {"workload": "qwen2-0.5b Q8_0 batch-1 greedy decode, reference CPU path "
+                               "(threaded scalar LinearQ80 + AVX2 F32 lm_head)",
+                   "model": "qwen2-0.5b-architecture", "seq": "1 prompt token + decode"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": f"{steps} decode steps after {warm} warm-up"},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4096)
+    ap.add_argument("--warmup", type=int, default=64)
+    ap.add_argument("--impl", default="dqmk", choices=["dqmk", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    pkg = ge.load_package()
+    S = pkg.synth
+    w = build_model(pkg, torch)
+    model = pkg.Model.from_synth(w, max_seq_len=N_PROMPT + N_DECODE_POS, device=local)
+    ctx = pkg.Context(model)
+    prompt = S.prompt_tokens(w.cfg["vocab"], N_PROMPT, PROMPT_SEED)
+    logits = ctx.ForwardBatch(prompt, 0)
+    first = int(np.argmax(logits))
+    n_layers = w.cfg["n_layers"]
+    launches_per_step = 1 + 5 * n_layers + 1
+
+    # ---- timed region: K device-resident decode steps
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        dt = time_decode(pkg, torch, ctx, first, args.steps, args.warmup)
+    clocks = clk.summary()
+    if dist:
+        t = torch.tensor([dt], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    value = world * args.steps / dt
+
+    # ---- e2e through the C ABI with host buffers
+    e2e_steps = min(args.steps, 256)
+    e2e_dt = time_e2e(ctx, first, e2e_steps)
+    if dist:
+        t = torch.tensor([e2e_dt], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_dt = float(t.item())
+    e2e = world * e2e_steps / e2e_dt
+
+    # ---- dominant-kernel roofline (lm_head-shaped Q8_0 GEMV)
+    gemv_s = time_gemv(pkg, torch, w)
+    peak, peak_kind = peaks()
+    achieved = LM_HEAD_BYTES / gemv_s / 1e9
+    bytes_per_token = (sum(getattr(L, n).nbytes for L in w.layers
+                           for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))
+                       + w.token_embd.nbytes + 896 * 4 * 2)
+    sweep = None if (args.no_sweep or rank != 0) else gemv_sweep(pkg, torch, S)
+
+    # ---- prefill (ForwardBatch) of a 602-token prompt
+    ctx.close()
+    model.close()
+    pmodel = pkg.Model.from_synth(w, max_seq_len=602)
+    pctx = pkg.Context(pmodel)
+    ptoks = S.prompt_tokens(w.cfg["vocab"], 602, 4)
+    pctx.ForwardBatch(ptoks[:8], 0)
+    pctx.reset()
+    t0 = time.perf_counter()
+    pctx.ForwardBatch(ptoks, 0)
+    prefill_tok_s = 602 / (time.perf_counter() - t0)
+    pctx.close()
+    pmodel.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        spt, status = reference_decode(w, 8, 1, threads)
+        if spt is not None:
+            cpu = {"value": round(1.0 / spt, 4), "unit": "tok/s", "cores": threads,
+                   "kind": "reference",
+                   "sample": "8 decode steps (after 1 warm-up) of the same model on the "
+                             "reference's CPU path, threaded over all host cores"}
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0xf32",
+        "data": "synthetic: random-init N(0,0.02) weights quantized to Q8_0, random prompt ids",
+        "config": {"workload": "qwen2-0.5b-architecture Q8_0, 32-token prompt then batch-1 "
+                               "greedy decode at positions 32..95 (cycled)",
+                   "model": "qwen2-0.5b", "global_batch": world, "seq_len": N_PROMPT + N_DECODE_POS,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "per-step weight stream 525 MB > 126 MB L2; no flush needed"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 151936 * 4},
+        "gpu_launches": args.steps * launches_per_step,
+        "decode_hbm": {"bytes_per_token": bytes_per_token,
+                       "GB_s": round(bytes_per_token * value / world / 1e9, 1),
+                       "frac_of_peak": round(bytes_per_token * value / world / 1e9 / peak, 4)},
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q8_0> lm_head 151936x896",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": profile_traffic(), "algorithmic_bytes": LM_HEAD_BYTES,
+                     "us_per_launch": round(gemv_s * 1e6, 2)},
+        "gemv_sweep": sweep,
+        "prefill": {"tokens": 602, "tok_s": round(prefill_tok_s, 1),
+                    "path": "ForwardBatch, per-token graph replays"},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

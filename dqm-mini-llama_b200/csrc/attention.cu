@@ -1,0 +1,280 @@
+// attention.cu -- GQA decode attention over the device-resident f32 KV cache.
+//
+// Reference math (src/forward.cc:461-506, the CPU branch the GPU must match):
+// for each query head h with KV head h / (n_heads / n_kv_heads):
+//   s_t = (q_h . K_t) / sqrt(head_dim), p = softmax(s_0..s_pos),
+//   out_h = sum_t p_t V_t.
+//
+// B200 form: grid (n_kv_heads, splits).  Each CTA takes one KV head and one
+// slice of positions, so the K/V rows of a head are read once for all of its
+// (n_heads / n_kv_heads) query heads.  It computes its slice's scores, a
+// local max m and sum l of exp(s - m), and o = sum exp(s - m) V; then bumps a
+// per-KV-head ticket.  The CTA that takes the last ticket merges the slices
+// (rescaling by exp(m_i - M)) and resets the ticket, so the whole op is one
+// launch and replays inside a CUDA graph.  Positions come from device memory
+// so a captured graph serves every decode step.
+#include "common.cuh"
+#include "internal.h"
+
+namespace dqmk {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kMaxGroup = 8;  // query heads per KV head
+constexpr int kMinChunk = 32;
+
+__device__ __forceinline__ int round_up32(int v) { return (v + 31) & ~31; }
+
+__global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, int chunk_cap) {
+  extern __shared__ float sm[];
+  __shared__ float head_m[kMaxGroup], head_l[kMaxGroup];
+  __shared__ int is_last;
+
+  pdl_trigger();
+  pdl_wait();
+
+  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int hd = a.head_dim;
+  const int G = a.n_heads / a.n_kv_heads;
+  const int pos = a.pos_dev ? *a.pos_dev : a.pos_arg;
+  const int T = pos + 1;
+  int chunk = round_up32((T + a.max_splits - 1) / a.max_splits);
+  if (chunk < kMinChunk) chunk = kMinChunk;
+  const int n_active = (T + chunk - 1) / chunk;
+  const int t0 = split * chunk;
+  const int t1 = min(T, t0 + chunk);
+  const int n = t1 - t0;
+  const size_t row_stride = (size_t)a.n_kv_heads * hd;
+  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * hd;
+  const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * hd;
+
+  float* sq = sm;                         // [G][hd]   query heads of this KV head
+  float* ss = sq + kMaxGroup * hd;        // [G][chunk_cap] scores -> exp
+  float* sacc = ss + kMaxGroup * chunk_cap;  // [groups][G][hd] PV partial sums
+
+  if (split < n_active) {
+    for (int i = threadIdx.x; i < G * hd; i += kThreads)
+      sq[i] = a.q[(size_t)(kvh * G) * hd + i];
+    __syncthreads();
+
+    // ---- scores: one thread per position, K row read once for all G heads
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
+    for (int t = threadIdx.x; t < n; t += kThreads) {
+      const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)(t0 + t) * row_stride);
+      float dot[kMaxGroup];
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h) dot[h] = 0.0f;
+      for (int i = 0; i < hd / 4; ++i) {
+        const float4 k4 = kr[i];
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) {
+          if (h < G) {
+            const float4 q4 = reinterpret_cast<const float4*>(sq + h * hd)[i];
+            float d = dot[h];
+            d = fmaf(q4.x, k4.x, d);
+            d = fmaf(q4.y, k4.y, d);
+            d = fmaf(q4.z, k4.z, d);
+            d = fmaf(q4.w, k4.w, d);
+            dot[h] = d;
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h)
+        if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
+    }
+    __syncthreads();
+
+    // ---- local softmax statistics, one warp per head
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int h = wid; h < G; h += kThreads / 32) {
+      float m = -INFINITY;
+      for (int t = lane; t < n; t += 32) m = fmaxf(m, ss[h * chunk_cap + t]);
+      m = warp_max(m);
+      float l = 0.0f;
+      for (int t = lane; t < n; t += 32) {
+        const float p = expf(ss[h * chunk_cap + t] - m);
+        ss[h * chunk_cap + t] = p;
+        l += p;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        head_m[h] = m;
+        head_l[h] = l;
+      }
+    }
+    __syncthreads();
+
+    // ---- o = sum_t p_t V_t: thread owns one d, positions split in groups
+    const int groups = kThreads / hd > 0 ? kThreads / hd : 1;
+    const int d = threadIdx.x % hd;
+    const int gi = threadIdx.x / hd;
+    if (gi < groups && threadIdx.x < groups * hd) {
+      float acc[kMaxGroup];
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
+      for (int t = gi; t < n; t += groups) {
+        const float v = vbase[(size_t)(t0 + t) * row_stride + d];
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+          if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t], v, acc[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h)
+        if (h < G) sacc[(gi * kMaxGroup + h) * hd + d] = acc[h];
+    }
+    // hd > kThreads: remaining d columns handled in a second pass
+    for (int dd = kThreads; dd < hd; dd += kThreads) {
+      const int d2 = dd + threadIdx.x;
+      if (d2 < hd) {
+        float acc[kMaxGroup];
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
+        for (int t = 0; t < n; ++t) {
+          const float v = vbase[(size_t)(t0 + t) * row_stride + d2];
+#pragma unroll
+          for (int h = 0; h < kMaxGroup; ++h)
+            if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t], v, acc[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+          if (h < G) sacc[h * hd + d2] = acc[h];
+      }
+    }
+    __syncthreads();
+
+    // ---- write this split's partial: [o_0..o_{hd-1}, m, l] per head
+    for (int i = threadIdx.x; i < G * hd; i += kThreads) {
+      const int h = i / hd, dcol = i % hd;
+      float o = 0.0f;
+      const int ng = hd <= kThreads ? groups : 1;
+      for (int g2 = 0; g2 < ng; ++g2) o += sacc[(g2 * kMaxGroup + h) * hd + dcol];
+      float* part = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * (hd + 2);
+      part[dcol] = o;
+      if (dcol == 0) {
+        part[hd] = head_m[h];
+        part[hd + 1] = head_l[h];
+      }
+    }
+  }
+
+  // ---- completion ticket; the last CTA of this KV head merges the splits
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(&a.tickets[kvh], 1u);
+    is_last = done == gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * hd; i += kThreads) {
+    const int h = i / hd, dcol = i % hd;
+    const float* part = a.partials + (size_t)(kvh * G + h) * a.max_splits * (hd + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(part + (size_t)s * (hd + 2) + hd));
+    float num = 0.0f, den = 0.0f;
+    for (int s = 0; s < n_active; ++s) {
+      const float* ps = part + (size_t)s * (hd + 2);
+      const float w = expf(__ldcg(ps + hd) - M);
+      num = fmaf(w, __ldcg(ps + dcol), num);
+      den = fmaf(w, __ldcg(ps + hd + 1), den);
+    }
+    a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(num, den);
+  }
+  if (threadIdx.x == 0) a.tickets[kvh] = 0u;
+}
+
+int chunk_cap_for(int max_seq, int max_splits) {
+  int c = (max_seq + max_splits - 1) / max_splits;
+  c = (c + 31) & ~31;
+  return c < kMinChunk ? kMinChunk : c;
+}
+
+size_t smem_bytes(int head_dim, int chunk_cap) {
+  const int groups = kThreads / head_dim > 0 ? kThreads / head_dim : 1;
+  return sizeof(float) * ((size_t)kMaxGroup * head_dim + (size_t)kMaxGroup * chunk_cap +
+                          (size_t)groups * kMaxGroup * head_dim);
+}
+
+}  // namespace
+
+int attention_splits(int max_seq, int n_kv_heads) {
+  int s = (max_seq + kMinChunk - 1) / kMinChunk;
+  int cap = (2 * sm_count()) / (n_kv_heads > 0 ? n_kv_heads : 1);
+  if (cap < 1) cap = 1;
+  if (s > cap) s = cap;
+  return s < 1 ? 1 : s;
+}
+
+size_t attention_partials_floats(int n_heads, int head_dim, int max_splits) {
+  return (size_t)n_heads * max_splits * (head_dim + 2);
+}
+
+cudaError_t attention_prepare() {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
+  const int cap = chunk_cap_for(a.max_seq, a.max_splits);
+  const size_t smem = smem_bytes(a.head_dim, cap);
+  cudaError_t e = attention_prepare();
+  if (e != cudaSuccess) return e;
+  return launch(attention_kernel, dim3(a.n_kv_heads, a.max_splits), dim3(kThreads), smem, stream,
+                pdl, a, cap);
+}
+
+}  // namespace dqmk
+
+// ------------------------------------------------------------------ C ABI
+using namespace dqmk;
+
+extern "C" int dqmk_attention_decode(const float* q, const float* keys, const float* values,
+                                     int n_layers, int max_seq, int n_kv_heads, int head_dim,
+                                     int layer, int pos, int n_heads, float* out,
+                                     void* stream) {
+  const char* api = "CudaAttentionDecode";
+  if (layer < 0 || layer >= n_layers) return fail(DQMK_ERR_RANGE, std::string(api) + ": layer out of range");
+  if (pos < 0 || pos >= max_seq) return fail(DQMK_ERR_RANGE, std::string(api) + ": pos out of range");
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || n_heads % n_kv_heads != 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid head configuration");
+  if (n_heads / n_kv_heads > 8)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": more than 8 query heads per KV head");
+  if (head_dim % 4 != 0 || head_dim > 256)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": head_dim must be a multiple of 4, <= 256");
+  if (!q || !keys || !values || !out) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": KV cache must be 16-byte aligned");
+  const int splits = attention_splits(max_seq, n_kv_heads);
+  const size_t tickets_bytes = 256;
+  const size_t part_bytes = attention_partials_floats(n_heads, head_dim, splits) * sizeof(float);
+  void* scratch = nullptr;
+  DQMK_CUDA_RET(api, device_scratch(4096 + tickets_bytes + part_bytes, &scratch));
+  AttnArgs a = {};
+  a.q = q;
+  a.keys = keys;
+  a.values = values;
+  a.max_seq = max_seq;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.layer = layer;
+  a.n_heads = n_heads;
+  a.pos_dev = nullptr;
+  a.pos_arg = pos;
+  a.out = out;
+  // scratch layout: [0,4096) argmax slot, then tickets, then partials
+  a.tickets = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + 4096);
+  a.partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + 4096 + tickets_bytes);
+  a.max_splits = splits;
+  if (n_kv_heads * sizeof(unsigned int) > tickets_bytes)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": too many KV heads");
+  DQMK_CUDA_RET(api, launch_attention(a, static_cast<cudaStream_t>(stream), false));
+  return DQMK_OK;
+}

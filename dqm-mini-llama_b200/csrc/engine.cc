@@ -1,0 +1,791 @@
+// engine.cc -- device-resident decode engine behind the dqmk C ABI (C++17).
+//
+// Mirrors the reference's CUDA branch of ForwardToken (src/forward.cc:667-754)
+// with the same inputs and outputs, restructured for the B200:
+//   * weights are repacked once at finalize into planar fused layouts:
+//     q|k|v rows concatenated and paired for RoPE, gate/up rows interleaved
+//     for the SwiGLU epilogue, the tied token_embd blocks kept quantized and
+//     reused as lm_head (the reference expands them to F32 twice,
+//     src/gguf_loader.cc:313-326,356-360);
+//   * one decode step is 1 + 5 * n_layers + 1 kernels on the context's own
+//     stream (embed; per layer QKV, attention, O, gate/up, down; lm_head),
+//     every kernel after the first launched with programmatic dependent
+//     launch, and the whole step captured once into a CUDA graph;
+//   * token and position live in device memory, so the graph replays for
+//     every step; greedy decoding advances them on the device.
+// Runtime counters follow the reference's per-logical-op accounting
+// (src/forward.cc:97-165) so the engine's counter tests still hold.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "dqmk.h"
+#include "internal.h"
+
+using namespace dqmk;
+
+namespace {
+
+struct Packed {
+  int qtype = 0;
+  int rows = 0, k = 0, kp = 0;
+  uint8_t* base = nullptr;  // owns qs plane followed by d plane
+  size_t bytes = 0;
+  const uint8_t* qs() const { return base; }
+  const uint16_t* d() const {
+    const size_t qb = (size_t)rows * (qtype == DQMK_Q80 ? kp : kp / 2);
+    return reinterpret_cast<const uint16_t*>(base + qb);
+  }
+};
+
+struct Raw {
+  int qtype = 0;
+  int rows = 0, cols = 0;
+  void* dev = nullptr;           // quantized blocks on the device
+  std::vector<float> host;       // F32 tensors (small) kept on the host
+};
+
+struct Layer {
+  Packed qkv, wo, gate_up, down;
+  float* qkv_bias = nullptr;  // packed (paired) row order
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+};
+
+}  // namespace
+
+struct dqmk_model {
+  dqmk_model_config cfg{};
+  int device = 0;
+  int qtype = 0;
+  bool finalized = false;
+  std::map<std::string, Raw> raw;
+  std::vector<Layer> layers;
+  Packed embd, lm_head;
+  bool tied = true;
+  float* final_norm = nullptr;
+  float2* rope_cs = nullptr;
+  std::vector<void*> allocs;
+  size_t memory_bytes = 0;
+  dqmk_model_stats stats{};
+
+  ~dqmk_model() {
+    cudaSetDevice(device);
+    for (void* p : allocs) cudaFree(p);
+    for (auto& kv : raw)
+      if (kv.second.dev) cudaFree(kv.second.dev);
+  }
+};
+
+struct dqmk_context {
+  dqmk_model* m = nullptr;
+  cudaStream_t stream = nullptr;
+  float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+  float *keys = nullptr, *values = nullptr, *partials = nullptr;
+  // device state block: [argmax u64][lm ticket u32][token i32][pos i32][pad]
+  //                     [attention tickets u32 x n_kv] ...
+  unsigned char* state = nullptr;
+  int* history_dev = nullptr;
+  int* pinned = nullptr;  // host staging: [token, pos]
+  cudaEvent_t staged = nullptr;  // recorded after the last copy out of `pinned`
+  int attn_splits = 1;
+  cudaGraphExec_t graph = nullptr;
+  int pos = 0;
+  std::vector<int> history;
+  std::vector<void*> allocs;
+
+  unsigned long long* argmax_slot() { return reinterpret_cast<unsigned long long*>(state); }
+  unsigned int* lm_ticket() { return reinterpret_cast<unsigned int*>(state + 8); }
+  int* token_slot() { return reinterpret_cast<int*>(state + 12); }
+  int* pos_slot() { return reinterpret_cast<int*>(state + 16); }
+  unsigned int* attn_tickets() { return reinterpret_cast<unsigned int*>(state + 64); }
+
+  ~dqmk_context() {
+    cudaSetDevice(m ? m->device : 0);
+    if (graph) cudaGraphExecDestroy(graph);
+    if (staged) cudaEventDestroy(staged);
+    if (stream) cudaStreamDestroy(stream);
+    for (void* p : allocs) cudaFree(p);
+    if (pinned) cudaFreeHost(pinned);
+  }
+};
+
+namespace dqmk {
+
+// Reference float arithmetic for the RoPE angles (src/ops.cc:18-23 and
+// :40-45): freq_i = 1 / pow(theta, (2i)/head_dim) in float, angle = pos *
+// freq_i, then float cos / sin.  Compiled by the host compiler against the
+// same libm as the reference, so the table matches it bit for bit.
+void rope_table(float theta, int head_dim, int pos_begin, int pos_count, float2* out) {
+  const int half = head_dim / 2;
+  for (int p = 0; p < pos_count; ++p) {
+    for (int i = 0; i < half; ++i) {
+      const float freq =
+          1.0f / std::pow(theta, static_cast<float>(2 * i) / static_cast<float>(head_dim));
+      const float angle = static_cast<float>(pos_begin + p) * freq;
+      out[(size_t)p * half + i] = make_float2(std::cos(angle), std::sin(angle));
+    }
+  }
+}
+
+}  // namespace dqmk
+
+namespace {
+
+int dev_alloc(std::vector<void*>& owner, size_t bytes, void** out, const char* api) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  owner.push_back(p);
+  *out = p;
+  return DQMK_OK;
+}
+
+size_t block_bytes(int qtype) { return qtype == DQMK_Q80 ? 34 : 18; }
+
+// Gather ggml rows from up to three sources (concatenated in order) through
+// a row map into one packed weight.
+int pack_rows(dqmk_model* m, const std::vector<const Raw*>& srcs, const std::vector<int>& map,
+              Packed* out, const char* api) {
+  const int qt = srcs[0]->qtype;
+  const int cols = srcs[0]->cols;
+  const int nb = (cols + 31) / 32;
+  const size_t row_b = (size_t)nb * block_bytes(qt);
+  int total = 0;
+  for (const Raw* r : srcs) total += r->rows;
+  // concatenate the sources in the map's order into one ggml buffer
+  void* tmp = nullptr;
+  cudaError_t e = cudaMalloc(&tmp, row_b * map.size());
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  std::vector<std::pair<const Raw*, int>> where(total);
+  int off = 0;
+  for (const Raw* r : srcs) {
+    for (int i = 0; i < r->rows; ++i) where[off + i] = {r, i};
+    off += r->rows;
+  }
+  // copy runs of consecutive rows with one memcpy each
+  size_t i = 0;
+  while (i < map.size()) {
+    const Raw* src = where[map[i]].first;
+    const int r0 = where[map[i]].second;
+    size_t j = i + 1;
+    while (j < map.size() && where[map[j]].first == src && where[map[j]].second == r0 + (int)(j - i))
+      ++j;
+    e = cudaMemcpy(static_cast<char*>(tmp) + i * row_b,
+                   static_cast<const char*>(src->dev) + (size_t)r0 * row_b, (j - i) * row_b,
+                   cudaMemcpyDeviceToDevice);
+    if (e != cudaSuccess) {
+      cudaFree(tmp);
+      return cuda_fail(api, e);
+    }
+    i = j;
+  }
+  out->qtype = qt;
+  out->rows = (int)map.size();
+  out->k = cols;
+  out->kp = nb * 32;
+  out->bytes = packed_bytes(qt, out->rows, cols);
+  void* p = nullptr;
+  int rc = dev_alloc(m->allocs, out->bytes, &p, api);
+  if (rc != DQMK_OK) {
+    cudaFree(tmp);
+    return rc;
+  }
+  out->base = static_cast<uint8_t*>(p);
+  e = launch_pack(qt, tmp, out->rows, cols, out->base, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(tmp);
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  m->memory_bytes += out->bytes;
+  return DQMK_OK;
+}
+
+int upload_f32(dqmk_model* m, const std::vector<float>& host, float** out, const char* api) {
+  void* p = nullptr;
+  int rc = dev_alloc(m->allocs, host.size() * sizeof(float), &p, api);
+  if (rc != DQMK_OK) return rc;
+  cudaError_t e = cudaMemcpy(p, host.data(), host.size() * sizeof(float), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  *out = static_cast<float*>(p);
+  m->memory_bytes += host.size() * sizeof(float);
+  return DQMK_OK;
+}
+
+std::vector<int> identity_map(int n) {
+  std::vector<int> v(n);
+  for (int i = 0; i < n; ++i) v[i] = i;
+  return v;
+}
+
+// Row order of the fused q|k|v weight: each RoPE pair adjacent.  NeoX pairs
+// (i, i + hd/2) of every head, Normal pairs (2i, 2i+1); V rows keep their
+// natural adjacent pairs.
+std::vector<int> qkv_map(const dqmk_model_config& c) {
+  const int hd = c.head_dim, half = hd / 2;
+  std::vector<int> map;
+  auto add_heads = [&](int base, int n_heads, bool rope) {
+    for (int h = 0; h < n_heads; ++h)
+      for (int i = 0; i < half; ++i) {
+        if (rope && c.rope_neox) {
+          map.push_back(base + h * hd + i);
+          map.push_back(base + h * hd + i + half);
+        } else {
+          map.push_back(base + h * hd + 2 * i);
+          map.push_back(base + h * hd + 2 * i + 1);
+        }
+      }
+  };
+  const int qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+  add_heads(0, c.n_heads, true);
+  add_heads(qd, c.n_kv_heads, true);
+  add_heads(qd + kvd, c.n_kv_heads, false);
+  return map;
+}
+
+int check_model(const dqmk_model* m, const char* api) {
+  if (!m) return fail(DQMK_ERR_INVALID, std::string(api) + ": null model");
+  return DQMK_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ model
+extern "C" int dqmk_model_create(const dqmk_model_config* config, int device_id,
+                                 dqmk_model** out) {
+  const char* api = "UploadModelWeightsToCuda";
+  if (!config || !out) return fail(DQMK_ERR_INVALID, std::string(api) + ": null argument");
+  const dqmk_model_config& c = *config;
+  if (c.vocab_size <= 0 || c.dim <= 0 || c.hidden_dim <= 0 || c.n_layers <= 0 ||
+      c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 || c.max_seq_len <= 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid model config");
+  if (c.n_heads % c.n_kv_heads != 0 || c.head_dim % 4 != 0 || c.head_dim > 256 ||
+      c.n_heads / c.n_kv_heads > 8)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": unsupported head configuration");
+  int n_dev = 0;
+  cudaError_t e = cudaGetDeviceCount(&n_dev);
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  if (device_id < 0 || device_id >= n_dev)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid device id");
+  auto* m = new dqmk_model();
+  m->cfg = c;
+  m->device = device_id;
+  *out = m;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_model_destroy(dqmk_model* model) {
+  delete model;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_model_upload(dqmk_model* m, const char* name, int qtype, const void* data,
+                                 size_t bytes, int rows, int cols) {
+  const char* api = "UploadModelWeightsToCuda";
+  int rc = check_model(m, api);
+  if (rc) return rc;
+  if (!name || !data) return fail(DQMK_ERR_INVALID, std::string(api) + ": null argument");
+  if (m->finalized) return fail(DQMK_ERR_INVALID, std::string(api) + ": model already finalized");
+  if (rows <= 0 || cols <= 0) return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid shape for " + name);
+  cudaSetDevice(m->device);
+  Raw r;
+  r.qtype = qtype;
+  r.rows = rows;
+  r.cols = cols;
+  if (qtype == DQMK_F32) {
+    if (bytes != (size_t)rows * cols * sizeof(float))
+      return fail(DQMK_ERR_INVALID, std::string(api) + ": size mismatch for " + name);
+    r.host.resize((size_t)rows * cols);
+    cudaError_t e = cudaMemcpy(r.host.data(), data, bytes, cudaMemcpyDefault);
+    if (e != cudaSuccess) return cuda_fail(api, e);
+  } else if (qtype == DQMK_Q80 || qtype == DQMK_Q40) {
+    const size_t expected = (size_t)rows * ((cols + 31) / 32) * block_bytes(qtype);
+    if (bytes != expected)
+      return fail(DQMK_ERR_INVALID, std::string("CUDA weight upload: block count mismatch for ") +
+                                        name + ", expected " +
+                                        std::to_string(expected / block_bytes(qtype)) + ", got " +
+                                        std::to_string(bytes / block_bytes(qtype)));
+    if (m->qtype == 0 && std::string(name) != "token_embedding") m->qtype = qtype;
+    cudaError_t e = cudaMalloc(&r.dev, bytes);
+    if (e != cudaSuccess) return cuda_fail(api, e);
+    e = cudaMemcpy(r.dev, data, bytes, cudaMemcpyDefault);
+    if (e != cudaSuccess) {
+      cudaFree(r.dev);
+      return cuda_fail(api, e);
+    }
+  } else {
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": unsupported weight type for " + name);
+  }
+  auto it = m->raw.find(name);
+  if (it != m->raw.end() && it->second.dev) cudaFree(it->second.dev);
+  m->raw[name] = std::move(r);
+  m->stats.uploaded_weight_count += 1;
+  m->stats.uploaded_bytes += bytes;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_model_finalize(dqmk_model* m) {
+  const char* api = "UploadModelWeightsToCuda";
+  int rc = check_model(m, api);
+  if (rc) return rc;
+  if (m->finalized) return DQMK_OK;
+  cudaSetDevice(m->device);
+  const dqmk_model_config& c = m->cfg;
+  const int hd = c.head_dim, qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
+  auto need = [&](const std::string& n, int qt_expect, int rows, int cols,
+                  const Raw** out) -> int {
+    auto it = m->raw.find(n);
+    if (it == m->raw.end())
+      return fail(DQMK_ERR_INVALID, "CUDA forward missing uploaded weight: " + n);
+    const Raw& r = it->second;
+    if (qt_expect >= 0 && ((qt_expect == DQMK_F32) != (r.qtype == DQMK_F32)))
+      return fail(DQMK_ERR_INVALID, "CUDA forward unsupported weight type: " + n);
+    if (r.rows * r.cols != rows * cols || (r.qtype != DQMK_F32 && (r.rows != rows || r.cols != cols)))
+      return fail(DQMK_ERR_INVALID, "CUDA forward uploaded weight shape mismatch: " + n);
+    *out = &r;
+    return DQMK_OK;
+  };
+  const Raw* emb = nullptr;
+  if ((rc = need("token_embedding", 1, c.vocab_size, c.dim, &emb))) return rc;
+  if (m->qtype == 0) m->qtype = emb->qtype;
+  const Raw* fn = nullptr;
+  if ((rc = need("final_norm", DQMK_F32, 1, c.dim, &fn))) return rc;
+  if ((rc = upload_f32(m, fn->host, &m->final_norm, api))) return rc;
+  if ((rc = pack_rows(m, {emb}, identity_map(c.vocab_size), &m->embd, api))) return rc;
+  auto lm = m->raw.find("lm_head");
+  m->tied = lm == m->raw.end();
+  if (!m->tied) {
+    const Raw* l = nullptr;
+    if ((rc = need("lm_head", 1, c.vocab_size, c.dim, &l))) return rc;
+    if ((rc = pack_rows(m, {l}, identity_map(c.vocab_size), &m->lm_head, api))) return rc;
+  } else {
+    m->lm_head = m->embd;
+  }
+  m->layers.resize(c.n_layers);
+  const std::vector<int> qmap = qkv_map(c);
+  std::vector<int> gmap(2 * c.hidden_dim);
+  for (int o = 0; o < c.hidden_dim; ++o) {
+    gmap[2 * o] = o;
+    gmap[2 * o + 1] = c.hidden_dim + o;
+  }
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    Layer& L = m->layers[l];
+    const Raw *an, *wq, *wk, *wv, *wo, *ffn, *wg, *wu, *wd;
+    if ((rc = need(p + "attention_norm", DQMK_F32, 1, c.dim, &an))) return rc;
+    if ((rc = need(p + "wq", 1, qd, c.dim, &wq))) return rc;
+    if ((rc = need(p + "wk", 1, kvd, c.dim, &wk))) return rc;
+    if ((rc = need(p + "wv", 1, kvd, c.dim, &wv))) return rc;
+    if ((rc = need(p + "wo", 1, c.dim, qd, &wo))) return rc;
+    if ((rc = need(p + "ffn_norm", DQMK_F32, 1, c.dim, &ffn))) return rc;
+    if ((rc = need(p + "w_gate", 1, c.hidden_dim, c.dim, &wg))) return rc;
+    if ((rc = need(p + "w_up", 1, c.hidden_dim, c.dim, &wu))) return rc;
+    if ((rc = need(p + "w_down", 1, c.dim, c.hidden_dim, &wd))) return rc;
+    for (const Raw* r : {wq, wk, wv, wo, wg, wu, wd})
+      if (r->qtype != m->qtype)
+        return fail(DQMK_ERR_UNSUPPORTED, "CUDA forward: mixed quant types in " + p);
+    if ((rc = upload_f32(m, an->host, &L.attn_norm, api))) return rc;
+    if ((rc = upload_f32(m, ffn->host, &L.ffn_norm, api))) return rc;
+    if ((rc = pack_rows(m, {wq, wk, wv}, qmap, &L.qkv, api))) return rc;
+    if ((rc = pack_rows(m, {wo}, identity_map(c.dim), &L.wo, api))) return rc;
+    if ((rc = pack_rows(m, {wg, wu}, gmap, &L.gate_up, api))) return rc;
+    if ((rc = pack_rows(m, {wd}, identity_map(c.dim), &L.down, api))) return rc;
+    // optional QKV bias, permuted like the rows
+    auto bq = m->raw.find(p + "bq"), bk = m->raw.find(p + "bk"), bv = m->raw.find(p + "bv");
+    const bool any = bq != m->raw.end() || bk != m->raw.end() || bv != m->raw.end();
+    if (any) {
+      std::vector<float> cat((size_t)qd + 2 * kvd, 0.0f);
+      auto put = [&](decltype(bq) it, int off, int n, const char* nm) -> int {
+        if (it == m->raw.end()) return DQMK_OK;
+        if ((int)it->second.host.size() != n)
+          return fail(DQMK_ERR_INVALID, "CUDA forward bias uploaded weight shape mismatch: " + p + nm);
+        std::memcpy(cat.data() + off, it->second.host.data(), n * sizeof(float));
+        return DQMK_OK;
+      };
+      if ((rc = put(bq, 0, qd, "bq"))) return rc;
+      if ((rc = put(bk, qd, kvd, "bk"))) return rc;
+      if ((rc = put(bv, qd + kvd, kvd, "bv"))) return rc;
+      std::vector<float> perm(qmap.size());
+      for (size_t i = 0; i < qmap.size(); ++i) perm[i] = cat[qmap[i]];
+      if ((rc = upload_f32(m, perm, &L.qkv_bias, api))) return rc;
+    }
+  }
+  // RoPE table for every cache position
+  std::vector<float2> cs((size_t)c.max_seq_len * (hd / 2));
+  rope_table(c.rope_theta, hd, 0, c.max_seq_len, cs.data());
+  void* p = nullptr;
+  if ((rc = dev_alloc(m->allocs, cs.size() * sizeof(float2), &p, api))) return rc;
+  cudaError_t e = cudaMemcpy(p, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  m->rope_cs = static_cast<float2*>(p);
+  // raw ggml copies are no longer needed
+  for (auto& kv : m->raw)
+    if (kv.second.dev) {
+      cudaFree(kv.second.dev);
+      kv.second.dev = nullptr;
+    }
+  m->finalized = true;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_model_stats_get(const dqmk_model* m, dqmk_model_stats* out) {
+  if (!m || !out) return fail(DQMK_ERR_INVALID, "ModelCudaStats: null argument");
+  *out = m->stats;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_model_stats_reset(dqmk_model* m) {
+  if (!m) return fail(DQMK_ERR_INVALID, "ResetModelCudaRuntimeStats: null model");
+  const uint64_t n = m->stats.uploaded_weight_count, b = m->stats.uploaded_bytes;
+  m->stats = dqmk_model_stats{};
+  m->stats.uploaded_weight_count = n;
+  m->stats.uploaded_bytes = b;
+  return DQMK_OK;
+}
+
+extern "C" size_t dqmk_model_memory_bytes(const dqmk_model* m) { return m ? m->memory_bytes : 0; }
+
+// ------------------------------------------------------------------ context
+namespace {
+
+int enqueue_step(dqmk_context* x) {
+  const char* api = "ForwardToken";
+  dqmk_model* m = x->m;
+  const dqmk_model_config& c = m->cfg;
+  cudaStream_t s = x->stream;
+  EmbedArgs ea = {};
+  ea.qtype = m->embd.qtype;
+  ea.qs = m->embd.qs();
+  ea.d = m->embd.d();
+  ea.vocab = c.vocab_size;
+  ea.dim = c.dim;
+  ea.kp = m->embd.kp;
+  ea.token_dev = x->token_slot();
+  ea.y = x->x;
+  ea.argmax_slot = x->argmax_slot();
+  DQMK_CUDA_RET(api, launch_embed_packed(ea, s));
+  for (int l = 0; l < c.n_layers; ++l) {
+    const Layer& L = m->layers[l];
+    GemvArgs g = {};
+    g.qtype = L.qkv.qtype;
+    g.qs = L.qkv.qs();
+    g.d = L.qkv.d();
+    g.n_rows = L.qkv.rows;
+    g.k = L.qkv.k;
+    g.kp = L.qkv.kp;
+    g.x = x->x;
+    g.norm_w = L.attn_norm;
+    g.eps = c.rms_norm_eps;
+    g.epi = kEpiQkv;
+    g.bias = L.qkv_bias;
+    g.rope_cs = m->rope_cs;
+    g.pos_dev = x->pos_slot();
+    g.q_out = x->q;
+    g.k_cache = x->keys;
+    g.v_cache = x->values;
+    g.layer = l;
+    g.max_seq = c.max_seq_len;
+    g.n_heads = c.n_heads;
+    g.n_kv_heads = c.n_kv_heads;
+    g.head_dim = c.head_dim;
+    g.neox = c.rope_neox;
+    DQMK_CUDA_RET(api, launch_gemv(g, s, true));
+
+    AttnArgs at = {};
+    at.q = x->q;
+    at.keys = x->keys;
+    at.values = x->values;
+    at.max_seq = c.max_seq_len;
+    at.n_kv_heads = c.n_kv_heads;
+    at.head_dim = c.head_dim;
+    at.layer = l;
+    at.n_heads = c.n_heads;
+    at.pos_dev = x->pos_slot();
+    at.out = x->att;
+    at.partials = x->partials;
+    at.tickets = x->attn_tickets();
+    at.max_splits = x->attn_splits;
+    DQMK_CUDA_RET(api, launch_attention(at, s, true));
+
+    GemvArgs o = {};
+    o.qtype = L.wo.qtype;
+    o.qs = L.wo.qs();
+    o.d = L.wo.d();
+    o.n_rows = L.wo.rows;
+    o.k = L.wo.k;
+    o.kp = L.wo.kp;
+    o.x = x->att;
+    o.epi = kEpiStore;
+    o.residual = x->x;
+    o.y = x->x;
+    DQMK_CUDA_RET(api, launch_gemv(o, s, true));
+
+    GemvArgs gu = {};
+    gu.qtype = L.gate_up.qtype;
+    gu.qs = L.gate_up.qs();
+    gu.d = L.gate_up.d();
+    gu.n_rows = L.gate_up.rows;
+    gu.k = L.gate_up.k;
+    gu.kp = L.gate_up.kp;
+    gu.x = x->x;
+    gu.norm_w = L.ffn_norm;
+    gu.eps = c.rms_norm_eps;
+    gu.epi = kEpiSwiGlu;
+    gu.y = x->h;
+    DQMK_CUDA_RET(api, launch_gemv(gu, s, true));
+
+    GemvArgs dn = {};
+    dn.qtype = L.down.qtype;
+    dn.qs = L.down.qs();
+    dn.d = L.down.d();
+    dn.n_rows = L.down.rows;
+    dn.k = L.down.k;
+    dn.kp = L.down.kp;
+    dn.x = x->h;
+    dn.epi = kEpiStore;
+    dn.residual = x->x;
+    dn.y = x->x;
+    DQMK_CUDA_RET(api, launch_gemv(dn, s, true));
+  }
+  GemvArgs lg = {};
+  lg.qtype = m->lm_head.qtype;
+  lg.qs = m->lm_head.qs();
+  lg.d = m->lm_head.d();
+  lg.n_rows = m->lm_head.rows;
+  lg.k = m->lm_head.k;
+  lg.kp = m->lm_head.kp;
+  lg.x = x->x;
+  lg.norm_w = m->final_norm;
+  lg.eps = c.rms_norm_eps;
+  lg.epi = kEpiLogits;
+  lg.y = x->logits;
+  lg.argmax_slot = x->argmax_slot();
+  lg.ticket = x->lm_ticket();
+  lg.token_slot = x->token_slot();
+  lg.pos_slot = x->pos_slot();
+  lg.history = x->history_dev;
+  lg.history_cap = c.max_seq_len;
+  DQMK_CUDA_RET(api, launch_gemv(lg, s, true));
+  return DQMK_OK;
+}
+
+int ensure_graph(dqmk_context* x) {
+  if (x->graph) return DQMK_OK;
+  const char* api = "ForwardToken";
+  cudaGraph_t g = nullptr;
+  DQMK_CUDA_RET(api, cudaStreamBeginCapture(x->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_step(x);
+  cudaError_t e = cudaStreamEndCapture(x->stream, &g);
+  if (rc != DQMK_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  e = cudaGraphInstantiate(&x->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  return DQMK_OK;
+}
+
+void count_token(dqmk_context* x, int pos) {
+  dqmk_model* m = x->m;
+  const dqmk_model_config& c = m->cfg;
+  const bool bias = !m->layers.empty() && m->layers[0].qkv_bias != nullptr;
+  auto& st = m->stats;
+  st.linear_calls += (uint64_t)7 * c.n_layers + 1;
+  // per layer: 2 RMSNorm, 1 RoPE, 2 residual adds, SiLU + mul (+3 bias adds)
+  st.activation_calls += (uint64_t)(bias ? 10 : 7) * c.n_layers + 1;
+  st.attention_calls += c.n_layers;
+  st.kv_cache_write_bytes += (uint64_t)c.n_layers * 2 * c.n_kv_heads * c.head_dim * sizeof(float);
+  st.kv_cache_read_bytes +=
+      (uint64_t)c.n_layers * (pos + 1) * c.n_heads * c.head_dim * sizeof(float) * 2;
+}
+
+int validate_token(const dqmk_context* x, int token, int pos) {
+  const dqmk_model_config& c = x->m->cfg;
+  if (token < 0 || token >= c.vocab_size)
+    return fail(DQMK_ERR_RANGE, "ForwardToken token id out of range");
+  if (pos < 0 || pos >= c.max_seq_len)
+    return fail(DQMK_ERR_RANGE, "ForwardToken position out of range");
+  return DQMK_OK;
+}
+
+// Upload (token, pos) into the device state.  The pinned staging slot is
+// reused, so wait until the previous copy out of it has executed.
+int stage_token(dqmk_context* x, int token, int pos, const char* api) {
+  DQMK_CUDA_RET(api, cudaEventSynchronize(x->staged));
+  x->pinned[0] = token;
+  x->pinned[1] = pos;
+  DQMK_CUDA_RET(api, cudaMemcpyAsync(x->token_slot(), x->pinned, 2 * sizeof(int),
+                                     cudaMemcpyHostToDevice, x->stream));
+  DQMK_CUDA_RET(api, cudaEventRecord(x->staged, x->stream));
+  return DQMK_OK;
+}
+
+int launch_token(dqmk_context* x, int token, int pos) {
+  const char* api = "ForwardToken";
+  int rc = stage_token(x, token, pos, api);
+  if (rc) return rc;
+  DQMK_CUDA_RET(api, cudaGraphLaunch(x->graph, x->stream));
+  count_token(x, pos);
+  return DQMK_OK;
+}
+
+}  // namespace
+
+extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
+  const char* api = "MiniLlamaContext";
+  if (!m || !out) return fail(DQMK_ERR_INVALID, std::string(api) + ": null argument");
+  if (!m->finalized) {
+    int rc = dqmk_model_finalize(m);
+    if (rc) return rc;
+  }
+  cudaSetDevice(m->device);
+  const dqmk_model_config& c = m->cfg;
+  std::unique_ptr<dqmk_context> x(new dqmk_context());
+  x->m = m;
+  DQMK_CUDA_RET(api, cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking));
+  DQMK_CUDA_RET(api, cudaMallocHost(&x->pinned, 64));
+  DQMK_CUDA_RET(api, cudaEventCreateWithFlags(&x->staged, cudaEventDisableTiming));
+  const size_t kv = (size_t)c.n_layers * c.max_seq_len * c.n_kv_heads * c.head_dim;
+  x->attn_splits = attention_splits(c.max_seq_len, c.n_kv_heads);
+  void* p = nullptr;
+  int rc;
+  const int hd = c.head_dim;
+  struct {
+    float** dst;
+    size_t n;
+  } bufs[] = {{&x->x, (size_t)c.dim},
+              {&x->q, (size_t)c.n_heads * hd},
+              {&x->att, (size_t)c.n_heads * hd},
+              {&x->h, (size_t)c.hidden_dim},
+              {&x->logits, (size_t)c.vocab_size},
+              {&x->keys, kv},
+              {&x->values, kv},
+              {&x->partials, attention_partials_floats(c.n_heads, hd, x->attn_splits)}};
+  for (auto& b : bufs) {
+    if ((rc = dev_alloc(x->allocs, b.n * sizeof(float), &p, api))) return rc;
+    *b.dst = static_cast<float*>(p);
+  }
+  if ((rc = dev_alloc(x->allocs, 64 + 4 * (size_t)c.n_kv_heads + 64, &p, api))) return rc;
+  x->state = static_cast<unsigned char*>(p);
+  if ((rc = dev_alloc(x->allocs, (size_t)c.max_seq_len * sizeof(int), &p, api))) return rc;
+  x->history_dev = static_cast<int*>(p);
+  DQMK_CUDA_RET(api, cudaMemset(x->state, 0, 64 + 4 * (size_t)c.n_kv_heads + 64));
+  DQMK_CUDA_RET(api, cudaMemset(x->keys, 0, kv * sizeof(float)));
+  DQMK_CUDA_RET(api, cudaMemset(x->values, 0, kv * sizeof(float)));
+  DQMK_CUDA_RET(api, gemv_prepare());
+  DQMK_CUDA_RET(api, attention_prepare());
+  DQMK_CUDA_RET(api, cudaDeviceSynchronize());
+  *out = x.release();
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_context_destroy(dqmk_context* x) {
+  delete x;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_context_reset(dqmk_context* x) {
+  const char* api = "MiniLlamaContext";
+  if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + ": null context");
+  const dqmk_model_config& c = x->m->cfg;
+  const size_t kv = (size_t)c.n_layers * c.max_seq_len * c.n_kv_heads * c.head_dim;
+  DQMK_CUDA_RET(api, cudaMemsetAsync(x->keys, 0, kv * sizeof(float), x->stream));
+  DQMK_CUDA_RET(api, cudaMemsetAsync(x->values, 0, kv * sizeof(float), x->stream));
+  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  x->pos = 0;
+  x->history.clear();
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_context_pos(const dqmk_context* x) { return x ? x->pos : -1; }
+
+extern "C" int dqmk_context_history(const dqmk_context* x, int* out, int cap) {
+  if (!x) return -1;
+  const int n = (int)x->history.size();
+  for (int i = 0; i < n && i < cap && out; ++i) out[i] = x->history[i];
+  return n;
+}
+
+extern "C" void* dqmk_context_stream(dqmk_context* x) { return x ? x->stream : nullptr; }
+
+extern "C" int dqmk_forward_token(dqmk_context* x, int token, int pos, float* logits) {
+  const char* api = "ForwardToken";
+  if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + " called with a null context");
+  int rc = validate_token(x, token, pos);
+  if (rc) return rc;
+  cudaSetDevice(x->m->device);
+  if ((rc = ensure_graph(x))) return rc;
+  if ((rc = launch_token(x, token, pos))) return rc;
+  if (logits) {
+    const size_t bytes = (size_t)x->m->cfg.vocab_size * sizeof(float);
+    DQMK_CUDA_RET(api, cudaMemcpyAsync(logits, x->logits, bytes, cudaMemcpyDeviceToHost, x->stream));
+    x->m->stats.device_to_host_copies += 1;
+    x->m->stats.device_to_host_bytes += bytes;
+  }
+  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int* positions, int n,
+                                  float* logits) {
+  const char* api = "ForwardBatch";
+  if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + ": null context");
+  if (n <= 0 || !tokens) return fail(DQMK_ERR_INVALID, "ForwardBatch: empty token");
+  if (!positions) return fail(DQMK_ERR_INVALID, "ForwardBatch: tokens and positions size mismatch");
+  int rc;
+  for (int i = 0; i < n; ++i)
+    if ((rc = validate_token(x, tokens[i], positions[i]))) return rc;
+  cudaSetDevice(x->m->device);
+  if ((rc = ensure_graph(x))) return rc;
+  for (int i = 0; i < n; ++i) {
+    x->pos = positions[i];
+    if ((rc = launch_token(x, tokens[i], positions[i]))) return rc;
+    x->history.push_back(tokens[i]);
+  }
+  if (logits) {
+    const size_t bytes = (size_t)x->m->cfg.vocab_size * sizeof(float);
+    DQMK_CUDA_RET(api, cudaMemcpyAsync(logits, x->logits, bytes, cudaMemcpyDeviceToHost, x->stream));
+    x->m->stats.device_to_host_copies += 1;
+    x->m->stats.device_to_host_bytes += bytes;
+  }
+  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_decode_enqueue(dqmk_context* x, int token, int pos, int n_steps) {
+  const char* api = "DecodeGreedy";
+  if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + ": null context");
+  if (n_steps <= 0) return fail(DQMK_ERR_INVALID, std::string(api) + ": n_steps must be positive");
+  int rc = validate_token(x, token, pos);
+  if (rc) return rc;
+  if (pos + n_steps > x->m->cfg.max_seq_len)
+    return fail(DQMK_ERR_RANGE, std::string(api) + ": position out of range");
+  cudaSetDevice(x->m->device);
+  if ((rc = ensure_graph(x))) return rc;
+  if ((rc = stage_token(x, token, pos, api))) return rc;
+  for (int i = 0; i < n_steps; ++i) {
+    DQMK_CUDA_RET(api, cudaGraphLaunch(x->graph, x->stream));
+    count_token(x, pos + i);
+  }
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_decode_greedy(dqmk_context* x, int token, int pos, int n_steps,
+                                  int* tokens_out) {
+  const char* api = "DecodeGreedy";
+  int rc = dqmk_decode_enqueue(x, token, pos, n_steps);
+  if (rc) return rc;
+  if (tokens_out) {
+    DQMK_CUDA_RET(api, cudaMemcpyAsync(tokens_out, x->history_dev + pos, n_steps * sizeof(int),
+                                       cudaMemcpyDeviceToHost, x->stream));
+  }
+  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  x->history.push_back(token);
+  for (int i = 0; i + 1 < n_steps && tokens_out; ++i) x->history.push_back(tokens_out[i]);
+  x->pos = pos + n_steps - 1;
+  return DQMK_OK;
+}

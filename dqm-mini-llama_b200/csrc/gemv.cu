@@ -1,0 +1,590 @@
+// gemv.cu -- batch-1 decode GEMV over Q8_0 / Q4_0 weights (sm_100a).
+//
+// The kernel behind every projection of the decode step, with the
+// memory-bound neighbours fused in:
+//   prologue  x staged once per CTA into shared memory (bank-swizzled),
+//             optionally RMS-normalised on the fly (src/ops.cc:68-90);
+//   main loop each warp owns RPW weight rows; each lane streams 16-byte
+//             chunks of them with 128-bit no-L1-allocate loads, converts
+//             bytes to floats with a PRMT "magic number" (no int->float
+//             unit), and accumulates with packed f32x2 FMAs; one fp16 scale
+//             multiply per 32-value block;
+//   epilogue  warp-shuffle reduction, then bias / residual add, SwiGLU of
+//             interleaved gate/up rows, QKV bias + RoPE + KV-cache store, or
+//             logits + device argmax.
+// Weights for the warp's first rows are loaded BEFORE griddepcontrol.wait,
+// so under programmatic dependent launch the weight stream of this kernel
+// overlaps the tail of the previous kernel in the decode chain.
+//
+// Reference semantics: LinearQuantizedImpl (src/quant.cc:278-346) computes
+// y[j] = sum_k (d*q_k) * x_k as one sequential FMA chain in k.  Here the sum
+// is split across lanes and the scale is applied per block, so results agree
+// to float rounding (checked against the oracle), not bit for bit.
+#include "common.cuh"
+#include "internal.h"
+
+namespace dqmk {
+namespace {
+
+constexpr float kMagicQ8 = -8388736.0f;  // -(2^23 + 128): biased byte -> int8 value
+constexpr float kMagicQ4 = -8388616.0f;  // -(2^23 + 8):   nibble -> value - 8
+constexpr int kWarps = 4;                // warps per CTA
+
+template <int QT>
+struct Fmt;
+template <>
+struct Fmt<DQMK_Q80> {
+  static constexpr int kElems = 16;  // values per 16-byte chunk
+  static constexpr int kSlots = 4;   // float4 slots of x per chunk
+};
+template <>
+struct Fmt<DQMK_Q40> {
+  static constexpr int kElems = 32;
+  static constexpr int kSlots = 8;
+};
+
+// Shared-memory float4 index of slot s of chunk c.  The XOR swizzle makes the
+// 8 lanes of one LDS.128 phase (consecutive chunks) hit 8 distinct 16-byte
+// bank groups.
+template <int QT>
+__device__ __forceinline__ int xslot(int c, int s) {
+  if constexpr (QT == DQMK_Q80) {
+    return c * 4 + (s ^ ((c >> 1) & 3));
+  } else {
+    return c * 8 + (s ^ (c & 7));
+  }
+}
+
+template <int QT>
+__device__ __forceinline__ int xphys(int e) {
+  constexpr int E = Fmt<QT>::kElems;
+  const int c = e / E;
+  const int s = (e % E) >> 2;
+  return xslot<QT>(c, s) * 4 + (e & 3);
+}
+
+// 16 int8 weights . 16 floats
+__device__ __forceinline__ float dot_q8(const uint4 w, const float4 (&xv)[8]) {
+  const unsigned long long M = f2_pack(kMagicQ8, kMagicQ8);
+  unsigned long long a0 = 0ull, a1 = 0ull;
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t wb = ws[i] ^ 0x80808080u;
+    const unsigned long long q01 = fadd2(f2_pack(magic_byte(wb, 0), magic_byte(wb, 1)), M);
+    const unsigned long long q23 = fadd2(f2_pack(magic_byte(wb, 2), magic_byte(wb, 3)), M);
+    a0 = ffma2(q01, f2_pack(xv[i].x, xv[i].y), a0);
+    a1 = ffma2(q23, f2_pack(xv[i].z, xv[i].w), a1);
+  }
+  const unsigned long long s = fadd2(a0, a1);
+  return f2_lo(s) + f2_hi(s);
+}
+
+// one Q4_0 block (32 nibbles) . 32 floats; word i holds values 4i..4i+3 in
+// its low nibbles and 16+4i..16+4i+3 in its high nibbles.
+__device__ __forceinline__ float dot_q4(const uint4 w, const float4 (&xv)[8]) {
+  const unsigned long long M = f2_pack(kMagicQ4, kMagicQ4);
+  unsigned long long a0 = 0ull, a1 = 0ull;
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = ws[i] & 0x0f0f0f0fu;
+    const uint32_t hi = (ws[i] >> 4) & 0x0f0f0f0fu;
+    const unsigned long long l01 = fadd2(f2_pack(magic_byte(lo, 0), magic_byte(lo, 1)), M);
+    const unsigned long long l23 = fadd2(f2_pack(magic_byte(lo, 2), magic_byte(lo, 3)), M);
+    const unsigned long long h01 = fadd2(f2_pack(magic_byte(hi, 0), magic_byte(hi, 1)), M);
+    const unsigned long long h23 = fadd2(f2_pack(magic_byte(hi, 2), magic_byte(hi, 3)), M);
+    a0 = ffma2(l01, f2_pack(xv[i].x, xv[i].y), a0);
+    a1 = ffma2(l23, f2_pack(xv[i].z, xv[i].w), a1);
+    a0 = ffma2(h01, f2_pack(xv[4 + i].x, xv[4 + i].y), a0);
+    a1 = ffma2(h23, f2_pack(xv[4 + i].z, xv[4 + i].w), a1);
+  }
+  const unsigned long long s = fadd2(a0, a1);
+  return f2_lo(s) + f2_hi(s);
+}
+
+template <int QT, int RPW, int CPL>
+struct Tile {
+  uint4 w[RPW][CPL];
+  uint16_t d[RPW][CPL];
+};
+
+struct Geo {
+  int chunks, row_bytes, nbk, seg_chunks, nseg, gw, nw;
+};
+
+template <int QT, int RPW, int CPL>
+__device__ __forceinline__ void load_step(Tile<QT, RPW, CPL>& t, const GemvArgs& a,
+                                          const Geo& g, int step, int lane) {
+  const int gi = step / g.nseg;
+  const int seg = step - gi * g.nseg;
+  const int grp = g.gw + gi * g.nw;
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const int row = grp * RPW + r;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const int c = seg * g.seg_chunks + j * 32 + lane;
+      if (row < a.n_rows && c < g.chunks) {
+        t.w[r][j] = ldg_stream(a.qs + (size_t)row * g.row_bytes + (size_t)c * 16);
+        t.d[r][j] = __ldg(a.d + (size_t)row * g.nbk + (QT == DQMK_Q80 ? (c >> 1) : c));
+      } else {
+        t.w[r][j] = make_uint4(0u, 0u, 0u, 0u);
+        t.d[r][j] = 0;
+      }
+    }
+  }
+}
+
+template <int QT, int RPW, int CPL>
+__device__ __forceinline__ void compute_step(const Tile<QT, RPW, CPL>& t, const Geo& g,
+                                             int step, int lane, const float4* xs,
+                                             float (&acc)[RPW]) {
+  const int seg = step % g.nseg;
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const int c = seg * g.seg_chunks + j * 32 + lane;
+    if (c < g.chunks) {
+      float4 xv[8];
+#pragma unroll
+      for (int s = 0; s < Fmt<QT>::kSlots; ++s) xv[s] = xs[xslot<QT>(c, s)];
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const float part = QT == DQMK_Q80 ? dot_q8(t.w[r][j], xv) : dot_q4(t.w[r][j], xv);
+        acc[r] = fmaf(h2f(t.d[r][j]), part, acc[r]);
+      }
+    }
+  }
+}
+
+// RoPE rotation of one (x0, x1) pair with the reference's rounding pattern:
+// NeoX pairs fuse the left product (src/ops.cc:46-49 as built), Normal pairs
+// round every product (src/ops.cc:24-27 as built).
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, float c, float s, int neox) {
+  const float a = x0, b = x1;
+  if (neox) {
+    x0 = __fmaf_rn(a, c, -__fmul_rn(b, s));
+    x1 = __fmaf_rn(a, s, __fmul_rn(b, c));
+  } else {
+    x0 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    x1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  }
+}
+
+template <int RPW>
+__device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
+                                         const float (&acc)[RPW], int pos,
+                                         unsigned long long& best) {
+  if (a.epi == kEpiStore) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int row = grp * RPW + r;
+      if (lane == r && row < a.n_rows) {
+        float v = acc[r];
+        if (a.bias) v = __fadd_rn(v, a.bias[row]);
+        if (a.residual) v = __fadd_rn(a.residual[row], v);
+        a.y[row] = v;
+      }
+    }
+  } else if (a.epi == kEpiLogits) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int row = grp * RPW + r;
+      if (lane == r && row < a.n_rows) {
+        a.y[row] = acc[r];
+        const unsigned long long key = argmax_key(acc[r], (uint32_t)row);
+        best = key > best ? key : best;
+      }
+    }
+  } else if (a.epi == kEpiSwiGlu) {
+    // packed rows (2p, 2p+1) = (gate_o, up_o); src/ops.cc:140-151
+#pragma unroll
+    for (int p = 0; p < RPW / 2; ++p) {
+      const int o = (grp * RPW) / 2 + p;
+      if (lane == p && 2 * o + 1 < a.n_rows) {
+        const float gt = acc[2 * p], up = acc[2 * p + 1];
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gt)));
+        a.y[o] = __fmul_rn(__fmul_rn(gt, sig), up);
+      }
+    }
+  } else {  // kEpiQkv
+    const int half = a.head_dim / 2;
+    const int q_pairs = a.n_heads * half;
+    const int kv_pairs = a.n_kv_heads * half;
+#pragma unroll
+    for (int p = 0; p < RPW / 2; ++p) {
+      const int pp = (grp * RPW) / 2 + p;  // packed pair index
+      if (lane == p && 2 * pp + 1 < a.n_rows) {
+        float x0 = acc[2 * p], x1 = acc[2 * p + 1];
+        if (a.bias) {
+          x0 = __fadd_rn(x0, a.bias[2 * pp]);
+          x1 = __fadd_rn(x1, a.bias[2 * pp + 1]);
+        }
+        int seg_pair, nh;
+        float* dst;
+        bool rotate = true;
+        if (pp < q_pairs) {
+          seg_pair = pp;
+          nh = a.n_heads;
+          dst = a.q_out;
+        } else if (pp < q_pairs + kv_pairs) {
+          seg_pair = pp - q_pairs;
+          nh = a.n_kv_heads;
+          dst = a.k_cache + ((size_t)a.layer * a.max_seq + pos) * nh * a.head_dim;
+        } else {
+          seg_pair = pp - q_pairs - kv_pairs;
+          nh = a.n_kv_heads;
+          dst = a.v_cache + ((size_t)a.layer * a.max_seq + pos) * nh * a.head_dim;
+          rotate = false;
+        }
+        const int h = seg_pair / half, i = seg_pair % half;
+        int o0, o1;
+        if (rotate && a.neox) {
+          o0 = h * a.head_dim + i;
+          o1 = o0 + half;
+        } else {
+          o0 = h * a.head_dim + 2 * i;
+          o1 = o0 + 1;
+        }
+        if (rotate) {
+          const float2 cs = a.rope_cs[(size_t)pos * half + i];
+          rope_pair(x0, x1, cs.x, cs.y, a.neox);
+        }
+        dst[o0] = x0;
+        dst[o1] = x1;
+      }
+    }
+  }
+}
+
+template <int QT, int RPW, int CPL>
+__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
+  extern __shared__ float4 xs[];
+  __shared__ float red[kWarps];
+  __shared__ float bcast;
+  __shared__ unsigned long long best_w[kWarps];
+
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  Geo g;
+  g.chunks = a.kp / Fmt<QT>::kElems;
+  g.row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
+  g.nbk = a.kp / 32;
+  g.seg_chunks = 32 * CPL;
+  g.nseg = (g.chunks + g.seg_chunks - 1) / g.seg_chunks;
+  g.gw = blockIdx.x * kWarps + wid;
+  g.nw = gridDim.x * kWarps;
+  const int n_groups = (a.n_rows + RPW - 1) / RPW;
+  const int my_groups = g.gw < n_groups ? (n_groups - g.gw + g.nw - 1) / g.nw : 0;
+  const int total = my_groups * g.nseg;
+
+  Tile<QT, RPW, CPL> ta, tb;
+  // Weights do not depend on the previous kernel: fetch before the wait.
+  if (total > 0) load_step(ta, a, g, 0, lane);
+  pdl_trigger();
+  pdl_wait();
+
+  // ---- prologue: stage x (optionally RMS-normalised) into shared memory
+  float* xsf = reinterpret_cast<float*>(xs);
+  float ss = 0.0f;
+  for (int e = threadIdx.x; e < a.kp; e += blockDim.x) {
+    const float v = e < a.k ? a.x[e] : 0.0f;
+    xsf[xphys<QT>(e)] = v;
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+  if (a.norm_w) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[wid] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+      for (int w = 0; w < kWarps; ++w) t += red[w];
+      const float mean = __fdiv_rn(t, (float)a.k);
+      bcast = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
+    }
+    __syncthreads();
+    const float scale = bcast;
+    for (int e = threadIdx.x; e < a.k; e += blockDim.x) {
+      const int p = xphys<QT>(e);
+      xsf[p] = __fmul_rn(__fmul_rn(xsf[p], scale), a.norm_w[e]);
+    }
+  }
+  __syncthreads();
+
+  int pos = 0;
+  if (a.epi == kEpiQkv) pos = a.pos_dev ? *a.pos_dev : a.pos_arg;
+  unsigned long long best = 0ull;
+  float acc[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+
+  auto finish = [&](int step) {
+    if ((step % g.nseg) != g.nseg - 1) return;
+    const int grp = g.gw + (step / g.nseg) * g.nw;
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]);
+    epilogue<RPW>(a, grp, lane, acc, pos, best);
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+  };
+
+  // two-stage register pipeline: load step s+1 while step s computes
+  for (int s = 0; s < total; s += 2) {
+    if (s + 1 < total) load_step(tb, a, g, s + 1, lane);
+    compute_step(ta, g, s, lane, xs, acc);
+    finish(s);
+    if (s + 1 < total) {
+      if (s + 2 < total) load_step(ta, a, g, s + 2, lane);
+      compute_step(tb, g, s + 1, lane, xs, acc);
+      finish(s + 1);
+    }
+  }
+
+  if (a.epi == kEpiLogits) {
+    // CTA max -> one atomic per CTA; the last CTA to finish advances the
+    // greedy decode state (token, position, history).
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) best_w[wid] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < kWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
+      if (a.argmax_slot) {
+        atomicMax(a.argmax_slot, b);
+        __threadfence();
+        const unsigned int done = atomicAdd(a.ticket, 1u);
+        if (done == gridDim.x - 1) {
+          __threadfence();
+          const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
+          const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+          const int p = *a.pos_slot;
+          if (a.history && p >= 0 && p < a.history_cap) a.history[p] = idx;
+          *a.token_slot = idx;
+          *a.pos_slot = p + 1;
+          *a.ticket = 0u;
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------ launch table
+// One-time kernel attributes and the resident-CTA cap for the grid-stride
+// case.  Run before any stream capture (context creation does).
+template <int QT, int RPW, int CPL>
+cudaError_t prepare_t(int* max_ctas_out) {
+  static int max_ctas = -1;
+  if (max_ctas < 0) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<QT, RPW, CPL>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<QT, RPW, CPL>,
+                                                      kWarps * 32, 4096 * sizeof(float));
+    if (e != cudaSuccess) return e;
+    max_ctas = (per_sm > 0 ? per_sm : 1) * sm_count();
+  }
+  if (max_ctas_out) *max_ctas_out = max_ctas;
+  return cudaSuccess;
+}
+
+template <int QT, int RPW, int CPL>
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  int max_ctas = 0;
+  cudaError_t e = prepare_t<QT, RPW, CPL>(&max_ctas);
+  if (e != cudaSuccess) return e;
+  const size_t smem = (size_t)a.kp * sizeof(float);
+  const int n_groups = (a.n_rows + RPW - 1) / RPW;
+  int grid = (n_groups + kWarps - 1) / kWarps;
+  if (grid > max_ctas) grid = max_ctas;
+  if (grid < 1) grid = 1;
+  return launch(gemv_kernel<QT, RPW, CPL>, dim3(grid), dim3(kWarps * 32), smem, stream, pdl, a);
+}
+
+// ------------------------------------------------ ggml-layout compatibility
+// One warp per weight row, blocks read in place (34 / 18 bytes, 2-byte
+// aligned), up to 8 input rows per pass.  Serves the drop-in entry points
+// that receive raw ggml blocks (CudaQ80LinearDeviceInput and friends).
+template <int QT>
+__global__ void linear_blocks_kernel(const float* __restrict__ x, int rows, int in_features,
+                                     const uint8_t* __restrict__ blocks, int out_features,
+                                     const float* __restrict__ bias, float* __restrict__ y) {
+  constexpr int BYTES = QT == DQMK_Q80 ? 34 : 18;
+  const int lane = threadIdx.x & 31;
+  const int nb = (in_features + 31) / 32;
+  const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  for (int o = warp; o < out_features; o += nwarps) {
+    for (int r0 = 0; r0 < rows; r0 += 8) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+      for (int b = lane; b < nb; b += 32) {
+        const uint8_t* p = blocks + ((size_t)o * nb + b) * BYTES;
+        const uint16_t* p16 = reinterpret_cast<const uint16_t*>(p);
+        const float d = h2f(__ldg(p16));
+        float w[32];
+#pragma unroll
+        for (int j = 0; j < (QT == DQMK_Q80 ? 16 : 8); ++j) {
+          const uint16_t v = __ldg(p16 + 1 + j);
+          if constexpr (QT == DQMK_Q80) {
+            w[2 * j] = (float)(int8_t)(v & 0xff);
+            w[2 * j + 1] = (float)(int8_t)(v >> 8);
+          } else {
+            w[2 * j] = (float)((v & 0x0f) - 8);
+            w[2 * j + 16] = (float)(((v >> 4) & 0x0f) - 8);
+            w[2 * j + 1] = (float)(((v >> 8) & 0x0f) - 8);
+            w[2 * j + 17] = (float)((v >> 12) - 8);
+          }
+        }
+        const int valid = min(32, in_features - b * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (r0 + i < rows) {
+            const float* xr = x + (size_t)(r0 + i) * in_features + b * 32;
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < valid) s = fmaf(w[j], xr[j], s);
+            acc[i] = fmaf(d, s, acc[i]);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float v = warp_sum(acc[i]);
+        if (lane == 0 && r0 + i < rows)
+          y[(size_t)(r0 + i) * out_features + o] = bias ? __fadd_rn(v, bias[o]) : v;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t gemv_prepare() {
+  cudaError_t e;
+  if ((e = prepare_t<DQMK_Q80, 2, 2>(nullptr)) != cudaSuccess) return e;
+  if ((e = prepare_t<DQMK_Q80, 4, 2>(nullptr)) != cudaSuccess) return e;
+  if ((e = prepare_t<DQMK_Q80, 2, 4>(nullptr)) != cudaSuccess) return e;
+  if ((e = prepare_t<DQMK_Q80, 4, 4>(nullptr)) != cudaSuccess) return e;
+  if ((e = prepare_t<DQMK_Q40, 2, 1>(nullptr)) != cudaSuccess) return e;
+  if ((e = prepare_t<DQMK_Q40, 4, 1>(nullptr)) != cudaSuccess) return e;
+  if ((e = prepare_t<DQMK_Q40, 2, 2>(nullptr)) != cudaSuccess) return e;
+  if ((e = prepare_t<DQMK_Q40, 2, 4>(nullptr)) != cudaSuccess) return e;
+  return prepare_t<DQMK_Q40, 4, 4>(nullptr);
+}
+
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  const bool paired = a.epi == kEpiSwiGlu || a.epi == kEpiQkv;
+  const bool wide = a.n_rows >= 32768;
+  if (a.qtype == DQMK_Q80) {
+    const int chunks = a.kp / 16;
+    if (chunks <= 64) {
+      return wide ? launch_t<DQMK_Q80, 4, 2>(a, stream, pdl)
+                  : launch_t<DQMK_Q80, 2, 2>(a, stream, pdl);
+    }
+    return (wide && !paired) ? launch_t<DQMK_Q80, 4, 4>(a, stream, pdl)
+                             : launch_t<DQMK_Q80, 2, 4>(a, stream, pdl);
+  }
+  const int chunks = a.kp / 32;
+  if (chunks <= 32) {
+    return wide ? launch_t<DQMK_Q40, 4, 1>(a, stream, pdl)
+                : launch_t<DQMK_Q40, 2, 1>(a, stream, pdl);
+  }
+  if (chunks <= 64) return launch_t<DQMK_Q40, 2, 2>(a, stream, pdl);
+  return wide ? launch_t<DQMK_Q40, 4, 4>(a, stream, pdl) : launch_t<DQMK_Q40, 2, 4>(a, stream, pdl);
+}
+
+cudaError_t launch_linear_blocks(int qtype, const float* x, int rows, int in_features,
+                                 const void* blocks, int out_features, const float* bias,
+                                 float* y, cudaStream_t stream) {
+  const int warps_per_cta = 4;
+  int grid = (out_features + warps_per_cta - 1) / warps_per_cta;
+  const int cap = sm_count() * 16;
+  if (grid > cap) grid = cap;
+  const uint8_t* b = static_cast<const uint8_t*>(blocks);
+  if (qtype == DQMK_Q80)
+    linear_blocks_kernel<DQMK_Q80><<<grid, warps_per_cta * 32, 0, stream>>>(
+        x, rows, in_features, b, out_features, bias, y);
+  else
+    linear_blocks_kernel<DQMK_Q40><<<grid, warps_per_cta * 32, 0, stream>>>(
+        x, rows, in_features, b, out_features, bias, y);
+  return cudaGetLastError();
+}
+
+}  // namespace dqmk
+
+// ------------------------------------------------------------------ C ABI
+using namespace dqmk;
+
+namespace {
+
+int linear_common(const char* api, int qtype, const float* x, int rows, int in_features,
+                  const void* blocks, size_t block_count, int out_features, const float* bias,
+                  float* y, void* stream) {
+  if (rows <= 0 || in_features <= 0 || out_features <= 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid shape");
+  const size_t expected = (size_t)out_features * (size_t)((in_features + 31) / 32);
+  if (block_count != expected)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": block count mismatch: expected " +
+                                      std::to_string(expected) + ", got " +
+                                      std::to_string(block_count));
+  if (!x || !blocks || !y) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  if (reinterpret_cast<uintptr_t>(blocks) & 1u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": blocks must be 2-byte aligned");
+  DQMK_CUDA_RET(api, launch_linear_blocks(qtype, x, rows, in_features, blocks, out_features,
+                                          bias, y, static_cast<cudaStream_t>(stream)));
+  return DQMK_OK;
+}
+
+}  // namespace
+
+extern "C" int dqmk_q80_linear(const float* x, int rows, int in_features, const void* blocks,
+                               size_t block_count, int out_features, const float* bias,
+                               float* y, void* stream) {
+  return linear_common("CudaQ80Linear", DQMK_Q80, x, rows, in_features, blocks, block_count,
+                       out_features, bias, y, stream);
+}
+
+extern "C" int dqmk_q40_linear(const float* x, int rows, int in_features, const void* blocks,
+                               size_t block_count, int out_features, const float* bias,
+                               float* y, void* stream) {
+  return linear_common("CudaQ40Linear", DQMK_Q40, x, rows, in_features, blocks, block_count,
+                       out_features, bias, y, stream);
+}
+
+extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, const void* packed,
+                                int out_features, const float* bias, const float* residual,
+                                float* y, void* stream) {
+  const char* api = qtype == DQMK_Q40 ? "CudaQ40Linear" : "CudaQ80Linear";
+  if (qtype != DQMK_Q80 && qtype != DQMK_Q40)
+    return fail(DQMK_ERR_UNSUPPORTED, "dqmk_gemv_packed: unsupported quant type");
+  if (in_features <= 0 || out_features <= 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid shape");
+  if (!x || !packed || !y) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  if (reinterpret_cast<uintptr_t>(packed) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": packed weight must be 16-byte aligned");
+  const int kp = (in_features + 31) / 32 * 32;
+  if (kp > 48 * 1024)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": in_features too large");
+  GemvArgs a = {};
+  a.qtype = qtype;
+  a.qs = static_cast<const uint8_t*>(packed);
+  const size_t qbytes = (size_t)out_features * (qtype == DQMK_Q80 ? kp : kp / 2);
+  a.d = reinterpret_cast<const uint16_t*>(a.qs + qbytes);
+  a.n_rows = out_features;
+  a.k = in_features;
+  a.kp = kp;
+  a.x = x;
+  a.epi = kEpiStore;
+  a.bias = bias;
+  a.residual = residual;
+  a.y = y;
+  DQMK_CUDA_RET(api, launch_gemv(a, static_cast<cudaStream_t>(stream), false));
+  return DQMK_OK;
+}

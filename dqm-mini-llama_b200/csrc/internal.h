@@ -1,0 +1,141 @@
+// internal.h -- launchers shared by the kernel files and the C++ engine.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+// Returns the dqmk status of a failed CUDA call from the enclosing function.
+#define DQMK_CUDA_RET(api, expr)                                \
+  do {                                                          \
+    cudaError_t _e = (expr);                                    \
+    if (_e != cudaSuccess) return ::dqmk::cuda_fail(api, _e);   \
+  } while (0)
+
+namespace dqmk {
+
+// --------------------------------------------------------------- status
+void set_error(const std::string& msg);
+int fail(int status, const std::string& msg);
+int cuda_fail(const char* api, cudaError_t err);
+const char* last_error_cstr();
+int sm_count();
+// Library-owned per-device scratch (grown on demand, zero-filled when
+// (re)allocated).  Callers that use it from several streams at once race.
+cudaError_t device_scratch(size_t bytes, void** out);
+
+// --------------------------------------------------------------- quant
+size_t packed_bytes(int qtype, int out_features, int in_features);
+cudaError_t launch_pack(int qtype, const void* blocks, int out_features, int in_features,
+                        void* packed, cudaStream_t stream);
+cudaError_t launch_quantize(int qtype, const float* src, int64_t n_rows, int64_t row_size,
+                            void* blocks, cudaStream_t stream);
+cudaError_t launch_dequantize(int qtype, const void* blocks, int64_t n_rows, int64_t row_size,
+                              float* dst, cudaStream_t stream);
+
+// --------------------------------------------------------------- GEMV
+// Epilogues of the packed GEMV.
+enum GemvEpilogue : int {
+  kEpiStore = 0,   // y[o] = residual[o] + (acc + bias[o])
+  kEpiSwiGlu = 1,  // rows interleaved (gate_o, up_o): y[o] = silu(gate) * up
+  kEpiQkv = 2,     // rows paired for RoPE: bias, rotate, write q / K / V cache
+  kEpiLogits = 3,  // y[o] = acc; device argmax + greedy advance
+};
+
+struct GemvArgs {
+  int qtype;
+  const uint8_t* qs;    // quant plane
+  const uint16_t* d;    // scale plane
+  int n_rows;           // packed rows
+  int k;                // in_features
+  int kp;               // in_features rounded up to 32
+  const float* x;       // input [k]
+  const float* norm_w;  // fused RMSNorm weight (nullptr: none)
+  float eps;
+  int epi;
+  const float* bias;      // by packed row
+  const float* residual;  // kEpiStore
+  float* y;
+  // kEpiQkv
+  const float2* rope_cs;  // [max_seq][head_dim/2] (cos, sin)
+  const int* pos_dev;     // device position (engine); nullptr -> pos_arg
+  int pos_arg;
+  float* q_out;
+  float* k_cache;
+  float* v_cache;
+  int layer, max_seq, n_heads, n_kv_heads, head_dim, neox;
+  // kEpiLogits
+  unsigned long long* argmax_slot;  // packed (value, index) max
+  unsigned int* ticket;             // CTA completion counter (reset by the last CTA)
+  int* token_slot;                  // greedy: next token
+  int* pos_slot;                    // greedy: next position (incremented)
+  int* history;                     // greedy: token written at history[pos+1]
+  int history_cap;
+};
+
+cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
+// Sets kernel attributes of every GEMV / attention instantiation; call
+// outside stream capture.
+cudaError_t gemv_prepare();
+cudaError_t attention_prepare();
+
+// ggml-layout Linear (compatibility entry point), rows >= 1.
+cudaError_t launch_linear_blocks(int qtype, const float* x, int rows, int in_features,
+                                 const void* blocks, int out_features, const float* bias,
+                                 float* y, cudaStream_t stream);
+
+// --------------------------------------------------------------- ops
+cudaError_t launch_rmsnorm(const float* x, const float* w, int dim, float eps, float* y,
+                           cudaStream_t stream);
+cudaError_t launch_silu_mul(const float* g, const float* u, int n, float* y, cudaStream_t s);
+cudaError_t launch_add(const float* a, const float* b, int n, float* y, cudaStream_t s);
+cudaError_t launch_rope(float* q, float* k, int n_heads, int n_kv_heads, int head_dim,
+                        const float2* cs, int neox, cudaStream_t s);
+cudaError_t launch_embed_f32(const float* table, int dim, int token, float* y, cudaStream_t s);
+
+// Embedding gather from packed Q8_0/Q4_0 rows.  Token from *token_dev when
+// non-null (graph replay), else `token`.  Also resets *argmax_slot.
+struct EmbedArgs {
+  int qtype;
+  const uint8_t* qs;
+  const uint16_t* d;
+  int vocab, dim, kp;
+  const int* token_dev;
+  int token;
+  float* y;
+  unsigned long long* argmax_slot;
+};
+cudaError_t launch_embed_packed(const EmbedArgs& a, cudaStream_t s);
+cudaError_t launch_embed_blocks(int qtype, const void* blocks, int dim, int token, float* y,
+                                cudaStream_t s);
+cudaError_t launch_argmax(const float* x, int n, unsigned long long* slot, int* index,
+                          cudaStream_t s);
+cudaError_t launch_kv_write(float* keys, float* values, int max_seq, int n_kv_heads,
+                            int head_dim, int layer, int pos, const float* k, const float* v,
+                            cudaStream_t s);
+
+// --------------------------------------------------------------- attention
+struct AttnArgs {
+  const float* q;        // [n_heads][hd]
+  const float* keys;     // cache base
+  const float* values;
+  int max_seq, n_kv_heads, head_dim, layer, n_heads;
+  const int* pos_dev;    // device position; nullptr -> pos_arg
+  int pos_arg;
+  float* out;            // [n_heads][hd]
+  float* partials;       // [n_heads][max_splits][hd + 2]
+  unsigned int* tickets; // [n_kv_heads], zero at rest
+  int max_splits;        // gridDim.y
+};
+// Splits (CTAs per KV head along the sequence) used for a cache of max_seq.
+int attention_splits(int max_seq, int n_kv_heads);
+size_t attention_partials_floats(int n_heads, int head_dim, int max_splits);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl);
+
+// host-side RoPE table in the reference's float arithmetic (src/ops.cc:18-23,
+// :40-45): entry [p][i] = (cos, sin) of p * 1/theta^(2i/head_dim).
+void rope_table(float theta, int head_dim, int pos_begin, int pos_count, float2* out);
+
+}  // namespace dqmk

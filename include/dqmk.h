@@ -1,0 +1,274 @@
+/*
+ * dqmk.h -- C ABI of the B200 (sm_100a) block-quantized matmul path for the
+ * dqm-mini-llama engine.
+ *
+ * Every entry point takes plain pointers and sizes, returns a dqmk_status and
+ * never throws.  On failure dqmk_last_error() returns a message that starts
+ * with the name of the reference API the entry point replaces (for example
+ * "CudaQ80Linear: block count mismatch ..."), so the engine's C++ shim can
+ * rethrow it unchanged.  DQMK_ERR_RANGE maps to std::out_of_range, every
+ * other non-zero status to std::runtime_error.
+ *
+ * Pointers named *_dev are device pointers (cudaMalloc, or any pointer the
+ * device can dereference); `stream` is a cudaStream_t passed as void*
+ * (NULL = legacy default stream).  Calls are asynchronous on `stream` unless
+ * stated otherwise.
+ *
+ * Block layouts are ggml's (include/dqm_llama/quantized_tensor.h:25-42):
+ * Q8_0 = { uint16 d (fp16); int8 qs[32] } (34 bytes), Q4_0 = { uint16 d;
+ * uint8 qs[16] } (18 bytes, element j in the low nibble of qs[j], element
+ * j+16 in the high nibble).  A [rows, cols] tensor is rows * ceil(cols/32)
+ * blocks, row-major.
+ *
+ * Citations are path:line inside the dqm-mini-llama project.
+ */
+#ifndef DQMK_H_
+#define DQMK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum dqmk_status {
+  DQMK_OK = 0,
+  DQMK_ERR_INVALID = 1,     /* bad shape / null pointer / count mismatch -> runtime_error */
+  DQMK_ERR_RANGE = 2,       /* layer, pos or token out of range -> out_of_range */
+  DQMK_ERR_CUDA = 3,        /* CUDA runtime error (message has cudaGetErrorString) */
+  DQMK_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up */
+  DQMK_ERR_UNSUPPORTED = 5, /* shape or type this build does not handle */
+  DQMK_ERR_NOMEM = 6        /* device allocation failed */
+} dqmk_status;
+
+enum { DQMK_F32 = 0, DQMK_Q80 = 1, DQMK_Q40 = 2 };
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* dqmk_last_error(void);
+
+/* 1: kernels built for sm_100a.  Replaces CudaQuantBuilt / CudaOpsBuilt /
+ * CudaAttentionBuilt / CudaKvCacheBuilt (include/dqm_llama/cuda_quant.h:15,
+ * cuda_ops.h:13, cuda_attention.h:11, cuda_kv_cache.h:12). */
+int dqmk_built(void);
+
+/* ------------------------------------------------------------------ */
+/* Block quantization (bit-exact with the reference's CPU routines)     */
+/* ------------------------------------------------------------------ */
+
+/* QuantizeToQ80 (src/quant.cc:372-418): src_dev [n_rows, row_size] f32 ->
+ * n_rows*ceil(row_size/32) Q8_0 blocks.  Scale = fp16(absmax/127) with the
+ * reference's fp16 rounding, inverse of the STORED scale, round half away
+ * from zero, clamp to +-127, tail lanes zero. */
+int dqmk_quantize_q80(const float* src_dev, int64_t n_rows, int64_t row_size,
+                      void* blocks_dev, void* stream);
+
+/* QuantizeToQ40 (src/quant.cc:420-476): scale absmax/7, q = clamp(round(x/d
+ * + 8), 0, 15). */
+int dqmk_quantize_q40(const float* src_dev, int64_t n_rows, int64_t row_size,
+                      void* blocks_dev, void* stream);
+
+/* DequantizeFromQ80 / DequantizeFromQ40 (src/quant.cc:117-190). */
+int dqmk_dequantize_q80(const void* blocks_dev, int64_t n_rows, int64_t row_size,
+                        float* dst_dev, void* stream);
+int dqmk_dequantize_q40(const void* blocks_dev, int64_t n_rows, int64_t row_size,
+                        float* dst_dev, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Quantized Linear on ggml blocks (drop-in)                            */
+/* ------------------------------------------------------------------ */
+
+/* y_dev[rows, out] = x_dev[rows, in] * W^T (+ bias_dev[out] if non-NULL),
+ * W = [out_features, in_features] as ggml blocks, block_count must equal
+ * out_features * ceil(in_features/32).  Replaces CudaQ80LinearDeviceInput
+ * (include/dqm_llama/cuda_quant.h:27-31; src/cuda_quant.cu:487) and the bias
+ * form of CudaQ80Linear / CudaQ80LinearDeviceWeight (cuda_quant.h:17-25). */
+int dqmk_q80_linear(const float* x_dev, int rows, int in_features, const void* blocks_dev,
+                    size_t block_count, int out_features, const float* bias_dev,
+                    float* y_dev, void* stream);
+
+/* Q4_0 twin: CudaQ40LinearDeviceInput / CudaQ40Linear(DeviceWeight)
+ * (include/dqm_llama/cuda_quant.h:33-47). */
+int dqmk_q40_linear(const float* x_dev, int rows, int in_features, const void* blocks_dev,
+                    size_t block_count, int out_features, const float* bias_dev,
+                    float* y_dev, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Planar ("packed") weights: the layout the engine keeps in HBM        */
+/* ------------------------------------------------------------------ */
+/* A packed [out, in] weight is the same bytes as its ggml blocks, split
+ * into two planes: quants first (Q8_0: int8 [out][kp], Q4_0: uint8
+ * [out][kp/2] with ggml's nibble order inside each 16-byte block; kp =
+ * 32*ceil(in/32), tail values zero), then scales (fp16 [out][kp/32]).
+ * Every quant row starts 16-byte aligned, so rows stream with 128-bit loads
+ * and tile cleanly for TMA.  Replaces the verbatim block upload of
+ * UploadQuantizedLinearWeight (src/model.cc:97-137). */
+size_t dqmk_packed_bytes(int qtype, int out_features, int in_features);
+int dqmk_pack_weight(int qtype, const void* blocks_dev, size_t block_count, int out_features,
+                     int in_features, void* packed_dev, void* stream);
+
+/* Batch-1 decode GEMV on a packed weight: y[o] = residual[o] + bias[o] +
+ * sum_k W[o][k] x[k] (residual_dev / bias_dev may be NULL; y_dev may equal
+ * residual_dev).  The kernel behind every projection of the decode step. */
+int dqmk_gemv_packed(int qtype, const float* x_dev, int in_features, const void* packed_dev,
+                     int out_features, const float* bias_dev, const float* residual_dev,
+                     float* y_dev, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Memory-bound ops                                                     */
+/* ------------------------------------------------------------------ */
+
+/* CudaRmsNormDeviceWeight (include/dqm_llama/cuda_ops.h:35-38; reference
+ * math src/ops.cc:68-90): y = x * (1/sqrt(mean(x^2) + eps)) * w. */
+int dqmk_rmsnorm(const float* x_dev, const float* w_dev, int dim, float eps, float* y_dev,
+                 void* stream);
+
+/* CudaSiluDeviceInput + CudaElementwiseMulDeviceInput (cuda_ops.h:39-44),
+ * reference SwiGlu (src/ops.cc:140-151): y = silu(gate) * up. */
+int dqmk_silu_mul(const float* gate_dev, const float* up_dev, int n, float* y_dev, void* stream);
+
+/* CudaElementwiseAddDeviceInput / DeviceWeight (cuda_ops.h:45-53): y = a + b. */
+int dqmk_add(const float* a_dev, const float* b_dev, int n, float* y_dev, void* stream);
+
+/* CudaRopeDeviceInput (cuda_ops.h:57-61; reference src/ops.cc:13-52,153-180):
+ * rotates q [n_heads, head_dim] and k [n_kv_heads, head_dim] in place at
+ * position pos.  neox != 0 pairs (i, i+head_dim/2), else (2i, 2i+1).  The
+ * cos/sin table is computed on the host with the reference's float
+ * expressions, so the rotation angles are the reference's bit for bit. */
+int dqmk_rope(float* q_dev, float* k_dev, int n_heads, int n_kv_heads, int head_dim, int pos,
+              float theta, int neox, void* stream);
+
+/* CudaEmbeddingLookupDeviceWeight (cuda_ops.h:28-31): y = table[token]. */
+int dqmk_embedding_lookup(const float* table_dev, int vocab, int dim, int token, float* y_dev,
+                          void* stream);
+
+/* Embedding row gathered straight from Q8_0 / Q4_0 token_embd blocks: the
+ * same values the reference's F32 table holds after DequantizeFromQ80/Q40
+ * (src/gguf_loader.cc:313-326). */
+int dqmk_embedding_lookup_blocks(int qtype, const void* blocks_dev, int vocab, int dim,
+                                 int token, float* y_dev, void* stream);
+
+/* ArgMax (src/ops.cc:182-195) on the device: first maximum wins.  The index
+ * is written to *index_dev. */
+int dqmk_argmax(const float* x_dev, int n, int* index_dev, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* KV cache and decode attention                                        */
+/* ------------------------------------------------------------------ */
+/* Cache layout is the reference's: f32 [n_layers][max_seq][n_kv_heads]
+ * [head_dim] for keys and for values (src/cuda_kv_cache.cc:63-96). */
+
+/* CudaKvCache::WriteDevice (include/dqm_llama/cuda_kv_cache.h:41-42,
+ * src/cuda_kv_cache.cc:134-164). */
+int dqmk_kv_write(float* keys_dev, float* values_dev, int n_layers, int max_seq, int n_kv_heads,
+                  int head_dim, int layer, int pos, const float* k_dev, const float* v_dev,
+                  void* stream);
+
+/* CudaAttentionDecodeDeviceInput (include/dqm_llama/cuda_attention.h:19-23,
+ * src/cuda_attention.cu:272-311; CPU math src/forward.cc:435-507): GQA
+ * decode attention of q [n_heads, head_dim] over cache positions 0..pos of
+ * `layer`, out [n_heads, head_dim].  Split over positions with an in-kernel
+ * combine; the split partials live in a per-device scratch buffer the
+ * library allocates once and reuses. */
+int dqmk_attention_decode(const float* q_dev, const float* keys_dev, const float* values_dev,
+                          int n_layers, int max_seq, int n_kv_heads, int head_dim, int layer,
+                          int pos, int n_heads, float* out_dev, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Engine: device-resident model + context (ForwardToken / ForwardBatch)*/
+/* ------------------------------------------------------------------ */
+
+typedef struct dqmk_model dqmk_model;
+typedef struct dqmk_context dqmk_context;
+
+/* ModelConfig (include/dqm_llama/model.h:23-35). */
+typedef struct dqmk_model_config {
+  int vocab_size;
+  int dim;
+  int hidden_dim;
+  int n_layers;
+  int n_heads;
+  int n_kv_heads;
+  int head_dim;
+  int max_seq_len;
+  float rope_theta;
+  float rms_norm_eps;
+  int rope_neox; /* 1 = RopeType::kNeoX (qwen2), 0 = kNormal */
+} dqmk_model_config;
+
+/* CudaModelWeights runtime counters (include/dqm_llama/model.h:64-79),
+ * counted per logical op as the reference's RecordCuda* helpers do
+ * (src/forward.cc:97-165). */
+typedef struct dqmk_model_stats {
+  uint64_t uploaded_weight_count;
+  uint64_t uploaded_bytes;
+  uint64_t linear_calls;
+  uint64_t activation_calls;
+  uint64_t attention_calls;
+  uint64_t kv_cache_write_bytes;
+  uint64_t kv_cache_read_bytes;
+  uint64_t host_to_device_copies;
+  uint64_t device_to_host_copies;
+  uint64_t host_to_device_bytes;
+  uint64_t device_to_host_bytes;
+} dqmk_model_stats;
+
+int dqmk_model_create(const dqmk_model_config* config, int device_id, dqmk_model** out);
+int dqmk_model_destroy(dqmk_model* model);
+
+/* UploadModelWeightsToCuda (include/dqm_llama/model.h:103, src/model.cc:227-260)
+ * one tensor at a time, under the reference's names: "token_embedding",
+ * "final_norm", "lm_head", "layers.<i>.{attention_norm,wq,wk,wv,bq,bk,bv,wo,
+ * ffn_norm,w_gate,w_up,w_down}".  qtype is DQMK_F32 for norms / biases and
+ * DQMK_Q80 / DQMK_Q40 for linears and the token embedding.  `data` may be a
+ * host or a device pointer; `bytes` is its size.  Without "lm_head" the
+ * token embedding blocks are reused as a tied lm_head. */
+int dqmk_model_upload(dqmk_model* model, const char* name, int qtype, const void* data,
+                      size_t bytes, int rows, int cols);
+
+/* Validates that every tensor is present and builds the fused layouts. */
+int dqmk_model_finalize(dqmk_model* model);
+int dqmk_model_stats_get(const dqmk_model* model, dqmk_model_stats* out);
+int dqmk_model_stats_reset(dqmk_model* model);
+/* ModelCudaMemoryBytes (include/dqm_llama/model.h:119). */
+size_t dqmk_model_memory_bytes(const dqmk_model* model);
+
+/* MiniLlamaContext (include/dqm_llama/context.h:14-31): KV cache, position,
+ * token history, its own CUDA stream and captured decode graph. */
+int dqmk_context_create(dqmk_model* model, dqmk_context** out);
+int dqmk_context_destroy(dqmk_context* ctx);
+/* Clears the KV cache, pos = 0, empty history. */
+int dqmk_context_reset(dqmk_context* ctx);
+int dqmk_context_pos(const dqmk_context* ctx);
+/* Copies up to `cap` history tokens into `out`; returns the history length. */
+int dqmk_context_history(const dqmk_context* ctx, int* out, int cap);
+
+/* ForwardToken (include/dqm_llama/forward.h:11-12, src/forward.cc:729-754):
+ * one token at position pos through the model; the vocab_size logits are
+ * copied to the host buffer logits (may be NULL to skip the copy).  Does
+ * not touch pos or history, like the reference.  Synchronous. */
+int dqmk_forward_token(dqmk_context* ctx, int token, int pos, float* logits);
+
+/* ForwardBatch (include/dqm_llama/forward.h:16-17, src/batch.cc:26-42):
+ * runs tokens[i] at positions[i] in order, sets ctx pos to the last position,
+ * appends every token to the history, writes the last token's logits.
+ * Synchronous. */
+int dqmk_forward_batch(dqmk_context* ctx, const int* tokens, const int* positions, int n,
+                       float* logits);
+
+/* Greedy decode on the device: feeds `token` at `pos`, then n_steps-1 more
+ * tokens chosen by the device argmax, replaying the captured decode graph
+ * with no host round trip per step.  tokens_out[i] receives the argmax after
+ * step i.  Synchronous. */
+int dqmk_decode_greedy(dqmk_context* ctx, int token, int pos, int n_steps, int* tokens_out);
+
+/* Timing hook: enqueue n_steps greedy decode steps (same as above) without
+ * synchronizing; returns the context stream for event timing. */
+int dqmk_decode_enqueue(dqmk_context* ctx, int token, int pos, int n_steps);
+void* dqmk_context_stream(dqmk_context* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DQMK_H_ */

@@ -1,0 +1,147 @@
+"""GPU parity of the whole decode path (engine + fused kernels) against the
+reference: ForwardToken logits, ForwardBatch side effects, greedy tokens, and
+the runtime counters the reference's CUDA tests assert.
+
+Logit tolerance: max |logit - ref| <= 1e-3 * (max - min
+of the reference logits).  Greedy decoding must produce identical tokens; the
+smallest top-1/top-2 margin of each run is reported alongside.
+"""
+import json
+
+import numpy as np
+import pytest
+
+from conftest import golden_path
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3  # relative to the logit range
+
+
+def check_logits(got, ref, label):
+    rng = float(ref.max() - ref.min())
+    err = float(np.abs(got - ref).max())
+    assert err <= LOGIT_TOL * rng, f"{label}: max err {err:.3e} > {LOGIT_TOL} * range {rng:.3f}"
+    return err / rng
+
+
+@pytest.fixture(scope="module")
+def mini(pkg, orc, S, cuda):
+    out = {}
+    for qt in (pkg.Q80, pkg.Q40):
+        out[qt] = S.make_model(S.QWEN2_MINI, qt, 2024,
+                               quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+    return out
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_forward_token_matches_reference_golden(pkg, mini, cuda, qt):
+    g = np.load(golden_path("mini_model.npz"))
+    w = mini[qt]
+    model = pkg.Model.from_synth(w, max_seq_len=64)
+    ctx = pkg.Context(model)
+    toks = g[f"q{qt}_tokens"]
+    worst = 0.0
+    for i, t in enumerate(toks):
+        logits = ctx.ForwardToken(int(t), i)
+        worst = max(worst, check_logits(logits, g[f"q{qt}_logits"][i], f"q{qt} step {i}"))
+    print(f"q{qt} worst relative logit error {worst:.2e}")
+
+
+def test_forward_batch_semantics(pkg, mini, cuda):
+    """tests/batch_test.cc:157-217: batched == per-token, pos / history updates."""
+    w = mini[pkg.Q80]
+    model = pkg.Model.from_synth(w, max_seq_len=64)
+    toks = [1, 104, 101, 108, 108, 111]
+    manual = pkg.Context(model)
+    for i, t in enumerate(toks):
+        manual_logits = manual.ForwardToken(t, i)
+    batched = pkg.Context(model)
+    batch_logits = batched.ForwardBatch(toks, 0)
+    assert np.array_equal(batch_logits, manual_logits)
+    assert batched.token_history == toks and batched.pos == 5
+    assert manual.token_history == [] and manual.pos == 0  # ForwardToken touches neither
+    batched.ForwardBatch([42], positions=[6])
+    assert batched.token_history == toks + [42] and batched.pos == 6
+    with pytest.raises(RuntimeError, match="ForwardBatch: empty token"):
+        batched.ForwardBatch([], 0)
+    with pytest.raises(pkg.OutOfRange, match="token id out of range"):
+        batched.ForwardToken(w.cfg["vocab"], 0)
+    with pytest.raises(pkg.OutOfRange, match="position out of range"):
+        batched.ForwardToken(0, 64)
+
+
+def test_runtime_counters(pkg, mini, cuda):
+    """Per-logical-op counters as TestCudaForwardQuant asserts them
+    (tests/test_cuda_quant.cc:442-472): Linear 7L+1, attention L per token,
+    one logits download, no activation uploads."""
+    w = mini[pkg.Q80]
+    L = w.cfg["n_layers"]
+    model = pkg.Model.from_synth(w, max_seq_len=16)
+    s = model.stats()
+    assert s["uploaded_weight_count"] == 2 + 12 * L  # embedding, final norm, 12 per layer
+    model.reset_stats()
+    ctx = pkg.Context(model)
+    ctx.ForwardToken(3, 0)
+    s = model.stats()
+    assert s["linear_calls"] == 7 * L + 1
+    assert s["attention_calls"] == L
+    assert s["activation_calls"] == 10 * L + 1  # bias adds present in Qwen2
+    assert s["device_to_host_copies"] == 1 and s["device_to_host_bytes"] == 4 * w.cfg["vocab"]
+    assert s["host_to_device_copies"] == 0
+    for i in range(1, 3):
+        ctx.ForwardToken(3, i)
+    assert model.stats()["linear_calls"] == 3 * (7 * L + 1)
+    # packed weights occupy exactly the ggml block bytes plus resident F32
+    c = w.cfg
+    hd = c["dim"] // c["n_heads"]
+    blocks = w.token_embd.nbytes + sum(getattr(Ly, n).nbytes for Ly in w.layers
+                                       for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))
+    f32 = 4 * (c["dim"] + L * (2 * c["dim"] + c["n_heads"] * hd + 2 * c["n_kv_heads"] * hd))
+    assert model.memory_bytes() == blocks + f32
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_greedy_decode_matches_oracle(pkg, orc, mini, cuda, qt):
+    w = mini[qt]
+    prompt = [5, 77, 300]
+    n_steps = 20
+    om = orc.OracleModel(w, 64)
+    for i, t in enumerate(prompt[:-1]):
+        om.forward_token(t, i)
+    tok, ref_tokens, margins = prompt[-1], [], []
+    for i in range(n_steps):
+        lg = om.forward_token(tok, len(prompt) - 1 + i)
+        top2 = np.sort(lg)[-2:]
+        margins.append(float(top2[1] - top2[0]))
+        tok = orc.argmax(lg)
+        ref_tokens.append(tok)
+    model = pkg.Model.from_synth(w, max_seq_len=64)
+    ctx = pkg.Context(model)
+    ctx.ForwardBatch(prompt[:-1], 0)
+    got = ctx.decode_greedy(prompt[-1], len(prompt) - 1, n_steps)
+    print(f"q{qt} min top1/top2 margin {min(margins):.3e}")
+    assert got.tolist() == ref_tokens
+
+
+def test_qwen2_0_5b_q8_0_greedy_64_matches_reference(pkg, S, cuda):
+    """Full-size Qwen2-0.5B-architecture Q8_0 (configuration 1): 32 random prompt
+    ids, 64 greedy steps; tokens must equal the reference's, and the first
+    step's logits must sit within tolerance of its top-5."""
+    g = json.load(open(golden_path("qwen2_0_5b_q8_0.json")))
+    w = S.make_model(S.QWEN2_0_5B, S.Q80, g["model_seed"],
+                     quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+    model = pkg.Model.from_synth(w, max_seq_len=96)
+    ctx = pkg.Context(model)
+    prompt = g["prompt"]
+    assert prompt == S.prompt_tokens(w.cfg["vocab"], 32, g["prompt_seed"]).tolist()
+    logits = ctx.ForwardBatch(prompt, 0)
+    for k, v in g["top5"][0]:
+        assert abs(logits[k] - v) <= 1e-3 * 6.0  # logit range of this model ~6
+    first = int(np.argmax(logits))
+    assert first == g["greedy_tokens"][0]
+    rest = ctx.decode_greedy(first, 32, 63)
+    tokens = [first] + rest.tolist()
+    assert tokens == g["greedy_tokens"], (
+        f"first divergence at {next(i for i, (a, b) in enumerate(zip(tokens, g['greedy_tokens'])) if a != b)}"
+        f", reference min margin {min(g['top1_top2_margin']):.3e}")
