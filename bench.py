@@ -270,6 +270,8 @@ def main():
     ap.add_argument("--impl", default="dqmk", choices=["dqmk", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="time only the decode steps (small runs for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -313,6 +315,15 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
     value = world * args.steps / dt
+
+    if args.decode_only:
+        if dist:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(value, 2), "unit": "tok/s",
+                              "steps": args.steps, "ms_per_step": dt / args.steps * 1e3,
+                              "decode_only": True, "clocks": clocks}))
+        return
 
     # ---- e2e through the C ABI with host buffers
     e2e_steps = min(args.steps, 256)

@@ -25,6 +25,197 @@ constexpr int kMinChunk = 32;
 
 __device__ __forceinline__ int round_up32(int v) { return (v + 31) & ~31; }
 
+// Split bookkeeping shared by both kernel forms.
+struct Split {
+  int T, chunk, n_active, t0, n;
+};
+
+__device__ __forceinline__ Split split_of(const AttnArgs& a, int split, int pos) {
+  Split s;
+  s.T = pos + 1;
+  s.chunk = round_up32((s.T + a.max_splits - 1) / a.max_splits);
+  if (s.chunk < kMinChunk) s.chunk = kMinChunk;
+  s.n_active = (s.T + s.chunk - 1) / s.chunk;
+  s.t0 = split * s.chunk;
+  s.n = max(0, min(s.T, s.t0 + s.chunk) - s.t0);
+  return s;
+}
+
+// Softmax statistics of one split's scores (one warp per head); scores are
+// replaced by exp(s - m).
+__device__ __forceinline__ void split_softmax(float* ss, int chunk_cap, int G, int n,
+                                              float* head_m, float* head_l) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int h = wid; h < G; h += kThreads / 32) {
+    float m = -INFINITY;
+    for (int t = lane; t < n; t += 32) m = fmaxf(m, ss[h * chunk_cap + t]);
+    m = warp_max(m);
+    float l = 0.0f;
+    for (int t = lane; t < n; t += 32) {
+      const float p = expf(ss[h * chunk_cap + t] - m);
+      ss[h * chunk_cap + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      head_m[h] = m;
+      head_l[h] = l;
+    }
+  }
+}
+
+// Completion ticket per KV head; the CTA that takes the last one merges the
+// splits: out = sum_i e^(m_i - M) o_i / sum_i e^(m_i - M) l_i.
+__device__ __forceinline__ void split_combine(const AttnArgs& a, int kvh, int G, int hd,
+                                              int n_active, int* is_last) {
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(&a.tickets[kvh], 1u);
+    *is_last = done == gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!*is_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * hd; i += kThreads) {
+    const int h = i / hd, dcol = i % hd;
+    const float* part = a.partials + (size_t)(kvh * G + h) * a.max_splits * (hd + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(part + (size_t)s * (hd + 2) + hd));
+    float num = 0.0f, den = 0.0f;
+#pragma unroll 4
+    for (int s = 0; s < n_active; ++s) {
+      const float* ps = part + (size_t)s * (hd + 2);
+      const float w = expf(__ldcg(ps + hd) - M);
+      num = fmaf(w, __ldcg(ps + dcol), num);
+      den = fmaf(w, __ldcg(ps + hd + 1), den);
+    }
+    a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(num, den);
+  }
+  if (threadIdx.x == 0) a.tickets[kvh] = 0u;
+}
+
+// head_dim known at compile time (64 / 128).  Scores: HD/16 threads per
+// position, each holding 16 dims of the K row (4 x 16-byte loads issued
+// together), partial dots folded with shuffles.  P.V: one thread per dim
+// (and per position group when HD < 128), V loads unrolled 4 deep.
+template <int HD>
+__global__ void __launch_bounds__(kThreads) attention_hd_kernel(const AttnArgs a, int chunk_cap) {
+  constexpr int TPT = HD / 16;           // threads per position (scores)
+  constexpr int TOK = kThreads / TPT;    // positions per score pass
+  constexpr int GROUPS = kThreads / HD;  // position groups in P.V
+  extern __shared__ float sm[];
+  __shared__ float head_m[kMaxGroup], head_l[kMaxGroup];
+  __shared__ int is_last;
+
+  pdl_trigger();
+  pdl_wait();
+
+  const int tid = threadIdx.x;
+  const int kvh = blockIdx.x, split = blockIdx.y;
+  const int G = a.n_heads / a.n_kv_heads;
+  const int pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+  const Split sp = split_of(a, split, pos);
+  const size_t row_stride = (size_t)a.n_kv_heads * HD;
+  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
+  const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
+  float* sq = sm;                            // [8][HD]
+  float* ss = sq + kMaxGroup * HD;           // [8][chunk_cap]
+  float* sacc = ss + kMaxGroup * chunk_cap;  // [GROUPS][8][HD]
+
+  if (split < sp.n_active) {
+    for (int i = tid; i < G * HD; i += kThreads) sq[i] = __ldcg(a.q + (size_t)(kvh * G) * HD + i);
+    __syncthreads();
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
+    const int part = tid % TPT;
+    for (int base = 0; base < sp.n; base += TOK) {
+      const int t = base + tid / TPT;
+      float dot[kMaxGroup];
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h) dot[h] = 0.0f;
+      if (t < sp.n) {
+        const float4* kr =
+            reinterpret_cast<const float4*>(kbase + (size_t)(sp.t0 + t) * row_stride) + part * 4;
+        float4 k4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) k4[i] = __ldcg(kr + i);
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) {
+          if (h < G) {
+            const float4* q4 = reinterpret_cast<const float4*>(sq + h * HD) + part * 4;
+            float d = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float4 qq = q4[i];
+              d = fmaf(qq.x, k4[i].x, d);
+              d = fmaf(qq.y, k4[i].y, d);
+              d = fmaf(qq.z, k4[i].z, d);
+              d = fmaf(qq.w, k4[i].w, d);
+            }
+            dot[h] = d;
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h) {
+#pragma unroll
+        for (int o = TPT / 2; o > 0; o >>= 1) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
+      }
+      if (t < sp.n && part == 0) {
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+          if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
+      }
+    }
+    __syncthreads();
+    split_softmax(ss, chunk_cap, G, sp.n, head_m, head_l);
+    __syncthreads();
+
+    const int d = tid % HD, gi = tid / HD;
+    float acc[kMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
+    int t = gi;
+    for (; t + 3 * GROUPS < sp.n; t += 4 * GROUPS) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        v[u] = __ldcg(vbase + (size_t)(sp.t0 + t + u * GROUPS) * row_stride + d);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+          if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t + u * GROUPS], v[u], acc[h]);
+      }
+    }
+    for (; t < sp.n; t += GROUPS) {
+      const float v = __ldcg(vbase + (size_t)(sp.t0 + t) * row_stride + d);
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h)
+        if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t], v, acc[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h)
+      if (h < G) sacc[(gi * kMaxGroup + h) * HD + d] = acc[h];
+    __syncthreads();
+
+    for (int i = tid; i < G * HD; i += kThreads) {
+      const int h = i / HD, dcol = i % HD;
+      float o = 0.0f;
+#pragma unroll
+      for (int g2 = 0; g2 < GROUPS; ++g2) o += sacc[(g2 * kMaxGroup + h) * HD + dcol];
+      float* pp = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * (HD + 2);
+      pp[dcol] = o;
+      if (dcol == 0) {
+        pp[HD] = head_m[h];
+        pp[HD + 1] = head_l[h];
+      }
+    }
+  }
+  split_combine(a, kvh, G, HD, sp.n_active, &is_last);
+}
+
+// Any head_dim that is a multiple of 4 up to 256: one thread per position.
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, int chunk_cap) {
   extern __shared__ float sm[];
   __shared__ float head_m[kMaxGroup], head_l[kMaxGroup];
@@ -36,28 +227,21 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int hd = a.head_dim;
   const int G = a.n_heads / a.n_kv_heads;
-  const int pos = a.pos_dev ? *a.pos_dev : a.pos_arg;
-  const int T = pos + 1;
-  int chunk = round_up32((T + a.max_splits - 1) / a.max_splits);
-  if (chunk < kMinChunk) chunk = kMinChunk;
-  const int n_active = (T + chunk - 1) / chunk;
-  const int t0 = split * chunk;
-  const int t1 = min(T, t0 + chunk);
-  const int n = t1 - t0;
+  const int pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+  const Split sp = split_of(a, split, pos);
+  const int t0 = sp.t0, n = sp.n;
   const size_t row_stride = (size_t)a.n_kv_heads * hd;
   const float* kbase = a.keys + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * hd;
   const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * hd;
 
-  float* sq = sm;                         // [G][hd]   query heads of this KV head
-  float* ss = sq + kMaxGroup * hd;        // [G][chunk_cap] scores -> exp
-  float* sacc = ss + kMaxGroup * chunk_cap;  // [groups][G][hd] PV partial sums
+  float* sq = sm;
+  float* ss = sq + kMaxGroup * hd;
+  float* sacc = ss + kMaxGroup * chunk_cap;
 
-  if (split < n_active) {
+  if (split < sp.n_active) {
     for (int i = threadIdx.x; i < G * hd; i += kThreads)
-      sq[i] = a.q[(size_t)(kvh * G) * hd + i];
+      sq[i] = __ldcg(a.q + (size_t)(kvh * G) * hd + i);
     __syncthreads();
-
-    // ---- scores: one thread per position, K row read once for all G heads
     const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
     for (int t = threadIdx.x; t < n; t += kThreads) {
       const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)(t0 + t) * row_stride);
@@ -65,7 +249,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
 #pragma unroll
       for (int h = 0; h < kMaxGroup; ++h) dot[h] = 0.0f;
       for (int i = 0; i < hd / 4; ++i) {
-        const float4 k4 = kr[i];
+        const float4 k4 = __ldcg(kr + i);
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) {
           if (h < G) {
@@ -84,28 +268,9 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
         if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
     }
     __syncthreads();
-
-    // ---- local softmax statistics, one warp per head
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int h = wid; h < G; h += kThreads / 32) {
-      float m = -INFINITY;
-      for (int t = lane; t < n; t += 32) m = fmaxf(m, ss[h * chunk_cap + t]);
-      m = warp_max(m);
-      float l = 0.0f;
-      for (int t = lane; t < n; t += 32) {
-        const float p = expf(ss[h * chunk_cap + t] - m);
-        ss[h * chunk_cap + t] = p;
-        l += p;
-      }
-      l = warp_sum(l);
-      if (lane == 0) {
-        head_m[h] = m;
-        head_l[h] = l;
-      }
-    }
+    split_softmax(ss, chunk_cap, G, n, head_m, head_l);
     __syncthreads();
 
-    // ---- o = sum_t p_t V_t: thread owns one d, positions split in groups
     const int groups = kThreads / hd > 0 ? kThreads / hd : 1;
     const int d = threadIdx.x % hd;
     const int gi = threadIdx.x / hd;
@@ -114,7 +279,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
 #pragma unroll
       for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
       for (int t = gi; t < n; t += groups) {
-        const float v = vbase[(size_t)(t0 + t) * row_stride + d];
+        const float v = __ldcg(vbase + (size_t)(t0 + t) * row_stride + d);
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h)
           if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t], v, acc[h]);
@@ -123,7 +288,6 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
       for (int h = 0; h < kMaxGroup; ++h)
         if (h < G) sacc[(gi * kMaxGroup + h) * hd + d] = acc[h];
     }
-    // hd > kThreads: remaining d columns handled in a second pass
     for (int dd = kThreads; dd < hd; dd += kThreads) {
       const int d2 = dd + threadIdx.x;
       if (d2 < hd) {
@@ -131,7 +295,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
         for (int t = 0; t < n; ++t) {
-          const float v = vbase[(size_t)(t0 + t) * row_stride + d2];
+          const float v = __ldcg(vbase + (size_t)(t0 + t) * row_stride + d2);
 #pragma unroll
           for (int h = 0; h < kMaxGroup; ++h)
             if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t], v, acc[h]);
@@ -143,7 +307,6 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
     }
     __syncthreads();
 
-    // ---- write this split's partial: [o_0..o_{hd-1}, m, l] per head
     for (int i = threadIdx.x; i < G * hd; i += kThreads) {
       const int h = i / hd, dcol = i % hd;
       float o = 0.0f;
@@ -157,32 +320,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
       }
     }
   }
-
-  // ---- completion ticket; the last CTA of this KV head merges the splits
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int done = atomicAdd(&a.tickets[kvh], 1u);
-    is_last = done == gridDim.y - 1;
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int i = threadIdx.x; i < G * hd; i += kThreads) {
-    const int h = i / hd, dcol = i % hd;
-    const float* part = a.partials + (size_t)(kvh * G + h) * a.max_splits * (hd + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(part + (size_t)s * (hd + 2) + hd));
-    float num = 0.0f, den = 0.0f;
-    for (int s = 0; s < n_active; ++s) {
-      const float* ps = part + (size_t)s * (hd + 2);
-      const float w = expf(__ldcg(ps + hd) - M);
-      num = fmaf(w, __ldcg(ps + dcol), num);
-      den = fmaf(w, __ldcg(ps + hd + 1), den);
-    }
-    a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(num, den);
-  }
-  if (threadIdx.x == 0) a.tickets[kvh] = 0u;
+  split_combine(a, kvh, G, hd, sp.n_active, &is_last);
 }
 
 int chunk_cap_for(int max_seq, int max_splits) {
@@ -216,6 +354,12 @@ cudaError_t attention_prepare() {
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(attention_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_hd_kernel<64>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_hd_kernel<128>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -227,8 +371,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
   const size_t smem = smem_bytes(a.head_dim, cap);
   cudaError_t e = attention_prepare();
   if (e != cudaSuccess) return e;
-  return launch(attention_kernel, dim3(a.n_kv_heads, a.max_splits), dim3(kThreads), smem, stream,
-                pdl, a, cap);
+  const dim3 grid(a.n_kv_heads, a.max_splits);
+  if (a.head_dim == 64)
+    return launch(attention_hd_kernel<64>, grid, dim3(kThreads), smem, stream, pdl, a, cap);
+  if (a.head_dim == 128)
+    return launch(attention_hd_kernel<128>, grid, dim3(kThreads), smem, stream, pdl, a, cap);
+  return launch(attention_kernel, grid, dim3(kThreads), smem, stream, pdl, a, cap);
 }
 
 }  // namespace dqmk

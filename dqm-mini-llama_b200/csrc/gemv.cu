@@ -109,13 +109,15 @@ struct Tile {
   uint16_t d[RPW][CPL];
 };
 
+// Row groups are RPW rows; GT threads (one warp, or the whole CTA) share a
+// group and stride over its 16-byte chunks.
 struct Geo {
   int chunks, row_bytes, nbk, seg_chunks, nseg, gw, nw;
 };
 
-template <int QT, int RPW, int CPL>
+template <int QT, int RPW, int CPL, int GT>
 __device__ __forceinline__ void load_step(Tile<QT, RPW, CPL>& t, const GemvArgs& a,
-                                          const Geo& g, int step, int lane) {
+                                          const Geo& g, int step, int gt) {
   const int gi = step / g.nseg;
   const int seg = step - gi * g.nseg;
   const int grp = g.gw + gi * g.nw;
@@ -124,7 +126,7 @@ __device__ __forceinline__ void load_step(Tile<QT, RPW, CPL>& t, const GemvArgs&
     const int row = grp * RPW + r;
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
-      const int c = seg * g.seg_chunks + j * 32 + lane;
+      const int c = seg * g.seg_chunks + j * GT + gt;
       if (row < a.n_rows && c < g.chunks) {
         t.w[r][j] = ldg_stream(a.qs + (size_t)row * g.row_bytes + (size_t)c * 16);
         t.d[r][j] = __ldg(a.d + (size_t)row * g.nbk + (QT == DQMK_Q80 ? (c >> 1) : c));
@@ -136,14 +138,14 @@ __device__ __forceinline__ void load_step(Tile<QT, RPW, CPL>& t, const GemvArgs&
   }
 }
 
-template <int QT, int RPW, int CPL>
+template <int QT, int RPW, int CPL, int GT>
 __device__ __forceinline__ void compute_step(const Tile<QT, RPW, CPL>& t, const Geo& g,
-                                             int step, int lane, const float4* xs,
+                                             int step, int gt, const float4* xs,
                                              float (&acc)[RPW]) {
   const int seg = step % g.nseg;
 #pragma unroll
   for (int j = 0; j < CPL; ++j) {
-    const int c = seg * g.seg_chunks + j * 32 + lane;
+    const int c = seg * g.seg_chunks + j * GT + gt;
     if (c < g.chunks) {
       float4 xv[8];
 #pragma unroll
@@ -182,7 +184,7 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
       if (lane == r && row < a.n_rows) {
         float v = acc[r];
         if (a.bias) v = __fadd_rn(v, a.bias[row]);
-        if (a.residual) v = __fadd_rn(a.residual[row], v);
+        if (a.residual) v = __fadd_rn(__ldcg(a.residual + row), v);
         a.y[row] = v;
       }
     }
@@ -257,61 +259,151 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
   }
 }
 
-template <int QT, int RPW, int CPL>
-__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
-  extern __shared__ float4 xs[];
-  __shared__ float red[kWarps];
-  __shared__ float bcast;
-  __shared__ unsigned long long best_w[kWarps];
+constexpr int kNormRegs = 8;  // float4 of RMSNorm weight prefetched per thread
 
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  Geo g;
-  g.chunks = a.kp / Fmt<QT>::kElems;
-  g.row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
-  g.nbk = a.kp / 32;
-  g.seg_chunks = 32 * CPL;
-  g.nseg = (g.chunks + g.seg_chunks - 1) / g.seg_chunks;
-  g.gw = blockIdx.x * kWarps + wid;
-  g.nw = gridDim.x * kWarps;
-  const int n_groups = (a.n_rows + RPW - 1) / RPW;
-  const int my_groups = g.gw < n_groups ? (n_groups - g.gw + g.nw - 1) / g.nw : 0;
-  const int total = my_groups * g.nseg;
-
-  Tile<QT, RPW, CPL> ta, tb;
-  // Weights do not depend on the previous kernel: fetch before the wait.
-  if (total > 0) load_step(ta, a, g, 0, lane);
-  pdl_trigger();
-  pdl_wait();
-
-  // ---- prologue: stage x (optionally RMS-normalised) into shared memory
+// Stage x (k floats, zero-padded to kp) into swizzled shared memory, RMS-
+// normalised when norm_w is set.  One global round trip: every thread issues
+// all of its loads before using any.  Activations come from the previous
+// kernel of the chain, so they are read through L2 (ld.global.cg).
+template <int QT>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const float4 (&nw)[kNormRegs],
+                                        bool norm_pref, float* red, float* bcast) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  constexpr int NT = kWarps * 32;
   float* xsf = reinterpret_cast<float*>(xs);
+  const int nf4 = a.kp >> 2;
+  const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.k & 3) == 0);
   float ss = 0.0f;
-  for (int e = threadIdx.x; e < a.kp; e += blockDim.x) {
-    const float v = e < a.k ? a.x[e] : 0.0f;
-    xsf[xphys<QT>(e)] = v;
-    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    const int k4 = a.k >> 2;
+    for (int base = 0; base < nf4; base += 8 * NT) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i4 = base + u * NT + tid;
+        v[u] = i4 < k4 ? __ldcg(x4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i4 = base + u * NT + tid;
+        if (i4 < nf4) {
+          ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
+          ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
+          ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
+          ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
+          const int e = i4 * 4;
+          xs[xslot<QT>(e / Fmt<QT>::kElems, (e % Fmt<QT>::kElems) >> 2)] = v[u];
+        }
+      }
+    }
+  } else {
+    for (int e = tid; e < a.kp; e += NT) {
+      const float v = e < a.k ? __ldcg(a.x + e) : 0.0f;
+      xsf[xphys<QT>(e)] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
   }
   if (a.norm_w) {
     ss = warp_sum(ss);
     if (lane == 0) red[wid] = ss;
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       float t = 0.0f;
       for (int w = 0; w < kWarps; ++w) t += red[w];
       const float mean = __fdiv_rn(t, (float)a.k);
-      bcast = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
+      *bcast = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
     }
     __syncthreads();
-    const float scale = bcast;
-    for (int e = threadIdx.x; e < a.k; e += blockDim.x) {
-      const int p = xphys<QT>(e);
-      xsf[p] = __fmul_rn(__fmul_rn(xsf[p], scale), a.norm_w[e]);
+    const float scale = *bcast;
+    if (vec && norm_pref) {
+#pragma unroll
+      for (int u = 0; u < kNormRegs; ++u) {
+        const int i4 = u * NT + tid;
+        if (i4 < (a.k >> 2)) {
+          const int e = i4 * 4;
+          float4* p = &xs[xslot<QT>(e / Fmt<QT>::kElems, (e % Fmt<QT>::kElems) >> 2)];
+          float4 v = *p;
+          v.x = __fmul_rn(__fmul_rn(v.x, scale), nw[u].x);
+          v.y = __fmul_rn(__fmul_rn(v.y, scale), nw[u].y);
+          v.z = __fmul_rn(__fmul_rn(v.z, scale), nw[u].z);
+          v.w = __fmul_rn(__fmul_rn(v.w, scale), nw[u].w);
+          *p = v;
+        }
+      }
+    } else {
+      // every element is rescaled by the thread that wrote it
+      if (vec) {
+        for (int i4 = tid; i4 < (a.k >> 2); i4 += NT) {
+          const int e = i4 * 4;
+          float4* p = &xs[xslot<QT>(e / Fmt<QT>::kElems, (e % Fmt<QT>::kElems) >> 2)];
+          const float4 w4 = __ldg(reinterpret_cast<const float4*>(a.norm_w) + i4);
+          float4 v = *p;
+          v.x = __fmul_rn(__fmul_rn(v.x, scale), w4.x);
+          v.y = __fmul_rn(__fmul_rn(v.y, scale), w4.y);
+          v.z = __fmul_rn(__fmul_rn(v.z, scale), w4.z);
+          v.w = __fmul_rn(__fmul_rn(v.w, scale), w4.w);
+          *p = v;
+        }
+      } else {
+        for (int e = tid; e < a.k; e += NT) {
+          const int p = xphys<QT>(e);
+          xsf[p] = __fmul_rn(__fmul_rn(xsf[p], scale), a.norm_w[e]);
+        }
+      }
     }
   }
   __syncthreads();
+}
+
+template <int QT, int RPW, int CPL, int GW>
+__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
+  static_assert(GW == 1 || GW == kWarps, "a row group is one warp or the whole CTA");
+  constexpr int GT = GW * 32;         // threads per row group
+  constexpr int GPC = kWarps / GW;    // row groups per CTA
+  extern __shared__ float4 xs[];
+  __shared__ float red[kWarps];
+  __shared__ float red_rows[kWarps][RPW];
+  __shared__ float bcast;
+  __shared__ unsigned long long best_w[kWarps];
+
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int gt = (wid % GW) * 32 + lane;
+  Geo g;
+  g.chunks = a.kp / Fmt<QT>::kElems;
+  g.row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
+  g.nbk = a.kp / 32;
+  g.seg_chunks = GT * CPL;
+  g.nseg = (g.chunks + g.seg_chunks - 1) / g.seg_chunks;
+  g.gw = blockIdx.x * GPC + wid / GW;
+  g.nw = gridDim.x * GPC;
+  const int n_groups = (a.n_rows + RPW - 1) / RPW;
+  const int my_groups = g.gw < n_groups ? (n_groups - g.gw + g.nw - 1) / g.nw : 0;
+  const int total = my_groups * g.nseg;
+
+  // Weights and norm weights do not depend on the previous kernel: fetch
+  // them before the programmatic-dependency wait.
+  Tile<QT, RPW, CPL> ta, tb;
+  if (total > 0) load_step<QT, RPW, CPL, GT>(ta, a, g, 0, gt);
+  float4 nw[kNormRegs];
+  const bool norm_pref = a.norm_w && (a.kp >> 2) <= kNormRegs * kWarps * 32 &&
+                         ((a.k & 3) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(a.norm_w) & 15u) == 0);
+  if (norm_pref) {
+#pragma unroll
+    for (int u = 0; u < kNormRegs; ++u) {
+      const int i4 = u * kWarps * 32 + tid;
+      nw[u] = i4 < (a.k >> 2) ? __ldg(reinterpret_cast<const float4*>(a.norm_w) + i4)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  pdl_trigger();
+  pdl_wait();
+
+  stage_x<QT>(a, xs, nw, norm_pref, red, &bcast);
 
   int pos = 0;
-  if (a.epi == kEpiQkv) pos = a.pos_dev ? *a.pos_dev : a.pos_arg;
+  if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
   unsigned long long best = 0ull;
   float acc[RPW];
 #pragma unroll
@@ -322,19 +414,37 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
     const int grp = g.gw + (step / g.nseg) * g.nw;
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]);
-    epilogue<RPW>(a, grp, lane, acc, pos, best);
+    if constexpr (GW > 1) {
+      // the CTA's warps hold partial sums of the same rows
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) red_rows[wid][r] = acc[r];
+      }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) t += red_rows[w][r];
+        acc[r] = t;
+      }
+      __syncthreads();
+      if (wid == 0) epilogue<RPW>(a, grp, lane, acc, pos, best);
+    } else {
+      epilogue<RPW>(a, grp, lane, acc, pos, best);
+    }
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
   };
 
   // two-stage register pipeline: load step s+1 while step s computes
   for (int s = 0; s < total; s += 2) {
-    if (s + 1 < total) load_step(tb, a, g, s + 1, lane);
-    compute_step(ta, g, s, lane, xs, acc);
+    if (s + 1 < total) load_step<QT, RPW, CPL, GT>(tb, a, g, s + 1, gt);
+    compute_step<QT, RPW, CPL, GT>(ta, g, s, gt, xs, acc);
     finish(s);
     if (s + 1 < total) {
-      if (s + 2 < total) load_step(ta, a, g, s + 2, lane);
-      compute_step(tb, g, s + 1, lane, xs, acc);
+      if (s + 2 < total) load_step<QT, RPW, CPL, GT>(ta, a, g, s + 2, gt);
+      compute_step<QT, RPW, CPL, GT>(tb, g, s + 1, gt, xs, acc);
       finish(s + 1);
     }
   }
@@ -349,7 +459,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
     }
     if (lane == 0) best_w[wid] = best;
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       unsigned long long b = 0ull;
       for (int w = 0; w < kWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
       if (a.argmax_slot) {
@@ -374,16 +484,16 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
 // ------------------------------------------------------------ launch table
 // One-time kernel attributes and the resident-CTA cap for the grid-stride
 // case.  Run before any stream capture (context creation does).
-template <int QT, int RPW, int CPL>
+template <int QT, int RPW, int CPL, int GW>
 cudaError_t prepare_t(int* max_ctas_out) {
   static int max_ctas = -1;
   if (max_ctas < 0) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<QT, RPW, CPL>,
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<QT, RPW, CPL, GW>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          200 * 1024);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<QT, RPW, CPL>,
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<QT, RPW, CPL, GW>,
                                                       kWarps * 32, 4096 * sizeof(float));
     if (e != cudaSuccess) return e;
     max_ctas = (per_sm > 0 ? per_sm : 1) * sm_count();
@@ -392,18 +502,27 @@ cudaError_t prepare_t(int* max_ctas_out) {
   return cudaSuccess;
 }
 
-template <int QT, int RPW, int CPL>
+template <int QT, int RPW, int CPL, int GW>
 cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   int max_ctas = 0;
-  cudaError_t e = prepare_t<QT, RPW, CPL>(&max_ctas);
+  cudaError_t e = prepare_t<QT, RPW, CPL, GW>(&max_ctas);
   if (e != cudaSuccess) return e;
   const size_t smem = (size_t)a.kp * sizeof(float);
   const int n_groups = (a.n_rows + RPW - 1) / RPW;
-  int grid = (n_groups + kWarps - 1) / kWarps;
+  constexpr int GPC = kWarps / GW;
+  int grid = (n_groups + GPC - 1) / GPC;
   if (grid > max_ctas) grid = max_ctas;
   if (grid < 1) grid = 1;
-  return launch(gemv_kernel<QT, RPW, CPL>, dim3(grid), dim3(kWarps * 32), smem, stream, pdl, a);
+  return launch(gemv_kernel<QT, RPW, CPL, GW>, dim3(grid), dim3(kWarps * 32), smem, stream, pdl,
+                a);
 }
+
+// Every instantiation the dispatcher below can pick.
+#define DQMK_GEMV_VARIANTS(X)                                                             \
+  X(DQMK_Q80, 2, 1, 1) X(DQMK_Q80, 2, 2, 1) X(DQMK_Q80, 4, 2, 1) X(DQMK_Q80, 2, 2, 4)       \
+  X(DQMK_Q80, 2, 3, 4) X(DQMK_Q80, 2, 4, 4) X(DQMK_Q80, 4, 2, 4) X(DQMK_Q80, 4, 4, 4)       \
+  X(DQMK_Q40, 2, 1, 1) X(DQMK_Q40, 4, 1, 1) X(DQMK_Q40, 2, 2, 1) X(DQMK_Q40, 4, 2, 1)       \
+  X(DQMK_Q40, 2, 2, 4) X(DQMK_Q40, 2, 4, 4) X(DQMK_Q40, 4, 2, 4) X(DQMK_Q40, 4, 4, 4)
 
 // ------------------------------------------------ ggml-layout compatibility
 // One warp per weight row, blocks read in place (34 / 18 bytes, 2-byte
@@ -467,37 +586,42 @@ __global__ void linear_blocks_kernel(const float* __restrict__ x, int rows, int 
 }  // namespace
 
 cudaError_t gemv_prepare() {
-  cudaError_t e;
-  if ((e = prepare_t<DQMK_Q80, 2, 2>(nullptr)) != cudaSuccess) return e;
-  if ((e = prepare_t<DQMK_Q80, 4, 2>(nullptr)) != cudaSuccess) return e;
-  if ((e = prepare_t<DQMK_Q80, 2, 4>(nullptr)) != cudaSuccess) return e;
-  if ((e = prepare_t<DQMK_Q80, 4, 4>(nullptr)) != cudaSuccess) return e;
-  if ((e = prepare_t<DQMK_Q40, 2, 1>(nullptr)) != cudaSuccess) return e;
-  if ((e = prepare_t<DQMK_Q40, 4, 1>(nullptr)) != cudaSuccess) return e;
-  if ((e = prepare_t<DQMK_Q40, 2, 2>(nullptr)) != cudaSuccess) return e;
-  if ((e = prepare_t<DQMK_Q40, 2, 4>(nullptr)) != cudaSuccess) return e;
-  return prepare_t<DQMK_Q40, 4, 4>(nullptr);
+  cudaError_t e = cudaSuccess;
+#define DQMK_PREP(QT, RPW, CPL, GW) \
+  if (e == cudaSuccess) e = prepare_t<QT, RPW, CPL, GW>(nullptr);
+  DQMK_GEMV_VARIANTS(DQMK_PREP)
+#undef DQMK_PREP
+  return e;
 }
 
+// Shape -> variant.  Rows that fit in one warp pass (<= 64 chunks) get a warp
+// per row group; longer rows are split across the whole CTA (4 warps), so no
+// warp walks a long row alone.  Very tall weights (lm_head) take 4 rows per
+// group to amortise the shared-memory reads of x.
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
-  const bool paired = a.epi == kEpiSwiGlu || a.epi == kEpiQkv;
-  const bool wide = a.n_rows >= 32768;
+  const bool wide = a.n_rows >= 32768 && a.epi != kEpiSwiGlu && a.epi != kEpiQkv;
+  const int chunks = a.qtype == DQMK_Q80 ? a.kp / 16 : a.kp / 32;
   if (a.qtype == DQMK_Q80) {
-    const int chunks = a.kp / 16;
-    if (chunks <= 64) {
-      return wide ? launch_t<DQMK_Q80, 4, 2>(a, stream, pdl)
-                  : launch_t<DQMK_Q80, 2, 2>(a, stream, pdl);
-    }
-    return (wide && !paired) ? launch_t<DQMK_Q80, 4, 4>(a, stream, pdl)
-                             : launch_t<DQMK_Q80, 2, 4>(a, stream, pdl);
+    if (chunks <= 32) return launch_t<DQMK_Q80, 2, 1, 1>(a, stream, pdl);
+    if (chunks <= 64)
+      return wide ? launch_t<DQMK_Q80, 4, 2, 1>(a, stream, pdl)
+                  : launch_t<DQMK_Q80, 2, 2, 1>(a, stream, pdl);
+    if (wide) return chunks <= 256 ? launch_t<DQMK_Q80, 4, 2, 4>(a, stream, pdl)
+                                   : launch_t<DQMK_Q80, 4, 4, 4>(a, stream, pdl);
+    if (chunks <= 256) return launch_t<DQMK_Q80, 2, 2, 4>(a, stream, pdl);
+    if (chunks <= 384) return launch_t<DQMK_Q80, 2, 3, 4>(a, stream, pdl);
+    return launch_t<DQMK_Q80, 2, 4, 4>(a, stream, pdl);
   }
-  const int chunks = a.kp / 32;
-  if (chunks <= 32) {
-    return wide ? launch_t<DQMK_Q40, 4, 1>(a, stream, pdl)
-                : launch_t<DQMK_Q40, 2, 1>(a, stream, pdl);
-  }
-  if (chunks <= 64) return launch_t<DQMK_Q40, 2, 2>(a, stream, pdl);
-  return wide ? launch_t<DQMK_Q40, 4, 4>(a, stream, pdl) : launch_t<DQMK_Q40, 2, 4>(a, stream, pdl);
+  if (chunks <= 32)
+    return wide ? launch_t<DQMK_Q40, 4, 1, 1>(a, stream, pdl)
+                : launch_t<DQMK_Q40, 2, 1, 1>(a, stream, pdl);
+  if (chunks <= 64)
+    return wide ? launch_t<DQMK_Q40, 4, 2, 1>(a, stream, pdl)
+                : launch_t<DQMK_Q40, 2, 2, 1>(a, stream, pdl);
+  if (wide) return chunks <= 256 ? launch_t<DQMK_Q40, 4, 2, 4>(a, stream, pdl)
+                                 : launch_t<DQMK_Q40, 4, 4, 4>(a, stream, pdl);
+  if (chunks <= 256) return launch_t<DQMK_Q40, 2, 2, 4>(a, stream, pdl);
+  return launch_t<DQMK_Q40, 2, 4, 4>(a, stream, pdl);
 }
 
 cudaError_t launch_linear_blocks(int qtype, const float* x, int rows, int in_features,
