@@ -43,10 +43,11 @@ __device__ __forceinline__ Split split_of(const AttnArgs& a, int split, int pos)
 
 // Softmax statistics of one split's scores (one warp per head); scores are
 // replaced by exp(s - m).
+template <int NT>
 __device__ __forceinline__ void split_softmax(float* ss, int chunk_cap, int G, int n,
                                               float* head_m, float* head_l) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  for (int h = wid; h < G; h += kThreads / 32) {
+  for (int h = wid; h < G; h += NT / 32) {
     float m = -INFINITY;
     for (int t = lane; t < n; t += 32) m = fmaxf(m, ss[h * chunk_cap + t]);
     m = warp_max(m);
@@ -65,9 +66,12 @@ __device__ __forceinline__ void split_softmax(float* ss, int chunk_cap, int G, i
 }
 
 // Completion ticket per KV head; the CTA that takes the last one merges the
-// splits: out = sum_i e^(m_i - M) o_i / sum_i e^(m_i - M) l_i.
+// splits: out = sum_i e^(m_i - M) o_i / sum_i e^(m_i - M) l_i.  Split
+// statistics are staged in shared memory in one pass, then every output
+// issues its partial-vector loads together.
+template <int NT>
 __device__ __forceinline__ void split_combine(const AttnArgs& a, int kvh, int G, int hd,
-                                              int n_active, int* is_last) {
+                                              int n_active, float* stats, int* is_last) {
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -77,33 +81,58 @@ __device__ __forceinline__ void split_combine(const AttnArgs& a, int kvh, int G,
   __syncthreads();
   if (!*is_last) return;
   __threadfence();
-  for (int i = threadIdx.x; i < G * hd; i += kThreads) {
-    const int h = i / hd, dcol = i % hd;
-    const float* part = a.partials + (size_t)(kvh * G + h) * a.max_splits * (hd + 2);
+  float* w = stats;                                  // [n_active][8] weights
+  float* inv_den = stats + (size_t)a.max_splits * kMaxGroup;  // [8]
+  for (int i = threadIdx.x; i < n_active * G; i += NT) {
+    const int sp = i / G, h = i % G;
+    const float* ps = a.partials + ((size_t)(kvh * G + h) * a.max_splits + sp) * (hd + 2);
+    w[sp * kMaxGroup + h] = __ldcg(ps + hd);
+    w[(a.max_splits + 1) * kMaxGroup + sp * kMaxGroup + h] = __ldcg(ps + hd + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
     float M = -INFINITY;
-    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(part + (size_t)s * (hd + 2) + hd));
-    float num = 0.0f, den = 0.0f;
-#pragma unroll 4
-    for (int s = 0; s < n_active; ++s) {
-      const float* ps = part + (size_t)s * (hd + 2);
-      const float w = expf(__ldcg(ps + hd) - M);
-      num = fmaf(w, __ldcg(ps + dcol), num);
-      den = fmaf(w, __ldcg(ps + hd + 1), den);
+    for (int sp = 0; sp < n_active; ++sp) M = fmaxf(M, w[sp * kMaxGroup + h]);
+    float den = 0.0f;
+    for (int sp = 0; sp < n_active; ++sp) {
+      const float e = expf(w[sp * kMaxGroup + h] - M);
+      w[sp * kMaxGroup + h] = e;
+      den = fmaf(e, w[(a.max_splits + 1) * kMaxGroup + sp * kMaxGroup + h], den);
     }
-    a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(num, den);
+    inv_den[h] = den;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * hd; i += NT) {
+    const int h = i / hd, dcol = i % hd;
+    const float* part = a.partials + (size_t)(kvh * G + h) * a.max_splits * (hd + 2) + dcol;
+    float num = 0.0f;
+    int sp = 0;
+    for (; sp + 8 <= n_active; sp += 8) {
+      float o[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o[u] = __ldcg(part + (size_t)(sp + u) * (hd + 2));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) num = fmaf(w[(sp + u) * kMaxGroup + h], o[u], num);
+    }
+    for (; sp < n_active; ++sp) num = fmaf(w[sp * kMaxGroup + h], __ldcg(part + (size_t)sp * (hd + 2)), num);
+    a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(num, inv_den[h]);
   }
   if (threadIdx.x == 0) a.tickets[kvh] = 0u;
 }
 
-// head_dim known at compile time (64 / 128).  Scores: HD/16 threads per
-// position, each holding 16 dims of the K row (4 x 16-byte loads issued
-// together), partial dots folded with shuffles.  P.V: one thread per dim
-// (and per position group when HD < 128), V loads unrolled 4 deep.
+// head_dim known at compile time (64 / 128), 256 threads.  Scores: HD/16
+// threads per position, each holding 16 dims of the K row (4 x 16-byte loads
+// issued together), partial dots folded with shuffles.  P.V: one thread per
+// (dim, position group), all of a thread's V loads for a 32-position chunk in
+// flight at once.  A single active split writes its output directly.
 template <int HD>
-__global__ void __launch_bounds__(kThreads) attention_hd_kernel(const AttnArgs a, int chunk_cap) {
-  constexpr int TPT = HD / 16;           // threads per position (scores)
-  constexpr int TOK = kThreads / TPT;    // positions per score pass
-  constexpr int GROUPS = kThreads / HD;  // position groups in P.V
+__global__ void __launch_bounds__(256) attention_hd_kernel(const AttnArgs a, int chunk_cap) {
+  constexpr int NT = 256;
+  constexpr int TPT = HD / 16;       // threads per position (scores)
+  constexpr int TOK = NT / TPT;      // positions per score pass
+  constexpr int GROUPS = NT / HD;    // position groups in P.V
+  constexpr int PV = 8;              // V loads in flight per thread
   extern __shared__ float sm[];
   __shared__ float head_m[kMaxGroup], head_l[kMaxGroup];
   __shared__ int is_last;
@@ -122,9 +151,10 @@ __global__ void __launch_bounds__(kThreads) attention_hd_kernel(const AttnArgs a
   float* sq = sm;                            // [8][HD]
   float* ss = sq + kMaxGroup * HD;           // [8][chunk_cap]
   float* sacc = ss + kMaxGroup * chunk_cap;  // [GROUPS][8][HD]
+  float* stats = sacc + GROUPS * kMaxGroup * HD;
 
   if (split < sp.n_active) {
-    for (int i = tid; i < G * HD; i += kThreads) sq[i] = __ldcg(a.q + (size_t)(kvh * G) * HD + i);
+    for (int i = tid; i < G * HD; i += NT) sq[i] = __ldcg(a.q + (size_t)(kvh * G) * HD + i);
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
     const int part = tid % TPT;
@@ -168,51 +198,54 @@ __global__ void __launch_bounds__(kThreads) attention_hd_kernel(const AttnArgs a
       }
     }
     __syncthreads();
-    split_softmax(ss, chunk_cap, G, sp.n, head_m, head_l);
+    split_softmax<NT>(ss, chunk_cap, G, sp.n, head_m, head_l);
     __syncthreads();
 
     const int d = tid % HD, gi = tid / HD;
     float acc[kMaxGroup];
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-    int t = gi;
-    for (; t + 3 * GROUPS < sp.n; t += 4 * GROUPS) {
-      float v[4];
+    for (int t = gi; t < sp.n; t += PV * GROUPS) {
+      float v[PV];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        v[u] = __ldcg(vbase + (size_t)(sp.t0 + t + u * GROUPS) * row_stride + d);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h)
-          if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t + u * GROUPS], v[u], acc[h]);
+      for (int u = 0; u < PV; ++u) {
+        const int tt = t + u * GROUPS;
+        v[u] = tt < sp.n ? __ldcg(vbase + (size_t)(sp.t0 + tt) * row_stride + d) : 0.0f;
       }
-    }
-    for (; t < sp.n; t += GROUPS) {
-      const float v = __ldcg(vbase + (size_t)(sp.t0 + t) * row_stride + d);
 #pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h)
-        if (h < G) acc[h] = fmaf(ss[h * chunk_cap + t], v, acc[h]);
+      for (int u = 0; u < PV; ++u) {
+        const int tt = t + u * GROUPS;
+        if (tt < sp.n) {
+#pragma unroll
+          for (int h = 0; h < kMaxGroup; ++h)
+            if (h < G) acc[h] = fmaf(ss[h * chunk_cap + tt], v[u], acc[h]);
+        }
+      }
     }
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h)
       if (h < G) sacc[(gi * kMaxGroup + h) * HD + d] = acc[h];
     __syncthreads();
 
-    for (int i = tid; i < G * HD; i += kThreads) {
+    const bool direct = sp.n_active == 1;
+    for (int i = tid; i < G * HD; i += NT) {
       const int h = i / HD, dcol = i % HD;
       float o = 0.0f;
 #pragma unroll
       for (int g2 = 0; g2 < GROUPS; ++g2) o += sacc[(g2 * kMaxGroup + h) * HD + dcol];
-      float* pp = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * (HD + 2);
-      pp[dcol] = o;
-      if (dcol == 0) {
-        pp[HD] = head_m[h];
-        pp[HD + 1] = head_l[h];
+      if (direct) {
+        a.out[(size_t)(kvh * G + h) * HD + dcol] = __fdiv_rn(o, head_l[h]);
+      } else {
+        float* pp = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * (HD + 2);
+        pp[dcol] = o;
+        if (dcol == 0) {
+          pp[HD] = head_m[h];
+          pp[HD + 1] = head_l[h];
+        }
       }
     }
   }
-  split_combine(a, kvh, G, HD, sp.n_active, &is_last);
+  if (sp.n_active > 1) split_combine<NT>(a, kvh, G, HD, sp.n_active, stats, &is_last);
 }
 
 // Any head_dim that is a multiple of 4 up to 256: one thread per position.
@@ -268,7 +301,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
         if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
     }
     __syncthreads();
-    split_softmax(ss, chunk_cap, G, n, head_m, head_l);
+    split_softmax<kThreads>(ss, chunk_cap, G, n, head_m, head_l);
     __syncthreads();
 
     const int groups = kThreads / hd > 0 ? kThreads / hd : 1;
@@ -312,6 +345,10 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
       float o = 0.0f;
       const int ng = hd <= kThreads ? groups : 1;
       for (int g2 = 0; g2 < ng; ++g2) o += sacc[(g2 * kMaxGroup + h) * hd + dcol];
+      if (sp.n_active == 1) {
+        a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(o, head_l[h]);
+        continue;
+      }
       float* part = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * (hd + 2);
       part[dcol] = o;
       if (dcol == 0) {
@@ -320,7 +357,8 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
       }
     }
   }
-  split_combine(a, kvh, G, hd, sp.n_active, &is_last);
+  if (sp.n_active > 1)
+    split_combine<kThreads>(a, kvh, G, hd, sp.n_active, sacc + kMaxGroup * hd * (kThreads / hd > 0 ? kThreads / hd : 1), &is_last);
 }
 
 int chunk_cap_for(int max_seq, int max_splits) {
@@ -329,10 +367,11 @@ int chunk_cap_for(int max_seq, int max_splits) {
   return c < kMinChunk ? kMinChunk : c;
 }
 
-size_t smem_bytes(int head_dim, int chunk_cap) {
-  const int groups = kThreads / head_dim > 0 ? kThreads / head_dim : 1;
+size_t smem_bytes(int threads, int head_dim, int chunk_cap, int max_splits) {
+  const int groups = threads / head_dim > 0 ? threads / head_dim : 1;
   return sizeof(float) * ((size_t)kMaxGroup * head_dim + (size_t)kMaxGroup * chunk_cap +
-                          (size_t)groups * kMaxGroup * head_dim);
+                          (size_t)groups * kMaxGroup * head_dim +
+                          (size_t)(2 * max_splits + 3) * kMaxGroup);
 }
 
 }  // namespace
@@ -368,14 +407,15 @@ cudaError_t attention_prepare() {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
   const int cap = chunk_cap_for(a.max_seq, a.max_splits);
-  const size_t smem = smem_bytes(a.head_dim, cap);
+  const bool hd_kernel = a.head_dim == 64 || a.head_dim == 128;
+  const size_t smem = smem_bytes(hd_kernel ? 256 : kThreads, a.head_dim, cap, a.max_splits);
   cudaError_t e = attention_prepare();
   if (e != cudaSuccess) return e;
   const dim3 grid(a.n_kv_heads, a.max_splits);
   if (a.head_dim == 64)
-    return launch(attention_hd_kernel<64>, grid, dim3(kThreads), smem, stream, pdl, a, cap);
+    return launch(attention_hd_kernel<64>, grid, dim3(256), smem, stream, pdl, a, cap);
   if (a.head_dim == 128)
-    return launch(attention_hd_kernel<128>, grid, dim3(kThreads), smem, stream, pdl, a, cap);
+    return launch(attention_hd_kernel<128>, grid, dim3(256), smem, stream, pdl, a, cap);
   return launch(attention_kernel, grid, dim3(kThreads), smem, stream, pdl, a, cap);
 }
 
