@@ -64,6 +64,7 @@ SIGNATURES = {
     "dqmk_argmax": ([_vp, _i, _vp, _vp], _i),
     "dqmk_kv_write": ([_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp], _i),
     "dqmk_attention_decode": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp], _i),
+    "dqmk_attention_decode_noalloc": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp], _i),
     "dqmk_model_create": ([C.POINTER(ModelConfig), _i, C.POINTER(_vp)], _i),
     "dqmk_model_destroy": ([_vp], _i),
     "dqmk_model_upload": ([_vp, C.c_char_p, _i, _vp, _sz, _i, _i], _i),

@@ -13,6 +13,8 @@
 // (rescaling by exp(m_i - M)) and resets the ticket, so the whole op is one
 // launch and replays inside a CUDA graph.  Positions come from device memory
 // so a captured graph serves every decode step.
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -464,5 +466,95 @@ extern "C" int dqmk_attention_decode(const float* q, const float* keys, const fl
   if (n_kv_heads * sizeof(unsigned int) > tickets_bytes)
     return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": too many KV heads");
   DQMK_CUDA_RET(api, launch_attention(a, static_cast<cudaStream_t>(stream), false));
+  return DQMK_OK;
+}
+
+// ------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory when they run attention: an
+// engine that reserves its whole device budget at start-up and treats any
+// later cudaMalloc as a failure, or a host that embeds this library and
+// forbids allocations outside its own allocator.  For them the split
+// partials and completion tickets live in this fixed, file-scope buffer
+// instead of the library's growable scratch.  Every GPU that loads the
+// library holds these 2 MiB until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB
+constexpr size_t kNoAllocTicketBytes = 256;               // zeroed before every call
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_attention_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};  // device address of the buffer, per device
+
+// Host code sees the array's name only as a stand-in symbol; the device
+// address comes from cudaGetSymbolAddress with that device current.
+cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attention_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int dqmk_attention_decode_noalloc(const float* q, const float* keys,
+                                             const float* values, int n_layers, int max_seq,
+                                             int n_kv_heads, int head_dim, int layer, int pos,
+                                             int n_heads, float* out, void* stream) {
+  const char* api = "CudaAttentionDecodeNoAlloc";
+  if (layer < 0 || layer >= n_layers) return fail(DQMK_ERR_RANGE, std::string(api) + ": layer out of range");
+  if (pos < 0 || pos >= max_seq) return fail(DQMK_ERR_RANGE, std::string(api) + ": pos out of range");
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || n_heads % n_kv_heads != 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid head configuration");
+  if (n_heads / n_kv_heads > 8)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": more than 8 query heads per KV head");
+  if (head_dim % 4 != 0 || head_dim > 256)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": head_dim must be a multiple of 4, <= 256");
+  if (!q || !keys || !values || !out) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": KV cache must be 16-byte aligned");
+  if (n_kv_heads * sizeof(unsigned int) > kNoAllocTicketBytes)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": too many KV heads");
+  const int splits = attention_splits(max_seq, n_kv_heads);
+  const size_t need =
+      kNoAllocTicketBytes + attention_partials_floats(n_heads, head_dim, splits) * sizeof(float);
+  if (need > kNoAllocScratchBytes)
+    return fail(DQMK_ERR_UNSUPPORTED,
+                std::string(api) + ": needs " + std::to_string(need) +
+                    " bytes of scratch, the static buffer holds " +
+                    std::to_string(kNoAllocScratchBytes) + " (fewer heads, a smaller head_dim or "
+                    "a shorter max_seq fit)");
+  void* scratch = nullptr;
+  DQMK_CUDA_RET(api, noalloc_scratch(&scratch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the buffer keeps the previous call's contents: tickets must start at zero
+  DQMK_CUDA_RET(api, cudaMemsetAsync(scratch, 0, kNoAllocTicketBytes, s));
+  AttnArgs a = {};
+  a.q = q;
+  a.keys = keys;
+  a.values = values;
+  a.max_seq = max_seq;
+  a.n_kv_heads = n_kv_heads;
+  a.head_dim = head_dim;
+  a.layer = layer;
+  a.n_heads = n_heads;
+  a.pos_dev = nullptr;
+  a.pos_arg = pos;
+  a.out = out;
+  a.tickets = static_cast<unsigned int*>(scratch);
+  a.partials = reinterpret_cast<float*>(static_cast<char*>(scratch) + kNoAllocTicketBytes);
+  a.max_splits = splits;
+  DQMK_CUDA_RET(api, launch_attention(a, s, false));
   return DQMK_OK;
 }

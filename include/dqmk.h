@@ -174,6 +174,27 @@ int dqmk_attention_decode(const float* q_dev, const float* keys_dev, const float
                           int n_layers, int max_seq, int n_kv_heads, int head_dim, int layer,
                           int pos, int n_heads, float* out_dev, void* stream);
 
+/* Allocation-free form of dqmk_attention_decode.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when
+ * they run attention (an engine that reserves its whole device budget at
+ * start-up and treats later cudaMalloc calls as failures, or a host that
+ * forbids allocations outside its own allocator).  Same arguments, results
+ * and errors as dqmk_attention_decode; it calls no cudaMalloc, cudaFree or
+ * other allocating routine.  The split partials and tickets live in one
+ * fixed 2 MiB device buffer compiled into the library (every GPU that loads
+ * it holds the 2 MiB until the process exits): n_heads * splits *
+ * (head_dim + 2) * 4 bytes + 256 must fit, where splits = min(ceil(max_seq /
+ * 32), 2 * SM count / n_kv_heads); larger shapes are rejected with
+ * DQMK_ERR_UNSUPPORTED and a message giving both sizes.  All calls share the
+ * buffer: each call zeroes the tickets first, and calls that overlap on the
+ * GPU (for example on two streams) race.  The first call on a device looks
+ * up the buffer's device address (cudaGetSymbolAddress, no allocation) with
+ * that device current; make that first call before any stream capture. */
+int dqmk_attention_decode_noalloc(const float* q_dev, const float* keys_dev,
+                                  const float* values_dev, int n_layers, int max_seq,
+                                  int n_kv_heads, int head_dim, int layer, int pos, int n_heads,
+                                  float* out_dev, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Engine: device-resident model + context (ForwardToken / ForwardBatch)*/
 /* ------------------------------------------------------------------ */
