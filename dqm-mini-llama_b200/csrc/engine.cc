@@ -16,6 +16,7 @@
 // Runtime counters follow the reference's per-logical-op accounting
 // (src/forward.cc:97-165) so the engine's counter tests still hold.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -450,8 +451,19 @@ extern "C" size_t dqmk_model_memory_bytes(const dqmk_model* m) { return m ? m->m
 // ------------------------------------------------------------------ context
 namespace {
 
+// Programmatic dependent launch between the kernels of a step; DQMK_PDL=0 in
+// the environment launches them plainly instead (diagnostics: same work).
+bool use_pdl() {
+  static const bool on = [] {
+    const char* v = std::getenv("DQMK_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int enqueue_step(dqmk_context* x) {
   const char* api = "ForwardToken";
+  const bool pdl = use_pdl();
   dqmk_model* m = x->m;
   const dqmk_model_config& c = m->cfg;
   cudaStream_t s = x->stream;
@@ -491,7 +503,7 @@ int enqueue_step(dqmk_context* x) {
     g.n_kv_heads = c.n_kv_heads;
     g.head_dim = c.head_dim;
     g.neox = c.rope_neox;
-    DQMK_CUDA_RET(api, launch_gemv(g, s, true));
+    DQMK_CUDA_RET(api, launch_gemv(g, s, pdl));
 
     AttnArgs at = {};
     at.q = x->q;
@@ -507,7 +519,7 @@ int enqueue_step(dqmk_context* x) {
     at.partials = x->partials;
     at.tickets = x->attn_tickets();
     at.max_splits = x->attn_splits;
-    DQMK_CUDA_RET(api, launch_attention(at, s, true));
+    DQMK_CUDA_RET(api, launch_attention(at, s, pdl));
 
     GemvArgs o = {};
     o.qtype = L.wo.qtype;
@@ -520,7 +532,7 @@ int enqueue_step(dqmk_context* x) {
     o.epi = kEpiStore;
     o.residual = x->x;
     o.y = x->x;
-    DQMK_CUDA_RET(api, launch_gemv(o, s, true));
+    DQMK_CUDA_RET(api, launch_gemv(o, s, pdl));
 
     GemvArgs gu = {};
     gu.qtype = L.gate_up.qtype;
@@ -534,7 +546,7 @@ int enqueue_step(dqmk_context* x) {
     gu.eps = c.rms_norm_eps;
     gu.epi = kEpiSwiGlu;
     gu.y = x->h;
-    DQMK_CUDA_RET(api, launch_gemv(gu, s, true));
+    DQMK_CUDA_RET(api, launch_gemv(gu, s, pdl));
 
     GemvArgs dn = {};
     dn.qtype = L.down.qtype;
@@ -547,7 +559,7 @@ int enqueue_step(dqmk_context* x) {
     dn.epi = kEpiStore;
     dn.residual = x->x;
     dn.y = x->x;
-    DQMK_CUDA_RET(api, launch_gemv(dn, s, true));
+    DQMK_CUDA_RET(api, launch_gemv(dn, s, pdl));
   }
   GemvArgs lg = {};
   lg.qtype = m->lm_head.qtype;
@@ -567,7 +579,7 @@ int enqueue_step(dqmk_context* x) {
   lg.pos_slot = x->pos_slot();
   lg.history = x->history_dev;
   lg.history_cap = c.max_seq_len;
-  DQMK_CUDA_RET(api, launch_gemv(lg, s, true));
+  DQMK_CUDA_RET(api, launch_gemv(lg, s, pdl));
   return DQMK_OK;
 }
 
@@ -601,6 +613,15 @@ void count_token(dqmk_context* x, int pos) {
   st.kv_cache_write_bytes += (uint64_t)c.n_layers * 2 * c.n_kv_heads * c.head_dim * sizeof(float);
   st.kv_cache_read_bytes +=
       (uint64_t)c.n_layers * (pos + 1) * c.n_heads * c.head_dim * sizeof(float) * 2;
+}
+
+// After a synchronizing call: a bounded device wait that ran out surfaces as
+// DQMK_ERR_TIMEOUT (the flag is cleared so the context stays usable).
+int check_device_error(const char* api) {
+  unsigned int flags = 0;
+  DQMK_CUDA_RET(api, read_device_error(&flags, true));
+  if (flags) return fail(DQMK_ERR_TIMEOUT, std::string(api) + ": a device-side wait timed out");
+  return DQMK_OK;
 }
 
 int validate_token(const dqmk_context* x, int token, int pos) {
@@ -727,7 +748,7 @@ extern "C" int dqmk_forward_token(dqmk_context* x, int token, int pos, float* lo
     x->m->stats.device_to_host_bytes += bytes;
   }
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
-  return DQMK_OK;
+  return check_device_error(api);
 }
 
 extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int* positions, int n,
@@ -753,7 +774,7 @@ extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int*
     x->m->stats.device_to_host_bytes += bytes;
   }
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
-  return DQMK_OK;
+  return check_device_error(api);
 }
 
 extern "C" int dqmk_decode_enqueue(dqmk_context* x, int token, int pos, int n_steps) {
@@ -787,5 +808,5 @@ extern "C" int dqmk_decode_greedy(dqmk_context* x, int token, int pos, int n_ste
   x->history.push_back(token);
   for (int i = 0; i + 1 < n_steps && tokens_out; ++i) x->history.push_back(tokens_out[i]);
   x->pos = pos + n_steps - 1;
-  return DQMK_OK;
+  return check_device_error(api);
 }

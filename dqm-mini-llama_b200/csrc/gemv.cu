@@ -265,11 +265,11 @@ constexpr int kNormRegs = 8;  // float4 of RMSNorm weight prefetched per thread
 // normalised when norm_w is set.  One global round trip: every thread issues
 // all of its loads before using any.  Activations come from the previous
 // kernel of the chain, so they are read through L2 (ld.global.cg).
-template <int QT>
-__device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const float4 (&nw)[kNormRegs],
+template <int QT, int NWARPS, int NR>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const float4 (&nw)[NR],
                                         bool norm_pref, float* red, float* bcast) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  constexpr int NT = kWarps * 32;
+  constexpr int NT = NWARPS * 32;
   float* xsf = reinterpret_cast<float*>(xs);
   const int nf4 = a.kp >> 2;
   const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.k & 3) == 0);
@@ -310,7 +310,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const flo
     __syncthreads();
     if (tid == 0) {
       float t = 0.0f;
-      for (int w = 0; w < kWarps; ++w) t += red[w];
+      for (int w = 0; w < NWARPS; ++w) t += red[w];
       const float mean = __fdiv_rn(t, (float)a.k);
       *bcast = __fdiv_rn(1.0f, sqrtf(__fadd_rn(mean, a.eps)));
     }
@@ -318,7 +318,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const flo
     const float scale = *bcast;
     if (vec && norm_pref) {
 #pragma unroll
-      for (int u = 0; u < kNormRegs; ++u) {
+      for (int u = 0; u < NR; ++u) {
         const int i4 = u * NT + tid;
         if (i4 < (a.k >> 2)) {
           const int e = i4 * 4;
@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
   pdl_trigger();
   pdl_wait();
 
-  stage_x<QT>(a, xs, nw, norm_pref, red, &bcast);
+  stage_x<QT, kWarps, kNormRegs>(a, xs, nw, norm_pref, red, &bcast);
 
   int pos = 0;
   if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
@@ -524,6 +524,512 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   X(DQMK_Q40, 2, 1, 1) X(DQMK_Q40, 4, 1, 1) X(DQMK_Q40, 2, 2, 1) X(DQMK_Q40, 4, 2, 1)       \
   X(DQMK_Q40, 2, 2, 4) X(DQMK_Q40, 2, 4, 4) X(DQMK_Q40, 4, 2, 4) X(DQMK_Q40, 4, 4, 4)
 
+// ============================================================ TMA-staged GEMV
+// Weights stream through a ring of shared-memory stages filled by bulk
+// asynchronous copies (cp.async.bulk, completion counted on an mbarrier), so
+// the bytes in flight cost shared memory instead of registers.  A CTA owns
+// tiles of TR = 8 warps x RPW contiguous rows; its first `nstage` tiles are
+// requested before griddepcontrol.wait, so under programmatic dependent
+// launch they arrive while the previous kernel of the chain still runs.
+// Every wait on a stage is bounded (about a second of %globaltimer); on
+// timeout the CTA records DQMK_ERR_TIMEOUT in a device flag, stops issuing,
+// waits (bounded) for its copies still in flight, and exits.
+constexpr int kTmaWarps = 8;
+constexpr int kTmaThreads = kTmaWarps * 32;
+constexpr int kMaxStages = 4;
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;
+
+__device__ unsigned int g_device_error;  // bit 0: a bounded wait timed out
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// true when the phase completed, false after kWaitLimitNs
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// global -> shared bulk copy completing on `bar`; 16-byte aligned, size % 16 == 0
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+struct TmaGeo {
+  int chunks, row_bytes, nbk, n_tiles, my_tiles;
+  size_t q_stage, stage_bytes;  // bytes of one stage's quants, of the whole stage
+};
+
+// Issue the copies of local tile i into stage s (thread 0 only).  Returns
+// whether the stage now has a copy in flight.
+template <int QT, int RPW>
+__device__ __forceinline__ bool tma_issue(const GemvArgs& a, const TmaGeo& g, unsigned char* stages,
+                                          uint64_t* full, int i, int s, uint64_t policy,
+                                          int skip_tile) {
+  constexpr int TR = kTmaWarps * RPW;
+  const int tile = blockIdx.x + i * gridDim.x;
+  const int r0 = tile * TR;
+  const int rows = min(TR, a.n_rows - r0);
+  const uint32_t qbytes = (uint32_t)rows * g.row_bytes;
+  const uint32_t dbytes = (uint32_t)rows * g.nbk * 2;
+  const uint32_t dbulk = (dbytes & 15u) == 0 ? dbytes : 0u;  // ragged tail: scales read directly
+  if (tile == skip_tile) return false;  // failure-detection hook: nothing arrives
+  unsigned char* st = stages + (size_t)s * g.stage_bytes;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_expect_tx(&full[s], qbytes + dbulk);
+  bulk_g2s(st, a.qs + (size_t)r0 * g.row_bytes, qbytes, &full[s], policy);
+  if (dbulk)
+    bulk_g2s(st + g.q_stage, reinterpret_cast<const unsigned char*>(a.d) + (size_t)r0 * g.nbk * 2,
+             dbulk, &full[s], policy);
+  return true;
+}
+
+// x staged linearly (fp32), RMS-normalised when norm_w is set.  Same single
+// round trip as stage_x; the float values are identical.
+template <int NWARPS, int NR>
+__device__ __forceinline__ void stage_x_linear(const GemvArgs& a, float* xf, const float4 (&nw)[NR],
+                                               bool norm_pref, float* red, float* bcast) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  constexpr int NT = NWARPS * 32;
+  const int nf4 = a.kp >> 2;
+  const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.k & 3) == 0);
+  float4* xf4 = reinterpret_cast<float4*>(xf);
+  float ss = 0.0f;
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    const int k4 = a.k >> 2;
+    for (int base = 0; base < nf4; base += 8 * NT) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i4 = base + u * NT + tid;
+        v[u] = i4 < k4 ? __ldcg(x4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i4 = base + u * NT + tid;
+        if (i4 < nf4) {
+          ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
+          ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
+          ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
+          ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
+          xf4[i4] = v[u];
+        }
+      }
+    }
+  } else {
+    for (int e = tid; e < a.kp; e += NT) {
+      const float v = e < a.k ? __ldcg(a.x + e) : 0.0f;
+      xf[e] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  }
+  if (a.norm_w) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[wid] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.0f;
+      for (int w = 0; w < NWARPS; ++w) t += red[w];
+      *bcast = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float)a.k), a.eps)));
+    }
+    __syncthreads();
+    const float scale = *bcast;
+    if (vec && norm_pref) {
+#pragma unroll
+      for (int u = 0; u < NR; ++u) {
+        const int i4 = u * NT + tid;
+        if (i4 < (a.k >> 2)) {
+          float4 v = xf4[i4];
+          v.x = __fmul_rn(__fmul_rn(v.x, scale), nw[u].x);
+          v.y = __fmul_rn(__fmul_rn(v.y, scale), nw[u].y);
+          v.z = __fmul_rn(__fmul_rn(v.z, scale), nw[u].z);
+          v.w = __fmul_rn(__fmul_rn(v.w, scale), nw[u].w);
+          xf4[i4] = v;
+        }
+      }
+    } else {
+      for (int e = tid; e < a.k; e += NT) xf[e] = __fmul_rn(__fmul_rn(xf[e], scale), a.norm_w[e]);
+    }
+  }
+  __syncthreads();
+}
+
+// Each 32-value block of x as three int8 terms, x ~= s1 q1 + s2 q2 + s3 q3
+// with s1 = absmax/127, s2 = s1/254, s3 = s2/254: every residual fits the next
+// term, and what is left is below 6e-8 of the block's absmax -- float
+// precision.  Eight threads own a block (four values each, one packed int8x4
+// store per term).  Planes [term][half][block][16 bytes] keep the 16-byte
+// reads of a lane-per-block loop conflict-free.  Each term's scale is stored,
+// and for Q4_0 the sum of its 32 values (for the nibble offset of 8).
+template <int NWARPS, bool SUMS>
+__device__ __forceinline__ void quantize_x_terms(const float* xf, int nbk, int8_t* q, float* sc,
+                                                 int* sum) {
+  constexpr int NT = NWARPS * 32;
+  const int tid = threadIdx.x;
+  const int sub = tid & 7;  // which 4 values of the block
+  for (int base = 0; base < nbk * 8; base += NT) {
+    const int b = (base + tid) >> 3;
+    const bool valid = b < nbk;  // uniform per group of 8 lanes
+    float4 v = valid ? reinterpret_cast<const float4*>(xf)[b * 8 + sub]
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    float r[4] = {v.x, v.y, v.z, v.w};
+    float s = m > 0.0f ? __fdiv_rn(m, 127.0f) : 0.0f;
+    const int h = sub >> 2, word = sub & 3;
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+      uint32_t packed = 0;
+      int tsum = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int qq = __float2int_rn(__fmul_rn(r[e], inv));
+        qq = qq > 127 ? 127 : (qq < -127 ? -127 : qq);
+        r[e] = __fmaf_rn(-s, (float)qq, r[e]);
+        packed |= ((uint32_t)qq & 0xffu) << (8 * e);
+        tsum += qq;
+      }
+      if (valid) {
+        reinterpret_cast<uint32_t*>(q)[((size_t)(t * 2 + h) * nbk + b) * 4 + word] = packed;
+        if (sub == 0) sc[t * nbk + b] = s;
+      }
+      if constexpr (SUMS) {
+        tsum += __shfl_xor_sync(0xffffffffu, tsum, 1);
+        tsum += __shfl_xor_sync(0xffffffffu, tsum, 2);
+        tsum += __shfl_xor_sync(0xffffffffu, tsum, 4);
+        if (valid && sub == 0) sum[t * nbk + b] = tsum;
+      }
+      s = __fmul_rn(s, 1.0f / 254.0f);
+    }
+  }
+}
+
+__device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+// Shared-memory layout of the staged x: fp32 copy, int8 term planes, term
+// scales, term sums; the weight stages follow.
+struct XLayout {
+  size_t q, sc, sum, stages;
+};
+__host__ __device__ __forceinline__ XLayout x_layout(int kp) {
+  const size_t nbk = (size_t)kp / 32;
+  XLayout l;
+  l.q = ((size_t)kp * 4 + 15) & ~(size_t)15;
+  l.sc = l.q + ((3 * (size_t)kp + 15) & ~(size_t)15);
+  l.sum = l.sc + ((12 * nbk + 15) & ~(size_t)15);
+  l.stages = l.sum + ((12 * nbk + 15) & ~(size_t)15);
+  return l;
+}
+
+template <int QT, int RPW>
+__global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a, int nstage,
+                                                              int skip_tile) {
+  constexpr int TR = kTmaWarps * RPW;
+  constexpr int NR = 4;  // float4 of RMSNorm weight prefetched per thread
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ float red[kTmaWarps];
+  __shared__ float bcast;
+  __shared__ unsigned long long best_w[kTmaWarps];
+  __shared__ int s_err;
+
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  TmaGeo g;
+  g.chunks = a.kp / Fmt<QT>::kElems;
+  g.row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
+  g.nbk = a.kp / 32;
+  g.n_tiles = (a.n_rows + TR - 1) / TR;
+  g.my_tiles = (int)blockIdx.x < g.n_tiles
+                   ? (g.n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                   : 0;
+  g.q_stage = (size_t)TR * g.row_bytes;
+  g.stage_bytes = g.q_stage + align16((size_t)TR * g.nbk * 2);
+  const XLayout xl = x_layout(a.kp);
+  float* xf = reinterpret_cast<float*>(smem);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + xl.q);
+  float* xsc = reinterpret_cast<float*>(smem + xl.sc);
+  int* xsum = reinterpret_cast<int*>(smem + xl.sum);
+  unsigned char* stages = smem + xl.stages;
+  const uint64_t policy = evict_first_policy();
+
+  if (tid == 0) {
+    for (int s = 0; s < nstage; ++s) mbar_init(&full[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_err = 0;
+  }
+  __syncthreads();
+  unsigned pending = 0;  // stages with a copy in flight (thread 0's bookkeeping)
+  if (tid == 0) {
+    const int pre = min(nstage, g.my_tiles);
+    for (int i = 0; i < pre; ++i)
+      if (tma_issue<QT, RPW>(a, g, stages, full, i, i, policy, skip_tile)) pending |= 1u << i;
+  }
+  float4 nw[NR];
+  const bool norm_pref = a.norm_w && (a.kp >> 2) <= NR * kTmaThreads && ((a.k & 3) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(a.norm_w) & 15u) == 0);
+  if (norm_pref) {
+#pragma unroll
+    for (int u = 0; u < NR; ++u) {
+      const int i4 = u * kTmaThreads + tid;
+      nw[u] = i4 < (a.k >> 2) ? __ldg(reinterpret_cast<const float4*>(a.norm_w) + i4)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  pdl_trigger();
+  pdl_wait();
+
+  stage_x_linear<kTmaWarps, NR>(a, xf, nw, norm_pref, red, &bcast);
+  quantize_x_terms<kTmaWarps, QT == DQMK_Q40>(xf, g.nbk, xq, xsc, xsum);
+  __syncthreads();
+
+  int pos = 0;
+  if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+  unsigned long long best = 0ull;
+  int consumed = 0;
+  const int4* xq4 = reinterpret_cast<const int4*>(xq);
+  for (int i = 0; i < g.my_tiles; ++i) {
+    const int s = i % nstage;
+    const uint32_t phase = (uint32_t)(i / nstage) & 1u;
+    if (!mbar_wait_bounded(&full[s], phase)) s_err = 1;
+    __syncthreads();
+    if (s_err) break;
+    consumed = i + 1;
+    const int tile = blockIdx.x + i * gridDim.x;
+    const int r0 = tile * TR;
+    const int rows = min(TR, a.n_rows - r0);
+    const bool d_smem = (((uint32_t)rows * g.nbk * 2) & 15u) == 0;
+    const unsigned char* sq = stages + (size_t)s * g.stage_bytes;
+    const uint16_t* sd = reinterpret_cast<const uint16_t*>(sq + g.q_stage);
+    float acc[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+    for (int b = lane; b < g.nbk; b += 32) {
+      int4 xv[6];  // [term][half]
+#pragma unroll
+      for (int t = 0; t < 6; ++t) xv[t] = xq4[(size_t)t * g.nbk + b];
+      float sc[3];
+      int sm8[3];
+#pragma unroll
+      for (int t = 0; t < 3; ++t) {
+        sc[t] = xsc[t * g.nbk + b];
+        sm8[t] = QT == DQMK_Q40 ? 8 * xsum[t * g.nbk + b] : 0;
+      }
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int rl = wid * RPW + r;
+        if (rl < rows) {
+          const unsigned char* wrow = sq + (size_t)rl * g.row_bytes;
+          int w[8];
+          if constexpr (QT == DQMK_Q80) {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(wrow + b * 32);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(wrow + b * 32 + 16);
+            w[0] = (int)w0.x; w[1] = (int)w0.y; w[2] = (int)w0.z; w[3] = (int)w0.w;
+            w[4] = (int)w1.x; w[5] = (int)w1.y; w[6] = (int)w1.z; w[7] = (int)w1.w;
+          } else {
+            const uint4 p = *reinterpret_cast<const uint4*>(wrow + b * 16);
+            const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              w[j] = (int)(pw[j] & 0x0f0f0f0fu);             // values 4j..4j+3
+              w[4 + j] = (int)((pw[j] >> 4) & 0x0f0f0f0fu);  // values 16+4j..
+            }
+          }
+          float blk = 0.0f;
+#pragma unroll
+          for (int t = 0; t < 3; ++t) {
+            const int4 lo = xv[t * 2], hi = xv[t * 2 + 1];
+            int S = __dp4a(w[0], lo.x, 0);
+            S = __dp4a(w[1], lo.y, S);
+            S = __dp4a(w[2], lo.z, S);
+            S = __dp4a(w[3], lo.w, S);
+            S = __dp4a(w[4], hi.x, S);
+            S = __dp4a(w[5], hi.y, S);
+            S = __dp4a(w[6], hi.z, S);
+            S = __dp4a(w[7], hi.w, S);
+            blk = __fmaf_rn(sc[t], (float)(S - sm8[t]), blk);
+          }
+          const uint16_t dv =
+              d_smem ? sd[rl * g.nbk + b] : __ldg(a.d + (size_t)(r0 + rl) * g.nbk + b);
+          acc[r] = __fmaf_rn(h2f(dv), blk, acc[r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]);
+    epilogue<RPW>(a, tile * kTmaWarps + wid, lane, acc, pos, best);
+    __syncthreads();  // every warp is done reading stage s
+    if (tid == 0) {
+      pending &= ~(1u << s);
+      if (i + nstage < g.my_tiles &&
+          tma_issue<QT, RPW>(a, g, stages, full, i + nstage, s, policy, skip_tile))
+        pending |= 1u << s;
+    }
+  }
+
+  if (s_err) {
+    // stop cleanly: record the error and let copies still in flight land
+    if (tid == 0) {
+      atomicOr(&g_device_error, 1u);
+      for (int i = consumed; i < min(consumed + nstage, g.my_tiles); ++i) {
+        const int s = i % nstage;
+        if (pending & (1u << s)) mbar_wait_bounded(&full[s], (uint32_t)(i / nstage) & 1u);
+      }
+    }
+    return;
+  }
+
+  if (a.epi == kEpiLogits) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) best_w[wid] = best;
+    __syncthreads();
+    if (tid == 0 && a.argmax_slot) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < kTmaWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
+      atomicMax(a.argmax_slot, b);
+      __threadfence();
+      const unsigned int done = atomicAdd(a.ticket, 1u);
+      if (done == gridDim.x - 1) {
+        __threadfence();
+        const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
+        const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+        const int p = *a.pos_slot;
+        if (a.history && p >= 0 && p < a.history_cap) a.history[p] = idx;
+        *a.token_slot = idx;
+        *a.pos_slot = p + 1;
+        *a.ticket = 0u;
+      }
+    }
+  }
+}
+
+struct TmaPlan {
+  int rpw, stages, grid;
+  size_t smem;
+};
+
+size_t tma_stage_bytes(int qtype, int rpw, int kp) {
+  const size_t tr = (size_t)kTmaWarps * rpw;
+  const size_t row = qtype == DQMK_Q80 ? (size_t)kp : (size_t)kp / 2;
+  return tr * row + ((tr * (kp / 32) * 2 + 15) & ~(size_t)15);
+}
+
+// Rows per warp by shape; stages so that (when the grid fits on the GPU at
+// once) every tile of a CTA is requested before the dependency wait; a
+// persistent ring for the very tall lm_head.
+TmaPlan tma_plan(const GemvArgs& a) {
+  TmaPlan p;
+  const bool paired = a.epi == kEpiSwiGlu || a.epi == kEpiQkv;
+  if (paired || a.n_rows >= 4096) p.rpw = 2;
+  else p.rpw = 1;
+  const int tr = kTmaWarps * p.rpw;
+  const int n_tiles = (a.n_rows + tr - 1) / tr;
+  const size_t stage = tma_stage_bytes(a.qtype, p.rpw, a.kp);
+  const size_t xbytes = x_layout(a.kp).stages;
+  const size_t budget = 200 * 1024;
+  const int sms = sm_count();
+  auto per_sm = [&](int stages) {
+    const size_t sm_bytes = xbytes + stages * stage + 1024;
+    int c = (int)(220 * 1024 / sm_bytes);
+    return c < 8 ? c : 8;
+  };
+  p.stages = 1;
+  p.grid = n_tiles;
+  while (p.stages < kMaxStages && p.grid > sms * per_sm(p.stages) &&
+         xbytes + (p.stages + 1) * stage <= budget) {
+    ++p.stages;
+    p.grid = (n_tiles + p.stages - 1) / p.stages;
+  }
+  const int cap = sms * (per_sm(p.stages) > 0 ? per_sm(p.stages) : 1);
+  if (p.grid > cap) p.grid = cap;
+  if (p.grid < 1) p.grid = 1;
+  p.smem = xbytes + p.stages * stage;
+  return p;
+}
+
+template <int QT, int RPW>
+cudaError_t tma_prepare() {
+  return cudaFuncSetAttribute(gemv_tma_kernel<QT, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              210 * 1024);
+}
+
+template <int QT, int RPW>
+cudaError_t tma_launch(const GemvArgs& a, const TmaPlan& p, cudaStream_t stream, bool pdl,
+                       int skip_tile) {
+  static bool prepared = false;
+  if (!prepared) {
+    cudaError_t e = tma_prepare<QT, RPW>();
+    if (e != cudaSuccess) return e;
+    prepared = true;
+  }
+  return launch(gemv_tma_kernel<QT, RPW>, dim3(p.grid), dim3(kTmaThreads), p.smem, stream, pdl,
+                a, p.stages, skip_tile);
+}
+
+#define DQMK_TMA_VARIANTS(X) \
+  X(DQMK_Q80, 1) X(DQMK_Q80, 2) X(DQMK_Q80, 4) X(DQMK_Q40, 1) X(DQMK_Q40, 2) X(DQMK_Q40, 4)
+
+cudaError_t tma_dispatch(const GemvArgs& a, cudaStream_t stream, bool pdl, int skip_tile) {
+  const TmaPlan p = tma_plan(a);
+#define DQMK_TMA_CASE(QT, RPW) \
+  if (a.qtype == QT && p.rpw == RPW) return tma_launch<QT, RPW>(a, p, stream, pdl, skip_tile);
+  DQMK_TMA_VARIANTS(DQMK_TMA_CASE)
+#undef DQMK_TMA_CASE
+  return cudaErrorInvalidValue;
+}
+
+// The TMA form streams the very tall weights (lm_head): there bandwidth
+// decides, and the shared-memory ring keeps more bytes in flight than
+// registers can.  The per-layer projections are latency-bound links of the
+// decode chain; the register-staged form, whose weights are already in
+// registers when the dependency resolves, finishes them sooner.
+bool tma_eligible(const GemvArgs& a) { return a.kp <= 8192 && a.n_rows >= 32768; }
+
 // ------------------------------------------------ ggml-layout compatibility
 // One warp per weight row, blocks read in place (34 / 18 bytes, 2-byte
 // aligned), up to 8 input rows per pass.  Serves the drop-in entry points
@@ -591,6 +1097,23 @@ cudaError_t gemv_prepare() {
   if (e == cudaSuccess) e = prepare_t<QT, RPW, CPL, GW>(nullptr);
   DQMK_GEMV_VARIANTS(DQMK_PREP)
 #undef DQMK_PREP
+#define DQMK_TMA_PREP(QT, RPW) \
+  if (e == cudaSuccess) e = tma_prepare<QT, RPW>();
+  DQMK_TMA_VARIANTS(DQMK_TMA_PREP)
+#undef DQMK_TMA_PREP
+  return e;
+}
+
+cudaError_t launch_gemv_tma_skip(const GemvArgs& a, cudaStream_t stream, int skip_tile) {
+  return tma_dispatch(a, stream, false, skip_tile);
+}
+
+cudaError_t read_device_error(unsigned int* flags, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_device_error, sizeof(unsigned int));
+  if (e == cudaSuccess && clear && *flags) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(unsigned int));
+  }
   return e;
 }
 
@@ -599,6 +1122,7 @@ cudaError_t gemv_prepare() {
 // warp walks a long row alone.  Very tall weights (lm_head) take 4 rows per
 // group to amortise the shared-memory reads of x.
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  if (tma_eligible(a)) return tma_dispatch(a, stream, pdl, -1);
   const bool wide = a.n_rows >= 32768 && a.epi != kEpiSwiGlu && a.epi != kEpiQkv;
   const int chunks = a.qtype == DQMK_Q80 ? a.kp / 16 : a.kp / 32;
   if (a.qtype == DQMK_Q80) {
@@ -710,5 +1234,41 @@ extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, cons
   a.residual = residual;
   a.y = y;
   DQMK_CUDA_RET(api, launch_gemv(a, static_cast<cudaStream_t>(stream), false));
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_device_error(int clear) {
+  unsigned int flags = 0;
+  cudaError_t e = read_device_error(&flags, clear != 0);
+  if (e != cudaSuccess) {
+    cuda_fail("dqmk_device_error", e);
+    return -1;
+  }
+  return (int)flags;
+}
+
+extern "C" int dqmk_gemv_packed_withhold_tile(int qtype, const float* x, int in_features,
+                                              const void* packed, int out_features, float* y,
+                                              int tile, void* stream) {
+  const char* api = "dqmk_gemv_packed_withhold_tile";
+  if (qtype != DQMK_Q80 && qtype != DQMK_Q40)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": unsupported quant type");
+  if (in_features <= 0 || out_features <= 0 || !x || !packed || !y)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid argument");
+  if (reinterpret_cast<uintptr_t>(packed) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": packed weight must be 16-byte aligned");
+  const int kp = (in_features + 31) / 32 * 32;
+  if (kp > 8192) return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": in_features too large");
+  GemvArgs a = {};
+  a.qtype = qtype;
+  a.qs = static_cast<const uint8_t*>(packed);
+  a.d = reinterpret_cast<const uint16_t*>(a.qs + (size_t)out_features * (qtype == DQMK_Q80 ? kp : kp / 2));
+  a.n_rows = out_features;
+  a.k = in_features;
+  a.kp = kp;
+  a.x = x;
+  a.epi = kEpiStore;
+  a.y = y;
+  DQMK_CUDA_RET(api, launch_gemv_tma_skip(a, static_cast<cudaStream_t>(stream), tile));
   return DQMK_OK;
 }

@@ -79,6 +79,11 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
 // Sets kernel attributes of every GEMV / attention instantiation; call
 // outside stream capture.
 cudaError_t gemv_prepare();
+// Failure-detection hook: the TMA GEMV with the copies of one tile withheld,
+// so that tile's bounded wait runs out and sets the device error flag.
+cudaError_t launch_gemv_tma_skip(const GemvArgs& a, cudaStream_t stream, int skip_tile);
+// Device error flags set by bounded waits (bit 0: timeout); optionally cleared.
+cudaError_t read_device_error(unsigned int* flags, bool clear);
 cudaError_t attention_prepare();
 
 // ggml-layout Linear (compatibility entry point), rows >= 1.

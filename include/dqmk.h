@@ -114,6 +114,22 @@ int dqmk_gemv_packed(int qtype, const float* x_dev, int in_features, const void*
                      int out_features, const float* bias_dev, const float* residual_dev,
                      float* y_dev, void* stream);
 
+/* Failure detection.  Kernels that wait on asynchronous copies bound every
+ * wait (about one second); a wait that runs out records a flag in device
+ * memory and the kernel exits instead of hanging.  dqmk_device_error returns
+ * the flags (bit 0: a bounded wait timed out; -1 if the read itself failed)
+ * and clears them when `clear` != 0.  The engine's synchronous calls check
+ * the flag and return DQMK_ERR_TIMEOUT.  No reference counterpart: the
+ * reference has no device-side waits. */
+int dqmk_device_error(int clear);
+
+/* Test hook for the above: dqmk_gemv_packed with the shared-memory copies of
+ * one row tile (tile index `tile`, 8-32 rows) withheld, so that tile's wait
+ * runs out.  Outputs are undefined; the device error flag is set. */
+int dqmk_gemv_packed_withhold_tile(int qtype, const float* x_dev, int in_features,
+                                   const void* packed_dev, int out_features, float* y_dev,
+                                   int tile, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Memory-bound ops                                                     */
 /* ------------------------------------------------------------------ */
