@@ -15,6 +15,7 @@
 //     every step; greedy decoding advances them on the device.
 // Runtime counters follow the reference's per-logical-op accounting
 // (src/forward.cc:97-165) so the engine's counter tests still hold.
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -25,6 +26,7 @@
 
 #include "dqmk.h"
 #include "internal.h"
+#include "prefill.h"
 
 using namespace dqmk;
 
@@ -40,6 +42,7 @@ struct Packed {
     const size_t qb = (size_t)rows * (qtype == DQMK_Q80 ? kp : kp / 2);
     return reinterpret_cast<const uint16_t*>(base + qb);
   }
+  int row_bytes_q8() const { return kp; }
 };
 
 struct Raw {
@@ -54,6 +57,20 @@ struct Layer {
   float* qkv_bias = nullptr;  // packed (paired) row order
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
+  // batched prefill: weight scales transposed to [kp/32][rows] fp32, and the
+  // TMA maps of the quant planes
+  float *dwt_qkv = nullptr, *dwt_o = nullptr, *dwt_gu = nullptr, *dwt_dn = nullptr;
+  CUtensorMap map_qkv, map_o, map_gu, map_dn;
+};
+
+// Per-context buffers of the batched prefill, allocated on first use.
+struct PrefillBufs {
+  int m_max = 0;  // rows, a multiple of 128
+  float *x = nullptr, *q = nullptr, *att = nullptr, *f = nullptr;
+  int8_t* qx = nullptr;  // [2][m_max][kp]
+  float* sx = nullptr;   // [2][m_max][kp/32]
+  int* tokens = nullptr;
+  CUtensorMap a_dim[2], a_qd[2], a_hid[2];
 };
 
 }  // namespace
@@ -67,6 +84,7 @@ struct dqmk_model {
   std::vector<Layer> layers;
   Packed embd, lm_head;
   bool tied = true;
+  bool prefill_ready = false;  // scales transposed and TMA maps built
   float* final_norm = nullptr;
   float2* rope_cs = nullptr;
   std::vector<void*> allocs;
@@ -93,6 +111,7 @@ struct dqmk_context {
   int* pinned = nullptr;  // host staging: [token, pos]
   cudaEvent_t staged = nullptr;  // recorded after the last copy out of `pinned`
   int attn_splits = 1;
+  PrefillBufs pf;
   cudaGraphExec_t graph = nullptr;
   int pos = 0;
   std::vector<int> history;
@@ -413,6 +432,40 @@ extern "C" int dqmk_model_finalize(dqmk_model* m) {
       if ((rc = upload_f32(m, perm, &L.qkv_bias, api))) return rc;
     }
   }
+  // batched-prefill side tables (see prefill.cu); skipped for head sizes the
+  // prefill attention kernel does not take, which then prefill token by token
+  if (hd == 64 || hd == 128) {
+    auto side = [&](const Packed& w, float** dwt, CUtensorMap* map) -> int {
+      const int nbk = w.kp / 32;
+      void* p = nullptr;
+      int r = dev_alloc(m->allocs, (size_t)w.rows * nbk * sizeof(float), &p, api);
+      if (r) return r;
+      *dwt = static_cast<float*>(p);
+      cudaError_t e = launch_transpose_scales(w.d(), w.rows, nbk, *dwt, nullptr);
+      if (e != cudaSuccess) return cuda_fail(api, e);
+      return make_i8_tile_map(map, w.qs(), w.rows, w.row_bytes_q8());
+    };
+    // the GEMM tiles 128 weight rows at a time and reads 16-byte vectors of
+    // the activation rows
+    bool ok = m->qtype == DQMK_Q80 && c.dim % 4 == 0;
+    for (int l = 0; ok && l < c.n_layers; ++l) {
+      const Layer& L = m->layers[l];
+      for (const Packed* w : {&L.qkv, &L.wo, &L.gate_up, &L.down}) ok = ok && w->rows % 128 == 0;
+    }
+    for (int l = 0; ok && l < c.n_layers; ++l) {
+      Layer& L = m->layers[l];
+      if ((rc = side(L.qkv, &L.dwt_qkv, &L.map_qkv))) return rc;
+      if ((rc = side(L.wo, &L.dwt_o, &L.map_o))) return rc;
+      if ((rc = side(L.gate_up, &L.dwt_gu, &L.map_gu))) return rc;
+      if ((rc = side(L.down, &L.dwt_dn, &L.map_dn))) return rc;
+    }
+    if (ok) {
+      cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) return cuda_fail(api, e);
+    }
+    m->prefill_ready = ok;
+  }
+
   // RoPE table for every cache position
   std::vector<float2> cs((size_t)c.max_seq_len * (hd / 2));
   rope_table(c.rope_theta, hd, 0, c.max_seq_len, cs.data());
@@ -654,6 +707,196 @@ int launch_token(dqmk_context* x, int token, int pos) {
   return DQMK_OK;
 }
 
+// ------------------------------------------------------------ batched prefill
+// A prompt of consecutive positions runs layer by layer over all its tokens
+// (chunks of up to PrefillBufs::m_max rows): every projection is one int8
+// tensor-core GEMM, attention is causal over the cache.  DQMK_PREFILL=0 in
+// the environment replays the decode graph per token instead.
+bool prefill_enabled() {
+  const char* v = std::getenv("DQMK_PREFILL");
+  return !(v && v[0] == '0');
+}
+
+int ensure_prefill(dqmk_context* x) {
+  PrefillBufs& b = x->pf;
+  if (b.m_max) return DQMK_OK;
+  const char* api = "ForwardBatch";
+  const dqmk_model* m = x->m;
+  const dqmk_model_config& c = m->cfg;
+  const Layer& L0 = m->layers[0];
+  const int qd = c.n_heads * c.head_dim;
+  const int kp_dim = L0.qkv.kp, kp_qd = L0.wo.kp, kp_hid = L0.down.kp;
+  const int kp_max = std::max(kp_dim, std::max(kp_qd, kp_hid));
+  const int m_max = std::min(1024, (c.max_seq_len + 127) / 128 * 128);
+  void* p = nullptr;
+  int rc;
+  struct {
+    void** dst;
+    size_t bytes;
+  } bufs[] = {{(void**)&b.x, (size_t)m_max * c.dim * sizeof(float)},
+              {(void**)&b.q, (size_t)m_max * qd * sizeof(float)},
+              {(void**)&b.att, (size_t)m_max * qd * sizeof(float)},
+              {(void**)&b.f, (size_t)m_max * c.hidden_dim * sizeof(float)},
+              {(void**)&b.qx, (size_t)2 * m_max * kp_max},
+              {(void**)&b.sx, (size_t)2 * m_max * (kp_max / 32) * sizeof(float)},
+              {(void**)&b.tokens, (size_t)m_max * sizeof(int)}};
+  for (auto& e : bufs) {
+    if ((rc = dev_alloc(x->allocs, e.bytes, &p, api))) return rc;
+    DQMK_CUDA_RET(api, cudaMemset(p, 0, e.bytes));
+    *e.dst = p;
+  }
+  struct {
+    CUtensorMap* maps;
+    int kp;
+  } ks[] = {{b.a_dim, kp_dim}, {b.a_qd, kp_qd}, {b.a_hid, kp_hid}};
+  for (auto& k : ks)
+    for (int t = 0; t < 2; ++t)
+      if ((rc = make_i8_tile_map(&k.maps[t], b.qx + (size_t)t * m_max * k.kp, m_max, k.kp)))
+        return rc;
+  DQMK_CUDA_RET(api, prefill_prepare());
+  b.m_max = m_max;
+  return DQMK_OK;
+}
+
+// One chunk: tokens[0..n) at positions pos0 .. pos0+n-1 (n <= m_max).  With
+// want_logits the final-norm lm_head runs on the last row into x->logits.
+int prefill_chunk(dqmk_context* x, const int* tokens, int pos0, int n, bool want_logits) {
+  const char* api = "ForwardBatch";
+  dqmk_model* m = x->m;
+  const dqmk_model_config& c = m->cfg;
+  PrefillBufs& b = x->pf;
+  cudaStream_t s = x->stream;
+  const int qd = c.n_heads * c.head_dim;
+  const float eps = c.rms_norm_eps;
+  // a copy from pageable memory is staged by the driver before it returns
+  DQMK_CUDA_RET(api, cudaMemcpyAsync(b.tokens, tokens, n * sizeof(int), cudaMemcpyHostToDevice, s));
+  DQMK_CUDA_RET(api, launch_embed_rows(m->embd.qtype, m->embd.qs(), m->embd.d(), c.dim,
+                                       m->embd.kp, b.tokens, n, b.x, s));
+  for (int l = 0; l < c.n_layers; ++l) {
+    const Layer& L = m->layers[l];
+    // attention block: RMSNorm + quantize, fused QKV GEMM (bias, RoPE, cache
+    // store), causal attention, O GEMM + residual
+    DQMK_CUDA_RET(api, launch_quantize_rows(b.x, n, c.dim, L.qkv.kp, c.dim, L.attn_norm, eps,
+                                            b.m_max, b.qx, b.sx, s));
+    PrefillGemm g = {};
+    g.m = n;
+    g.m_pad = b.m_max;
+    g.n = L.qkv.rows;
+    g.kp = L.qkv.kp;
+    g.sx = b.sx;
+    g.dwt = L.dwt_qkv;
+    g.epi = kEpiQkv;
+    g.bias = L.qkv_bias;
+    g.rope_cs = m->rope_cs;
+    g.pos0 = pos0;
+    g.q_out = b.q;
+    g.ldq = qd;
+    g.k_cache = x->keys;
+    g.v_cache = x->values;
+    g.layer = l;
+    g.max_seq = c.max_seq_len;
+    g.n_heads = c.n_heads;
+    g.n_kv_heads = c.n_kv_heads;
+    g.head_dim = c.head_dim;
+    g.neox = c.rope_neox;
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_dim[0], b.a_dim[1], L.map_qkv, g, s));
+
+    PrefillAttn a = {};
+    a.q = b.q;
+    a.ldq = qd;
+    a.keys = x->keys;
+    a.values = x->values;
+    a.out = b.att;
+    a.ldo = qd;
+    a.m = n;
+    a.pos0 = pos0;
+    a.layer = l;
+    a.max_seq = c.max_seq_len;
+    a.n_heads = c.n_heads;
+    a.n_kv_heads = c.n_kv_heads;
+    a.head_dim = c.head_dim;
+    DQMK_CUDA_RET(api, launch_attention_prefill(a, s));
+
+    DQMK_CUDA_RET(api, launch_quantize_rows(b.att, n, qd, L.wo.kp, qd, nullptr, eps, b.m_max,
+                                            b.qx, b.sx, s));
+    PrefillGemm o = {};
+    o.m = n;
+    o.m_pad = b.m_max;
+    o.n = L.wo.rows;
+    o.kp = L.wo.kp;
+    o.sx = b.sx;
+    o.dwt = L.dwt_o;
+    o.epi = kEpiStore;
+    o.residual = b.x;
+    o.y = b.x;
+    o.ldy = c.dim;
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_qd[0], b.a_qd[1], L.map_o, o, s));
+
+    // feed-forward block: RMSNorm + quantize, gate/up GEMM with SwiGLU,
+    // down GEMM + residual
+    DQMK_CUDA_RET(api, launch_quantize_rows(b.x, n, c.dim, L.gate_up.kp, c.dim, L.ffn_norm, eps,
+                                            b.m_max, b.qx, b.sx, s));
+    PrefillGemm gu = {};
+    gu.m = n;
+    gu.m_pad = b.m_max;
+    gu.n = L.gate_up.rows;
+    gu.kp = L.gate_up.kp;
+    gu.sx = b.sx;
+    gu.dwt = L.dwt_gu;
+    gu.epi = kEpiSwiGlu;
+    gu.y = b.f;
+    gu.ldy = c.hidden_dim;
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_dim[0], b.a_dim[1], L.map_gu, gu, s));
+
+    DQMK_CUDA_RET(api, launch_quantize_rows(b.f, n, c.hidden_dim, L.down.kp, c.hidden_dim,
+                                            nullptr, eps, b.m_max, b.qx, b.sx, s));
+    PrefillGemm dn = {};
+    dn.m = n;
+    dn.m_pad = b.m_max;
+    dn.n = L.down.rows;
+    dn.kp = L.down.kp;
+    dn.sx = b.sx;
+    dn.dwt = L.dwt_dn;
+    dn.epi = kEpiStore;
+    dn.residual = b.x;
+    dn.y = b.x;
+    dn.ldy = c.dim;
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_hid[0], b.a_hid[1], L.map_dn, dn, s));
+  }
+  if (!want_logits) return DQMK_OK;
+  // lm_head on the last row; the greedy state then points past it
+  int rc = stage_token(x, tokens[n - 1], pos0 + n - 1, api);
+  if (rc) return rc;
+  DQMK_CUDA_RET(api, cudaMemsetAsync(x->argmax_slot(), 0, sizeof(unsigned long long), s));
+  GemvArgs lg = {};
+  lg.qtype = m->lm_head.qtype;
+  lg.qs = m->lm_head.qs();
+  lg.d = m->lm_head.d();
+  lg.n_rows = m->lm_head.rows;
+  lg.k = m->lm_head.k;
+  lg.kp = m->lm_head.kp;
+  lg.x = b.x + (size_t)(n - 1) * c.dim;
+  lg.norm_w = m->final_norm;
+  lg.eps = c.rms_norm_eps;
+  lg.epi = kEpiLogits;
+  lg.y = x->logits;
+  lg.argmax_slot = x->argmax_slot();
+  lg.ticket = x->lm_ticket();
+  lg.token_slot = x->token_slot();
+  lg.pos_slot = x->pos_slot();
+  lg.history = x->history_dev;
+  lg.history_cap = c.max_seq_len;
+  DQMK_CUDA_RET(api, launch_gemv(lg, s, false));
+  return DQMK_OK;
+}
+
+int check_prefill_error(const char* api) {
+  unsigned int flags = 0;
+  DQMK_CUDA_RET(api, read_prefill_error(&flags, true));
+  if (flags) return fail(DQMK_ERR_TIMEOUT, std::string(api) + ": a device-side wait timed out");
+  return DQMK_OK;
+}
+
 }  // namespace
 
 extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
@@ -761,11 +1004,26 @@ extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int*
   for (int i = 0; i < n; ++i)
     if ((rc = validate_token(x, tokens[i], positions[i]))) return rc;
   cudaSetDevice(x->m->device);
-  if ((rc = ensure_graph(x))) return rc;
-  for (int i = 0; i < n; ++i) {
-    x->pos = positions[i];
-    if ((rc = launch_token(x, tokens[i], positions[i]))) return rc;
-    x->history.push_back(tokens[i]);
+  bool consecutive = true;
+  for (int i = 1; i < n && consecutive; ++i) consecutive = positions[i] == positions[0] + i;
+  if (n > 1 && consecutive && x->m->prefill_ready && prefill_enabled()) {
+    if ((rc = ensure_prefill(x))) return rc;
+    for (int i0 = 0; i0 < n; i0 += x->pf.m_max) {
+      const int cnt = std::min(x->pf.m_max, n - i0);
+      if ((rc = prefill_chunk(x, tokens + i0, positions[i0], cnt, i0 + cnt == n))) return rc;
+    }
+    for (int i = 0; i < n; ++i) {
+      count_token(x, positions[i]);
+      x->history.push_back(tokens[i]);
+    }
+    x->pos = positions[n - 1];
+  } else {
+    if ((rc = ensure_graph(x))) return rc;
+    for (int i = 0; i < n; ++i) {
+      x->pos = positions[i];
+      if ((rc = launch_token(x, tokens[i], positions[i]))) return rc;
+      x->history.push_back(tokens[i]);
+    }
   }
   if (logits) {
     const size_t bytes = (size_t)x->m->cfg.vocab_size * sizeof(float);
@@ -774,6 +1032,7 @@ extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int*
     x->m->stats.device_to_host_bytes += bytes;
   }
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  if ((rc = check_prefill_error(api))) return rc;
   return check_device_error(api);
 }
 

@@ -13,8 +13,11 @@ tests and bench.py regenerate on any machine, and stores its outputs:
                         prompt ids, then 64 greedy decode steps; the tokens,
                         each step's top-1/top-2 logit margin and top-5, plus
                         sha256 digests of reference-quantized weight blocks.
+  qwen2_0_5b_q4_0_ctx2048.json  Qwen2-0.5B-architecture with ggml-convention
+                        Q4_0 weights: a 2048-id random prompt fills the KV cache,
+                        then 128 greedy steps (same fields).
 
-Usage: python tests/golden/make_golden.py [--skip-full]
+Usage: python tests/golden/make_golden.py [--skip-full] [--q4-long]
 """
 from __future__ import annotations
 
@@ -118,11 +121,51 @@ def make_full(threads: int):
     print(json.dumps(res["seconds"]))
 
 
+def make_q4_long(threads: int):
+    t0 = time.time()
+    seed, prompt_seed, n_prompt, n_steps = 20261202, 3, 2048, 128
+    w = S.make_model(S.QWEN2_0_5B, S.Q40, seed)
+    rm = O.RefModel(w, n_prompt + n_steps, threads=threads)
+    prompt = S.prompt_tokens(w.cfg["vocab"], n_prompt, prompt_seed)
+    t1 = time.time()
+    logits = rm.forward_batch(prompt, 0)
+    t2 = time.time()
+    tokens, margins, top5 = [], [], []
+    pos = n_prompt
+    for step in range(n_steps):
+        order = np.argsort(-logits, kind="stable")[:5]
+        nxt = int(order[0])
+        tokens.append(nxt)
+        margins.append(float(logits[order[0]] - logits[order[1]]))
+        top5.append([[int(k), float(logits[k])] for k in order])
+        if step + 1 < n_steps:
+            logits = rm.forward_batch([nxt], pos)
+            pos += 1
+    t3 = time.time()
+    res = {
+        "workload": "qwen2-0.5b-architecture, random-init N(0,0.02), Q4_0 (ggml convention), "
+                    "tied embeddings; 2048 prompt ids then 128 greedy steps",
+        "model_seed": seed, "prompt_seed": prompt_seed, "n_prompt": n_prompt,
+        "prompt_sha256": digest(prompt), "greedy_tokens": tokens, "top1_top2_margin": margins,
+        "top5": top5, "digests": {"token_embd": digest(w.token_embd),
+                                  "layers.0.wq": digest(w.layers[0].wq)},
+        "reference_threads": threads,
+        "seconds": {"build": t1 - t0, "prefill_2048": t2 - t1, "decode_128": t3 - t2},
+    }
+    with open(os.path.join(HERE, "qwen2_0_5b_q4_0_ctx2048.json"), "w") as f:
+        json.dump(res, f, indent=1)
+    print(json.dumps(res["seconds"]))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-full", action="store_true")
+    ap.add_argument("--q4-long", action="store_true")
     ap.add_argument("--threads", type=int, default=os.cpu_count())
     args = ap.parse_args()
+    if args.q4_long:
+        make_q4_long(args.threads)
+        return
     make_gemv()
     make_mini()
     if not args.skip_full:

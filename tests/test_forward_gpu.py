@@ -7,6 +7,7 @@ of the reference logits).  Greedy decoding must produce identical tokens; the
 smallest top-1/top-2 margin of each run is reported alongside.
 """
 import json
+import os
 
 import numpy as np
 import pytest
@@ -57,7 +58,11 @@ def test_forward_batch_semantics(pkg, mini, cuda):
     for i, t in enumerate(toks):
         manual_logits = manual.ForwardToken(t, i)
     batched = pkg.Context(model)
-    batch_logits = batched.ForwardBatch(toks, 0)
+    os.environ["DQMK_PREFILL"] = "0"  # per-token replays: bit-identical to ForwardToken
+    try:
+        batch_logits = batched.ForwardBatch(toks, 0)
+    finally:
+        del os.environ["DQMK_PREFILL"]
     assert np.array_equal(batch_logits, manual_logits)
     assert batched.token_history == toks and batched.pos == 5
     assert manual.token_history == [] and manual.pos == 0  # ForwardToken touches neither

@@ -1,0 +1,121 @@
+"""GPU parity of the batched prefill (ForwardBatch over consecutive positions).
+
+The reference's ForwardBatch runs ForwardToken once per token
+(src/batch.cc:35-40).  Here a prompt runs layer by layer as int8
+tensor-core GEMMs (tcgen05, two-term int8 activations, per-block scale
+epilogue) plus causal attention, so its logits and KV cache are compared
+with the reference within the logit tolerance (max |logit - ref| <= 1e-3 x
+the reference's logit range), and decoding after it must continue exactly
+as the reference does.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import golden_path
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3
+
+
+def check_logits(got, ref, label):
+    rng = float(ref.max() - ref.min())
+    err = float(np.abs(got - ref).max())
+    assert err <= LOGIT_TOL * rng, f"{label}: max err {err:.3e} > {LOGIT_TOL} * range {rng:.3f}"
+    return err / rng
+
+
+@pytest.fixture(scope="module")
+def mini_q8(pkg, S, cuda):
+    return S.make_model(S.QWEN2_MINI, pkg.Q80, 2024,
+                        quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+
+
+class per_token_path:
+    """DQMK_PREFILL=0: ForwardBatch replays the decode graph per token."""
+
+    def __enter__(self):
+        self.old = os.environ.get("DQMK_PREFILL")
+        os.environ["DQMK_PREFILL"] = "0"
+
+    def __exit__(self, *exc):
+        if self.old is None:
+            del os.environ["DQMK_PREFILL"]
+        else:
+            os.environ["DQMK_PREFILL"] = self.old
+
+
+def test_prefill_then_decode_matches_reference_golden(pkg, mini_q8, cuda):
+    """8 prompt tokens batched, then 4 ForwardToken steps that attend over the
+    KV cache the prefill wrote; every logits vector against the reference."""
+    g = np.load(golden_path("mini_model.npz"))
+    toks = g["q1_tokens"]
+    ref = g["q1_logits"]
+    ctx = pkg.Context(pkg.Model.from_synth(mini_q8, max_seq_len=64))
+    worst = check_logits(ctx.ForwardBatch([int(t) for t in toks[:8]], 0), ref[7], "prefill")
+    for i in range(8, len(toks)):
+        worst = max(worst, check_logits(ctx.ForwardToken(int(toks[i]), i), ref[i], f"step {i}"))
+    print(f"worst relative logit error {worst:.2e}")
+
+
+def test_prefill_matches_per_token_path(pkg, mini_q8, cuda):
+    """Batched and per-token ForwardBatch agree (the reference asserts exact
+    equality, tests/batch_test.cc:157-217, because its batch IS per-token; the
+    per-token path here is still exact, the batched one within tolerance)."""
+    model = pkg.Model.from_synth(mini_q8, max_seq_len=64)
+    toks = [1, 104, 101, 108, 108, 111, 7, 900, 3, 44]
+    with per_token_path():
+        a = pkg.Context(model)
+        la = a.ForwardBatch(toks, 0)
+        manual = pkg.Context(model)
+        for i, t in enumerate(toks):
+            lm = manual.ForwardToken(t, i)
+        assert np.array_equal(la, lm)
+    b = pkg.Context(model)
+    lb = b.ForwardBatch(toks, 0)
+    check_logits(lb, la, "batched vs per-token")
+    assert b.token_history == toks and b.pos == len(toks) - 1
+    # the caches agree too: one more token through the decode path
+    check_logits(b.ForwardToken(5, len(toks)), a.ForwardToken(5, len(toks)), "next token")
+
+
+def test_prefill_offset_start_and_second_batch(pkg, mini_q8, orc, cuda):
+    """A batch that starts mid-sequence attends over what earlier calls cached."""
+    model = pkg.Model.from_synth(mini_q8, max_seq_len=64)
+    toks = [9, 8, 7, 6, 5, 4, 3, 2, 1, 10, 11, 12, 13]
+    om = orc.OracleModel(mini_q8, 64)
+    for i, t in enumerate(toks):
+        ref = om.forward_token(t, i)
+    ctx = pkg.Context(model)
+    ctx.ForwardBatch(toks[:5], 0)
+    ctx.ForwardBatch(toks[5:9], 5)
+    check_logits(ctx.ForwardBatch(toks[9:], 9), ref, "three batches")
+
+
+def test_prefill_chunked_long_prompt_matches_reference(pkg, orc, S, mini_q8, cuda):
+    """1100 tokens: two chunks (1024 + 76 rows) of the batched path; last
+    logits against the reference's own ForwardBatch, then 16 greedy steps
+    must equal the reference's."""
+    n, steps = 1100, 16
+    prompt = S.prompt_tokens(mini_q8.cfg["vocab"], n, 5).tolist()
+    rm = orc.RefModel(mini_q8, n + steps)
+    ref = rm.forward_batch(prompt, 0)
+    ref_tokens, tok, margins = [], None, []
+    lg = ref
+    for i in range(steps):
+        top2 = np.sort(lg)[-2:]
+        margins.append(float(top2[1] - top2[0]))
+        tok = int(np.argmax(lg))
+        ref_tokens.append(tok)
+        if i + 1 < steps:
+            lg = rm.forward_batch([tok], n + i)
+    ctx = pkg.Context(pkg.Model.from_synth(mini_q8, max_seq_len=n + steps))
+    got = ctx.ForwardBatch(prompt, 0)
+    print(f"relative logit error {check_logits(got, ref, 'chunked prefill'):.2e}, "
+          f"min margin {min(margins):.2e}")
+    first = int(np.argmax(got))
+    assert first == ref_tokens[0]
+    rest = ctx.decode_greedy(first, n, steps - 1).tolist()
+    assert [first] + rest == ref_tokens
