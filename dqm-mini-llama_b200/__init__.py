@@ -171,6 +171,18 @@ def gemv_packed(qtype: int, x, packed, out_features: int, bias=None, residual=No
     return y
 
 
+def linear_batch_packed(qtype: int, x, packed, out_features: int, bias=None, residual=None,
+                        y=None, stream=None):
+    """x [m, in] (device, float32) times a packed weight on the tensor cores."""
+    torch = _torch()
+    m, k = x.shape
+    if y is None:
+        y = torch.empty(m, out_features, dtype=torch.float32, device=x.device)
+    check(lib().dqmk_linear_batch_packed(qtype, _ptr(x), m, k, _ptr(packed), out_features,
+                                         _ptr(bias), _ptr(residual), _ptr(y), _stream(stream)))
+    return y
+
+
 # ------------------------------------------------------------ ops
 def CudaRmsNormDeviceWeight(x, weight, eps: float):
     torch = _torch()

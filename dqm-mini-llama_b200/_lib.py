@@ -55,6 +55,7 @@ SIGNATURES = {
     "dqmk_packed_bytes": ([_i, _i, _i], _sz),
     "dqmk_pack_weight": ([_i, _vp, _sz, _i, _i, _vp, _vp], _i),
     "dqmk_gemv_packed": ([_i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp], _i),
+    "dqmk_linear_batch_packed": ([_i, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp], _i),
     "dqmk_device_error": ([_i], _i),
     "dqmk_gemv_packed_withhold_tile": ([_i, _vp, _i, _vp, _i, _vp, _i, _vp], _i),
     "dqmk_rmsnorm": ([_vp, _vp, _i, _f, _vp, _vp], _i),

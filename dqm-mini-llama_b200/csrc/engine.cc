@@ -42,7 +42,6 @@ struct Packed {
     const size_t qb = (size_t)rows * (qtype == DQMK_Q80 ? kp : kp / 2);
     return reinterpret_cast<const uint16_t*>(base + qb);
   }
-  int row_bytes_q8() const { return kp; }
 };
 
 struct Raw {
@@ -57,20 +56,21 @@ struct Layer {
   float* qkv_bias = nullptr;  // packed (paired) row order
   float* attn_norm = nullptr;
   float* ffn_norm = nullptr;
-  // batched prefill: weight scales transposed to [kp/32][rows] fp32, and the
-  // TMA maps of the quant planes
-  float *dwt_qkv = nullptr, *dwt_o = nullptr, *dwt_gu = nullptr, *dwt_dn = nullptr;
-  CUtensorMap map_qkv, map_o, map_gu, map_dn;
+  // batched prefill: each weight as two exact fp16 planes (TMA maps {hi, lo})
+  // of its dequantized values scaled per row by 2^-f, and the 2^f
+  float *cs_qkv = nullptr, *cs_o = nullptr, *cs_gu = nullptr, *cs_dn = nullptr;
+  CUtensorMap map_qkv[2], map_o[2], map_gu[2], map_dn[2];
 };
 
 // Per-context buffers of the batched prefill, allocated on first use.
 struct PrefillBufs {
-  int m_max = 0;  // rows, a multiple of 128
+  int m_max = 0;  // rows per chunk
   float *x = nullptr, *q = nullptr, *att = nullptr, *f = nullptr;
-  int8_t* qx = nullptr;  // [2][m_max][kp]
-  float* sx = nullptr;   // [2][m_max][kp/32]
+  uint16_t *hi = nullptr, *lo = nullptr;  // fp16 activation planes [m_max][kp]
+  float* rs = nullptr;                    // their row scales [m_max]
+  float* partial = nullptr;               // split-K partial sums
   int* tokens = nullptr;
-  CUtensorMap a_dim[2], a_qd[2], a_hid[2];
+  CUtensorMap a_dim[2], a_qd[2], a_hid[2];  // {hi, lo} per K
 };
 
 }  // namespace
@@ -435,29 +435,32 @@ extern "C" int dqmk_model_finalize(dqmk_model* m) {
   // batched-prefill side tables (see prefill.cu); skipped for head sizes the
   // prefill attention kernel does not take, which then prefill token by token
   if (hd == 64 || hd == 128) {
-    auto side = [&](const Packed& w, float** dwt, CUtensorMap* map) -> int {
-      const int nbk = w.kp / 32;
+    // the decode path keeps streaming the packed quants; the tensor cores
+    // take the same values as two exact fp16 planes per weight
+    auto side = [&](const Packed& w, float** cs, CUtensorMap* maps) -> int {
       void* p = nullptr;
-      int r = dev_alloc(m->allocs, (size_t)w.rows * nbk * sizeof(float), &p, api);
+      int r = dev_alloc(m->allocs, (size_t)w.rows * sizeof(float), &p, api);
       if (r) return r;
-      *dwt = static_cast<float*>(p);
-      cudaError_t e = launch_transpose_scales(w.d(), w.rows, nbk, *dwt, nullptr);
+      *cs = static_cast<float*>(p);
+      void* planes[2];
+      for (int t = 0; t < 2; ++t) {
+        if ((r = dev_alloc(m->allocs, (size_t)w.rows * w.kp * 2, &planes[t], api))) return r;
+        if ((r = make_f16_tile_map(&maps[t], planes[t], w.rows, w.kp))) return r;
+      }
+      cudaError_t e = launch_weights_split(w.qtype, w.qs(), w.d(), w.rows, w.kp,
+                                           static_cast<uint16_t*>(planes[0]),
+                                           static_cast<uint16_t*>(planes[1]), *cs, nullptr);
       if (e != cudaSuccess) return cuda_fail(api, e);
-      return make_i8_tile_map(map, w.qs(), w.rows, w.row_bytes_q8());
+      return DQMK_OK;
     };
-    // the GEMM tiles 128 weight rows at a time and reads 16-byte vectors of
-    // the activation rows
-    bool ok = m->qtype == DQMK_Q80 && c.dim % 4 == 0;
-    for (int l = 0; ok && l < c.n_layers; ++l) {
-      const Layer& L = m->layers[l];
-      for (const Packed* w : {&L.qkv, &L.wo, &L.gate_up, &L.down}) ok = ok && w->rows % 128 == 0;
-    }
+    // the lm_head GEMV reads the last activation row with 16-byte vectors
+    bool ok = c.dim % 4 == 0;
     for (int l = 0; ok && l < c.n_layers; ++l) {
       Layer& L = m->layers[l];
-      if ((rc = side(L.qkv, &L.dwt_qkv, &L.map_qkv))) return rc;
-      if ((rc = side(L.wo, &L.dwt_o, &L.map_o))) return rc;
-      if ((rc = side(L.gate_up, &L.dwt_gu, &L.map_gu))) return rc;
-      if ((rc = side(L.down, &L.dwt_dn, &L.map_dn))) return rc;
+      if ((rc = side(L.qkv, &L.cs_qkv, L.map_qkv))) return rc;
+      if ((rc = side(L.wo, &L.cs_o, L.map_o))) return rc;
+      if ((rc = side(L.gate_up, &L.cs_gu, L.map_gu))) return rc;
+      if ((rc = side(L.down, &L.cs_dn, L.map_dn))) return rc;
     }
     if (ok) {
       cudaError_t e = cudaDeviceSynchronize();
@@ -727,7 +730,10 @@ int ensure_prefill(dqmk_context* x) {
   const int qd = c.n_heads * c.head_dim;
   const int kp_dim = L0.qkv.kp, kp_qd = L0.wo.kp, kp_hid = L0.down.kp;
   const int kp_max = std::max(kp_dim, std::max(kp_qd, kp_hid));
-  const int m_max = std::min(1024, (c.max_seq_len + 127) / 128 * 128);
+  const int m_max = std::min(1024, c.max_seq_len);
+  size_t part = 0;
+  for (const Packed* w : {&L0.qkv, &L0.wo, &L0.gate_up, &L0.down})
+    part = std::max(part, partial_floats_bound(m_max, w->rows, w->kp));
   void* p = nullptr;
   int rc;
   struct {
@@ -737,22 +743,24 @@ int ensure_prefill(dqmk_context* x) {
               {(void**)&b.q, (size_t)m_max * qd * sizeof(float)},
               {(void**)&b.att, (size_t)m_max * qd * sizeof(float)},
               {(void**)&b.f, (size_t)m_max * c.hidden_dim * sizeof(float)},
-              {(void**)&b.qx, (size_t)2 * m_max * kp_max},
-              {(void**)&b.sx, (size_t)2 * m_max * (kp_max / 32) * sizeof(float)},
+              {(void**)&b.hi, (size_t)m_max * kp_max * 2},
+              {(void**)&b.lo, (size_t)m_max * kp_max * 2},
+              {(void**)&b.rs, (size_t)m_max * sizeof(float)},
+              {(void**)&b.partial, part * sizeof(float)},
               {(void**)&b.tokens, (size_t)m_max * sizeof(int)}};
   for (auto& e : bufs) {
     if ((rc = dev_alloc(x->allocs, e.bytes, &p, api))) return rc;
-    DQMK_CUDA_RET(api, cudaMemset(p, 0, e.bytes));
+    DQMK_CUDA_RET(api, cudaMemset(p, 0, e.bytes ? e.bytes : 16));
     *e.dst = p;
   }
   struct {
     CUtensorMap* maps;
     int kp;
   } ks[] = {{b.a_dim, kp_dim}, {b.a_qd, kp_qd}, {b.a_hid, kp_hid}};
-  for (auto& k : ks)
-    for (int t = 0; t < 2; ++t)
-      if ((rc = make_i8_tile_map(&k.maps[t], b.qx + (size_t)t * m_max * k.kp, m_max, k.kp)))
-        return rc;
+  for (auto& k : ks) {
+    if ((rc = make_f16_tile_map(&k.maps[0], b.hi, m_max, k.kp))) return rc;
+    if ((rc = make_f16_tile_map(&k.maps[1], b.lo, m_max, k.kp))) return rc;
+  }
   DQMK_CUDA_RET(api, prefill_prepare());
   b.m_max = m_max;
   return DQMK_OK;
@@ -774,17 +782,18 @@ int prefill_chunk(dqmk_context* x, const int* tokens, int pos0, int n, bool want
                                        m->embd.kp, b.tokens, n, b.x, s));
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = m->layers[l];
-    // attention block: RMSNorm + quantize, fused QKV GEMM (bias, RoPE, cache
+    // attention block: RMSNorm + fp16 split, fused QKV GEMM (bias, RoPE, cache
     // store), causal attention, O GEMM + residual
-    DQMK_CUDA_RET(api, launch_quantize_rows(b.x, n, c.dim, L.qkv.kp, c.dim, L.attn_norm, eps,
-                                            b.m_max, b.qx, b.sx, s));
+    DQMK_CUDA_RET(api, launch_split_rows(b.x, n, c.dim, L.qkv.kp, c.dim, L.attn_norm, eps, b.hi,
+                                         b.lo, b.rs, s));
     PrefillGemm g = {};
     g.m = n;
-    g.m_pad = b.m_max;
     g.n = L.qkv.rows;
     g.kp = L.qkv.kp;
-    g.sx = b.sx;
-    g.dwt = L.dwt_qkv;
+    g.rs = b.rs;
+    g.partial = b.partial;
+    g.plan = plan_gemm(n, L.qkv.rows, L.qkv.kp);
+    g.cs = L.cs_qkv;
     g.epi = kEpiQkv;
     g.bias = L.qkv_bias;
     g.rope_cs = m->rope_cs;
@@ -799,7 +808,7 @@ int prefill_chunk(dqmk_context* x, const int* tokens, int pos0, int n, bool want
     g.n_kv_heads = c.n_kv_heads;
     g.head_dim = c.head_dim;
     g.neox = c.rope_neox;
-    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_dim[0], b.a_dim[1], L.map_qkv, g, s));
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_dim[0], b.a_dim[1], L.map_qkv[0], L.map_qkv[1], g, s));
 
     PrefillAttn a = {};
     a.q = b.q;
@@ -817,51 +826,54 @@ int prefill_chunk(dqmk_context* x, const int* tokens, int pos0, int n, bool want
     a.head_dim = c.head_dim;
     DQMK_CUDA_RET(api, launch_attention_prefill(a, s));
 
-    DQMK_CUDA_RET(api, launch_quantize_rows(b.att, n, qd, L.wo.kp, qd, nullptr, eps, b.m_max,
-                                            b.qx, b.sx, s));
+    DQMK_CUDA_RET(api, launch_split_rows(b.att, n, qd, L.wo.kp, qd, nullptr, eps, b.hi, b.lo,
+                                         b.rs, s));
     PrefillGemm o = {};
     o.m = n;
-    o.m_pad = b.m_max;
     o.n = L.wo.rows;
     o.kp = L.wo.kp;
-    o.sx = b.sx;
-    o.dwt = L.dwt_o;
+    o.rs = b.rs;
+    o.partial = b.partial;
+    o.plan = plan_gemm(n, L.wo.rows, L.wo.kp);
+    o.cs = L.cs_o;
     o.epi = kEpiStore;
     o.residual = b.x;
     o.y = b.x;
     o.ldy = c.dim;
-    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_qd[0], b.a_qd[1], L.map_o, o, s));
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_qd[0], b.a_qd[1], L.map_o[0], L.map_o[1], o, s));
 
-    // feed-forward block: RMSNorm + quantize, gate/up GEMM with SwiGLU,
+    // feed-forward block: RMSNorm + fp16 split, gate/up GEMM with SwiGLU,
     // down GEMM + residual
-    DQMK_CUDA_RET(api, launch_quantize_rows(b.x, n, c.dim, L.gate_up.kp, c.dim, L.ffn_norm, eps,
-                                            b.m_max, b.qx, b.sx, s));
+    DQMK_CUDA_RET(api, launch_split_rows(b.x, n, c.dim, L.gate_up.kp, c.dim, L.ffn_norm, eps,
+                                         b.hi, b.lo, b.rs, s));
     PrefillGemm gu = {};
     gu.m = n;
-    gu.m_pad = b.m_max;
     gu.n = L.gate_up.rows;
     gu.kp = L.gate_up.kp;
-    gu.sx = b.sx;
-    gu.dwt = L.dwt_gu;
+    gu.rs = b.rs;
+    gu.partial = b.partial;
+    gu.plan = plan_gemm(n, L.gate_up.rows, L.gate_up.kp);
+    gu.cs = L.cs_gu;
     gu.epi = kEpiSwiGlu;
     gu.y = b.f;
     gu.ldy = c.hidden_dim;
-    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_dim[0], b.a_dim[1], L.map_gu, gu, s));
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_dim[0], b.a_dim[1], L.map_gu[0], L.map_gu[1], gu, s));
 
-    DQMK_CUDA_RET(api, launch_quantize_rows(b.f, n, c.hidden_dim, L.down.kp, c.hidden_dim,
-                                            nullptr, eps, b.m_max, b.qx, b.sx, s));
+    DQMK_CUDA_RET(api, launch_split_rows(b.f, n, c.hidden_dim, L.down.kp, c.hidden_dim, nullptr,
+                                         eps, b.hi, b.lo, b.rs, s));
     PrefillGemm dn = {};
     dn.m = n;
-    dn.m_pad = b.m_max;
     dn.n = L.down.rows;
     dn.kp = L.down.kp;
-    dn.sx = b.sx;
-    dn.dwt = L.dwt_dn;
+    dn.rs = b.rs;
+    dn.partial = b.partial;
+    dn.plan = plan_gemm(n, L.down.rows, L.down.kp);
+    dn.cs = L.cs_dn;
     dn.epi = kEpiStore;
     dn.residual = b.x;
     dn.y = b.x;
     dn.ldy = c.dim;
-    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_hid[0], b.a_hid[1], L.map_dn, dn, s));
+    DQMK_CUDA_RET(api, launch_prefill_gemm(b.a_hid[0], b.a_hid[1], L.map_dn[0], L.map_dn[1], dn, s));
   }
   if (!want_logits) return DQMK_OK;
   // lm_head on the last row; the greedy state then points past it

@@ -22,6 +22,7 @@
 // to float rounding (checked against the oracle), not bit for bit.
 #include "common.cuh"
 #include "internal.h"
+#include "prefill.h"
 
 namespace dqmk {
 namespace {
@@ -1238,8 +1239,10 @@ extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, cons
 }
 
 extern "C" int dqmk_device_error(int clear) {
-  unsigned int flags = 0;
+  unsigned int flags = 0, prefill_flags = 0;
   cudaError_t e = read_device_error(&flags, clear != 0);
+  if (e == cudaSuccess) e = read_prefill_error(&prefill_flags, clear != 0);
+  flags |= prefill_flags;
   if (e != cudaSuccess) {
     cuda_fail("dqmk_device_error", e);
     return -1;

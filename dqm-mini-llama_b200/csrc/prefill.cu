@@ -1,32 +1,40 @@
-// prefill.cu -- batched prefill on tcgen05 int8 tensor cores (sm_100a).
+// prefill.cu -- batched prefill on tcgen05 tensor cores (sm_100a).
 //
 // ForwardBatch in the reference runs ForwardToken once per prompt token
 // (src/batch.cc:35-40), re-reading every weight per token.  Here a prompt of M
-// tokens runs each projection as one GEMM, C[M,N] = X[M,K] W[N,K]^T, with the
-// Q8_0 / Q4_0 weights kept as int8 on the tensor cores:
+// tokens runs each projection as one GEMM, C[M,N] = X[M,K] W[N,K]^T, on the
+// tensor cores, with results within fp32 summation-order differences of the
+// F32 reference:
 //
-//   * activations: each 32-value block of a row of X (after its RMSNorm) is
-//     split into two int8 terms, x ~= s1 q1 + s2 q2 (s2 = s1/254; the
-//     residual is below 1.6e-5 of the block's absmax), by quantize_rows;
-//   * the GEMM: per 32-wide K block kb and term t one tcgen05.mma kind::i8
-//     (M=128, N=128, K=32) computes the exact int32 block sums
-//     P[m,n] = sum_j q_t[m,j] qW[n,j] into tensor memory (TMEM);
-//   * per-block scale epilogue: four epilogue warps read each block's two
-//     accumulators back (tcgen05.ld) and fold
-//     acc[m,n] += dW[n,kb] (s1[m,kb] P1 + s2[m,kb] P2) into fp32 registers.
-//     The weight scales differ per block, so int32 sums cannot run across
-//     blocks; TMEM is double-buffered so the tensor core works on block kb+1
-//     while block kb drains.
-//   * operand tiles arrive by TMA (cp.async.bulk.tensor, 128-byte swizzle,
-//     no multicast) through a 3-stage shared-memory ring; one warp issues
-//     TMA, one issues MMAs, four run the epilogue (warp specialisation), all
-//     hand-offs on mbarriers with bounded waits.
+//   * weights: every dequantized weight d*q (fp16 scale times an integer of at
+//     most 8 bits: at most 18 significant bits) is exact as the sum of two
+//     fp16 values once its row is scaled by a power of two 2^-f (row maximum
+//     in [2^14, 2^15)); the planes B_hi, B_lo and the row scales 2^f are
+//     built once per weight;
+//   * activations: each row (after its RMSNorm) is scaled by 2^-e the same way
+//     and split into two fp16 planes, x 2^-e = A_hi + A_lo + r with
+//     |r| <= 2^-22 |x 2^-e|;
+//   * the GEMM: tcgen05.mma kind::f16 (M=128, N=128, K=16) accumulates
+//     A_hi B_hi + A_hi B_lo + A_lo B_hi over the whole K dimension into an
+//     fp32 tensor-memory (TMEM) accumulator (the dropped A_lo B_lo term is
+//     below 2^-22 relative); the epilogue multiplies by 2^(e+f) (exact);
+//   * persistent CTAs walk the output tiles; operand tiles arrive by TMA
+//     (cp.async.bulk.tensor, 128-byte swizzle, no multicast) through a 3-stage
+//     shared-memory ring; one warp issues TMA, one issues MMAs, four drain
+//     the accumulators, with two TMEM accumulators so the epilogue of one
+//     tile overlaps the main loop of the next; all hand-offs on mbarriers with
+//     bounded waits;
+//   * split-K: projections with few output tiles (N = dim) split K across
+//     CTAs so all SMs work; a reduce kernel sums the partial products in a
+//     fixed order (deterministic) and applies the epilogue.
 // Epilogues mirror the decode GEMV's: residual add, SwiGLU of interleaved
 // gate/up columns, QKV bias + RoPE + KV-cache store at each token's position.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "internal.h"
@@ -35,14 +43,15 @@
 namespace dqmk {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 128;  // BK in int8 elements (4 scale blocks)
+constexpr int BM = 128, BN = 128;
+constexpr int BKE = 64;                      // fp16 elements of K per stage
 constexpr int kStages = 3;
-constexpr int kTileBytes = BM * BK;          // 16 KB per operand tile
-constexpr int kStageBytes = 3 * kTileBytes;  // A term 0, A term 1, B
-constexpr int kEpiWarps = 8;                 // two per TMEM lane quarter, 64 columns each
-constexpr int kEpiCols = BN / 2;
+constexpr int kTileBytes = BM * BKE * 2;     // 16 KB per operand tile
+constexpr int kStageBytes = 4 * kTileBytes;  // A hi, A lo, B hi, B lo
+constexpr int kAccBufs = 2;                  // TMEM accumulators (tile t, t+1)
+constexpr uint32_t kTmemCols = kAccBufs * BN;
+constexpr int kEpiWarps = 4;                 // one per TMEM lane quarter, 128 columns each
 constexpr int kGemmThreads = (2 + kEpiWarps) * 32;
-constexpr uint32_t kTmemCols = 512;          // 2 buffers x 2 terms x 128 columns
 constexpr unsigned long long kWaitNs = 1000000000ull;
 
 __device__ unsigned int g_prefill_error;  // bit 0: a bounded wait timed out
@@ -102,7 +111,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 
 // K-major operand in a 128-byte-swizzled tile: rows of 128 bytes, 8-row atoms
 // 1024 bytes apart (stride byte offset), version 1 (sm_100), layout
-// SWIZZLE_128B.  The start address moves by 32 bytes per K=32 slice.
+// SWIZZLE_128B.  The start address moves by 32 bytes per K=16 fp16 slice.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)1u << 16;            // leading byte offset (unused when swizzled)
@@ -112,17 +121,17 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
   return d;
 }
 
-// kind::i8 instruction descriptor: s32 accumulate, signed int8 A and B, both
+// kind::f16 instruction descriptor: f32 accumulate, f16 A and B, both
 // K-major, M = 128, N = 128.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t kIdesc =
+    (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t a, uint64_t b) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdesc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -137,130 +146,167 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// int32 in (-2^22, 2^22) -> float, exact, without the int->float unit
-__device__ __forceinline__ float i2f_exact(uint32_t v) {
-  return __int_as_float((int)v + 0x4B400000) - 12582912.0f;
-}
-
-__device__ __forceinline__ void prefill_epilogue(const PrefillGemm& p, int m, int n0,
-                                                 const float (&acc)[kEpiCols]) {
+// Output columns n, n+1 (n even) of token row m; column n+1 may lie past p.n.
+__device__ __forceinline__ void epilogue_pair(const PrefillGemm& p, int m, int n, float v0,
+                                              float v1) {
   if (p.epi == kEpiStore) {
     float* yr = p.y + (size_t)m * p.ldy;
     const float* rr = p.residual ? p.residual + (size_t)m * p.ldy : nullptr;
 #pragma unroll
-    for (int c = 0; c < kEpiCols; ++c) {
-      const int n = n0 + c;
-      if (n < p.n) {
-        float v = acc[c];
-        if (p.bias) v = __fadd_rn(v, p.bias[n]);
-        if (rr) v = __fadd_rn(rr[n], v);
-        yr[n] = v;
+    for (int e = 0; e < 2; ++e) {
+      const int nn = n + e;
+      if (nn < p.n) {
+        float v = e ? v1 : v0;
+        if (p.bias) v = __fadd_rn(v, p.bias[nn]);
+        if (rr) v = __fadd_rn(rr[nn], v);
+        yr[nn] = v;
       }
     }
   } else if (p.epi == kEpiSwiGlu) {
-    float* yr = p.y + (size_t)m * p.ldy;
-#pragma unroll
-    for (int c = 0; c < kEpiCols; c += 2) {
-      const int n = n0 + c;
-      if (n + 1 < p.n) {
-        const float g = acc[c], u = acc[c + 1];
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-        yr[n / 2] = __fmul_rn(__fmul_rn(g, sig), u);
-      }
+    if (n + 1 < p.n) {
+      const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v0)));
+      p.y[(size_t)m * p.ldy + n / 2] = __fmul_rn(__fmul_rn(v0, sig), v1);
     }
   } else {  // kEpiQkv
+    if (n + 1 >= p.n) return;
     const int pos = p.pos0 + m;
     const int half = p.head_dim / 2;
     const int q_pairs = p.n_heads * half;
     const int kv_pairs = p.n_kv_heads * half;
-#pragma unroll
-    for (int c = 0; c < kEpiCols; c += 2) {
-      const int n = n0 + c;
-      if (n + 1 >= p.n) continue;
-      const int pp = n / 2;
-      float x0 = acc[c], x1 = acc[c + 1];
-      if (p.bias) {
-        x0 = __fadd_rn(x0, p.bias[n]);
-        x1 = __fadd_rn(x1, p.bias[n + 1]);
-      }
-      int seg_pair, nh;
-      float* dst;
-      bool rotate = true;
-      if (pp < q_pairs) {
-        seg_pair = pp;
-        nh = p.n_heads;
-        dst = p.q_out + (size_t)m * p.ldq;
-      } else if (pp < q_pairs + kv_pairs) {
-        seg_pair = pp - q_pairs;
-        nh = p.n_kv_heads;
-        dst = p.k_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
+    const int pp = n / 2;
+    float x0 = v0, x1 = v1;
+    if (p.bias) {
+      x0 = __fadd_rn(x0, p.bias[n]);
+      x1 = __fadd_rn(x1, p.bias[n + 1]);
+    }
+    int seg_pair, nh;
+    float* dst;
+    bool rotate = true;
+    if (pp < q_pairs) {
+      seg_pair = pp;
+      nh = p.n_heads;
+      dst = p.q_out + (size_t)m * p.ldq;
+    } else if (pp < q_pairs + kv_pairs) {
+      seg_pair = pp - q_pairs;
+      nh = p.n_kv_heads;
+      dst = p.k_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
+    } else {
+      seg_pair = pp - q_pairs - kv_pairs;
+      nh = p.n_kv_heads;
+      dst = p.v_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
+      rotate = false;
+    }
+    const int h = seg_pair / half, i = seg_pair % half;
+    int o0, o1;
+    if (rotate && p.neox) {
+      o0 = h * p.head_dim + i;
+      o1 = o0 + half;
+    } else {
+      o0 = h * p.head_dim + 2 * i;
+      o1 = o0 + 1;
+    }
+    if (rotate) {
+      const float2 cs = p.rope_cs[(size_t)pos * half + i];
+      const float a = x0, b = x1;
+      if (p.neox) {
+        x0 = __fmaf_rn(a, cs.x, -__fmul_rn(b, cs.y));
+        x1 = __fmaf_rn(a, cs.y, __fmul_rn(b, cs.x));
       } else {
-        seg_pair = pp - q_pairs - kv_pairs;
-        nh = p.n_kv_heads;
-        dst = p.v_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
-        rotate = false;
+        x0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+        x1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
       }
-      const int h = seg_pair / half, i = seg_pair % half;
-      int o0, o1;
-      if (rotate && p.neox) {
-        o0 = h * p.head_dim + i;
-        o1 = o0 + half;
-      } else {
-        o0 = h * p.head_dim + 2 * i;
-        o1 = o0 + 1;
-      }
-      if (rotate) {
-        const float2 cs = p.rope_cs[(size_t)pos * half + i];
-        const float a = x0, b = x1;
-        if (p.neox) {
-          x0 = __fmaf_rn(a, cs.x, -__fmul_rn(b, cs.y));
-          x1 = __fmaf_rn(a, cs.y, __fmul_rn(b, cs.x));
-        } else {
-          x0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
-          x1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
-        }
-      }
-      dst[o0] = x0;
-      dst[o1] = x1;
+    }
+    dst[o0] = x0;
+    dst[o1] = x1;
+  }
+}
+
+// 32 rows (from m0) x 32 columns (from n0) of finished accumulators staged in
+// shared memory [row][33]: scale by 2^(e+f), then the epilogue (or park the
+// partial sums for split-K).  Lanes 0-15 take the column pairs of one row,
+// lanes 16-31 those of the next, so each store instruction covers whole rows.
+__device__ __forceinline__ void drain_chunk(const PrefillGemm& p, const float* stage, int m0,
+                                            int n0, int z, int lane) {
+  const int j = lane & 15;
+  const int n = n0 + 2 * j;
+  if (n >= p.n) return;
+  const float c0 = p.cs[n], c1 = n + 1 < p.n ? p.cs[n + 1] : 0.0f;
+#pragma unroll 1
+  for (int rr = lane >> 4; rr < 32; rr += 2) {
+    const int m = m0 + rr;
+    if (m >= p.m) break;
+    const float rs = p.rs[m];
+    const float v0 = __fmul_rn(__fmul_rn(stage[rr * 33 + 2 * j], rs), c0);
+    const float v1 = __fmul_rn(__fmul_rn(stage[rr * 33 + 2 * j + 1], rs), c1);
+    if (p.plan.splits == 1) {
+      epilogue_pair(p, m, n, v0, v1);
+    } else {
+      float* dst = p.partial + ((size_t)z * p.m + m) * p.n + n;
+      dst[0] = v0;
+      if (n + 1 < p.n) dst[1] = v1;
     }
   }
 }
 
+// Work item w of the persistent walk -> (row tile, column tile, K split).
+// Consecutive items share a column tile, so a weight tile is fetched from HBM
+// once and served to the other row tiles from L2.
+struct Work {
+  int m0, n0, z, kb0, kb1;
+};
+__device__ __forceinline__ Work decode_work(const PrefillGemm& p, int w, int m_tiles, int n_tiles) {
+  Work r;
+  const int mt = w % m_tiles;
+  const int rest = w / m_tiles;
+  const int nt = rest % n_tiles;
+  r.z = rest / n_tiles;
+  r.m0 = mt * BM;
+  r.n0 = nt * BN;
+  r.kb0 = r.z * p.plan.kb_per;
+  r.kb1 = min(p.kp / 32, r.kb0 + p.plan.kb_per);
+  return r;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_i8_kernel(const __grid_constant__ CUtensorMap map_a0,
-                   const __grid_constant__ CUtensorMap map_a1,
-                   const __grid_constant__ CUtensorMap map_b, const PrefillGemm p) {
+    gemm_f16_kernel(const __grid_constant__ CUtensorMap map_ahi,
+                    const __grid_constant__ CUtensorMap map_alo,
+                    const __grid_constant__ CUtensorMap map_bhi,
+                    const __grid_constant__ CUtensorMap map_blo, const PrefillGemm p) {
   extern __shared__ unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tfull[2], tempty[2];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], tfull[kAccBufs],
+      tempty[kAccBufs];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-  const int nbk = p.kp / 32;
-  const int ksteps = (nbk + 3) / 4;
+  const int m_tiles = (p.m + BM - 1) / BM, n_tiles = (p.n + BN - 1) / BN;
+  const int total = m_tiles * n_tiles * p.plan.splits;
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  float* epi_stage = reinterpret_cast<float*>(tiles + (size_t)kStages * kStageBytes);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       bar_init(&full[s], 1);
       bar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAccBufs; ++b) {
       bar_init(&tfull[b], 1);
       bar_init(&tempty[b], kEpiWarps);
     }
@@ -281,86 +327,98 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // ---------------- TMA producer
-      for (int s = 0; s < ksteps; ++s) {
-        const int st = s % kStages;
-        if (s >= kStages && !bar_wait(&empty[st], (uint32_t)((s / kStages - 1) & 1), &abort_flag))
-          break;
-        unsigned char* base = tiles + (size_t)st * kStageBytes;
-        bar_expect_tx(&full[st], kStageBytes);
-        tma_load_2d(base, &map_a0, s * BK, m0, &full[st]);
-        tma_load_2d(base + kTileBytes, &map_a1, s * BK, m0, &full[st]);
-        tma_load_2d(base + 2 * kTileBytes, &map_b, s * BK, n0, &full[st]);
+      int it = 0;
+      for (int w = blockIdx.x; w < total && !abort_flag; w += gridDim.x) {
+        const Work t = decode_work(p, w, m_tiles, n_tiles);
+        for (int ks = t.kb0 / 2; ks * 2 < t.kb1; ++ks, ++it) {
+          const int st = it % kStages;
+          if (it >= kStages &&
+              !bar_wait(&empty[st], (uint32_t)((it / kStages - 1) & 1), &abort_flag))
+            break;
+          unsigned char* base = tiles + (size_t)st * kStageBytes;
+          const int x = ks * BKE;
+          bar_expect_tx(&full[st], kStageBytes);
+          tma_load_2d(base, &map_ahi, x, t.m0, &full[st]);
+          tma_load_2d(base + kTileBytes, &map_alo, x, t.m0, &full[st]);
+          tma_load_2d(base + 2 * kTileBytes, &map_bhi, x, t.n0, &full[st]);
+          tma_load_2d(base + 3 * kTileBytes, &map_blo, x, t.n0, &full[st]);
+        }
       }
       // tail: every stage's last release (an MMA commit) has landed before
       // the CTA may exit
-      for (int s = ksteps > kStages ? ksteps - kStages : 0; s < ksteps && !abort_flag; ++s)
-        if (!bar_wait(&empty[s % kStages], (uint32_t)((s / kStages) & 1), &abort_flag)) break;
+      for (int i = it > kStages ? it - kStages : 0; i < it && !abort_flag; ++i)
+        if (!bar_wait(&empty[i % kStages], (uint32_t)((i / kStages) & 1), &abort_flag)) break;
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---------------- MMA issuer
-      int g = 0;
-      for (int s = 0; s < ksteps && !abort_flag; ++s) {
-        const int st = s % kStages;
-        if (!bar_wait(&full[st], (uint32_t)((s / kStages) & 1), &abort_flag)) break;
+      int it = 0, tc = 0;
+      for (int w = blockIdx.x; w < total && !abort_flag; w += gridDim.x, ++tc) {
+        const Work t = decode_work(p, w, m_tiles, n_tiles);
+        const int buf = tc % kAccBufs;
+        if (tc >= kAccBufs &&
+            !bar_wait(&tempty[buf], (uint32_t)((tc / kAccBufs - 1) & 1), &abort_flag))
+          break;
         tc_fence_after();
-        const uint32_t base = su32(tiles + (size_t)st * kStageBytes);
-        for (int j = 0; j < 4; ++j) {
-          const int kb = s * 4 + j;
-          if (kb >= nbk) break;
-          const int buf = g & 1;
-          if (g >= 2 && !bar_wait(&tempty[buf], (uint32_t)((g / 2 - 1) & 1), &abort_flag)) break;
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        uint32_t accumulate = 0u;
+        bool ok = true;
+        for (int ks = t.kb0 / 2; ks * 2 < t.kb1; ++ks, ++it) {
+          const int st = it % kStages;
+          if (!bar_wait(&full[st], (uint32_t)((it / kStages) & 1), &abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          const uint64_t bdesc = smem_desc(base + 2 * kTileBytes + j * 32);
-          mma_i8(tmem + buf * 256 + 0, smem_desc(base + j * 32), bdesc);
-          mma_i8(tmem + buf * 256 + 128, smem_desc(base + kTileBytes + j * 32), bdesc);
-          mma_commit(&tfull[buf]);
-          ++g;
+          const uint32_t ahi = su32(tiles + (size_t)st * kStageBytes);
+          const uint32_t alo = ahi + kTileBytes, bhi = ahi + 2 * kTileBytes,
+                         blo = ahi + 3 * kTileBytes;
+#pragma unroll
+          for (int k = 0; k < BKE / 16; ++k) {  // K=16 slices: 32 bytes apart
+            const uint32_t off = (uint32_t)k * 32;
+            const uint64_t dbhi = smem_desc(bhi + off);
+            mma_f16(d, smem_desc(ahi + off), dbhi, accumulate);
+            mma_f16(d, smem_desc(ahi + off), smem_desc(blo + off), 1u);
+            mma_f16(d, smem_desc(alo + off), dbhi, 1u);
+            accumulate = 1u;
+          }
+          mma_commit(&empty[st]);  // the stage is free once these MMAs finish
         }
-        mma_commit(&empty[st]);  // the stage is free once these MMAs finish
+        if (!ok) break;
+        mma_commit(&tfull[buf]);  // the accumulator is complete
       }
     }
-  } else {  // ---------------- epilogue warps 2..9: TMEM lanes 32*(warp%4) ..
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;    // which 64 columns of the tile
-    const int ml = quarter * 32 + lane;  // tile row == TMEM lane
-    const int m = m0 + ml;
-    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + half * kEpiCols;
-    float acc[kEpiCols];
-#pragma unroll
-    for (int c = 0; c < kEpiCols; ++c) acc[c] = 0.0f;
-    const float* sx0 = p.sx + (size_t)m * nbk;
-    const float* sx1 = p.sx + (size_t)(p.m_pad + m) * nbk;
-    for (int kb = 0; kb < nbk; ++kb) {
-      const int buf = kb & 1;
+  } else {  // ---------------- epilogue warps 2..5: TMEM lanes 32*(warp%4) ..
+    const int quarter = warp & 3;  // tile rows 32*quarter + lane == TMEM lanes
+    int tc = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x, ++tc) {
+      const Work t = decode_work(p, w, m_tiles, n_tiles);
+      const int buf = tc % kAccBufs;
       // warp-uniform outcome: the TMEM loads below are .sync.aligned
-      if (!__all_sync(0xffffffffu, bar_wait(&tfull[buf], (uint32_t)((kb >> 1) & 1), &abort_flag)))
+      if (!__all_sync(0xffffffffu,
+                      bar_wait(&tfull[buf], (uint32_t)((tc / kAccBufs) & 1), &abort_flag)))
         break;
       tc_fence_after();
-      const float s0 = __ldg(sx0 + kb), s1 = __ldg(sx1 + kb);
-      const float4* dw = reinterpret_cast<const float4*>(p.dwt + (size_t)kb * p.n + n0 + half * kEpiCols);
+      uint32_t r[BN];
+      const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN);
 #pragma unroll
-      for (int q = 0; q < kEpiCols / 16; ++q) {
-        uint32_t r0[16], r1[16];
-        tmem_ld16(trow + buf * 256 + q * 16, r0);
-        tmem_ld16(trow + buf * 256 + 128 + q * 16, r1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 w = __ldg(dw + q * 4 + j4);
-          const float wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = j4 * 4 + e;
-            const float u = __fmaf_rn(i2f_exact(r1[j]), s1, __fmul_rn(i2f_exact(r0[j]), s0));
-            acc[q * 16 + j] = __fmaf_rn(u, wv[e], acc[q * 16 + j]);
-          }
-        }
-      }
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_ld32(trow + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(&tempty[buf]);
+      if (lane == 0) bar_arrive(&tempty[buf]);  // the next-but-one tile may start
+      // each 32 x 32 chunk (this warp's rows x 32 columns) goes through shared
+      // memory so that the stores are row-contiguous across the warp
+      float* stage = epi_stage + (size_t)(warp - 2) * 32 * 33;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(r[c * 32 + j]);
+        __syncwarp();
+        drain_chunk(p, stage, t.m0 + quarter * 32, t.n0 + c * 32, t.z, lane);
+        __syncwarp();
+      }
     }
-    if (m < p.m && !abort_flag) prefill_epilogue(p, m, n0 + half * kEpiCols, acc);
   }
   tc_fence_before();
   __syncthreads();
@@ -372,70 +430,92 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// Split-K: sum the partial products in split order, then the epilogue.
+__global__ void splitk_epilogue_kernel(const PrefillGemm p) {
+  const int m = blockIdx.x;
+  const int n = 2 * (blockIdx.y * blockDim.x + threadIdx.x);
+  if (n >= p.n) return;
+  float v0 = 0.0f, v1 = 0.0f;
+  for (int z = 0; z < p.plan.splits; ++z) {
+    const float* src = p.partial + ((size_t)z * p.m + m) * p.n + n;
+    v0 = __fadd_rn(v0, src[0]);
+    if (n + 1 < p.n) v1 = __fadd_rn(v1, src[1]);
+  }
+  epilogue_pair(p, m, n, v0, v1);
+}
+
 // ----------------------------------------------------------- activations
-// One CTA per token row: optional RMSNorm (src/ops.cc:68-90), then each
-// 32-value block split into two int8 terms (see the file comment).  Writes
-// q[t][row][kp] (zero past k) and s[t][row][nbk].
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const float* __restrict__ x, int k,
-                                                            int kp, int ldx,
-                                                            const float* __restrict__ norm_w,
-                                                            float eps, int m_pad,
-                                                            int8_t* __restrict__ q,
-                                                            float* __restrict__ s) {
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.0f;
+  for (int w = 0; w < 8; ++w) t = __fadd_rn(t, red[w]);
+  return t;
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.0f;
+  for (int w = 0; w < 8; ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+
+// One CTA per token row: optional RMSNorm (src/ops.cc:68-90), a power-of-two
+// row scale 2^-e that brings the row's absmax into [2^14, 2^15), and the
+// two-term fp16 split hi = fp16(v), lo = fp16(v - hi) of v = x 2^-e.  Writes
+// hi/lo [row][kp] (zero past k) and rs[row] = 2^e.
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ x, int k,
+                                                         int kp, int ldx,
+                                                         const float* __restrict__ norm_w,
+                                                         float eps, uint16_t* __restrict__ hi,
+                                                         uint16_t* __restrict__ lo,
+                                                         float* __restrict__ rs) {
   __shared__ float red[8];
-  __shared__ float scale_s;
   const int row = blockIdx.x, tid = threadIdx.x;
   const float* xr = x + (size_t)row * ldx;
-  const int nbk = kp / 32;
   float scale = 1.0f;
   if (norm_w) {
     float ss = 0.0f;
     for (int e = tid; e < k; e += 256) ss = __fadd_rn(ss, __fmul_rn(xr[e], xr[e]));
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    if (tid == 0) {
-      float t = 0.0f;
-      for (int w = 0; w < 8; ++w) t += red[w];
-      scale_s = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float)k), eps)));
-    }
-    __syncthreads();
-    scale = scale_s;
+    const float t = block_sum(ss, red);
+    scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float)k), eps)));
   }
-  const int sub = tid & 7;
-  for (int base = 0; base < nbk * 8; base += 256) {
-    const int b = (base + tid) >> 3;
-    const bool valid = b < nbk;
-    float v[4];
+  auto val = [&](int col) -> float {
+    const float v = xr[col];
+    return norm_w ? __fmul_rn(__fmul_rn(v, scale), norm_w[col]) : v;
+  };
+  float mx = 0.0f;
+  for (int e = tid; e < k; e += 256) mx = fmaxf(mx, fabsf(val(e)));
+  mx = block_max(mx, red);
+  int ex = 0;
+  if (mx > 0.0f && mx <= 3.0e38f) {
+    int fe;
+    frexpf(mx, &fe);  // mx in [2^(fe-1), 2^fe)
+    ex = min(max(fe - 15, -120), 120);
+  }
+  const float down = ldexpf(1.0f, -ex);
+  if (tid == 0) rs[row] = ldexpf(1.0f, ex);
+  uint16_t* hr = hi + (size_t)row * kp;
+  uint16_t* lr = lo + (size_t)row * kp;
+  for (int c = tid * 4; c < kp; c += 1024) {
+    uint32_t h2[2], l2[2];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int col = b * 32 + sub * 4 + e;
-      float val = (valid && col < k) ? xr[col] : 0.0f;
-      if (norm_w && valid && col < k) val = __fmul_rn(__fmul_rn(val, scale), norm_w[col]);
-      v[e] = val;
+    for (int e = 0; e < 4; e += 2) {
+      float v[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) v[t] = c + e + t < k ? __fmul_rn(val(c + e + t), down) : 0.0f;
+      const __half ha = __float2half_rn(v[0]), hb = __float2half_rn(v[1]);
+      const __half la = __float2half_rn(__fsub_rn(v[0], __half2float(ha)));
+      const __half lb = __float2half_rn(__fsub_rn(v[1], __half2float(hb)));
+      h2[e / 2] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+      l2[e / 2] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
     }
-    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    float sc = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 0.0f;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const float inv = sc > 0.0f ? __frcp_rn(sc) : 0.0f;
-      uint32_t packed = 0;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int qq = __float2int_rn(__fmul_rn(v[e], inv));
-        qq = qq > 127 ? 127 : (qq < -127 ? -127 : qq);
-        v[e] = __fmaf_rn(-sc, (float)qq, v[e]);
-        packed |= ((uint32_t)qq & 0xffu) << (8 * e);
-      }
-      if (valid) {
-        reinterpret_cast<uint32_t*>(q + ((size_t)t * m_pad + row) * kp)[b * 8 + sub] = packed;
-        if (sub == 0) s[((size_t)t * m_pad + row) * nbk + b] = sc;
-      }
-      sc = __fmul_rn(sc, 1.0f / 254.0f);
-    }
+    *reinterpret_cast<uint2*>(hr + c) = make_uint2(h2[0], h2[1]);
+    *reinterpret_cast<uint2*>(lr + c) = make_uint2(l2[0], l2[1]);
   }
 }
 
@@ -460,6 +540,56 @@ __global__ void embed_rows_kernel(int qtype, const uint8_t* __restrict__ qs,
       v = (float)((j < 16 ? (byte & 0x0f) : (byte >> 4)) - 8);
     }
     y[(size_t)row * dim + i] = __fmul_rn(sc, v);
+  }
+}
+
+// One CTA per weight row: the dequantized values w = d * q (Q8_0 int8 q;
+// Q4_0 nibble - 8 with low nibbles as values 0..15 of a block and high
+// nibbles as 16..31, src/quant.cc:148-175) are exact in fp32 (at most 19
+// significant bits); scaled by 2^-f (row maximum in [2^14, 2^15)) each splits
+// exactly into hi = fp16(w 2^-f) and lo = fp16(w 2^-f - hi).  Writes the two
+// planes [row][kp] and cs[row] = 2^f.
+__global__ void __launch_bounds__(256) weights_split_kernel(int qtype, const uint8_t* __restrict__ qs,
+                                                            const uint16_t* __restrict__ d, int kp,
+                                                            uint16_t* __restrict__ bhi,
+                                                            uint16_t* __restrict__ blo,
+                                                            float* __restrict__ cs) {
+  __shared__ float red[8];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int nbk = kp / 32;
+  const uint16_t* dr = d + (size_t)row * nbk;
+  const uint8_t* qr = qs + (size_t)row * (qtype == DQMK_Q80 ? kp : kp / 2);
+  auto quant = [&](int e) -> int {
+    if (qtype == DQMK_Q80) return (int)(int8_t)qr[e];
+    const int j = e & 31;
+    const uint8_t byte = qr[(e >> 5) * 16 + (j & 15)];
+    return (int)(j < 16 ? (byte & 0x0f) : (byte >> 4)) - 8;
+  };
+  float mx = 0.0f;
+  for (int e = tid; e < kp; e += 256) mx = fmaxf(mx, fabsf(__fmul_rn(h2f(dr[e >> 5]), (float)quant(e))));
+  mx = block_max(mx, red);
+  int ex = 0;
+  if (mx > 0.0f && mx <= 3.0e38f) {
+    int fe;
+    frexpf(mx, &fe);
+    ex = min(max(fe - 15, -120), 120);
+  }
+  const float down = ldexpf(1.0f, -ex);
+  if (tid == 0) cs[row] = ldexpf(1.0f, ex);
+  uint16_t* hr = bhi + (size_t)row * kp;
+  uint16_t* lr = blo + (size_t)row * kp;
+  for (int e = tid * 2; e < kp; e += 512) {
+    uint32_t h2 = 0, l2 = 0;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float w = __fmul_rn(__fmul_rn(h2f(dr[(e + t) >> 5]), (float)quant(e + t)), down);
+      const __half h = __float2half_rn(w);
+      const __half l = __float2half_rn(__fsub_rn(w, __half2float(h)));
+      h2 |= (uint32_t)__half_as_ushort(h) << (16 * t);
+      l2 |= (uint32_t)__half_as_ushort(l) << (16 * t);
+    }
+    *reinterpret_cast<uint32_t*>(hr + e) = h2;
+    *reinterpret_cast<uint32_t*>(lr + e) = l2;
   }
 }
 
@@ -551,17 +681,6 @@ __global__ void __launch_bounds__(256) attention_prefill_kernel(PrefillAttn a) {
   }
 }
 
-// [N][nbk] fp16 scales -> [nbk][N] fp32 (the epilogue's per-block row of dW)
-__global__ void transpose_scales_kernel(const uint16_t* __restrict__ d, int n, int nbk,
-                                        float* __restrict__ out) {
-  const size_t total = (size_t)n * nbk;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t row = i / nbk, kb = i % nbk;
-    out[kb * n + row] = h2f(d[i]);
-  }
-}
-
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -576,19 +695,23 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+size_t gemm_smem() {
+  return (size_t)kStages * kStageBytes + (size_t)kEpiWarps * 32 * 33 * sizeof(float) + 1024;
+}
+
 }  // namespace
 
-// [rows][kp] int8 matrix, 128 x 128-byte boxes, 128-byte swizzle.
-int make_i8_tile_map(CUtensorMap* map, const void* base, int rows, int kp) {
+// [rows][kp] fp16 plane, 128-row x 64-element (128-byte) boxes, 128-byte swizzle.
+int make_f16_tile_map(CUtensorMap* map, const void* base, int rows, int kp) {
   auto fn = encode_fn();
   if (!fn) return fail(DQMK_ERR_CUDA, "ForwardBatch: cuTensorMapEncodeTiled unavailable");
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (kp % 16) != 0)
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (kp % 8) != 0 || rows <= 0)
     return fail(DQMK_ERR_INVALID, "ForwardBatch: tensor map base or stride not 16-byte aligned");
   cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)kp};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+  cuuint64_t strides[1] = {(cuuint64_t)kp * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BKE, (cuuint32_t)BM};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -597,13 +720,33 @@ int make_i8_tile_map(CUtensorMap* map, const void* base, int rows, int kp) {
   return DQMK_OK;
 }
 
-size_t prefill_gemm_smem() { return (size_t)kStages * kStageBytes + 1024; }
+// Enough work items to cover the SMs, at least 8 scale blocks per split; an
+// even block count per split keeps stages aligned to 64-element K steps.
+GemmPlan plan_gemm(int m, int n, int kp) {
+  const int nbk = kp / 32;
+  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  int splits = std::max(1, std::min(sm_count() / std::max(tiles, 1), nbk / 8));
+  int kb_per = (nbk + splits - 1) / splits;
+  kb_per = (kb_per + 1) / 2 * 2;
+  splits = (nbk + kb_per - 1) / kb_per;
+  return GemmPlan{splits, kb_per};
+}
+
+size_t partial_floats_bound(int m_max, int n, int kp) {
+  size_t most = 0;
+  for (int mt = 1; (mt - 1) * BM < m_max; ++mt) {
+    const int m = std::min(mt * BM, m_max);
+    const GemmPlan g = plan_gemm(m, n, kp);
+    if (g.splits > 1) most = std::max(most, (size_t)g.splits * m * n);
+  }
+  return most;
+}
 
 cudaError_t prefill_prepare() {
   static bool done = false;
   if (done) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)prefill_gemm_smem());
+  cudaError_t e = cudaFuncSetAttribute(gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gemm_smem());
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attention_prefill_kernel<64>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
@@ -614,21 +757,32 @@ cudaError_t prefill_prepare() {
   return e;
 }
 
-cudaError_t launch_prefill_gemm(const CUtensorMap& a0, const CUtensorMap& a1,
-                                const CUtensorMap& b, const PrefillGemm& p, cudaStream_t s) {
+cudaError_t launch_prefill_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo,
+                                const CUtensorMap& b_hi, const CUtensorMap& b_lo,
+                                const PrefillGemm& p, cudaStream_t s) {
+  const int nbk = p.kp / 32;
+  const GemmPlan& g = p.plan;
+  if (p.m <= 0 || p.n <= 0 || p.kp <= 0 || p.kp % 32 != 0 || !p.rs || !p.cs || g.splits < 1 ||
+      g.kb_per < 2 || g.kb_per % 2 != 0 || (g.splits - 1) * g.kb_per >= nbk ||
+      g.splits * g.kb_per < nbk || (g.splits > 1 && !p.partial))
+    return cudaErrorInvalidValue;
   cudaError_t e = prefill_prepare();
   if (e != cudaSuccess) return e;
-  if (p.m <= 0 || p.m > p.m_pad || p.m_pad % BM != 0 || p.n % BN != 0 || p.kp % 32 != 0)
-    return cudaErrorInvalidValue;
-  dim3 grid(p.n / BN, (p.m + BM - 1) / BM);
-  gemm_i8_kernel<<<grid, kGemmThreads, prefill_gemm_smem(), s>>>(a0, a1, b, p);
+  const long long total =
+      (long long)((p.m + BM - 1) / BM) * ((p.n + BN - 1) / BN) * g.splits;
+  if (total > (1ll << 30)) return cudaErrorInvalidValue;
+  const int grid = (int)std::min<long long>(total, sm_count());
+  gemm_f16_kernel<<<grid, kGemmThreads, gemm_smem(), s>>>(a_hi, a_lo, b_hi, b_lo, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || g.splits == 1) return e;
+  const int pairs = (p.n + 1) / 2;
+  splitk_epilogue_kernel<<<dim3(p.m, (pairs + 127) / 128), 128, 0, s>>>(p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_rows(const float* x, int m, int k, int kp, int ldx,
-                                 const float* norm_w, float eps, int m_pad, int8_t* q, float* s,
-                                 cudaStream_t st) {
-  quantize_rows_kernel<<<m, 256, 0, st>>>(x, k, kp, ldx, norm_w, eps, m_pad, q, s);
+cudaError_t launch_split_rows(const float* x, int m, int k, int kp, int ldx, const float* norm_w,
+                              float eps, uint16_t* hi, uint16_t* lo, float* rs, cudaStream_t st) {
+  split_rows_kernel<<<m, 256, 0, st>>>(x, k, kp, ldx, norm_w, eps, hi, lo, rs);
   return cudaGetLastError();
 }
 
@@ -654,9 +808,10 @@ cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_transpose_scales(const uint16_t* d, int n, int nbk, float* out,
-                                    cudaStream_t st) {
-  transpose_scales_kernel<<<sm_count() * 4, 256, 0, st>>>(d, n, nbk, out);
+cudaError_t launch_weights_split(int qtype, const uint8_t* qs, const uint16_t* d, int rows, int kp,
+                                 uint16_t* bhi, uint16_t* blo, float* cs, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  weights_split_kernel<<<rows, 256, 0, st>>>(qtype, qs, d, kp, bhi, blo, cs);
   return cudaGetLastError();
 }
 
@@ -670,3 +825,81 @@ cudaError_t read_prefill_error(unsigned int* flags, bool clear) {
 }
 
 }  // namespace dqmk
+
+// ------------------------------------------------------------------ C ABI
+using namespace dqmk;
+
+extern "C" int dqmk_linear_batch_packed(int qtype, const float* x, int m, int in_features,
+                                        const void* packed, int out_features, const float* bias,
+                                        const float* residual, float* y, void* stream) {
+  const char* api = qtype == DQMK_Q40 ? "CudaQ40Linear" : "CudaQ80Linear";
+  if (qtype != DQMK_Q80 && qtype != DQMK_Q40)
+    return fail(DQMK_ERR_UNSUPPORTED, "dqmk_linear_batch_packed: unsupported quant type");
+  if (m <= 0 || in_features <= 0 || out_features <= 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid shape");
+  if (!x || !packed || !y) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  if (reinterpret_cast<uintptr_t>(packed) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": packed weight must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int kp = (in_features + 31) / 32 * 32;
+  const uint8_t* qs = static_cast<const uint8_t*>(packed);
+  const size_t qbytes = (size_t)out_features * (qtype == DQMK_Q80 ? kp : kp / 2);
+  const uint16_t* d = reinterpret_cast<const uint16_t*>(qs + qbytes);
+  const GemmPlan plan = plan_gemm(m, out_features, kp);
+  // stream-ordered scratch: fp16 activation planes and row scales, the fp16
+  // weight planes and column scales, split-K partial sums
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t b_act = up((size_t)m * kp * 2), b_rs = up((size_t)m * 4);
+  const size_t b_w = up((size_t)out_features * kp * 2), b_cs = up((size_t)out_features * 4);
+  const size_t b_part = plan.splits > 1 ? up((size_t)plan.splits * m * out_features * 4) : 0;
+  unsigned char* scratch = nullptr;
+  DQMK_CUDA_RET(api, cudaMallocAsync(reinterpret_cast<void**>(&scratch),
+                                     2 * b_act + b_rs + 2 * b_w + b_cs + b_part + 256, st));
+  unsigned char* cur = scratch;
+  auto take = [&](size_t b) {
+    unsigned char* r = cur;
+    cur += b;
+    return r;
+  };
+  uint16_t* ahi = reinterpret_cast<uint16_t*>(take(b_act));
+  uint16_t* alo = reinterpret_cast<uint16_t*>(take(b_act));
+  float* rs = reinterpret_cast<float*>(take(b_rs));
+  uint16_t* bhi = reinterpret_cast<uint16_t*>(take(b_w));
+  uint16_t* blo = reinterpret_cast<uint16_t*>(take(b_w));
+  float* cs = reinterpret_cast<float*>(take(b_cs));
+  float* part = reinterpret_cast<float*>(take(b_part));
+  int rc = DQMK_OK;
+  cudaError_t e = cudaSuccess;
+  CUtensorMap mahi, malo, mbhi, mblo;
+  do {
+    if ((rc = make_f16_tile_map(&mahi, ahi, m, kp))) break;
+    if ((rc = make_f16_tile_map(&malo, alo, m, kp))) break;
+    if ((rc = make_f16_tile_map(&mbhi, bhi, out_features, kp))) break;
+    if ((rc = make_f16_tile_map(&mblo, blo, out_features, kp))) break;
+    if ((e = launch_weights_split(qtype, qs, d, out_features, kp, bhi, blo, cs, st)) !=
+        cudaSuccess)
+      break;
+    if ((e = launch_split_rows(x, m, in_features, kp, in_features, nullptr, 0.0f, ahi, alo, rs,
+                               st)) != cudaSuccess)
+      break;
+    PrefillGemm g = {};
+    g.m = m;
+    g.n = out_features;
+    g.kp = kp;
+    g.rs = rs;
+    g.cs = cs;
+    g.plan = plan;
+    g.partial = part;
+    g.epi = kEpiStore;
+    g.bias = bias;
+    g.residual = residual;
+    g.y = y;
+    g.ldy = out_features;
+    e = launch_prefill_gemm(mahi, malo, mbhi, mblo, g, st);
+  } while (false);
+  cudaError_t ef = cudaFreeAsync(scratch, st);
+  if (rc) return rc;
+  if (e == cudaSuccess) e = ef;
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  return DQMK_OK;
+}

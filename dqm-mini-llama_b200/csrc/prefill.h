@@ -1,25 +1,33 @@
-// prefill.h -- batched prefill (tcgen05 int8 GEMM, causal attention) shared
-// between prefill.cu and the engine.
+// prefill.h -- batched prefill (tcgen05 GEMM, causal attention) shared between
+// prefill.cu and the engine.
 #pragma once
 
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstddef>
 #include <cstdint>
 
 namespace dqmk {
 
+// Split of the K dimension of one GEMM across CTAs.
+struct GemmPlan {
+  int splits;  // CTAs along K; > 1 adds a deterministic reduce + epilogue kernel
+  int kb_per;  // 32-value scale blocks per split (even)
+};
+
 // One projection of a prompt chunk: C[m][n] over weight rows n (packed order).
 struct PrefillGemm {
   int m;                  // valid token rows
-  int m_pad;              // rows of the activation buffers (multiple of 128)
   int n;                  // weight rows
   int kp;                 // padded in_features (multiple of 32)
-  const float* sx;        // activation term scales [2][m_pad][kp/32]
-  const float* dwt;       // weight scales, transposed [kp/32][n], fp32
+  const float* rs;        // power-of-two row scales of the fp16 activation planes [m]
+  const float* cs;        // power-of-two row scales of the fp16 weight planes [n]
+  GemmPlan plan;
+  float* partial;         // plan.splits > 1: [splits][m][n] raw sums
   int epi;                // kEpiStore / kEpiSwiGlu / kEpiQkv
   const float* bias;      // by packed row (may be null)
-  const float* residual;  // kEpiStore: y = residual + acc (may alias y)
+  const float* residual;  // kEpiStore: y = residual + (acc + bias) (may alias y)
   float* y;               // kEpiStore: [m][ldy]; kEpiSwiGlu: [m][ldy] with n/2 columns
   int ldy;
   // kEpiQkv: rows paired for RoPE like the decode GEMV
@@ -42,19 +50,26 @@ struct PrefillAttn {
   int m, pos0, layer, max_seq, n_heads, n_kv_heads, head_dim;
 };
 
-int make_i8_tile_map(CUtensorMap* map, const void* base, int rows, int kp);
-size_t prefill_gemm_smem();
+// Tensor map of an fp16 [rows][kp] plane in 128 x 64-element boxes.
+int make_f16_tile_map(CUtensorMap* map, const void* base, int rows, int kp);
+GemmPlan plan_gemm(int m, int n, int kp);
+// Largest splits * m * n over every m <= m_max (floats of the partial buffer).
+size_t partial_floats_bound(int m_max, int n, int kp);
 cudaError_t prefill_prepare();
-cudaError_t launch_prefill_gemm(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
+cudaError_t launch_prefill_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo,
+                                const CUtensorMap& b_hi, const CUtensorMap& b_lo,
                                 const PrefillGemm& p, cudaStream_t s);
-cudaError_t launch_quantize_rows(const float* x, int m, int k, int kp, int ldx,
-                                 const float* norm_w, float eps, int m_pad, int8_t* q, float* s,
-                                 cudaStream_t st);
+// x [m][ldx] (optionally RMS-normalised with norm_w) -> fp16 planes hi, lo
+// [m][kp] with x * 2^-e ~= hi + lo, and rs[row] = 2^e.
+cudaError_t launch_split_rows(const float* x, int m, int k, int kp, int ldx, const float* norm_w,
+                              float eps, uint16_t* hi, uint16_t* lo, float* rs, cudaStream_t st);
 cudaError_t launch_embed_rows(int qtype, const uint8_t* qs, const uint16_t* d, int dim, int kp,
                               const int* tokens, int m, float* y, cudaStream_t st);
 cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st);
-cudaError_t launch_transpose_scales(const uint16_t* d, int n, int nbk, float* out,
-                                    cudaStream_t st);
+// Packed Q8_0 / Q4_0 weight [rows][kp] -> exact two-term fp16 planes of
+// d * q * 2^-f and the row scales cs[row] = 2^f.
+cudaError_t launch_weights_split(int qtype, const uint8_t* qs, const uint16_t* d, int rows, int kp,
+                                 uint16_t* bhi, uint16_t* blo, float* cs, cudaStream_t st);
 cudaError_t read_prefill_error(unsigned int* flags, bool clear);
 
 }  // namespace dqmk

@@ -114,6 +114,23 @@ int dqmk_gemv_packed(int qtype, const float* x_dev, int in_features, const void*
                      int out_features, const float* bias_dev, const float* residual_dev,
                      float* y_dev, void* stream);
 
+/* Batched (prefill) linear on a packed weight, on the int8 tensor cores:
+ * y[m][o] = residual[m][o] + bias[o] + sum_k W[o][k] x[m][k] for `m` rows
+ * (residual_dev / bias_dev may be NULL; y_dev may equal residual_dev).  The
+ * batched form of LinearQ80 / LinearQ40 (src/quant.cc:350-360, rows of x
+ * times the block-dequantized weight) and of the reference's per-token
+ * Linear calls inside ForwardBatch (src/batch.cc:35-40).  Every
+ * dequantized weight is exact as two fp16 terms once its row is scaled by a
+ * power of two; each row of x is scaled likewise and split into two fp16
+ * terms (relative error <= 2^-22); the tensor cores accumulate the products
+ * in fp32 over all of K, so results match the F32 product to fp32
+ * summation-order differences.  Scratch (including the weight's fp16 planes)
+ * is allocated stream-ordered on `stream`; the engine keeps its weights'
+ * planes resident instead. */
+int dqmk_linear_batch_packed(int qtype, const float* x_dev, int m, int in_features,
+                             const void* packed_dev, int out_features, const float* bias_dev,
+                             const float* residual_dev, float* y_dev, void* stream);
+
 /* Failure detection.  Kernels that wait on asynchronous copies bound every
  * wait (about one second); a wait that runs out records a flag in device
  * memory and the kernel exits instead of hanging.  dqmk_device_error returns

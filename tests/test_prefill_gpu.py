@@ -28,9 +28,15 @@ def check_logits(got, ref, label):
 
 
 @pytest.fixture(scope="module")
-def mini_q8(pkg, S, cuda):
-    return S.make_model(S.QWEN2_MINI, pkg.Q80, 2024,
-                        quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+def minis(pkg, S, cuda):
+    return {qt: S.make_model(S.QWEN2_MINI, qt, 2024,
+                             quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+            for qt in (pkg.Q80, pkg.Q40)}
+
+
+@pytest.fixture(scope="module")
+def mini_q8(minis, pkg):
+    return minis[pkg.Q80]
 
 
 class per_token_path:
@@ -47,13 +53,15 @@ class per_token_path:
             os.environ["DQMK_PREFILL"] = self.old
 
 
-def test_prefill_then_decode_matches_reference_golden(pkg, mini_q8, cuda):
+@pytest.mark.parametrize("qt", [1, 2])
+def test_prefill_then_decode_matches_reference_golden(pkg, minis, cuda, qt):
     """8 prompt tokens batched, then 4 ForwardToken steps that attend over the
-    KV cache the prefill wrote; every logits vector against the reference."""
+    KV cache the prefill wrote; every logits vector against the reference
+    (Q8_0, and Q4_0 whose nibbles the prefill expands to int8 once)."""
     g = np.load(golden_path("mini_model.npz"))
-    toks = g["q1_tokens"]
-    ref = g["q1_logits"]
-    ctx = pkg.Context(pkg.Model.from_synth(mini_q8, max_seq_len=64))
+    toks = g[f"q{qt}_tokens"]
+    ref = g[f"q{qt}_logits"]
+    ctx = pkg.Context(pkg.Model.from_synth(minis[qt], max_seq_len=64))
     worst = check_logits(ctx.ForwardBatch([int(t) for t in toks[:8]], 0), ref[7], "prefill")
     for i in range(8, len(toks)):
         worst = max(worst, check_logits(ctx.ForwardToken(int(toks[i]), i), ref[i], f"step {i}"))
