@@ -593,92 +593,147 @@ __global__ void __launch_bounds__(256) weights_split_kernel(int qtype, const uin
   }
 }
 
-// Causal GQA attention for a block of BQ consecutive query positions of one
-// head, over cache positions 0 .. pos0 + m (flash-style online softmax).
+// Causal GQA attention for a block of 64 consecutive query positions of one
+// head over cache positions 0 .. its last query (src/ops.cc attention per
+// token: scores q.k / sqrt(head_dim), softmax, weighted sum of values), fp32
+// throughout, flash-style online softmax over 64-key tiles.  Thread (ty, tx)
+// of 256 owns queries ty + 16 i and keys tx + 16 j (i, j < 4) of each score
+// tile and output dims tx*4 + 64 e of its queries: with 16-strided keys and
+// rows padded to HD + 4 floats, the float4 shared-memory reads of a quarter
+// warp hit distinct banks.
 template <int HD>
 __global__ void __launch_bounds__(256) attention_prefill_kernel(PrefillAttn a) {
-  constexpr int BQ = 32, BKV = 64, PAD = HD + 1;
-  constexpr int DPT = HD / 8;  // output dims per thread
-  extern __shared__ float sm[];
-  float* sq = sm;                    // [BQ][PAD]
-  float* sk = sq + BQ * PAD;         // [BKV][PAD]
-  float* sv = sk + BKV * PAD;        // [BKV][HD]
-  float* sp = sv + BKV * HD;         // [BQ][BKV]
-  const int tid = threadIdx.x;
-  const int h = blockIdx.x;
-  const int q0 = blockIdx.y * BQ;
-  const int G = a.n_heads / a.n_kv_heads;
-  const int kvh = h / G;
-  const size_t row_stride = (size_t)a.n_kv_heads * HD;
-  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
-  const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
+  constexpr int BQ = 64, BKV = 64, LD = HD + 4, NV4 = HD / 64, LP = BKV + 1;
+  extern __shared__ float4 smem4[];
+  float* qs = reinterpret_cast<float*>(smem4);  // [BQ][LD]
+  float* ks = qs + BQ * LD;                     // [BKV][LD]
+  float* vs = ks + BKV * LD;                    // [BKV][HD]
+  float* ps = vs + BKV * HD;                    // [BQ][LP]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int h = blockIdx.x, q0 = blockIdx.y * BQ;
+  const int kvh = h / (a.n_heads / a.n_kv_heads);
+  const size_t rstride = (size_t)a.n_kv_heads * HD;
+  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * rstride + (size_t)kvh * HD;
+  const float* vbase = a.values + (size_t)a.layer * a.max_seq * rstride + (size_t)kvh * HD;
   const int nq = min(BQ, a.m - q0);
-  for (int i = tid; i < BQ * HD; i += 256) {
-    const int r = i / HD, d = i % HD;
-    sq[r * PAD + d] = r < nq ? a.q[(size_t)(q0 + r) * a.ldq + (size_t)h * HD + d] : 0.0f;
+  const int last = a.pos0 + q0 + nq - 1;  // the last key any query here sees
+  for (int i = tid; i < BQ * HD / 4; i += 256) {
+    const int r = i / (HD / 4), c4 = i % (HD / 4);
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (r < nq)
+      v = *reinterpret_cast<const float4*>(a.q + (size_t)(q0 + r) * a.ldq + (size_t)h * HD + c4 * 4);
+    *reinterpret_cast<float4*>(qs + r * LD + c4 * 4) = v;
   }
-  const int qi = tid >> 3;       // query row of this thread
-  const int sub = tid & 7;       // score columns sub*8 .. +7 / output dims sub*DPT ..
-  const int qpos = a.pos0 + q0 + qi;
-  const int last = a.pos0 + q0 + nq - 1;
   const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
-  float mrow = -INFINITY, lrow = 0.0f;
-  float o[DPT];
+  float mrow[4], lrow[4], o[4][4 * NV4];
 #pragma unroll
-  for (int e = 0; e < DPT; ++e) o[e] = 0.0f;
+  for (int i = 0; i < 4; ++i) {
+    mrow[i] = -INFINITY;
+    lrow[i] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4 * NV4; ++e) o[i][e] = 0.0f;
+  }
   for (int kt = 0; kt <= last; kt += BKV) {
-    __syncthreads();
-    for (int i = tid; i < BKV * HD; i += 256) {
-      const int r = i / HD, d = i % HD;
+    __syncthreads();  // the previous tile's K, V and P are consumed
+    for (int i = tid; i < BKV * HD / 4; i += 256) {
+      const int r = i / (HD / 4), c4 = i % (HD / 4);
       const int pos = kt + r;
-      const bool ok = pos <= last;
-      sk[r * PAD + d] = ok ? __ldcg(kbase + (size_t)pos * row_stride + d) : 0.0f;
-      sv[r * HD + d] = ok ? __ldcg(vbase + (size_t)pos * row_stride + d) : 0.0f;
+      float4 kv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vv = kv;
+      if (pos <= last) {
+        kv = __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)pos * rstride) + c4);
+        vv = __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)pos * rstride) + c4);
+      }
+      *reinterpret_cast<float4*>(ks + r * LD + c4 * 4) = kv;
+      *reinterpret_cast<float4*>(vs + r * HD + c4 * 4) = vv;
     }
     __syncthreads();
-    float s[8];
-    float tmax = -INFINITY;
+    float sc[4][4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int j = sub * 8 + c;
-      float dot = 0.0f;
-#pragma unroll 16
-      for (int d = 0; d < HD; ++d) dot = fmaf(sq[qi * PAD + d], sk[j * PAD + d], dot);
-      const bool visible = qi < nq && kt + j <= qpos;
-      s[c] = visible ? __fmul_rn(dot, scale) : -INFINITY;
-      tmax = fmaxf(tmax, s[c]);
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+#pragma unroll 4
+    for (int d = 0; d < HD; d += 4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(qs + (ty + 16 * i) * LD + d);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(ks + (tx + 16 * j) * LD + d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sc[i][j] = fmaf(qv[i].x, kv[j].x, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].y, kv[j].y, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].z, kv[j].z, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].w, kv[j].w, sc[i][j]);
+        }
     }
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-    const float mnew = fmaxf(mrow, tmax);
-    const float corr = mnew == -INFINITY ? 1.0f : expf(mrow - mnew);
-    float psum = 0.0f;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float pv = s[c] == -INFINITY ? 0.0f : expf(s[c] - mnew);
-      sp[qi * BKV + sub * 8 + c] = pv;
-      psum += pv;
+    for (int i = 0; i < 4; ++i) {
+      const int ql = ty + 16 * i;
+      const int qpos = a.pos0 + q0 + ql;
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool vis = ql < nq && kt + tx + 16 * j <= qpos;
+        sc[i][j] = vis ? __fmul_rn(sc[i][j], scale) : -INFINITY;
+        tmax = fmaxf(tmax, sc[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1)
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+      const float mnew = fmaxf(mrow[i], tmax);
+      const float corr = mnew == -INFINITY ? 1.0f : expf(mrow[i] - mnew);
+      float psum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float pv = sc[i][j] == -INFINITY ? 0.0f : expf(sc[i][j] - mnew);
+        ps[ql * LP + tx + 16 * j] = pv;
+        psum += pv;
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+      lrow[i] = fmaf(lrow[i], corr, psum);
+      mrow[i] = mnew;
+#pragma unroll
+      for (int e = 0; e < 4 * NV4; ++e) o[i][e] *= corr;
     }
-    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-    psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-    psum += __shfl_xor_sync(0xffffffffu, psum, 4);
-    lrow = fmaf(lrow, corr, psum);
-    mrow = mnew;
-    __syncwarp();
+    __syncwarp();  // a query row's P is written and read by the same 16 lanes
+#pragma unroll 4
+    for (int k = 0; k < BKV; ++k) {
+      float pk[4];
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) o[e] *= corr;
-    for (int j = 0; j < BKV; ++j) {
-      const float pv = sp[qi * BKV + j];
+      for (int i = 0; i < 4; ++i) pk[i] = ps[(ty + 16 * i) * LP + k];
 #pragma unroll
-      for (int e = 0; e < DPT; ++e) o[e] = fmaf(pv, sv[j * HD + sub * DPT + e], o[e]);
+      for (int e4 = 0; e4 < NV4; ++e4) {
+        const float4 v = *reinterpret_cast<const float4*>(vs + k * HD + e4 * 64 + tx * 4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          o[i][e4 * 4 + 0] = fmaf(pk[i], v.x, o[i][e4 * 4 + 0]);
+          o[i][e4 * 4 + 1] = fmaf(pk[i], v.y, o[i][e4 * 4 + 1]);
+          o[i][e4 * 4 + 2] = fmaf(pk[i], v.z, o[i][e4 * 4 + 2]);
+          o[i][e4 * 4 + 3] = fmaf(pk[i], v.w, o[i][e4 * 4 + 3]);
+        }
+      }
     }
   }
-  if (qi < nq) {
-    float* out = a.out + (size_t)(q0 + qi) * a.ldo + (size_t)h * HD + sub * DPT;
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) out[e] = __fdiv_rn(o[e], lrow);
+  for (int i = 0; i < 4; ++i) {
+    const int ql = ty + 16 * i;
+    if (ql >= nq) continue;
+    float* out = a.out + (size_t)(q0 + ql) * a.ldo + (size_t)h * HD;
+#pragma unroll
+    for (int e4 = 0; e4 < NV4; ++e4)
+      *reinterpret_cast<float4*>(out + e4 * 64 + tx * 4) =
+          make_float4(__fdiv_rn(o[i][e4 * 4 + 0], lrow[i]), __fdiv_rn(o[i][e4 * 4 + 1], lrow[i]),
+                      __fdiv_rn(o[i][e4 * 4 + 2], lrow[i]), __fdiv_rn(o[i][e4 * 4 + 3], lrow[i]));
   }
+}
+
+template <int HD>
+constexpr size_t attention_prefill_smem() {
+  return sizeof(float) * (2 * 64 * (HD + 4) + 64 * HD + 64 * 65);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -749,10 +804,12 @@ cudaError_t prefill_prepare() {
                                        (int)gemm_smem());
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attention_prefill_kernel<64>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attention_prefill_smem<64>());
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attention_prefill_kernel<128>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attention_prefill_smem<128>());
   if (e == cudaSuccess) done = true;
   return e;
 }
@@ -795,13 +852,14 @@ cudaError_t launch_embed_rows(int qtype, const uint8_t* qs, const uint16_t* d, i
 cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st) {
   cudaError_t e = prefill_prepare();
   if (e != cudaSuccess) return e;
-  dim3 grid(a.n_heads, (a.m + 31) / 32);
+  if (a.m <= 0 || a.n_kv_heads <= 0 || a.n_heads % a.n_kv_heads != 0 || a.ldq % 4 != 0 ||
+      a.ldo % 4 != 0)
+    return cudaErrorInvalidValue;
+  dim3 grid(a.n_heads, (a.m + 63) / 64);
   if (a.head_dim == 64) {
-    const size_t smem = sizeof(float) * (32 * 65 + 64 * 65 + 64 * 64 + 32 * 64);
-    attention_prefill_kernel<64><<<grid, 256, smem, st>>>(a);
+    attention_prefill_kernel<64><<<grid, 256, attention_prefill_smem<64>(), st>>>(a);
   } else if (a.head_dim == 128) {
-    const size_t smem = sizeof(float) * (32 * 129 + 64 * 129 + 64 * 128 + 32 * 64);
-    attention_prefill_kernel<128><<<grid, 256, smem, st>>>(a);
+    attention_prefill_kernel<128><<<grid, 256, attention_prefill_smem<128>(), st>>>(a);
   } else {
     return cudaErrorInvalidValue;
   }

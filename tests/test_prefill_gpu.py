@@ -127,3 +127,29 @@ def test_prefill_chunked_long_prompt_matches_reference(pkg, orc, S, mini_q8, cud
     assert first == ref_tokens[0]
     rest = ctx.decode_greedy(first, n, steps - 1).tolist()
     assert [first] + rest == ref_tokens
+
+
+def test_qwen2_0_5b_q4_0_ctx2048_prefill_then_128_greedy(pkg, S, cuda):
+    """Qwen2-0.5B-architecture with ggml-convention Q4_0 weights: a 2048-id
+    prompt through the batched prefill (two 1024-row chunks) fills the KV
+    cache, then 128 greedy steps over it must equal the reference's tokens."""
+    import hashlib
+    import json
+
+    g = json.load(open(golden_path("qwen2_0_5b_q4_0_ctx2048.json")))
+    w = S.make_model(S.QWEN2_0_5B, S.Q40, g["model_seed"])
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+    assert sha(w.token_embd) == g["digests"]["token_embd"]
+    n = g["n_prompt"]
+    prompt = S.prompt_tokens(w.cfg["vocab"], n, g["prompt_seed"])
+    assert sha(prompt) == g["prompt_sha256"]
+    ctx = pkg.Context(pkg.Model.from_synth(w, max_seq_len=n + len(g["greedy_tokens"])))
+    logits = ctx.ForwardBatch(prompt.tolist(), 0)
+    for k, v in g["top5"][0]:
+        assert abs(logits[k] - v) <= 1e-3 * 6.0, (k, logits[k], v)
+    first = int(np.argmax(logits))
+    rest = ctx.decode_greedy(first, n, len(g["greedy_tokens"]) - 1).tolist()
+    tokens = [first] + rest
+    assert tokens == g["greedy_tokens"], (
+        f"first divergence at {next(i for i, (a, b) in enumerate(zip(tokens, g['greedy_tokens'])) if a != b)}"
+        f", reference min margin {min(g['top1_top2_margin']):.3e}")
