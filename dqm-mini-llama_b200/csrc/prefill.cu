@@ -162,6 +162,50 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// QKV epilogue for the pair pp (head hh, pair index i) of token row m, bias
+// already added: rotate (NeoX pairs (i, i + hd/2), Normal pairs (2i, 2i+1))
+// with the position's (cos, sin) and store to q_out or the K / V cache.
+__device__ __forceinline__ void epilogue_qkv(const PrefillGemm& p, int m, int pp, int q_pairs,
+                                             int kv_pairs, int hh, int i, float x0, float x1,
+                                             float2 cs) {
+  const int pos = p.pos0 + m;
+  float* dst;
+  bool rotate = true;
+  int nh;
+  if (pp < q_pairs) {
+    nh = p.n_heads;
+    dst = p.q_out + (size_t)m * p.ldq;
+  } else if (pp < q_pairs + kv_pairs) {
+    nh = p.n_kv_heads;
+    dst = p.k_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
+  } else {
+    nh = p.n_kv_heads;
+    dst = p.v_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
+    rotate = false;
+  }
+  const int half = p.head_dim / 2;
+  int o0, o1;
+  if (rotate && p.neox) {
+    o0 = hh * p.head_dim + i;
+    o1 = o0 + half;
+  } else {
+    o0 = hh * p.head_dim + 2 * i;
+    o1 = o0 + 1;
+  }
+  if (rotate) {
+    const float a = x0, b = x1;
+    if (p.neox) {
+      x0 = __fmaf_rn(a, cs.x, -__fmul_rn(b, cs.y));
+      x1 = __fmaf_rn(a, cs.y, __fmul_rn(b, cs.x));
+    } else {
+      x0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+      x1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+    }
+  }
+  dst[o0] = x0;
+  dst[o1] = x1;
+}
+
 // Output columns n, n+1 (n even) of token row m; column n+1 may lie past p.n.
 __device__ __forceinline__ void epilogue_pair(const PrefillGemm& p, int m, int n, float v0,
                                               float v1) {
@@ -185,81 +229,115 @@ __device__ __forceinline__ void epilogue_pair(const PrefillGemm& p, int m, int n
     }
   } else {  // kEpiQkv
     if (n + 1 >= p.n) return;
-    const int pos = p.pos0 + m;
     const int half = p.head_dim / 2;
-    const int q_pairs = p.n_heads * half;
-    const int kv_pairs = p.n_kv_heads * half;
+    const int q_pairs = p.n_heads * half, kv_pairs = p.n_kv_heads * half;
     const int pp = n / 2;
-    float x0 = v0, x1 = v1;
+    const bool rotate = pp < q_pairs + kv_pairs;
+    const int seg_pair = pp < q_pairs ? pp : (rotate ? pp - q_pairs : pp - q_pairs - kv_pairs);
+    const int hh = seg_pair / half, i = seg_pair % half;
+    const float2 cs =
+        rotate ? p.rope_cs[(size_t)(p.pos0 + m) * half + i] : make_float2(1.0f, 0.0f);
     if (p.bias) {
-      x0 = __fadd_rn(x0, p.bias[n]);
-      x1 = __fadd_rn(x1, p.bias[n + 1]);
+      v0 = __fadd_rn(v0, p.bias[n]);
+      v1 = __fadd_rn(v1, p.bias[n + 1]);
     }
-    int seg_pair, nh;
-    float* dst;
-    bool rotate = true;
-    if (pp < q_pairs) {
-      seg_pair = pp;
-      nh = p.n_heads;
-      dst = p.q_out + (size_t)m * p.ldq;
-    } else if (pp < q_pairs + kv_pairs) {
-      seg_pair = pp - q_pairs;
-      nh = p.n_kv_heads;
-      dst = p.k_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
-    } else {
-      seg_pair = pp - q_pairs - kv_pairs;
-      nh = p.n_kv_heads;
-      dst = p.v_cache + ((size_t)p.layer * p.max_seq + pos) * nh * p.head_dim;
-      rotate = false;
-    }
-    const int h = seg_pair / half, i = seg_pair % half;
-    int o0, o1;
-    if (rotate && p.neox) {
-      o0 = h * p.head_dim + i;
-      o1 = o0 + half;
-    } else {
-      o0 = h * p.head_dim + 2 * i;
-      o1 = o0 + 1;
-    }
-    if (rotate) {
-      const float2 cs = p.rope_cs[(size_t)pos * half + i];
-      const float a = x0, b = x1;
-      if (p.neox) {
-        x0 = __fmaf_rn(a, cs.x, -__fmul_rn(b, cs.y));
-        x1 = __fmaf_rn(a, cs.y, __fmul_rn(b, cs.x));
-      } else {
-        x0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
-        x1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
-      }
-    }
-    dst[o0] = x0;
-    dst[o1] = x1;
+    epilogue_qkv(p, m, pp, q_pairs, kv_pairs, hh, i, v0, v1, cs);
   }
 }
 
 // 32 rows (from m0) x 32 columns (from n0) of finished accumulators staged in
 // shared memory [row][33]: scale by 2^(e+f), then the epilogue (or park the
-// partial sums for split-K).  Lanes 0-15 take the column pairs of one row,
-// lanes 16-31 those of the next, so each store instruction covers whole rows.
+// partial sums for split-K).  Lanes 0-15 take the column pairs of even rows,
+// lanes 16-31 those of odd rows, so each store instruction covers whole row
+// segments.  Every global load of the chunk (residual, RoPE table) is issued
+// before the first store, so the loads overlap instead of serialising;
+// rs_lane holds the row scale of row m0 + lane.
 __device__ __forceinline__ void drain_chunk(const PrefillGemm& p, const float* stage, int m0,
-                                            int n0, int z, int lane) {
-  const int j = lane & 15;
+                                            int n0, int z, int lane, float rs_lane) {
+  constexpr int R = 16;  // rows per lane
+  const int j = lane & 15, r0 = lane >> 4;
   const int n = n0 + 2 * j;
-  if (n >= p.n) return;
-  const float c0 = p.cs[n], c1 = n + 1 < p.n ? p.cs[n + 1] : 0.0f;
-#pragma unroll 1
-  for (int rr = lane >> 4; rr < 32; rr += 2) {
-    const int m = m0 + rr;
-    if (m >= p.m) break;
-    const float rs = p.rs[m];
-    const float v0 = __fmul_rn(__fmul_rn(stage[rr * 33 + 2 * j], rs), c0);
-    const float v1 = __fmul_rn(__fmul_rn(stage[rr * 33 + 2 * j + 1], rs), c1);
-    if (p.plan.splits == 1) {
-      epilogue_pair(p, m, n, v0, v1);
-    } else {
-      float* dst = p.partial + ((size_t)z * p.m + m) * p.n + n;
-      dst[0] = v0;
-      if (n + 1 < p.n) dst[1] = v1;
+  const bool ok0 = n < p.n, ok1 = n + 1 < p.n;
+  const float c0 = ok0 ? p.cs[n] : 0.0f, c1 = ok1 ? p.cs[n + 1] : 0.0f;
+  float v0[R], v1[R];
+#pragma unroll
+  for (int it = 0; it < R; ++it) {
+    const int rr = r0 + 2 * it;
+    const float rs = __shfl_sync(0xffffffffu, rs_lane, rr);
+    v0[it] = __fmul_rn(__fmul_rn(stage[rr * 33 + 2 * j], rs), c0);
+    v1[it] = __fmul_rn(__fmul_rn(stage[rr * 33 + 2 * j + 1], rs), c1);
+  }
+  if (!ok0) return;
+  const int rows = min(R, (p.m - m0 - r0 + 1) / 2);  // rows of this lane below p.m
+  if (p.plan.splits > 1) {
+#pragma unroll
+    for (int it = 0; it < R; ++it) {
+      if (it >= rows) break;
+      float* dst = p.partial + ((size_t)z * p.m + m0 + r0 + 2 * it) * p.n + n;
+      dst[0] = v0[it];
+      if (ok1) dst[1] = v1[it];
+    }
+    return;
+  }
+  if (p.epi == kEpiStore) {
+    const float b0 = p.bias ? p.bias[n] : 0.0f, b1 = p.bias && ok1 ? p.bias[n + 1] : 0.0f;
+    float q0[R], q1[R];
+#pragma unroll
+    for (int it = 0; it < R; ++it) {
+      q0[it] = 0.0f;
+      q1[it] = 0.0f;
+      if (p.residual && it < rows) {
+        const float* rr = p.residual + (size_t)(m0 + r0 + 2 * it) * p.ldy + n;
+        q0[it] = rr[0];
+        if (ok1) q1[it] = rr[1];
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < R; ++it) {
+      if (it >= rows) break;
+      float x0 = v0[it], x1 = v1[it];
+      if (p.bias) {
+        x0 = __fadd_rn(x0, b0);
+        x1 = __fadd_rn(x1, b1);
+      }
+      if (p.residual) {
+        x0 = __fadd_rn(q0[it], x0);
+        x1 = __fadd_rn(q1[it], x1);
+      }
+      float* yr = p.y + (size_t)(m0 + r0 + 2 * it) * p.ldy + n;
+      yr[0] = x0;
+      if (ok1) yr[1] = x1;
+    }
+  } else if (p.epi == kEpiSwiGlu) {
+    if (!ok1) return;
+#pragma unroll
+    for (int it = 0; it < R; ++it) {
+      if (it >= rows) break;
+      const float g = v0[it];
+      const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+      p.y[(size_t)(m0 + r0 + 2 * it) * p.ldy + n / 2] = __fmul_rn(__fmul_rn(g, sig), v1[it]);
+    }
+  } else {  // kEpiQkv: the RoPE rotations of this lane's rows first
+    if (!ok1) return;
+    const int half = p.head_dim / 2;
+    const int pp = n / 2;
+    const int q_pairs = p.n_heads * half, kv_pairs = p.n_kv_heads * half;
+    const bool rotate = pp < q_pairs + kv_pairs;
+    const int seg_pair = pp < q_pairs ? pp : (rotate ? pp - q_pairs : pp - q_pairs - kv_pairs);
+    const int hh = seg_pair / half, i = seg_pair % half;
+    float2 rc[R];
+#pragma unroll
+    for (int it = 0; it < R; ++it)
+      rc[it] = rotate && it < rows
+                   ? p.rope_cs[(size_t)(p.pos0 + m0 + r0 + 2 * it) * half + i]
+                   : make_float2(1.0f, 0.0f);
+    const float bb0 = p.bias ? p.bias[n] : 0.0f, bb1 = p.bias ? p.bias[n + 1] : 0.0f;
+#pragma unroll
+    for (int it = 0; it < R; ++it) {
+      if (it >= rows) break;
+      epilogue_qkv(p, m0 + r0 + 2 * it, pp, q_pairs, kv_pairs, hh, i,
+                   p.bias ? __fadd_rn(v0[it], bb0) : v0[it],
+                   p.bias ? __fadd_rn(v1[it], bb1) : v1[it], rc[it]);
     }
   }
 }
@@ -410,12 +488,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // each 32 x 32 chunk (this warp's rows x 32 columns) goes through shared
       // memory so that the stores are row-contiguous across the warp
       float* stage = epi_stage + (size_t)(warp - 2) * 32 * 33;
+      const int my_row = t.m0 + quarter * 32 + lane;
+      const float rs_lane = my_row < p.m ? p.rs[my_row] : 0.0f;
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) stage[lane * 33 + j] = __uint_as_float(r[c * 32 + j]);
         __syncwarp();
-        drain_chunk(p, stage, t.m0 + quarter * 32, t.n0 + c * 32, t.z, lane);
+        drain_chunk(p, stage, t.m0 + quarter * 32, t.n0 + c * 32, t.z, lane, rs_lane);
         __syncwarp();
       }
     }
