@@ -279,6 +279,39 @@ def time_prefill(pkg, torch, S, w, n_tokens: int = 602):
     }
 
 
+def time_q4_ctx2048(pkg, torch, S, n_prompt: int = 2048, n_steps: int = 128):
+    """Qwen2-0.5B-architecture with Q4_0 weights: a 2048-id prompt through the
+    batched prefill, then 128 greedy decode steps over the 2048-long KV cache
+    (device argmax, graph replays), each timed with CUDA events."""
+    w = S.make_model(S.QWEN2_0_5B, S.Q40, 20261202)
+    model = pkg.Model.from_synth(w, max_seq_len=n_prompt + n_steps)
+    ctx = pkg.Context(model)
+    stream = torch.cuda.ExternalStream(ctx.stream_handle)
+    prompt = S.prompt_tokens(w.cfg["vocab"], n_prompt, 3).tolist()
+    ctx.ForwardBatch(prompt[:64], 0)  # allocates the prefill buffers
+    ctx.reset()
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(stream)
+    logits = ctx.ForwardBatch(prompt, 0)
+    e1.record(stream)
+    first = int(np.argmax(logits))
+    ctx.decode_enqueue(first, n_prompt, n_steps)
+    e2.record(stream)
+    e2.synchronize()
+    pre, dec = e0.elapsed_time(e1) / 1e3, e1.elapsed_time(e2) / 1e3
+    ctx.close()
+    model.close()
+    bytes_per_token = (sum(getattr(L, n).nbytes for L in w.layers
+                           for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))
+                       + w.token_embd.nbytes + 24576 * (n_prompt + n_steps // 2))
+    return {"workload": "qwen2-0.5b-architecture Q4_0, 2048-id prompt (batched prefill) then "
+                        "128 greedy decode steps at positions 2048..2175",
+            "prefill_tok_s": round(n_prompt / pre, 1), "decode_tok_s": round(n_steps / dec, 1),
+            "decode_ms_per_token": round(dec / n_steps * 1e3, 4),
+            "decode_bytes_per_token": bytes_per_token,
+            "decode_GB_s": round(bytes_per_token * n_steps / dec / 1e9, 1)}
+
+
 def reference_decode(w, steps: int, warmup: int, threads: int):
     """The reference's CPU decode (oracle/_ref) on this host: returns s/token."""
     orc = ge.load_oracle()
@@ -423,6 +456,7 @@ def main():
     ctx.close()
     model.close()
     prefill = time_prefill(pkg, torch, S, w) if rank == 0 else None
+    q4_ctx2048 = time_q4_ctx2048(pkg, torch, S) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -463,6 +497,7 @@ def main():
                      "us_per_launch": round(gemv_s * 1e6, 2)},
         "gemv_sweep": sweep,
         "prefill": prefill,
+        "q4_0_ctx2048": q4_ctx2048,
         "cpu_baseline": cpu,
         "clocks": clocks,
     }

@@ -15,8 +15,8 @@ from typing import Optional, Sequence
 import numpy as np
 
 from . import synth
-from ._lib import (F32, Q40, Q80, CudaError, ModelConfig, ModelStats, OutOfRange, build, check,
-                   lib)
+from ._lib import (F32, Q40, Q80, CudaError, ModelConfig, ModelStats, OutOfRange, TpPlan, build,
+                   check, lib)
 
 __all__ = [
     "F32", "Q80", "Q40", "OutOfRange", "CudaError", "build", "lib", "synth",
@@ -272,6 +272,26 @@ def CudaAttentionDecodeDeviceInput(q, kv: CudaKvCache, layer: int, pos: int, n_h
 
 
 # ------------------------------------------------------------ engine
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for Model.set_tp."""
+    buf = C.create_string_buffer(128)
+    check(lib().dqmk_nccl_unique_id(buf))
+    return buf.raw
+
+
+def tp_plan(cfg: dict, rank: int, world: int, max_seq_len: int = 1) -> dict:
+    """This rank's tensor-parallel shard of a model shape (host only)."""
+    c = ModelConfig()
+    c.vocab_size, c.dim, c.hidden_dim = cfg["vocab"], cfg["dim"], cfg["hidden"]
+    c.n_layers, c.n_heads, c.n_kv_heads = cfg["n_layers"], cfg["n_heads"], cfg["n_kv_heads"]
+    c.head_dim = cfg["dim"] // cfg["n_heads"]
+    c.max_seq_len = max_seq_len
+    c.rope_theta, c.rms_norm_eps, c.rope_neox = cfg["rope_theta"], cfg["eps"], 1
+    p = TpPlan()
+    check(lib().dqmk_tp_plan_get(C.byref(c), rank, world, C.byref(p)))
+    return {n: getattr(p, n) for n, _ in TpPlan._fields_}
+
+
 class Model:
     """A device-resident model: UploadModelWeightsToCuda + the fused layouts.
 
@@ -294,6 +314,10 @@ class Model:
         check(lib().dqmk_model_create(C.byref(c), device, C.byref(h)))
         self.h = h
 
+    def set_tp(self, rank: int, world: int, nccl_id: Optional[bytes]) -> None:
+        """Tensor parallelism before finalize (collective: all ranks call it)."""
+        check(lib().dqmk_model_set_tp(self.h, rank, world, nccl_id))
+
     def upload(self, name: str, qtype: int, data, rows: int, cols: int) -> None:
         if hasattr(data, "data_ptr"):
             ptr, nbytes = data.data_ptr(), data.numel() * data.element_size()
@@ -308,9 +332,13 @@ class Model:
         check(lib().dqmk_model_finalize(self.h))
 
     @classmethod
-    def from_synth(cls, w: "synth.SynthModel", max_seq_len: int, device: int = 0) -> "Model":
+    def from_synth(cls, w: "synth.SynthModel", max_seq_len: int, device: int = 0,
+                   tp: Optional[tuple] = None) -> "Model":
+        """tp = (rank, world, nccl_id): keep this rank's tensor-parallel shard."""
         c = w.cfg
         m = cls(c, max_seq_len, device)
+        if tp is not None:
+            m.set_tp(*tp)
         qt, hd = w.qtype, c["dim"] // c["n_heads"]
         qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
         m.upload("token_embedding", qt, w.token_embd, c["vocab"], c["dim"])

@@ -43,6 +43,12 @@ class ModelStats(C.Structure):
         "device_to_host_bytes")]
 
 
+class TpPlan(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("rank", "world", "q_head0", "n_q_heads", "kv_head0",
+                                         "n_kv_heads", "hidden0", "hidden", "vocab0", "vocab",
+                                         "vocab_stride")]
+
+
 SIGNATURES = {
     "dqmk_last_error": ([], C.c_char_p),
     "dqmk_built": ([], _i),
@@ -72,6 +78,9 @@ SIGNATURES = {
     "dqmk_model_destroy": ([_vp], _i),
     "dqmk_model_upload": ([_vp, C.c_char_p, _i, _vp, _sz, _i, _i], _i),
     "dqmk_model_finalize": ([_vp], _i),
+    "dqmk_tp_plan_get": ([C.POINTER(ModelConfig), _i, _i, C.POINTER(TpPlan)], _i),
+    "dqmk_nccl_unique_id": ([C.c_char_p], _i),
+    "dqmk_model_set_tp": ([_vp, _i, _i, C.c_char_p], _i),
     "dqmk_model_stats_get": ([_vp, C.POINTER(ModelStats)], _i),
     "dqmk_model_stats_reset": ([_vp], _i),
     "dqmk_model_memory_bytes": ([_vp], _sz),

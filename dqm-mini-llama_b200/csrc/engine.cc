@@ -27,6 +27,7 @@
 #include "dqmk.h"
 #include "internal.h"
 #include "prefill.h"
+#include "tp.h"
 
 using namespace dqmk;
 
@@ -84,7 +85,9 @@ struct dqmk_model {
   std::vector<Layer> layers;
   Packed embd, lm_head;
   bool tied = true;
-  bool prefill_ready = false;  // scales transposed and TMA maps built
+  bool prefill_ready = false;  // two-term weight planes and TMA maps built
+  dqmk_tp_plan tp{};           // this model's shard (world 1: everything)
+  void* comm = nullptr;        // NCCL communicator when tp.world > 1
   float* final_norm = nullptr;
   float2* rope_cs = nullptr;
   std::vector<void*> allocs;
@@ -96,6 +99,7 @@ struct dqmk_model {
     for (void* p : allocs) cudaFree(p);
     for (auto& kv : raw)
       if (kv.second.dev) cudaFree(kv.second.dev);
+    tp_comm_destroy(comm);
   }
 };
 
@@ -103,6 +107,8 @@ struct dqmk_context {
   dqmk_model* m = nullptr;
   cudaStream_t stream = nullptr;
   float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+  float* part = nullptr;        // tensor parallel: row-parallel partial sums [dim]
+  float* logits_all = nullptr;  // tensor parallel: gathered logits [world][vocab_stride]
   float *keys = nullptr, *values = nullptr, *partials = nullptr;
   // device state block: [argmax u64][lm ticket u32][token i32][pos i32][pad]
   //                     [attention tickets u32 x n_kv] ...
@@ -242,12 +248,12 @@ std::vector<int> identity_map(int n) {
 
 // Row order of the fused q|k|v weight: each RoPE pair adjacent.  NeoX pairs
 // (i, i + hd/2) of every head, Normal pairs (2i, 2i+1); V rows keep their
-// natural adjacent pairs.
-std::vector<int> qkv_map(const dqmk_model_config& c) {
+// natural adjacent pairs.  Only the heads of the tensor-parallel shard.
+std::vector<int> qkv_map(const dqmk_model_config& c, const dqmk_tp_plan& tp) {
   const int hd = c.head_dim, half = hd / 2;
   std::vector<int> map;
-  auto add_heads = [&](int base, int n_heads, bool rope) {
-    for (int h = 0; h < n_heads; ++h)
+  auto add_heads = [&](int base, int head0, int n_heads, bool rope) {
+    for (int h = head0; h < head0 + n_heads; ++h)
       for (int i = 0; i < half; ++i) {
         if (rope && c.rope_neox) {
           map.push_back(base + h * hd + i);
@@ -259,10 +265,37 @@ std::vector<int> qkv_map(const dqmk_model_config& c) {
       }
   };
   const int qd = c.n_heads * hd, kvd = c.n_kv_heads * hd;
-  add_heads(0, c.n_heads, true);
-  add_heads(qd, c.n_kv_heads, true);
-  add_heads(qd + kvd, c.n_kv_heads, false);
+  add_heads(0, tp.q_head0, tp.n_q_heads, true);
+  add_heads(qd, tp.kv_head0, tp.n_kv_heads, true);
+  add_heads(qd + kvd, tp.kv_head0, tp.n_kv_heads, false);
   return map;
+}
+
+// Columns [c0, c0 + n) of every row of a quantized weight (c0 and n multiples
+// of 32) as a new temporary Raw whose device blocks the caller frees.
+int slice_cols(const Raw& r, int c0, int n, Raw* out, const char* api) {
+  const size_t bb = block_bytes(r.qtype);
+  const int nb = (r.cols + 31) / 32, nbl = (n + 31) / 32;
+  out->qtype = r.qtype;
+  out->rows = r.rows;
+  out->cols = n;
+  cudaError_t e = cudaMalloc(&out->dev, (size_t)r.rows * nbl * bb);
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  e = cudaMemcpy2D(out->dev, nbl * bb, static_cast<const char*>(r.dev) + (size_t)(c0 / 32) * bb,
+                   nb * bb, nbl * bb, r.rows, cudaMemcpyDeviceToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(out->dev);
+    out->dev = nullptr;
+    return cuda_fail(api, e);
+  }
+  return DQMK_OK;
+}
+
+// Rows [r0, r0 + n) map.
+std::vector<int> range_map(int r0, int n) {
+  std::vector<int> v(n);
+  for (int i = 0; i < n; ++i) v[i] = r0 + i;
+  return v;
 }
 
 int check_model(const dqmk_model* m, const char* api) {
@@ -292,12 +325,31 @@ extern "C" int dqmk_model_create(const dqmk_model_config* config, int device_id,
   auto* m = new dqmk_model();
   m->cfg = c;
   m->device = device_id;
+  m->tp = dqmk_tp_plan{0, 1, 0, c.n_heads, 0, c.n_kv_heads, 0, c.hidden_dim,
+                       0, c.vocab_size, c.vocab_size};
   *out = m;
   return DQMK_OK;
 }
 
 extern "C" int dqmk_model_destroy(dqmk_model* model) {
   delete model;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_model_set_tp(dqmk_model* m, int rank, int world, const unsigned char* id) {
+  const char* api = "dqmk_model_set_tp";
+  int rc = check_model(m, api);
+  if (rc) return rc;
+  if (m->finalized) return fail(DQMK_ERR_INVALID, std::string(api) + ": model already finalized");
+  if (m->comm) return fail(DQMK_ERR_INVALID, std::string(api) + ": already set");
+  dqmk_tp_plan plan;
+  if ((rc = tp_plan(m->cfg, rank, world, &plan))) return rc;
+  if (world > 1) {
+    if (!id) return fail(DQMK_ERR_INVALID, std::string(api) + ": null NCCL id");
+    cudaSetDevice(m->device);
+    if ((rc = tp_comm_create(rank, world, id, &m->comm))) return rc;
+  }
+  m->tp = plan;
   return DQMK_OK;
 }
 
@@ -374,21 +426,25 @@ extern "C" int dqmk_model_finalize(dqmk_model* m) {
   if ((rc = need("final_norm", DQMK_F32, 1, c.dim, &fn))) return rc;
   if ((rc = upload_f32(m, fn->host, &m->final_norm, api))) return rc;
   if ((rc = pack_rows(m, {emb}, identity_map(c.vocab_size), &m->embd, api))) return rc;
+  const dqmk_tp_plan& tp = m->tp;
   auto lm = m->raw.find("lm_head");
   m->tied = lm == m->raw.end();
   if (!m->tied) {
     const Raw* l = nullptr;
     if ((rc = need("lm_head", 1, c.vocab_size, c.dim, &l))) return rc;
-    if ((rc = pack_rows(m, {l}, identity_map(c.vocab_size), &m->lm_head, api))) return rc;
+    if ((rc = pack_rows(m, {l}, range_map(tp.vocab0, tp.vocab), &m->lm_head, api))) return rc;
+  } else if (tp.world > 1) {
+    // vocabulary-parallel slice of the tied embedding blocks
+    if ((rc = pack_rows(m, {emb}, range_map(tp.vocab0, tp.vocab), &m->lm_head, api))) return rc;
   } else {
     m->lm_head = m->embd;
   }
   m->layers.resize(c.n_layers);
-  const std::vector<int> qmap = qkv_map(c);
-  std::vector<int> gmap(2 * c.hidden_dim);
-  for (int o = 0; o < c.hidden_dim; ++o) {
-    gmap[2 * o] = o;
-    gmap[2 * o + 1] = c.hidden_dim + o;
+  const std::vector<int> qmap = qkv_map(c, tp);
+  std::vector<int> gmap(2 * tp.hidden);
+  for (int o = 0; o < tp.hidden; ++o) {
+    gmap[2 * o] = tp.hidden0 + o;
+    gmap[2 * o + 1] = c.hidden_dim + tp.hidden0 + o;
   }
   for (int l = 0; l < c.n_layers; ++l) {
     const std::string p = "layers." + std::to_string(l) + ".";
@@ -409,9 +465,21 @@ extern "C" int dqmk_model_finalize(dqmk_model* m) {
     if ((rc = upload_f32(m, an->host, &L.attn_norm, api))) return rc;
     if ((rc = upload_f32(m, ffn->host, &L.ffn_norm, api))) return rc;
     if ((rc = pack_rows(m, {wq, wk, wv}, qmap, &L.qkv, api))) return rc;
-    if ((rc = pack_rows(m, {wo}, identity_map(c.dim), &L.wo, api))) return rc;
     if ((rc = pack_rows(m, {wg, wu}, gmap, &L.gate_up, api))) return rc;
-    if ((rc = pack_rows(m, {wd}, identity_map(c.dim), &L.down, api))) return rc;
+    if (tp.world == 1) {
+      if ((rc = pack_rows(m, {wo}, identity_map(c.dim), &L.wo, api))) return rc;
+      if ((rc = pack_rows(m, {wd}, identity_map(c.dim), &L.down, api))) return rc;
+    } else {  // row-parallel: this shard's K columns
+      Raw so, sd;
+      if ((rc = slice_cols(*wo, tp.q_head0 * hd, tp.n_q_heads * hd, &so, api))) return rc;
+      rc = pack_rows(m, {&so}, identity_map(c.dim), &L.wo, api);
+      cudaFree(so.dev);
+      if (rc) return rc;
+      if ((rc = slice_cols(*wd, tp.hidden0, tp.hidden, &sd, api))) return rc;
+      rc = pack_rows(m, {&sd}, identity_map(c.dim), &L.down, api);
+      cudaFree(sd.dev);
+      if (rc) return rc;
+    }
     // optional QKV bias, permuted like the rows
     auto bq = m->raw.find(p + "bq"), bk = m->raw.find(p + "bk"), bv = m->raw.find(p + "bv");
     const bool any = bq != m->raw.end() || bk != m->raw.end() || bv != m->raw.end();
@@ -434,7 +502,7 @@ extern "C" int dqmk_model_finalize(dqmk_model* m) {
   }
   // batched-prefill side tables (see prefill.cu); skipped for head sizes the
   // prefill attention kernel does not take, which then prefill token by token
-  if (hd == 64 || hd == 128) {
+  if ((hd == 64 || hd == 128) && tp.world == 1) {
     // the decode path keeps streaming the packed quants; the tensor cores
     // take the same values as two exact fp16 planes per weight
     auto side = [&](const Packed& w, float** cs, CUtensorMap* maps) -> int {
@@ -522,7 +590,10 @@ int enqueue_step(dqmk_context* x) {
   const bool pdl = use_pdl();
   dqmk_model* m = x->m;
   const dqmk_model_config& c = m->cfg;
+  const dqmk_tp_plan& tp = m->tp;
+  const bool tpar = tp.world > 1;
   cudaStream_t s = x->stream;
+  int rc;
   EmbedArgs ea = {};
   ea.qtype = m->embd.qtype;
   ea.qs = m->embd.qs();
@@ -555,8 +626,8 @@ int enqueue_step(dqmk_context* x) {
     g.v_cache = x->values;
     g.layer = l;
     g.max_seq = c.max_seq_len;
-    g.n_heads = c.n_heads;
-    g.n_kv_heads = c.n_kv_heads;
+    g.n_heads = tp.n_q_heads;
+    g.n_kv_heads = tp.n_kv_heads;
     g.head_dim = c.head_dim;
     g.neox = c.rope_neox;
     DQMK_CUDA_RET(api, launch_gemv(g, s, pdl));
@@ -566,10 +637,10 @@ int enqueue_step(dqmk_context* x) {
     at.keys = x->keys;
     at.values = x->values;
     at.max_seq = c.max_seq_len;
-    at.n_kv_heads = c.n_kv_heads;
+    at.n_kv_heads = tp.n_kv_heads;
     at.head_dim = c.head_dim;
     at.layer = l;
-    at.n_heads = c.n_heads;
+    at.n_heads = tp.n_q_heads;
     at.pos_dev = x->pos_slot();
     at.out = x->att;
     at.partials = x->partials;
@@ -586,9 +657,13 @@ int enqueue_step(dqmk_context* x) {
     o.kp = L.wo.kp;
     o.x = x->att;
     o.epi = kEpiStore;
-    o.residual = x->x;
-    o.y = x->x;
+    o.residual = tpar ? nullptr : x->x;
+    o.y = tpar ? x->part : x->x;
     DQMK_CUDA_RET(api, launch_gemv(o, s, pdl));
+    if (tpar) {  // complete the row-parallel sum, then the residual add
+      if ((rc = tp_allreduce_sum(m->comm, x->part, c.dim, s, api))) return rc;
+      DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
+    }
 
     GemvArgs gu = {};
     gu.qtype = L.gate_up.qtype;
@@ -613,9 +688,13 @@ int enqueue_step(dqmk_context* x) {
     dn.kp = L.down.kp;
     dn.x = x->h;
     dn.epi = kEpiStore;
-    dn.residual = x->x;
-    dn.y = x->x;
+    dn.residual = tpar ? nullptr : x->x;
+    dn.y = tpar ? x->part : x->x;
     DQMK_CUDA_RET(api, launch_gemv(dn, s, pdl));
+    if (tpar) {
+      if ((rc = tp_allreduce_sum(m->comm, x->part, c.dim, s, api))) return rc;
+      DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
+    }
   }
   GemvArgs lg = {};
   lg.qtype = m->lm_head.qtype;
@@ -630,12 +709,36 @@ int enqueue_step(dqmk_context* x) {
   lg.epi = kEpiLogits;
   lg.y = x->logits;
   lg.argmax_slot = x->argmax_slot();
-  lg.ticket = x->lm_ticket();
+  lg.row_offset = tp.vocab0;
+  lg.ticket = tpar ? nullptr : x->lm_ticket();
   lg.token_slot = x->token_slot();
   lg.pos_slot = x->pos_slot();
   lg.history = x->history_dev;
   lg.history_cap = c.max_seq_len;
   DQMK_CUDA_RET(api, launch_gemv(lg, s, pdl));
+  if (tpar) {  // global greedy choice: max over the ranks' (value, index) keys
+    if ((rc = tp_allreduce_max_u64(m->comm, x->argmax_slot(), 1, s, api))) return rc;
+    DQMK_CUDA_RET(api, launch_greedy_advance(x->argmax_slot(), x->token_slot(), x->pos_slot(),
+                                             x->history_dev, c.max_seq_len, s));
+  }
+  return DQMK_OK;
+}
+
+// Host logits of the last step: the local vocabulary slice, or under tensor
+// parallelism all slices gathered (every rank takes part).
+int copy_logits(dqmk_context* x, float* logits, const char* api) {
+  dqmk_model* m = x->m;
+  const size_t bytes = (size_t)m->cfg.vocab_size * sizeof(float);
+  const float* src = x->logits;
+  if (m->tp.world > 1) {
+    int rc = tp_allgather(m->comm, x->logits, x->logits_all, (size_t)m->tp.vocab_stride,
+                          x->stream, api);
+    if (rc) return rc;
+    src = x->logits_all;
+  }
+  DQMK_CUDA_RET(api, cudaMemcpyAsync(logits, src, bytes, cudaMemcpyDeviceToHost, x->stream));
+  m->stats.device_to_host_copies += 1;
+  m->stats.device_to_host_bytes += bytes;
   return DQMK_OK;
 }
 
@@ -925,8 +1028,9 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
   DQMK_CUDA_RET(api, cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking));
   DQMK_CUDA_RET(api, cudaMallocHost(&x->pinned, 64));
   DQMK_CUDA_RET(api, cudaEventCreateWithFlags(&x->staged, cudaEventDisableTiming));
-  const size_t kv = (size_t)c.n_layers * c.max_seq_len * c.n_kv_heads * c.head_dim;
-  x->attn_splits = attention_splits(c.max_seq_len, c.n_kv_heads);
+  const dqmk_tp_plan& tp = m->tp;
+  const size_t kv = (size_t)c.n_layers * c.max_seq_len * tp.n_kv_heads * c.head_dim;
+  x->attn_splits = attention_splits(c.max_seq_len, tp.n_kv_heads);
   void* p = nullptr;
   int rc;
   const int hd = c.head_dim;
@@ -934,22 +1038,24 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
     float** dst;
     size_t n;
   } bufs[] = {{&x->x, (size_t)c.dim},
-              {&x->q, (size_t)c.n_heads * hd},
-              {&x->att, (size_t)c.n_heads * hd},
-              {&x->h, (size_t)c.hidden_dim},
-              {&x->logits, (size_t)c.vocab_size},
+              {&x->q, (size_t)tp.n_q_heads * hd},
+              {&x->att, (size_t)tp.n_q_heads * hd},
+              {&x->h, (size_t)tp.hidden},
+              {&x->logits, (size_t)tp.vocab_stride},
               {&x->keys, kv},
               {&x->values, kv},
-              {&x->partials, attention_partials_floats(c.n_heads, hd, x->attn_splits)}};
+              {&x->partials, attention_partials_floats(tp.n_q_heads, hd, x->attn_splits)},
+              {&x->part, (size_t)c.dim},
+              {&x->logits_all, tp.world > 1 ? (size_t)tp.vocab_stride * tp.world : 1}};
   for (auto& b : bufs) {
     if ((rc = dev_alloc(x->allocs, b.n * sizeof(float), &p, api))) return rc;
     *b.dst = static_cast<float*>(p);
   }
-  if ((rc = dev_alloc(x->allocs, 64 + 4 * (size_t)c.n_kv_heads + 64, &p, api))) return rc;
+  if ((rc = dev_alloc(x->allocs, 64 + 4 * (size_t)tp.n_kv_heads + 64, &p, api))) return rc;
   x->state = static_cast<unsigned char*>(p);
   if ((rc = dev_alloc(x->allocs, (size_t)c.max_seq_len * sizeof(int), &p, api))) return rc;
   x->history_dev = static_cast<int*>(p);
-  DQMK_CUDA_RET(api, cudaMemset(x->state, 0, 64 + 4 * (size_t)c.n_kv_heads + 64));
+  DQMK_CUDA_RET(api, cudaMemset(x->state, 0, 64 + 4 * (size_t)tp.n_kv_heads + 64));
   DQMK_CUDA_RET(api, cudaMemset(x->keys, 0, kv * sizeof(float)));
   DQMK_CUDA_RET(api, cudaMemset(x->values, 0, kv * sizeof(float)));
   DQMK_CUDA_RET(api, gemv_prepare());
@@ -968,7 +1074,7 @@ extern "C" int dqmk_context_reset(dqmk_context* x) {
   const char* api = "MiniLlamaContext";
   if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + ": null context");
   const dqmk_model_config& c = x->m->cfg;
-  const size_t kv = (size_t)c.n_layers * c.max_seq_len * c.n_kv_heads * c.head_dim;
+  const size_t kv = (size_t)c.n_layers * c.max_seq_len * x->m->tp.n_kv_heads * c.head_dim;
   DQMK_CUDA_RET(api, cudaMemsetAsync(x->keys, 0, kv * sizeof(float), x->stream));
   DQMK_CUDA_RET(api, cudaMemsetAsync(x->values, 0, kv * sizeof(float), x->stream));
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
@@ -996,12 +1102,7 @@ extern "C" int dqmk_forward_token(dqmk_context* x, int token, int pos, float* lo
   cudaSetDevice(x->m->device);
   if ((rc = ensure_graph(x))) return rc;
   if ((rc = launch_token(x, token, pos))) return rc;
-  if (logits) {
-    const size_t bytes = (size_t)x->m->cfg.vocab_size * sizeof(float);
-    DQMK_CUDA_RET(api, cudaMemcpyAsync(logits, x->logits, bytes, cudaMemcpyDeviceToHost, x->stream));
-    x->m->stats.device_to_host_copies += 1;
-    x->m->stats.device_to_host_bytes += bytes;
-  }
+  if (logits && (rc = copy_logits(x, logits, api))) return rc;
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
   return check_device_error(api);
 }
@@ -1037,12 +1138,7 @@ extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int*
       x->history.push_back(tokens[i]);
     }
   }
-  if (logits) {
-    const size_t bytes = (size_t)x->m->cfg.vocab_size * sizeof(float);
-    DQMK_CUDA_RET(api, cudaMemcpyAsync(logits, x->logits, bytes, cudaMemcpyDeviceToHost, x->stream));
-    x->m->stats.device_to_host_copies += 1;
-    x->m->stats.device_to_host_bytes += bytes;
-  }
+  if (logits && (rc = copy_logits(x, logits, api))) return rc;
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
   if ((rc = check_prefill_error(api))) return rc;
   return check_device_error(api);

@@ -195,7 +195,7 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
       const int row = grp * RPW + r;
       if (lane == r && row < a.n_rows) {
         a.y[row] = acc[r];
-        const unsigned long long key = argmax_key(acc[r], (uint32_t)row);
+        const unsigned long long key = argmax_key(acc[r], (uint32_t)(row + a.row_offset));
         best = key > best ? key : best;
       }
     }
@@ -465,6 +465,8 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
       for (int w = 0; w < kWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
       if (a.argmax_slot) {
         atomicMax(a.argmax_slot, b);
+      }
+      if (a.argmax_slot && a.ticket) {
         __threadfence();
         const unsigned int done = atomicAdd(a.ticket, 1u);
         if (done == gridDim.x - 1) {
@@ -933,9 +935,8 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
       unsigned long long b = 0ull;
       for (int w = 0; w < kTmaWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
       atomicMax(a.argmax_slot, b);
-      __threadfence();
-      const unsigned int done = atomicAdd(a.ticket, 1u);
-      if (done == gridDim.x - 1) {
+      const unsigned int done = a.ticket ? (__threadfence(), atomicAdd(a.ticket, 1u)) : 0u;
+      if (a.ticket && done == gridDim.x - 1) {
         __threadfence();
         const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
         const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));

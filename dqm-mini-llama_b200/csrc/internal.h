@@ -68,7 +68,9 @@ struct GemvArgs {
   int layer, max_seq, n_heads, n_kv_heads, head_dim, neox;
   // kEpiLogits
   unsigned long long* argmax_slot;  // packed (value, index) max
-  unsigned int* ticket;             // CTA completion counter (reset by the last CTA)
+  int row_offset;                   // index of packed row 0 in the full vocabulary
+  unsigned int* ticket;             // CTA completion counter (reset by the last CTA);
+                                    // nullptr: no greedy advance in the kernel
   int* token_slot;                  // greedy: next token
   int* pos_slot;                    // greedy: next position (incremented)
   int* history;                     // greedy: token written at history[pos+1]
@@ -117,6 +119,8 @@ cudaError_t launch_embed_blocks(int qtype, const void* blocks, int dim, int toke
                                 cudaStream_t s);
 cudaError_t launch_argmax(const float* x, int n, unsigned long long* slot, int* index,
                           cudaStream_t s);
+cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, int* pos,
+                                  int* history, int cap, cudaStream_t s);
 cudaError_t launch_kv_write(float* keys, float* values, int max_seq, int n_kv_heads,
                             int head_dim, int layer, int pos, const float* k, const float* v,
                             cudaStream_t s);

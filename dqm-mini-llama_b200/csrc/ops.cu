@@ -239,6 +239,24 @@ cudaError_t launch_argmax(const float* x, int n, unsigned long long* slot, int* 
   return cudaGetLastError();
 }
 
+// Greedy decode state after a tensor-parallel lm_head: the all-reduced
+// (value, index) key names the next token; record it, advance the position.
+__global__ void greedy_advance_kernel(const unsigned long long* slot, int* token, int* pos,
+                                      int* history, int cap) {
+  const unsigned long long key = *slot;
+  const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+  const int p = *pos;
+  if (history && p >= 0 && p < cap) history[p] = idx;
+  *token = idx;
+  *pos = p + 1;
+}
+
+cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, int* pos,
+                                  int* history, int cap, cudaStream_t s) {
+  greedy_advance_kernel<<<1, 1, 0, s>>>(slot, token, pos, history, cap);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_kv_write(float* keys, float* values, int max_seq, int n_kv_heads,
                             int head_dim, int layer, int pos, const float* k, const float* v,
                             cudaStream_t s) {

@@ -282,6 +282,29 @@ int dqmk_model_upload(dqmk_model* model, const char* name, int qtype, const void
 
 /* Validates that every tensor is present and builds the fused layouts. */
 int dqmk_model_finalize(dqmk_model* model);
+
+/* Tensor parallelism (Megatron split; no reference counterpart -- the
+ * reference runs one device).  A rank's share of the model: */
+typedef struct dqmk_tp_plan {
+  int rank, world;
+  int q_head0, n_q_heads;   /* query heads: columns of wq, rows of wo's K */
+  int kv_head0, n_kv_heads; /* key/value heads: wk, wv rows; the KV cache shard */
+  int hidden0, hidden;      /* FFN: w_gate / w_up rows, w_down's K columns */
+  int vocab0, vocab;        /* lm_head rows (vocabulary-parallel) */
+  int vocab_stride;         /* ceil(vocab_size / world): rows per rank slot */
+} dqmk_tp_plan;
+/* Host-only: the plan of `rank` in a `world`-way group (DQMK_ERR_UNSUPPORTED
+ * when heads, key/value heads, or the FFN / query widths at 32-value blocks
+ * do not split evenly). */
+int dqmk_tp_plan_get(const dqmk_model_config* config, int rank, int world, dqmk_tp_plan* out);
+/* NCCL unique id (128 bytes) for dqmk_model_set_tp; created on one rank and
+ * passed to the others out of band (e.g. a torch.distributed broadcast). */
+int dqmk_nccl_unique_id(unsigned char* id_out);
+/* Before dqmk_model_finalize, with the full weights uploaded: the model keeps
+ * only rank `rank`'s shard, and its decode step all-reduces the row-parallel
+ * projections over NCCL.  Collective: every rank of the group calls it with
+ * the same id, each on its own device. */
+int dqmk_model_set_tp(dqmk_model* model, int rank, int world, const unsigned char* nccl_id);
 int dqmk_model_stats_get(const dqmk_model* model, dqmk_model_stats* out);
 int dqmk_model_stats_reset(dqmk_model* model);
 /* ModelCudaMemoryBytes (include/dqm_llama/model.h:119). */

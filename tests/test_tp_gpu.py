@@ -1,0 +1,75 @@
+"""Tensor parallelism on 2 (and 4) GPUs: a reduced Qwen2-7B-shaped Q4_0 model
+(full layer widths: dim 3584, FFN 18944, 28/4 heads of 128; one layer; 8192
+vocabulary ids; untied lm_head) sharded Megatron-style, one rank per GPU over
+NCCL.  The gathered prompt logits must sit within 1e-3 x logit range of the
+oracle, greedy tokens must equal the oracle's, and the degrees must agree with
+each other.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+import tp_worker  # noqa: E402
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.fixture(scope="module")
+def reference(pkg, orc, S):
+    w, prompt = tp_worker.reduced_7b(S)
+    r = tp_worker.REDUCED_7B
+    om = orc.OracleModel(w, r["n_prompt"] + r["n_steps"])
+    for i, t in enumerate(prompt):
+        logits = om.forward_token(t, i)
+    first_logits = logits.copy()
+    tokens, margins = [], []
+    pos = r["n_prompt"]
+    for step in range(r["n_steps"]):
+        top2 = np.sort(logits)[-2:]
+        margins.append(float(top2[1] - top2[0]))
+        tok = int(orc.argmax(logits))
+        tokens.append(tok)
+        logits = om.forward_token(tok, pos)
+        pos += 1
+    return first_logits, tokens, logits, min(margins)
+
+
+def test_tensor_parallel_matches_oracle(cuda, reference, tmp_path):
+    n_gpu = cuda.cuda.device_count()
+    if n_gpu < 2:
+        pytest.skip("tensor parallelism needs at least 2 GPUs")
+    first_logits, ref_tokens, last_logits, margin = reference
+    rng = float(first_logits.max() - first_logits.min())
+    results = {}
+    for world in [w for w in (2, 4) if w <= n_gpu]:
+        out = tmp_path / f"tp{world}.npz"
+        cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+               "--nnodes=1", f"--nproc-per-node={world}", "--master-addr=127.0.0.1",
+               f"--master-port={_free_port()}", os.path.join(ROOT, "tests", "tp_worker.py"),
+               "--mode", "gpu", "--out", str(out)]
+        env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=700, env=env)
+        assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-6000:]
+        got = np.load(out)
+        err = float(np.abs(got["logits"] - first_logits).max())
+        assert err <= 1e-3 * rng, f"TP{world}: prompt logits err {err:.3e}, range {rng:.3f}"
+        assert got["tokens"].tolist() == ref_tokens, (got["tokens"].tolist(), ref_tokens, margin)
+        srng = float(last_logits.max() - last_logits.min())
+        serr = float(np.abs(got["step_logits"] - last_logits).max())
+        assert serr <= 1e-3 * srng, f"TP{world}: step logits err {serr:.3e}"
+        results[world] = got
+        print(f"TP{world}: prompt logit err {err / rng:.2e} of range, min margin {margin:.2e}")
+    if len(results) == 2:
+        a, b = results[2]["logits"], results[4]["logits"]
+        assert float(np.abs(a - b).max()) <= 1e-3 * rng
