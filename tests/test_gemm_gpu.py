@@ -10,8 +10,9 @@ hi*hi + hi*lo + lo*hi in fp32 over all of K.  The test bound per output is
     |y - ref| <= 1e-5 * sum_k |W[o,k] x[k]|
 
 (fp32 summation in a different order than the reference's per-element FMA
-chain, plus the 2^-22 split and the dropped lo*lo term), against the oracle's F32 LinearQ80 / LinearQ40
-(itself pinned to the reference), on ragged shapes: single rows, rows across
+chain, plus the 2^-22 split and the dropped lo*lo term), against the
+oracle's F32 LinearQ80 / LinearQ40 (itself pinned to the reference), on
+ragged shapes: single rows, rows across
 the 128-row tile boundary, K tails (in % 32 != 0, in % 128 != 0),
 out % 128 != 0, split-K (few output tiles), a zero row, rows with outliers,
 bias and an in-place residual.

@@ -1,12 +1,12 @@
 """GPU parity of the batched prefill (ForwardBatch over consecutive positions).
 
 The reference's ForwardBatch runs ForwardToken once per token
-(src/batch.cc:35-40).  Here a prompt runs layer by layer as int8
-tensor-core GEMMs (tcgen05, two-term int8 activations, per-block scale
-epilogue) plus causal attention, so its logits and KV cache are compared
-with the reference within the logit tolerance (max |logit - ref| <= 1e-3 x
-the reference's logit range), and decoding after it must continue exactly
-as the reference does.
+(src/batch.cc:35-40).  Here a prompt runs layer by layer as tcgen05
+tensor-core GEMMs (two-term fp16 activations times exact two-term fp16
+weights, fp32 accumulation) plus causal attention, so its logits and KV
+cache are compared with the reference within the logit tolerance
+(max |logit - ref| <= 1e-3 x the reference's logit range), and decoding
+after it must continue exactly as the reference does.
 """
 import os
 
@@ -57,7 +57,8 @@ class per_token_path:
 def test_prefill_then_decode_matches_reference_golden(pkg, minis, cuda, qt):
     """8 prompt tokens batched, then 4 ForwardToken steps that attend over the
     KV cache the prefill wrote; every logits vector against the reference
-    (Q8_0, and Q4_0 whose nibbles the prefill expands to int8 once)."""
+    (Q8_0, and Q4_0 whose dequantized values the prefill splits into fp16
+    planes once)."""
     g = np.load(golden_path("mini_model.npz"))
     toks = g[f"q{qt}_tokens"]
     ref = g[f"q{qt}_logits"]
