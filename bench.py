@@ -312,6 +312,103 @@ def time_q4_ctx2048(pkg, torch, S, n_prompt: int = 2048, n_steps: int = 128):
             "decode_GB_s": round(bytes_per_token * n_steps / dec / 1e9, 1)}
 
 
+def random_q40_blocks(torch, rows: int, cols: int, gen) -> "torch.Tensor":
+    """Q4_0 blocks on the device: uniform nibbles, fp16 scales in [0.003, 0.006]
+    (weights of std ~0.02, like the N(0, 0.02) models), generated in place."""
+    nb = rows * ((cols + 31) // 32)
+    d = (torch.rand(nb, device="cuda", generator=gen) * 0.003 + 0.003).half()
+    q = torch.randint(0, 256, (nb, 16), dtype=torch.uint8, device="cuda", generator=gen)
+    return torch.cat([d.view(torch.uint8).view(nb, 2), q], dim=1).contiguous()
+
+
+def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
+    """Qwen2-7B-architecture Q4_0 (untied lm_head), one sequence, tensor
+    parallel over the ranks (one GPU each): a --ctx-long prompt fills the KV
+    cache, then --steps greedy decode steps are timed (device argmax, captured
+    step graph with the NCCL all-reduces inside)."""
+    S = pkg.synth
+    c = dict(S.QWEN2_7B)
+    n_steps, ctx_len = args.steps, args.ctx
+    nccl_id = None
+    if world > 1:
+        obj = [pkg.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    model = pkg.Model(c, ctx_len + n_steps + args.warmup, local)
+    model.set_tp(rank, world, nccl_id)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(20261205)
+    hd = c["dim"] // c["n_heads"]
+    qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
+    model.upload("token_embedding", pkg.Q40, random_q40_blocks(torch, c["vocab"], c["dim"], gen),
+                 c["vocab"], c["dim"])
+    model.upload("lm_head", pkg.Q40, random_q40_blocks(torch, c["vocab"], c["dim"], gen),
+                 c["vocab"], c["dim"])
+    ones = np.ones(c["dim"], np.float32)
+    model.upload("final_norm", pkg.F32, ones, 1, c["dim"])
+    shapes = {"wq": (qd, c["dim"]), "wk": (kvd, c["dim"]), "wv": (kvd, c["dim"]),
+              "wo": (c["dim"], qd), "w_gate": (c["hidden"], c["dim"]),
+              "w_up": (c["hidden"], c["dim"]), "w_down": (c["dim"], c["hidden"])}
+    brng = np.random.default_rng(5)
+    for i in range(c["n_layers"]):
+        p = f"layers.{i}."
+        model.upload(p + "attention_norm", pkg.F32, ones, 1, c["dim"])
+        model.upload(p + "ffn_norm", pkg.F32, ones, 1, c["dim"])
+        for n, (r, cc) in shapes.items():
+            model.upload(p + n, pkg.Q40, random_q40_blocks(torch, r, cc, gen), r, cc)
+        for n, size in (("bq", qd), ("bk", kvd), ("bv", kvd)):
+            model.upload(p + n, pkg.F32, brng.normal(0, 0.02, size).astype(np.float32), 1, size)
+        torch.cuda.synchronize()
+    model.finalize()
+    ctx = pkg.Context(model)
+    stream = torch.cuda.ExternalStream(ctx.stream_handle)
+    prompt = S.prompt_tokens(c["vocab"], ctx_len, 11).tolist()
+    logits = ctx.ForwardBatch(prompt, 0)
+    first = int(np.argmax(logits))
+    ctx.decode_enqueue(first, ctx_len, args.warmup)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        ctx.decode_enqueue(first, ctx_len + args.warmup, n_steps)
+        e1.record(stream)
+        e1.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3
+    if dist:
+        t = torch.tensor([dt], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    ctx.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    weights = (c["n_layers"] * (qd + 2 * kvd + qd + 3 * c["hidden"]) * c["dim"] * 18 // 32
+               + c["vocab"] * c["dim"] * 18 // 32)
+    kv = c["n_layers"] * 2 * kvd * 4 * (ctx_len + args.warmup + n_steps // 2)
+    per_gpu = (weights + kv) / world
+    peak, peak_kind = peaks()
+    gbs = per_gpu * n_steps / dt / 1e9
+    print(json.dumps({
+        "metric": "decode tok/s, Qwen2-7B Q4_0, batch 1, tensor parallel",
+        "value": round(n_steps / dt, 2), "unit": "tok/s", "n_gpus": world, "steps": n_steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / n_steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_0xf32",
+        "data": "synthetic: random Q4_0 blocks (uniform nibbles, fp16 scales 0.003-0.006), "
+                "random prompt ids",
+        "config": {"workload": f"qwen2-7b-architecture Q4_0, untied lm_head, {ctx_len}-token "
+                               f"prompt then batch-1 greedy decode", "model": "qwen2-7b",
+                   "parallelism": f"tp{world}", "seq_len": ctx_len + args.warmup + n_steps},
+        "hbm": {"bytes_per_token_per_gpu": int(per_gpu), "GB_s_per_gpu": round(gbs, 1),
+                "frac_of_peak": round(gbs / peak, 4), "peak_source": peak_kind},
+        "clocks": clk.summary()}))
+
+
 def reference_decode(w, steps: int, warmup: int, threads: int):
     """The reference's CPU decode (oracle/_ref) on this host: returns s/token."""
     orc = ge.load_oracle()
@@ -377,6 +474,9 @@ def main():
                     help="time only the decode steps (small runs for profiling)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="time only the 602-token prefill and the batched linear (profiling)")
+    ap.add_argument("--model", default="qwen2-0.5b", choices=["qwen2-0.5b", "qwen2-7b"],
+                    help="qwen2-7b: tensor-parallel decode over the --gpus ranks")
+    ap.add_argument("--ctx", type=int, default=2048, help="qwen2-7b: KV length before decoding")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -399,6 +499,9 @@ def main():
 
     pkg = ge.load_package()
     S = pkg.synth
+    if args.model == "qwen2-7b":
+        bench_7b_tp(args, pkg, torch, dist, world, rank, local)
+        return
     w = build_model(pkg, torch)
     if args.prefill_only:
         print(json.dumps({"prefill": time_prefill(pkg, torch, S, w)}))
@@ -490,7 +593,7 @@ def main():
         "decode_hbm": {"bytes_per_token": bytes_per_token,
                        "GB_s": round(bytes_per_token * value / world / 1e9, 1),
                        "frac_of_peak": round(bytes_per_token * value / world / 1e9 / peak, 4)},
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q8_0> lm_head 151936x896",
+        "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel<Q8_0> lm_head 151936x896",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": profile_traffic(), "algorithmic_bytes": LM_HEAD_BYTES,

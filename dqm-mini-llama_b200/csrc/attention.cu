@@ -25,6 +25,10 @@ constexpr int kThreads = 128;
 constexpr int kMaxGroup = 8;  // query heads per KV head
 constexpr int kMinChunk = 32;
 
+// Floats per split partial: the head_dim sums, then m and l, padded so every
+// row starts 16-byte aligned (float4 reads in the combine).
+__host__ __device__ constexpr int part_stride(int hd) { return hd + 4; }
+
 __device__ __forceinline__ int round_up32(int v) { return (v + 31) & ~31; }
 
 // Split bookkeeping shared by both kernel forms.
@@ -87,7 +91,7 @@ __device__ __forceinline__ void split_combine(const AttnArgs& a, int kvh, int G,
   float* inv_den = stats + (size_t)a.max_splits * kMaxGroup;  // [8]
   for (int i = threadIdx.x; i < n_active * G; i += NT) {
     const int sp = i / G, h = i % G;
-    const float* ps = a.partials + ((size_t)(kvh * G + h) * a.max_splits + sp) * (hd + 2);
+    const float* ps = a.partials + ((size_t)(kvh * G + h) * a.max_splits + sp) * part_stride(hd);
     w[sp * kMaxGroup + h] = __ldcg(ps + hd);
     w[(a.max_splits + 1) * kMaxGroup + sp * kMaxGroup + h] = __ldcg(ps + hd + 1);
   }
@@ -107,34 +111,112 @@ __device__ __forceinline__ void split_combine(const AttnArgs& a, int kvh, int G,
   __syncthreads();
   for (int i = threadIdx.x; i < G * hd; i += NT) {
     const int h = i / hd, dcol = i % hd;
-    const float* part = a.partials + (size_t)(kvh * G + h) * a.max_splits * (hd + 2) + dcol;
+    const float* part = a.partials + (size_t)(kvh * G + h) * a.max_splits * part_stride(hd) + dcol;
     float num = 0.0f;
     int sp = 0;
     for (; sp + 8 <= n_active; sp += 8) {
       float o[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) o[u] = __ldcg(part + (size_t)(sp + u) * (hd + 2));
+      for (int u = 0; u < 8; ++u) o[u] = __ldcg(part + (size_t)(sp + u) * part_stride(hd));
 #pragma unroll
       for (int u = 0; u < 8; ++u) num = fmaf(w[(sp + u) * kMaxGroup + h], o[u], num);
     }
-    for (; sp < n_active; ++sp) num = fmaf(w[sp * kMaxGroup + h], __ldcg(part + (size_t)sp * (hd + 2)), num);
+    for (; sp < n_active; ++sp) num = fmaf(w[sp * kMaxGroup + h], __ldcg(part + (size_t)sp * part_stride(hd)), num);
     a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(num, inv_den[h]);
   }
   if (threadIdx.x == 0) a.tickets[kvh] = 0u;
 }
 
+// Last-CTA merge for the head_dim-templated kernel: the same arithmetic as
+// split_combine, with each thread producing 4 consecutive output dims from
+// float4 partial reads, all of its splits' loads issued in groups of 16.
+template <int NT, int HD>
+__device__ __forceinline__ void split_combine_hd(const AttnArgs& a, int kvh, int G, int n_active,
+                                                 float* stats, int* is_last) {
+  constexpr int PS = part_stride(HD);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(&a.tickets[kvh], 1u);
+    *is_last = done == gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!*is_last) return;
+  __threadfence();
+  float* w = stats;                                              // [n_active][8] weights
+  float* lsum = stats + (size_t)a.max_splits * kMaxGroup;        // [n_active][8] l
+  float* inv_den = lsum + (size_t)a.max_splits * kMaxGroup;      // [8]
+  for (int i = threadIdx.x; i < n_active * G; i += NT) {
+    const int sp = i / G, h = i % G;
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(
+        a.partials + ((size_t)(kvh * G + h) * a.max_splits + sp) * PS + HD));
+    w[sp * kMaxGroup + h] = ml.x;
+    lsum[sp * kMaxGroup + h] = ml.y;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
+    float M = -INFINITY;
+    for (int sp = 0; sp < n_active; ++sp) M = fmaxf(M, w[sp * kMaxGroup + h]);
+    float den = 0.0f;
+    for (int sp = 0; sp < n_active; ++sp) {
+      const float e = expf(w[sp * kMaxGroup + h] - M);
+      w[sp * kMaxGroup + h] = e;
+      den = fmaf(e, lsum[sp * kMaxGroup + h], den);
+    }
+    inv_den[h] = den;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * (HD / 4); i += NT) {
+    const int h = i / (HD / 4), d4 = i % (HD / 4);
+    const float4* part = reinterpret_cast<const float4*>(
+                             a.partials + (size_t)(kvh * G + h) * a.max_splits * PS) + d4;
+    float4 num = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int sp0 = 0; sp0 < n_active; sp0 += 16) {
+      float4 o[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        o[u] = sp0 + u < n_active ? __ldcg(part + (size_t)(sp0 + u) * (PS / 4))
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        if (sp0 + u < n_active) {
+          const float wt = w[(sp0 + u) * kMaxGroup + h];
+          num.x = fmaf(wt, o[u].x, num.x);
+          num.y = fmaf(wt, o[u].y, num.y);
+          num.z = fmaf(wt, o[u].z, num.z);
+          num.w = fmaf(wt, o[u].w, num.w);
+        }
+      }
+    }
+    const float den = inv_den[h];
+    *reinterpret_cast<float4*>(a.out + (size_t)(kvh * G + h) * HD + d4 * 4) =
+        make_float4(__fdiv_rn(num.x, den), __fdiv_rn(num.y, den), __fdiv_rn(num.z, den),
+                    __fdiv_rn(num.w, den));
+  }
+  if (threadIdx.x == 0) a.tickets[kvh] = 0u;
+}
+
 // head_dim known at compile time (64 / 128), 256 threads.  Scores: HD/16
-// threads per position, each holding 16 dims of the K row (4 x 16-byte loads
-// issued together), partial dots folded with shuffles.  P.V: one thread per
-// (dim, position group), all of a thread's V loads for a 32-position chunk in
-// flight at once.  A single active split writes its output directly.
+// threads per position, each holding 16 dims of the K row (4 x 16-byte loads),
+// two position passes' loads issued together, partial dots folded with
+// shuffles.  P.V: thread (d4, group) owns 4 consecutive dims and every
+// GROUPS-th position, with 8 float4 V loads in flight.  A single active split
+// writes its output directly.
+template <int HD>
+constexpr int hd_groups() {
+  return 256 / (HD / 4);
+}
+
 template <int HD>
 __global__ void __launch_bounds__(256) attention_hd_kernel(const AttnArgs a, int chunk_cap) {
   constexpr int NT = 256;
-  constexpr int TPT = HD / 16;       // threads per position (scores)
-  constexpr int TOK = NT / TPT;      // positions per score pass
-  constexpr int GROUPS = NT / HD;    // position groups in P.V
-  constexpr int PV = 8;              // V loads in flight per thread
+  constexpr int TPT = HD / 16;          // threads per position (scores)
+  constexpr int TOK = NT / TPT;         // positions per score pass
+  constexpr int D4 = HD / 4;            // float4 columns
+  constexpr int GROUPS = hd_groups<HD>();  // position groups in P.V
+  constexpr int PV = 8;                 // float4 V loads in flight per thread
+  constexpr int PS = part_stride(HD);
   extern __shared__ float sm[];
   __shared__ float head_m[kMaxGroup], head_l[kMaxGroup];
   __shared__ int is_last;
@@ -156,98 +238,119 @@ __global__ void __launch_bounds__(256) attention_hd_kernel(const AttnArgs a, int
   float* stats = sacc + GROUPS * kMaxGroup * HD;
 
   if (split < sp.n_active) {
-    for (int i = tid; i < G * HD; i += NT) sq[i] = __ldcg(a.q + (size_t)(kvh * G) * HD + i);
+    for (int i = tid; i < G * D4; i += NT)
+      reinterpret_cast<float4*>(sq)[i] =
+          __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)(kvh * G) * HD) + i);
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
     const int part = tid % TPT;
-    for (int base = 0; base < sp.n; base += TOK) {
-      const int t = base + tid / TPT;
-      float dot[kMaxGroup];
+    for (int base = 0; base < sp.n; base += 2 * TOK) {
+      float4 k4[2][4];
 #pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h) dot[h] = 0.0f;
-      if (t < sp.n) {
+      for (int u = 0; u < 2; ++u) {
+        const int t = base + u * TOK + tid / TPT;
         const float4* kr =
             reinterpret_cast<const float4*>(kbase + (size_t)(sp.t0 + t) * row_stride) + part * 4;
-        float4 k4[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) k4[i] = __ldcg(kr + i);
+        for (int i = 0; i < 4; ++i)
+          k4[u][i] = t < sp.n ? __ldcg(kr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int t = base + u * TOK + tid / TPT;
+        float dot[kMaxGroup];
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) {
+          float d = 0.0f;
           if (h < G) {
             const float4* q4 = reinterpret_cast<const float4*>(sq + h * HD) + part * 4;
-            float d = 0.0f;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const float4 qq = q4[i];
-              d = fmaf(qq.x, k4[i].x, d);
-              d = fmaf(qq.y, k4[i].y, d);
-              d = fmaf(qq.z, k4[i].z, d);
-              d = fmaf(qq.w, k4[i].w, d);
+              d = fmaf(qq.x, k4[u][i].x, d);
+              d = fmaf(qq.y, k4[u][i].y, d);
+              d = fmaf(qq.z, k4[u][i].z, d);
+              d = fmaf(qq.w, k4[u][i].w, d);
             }
-            dot[h] = d;
           }
+          dot[h] = d;
         }
-      }
 #pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h) {
+        for (int h = 0; h < kMaxGroup; ++h) {
 #pragma unroll
-        for (int o = TPT / 2; o > 0; o >>= 1) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
-      }
-      if (t < sp.n && part == 0) {
+          for (int o = TPT / 2; o > 0; o >>= 1) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
+        }
+        if (t < sp.n && part == 0) {
 #pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h)
-          if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
+          for (int h = 0; h < kMaxGroup; ++h)
+            if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
+        }
       }
     }
     __syncthreads();
     split_softmax<NT>(ss, chunk_cap, G, sp.n, head_m, head_l);
     __syncthreads();
 
-    const int d = tid % HD, gi = tid / HD;
-    float acc[kMaxGroup];
+    const int d4 = tid % D4, gi = tid / D4;
+    float4 acc[kMaxGroup];
 #pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
+    for (int h = 0; h < kMaxGroup; ++h) acc[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int t = gi; t < sp.n; t += PV * GROUPS) {
-      float v[PV];
+      float4 v[PV];
 #pragma unroll
       for (int u = 0; u < PV; ++u) {
         const int tt = t + u * GROUPS;
-        v[u] = tt < sp.n ? __ldcg(vbase + (size_t)(sp.t0 + tt) * row_stride + d) : 0.0f;
+        v[u] = tt < sp.n ? __ldcg(reinterpret_cast<const float4*>(
+                               vbase + (size_t)(sp.t0 + tt) * row_stride) + d4)
+                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
 #pragma unroll
       for (int u = 0; u < PV; ++u) {
         const int tt = t + u * GROUPS;
         if (tt < sp.n) {
 #pragma unroll
-          for (int h = 0; h < kMaxGroup; ++h)
-            if (h < G) acc[h] = fmaf(ss[h * chunk_cap + tt], v[u], acc[h]);
+          for (int h = 0; h < kMaxGroup; ++h) {
+            if (h < G) {
+              const float pr = ss[h * chunk_cap + tt];
+              acc[h].x = fmaf(pr, v[u].x, acc[h].x);
+              acc[h].y = fmaf(pr, v[u].y, acc[h].y);
+              acc[h].z = fmaf(pr, v[u].z, acc[h].z);
+              acc[h].w = fmaf(pr, v[u].w, acc[h].w);
+            }
+          }
         }
       }
     }
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h)
-      if (h < G) sacc[(gi * kMaxGroup + h) * HD + d] = acc[h];
+      if (h < G) reinterpret_cast<float4*>(sacc + (gi * kMaxGroup + h) * HD)[d4] = acc[h];
     __syncthreads();
 
     const bool direct = sp.n_active == 1;
-    for (int i = tid; i < G * HD; i += NT) {
-      const int h = i / HD, dcol = i % HD;
-      float o = 0.0f;
+    for (int i = tid; i < G * D4; i += NT) {
+      const int h = i / D4, c4 = i % D4;
+      float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-      for (int g2 = 0; g2 < GROUPS; ++g2) o += sacc[(g2 * kMaxGroup + h) * HD + dcol];
+      for (int g2 = 0; g2 < GROUPS; ++g2) {
+        const float4 x = reinterpret_cast<const float4*>(sacc + (g2 * kMaxGroup + h) * HD)[c4];
+        o.x += x.x;
+        o.y += x.y;
+        o.z += x.z;
+        o.w += x.w;
+      }
       if (direct) {
-        a.out[(size_t)(kvh * G + h) * HD + dcol] = __fdiv_rn(o, head_l[h]);
+        const float l = head_l[h];
+        *reinterpret_cast<float4*>(a.out + (size_t)(kvh * G + h) * HD + c4 * 4) =
+            make_float4(__fdiv_rn(o.x, l), __fdiv_rn(o.y, l), __fdiv_rn(o.z, l),
+                        __fdiv_rn(o.w, l));
       } else {
-        float* pp = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * (HD + 2);
-        pp[dcol] = o;
-        if (dcol == 0) {
-          pp[HD] = head_m[h];
-          pp[HD + 1] = head_l[h];
-        }
+        float* pp = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * PS;
+        reinterpret_cast<float4*>(pp)[c4] = o;
+        if (c4 == 0) *reinterpret_cast<float2*>(pp + HD) = make_float2(head_m[h], head_l[h]);
       }
     }
   }
-  if (sp.n_active > 1) split_combine<NT>(a, kvh, G, HD, sp.n_active, stats, &is_last);
+  if (sp.n_active > 1) split_combine_hd<NT, HD>(a, kvh, G, sp.n_active, stats, &is_last);
 }
 
 // Any head_dim that is a multiple of 4 up to 256: one thread per position.
@@ -351,7 +454,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
         a.out[(size_t)(kvh * G + h) * hd + dcol] = __fdiv_rn(o, head_l[h]);
         continue;
       }
-      float* part = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * (hd + 2);
+      float* part = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * part_stride(hd);
       part[dcol] = o;
       if (dcol == 0) {
         part[hd] = head_m[h];
@@ -369,6 +472,13 @@ int chunk_cap_for(int max_seq, int max_splits) {
   return c < kMinChunk ? kMinChunk : c;
 }
 
+size_t smem_bytes_hd(int head_dim, int chunk_cap, int max_splits) {
+  const int groups = 256 / (head_dim / 4);
+  return sizeof(float) * ((size_t)kMaxGroup * head_dim + (size_t)kMaxGroup * chunk_cap +
+                          (size_t)groups * kMaxGroup * head_dim +
+                          (size_t)(2 * max_splits + 1) * kMaxGroup);
+}
+
 size_t smem_bytes(int threads, int head_dim, int chunk_cap, int max_splits) {
   const int groups = threads / head_dim > 0 ? threads / head_dim : 1;
   return sizeof(float) * ((size_t)kMaxGroup * head_dim + (size_t)kMaxGroup * chunk_cap +
@@ -380,14 +490,14 @@ size_t smem_bytes(int threads, int head_dim, int chunk_cap, int max_splits) {
 
 int attention_splits(int max_seq, int n_kv_heads) {
   int s = (max_seq + kMinChunk - 1) / kMinChunk;
-  int cap = (2 * sm_count()) / (n_kv_heads > 0 ? n_kv_heads : 1);
+  int cap = sm_count() / (n_kv_heads > 0 ? n_kv_heads : 1);
   if (cap < 1) cap = 1;
   if (s > cap) s = cap;
   return s < 1 ? 1 : s;
 }
 
 size_t attention_partials_floats(int n_heads, int head_dim, int max_splits) {
-  return (size_t)n_heads * max_splits * (head_dim + 2);
+  return (size_t)n_heads * max_splits * part_stride(head_dim);
 }
 
 cudaError_t attention_prepare() {
@@ -409,14 +519,19 @@ cudaError_t attention_prepare() {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
   const int cap = chunk_cap_for(a.max_seq, a.max_splits);
-  const bool hd_kernel = a.head_dim == 64 || a.head_dim == 128;
-  const size_t smem = smem_bytes(hd_kernel ? 256 : kThreads, a.head_dim, cap, a.max_splits);
+  // the templated kernel reads q and writes out with 16-byte vectors
+  const bool aligned =
+      ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.out) |
+        reinterpret_cast<uintptr_t>(a.partials)) & 15u) == 0;
+  const bool hd_kernel = (a.head_dim == 64 || a.head_dim == 128) && aligned;
+  const size_t smem = hd_kernel ? smem_bytes_hd(a.head_dim, cap, a.max_splits)
+                                : smem_bytes(kThreads, a.head_dim, cap, a.max_splits);
   cudaError_t e = attention_prepare();
   if (e != cudaSuccess) return e;
   const dim3 grid(a.n_kv_heads, a.max_splits);
-  if (a.head_dim == 64)
+  if (hd_kernel && a.head_dim == 64)
     return launch(attention_hd_kernel<64>, grid, dim3(256), smem, stream, pdl, a, cap);
-  if (a.head_dim == 128)
+  if (hd_kernel && a.head_dim == 128)
     return launch(attention_hd_kernel<128>, grid, dim3(256), smem, stream, pdl, a, cap);
   return launch(attention_kernel, grid, dim3(kThreads), smem, stream, pdl, a, cap);
 }

@@ -523,9 +523,9 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 // Every instantiation the dispatcher below can pick.
 #define DQMK_GEMV_VARIANTS(X)                                                             \
   X(DQMK_Q80, 2, 1, 1) X(DQMK_Q80, 2, 2, 1) X(DQMK_Q80, 4, 2, 1) X(DQMK_Q80, 2, 2, 4)       \
-  X(DQMK_Q80, 2, 3, 4) X(DQMK_Q80, 2, 4, 4) X(DQMK_Q80, 4, 2, 4) X(DQMK_Q80, 4, 4, 4)       \
-  X(DQMK_Q40, 2, 1, 1) X(DQMK_Q40, 4, 1, 1) X(DQMK_Q40, 2, 2, 1) X(DQMK_Q40, 4, 2, 1)       \
-  X(DQMK_Q40, 2, 2, 4) X(DQMK_Q40, 2, 4, 4) X(DQMK_Q40, 4, 2, 4) X(DQMK_Q40, 4, 4, 4)
+  X(DQMK_Q80, 4, 2, 4) X(DQMK_Q80, 4, 4, 4)                                                 \
+  X(DQMK_Q40, 4, 1, 1) X(DQMK_Q40, 2, 2, 1) X(DQMK_Q40, 4, 2, 1) X(DQMK_Q40, 2, 2, 4)       \
+  X(DQMK_Q40, 2, 4, 4) X(DQMK_Q40, 2, 5, 4)
 
 // ============================================================ TMA-staged GEMV
 // Weights stream through a ring of shared-memory stages filled by bulk
@@ -1025,12 +1025,16 @@ cudaError_t tma_dispatch(const GemvArgs& a, cudaStream_t stream, bool pdl, int s
   return cudaErrorInvalidValue;
 }
 
-// The TMA form streams the very tall weights (lm_head): there bandwidth
+// The TMA form streams the very tall Q8_0 weights (lm_head): there bandwidth
 // decides, and the shared-memory ring keeps more bytes in flight than
-// registers can.  The per-layer projections are latency-bound links of the
-// decode chain; the register-staged form, whose weights are already in
-// registers when the dependency resolves, finishes them sooner.
-bool tma_eligible(const GemvArgs& a) { return a.kp <= 8192 && a.n_rows >= 32768; }
+// registers can.  For Q4_0 the register form with 4 rows per warp measured
+// faster at every tall shape (the consumer work per byte doubles), and the
+// per-layer projections are latency-bound links of the decode chain where the
+// register form, whose weights are already in registers when the dependency
+// resolves, finishes sooner.
+bool tma_eligible(const GemvArgs& a) {
+  return a.qtype == DQMK_Q80 && a.kp <= 8192 && a.n_rows >= 32768;
+}
 
 // ------------------------------------------------ ggml-layout compatibility
 // One warp per weight row, blocks read in place (34 / 18 bytes, 2-byte
@@ -1119,10 +1123,13 @@ cudaError_t read_device_error(unsigned int* flags, bool clear) {
   return e;
 }
 
-// Shape -> variant.  Rows that fit in one warp pass (<= 64 chunks) get a warp
-// per row group; longer rows are split across the whole CTA (4 warps), so no
-// warp walks a long row alone.  Very tall weights (lm_head) take 4 rows per
-// group to amortise the shared-memory reads of x.
+// Shape -> variant, from a sweep of every variant over the decode shapes
+// (Qwen2-0.5B Q8_0 / Q4_0, Qwen2-7B Q4_0 at TP 1/2/4) with HBM-cold weights.
+// Q8_0 rows up to 64 chunks take a warp per row group; longer rows are split
+// across the whole CTA.  Q4_0 rows (32 values per chunk) up to 128 chunks are
+// fastest with a warp per group of 4 rows walking the row in several passes;
+// longer ones across the CTA.  Very tall weights take 4 rows per group to
+// amortise the shared-memory reads of x.
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   if (tma_eligible(a)) return tma_dispatch(a, stream, pdl, -1);
   const bool wide = a.n_rows >= 32768 && a.epi != kEpiSwiGlu && a.epi != kEpiQkv;
@@ -1135,19 +1142,21 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     if (wide) return chunks <= 256 ? launch_t<DQMK_Q80, 4, 2, 4>(a, stream, pdl)
                                    : launch_t<DQMK_Q80, 4, 4, 4>(a, stream, pdl);
     if (chunks <= 256) return launch_t<DQMK_Q80, 2, 2, 4>(a, stream, pdl);
-    if (chunks <= 384) return launch_t<DQMK_Q80, 2, 3, 4>(a, stream, pdl);
-    return launch_t<DQMK_Q80, 2, 4, 4>(a, stream, pdl);
+    return launch_t<DQMK_Q80, 4, 4, 4>(a, stream, pdl);
   }
+  const bool tall = a.n_rows >= 8192;
   if (chunks <= 32)
-    return wide ? launch_t<DQMK_Q40, 4, 1, 1>(a, stream, pdl)
-                : launch_t<DQMK_Q40, 2, 1, 1>(a, stream, pdl);
-  if (chunks <= 64)
-    return wide ? launch_t<DQMK_Q40, 4, 2, 1>(a, stream, pdl)
+    return tall ? launch_t<DQMK_Q40, 4, 1, 1>(a, stream, pdl)
                 : launch_t<DQMK_Q40, 2, 2, 1>(a, stream, pdl);
-  if (wide) return chunks <= 256 ? launch_t<DQMK_Q40, 4, 2, 4>(a, stream, pdl)
-                                 : launch_t<DQMK_Q40, 4, 4, 4>(a, stream, pdl);
+  if (chunks <= 64)
+    return tall ? launch_t<DQMK_Q40, 4, 2, 1>(a, stream, pdl)
+                : launch_t<DQMK_Q40, 2, 2, 1>(a, stream, pdl);
+  if (chunks <= 128)
+    return (a.n_rows >= 16384 && a.n_rows < 65536) ? launch_t<DQMK_Q40, 4, 1, 1>(a, stream, pdl)
+                                                   : launch_t<DQMK_Q40, 4, 2, 1>(a, stream, pdl);
   if (chunks <= 256) return launch_t<DQMK_Q40, 2, 2, 4>(a, stream, pdl);
-  return launch_t<DQMK_Q40, 2, 4, 4>(a, stream, pdl);
+  if (chunks <= 512 || chunks > 640) return launch_t<DQMK_Q40, 2, 4, 4>(a, stream, pdl);
+  return launch_t<DQMK_Q40, 2, 5, 4>(a, stream, pdl);
 }
 
 cudaError_t launch_linear_blocks(int qtype, const float* x, int rows, int in_features,

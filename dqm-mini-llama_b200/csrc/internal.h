@@ -134,7 +134,7 @@ struct AttnArgs {
   const int* pos_dev;    // device position; nullptr -> pos_arg
   int pos_arg;
   float* out;            // [n_heads][hd]
-  float* partials;       // [n_heads][max_splits][hd + 2]
+  float* partials;       // [n_heads][max_splits][hd + 4]: sums, m, l, pad
   unsigned int* tickets; // [n_kv_heads], zero at rest
   int max_splits;        // gridDim.y
 };
