@@ -361,6 +361,15 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
         torch.cuda.synchronize()
     model.finalize()
     ctx = pkg.Context(model)
+    exchange = "none"
+    if world > 1:
+        exchange = "nccl"
+        if not args.nccl:
+            handles = [None] * world
+            dist.all_gather_object(handles, ctx.tp_ipc_handle())
+            ctx.tp_connect(handles)
+            dist.barrier()
+            exchange = "peer memory"
     stream = torch.cuda.ExternalStream(ctx.stream_handle)
     prompt = S.prompt_tokens(c["vocab"], ctx_len, 11).tolist()
     logits = ctx.ForwardBatch(prompt, 0)
@@ -403,7 +412,8 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
                 "random prompt ids",
         "config": {"workload": f"qwen2-7b-architecture Q4_0, untied lm_head, {ctx_len}-token "
                                f"prompt then batch-1 greedy decode", "model": "qwen2-7b",
-                   "parallelism": f"tp{world}", "seq_len": ctx_len + args.warmup + n_steps},
+                   "parallelism": f"tp{world}", "exchange": exchange,
+                   "seq_len": ctx_len + args.warmup + n_steps},
         "hbm": {"bytes_per_token_per_gpu": int(per_gpu), "GB_s_per_gpu": round(gbs, 1),
                 "frac_of_peak": round(gbs / peak, 4), "peak_source": peak_kind},
         "clocks": clk.summary()}))
@@ -477,6 +487,9 @@ def main():
     ap.add_argument("--model", default="qwen2-0.5b", choices=["qwen2-0.5b", "qwen2-7b"],
                     help="qwen2-7b: tensor-parallel decode over the --gpus ranks")
     ap.add_argument("--ctx", type=int, default=2048, help="qwen2-7b: KV length before decoding")
+    ap.add_argument("--nccl", action="store_true",
+                    help="qwen2-7b under tensor parallelism: all-reduce over NCCL instead of "
+                         "the peer-memory exchange")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

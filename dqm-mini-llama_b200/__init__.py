@@ -438,6 +438,17 @@ class Context:
     def decode_enqueue(self, token: int, pos: int, n_steps: int) -> None:
         check(lib().dqmk_decode_enqueue(self.h, int(token), int(pos), int(n_steps)))
 
+    def tp_ipc_handle(self) -> bytes:
+        """This rank's exchange buffer as a 64-byte CUDA IPC handle."""
+        buf = C.create_string_buffer(64)
+        check(lib().dqmk_context_tp_ipc_handle(self.h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """Map every rank's exchange buffer (handles in rank order): the decode
+        step then exchanges partial sums over peer memory instead of NCCL."""
+        check(lib().dqmk_context_tp_connect(self.h, b"".join(handles)))
+
     @property
     def stream_handle(self) -> int:
         return lib().dqmk_context_stream(self.h)

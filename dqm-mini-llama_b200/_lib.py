@@ -81,6 +81,8 @@ SIGNATURES = {
     "dqmk_tp_plan_get": ([C.POINTER(ModelConfig), _i, _i, C.POINTER(TpPlan)], _i),
     "dqmk_nccl_unique_id": ([C.c_char_p], _i),
     "dqmk_model_set_tp": ([_vp, _i, _i, C.c_char_p], _i),
+    "dqmk_context_tp_ipc_handle": ([_vp, C.c_char_p], _i),
+    "dqmk_context_tp_connect": ([_vp, C.c_char_p], _i),
     "dqmk_model_stats_get": ([_vp, C.POINTER(ModelStats)], _i),
     "dqmk_model_stats_reset": ([_vp], _i),
     "dqmk_model_memory_bytes": ([_vp], _sz),

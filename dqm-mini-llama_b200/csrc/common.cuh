@@ -126,6 +126,37 @@ __device__ __forceinline__ float warp_max(float v) {
 // Total-order key for a float so that unsigned max == float max; among equal
 // values the smaller index wins (the reference's ArgMax keeps the first max,
 // src/ops.cc:182-195).
+// System-scope release store / acquire load (flags exchanged with peer GPUs).
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned int* tp_flag(char* base, int world, int dim, int channel,
+                                                 int rank) {
+  return reinterpret_cast<unsigned int*>(base + tp_flags_off(world, dim)) + channel * world + rank;
+}
+
+// After every thread of the CTA stored its share of exchange s: the last CTA
+// of the grid raises flag [channel][own rank] to s on every rank.  Called by
+// all threads of every CTA.
+__device__ __forceinline__ void peer_signal(const PeerSet& ps, int channel, unsigned int s) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(ps.ticket, 1u);
+    if (done == gridDim.x - 1) {
+      __threadfence_system();
+      for (int w = 0; w < ps.world; ++w)
+        st_release_sys(tp_flag(ps.base[w], ps.world, ps.dim, channel, ps.rank), s);
+      *ps.ticket = 0u;
+    }
+  }
+}
+
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
   uint32_t b = __float_as_uint(v);
   b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);

@@ -109,6 +109,14 @@ struct dqmk_context {
   float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
   float* part = nullptr;        // tensor parallel: row-parallel partial sums [dim]
   float* logits_all = nullptr;  // tensor parallel: gathered logits [world][vocab_stride]
+  // tensor parallel over peer memory: this rank's exchange buffer (its own
+  // allocation, exported by IPC), the device array of every rank's mapping,
+  // exchange counters [2] + the writers' CTA ticket; p2p once connected
+  char* tp_buf = nullptr;
+  char** peer_base = nullptr;
+  unsigned int* tp_seq = nullptr;
+  bool p2p = false;
+  std::vector<void*> ipc_opened;
   float *keys = nullptr, *values = nullptr, *partials = nullptr;
   // device state block: [argmax u64][lm ticket u32][token i32][pos i32][pad]
   //                     [attention tickets u32 x n_kv] ...
@@ -132,6 +140,7 @@ struct dqmk_context {
   ~dqmk_context() {
     cudaSetDevice(m ? m->device : 0);
     if (graph) cudaGraphExecDestroy(graph);
+    for (void* p : ipc_opened) cudaIpcCloseMemHandle(p);
     if (staged) cudaEventDestroy(staged);
     if (stream) cudaStreamDestroy(stream);
     for (void* p : allocs) cudaFree(p);
@@ -585,6 +594,17 @@ bool use_pdl() {
   return on;
 }
 
+PeerSet peer_set(const dqmk_context* x) {
+  PeerSet ps{};
+  ps.base = x->peer_base;
+  ps.rank = x->m->tp.rank;
+  ps.world = x->m->tp.world;
+  ps.dim = x->m->cfg.dim;
+  ps.seq = x->tp_seq;
+  ps.ticket = x->tp_seq + 2;
+  return ps;
+}
+
 int enqueue_step(dqmk_context* x) {
   const char* api = "ForwardToken";
   const bool pdl = use_pdl();
@@ -592,6 +612,8 @@ int enqueue_step(dqmk_context* x) {
   const dqmk_model_config& c = m->cfg;
   const dqmk_tp_plan& tp = m->tp;
   const bool tpar = tp.world > 1;
+  const bool p2p = tpar && x->p2p;
+  const PeerSet ps = peer_set(x);
   cudaStream_t s = x->stream;
   int rc;
   EmbedArgs ea = {};
@@ -659,8 +681,14 @@ int enqueue_step(dqmk_context* x) {
     o.epi = kEpiStore;
     o.residual = tpar ? nullptr : x->x;
     o.y = tpar ? x->part : x->x;
+    if (p2p) {  // partial rows straight into every rank's slot
+      o.epi = kEpiPeer;
+      o.peer = ps;
+    }
     DQMK_CUDA_RET(api, launch_gemv(o, s, pdl));
-    if (tpar) {  // complete the row-parallel sum, then the residual add
+    if (p2p) {
+      DQMK_CUDA_RET(api, launch_tp_reduce(x->x, ps, s, pdl));
+    } else if (tpar) {  // complete the row-parallel sum, then the residual add
       if ((rc = tp_allreduce_sum(m->comm, x->part, c.dim, s, api))) return rc;
       DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
     }
@@ -690,8 +718,14 @@ int enqueue_step(dqmk_context* x) {
     dn.epi = kEpiStore;
     dn.residual = tpar ? nullptr : x->x;
     dn.y = tpar ? x->part : x->x;
+    if (p2p) {
+      dn.epi = kEpiPeer;
+      dn.peer = ps;
+    }
     DQMK_CUDA_RET(api, launch_gemv(dn, s, pdl));
-    if (tpar) {
+    if (p2p) {
+      DQMK_CUDA_RET(api, launch_tp_reduce(x->x, ps, s, pdl));
+    } else if (tpar) {
       if ((rc = tp_allreduce_sum(m->comm, x->part, c.dim, s, api))) return rc;
       DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
     }
@@ -710,13 +744,17 @@ int enqueue_step(dqmk_context* x) {
   lg.y = x->logits;
   lg.argmax_slot = x->argmax_slot();
   lg.row_offset = tp.vocab0;
-  lg.ticket = tpar ? nullptr : x->lm_ticket();
+  lg.ticket = tpar && !p2p ? nullptr : x->lm_ticket();
+  if (p2p) lg.peer = ps;
   lg.token_slot = x->token_slot();
   lg.pos_slot = x->pos_slot();
   lg.history = x->history_dev;
   lg.history_cap = c.max_seq_len;
   DQMK_CUDA_RET(api, launch_gemv(lg, s, pdl));
-  if (tpar) {  // global greedy choice: max over the ranks' (value, index) keys
+  if (p2p) {
+    DQMK_CUDA_RET(api, launch_tp_argmax_advance(ps, x->token_slot(), x->pos_slot(),
+                                                x->history_dev, c.max_seq_len, s, pdl));
+  } else if (tpar) {  // global greedy choice: max over the ranks' (value, index) keys
     if ((rc = tp_allreduce_max_u64(m->comm, x->argmax_slot(), 1, s, api))) return rc;
     DQMK_CUDA_RET(api, launch_greedy_advance(x->argmax_slot(), x->token_slot(), x->pos_slot(),
                                              x->history_dev, c.max_seq_len, s));
@@ -777,8 +815,10 @@ void count_token(dqmk_context* x, int pos) {
 // After a synchronizing call: a bounded device wait that ran out surfaces as
 // DQMK_ERR_TIMEOUT (the flag is cleared so the context stays usable).
 int check_device_error(const char* api) {
-  unsigned int flags = 0;
+  unsigned int flags = 0, tp_flags = 0;
   DQMK_CUDA_RET(api, read_device_error(&flags, true));
+  DQMK_CUDA_RET(api, read_tp_error(&tp_flags, true));
+  flags |= tp_flags;
   if (flags) return fail(DQMK_ERR_TIMEOUT, std::string(api) + ": a device-side wait timed out");
   return DQMK_OK;
 }
@@ -1051,6 +1091,17 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
     if ((rc = dev_alloc(x->allocs, b.n * sizeof(float), &p, api))) return rc;
     *b.dst = static_cast<float*>(p);
   }
+  if (tp.world > 1) {
+    const size_t tb = tp_buf_bytes(tp.world, c.dim);
+    DQMK_CUDA_RET(api, cudaMalloc(reinterpret_cast<void**>(&x->tp_buf), tb));
+    x->allocs.push_back(x->tp_buf);
+    DQMK_CUDA_RET(api, cudaMemset(x->tp_buf, 0, tb));
+    if ((rc = dev_alloc(x->allocs, (size_t)tp.world * sizeof(char*), &p, api))) return rc;
+    x->peer_base = static_cast<char**>(p);
+    if ((rc = dev_alloc(x->allocs, 4 * sizeof(unsigned int), &p, api))) return rc;
+    x->tp_seq = static_cast<unsigned int*>(p);
+    DQMK_CUDA_RET(api, cudaMemset(x->tp_seq, 0, 4 * sizeof(unsigned int)));
+  }
   if ((rc = dev_alloc(x->allocs, 64 + 4 * (size_t)tp.n_kv_heads + 64, &p, api))) return rc;
   x->state = static_cast<unsigned char*>(p);
   if ((rc = dev_alloc(x->allocs, (size_t)c.max_seq_len * sizeof(int), &p, api))) return rc;
@@ -1093,6 +1144,49 @@ extern "C" int dqmk_context_history(const dqmk_context* x, int* out, int cap) {
 }
 
 extern "C" void* dqmk_context_stream(dqmk_context* x) { return x ? x->stream : nullptr; }
+
+extern "C" int dqmk_context_tp_ipc_handle(dqmk_context* x, unsigned char* handle_out) {
+  const char* api = "dqmk_context_tp_ipc_handle";
+  if (!x || !handle_out) return fail(DQMK_ERR_INVALID, std::string(api) + ": null argument");
+  if (!x->tp_buf) return fail(DQMK_ERR_INVALID, std::string(api) + ": not tensor parallel");
+  cudaSetDevice(x->m->device);
+  cudaIpcMemHandle_t h;
+  DQMK_CUDA_RET(api, cudaIpcGetMemHandle(&h, x->tp_buf));
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  std::memcpy(handle_out, &h, 64);
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_context_tp_connect(dqmk_context* x, const unsigned char* handles) {
+  const char* api = "dqmk_context_tp_connect";
+  if (!x || !handles) return fail(DQMK_ERR_INVALID, std::string(api) + ": null argument");
+  if (!x->tp_buf) return fail(DQMK_ERR_INVALID, std::string(api) + ": not tensor parallel");
+  if (x->p2p) return fail(DQMK_ERR_INVALID, std::string(api) + ": already connected");
+  cudaSetDevice(x->m->device);
+  const dqmk_tp_plan& tp = x->m->tp;
+  std::vector<char*> bases(tp.world, nullptr);
+  for (int w = 0; w < tp.world; ++w) {
+    if (w == tp.rank) {
+      bases[w] = x->tp_buf;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles + (size_t)w * 64, 64);
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(api, e);
+    x->ipc_opened.push_back(ptr);
+    bases[w] = static_cast<char*>(ptr);
+  }
+  DQMK_CUDA_RET(api, cudaMemcpy(x->peer_base, bases.data(), tp.world * sizeof(char*),
+                                cudaMemcpyHostToDevice));
+  if (x->graph) {  // the step is captured again with the peer-memory exchange
+    cudaGraphExecDestroy(x->graph);
+    x->graph = nullptr;
+  }
+  x->p2p = true;
+  return DQMK_OK;
+}
 
 extern "C" int dqmk_forward_token(dqmk_context* x, int token, int pos, float* logits) {
   const char* api = "ForwardToken";

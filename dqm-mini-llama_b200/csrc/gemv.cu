@@ -189,6 +189,19 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
         a.y[row] = v;
       }
     }
+  } else if (a.epi == kEpiPeer) {
+    // row-parallel partial sum: to slot [parity][own rank] of every rank
+    const unsigned int s = a.peer.seq[0] + 1;
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int row = grp * RPW + r;
+      if (lane == r && row < a.n_rows) {
+        for (int w = 0; w < a.peer.world; ++w)
+          reinterpret_cast<float*>(a.peer.base[w] + tp_vec_off((int)(s & 1u), a.peer.rank,
+                                                               a.peer.world, a.peer.dim))[row] =
+              acc[r];
+      }
+    }
   } else if (a.epi == kEpiLogits) {
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
@@ -357,6 +370,38 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const flo
   __syncthreads();
 }
 
+// Thread 0 of each CTA with the CTA's best (value, index) key: fold it into
+// the device argmax; the last CTA then advances the greedy state (token,
+// position, history) or, under peer-memory tensor parallelism, sends this
+// rank's key to every rank and raises its flag (channel 1).
+__device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long long b) {
+  if (!a.argmax_slot) return;
+  atomicMax(a.argmax_slot, b);
+  if (!a.ticket) return;
+  __threadfence();
+  const unsigned int done = atomicAdd(a.ticket, 1u);
+  if (done != gridDim.x - 1) return;
+  __threadfence();
+  const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
+  *a.ticket = 0u;
+  if (a.peer.base) {
+    const PeerSet& ps = a.peer;
+    const unsigned int s = ps.seq[1] + 1;
+    for (int w = 0; w < ps.world; ++w)
+      reinterpret_cast<unsigned long long*>(ps.base[w] + tp_keys_off(ps.world, ps.dim))
+          [(s & 1u) * ps.world + ps.rank] = key;
+    __threadfence_system();
+    for (int w = 0; w < ps.world; ++w)
+      st_release_sys(tp_flag(ps.base[w], ps.world, ps.dim, 1, ps.rank), s);
+    return;
+  }
+  const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+  const int p = *a.pos_slot;
+  if (a.history && p >= 0 && p < a.history_cap) a.history[p] = idx;
+  *a.token_slot = idx;
+  *a.pos_slot = p + 1;
+}
+
 template <int QT, int RPW, int CPL, int GW>
 __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
   static_assert(GW == 1 || GW == kWarps, "a row group is one warp or the whole CTA");
@@ -463,24 +508,10 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
     if (tid == 0) {
       unsigned long long b = 0ull;
       for (int w = 0; w < kWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
-      if (a.argmax_slot) {
-        atomicMax(a.argmax_slot, b);
-      }
-      if (a.argmax_slot && a.ticket) {
-        __threadfence();
-        const unsigned int done = atomicAdd(a.ticket, 1u);
-        if (done == gridDim.x - 1) {
-          __threadfence();
-          const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
-          const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
-          const int p = *a.pos_slot;
-          if (a.history && p >= 0 && p < a.history_cap) a.history[p] = idx;
-          *a.token_slot = idx;
-          *a.pos_slot = p + 1;
-          *a.ticket = 0u;
-        }
-      }
+      logits_finish(a, b);
     }
+  } else if (a.epi == kEpiPeer) {
+    peer_signal(a.peer, 0, a.peer.seq[0] + 1);
   }
 }
 
@@ -931,21 +962,10 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
     }
     if (lane == 0) best_w[wid] = best;
     __syncthreads();
-    if (tid == 0 && a.argmax_slot) {
+    if (tid == 0) {
       unsigned long long b = 0ull;
       for (int w = 0; w < kTmaWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
-      atomicMax(a.argmax_slot, b);
-      const unsigned int done = a.ticket ? (__threadfence(), atomicAdd(a.ticket, 1u)) : 0u;
-      if (a.ticket && done == gridDim.x - 1) {
-        __threadfence();
-        const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
-        const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
-        const int p = *a.pos_slot;
-        if (a.history && p >= 0 && p < a.history_cap) a.history[p] = idx;
-        *a.token_slot = idx;
-        *a.pos_slot = p + 1;
-        *a.ticket = 0u;
-      }
+      logits_finish(a, b);
     }
   }
 }
@@ -1033,7 +1053,7 @@ cudaError_t tma_dispatch(const GemvArgs& a, cudaStream_t stream, bool pdl, int s
 // register form, whose weights are already in registers when the dependency
 // resolves, finishes sooner.
 bool tma_eligible(const GemvArgs& a) {
-  return a.qtype == DQMK_Q80 && a.kp <= 8192 && a.n_rows >= 32768;
+  return a.qtype == DQMK_Q80 && a.kp <= 8192 && a.n_rows >= 32768 && a.epi != kEpiPeer;
 }
 
 // ------------------------------------------------ ggml-layout compatibility
@@ -1249,10 +1269,11 @@ extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, cons
 }
 
 extern "C" int dqmk_device_error(int clear) {
-  unsigned int flags = 0, prefill_flags = 0;
+  unsigned int flags = 0, prefill_flags = 0, tp_flags = 0;
   cudaError_t e = read_device_error(&flags, clear != 0);
   if (e == cudaSuccess) e = read_prefill_error(&prefill_flags, clear != 0);
-  flags |= prefill_flags;
+  if (e == cudaSuccess) e = read_tp_error(&tp_flags, clear != 0);
+  flags |= prefill_flags | tp_flags;
   if (e != cudaSuccess) {
     cuda_fail("dqmk_device_error", e);
     return -1;

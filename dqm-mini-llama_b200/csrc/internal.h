@@ -42,7 +42,35 @@ enum GemvEpilogue : int {
   kEpiSwiGlu = 1,  // rows interleaved (gate_o, up_o): y[o] = silu(gate) * up
   kEpiQkv = 2,     // rows paired for RoPE: bias, rotate, write q / K / V cache
   kEpiLogits = 3,  // y[o] = acc; device argmax + greedy advance
+  kEpiPeer = 4,    // tensor parallel: row o of the partial sum goes to every rank's slot
 };
+
+// Tensor-parallel exchange over peer memory.  Every rank owns one
+// communication buffer (mapped into the other ranks' address spaces):
+//   vector slots [2 parities][world][dim] fp32, key slots [2][world] u64,
+//   flags [2 channels][world] u32 (channel 0: vectors, 1: argmax keys).
+// Exchange number s (1, 2, ...) of a channel uses parity s & 1; its writers
+// store into slot [s & 1][own rank] of every rank, then raise flag
+// [channel][own rank] to s everywhere; a reader waits for all flags >= s.
+struct PeerSet {
+  char* const* base;   // device array [world]: each rank's buffer (own included)
+  int rank, world, dim;
+  unsigned int* seq;   // this rank's completed exchanges per channel [2]
+  unsigned int* ticket;  // CTA completion counter of the writing kernel
+};
+__host__ __device__ inline size_t tp_round256(size_t b) { return (b + 255) / 256 * 256; }
+__host__ __device__ inline size_t tp_vec_off(int parity, int rank, int world, int dim) {
+  return ((size_t)(parity * world + rank) * dim) * sizeof(float);
+}
+__host__ __device__ inline size_t tp_keys_off(int world, int dim) {
+  return tp_round256((size_t)2 * world * dim * sizeof(float));
+}
+__host__ __device__ inline size_t tp_flags_off(int world, int dim) {
+  return tp_keys_off(world, dim) + tp_round256((size_t)2 * world * 8);
+}
+__host__ __device__ inline size_t tp_buf_bytes(int world, int dim) {
+  return tp_flags_off(world, dim) + tp_round256((size_t)2 * world * 4);
+}
 
 struct GemvArgs {
   int qtype;
@@ -75,6 +103,9 @@ struct GemvArgs {
   int* pos_slot;                    // greedy: next position (incremented)
   int* history;                     // greedy: token written at history[pos+1]
   int history_cap;
+  // kEpiPeer, and kEpiLogits under peer-memory tensor parallelism (base set):
+  // the last CTA broadcasts the local argmax key instead of advancing
+  PeerSet peer;
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
@@ -119,6 +150,13 @@ cudaError_t launch_embed_blocks(int qtype, const void* blocks, int dim, int toke
                                 cudaStream_t s);
 cudaError_t launch_argmax(const float* x, int n, unsigned long long* slot, int* index,
                           cudaStream_t s);
+// Peer-memory tensor parallelism (tp_p2p.cu): wait for every rank's partial
+// of exchange seq[0] + 1, x += their sum (fixed rank order); and the greedy
+// step after a vocabulary-parallel lm_head (max over the ranks' keys).
+cudaError_t launch_tp_reduce(float* x, const PeerSet& ps, cudaStream_t s, bool pdl);
+cudaError_t launch_tp_argmax_advance(const PeerSet& ps, int* token, int* pos, int* history,
+                                     int cap, cudaStream_t s, bool pdl);
+cudaError_t read_tp_error(unsigned int* flags, bool clear);
 cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, int* pos,
                                   int* history, int cap, cudaStream_t s);
 cudaError_t launch_kv_write(float* keys, float* values, int max_seq, int n_kv_heads,

@@ -307,6 +307,19 @@ int dqmk_nccl_unique_id(unsigned char* id_out);
  * projections over NCCL.  Collective: every rank of the group calls it with
  * the same id, each on its own device. */
 int dqmk_model_set_tp(dqmk_model* model, int rank, int world, const unsigned char* nccl_id);
+
+/* Peer-memory exchange for a tensor-parallel context (optional; without it
+ * the decode step all-reduces over NCCL).  Each rank's context owns one
+ * exchange buffer; dqmk_context_tp_ipc_handle exports it (64-byte CUDA IPC
+ * handle), the host gathers the handles of all ranks in rank order, and
+ * dqmk_context_tp_connect maps the peers' buffers.  From then on the O and
+ * down GEMVs store their partial rows straight into every rank's buffer over
+ * NVLink and raise a flag there, a one-CTA kernel waits (bounded, ~2 s; a
+ * timeout sets the device error flag) for all ranks' flags and sums the
+ * partials in rank order, and the greedy argmax is exchanged the same way.
+ * Every rank connects its context before the next step. */
+int dqmk_context_tp_ipc_handle(dqmk_context* ctx, unsigned char* handle_out);
+int dqmk_context_tp_connect(dqmk_context* ctx, const unsigned char* handles);
 int dqmk_model_stats_get(const dqmk_model* model, dqmk_model_stats* out);
 int dqmk_model_stats_reset(dqmk_model* model);
 /* ModelCudaMemoryBytes (include/dqm_llama/model.h:119). */

@@ -1,9 +1,11 @@
 """Tensor parallelism on 2 (and 4) GPUs: a reduced Qwen2-7B-shaped Q4_0 model
 (full layer widths: dim 3584, FFN 18944, 28/4 heads of 128; one layer; 8192
 vocabulary ids; untied lm_head) sharded Megatron-style, one rank per GPU over
-NCCL.  The gathered prompt logits must sit within 1e-3 x logit range of the
-oracle, greedy tokens must equal the oracle's, and the degrees must agree with
-each other.  Skipped with fewer than 2 GPUs."""
+NCCL, and again with the decode step's partial sums exchanged over peer
+memory (IPC-mapped buffers, flags, bounded waits).  The gathered prompt logits
+must sit within 1e-3 x logit range of the oracle, greedy tokens must equal the
+oracle's, and all runs must agree with each other.  Skipped with fewer than 2
+GPUs."""
 import os
 import socket
 import subprocess
@@ -52,12 +54,13 @@ def test_tensor_parallel_matches_oracle(cuda, reference, tmp_path):
     first_logits, ref_tokens, last_logits, margin = reference
     rng = float(first_logits.max() - first_logits.min())
     results = {}
-    for world in [w for w in (2, 4) if w <= n_gpu]:
-        out = tmp_path / f"tp{world}.npz"
+    runs = [(w, p2p) for w in (2, 4) if w <= n_gpu for p2p in (False, True)]
+    for world, p2p in runs:
+        out = tmp_path / f"tp{world}_{int(p2p)}.npz"
         cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
                "--nnodes=1", f"--nproc-per-node={world}", "--master-addr=127.0.0.1",
                f"--master-port={_free_port()}", os.path.join(ROOT, "tests", "tp_worker.py"),
-               "--mode", "gpu", "--out", str(out)]
+               "--mode", "gpu", "--out", str(out)] + (["--p2p"] if p2p else [])
         env = dict(os.environ, NCCL_NVLS_ENABLE="0")
         r = subprocess.run(cmd, capture_output=True, text=True, timeout=700, env=env)
         assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-6000:]
@@ -68,8 +71,10 @@ def test_tensor_parallel_matches_oracle(cuda, reference, tmp_path):
         srng = float(last_logits.max() - last_logits.min())
         serr = float(np.abs(got["step_logits"] - last_logits).max())
         assert serr <= 1e-3 * srng, f"TP{world}: step logits err {serr:.3e}"
-        results[world] = got
-        print(f"TP{world}: prompt logit err {err / rng:.2e} of range, min margin {margin:.2e}")
-    if len(results) == 2:
-        a, b = results[2]["logits"], results[4]["logits"]
-        assert float(np.abs(a - b).max()) <= 1e-3 * rng
+        results[(world, p2p)] = got
+        print(f"TP{world} {'peer memory' if p2p else 'NCCL'}: prompt logit err "
+              f"{err / rng:.2e} of range, min margin {margin:.2e}")
+    for (wa, pa), a in results.items():
+        for (wb, pb), b in results.items():
+            assert float(np.abs(a["logits"] - b["logits"]).max()) <= 1e-3 * rng
+            assert a["tokens"].tolist() == b["tokens"].tolist()

@@ -8,7 +8,9 @@
     Qwen2-7B-shaped model (full layer widths, fewer layers, smaller
     vocabulary), keeps its shard (Model.from_synth(..., tp=...)), runs
     ForwardBatch over the prompt and greedy decoding; rank 0 writes the
-    gathered logits and the tokens to --out.
+    gathered logits and the tokens to --out.  With --p2p the contexts
+    exchange IPC handles and connect, so the decode step's partial sums
+    travel over peer memory instead of NCCL.
 """
 import argparse
 import datetime
@@ -60,7 +62,7 @@ def mode_plan(pkg, rank, world):
         print("plan ok", world)
 
 
-def mode_gpu(pkg, rank, world, local, out):
+def mode_gpu(pkg, rank, world, local, out, p2p):
     S = pkg.synth
     torch.cuda.set_device(local)
     w, prompt = reduced_7b(S)
@@ -70,6 +72,11 @@ def mode_gpu(pkg, rank, world, local, out):
     model = pkg.Model.from_synth(w, max_seq_len=r["n_prompt"] + r["n_steps"], device=local,
                                  tp=(rank, world, obj[0]))
     ctx = pkg.Context(model)
+    if p2p:
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.tp_ipc_handle())
+        ctx.tp_connect(handles)
+        dist.barrier()
     logits = ctx.ForwardBatch(prompt, 0)
     first = int(np.argmax(logits))
     tokens = [first] + ctx.decode_greedy(first, r["n_prompt"], r["n_steps"] - 1).tolist()
@@ -89,6 +96,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--mode", choices=["plan", "gpu"], required=True)
     ap.add_argument("--out", default="")
+    ap.add_argument("--p2p", action="store_true",
+                    help="exchange partial sums over peer memory instead of NCCL")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -98,7 +107,7 @@ def main():
         if args.mode == "plan":
             mode_plan(pkg, rank, world)
         else:
-            mode_gpu(pkg, rank, world, local, args.out)
+            mode_gpu(pkg, rank, world, local, args.out, args.p2p)
         dist.barrier()
     finally:
         dist.destroy_process_group()
