@@ -744,16 +744,16 @@ int enqueue_step(dqmk_context* x) {
   lg.y = x->logits;
   lg.argmax_slot = x->argmax_slot();
   lg.row_offset = tp.vocab0;
-  lg.ticket = tpar && !p2p ? nullptr : x->lm_ticket();
-  if (p2p) lg.peer = ps;
+  lg.ticket = tpar ? nullptr : x->lm_ticket();
   lg.token_slot = x->token_slot();
   lg.pos_slot = x->pos_slot();
   lg.history = x->history_dev;
   lg.history_cap = c.max_seq_len;
   DQMK_CUDA_RET(api, launch_gemv(lg, s, pdl));
   if (p2p) {
-    DQMK_CUDA_RET(api, launch_tp_argmax_advance(ps, x->token_slot(), x->pos_slot(),
-                                                x->history_dev, c.max_seq_len, s, pdl));
+    DQMK_CUDA_RET(api, launch_tp_argmax_advance(ps, x->argmax_slot(), x->token_slot(),
+                                                x->pos_slot(), x->history_dev, c.max_seq_len,
+                                                s, pdl));
   } else if (tpar) {  // global greedy choice: max over the ranks' (value, index) keys
     if ((rc = tp_allreduce_max_u64(m->comm, x->argmax_slot(), 1, s, api))) return rc;
     DQMK_CUDA_RET(api, launch_greedy_advance(x->argmax_slot(), x->token_slot(), x->pos_slot(),

@@ -174,23 +174,13 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, float c, float s
   }
 }
 
-template <int RPW>
+template <int RPW, bool PEER>
 __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
                                          const float (&acc)[RPW], int pos,
                                          unsigned long long& best) {
-  if (a.epi == kEpiStore) {
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      const int row = grp * RPW + r;
-      if (lane == r && row < a.n_rows) {
-        float v = acc[r];
-        if (a.bias) v = __fadd_rn(v, a.bias[row]);
-        if (a.residual) v = __fadd_rn(__ldcg(a.residual + row), v);
-        a.y[row] = v;
-      }
-    }
-  } else if (a.epi == kEpiPeer) {
-    // row-parallel partial sum: to slot [parity][own rank] of every rank
+  if constexpr (PEER) {
+    // row-parallel partial sum (kEpiPeer): to slot [parity][own rank] of every
+    // rank.  A separate instantiation, so the other kernels' code is untouched.
     const unsigned int s = a.peer.seq[0] + 1;
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
@@ -200,6 +190,19 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
           reinterpret_cast<float*>(a.peer.base[w] + tp_vec_off((int)(s & 1u), a.peer.rank,
                                                                a.peer.world, a.peer.dim))[row] =
               acc[r];
+      }
+    }
+    return;
+  }
+  if (a.epi == kEpiStore) {
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int row = grp * RPW + r;
+      if (lane == r && row < a.n_rows) {
+        float v = acc[r];
+        if (a.bias) v = __fadd_rn(v, a.bias[row]);
+        if (a.residual) v = __fadd_rn(__ldcg(a.residual + row), v);
+        a.y[row] = v;
       }
     }
   } else if (a.epi == kEpiLogits) {
@@ -372,8 +375,8 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const flo
 
 // Thread 0 of each CTA with the CTA's best (value, index) key: fold it into
 // the device argmax; the last CTA then advances the greedy state (token,
-// position, history) or, under peer-memory tensor parallelism, sends this
-// rank's key to every rank and raises its flag (channel 1).
+// position, history) unless ticket is null (tensor parallel: the ranks' keys
+// are combined by a later kernel).
 __device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long long b) {
   if (!a.argmax_slot) return;
   atomicMax(a.argmax_slot, b);
@@ -384,17 +387,6 @@ __device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long l
   __threadfence();
   const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
   *a.ticket = 0u;
-  if (a.peer.base) {
-    const PeerSet& ps = a.peer;
-    const unsigned int s = ps.seq[1] + 1;
-    for (int w = 0; w < ps.world; ++w)
-      reinterpret_cast<unsigned long long*>(ps.base[w] + tp_keys_off(ps.world, ps.dim))
-          [(s & 1u) * ps.world + ps.rank] = key;
-    __threadfence_system();
-    for (int w = 0; w < ps.world; ++w)
-      st_release_sys(tp_flag(ps.base[w], ps.world, ps.dim, 1, ps.rank), s);
-    return;
-  }
   const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
   const int p = *a.pos_slot;
   if (a.history && p >= 0 && p < a.history_cap) a.history[p] = idx;
@@ -402,7 +394,7 @@ __device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long l
   *a.pos_slot = p + 1;
 }
 
-template <int QT, int RPW, int CPL, int GW>
+template <int QT, int RPW, int CPL, int GW, bool PEER>
 __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
   static_assert(GW == 1 || GW == kWarps, "a row group is one warp or the whole CTA");
   constexpr int GT = GW * 32;         // threads per row group
@@ -475,9 +467,9 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
         acc[r] = t;
       }
       __syncthreads();
-      if (wid == 0) epilogue<RPW>(a, grp, lane, acc, pos, best);
+      if (wid == 0) epilogue<RPW, PEER>(a, grp, lane, acc, pos, best);
     } else {
-      epilogue<RPW>(a, grp, lane, acc, pos, best);
+      epilogue<RPW, PEER>(a, grp, lane, acc, pos, best);
     }
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
@@ -510,24 +502,24 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
       for (int w = 0; w < kWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
       logits_finish(a, b);
     }
-  } else if (a.epi == kEpiPeer) {
-    peer_signal(a.peer, 0, a.peer.seq[0] + 1);
   }
+  if constexpr (PEER) peer_signal(a.peer, 0, a.peer.seq[0] + 1);
 }
 
 // ------------------------------------------------------------ launch table
 // One-time kernel attributes and the resident-CTA cap for the grid-stride
 // case.  Run before any stream capture (context creation does).
-template <int QT, int RPW, int CPL, int GW>
+template <int QT, int RPW, int CPL, int GW, bool PEER>
 cudaError_t prepare_t(int* max_ctas_out) {
   static int max_ctas = -1;
   if (max_ctas < 0) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<QT, RPW, CPL, GW>,
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<QT, RPW, CPL, GW, PEER>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          200 * 1024);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<QT, RPW, CPL, GW>,
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm,
+                                                      gemv_kernel<QT, RPW, CPL, GW, PEER>,
                                                       kWarps * 32, 4096 * sizeof(float));
     if (e != cudaSuccess) return e;
     max_ctas = (per_sm > 0 ? per_sm : 1) * sm_count();
@@ -536,10 +528,10 @@ cudaError_t prepare_t(int* max_ctas_out) {
   return cudaSuccess;
 }
 
-template <int QT, int RPW, int CPL, int GW>
-cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+template <int QT, int RPW, int CPL, int GW, bool PEER>
+cudaError_t launch_impl(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   int max_ctas = 0;
-  cudaError_t e = prepare_t<QT, RPW, CPL, GW>(&max_ctas);
+  cudaError_t e = prepare_t<QT, RPW, CPL, GW, PEER>(&max_ctas);
   if (e != cudaSuccess) return e;
   const size_t smem = (size_t)a.kp * sizeof(float);
   const int n_groups = (a.n_rows + RPW - 1) / RPW;
@@ -547,14 +539,21 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   int grid = (n_groups + GPC - 1) / GPC;
   if (grid > max_ctas) grid = max_ctas;
   if (grid < 1) grid = 1;
-  return launch(gemv_kernel<QT, RPW, CPL, GW>, dim3(grid), dim3(kWarps * 32), smem, stream, pdl,
-                a);
+  return launch(gemv_kernel<QT, RPW, CPL, GW, PEER>, dim3(grid), dim3(kWarps * 32), smem,
+                stream, pdl, a);
+}
+
+// kEpiPeer takes its own instantiation of the variant (see epilogue).
+template <int QT, int RPW, int CPL, int GW>
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.epi == kEpiPeer) return launch_impl<QT, RPW, CPL, GW, true>(a, stream, pdl);
+  return launch_impl<QT, RPW, CPL, GW, false>(a, stream, pdl);
 }
 
 // Every instantiation the dispatcher below can pick.
 #define DQMK_GEMV_VARIANTS(X)                                                             \
   X(DQMK_Q80, 2, 1, 1) X(DQMK_Q80, 2, 2, 1) X(DQMK_Q80, 4, 2, 1) X(DQMK_Q80, 2, 2, 4)       \
-  X(DQMK_Q80, 4, 2, 4) X(DQMK_Q80, 4, 4, 4)                                                 \
+  X(DQMK_Q80, 2, 3, 4) X(DQMK_Q80, 2, 4, 4) X(DQMK_Q80, 4, 2, 4) X(DQMK_Q80, 4, 4, 4)       \
   X(DQMK_Q40, 4, 1, 1) X(DQMK_Q40, 2, 2, 1) X(DQMK_Q40, 4, 2, 1) X(DQMK_Q40, 2, 2, 4)       \
   X(DQMK_Q40, 2, 4, 4) X(DQMK_Q40, 2, 5, 4)
 
@@ -932,7 +931,7 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
     }
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]);
-    epilogue<RPW>(a, tile * kTmaWarps + wid, lane, acc, pos, best);
+    epilogue<RPW, false>(a, tile * kTmaWarps + wid, lane, acc, pos, best);
     __syncthreads();  // every warp is done reading stage s
     if (tid == 0) {
       pending &= ~(1u << s);
@@ -1119,8 +1118,9 @@ __global__ void linear_blocks_kernel(const float* __restrict__ x, int rows, int 
 
 cudaError_t gemv_prepare() {
   cudaError_t e = cudaSuccess;
-#define DQMK_PREP(QT, RPW, CPL, GW) \
-  if (e == cudaSuccess) e = prepare_t<QT, RPW, CPL, GW>(nullptr);
+#define DQMK_PREP(QT, RPW, CPL, GW)                                     \
+  if (e == cudaSuccess) e = prepare_t<QT, RPW, CPL, GW, false>(nullptr); \
+  if (e == cudaSuccess) e = prepare_t<QT, RPW, CPL, GW, true>(nullptr);
   DQMK_GEMV_VARIANTS(DQMK_PREP)
 #undef DQMK_PREP
 #define DQMK_TMA_PREP(QT, RPW) \
@@ -1162,7 +1162,8 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     if (wide) return chunks <= 256 ? launch_t<DQMK_Q80, 4, 2, 4>(a, stream, pdl)
                                    : launch_t<DQMK_Q80, 4, 4, 4>(a, stream, pdl);
     if (chunks <= 256) return launch_t<DQMK_Q80, 2, 2, 4>(a, stream, pdl);
-    return launch_t<DQMK_Q80, 4, 4, 4>(a, stream, pdl);
+    if (chunks <= 384) return launch_t<DQMK_Q80, 2, 3, 4>(a, stream, pdl);
+    return launch_t<DQMK_Q80, 2, 4, 4>(a, stream, pdl);
   }
   const bool tall = a.n_rows >= 8192;
   if (chunks <= 32)

@@ -58,17 +58,17 @@ struct PeerSet {
   unsigned int* seq;   // this rank's completed exchanges per channel [2]
   unsigned int* ticket;  // CTA completion counter of the writing kernel
 };
-__host__ __device__ inline size_t tp_round256(size_t b) { return (b + 255) / 256 * 256; }
-__host__ __device__ inline size_t tp_vec_off(int parity, int rank, int world, int dim) {
+__host__ __device__ __forceinline__ size_t tp_round256(size_t b) { return (b + 255) / 256 * 256; }
+__host__ __device__ __forceinline__ size_t tp_vec_off(int parity, int rank, int world, int dim) {
   return ((size_t)(parity * world + rank) * dim) * sizeof(float);
 }
-__host__ __device__ inline size_t tp_keys_off(int world, int dim) {
+__host__ __device__ __forceinline__ size_t tp_keys_off(int world, int dim) {
   return tp_round256((size_t)2 * world * dim * sizeof(float));
 }
-__host__ __device__ inline size_t tp_flags_off(int world, int dim) {
+__host__ __device__ __forceinline__ size_t tp_flags_off(int world, int dim) {
   return tp_keys_off(world, dim) + tp_round256((size_t)2 * world * 8);
 }
-__host__ __device__ inline size_t tp_buf_bytes(int world, int dim) {
+__host__ __device__ __forceinline__ size_t tp_buf_bytes(int world, int dim) {
   return tp_flags_off(world, dim) + tp_round256((size_t)2 * world * 4);
 }
 
@@ -103,8 +103,7 @@ struct GemvArgs {
   int* pos_slot;                    // greedy: next position (incremented)
   int* history;                     // greedy: token written at history[pos+1]
   int history_cap;
-  // kEpiPeer, and kEpiLogits under peer-memory tensor parallelism (base set):
-  // the last CTA broadcasts the local argmax key instead of advancing
+  // kEpiPeer: where the partial rows go
   PeerSet peer;
 };
 
@@ -154,8 +153,9 @@ cudaError_t launch_argmax(const float* x, int n, unsigned long long* slot, int* 
 // of exchange seq[0] + 1, x += their sum (fixed rank order); and the greedy
 // step after a vocabulary-parallel lm_head (max over the ranks' keys).
 cudaError_t launch_tp_reduce(float* x, const PeerSet& ps, cudaStream_t s, bool pdl);
-cudaError_t launch_tp_argmax_advance(const PeerSet& ps, int* token, int* pos, int* history,
-                                     int cap, cudaStream_t s, bool pdl);
+cudaError_t launch_tp_argmax_advance(const PeerSet& ps, const unsigned long long* local_key,
+                                     int* token, int* pos, int* history, int cap, cudaStream_t s,
+                                     bool pdl);
 cudaError_t read_tp_error(unsigned int* flags, bool clear);
 cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, int* pos,
                                   int* history, int cap, cudaStream_t s);

@@ -2,10 +2,10 @@
 // memory (NVLink / NVSwitch), which replaces an NCCL all-reduce per
 // row-parallel GEMV in the decode step.
 //
-// The writing side lives in the GEMV epilogues (gemv.cu, kEpiPeer and the
-// lm_head's last CTA): each rank stores its partial rows straight into slot
+// The writing side of the vector exchange lives in the row-parallel GEMV
+// (gemv.cu, kEpiPeer): each rank stores its partial rows straight into slot
 // [parity][own rank] of every rank's buffer and raises its flag there with a
-// system-scope release.  Here a rank waits until every rank's flag for the
+// system-scope release.  The argmax exchange is one kernel here.  Here a rank waits until every rank's flag for the
 // exchange has arrived (acquire loads on its own memory, bounded to about two
 // seconds), then sums the slots in fixed rank order -- the same order on
 // every rank, so all ranks hold bit-identical sums -- and adds the residual.
@@ -76,11 +76,21 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(float* __restrict__ x, c
   if (threadIdx.x == 0) ps.seq[0] = s;
 }
 
-__global__ void tp_argmax_advance_kernel(const PeerSet ps, int* token, int* pos, int* history,
-                                         int cap) {
+// One thread: send this rank's argmax key (from the vocabulary-parallel
+// lm_head) to every rank, wait for all ranks' keys, take the max -- first
+// maximum wins through the packed index -- and advance the greedy state.
+__global__ void tp_argmax_advance_kernel(const PeerSet ps, const unsigned long long* local_key,
+                                         int* token, int* pos, int* history, int cap) {
   pdl_trigger();
   pdl_wait();
   const unsigned int s = ps.seq[1] + 1;
+  const unsigned long long mine = *local_key;
+  for (int w = 0; w < ps.world; ++w)
+    reinterpret_cast<unsigned long long*>(ps.base[w] + tp_keys_off(ps.world, ps.dim))
+        [(s & 1u) * ps.world + ps.rank] = mine;
+  __threadfence_system();
+  for (int w = 0; w < ps.world; ++w)
+    st_release_sys(tp_flag(ps.base[w], ps.world, ps.dim, 1, ps.rank), s);
   unsigned long long best = 0ull;
   if (wait_flags(ps, 1, s)) {
     const unsigned long long* keys = reinterpret_cast<const unsigned long long*>(
@@ -105,10 +115,11 @@ cudaError_t launch_tp_reduce(float* x, const PeerSet& ps, cudaStream_t s, bool p
   return launch(tp_reduce_kernel, dim3(1), dim3(256), 0, s, pdl, x, ps);
 }
 
-cudaError_t launch_tp_argmax_advance(const PeerSet& ps, int* token, int* pos, int* history,
-                                     int cap, cudaStream_t s, bool pdl) {
-  return launch(tp_argmax_advance_kernel, dim3(1), dim3(1), 0, s, pdl, ps, token, pos, history,
-                cap);
+cudaError_t launch_tp_argmax_advance(const PeerSet& ps, const unsigned long long* local_key,
+                                     int* token, int* pos, int* history, int cap, cudaStream_t s,
+                                     bool pdl) {
+  return launch(tp_argmax_advance_kernel, dim3(1), dim3(1), 0, s, pdl, ps, local_key, token, pos,
+                history, cap);
 }
 
 cudaError_t read_tp_error(unsigned int* flags, bool clear) {
