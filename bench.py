@@ -364,7 +364,7 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
     exchange = "none"
     if world > 1:
         exchange = "nccl"
-        if not args.nccl:
+        if args.p2p:
             handles = [None] * world
             dist.all_gather_object(handles, ctx.tp_ipc_handle())
             ctx.tp_connect(handles)
@@ -487,9 +487,9 @@ def main():
     ap.add_argument("--model", default="qwen2-0.5b", choices=["qwen2-0.5b", "qwen2-7b"],
                     help="qwen2-7b: tensor-parallel decode over the --gpus ranks")
     ap.add_argument("--ctx", type=int, default=2048, help="qwen2-7b: KV length before decoding")
-    ap.add_argument("--nccl", action="store_true",
-                    help="qwen2-7b under tensor parallelism: all-reduce over NCCL instead of "
-                         "the peer-memory exchange")
+    ap.add_argument("--p2p", action="store_true",
+                    help="qwen2-7b under tensor parallelism: exchange partial sums over peer "
+                         "memory (IPC-mapped buffers) instead of NCCL all-reduces")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

@@ -142,11 +142,13 @@ __device__ __forceinline__ unsigned int* tp_flag(char* base, int world, int dim,
 
 // After every thread of the CTA stored its share of exchange s: the last CTA
 // of the grid raises flag [channel][own rank] to s on every rank.  Called by
-// all threads of every CTA.
+// all threads of every CTA.  One system-scope fence per CTA: the barrier
+// orders the CTA's stores before thread 0's fence, and release cumulativity
+// carries them to any rank that acquires the flag.
 __device__ __forceinline__ void peer_signal(const PeerSet& ps, int channel, unsigned int s) {
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned int done = atomicAdd(ps.ticket, 1u);
     if (done == gridDim.x - 1) {
       __threadfence_system();
