@@ -15,61 +15,15 @@
 // so a captured graph serves every decode step.
 #include <mutex>
 
+#include "attention_dev.cuh"
 #include "common.cuh"
 #include "internal.h"
 
 namespace dqmk {
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kMaxGroup = 8;  // query heads per KV head
-constexpr int kMinChunk = 32;
+using namespace at;
 
-// Floats per split partial: the head_dim sums, then m and l, padded so every
-// row starts 16-byte aligned (float4 reads in the combine).
-__host__ __device__ constexpr int part_stride(int hd) { return hd + 4; }
-
-__device__ __forceinline__ int round_up32(int v) { return (v + 31) & ~31; }
-
-// Split bookkeeping shared by both kernel forms.
-struct Split {
-  int T, chunk, n_active, t0, n;
-};
-
-__device__ __forceinline__ Split split_of(const AttnArgs& a, int split, int pos) {
-  Split s;
-  s.T = pos + 1;
-  s.chunk = round_up32((s.T + a.max_splits - 1) / a.max_splits);
-  if (s.chunk < kMinChunk) s.chunk = kMinChunk;
-  s.n_active = (s.T + s.chunk - 1) / s.chunk;
-  s.t0 = split * s.chunk;
-  s.n = max(0, min(s.T, s.t0 + s.chunk) - s.t0);
-  return s;
-}
-
-// Softmax statistics of one split's scores (one warp per head); scores are
-// replaced by exp(s - m).
-template <int NT>
-__device__ __forceinline__ void split_softmax(float* ss, int chunk_cap, int G, int n,
-                                              float* head_m, float* head_l) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  for (int h = wid; h < G; h += NT / 32) {
-    float m = -INFINITY;
-    for (int t = lane; t < n; t += 32) m = fmaxf(m, ss[h * chunk_cap + t]);
-    m = warp_max(m);
-    float l = 0.0f;
-    for (int t = lane; t < n; t += 32) {
-      const float p = expf(ss[h * chunk_cap + t] - m);
-      ss[h * chunk_cap + t] = p;
-      l += p;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      head_m[h] = m;
-      head_l[h] = l;
-    }
-  }
-}
 
 // Completion ticket per KV head; the CTA that takes the last one merges the
 // splits: out = sum_i e^(m_i - M) o_i / sum_i e^(m_i - M) l_i.  Split
@@ -127,230 +81,12 @@ __device__ __forceinline__ void split_combine(const AttnArgs& a, int kvh, int G,
   if (threadIdx.x == 0) a.tickets[kvh] = 0u;
 }
 
-// Last-CTA merge for the head_dim-templated kernel: the same arithmetic as
-// split_combine, with each thread producing 4 consecutive output dims from
-// float4 partial reads, all of its splits' loads issued in groups of 16.
-template <int NT, int HD>
-__device__ __forceinline__ void split_combine_hd(const AttnArgs& a, int kvh, int G, int n_active,
-                                                 float* stats, int* is_last) {
-  constexpr int PS = part_stride(HD);
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int done = atomicAdd(&a.tickets[kvh], 1u);
-    *is_last = done == gridDim.y - 1;
-  }
-  __syncthreads();
-  if (!*is_last) return;
-  __threadfence();
-  float* w = stats;                                              // [n_active][8] weights
-  float* lsum = stats + (size_t)a.max_splits * kMaxGroup;        // [n_active][8] l
-  float* inv_den = lsum + (size_t)a.max_splits * kMaxGroup;      // [8]
-  for (int i = threadIdx.x; i < n_active * G; i += NT) {
-    const int sp = i / G, h = i % G;
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(
-        a.partials + ((size_t)(kvh * G + h) * a.max_splits + sp) * PS + HD));
-    w[sp * kMaxGroup + h] = ml.x;
-    lsum[sp * kMaxGroup + h] = ml.y;
-  }
-  __syncthreads();
-  if (threadIdx.x < G) {
-    const int h = threadIdx.x;
-    float M = -INFINITY;
-    for (int sp = 0; sp < n_active; ++sp) M = fmaxf(M, w[sp * kMaxGroup + h]);
-    float den = 0.0f;
-    for (int sp = 0; sp < n_active; ++sp) {
-      const float e = expf(w[sp * kMaxGroup + h] - M);
-      w[sp * kMaxGroup + h] = e;
-      den = fmaf(e, lsum[sp * kMaxGroup + h], den);
-    }
-    inv_den[h] = den;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < G * (HD / 4); i += NT) {
-    const int h = i / (HD / 4), d4 = i % (HD / 4);
-    const float4* part = reinterpret_cast<const float4*>(
-                             a.partials + (size_t)(kvh * G + h) * a.max_splits * PS) + d4;
-    float4 num = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int sp0 = 0; sp0 < n_active; sp0 += 16) {
-      float4 o[16];
-#pragma unroll
-      for (int u = 0; u < 16; ++u)
-        o[u] = sp0 + u < n_active ? __ldcg(part + (size_t)(sp0 + u) * (PS / 4))
-                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        if (sp0 + u < n_active) {
-          const float wt = w[(sp0 + u) * kMaxGroup + h];
-          num.x = fmaf(wt, o[u].x, num.x);
-          num.y = fmaf(wt, o[u].y, num.y);
-          num.z = fmaf(wt, o[u].z, num.z);
-          num.w = fmaf(wt, o[u].w, num.w);
-        }
-      }
-    }
-    const float den = inv_den[h];
-    *reinterpret_cast<float4*>(a.out + (size_t)(kvh * G + h) * HD + d4 * 4) =
-        make_float4(__fdiv_rn(num.x, den), __fdiv_rn(num.y, den), __fdiv_rn(num.z, den),
-                    __fdiv_rn(num.w, den));
-  }
-  if (threadIdx.x == 0) a.tickets[kvh] = 0u;
-}
-
-// head_dim known at compile time (64 / 128), 256 threads.  Scores: HD/16
-// threads per position, each holding 16 dims of the K row (4 x 16-byte loads),
-// two position passes' loads issued together, partial dots folded with
-// shuffles.  P.V: thread (d4, group) owns 4 consecutive dims and every
-// GROUPS-th position, with 8 float4 V loads in flight.  A single active split
-// writes its output directly.
-template <int HD>
-constexpr int hd_groups() {
-  return 256 / (HD / 4);
-}
-
 template <int HD>
 __global__ void __launch_bounds__(256) attention_hd_kernel(const AttnArgs a, int chunk_cap) {
-  constexpr int NT = 256;
-  constexpr int TPT = HD / 16;          // threads per position (scores)
-  constexpr int TOK = NT / TPT;         // positions per score pass
-  constexpr int D4 = HD / 4;            // float4 columns
-  constexpr int GROUPS = hd_groups<HD>();  // position groups in P.V
-  constexpr int PV = 8;                 // float4 V loads in flight per thread
-  constexpr int PS = part_stride(HD);
   extern __shared__ float sm[];
-  __shared__ float head_m[kMaxGroup], head_l[kMaxGroup];
-  __shared__ int is_last;
-
   pdl_trigger();
   pdl_wait();
-
-  const int tid = threadIdx.x;
-  const int kvh = blockIdx.x, split = blockIdx.y;
-  const int G = a.n_heads / a.n_kv_heads;
-  const int pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
-  const Split sp = split_of(a, split, pos);
-  const size_t row_stride = (size_t)a.n_kv_heads * HD;
-  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
-  const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
-  float* sq = sm;                            // [8][HD]
-  float* ss = sq + kMaxGroup * HD;           // [8][chunk_cap]
-  float* sacc = ss + kMaxGroup * chunk_cap;  // [GROUPS][8][HD]
-  float* stats = sacc + GROUPS * kMaxGroup * HD;
-
-  if (split < sp.n_active) {
-    for (int i = tid; i < G * D4; i += NT)
-      reinterpret_cast<float4*>(sq)[i] =
-          __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)(kvh * G) * HD) + i);
-    __syncthreads();
-    const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
-    const int part = tid % TPT;
-    for (int base = 0; base < sp.n; base += 2 * TOK) {
-      float4 k4[2][4];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int t = base + u * TOK + tid / TPT;
-        const float4* kr =
-            reinterpret_cast<const float4*>(kbase + (size_t)(sp.t0 + t) * row_stride) + part * 4;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          k4[u][i] = t < sp.n ? __ldcg(kr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int t = base + u * TOK + tid / TPT;
-        float dot[kMaxGroup];
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-          float d = 0.0f;
-          if (h < G) {
-            const float4* q4 = reinterpret_cast<const float4*>(sq + h * HD) + part * 4;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float4 qq = q4[i];
-              d = fmaf(qq.x, k4[u][i].x, d);
-              d = fmaf(qq.y, k4[u][i].y, d);
-              d = fmaf(qq.z, k4[u][i].z, d);
-              d = fmaf(qq.w, k4[u][i].w, d);
-            }
-          }
-          dot[h] = d;
-        }
-#pragma unroll
-        for (int h = 0; h < kMaxGroup; ++h) {
-#pragma unroll
-          for (int o = TPT / 2; o > 0; o >>= 1) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
-        }
-        if (t < sp.n && part == 0) {
-#pragma unroll
-          for (int h = 0; h < kMaxGroup; ++h)
-            if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
-        }
-      }
-    }
-    __syncthreads();
-    split_softmax<NT>(ss, chunk_cap, G, sp.n, head_m, head_l);
-    __syncthreads();
-
-    const int d4 = tid % D4, gi = tid / D4;
-    float4 acc[kMaxGroup];
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) acc[h] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int t = gi; t < sp.n; t += PV * GROUPS) {
-      float4 v[PV];
-#pragma unroll
-      for (int u = 0; u < PV; ++u) {
-        const int tt = t + u * GROUPS;
-        v[u] = tt < sp.n ? __ldcg(reinterpret_cast<const float4*>(
-                               vbase + (size_t)(sp.t0 + tt) * row_stride) + d4)
-                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
-#pragma unroll
-      for (int u = 0; u < PV; ++u) {
-        const int tt = t + u * GROUPS;
-        if (tt < sp.n) {
-#pragma unroll
-          for (int h = 0; h < kMaxGroup; ++h) {
-            if (h < G) {
-              const float pr = ss[h * chunk_cap + tt];
-              acc[h].x = fmaf(pr, v[u].x, acc[h].x);
-              acc[h].y = fmaf(pr, v[u].y, acc[h].y);
-              acc[h].z = fmaf(pr, v[u].z, acc[h].z);
-              acc[h].w = fmaf(pr, v[u].w, acc[h].w);
-            }
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h)
-      if (h < G) reinterpret_cast<float4*>(sacc + (gi * kMaxGroup + h) * HD)[d4] = acc[h];
-    __syncthreads();
-
-    const bool direct = sp.n_active == 1;
-    for (int i = tid; i < G * D4; i += NT) {
-      const int h = i / D4, c4 = i % D4;
-      float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-      for (int g2 = 0; g2 < GROUPS; ++g2) {
-        const float4 x = reinterpret_cast<const float4*>(sacc + (g2 * kMaxGroup + h) * HD)[c4];
-        o.x += x.x;
-        o.y += x.y;
-        o.z += x.z;
-        o.w += x.w;
-      }
-      if (direct) {
-        const float l = head_l[h];
-        *reinterpret_cast<float4*>(a.out + (size_t)(kvh * G + h) * HD + c4 * 4) =
-            make_float4(__fdiv_rn(o.x, l), __fdiv_rn(o.y, l), __fdiv_rn(o.z, l),
-                        __fdiv_rn(o.w, l));
-      } else {
-        float* pp = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * PS;
-        reinterpret_cast<float4*>(pp)[c4] = o;
-        if (c4 == 0) *reinterpret_cast<float2*>(pp + HD) = make_float2(head_m[h], head_l[h]);
-      }
-    }
-  }
-  if (sp.n_active > 1) split_combine_hd<NT, HD>(a, kvh, G, sp.n_active, stats, &is_last);
+  attention_hd_body<HD, 256>(a, chunk_cap, blockIdx.x, blockIdx.y, gridDim.y, sm);
 }
 
 // Any head_dim that is a multiple of 4 up to 256: one thread per position.
@@ -466,17 +202,20 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, i
     split_combine<kThreads>(a, kvh, G, hd, sp.n_active, sacc + kMaxGroup * hd * (kThreads / hd > 0 ? kThreads / hd : 1), &is_last);
 }
 
-int chunk_cap_for(int max_seq, int max_splits) {
+}  // namespace
+
+int attention_chunk_cap(int max_seq, int max_splits) {
   int c = (max_seq + max_splits - 1) / max_splits;
   c = (c + 31) & ~31;
   return c < kMinChunk ? kMinChunk : c;
 }
 
-size_t smem_bytes_hd(int head_dim, int chunk_cap, int max_splits) {
-  const int groups = 256 / (head_dim / 4);
-  return sizeof(float) * ((size_t)kMaxGroup * head_dim + (size_t)kMaxGroup * chunk_cap +
-                          (size_t)groups * kMaxGroup * head_dim +
-                          (size_t)(2 * max_splits + 1) * kMaxGroup);
+namespace {
+
+int chunk_cap_for(int max_seq, int max_splits) {
+  int c = (max_seq + max_splits - 1) / max_splits;
+  c = (c + 31) & ~31;
+  return c < kMinChunk ? kMinChunk : c;
 }
 
 size_t smem_bytes(int threads, int head_dim, int chunk_cap, int max_splits) {
@@ -524,7 +263,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
       ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.out) |
         reinterpret_cast<uintptr_t>(a.partials)) & 15u) == 0;
   const bool hd_kernel = (a.head_dim == 64 || a.head_dim == 128) && aligned;
-  const size_t smem = hd_kernel ? smem_bytes_hd(a.head_dim, cap, a.max_splits)
+  const size_t smem = hd_kernel ? smem_bytes_hd(a.head_dim, cap, a.max_splits, 256)
                                 : smem_bytes(kThreads, a.head_dim, cap, a.max_splits);
   cudaError_t e = attention_prepare();
   if (e != cudaSuccess) return e;

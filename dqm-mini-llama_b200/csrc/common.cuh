@@ -145,12 +145,13 @@ __device__ __forceinline__ unsigned int* tp_flag(char* base, int world, int dim,
 // all threads of every CTA.  One system-scope fence per CTA: the barrier
 // orders the CTA's stores before thread 0's fence, and release cumulativity
 // carries them to any rank that acquires the flag.
-__device__ __forceinline__ void peer_signal(const PeerSet& ps, int channel, unsigned int s) {
+__device__ __forceinline__ void peer_signal(const PeerSet& ps, int channel, unsigned int s,
+                                            int n_ctas) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
     const unsigned int done = atomicAdd(ps.ticket, 1u);
-    if (done == gridDim.x - 1) {
+    if (done == (unsigned int)n_ctas - 1) {
       __threadfence_system();
       for (int w = 0; w < ps.world; ++w)
         st_release_sys(tp_flag(ps.base[w], ps.world, ps.dim, channel, ps.rank), s);

@@ -117,6 +117,12 @@ struct dqmk_context {
   unsigned int* tp_seq = nullptr;
   bool p2p = false;
   std::vector<void*> ipc_opened;
+  // persistent decode step: phase table, grid-barrier words, launch shape
+  StepPhase* step_phases = nullptr;
+  int step_n = 0, step_grid = 0;
+  int step_set[3] = {-1, -1, -1};
+  size_t step_smem = 0;
+  unsigned int* step_sync = nullptr;
   float *keys = nullptr, *values = nullptr, *partials = nullptr;
   // device state block: [argmax u64][lm ticket u32][token i32][pos i32][pad]
   //                     [attention tickets u32 x n_kv] ...
@@ -605,7 +611,12 @@ PeerSet peer_set(const dqmk_context* x) {
   return ps;
 }
 
-int enqueue_step(dqmk_context* x) {
+int enqueue_lm_head(dqmk_context* x);
+
+// The decode step.  With rec set (single-GPU only), the embedding, GEMV and
+// attention operations are recorded as phases of the persistent step kernel
+// instead of being launched, and the lm_head is left to enqueue_lm_head.
+int enqueue_step(dqmk_context* x, std::vector<StepPhase>* rec = nullptr) {
   const char* api = "ForwardToken";
   const bool pdl = use_pdl();
   dqmk_model* m = x->m;
@@ -616,6 +627,24 @@ int enqueue_step(dqmk_context* x) {
   const PeerSet ps = peer_set(x);
   cudaStream_t s = x->stream;
   int rc;
+  auto gemv_op = [&](const GemvArgs& a) -> cudaError_t {
+    if (!rec) return launch_gemv(a, s, pdl);
+    StepPhase p = {};
+    p.kind = kPhaseGemv;
+    p.variant = gemv_variant_id(a);
+    p.g = a;
+    rec->push_back(p);
+    return cudaSuccess;
+  };
+  auto attn_op = [&](const AttnArgs& a) -> cudaError_t {
+    if (!rec) return launch_attention(a, s, pdl);
+    StepPhase p = {};
+    p.kind = kPhaseAttn;
+    p.chunk_cap = attention_chunk_cap(a.max_seq, a.max_splits);
+    p.at = a;
+    rec->push_back(p);
+    return cudaSuccess;
+  };
   EmbedArgs ea = {};
   ea.qtype = m->embd.qtype;
   ea.qs = m->embd.qs();
@@ -626,7 +655,14 @@ int enqueue_step(dqmk_context* x) {
   ea.token_dev = x->token_slot();
   ea.y = x->x;
   ea.argmax_slot = x->argmax_slot();
-  DQMK_CUDA_RET(api, launch_embed_packed(ea, s));
+  if (rec) {
+    StepPhase p = {};
+    p.kind = kPhaseEmbed;
+    p.e = ea;
+    rec->push_back(p);
+  } else {
+    DQMK_CUDA_RET(api, launch_embed_packed(ea, s));
+  }
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = m->layers[l];
     GemvArgs g = {};
@@ -652,7 +688,7 @@ int enqueue_step(dqmk_context* x) {
     g.n_kv_heads = tp.n_kv_heads;
     g.head_dim = c.head_dim;
     g.neox = c.rope_neox;
-    DQMK_CUDA_RET(api, launch_gemv(g, s, pdl));
+    DQMK_CUDA_RET(api, gemv_op(g));
 
     AttnArgs at = {};
     at.q = x->q;
@@ -668,7 +704,7 @@ int enqueue_step(dqmk_context* x) {
     at.partials = x->partials;
     at.tickets = x->attn_tickets();
     at.max_splits = x->attn_splits;
-    DQMK_CUDA_RET(api, launch_attention(at, s, pdl));
+    DQMK_CUDA_RET(api, attn_op(at));
 
     GemvArgs o = {};
     o.qtype = L.wo.qtype;
@@ -685,7 +721,7 @@ int enqueue_step(dqmk_context* x) {
       o.epi = kEpiPeer;
       o.peer = ps;
     }
-    DQMK_CUDA_RET(api, launch_gemv(o, s, pdl));
+    DQMK_CUDA_RET(api, gemv_op(o));
     if (p2p) {
       DQMK_CUDA_RET(api, launch_tp_reduce(x->x, ps, s, pdl));
     } else if (tpar) {  // complete the row-parallel sum, then the residual add
@@ -705,7 +741,7 @@ int enqueue_step(dqmk_context* x) {
     gu.eps = c.rms_norm_eps;
     gu.epi = kEpiSwiGlu;
     gu.y = x->h;
-    DQMK_CUDA_RET(api, launch_gemv(gu, s, pdl));
+    DQMK_CUDA_RET(api, gemv_op(gu));
 
     GemvArgs dn = {};
     dn.qtype = L.down.qtype;
@@ -722,7 +758,7 @@ int enqueue_step(dqmk_context* x) {
       dn.epi = kEpiPeer;
       dn.peer = ps;
     }
-    DQMK_CUDA_RET(api, launch_gemv(dn, s, pdl));
+    DQMK_CUDA_RET(api, gemv_op(dn));
     if (p2p) {
       DQMK_CUDA_RET(api, launch_tp_reduce(x->x, ps, s, pdl));
     } else if (tpar) {
@@ -730,6 +766,21 @@ int enqueue_step(dqmk_context* x) {
       DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
     }
   }
+  if (rec) return DQMK_OK;
+  return enqueue_lm_head(x);
+}
+
+int enqueue_lm_head(dqmk_context* x) {
+  const char* api = "ForwardToken";
+  const bool pdl = use_pdl();
+  dqmk_model* m = x->m;
+  const dqmk_model_config& c = m->cfg;
+  const dqmk_tp_plan& tp = m->tp;
+  const bool tpar = tp.world > 1;
+  const bool p2p = tpar && x->p2p;
+  const PeerSet ps = peer_set(x);
+  cudaStream_t s = x->stream;
+  int rc;
   GemvArgs lg = {};
   lg.qtype = m->lm_head.qtype;
   lg.qs = m->lm_head.qs();
@@ -780,12 +831,77 @@ int copy_logits(dqmk_context* x, float* logits, const char* api) {
   return DQMK_OK;
 }
 
+// The persistent step kernel (step.cu) runs the embedding and the layers of a
+// single-GPU step as one cooperative launch.  Measured slower than the
+// kernel-per-operation chain under programmatic dependent launch (a grid
+// barrier costs 2.5-3.5 us, one per phase), so it runs only with
+// DQMK_STEP_KERNEL=1 in the environment.  Variant sets without an
+// instantiation, head sizes other than 64 / 128 and tensor parallelism always
+// use the chain.
+bool step_kernel_enabled() {
+  const char* v = std::getenv("DQMK_STEP_KERNEL");
+  return v && v[0] == '1';
+}
+
+int prepare_step_kernel(dqmk_context* x, bool* use) {
+  *use = false;
+  const char* api = "ForwardToken";
+  dqmk_model* m = x->m;
+  const dqmk_model_config& c = m->cfg;
+  if (!step_kernel_enabled() || m->tp.world > 1 || (c.head_dim != 64 && c.head_dim != 128))
+    return DQMK_OK;
+  std::vector<StepPhase> phases;
+  int rc = enqueue_step(x, &phases);
+  if (rc) return rc;
+  size_t smem = 0;
+  std::vector<int> ids;
+  for (const StepPhase& p : phases) {
+    if (p.kind == kPhaseGemv) {
+      ids.push_back(p.variant);
+      smem = std::max(smem, (size_t)p.g.kp * sizeof(float));
+    } else if (p.kind == kPhaseAttn) {
+      smem = std::max(smem, step_attention_smem(c.head_dim, p.chunk_cap, p.at.max_splits));
+    }
+  }
+  if (!step_kernel_variants(ids.data(), (int)ids.size(), x->step_set)) return DQMK_OK;
+  int grid = 0;
+  if (step_kernel_grid(x->step_set, smem, &grid) != cudaSuccess) {
+    cudaGetLastError();
+    return DQMK_OK;  // no resident grid at this shared-memory size: keep the chain
+  }
+  void* p = nullptr;
+  if (!x->step_phases) {
+    if ((rc = dev_alloc(x->allocs, phases.size() * sizeof(StepPhase), &p, api))) return rc;
+    x->step_phases = static_cast<StepPhase*>(p);
+    if ((rc = dev_alloc(x->allocs, 4 * sizeof(unsigned int), &p, api))) return rc;
+    x->step_sync = static_cast<unsigned int*>(p);
+  }
+  DQMK_CUDA_RET(api, cudaMemcpy(x->step_phases, phases.data(), phases.size() * sizeof(StepPhase),
+                                cudaMemcpyHostToDevice));
+  DQMK_CUDA_RET(api, cudaMemset(x->step_sync, 0, 4 * sizeof(unsigned int)));
+  x->step_n = (int)phases.size();
+  x->step_grid = grid;
+  x->step_smem = smem;
+  *use = true;
+  return DQMK_OK;
+}
+
 int ensure_graph(dqmk_context* x) {
   if (x->graph) return DQMK_OK;
   const char* api = "ForwardToken";
+  bool step = false;
+  int rc = prepare_step_kernel(x, &step);
+  if (rc) return rc;
   cudaGraph_t g = nullptr;
   DQMK_CUDA_RET(api, cudaStreamBeginCapture(x->stream, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue_step(x);
+  if (step) {
+    const StepSync sync{x->step_sync, x->step_sync + 1};
+    cudaError_t e = launch_step_kernel(x->step_set, x->step_phases, x->step_n, sync,
+                                       x->step_grid, x->step_smem, x->stream);
+    rc = e == cudaSuccess ? enqueue_lm_head(x) : cuda_fail(api, e);
+  } else {
+    rc = enqueue_step(x);
+  }
   cudaError_t e = cudaStreamEndCapture(x->stream, &g);
   if (rc != DQMK_OK) {
     if (g) cudaGraphDestroy(g);
@@ -814,11 +930,15 @@ void count_token(dqmk_context* x, int pos) {
 
 // After a synchronizing call: a bounded device wait that ran out surfaces as
 // DQMK_ERR_TIMEOUT (the flag is cleared so the context stays usable).
-int check_device_error(const char* api) {
-  unsigned int flags = 0, tp_flags = 0;
+int check_device_error(const char* api, dqmk_context* x = nullptr) {
+  unsigned int flags = 0, tp_flags = 0, step_flags = 0;
   DQMK_CUDA_RET(api, read_device_error(&flags, true));
   DQMK_CUDA_RET(api, read_tp_error(&tp_flags, true));
-  flags |= tp_flags;
+  DQMK_CUDA_RET(api, read_step_error(&step_flags, true));
+  // a barrier wait that ran out can leave arrivals counted: start clean
+  if (step_flags && x && x->step_sync)
+    DQMK_CUDA_RET(api, cudaMemset(x->step_sync, 0, 4 * sizeof(unsigned int)));
+  flags |= tp_flags | step_flags;
   if (flags) return fail(DQMK_ERR_TIMEOUT, std::string(api) + ": a device-side wait timed out");
   return DQMK_OK;
 }
@@ -1198,7 +1318,7 @@ extern "C" int dqmk_forward_token(dqmk_context* x, int token, int pos, float* lo
   if ((rc = launch_token(x, token, pos))) return rc;
   if (logits && (rc = copy_logits(x, logits, api))) return rc;
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
-  return check_device_error(api);
+  return check_device_error(api, x);
 }
 
 extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int* positions, int n,
@@ -1235,7 +1355,7 @@ extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int*
   if (logits && (rc = copy_logits(x, logits, api))) return rc;
   DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
   if ((rc = check_prefill_error(api))) return rc;
-  return check_device_error(api);
+  return check_device_error(api, x);
 }
 
 extern "C" int dqmk_decode_enqueue(dqmk_context* x, int token, int pos, int n_steps) {
@@ -1269,5 +1389,5 @@ extern "C" int dqmk_decode_greedy(dqmk_context* x, int token, int pos, int n_ste
   x->history.push_back(token);
   for (int i = 0; i + 1 < n_steps && tokens_out; ++i) x->history.push_back(tokens_out[i]);
   x->pos = pos + n_steps - 1;
-  return check_device_error(api);
+  return check_device_error(api, x);
 }

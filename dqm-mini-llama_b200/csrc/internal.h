@@ -108,6 +108,8 @@ struct GemvArgs {
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
+// Register-GEMV variant the dispatcher picks for a shape (-1: the TMA form).
+int gemv_variant_id(const GemvArgs& a);
 // Sets kernel attributes of every GEMV / attention instantiation; call
 // outside stream capture.
 cudaError_t gemv_prepare();
@@ -180,6 +182,31 @@ struct AttnArgs {
 int attention_splits(int max_seq, int n_kv_heads);
 size_t attention_partials_floats(int n_heads, int head_dim, int max_splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl);
+int attention_chunk_cap(int max_seq, int max_splits);
+
+// ------------------------------------------------------ persistent decode step
+enum StepPhaseKind : int { kPhaseEmbed = 0, kPhaseGemv = 1, kPhaseAttn = 2 };
+struct StepPhase {
+  int kind;
+  int variant;    // kPhaseGemv: gemv_variant_id of g
+  int chunk_cap;  // kPhaseAttn
+  GemvArgs g;
+  AttnArgs at;
+  EmbedArgs e;
+};
+struct StepSync {
+  unsigned int* count;  // grid-barrier arrivals
+  unsigned int* gen;    // grid-barrier generation
+};
+// The step kernel is instantiated per set of GEMV variants (at most three);
+// true with the set (ordered as instantiated) when one covers ids[0..n).
+bool step_kernel_variants(const int* ids, int n, int out[3]);
+// Dynamic shared memory -> the cooperative grid (resident CTAs x SMs).
+cudaError_t step_kernel_grid(const int set[3], size_t smem, int* grid);
+cudaError_t launch_step_kernel(const int set[3], const StepPhase* phases, int n_phases,
+                               const StepSync& sync, int grid, size_t smem, cudaStream_t s);
+size_t step_attention_smem(int head_dim, int chunk_cap, int max_splits);
+cudaError_t read_step_error(unsigned int* flags, bool clear);
 
 // host-side RoPE table in the reference's float arithmetic (src/ops.cc:18-23,
 // :40-45): entry [p][i] = (cos, sin) of p * 1/theta^(2i/head_dim).
