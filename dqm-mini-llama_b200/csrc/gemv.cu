@@ -675,10 +675,11 @@ cudaError_t read_device_error(unsigned int* flags, bool clear) {
 // Shape -> variant, from a sweep of every variant over the decode shapes
 // (Qwen2-0.5B Q8_0 / Q4_0, Qwen2-7B Q4_0 at TP 1/2/4) with HBM-cold weights.
 // Q8_0 rows up to 64 chunks take a warp per row group; longer rows are split
-// across the whole CTA.  Q4_0 rows (32 values per chunk) up to 128 chunks are
-// fastest with a warp per group of 4 rows walking the row in several passes;
-// longer ones across the CTA.  Very tall weights take 4 rows per group to
-// amortise the shared-memory reads of x.
+// across the whole CTA.  Q4_0 rows (32 values per chunk) up to 32 chunks take
+// a warp per pair of rows in one pass; up to 128 chunks a warp per group of 4
+// rows walking the row in several passes; longer ones are split across the
+// CTA.  Very tall weights take 4 rows per group to amortise the shared-memory
+// reads of x.
 int gemv_variant_id(const GemvArgs& a) {
   if (tma_eligible(a)) return -1;
   const bool wide = a.n_rows >= 32768 && a.epi != kEpiSwiGlu && a.epi != kEpiQkv;
@@ -692,7 +693,7 @@ int gemv_variant_id(const GemvArgs& a) {
     return 5;                                     // <2, 4, 4>
   }
   const bool tall = a.n_rows >= 8192;
-  if (chunks <= 32) return tall ? 8 : 9;          // <Q4_0, 4, 1, 1> / <2, 2, 1>
+  if (chunks <= 32) return wide ? 8 : 14;         // <Q4_0, 4, 1, 1> / <2, 1, 1>
   if (chunks <= 64) return tall ? 10 : 9;         // <4, 2, 1> / <2, 2, 1>
   if (chunks <= 128)
     return (a.n_rows >= 16384 && a.n_rows < 65536) ? 8 : 10;

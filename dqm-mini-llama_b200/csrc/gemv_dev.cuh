@@ -16,7 +16,8 @@
 #define DQMK_GEMV_VARIANT_IDS_WIDE(X) X(6, DQMK_Q80, 4, 2, 4) X(7, DQMK_Q80, 4, 4, 4)
 #define DQMK_GEMV_VARIANT_IDS_Q40(X)                                                        \
   X(8, DQMK_Q40, 4, 1, 1) X(9, DQMK_Q40, 2, 2, 1) X(10, DQMK_Q40, 4, 2, 1)                 \
-  X(11, DQMK_Q40, 2, 2, 4) X(12, DQMK_Q40, 2, 4, 4) X(13, DQMK_Q40, 2, 5, 4)
+  X(11, DQMK_Q40, 2, 2, 4) X(12, DQMK_Q40, 2, 4, 4) X(13, DQMK_Q40, 2, 5, 4)                 \
+  X(14, DQMK_Q40, 2, 1, 1)
 #define DQMK_GEMV_VARIANT_IDS(X) \
   DQMK_GEMV_VARIANT_IDS_Q80(X) DQMK_GEMV_VARIANT_IDS_WIDE(X) DQMK_GEMV_VARIANT_IDS_Q40(X)
 
