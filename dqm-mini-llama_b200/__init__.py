@@ -25,7 +25,7 @@ __all__ = [
     "pack_weight", "gemv_packed", "CudaRmsNormDeviceWeight", "CudaSiluMulDeviceInput",
     "CudaElementwiseAddDeviceInput", "CudaRopeDeviceInput", "CudaEmbeddingLookupDeviceWeight",
     "embedding_lookup_blocks", "argmax", "CudaKvCache", "CudaAttentionDecodeDeviceInput",
-    "Model", "Context", "BLOCK_BYTES",
+    "Model", "Context", "Batch", "BLOCK_BYTES", "linear_batch_packed", "linear_cols_packed",
 ]
 
 BLOCK_BYTES = {Q80: 34, Q40: 18}
@@ -180,6 +180,20 @@ def linear_batch_packed(qtype: int, x, packed, out_features: int, bias=None, res
         y = torch.empty(m, out_features, dtype=torch.float32, device=x.device)
     check(lib().dqmk_linear_batch_packed(qtype, _ptr(x), m, k, _ptr(packed), out_features,
                                          _ptr(bias), _ptr(residual), _ptr(y), _stream(stream)))
+    return y
+
+
+def linear_cols_packed(qtype: int, x, packed, out_features: int, bias=None, residual=None,
+                       y=None, stream=None):
+    """x [cols, in] (device, float32, 1..64 columns, one per sequence) times a
+    packed weight the way a multi-sequence decode step runs it: the quantized
+    blocks stream once and become tensor-core operands on chip."""
+    torch = _torch()
+    m, k = x.shape
+    if y is None:
+        y = torch.empty(m, out_features, dtype=torch.float32, device=x.device)
+    check(lib().dqmk_linear_cols_packed(qtype, _ptr(x), m, k, _ptr(packed), out_features,
+                                        _ptr(bias), _ptr(residual), _ptr(y), _stream(stream)))
     return y
 
 
@@ -456,6 +470,96 @@ class Context:
     def close(self) -> None:
         if getattr(self, "h", None):
             lib().dqmk_context_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """Many sequences decoded together over one model (dqmk_batch): n_slots
+    independent KV caches; each step runs up to 64 (slot, position, token)
+    columns, streaming every weight once per step."""
+
+    MAX_COLS = 64
+
+    def __init__(self, model: Model, n_slots: int, max_seq: Optional[int] = None):
+        self.model = model
+        self.n_slots = int(n_slots)
+        self.max_seq = int(max_seq if max_seq is not None else model.max_seq_len)
+        h = C.c_void_p()
+        check(lib().dqmk_batch_create(model.h, self.n_slots, self.max_seq, C.byref(h)))
+        self.h = h
+        self.vocab = model.cfg["vocab"]
+
+    @staticmethod
+    def _i32(a):
+        return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+    def reset(self) -> None:
+        check(lib().dqmk_batch_reset(self.h))
+
+    def step(self, slots: Optional[Sequence[int]], tokens: Sequence[int],
+             positions: Sequence[int], want_logits: bool = True):
+        """One step over columns (slot, token, position); returns (logits
+        [n, vocab] or None, next greedy tokens [n])."""
+        toks, pos = self._i32(tokens), self._i32(positions)
+        n = toks.size
+        if pos.size != n:
+            raise RuntimeError("DecodeBatch: tokens and positions size mismatch")
+        ip = C.POINTER(C.c_int)
+        sl = None if slots is None else self._i32(slots)
+        logits = np.empty((n, self.vocab), np.float32) if want_logits else None
+        nxt = np.zeros(n, np.int32)
+        check(lib().dqmk_batch_step(
+            self.h, None if sl is None else sl.ctypes.data_as(ip), toks.ctypes.data_as(ip),
+            pos.ctypes.data_as(ip), n,
+            None if logits is None else logits.ctypes.data_as(C.POINTER(C.c_float)),
+            nxt.ctypes.data_as(ip)))
+        return logits, nxt
+
+    def prefill(self, slot: int, tokens: Sequence[int], pos0: int = 0) -> None:
+        """The prompt of one slot, up to 64 positions per step."""
+        toks = self._i32(tokens)
+        for i0 in range(0, toks.size, self.MAX_COLS):
+            chunk = toks[i0:i0 + self.MAX_COLS]
+            self.step([slot] * chunk.size, chunk, np.arange(pos0 + i0, pos0 + i0 + chunk.size),
+                      want_logits=False)
+
+    def decode_greedy(self, tokens: Sequence[int], positions: Sequence[int],
+                      n_steps: int) -> np.ndarray:
+        """Slots 0..n-1 decode together; returns [n_steps, n] tokens."""
+        toks, pos = self._i32(tokens), self._i32(positions)
+        out = np.zeros((n_steps, toks.size), np.int32)
+        ip = C.POINTER(C.c_int)
+        check(lib().dqmk_batch_decode_greedy(self.h, toks.ctypes.data_as(ip),
+                                             pos.ctypes.data_as(ip), toks.size, int(n_steps),
+                                             out.ctypes.data_as(ip)))
+        return out
+
+    def decode_enqueue(self, tokens: Sequence[int], positions: Sequence[int],
+                       n_steps: int) -> None:
+        toks, pos = self._i32(tokens), self._i32(positions)
+        ip = C.POINTER(C.c_int)
+        check(lib().dqmk_batch_decode_enqueue(self.h, toks.ctypes.data_as(ip),
+                                              pos.ctypes.data_as(ip), toks.size, int(n_steps)))
+
+    def history(self, slot: int, pos0: int, count: int) -> np.ndarray:
+        out = np.zeros(count, np.int32)
+        check(lib().dqmk_batch_history(self.h, int(slot), int(pos0), int(count),
+                                       out.ctypes.data_as(C.POINTER(C.c_int))))
+        return out
+
+    @property
+    def stream_handle(self) -> int:
+        return lib().dqmk_batch_stream(self.h)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            lib().dqmk_batch_destroy(self.h)
             self.h = None
 
     def __del__(self):

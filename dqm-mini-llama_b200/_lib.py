@@ -62,6 +62,7 @@ SIGNATURES = {
     "dqmk_pack_weight": ([_i, _vp, _sz, _i, _i, _vp, _vp], _i),
     "dqmk_gemv_packed": ([_i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp], _i),
     "dqmk_linear_batch_packed": ([_i, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp], _i),
+    "dqmk_linear_cols_packed": ([_i, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp], _i),
     "dqmk_device_error": ([_i], _i),
     "dqmk_gemv_packed_withhold_tile": ([_i, _vp, _i, _vp, _i, _vp, _i, _vp], _i),
     "dqmk_rmsnorm": ([_vp, _vp, _i, _f, _vp, _vp], _i),
@@ -96,6 +97,14 @@ SIGNATURES = {
     "dqmk_decode_greedy": ([_vp, _i, _i, _i, _ip], _i),
     "dqmk_decode_enqueue": ([_vp, _i, _i, _i], _i),
     "dqmk_context_stream": ([_vp], _vp),
+    "dqmk_batch_create": ([_vp, _i, _i, C.POINTER(_vp)], _i),
+    "dqmk_batch_destroy": ([_vp], _i),
+    "dqmk_batch_reset": ([_vp], _i),
+    "dqmk_batch_step": ([_vp, _ip, _ip, _ip, _i, _fp, _ip], _i),
+    "dqmk_batch_decode_greedy": ([_vp, _ip, _ip, _i, _i, _ip], _i),
+    "dqmk_batch_decode_enqueue": ([_vp, _ip, _ip, _i, _i], _i),
+    "dqmk_batch_stream": ([_vp], _vp),
+    "dqmk_batch_history": ([_vp, _i, _i, _i, _ip], _i),
 }
 
 _lib = None

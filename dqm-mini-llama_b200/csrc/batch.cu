@@ -1,0 +1,916 @@
+// batch.cu -- decode of many sequences at once on tcgen05 tensor cores (sm_100a).
+//
+// The reference decodes one sequence at a time (ForwardToken,
+// src/forward.cc:667-754), so every weight byte is read once per token.  With
+// C sequences decoded together each weight is read once per step and used C
+// times, and the projection becomes a skinny GEMM Y[c][row] = sum_k W[row][k]
+// X[c][k] that belongs on the tensor cores.  Results stay within fp32
+// summation-order differences of the F32 reference:
+//
+//   * weights stay in HBM as the packed Q8_0 / Q4_0 blocks of the decode GEMV
+//     (the step streams the same bytes a batch-1 step would).  TMA brings a
+//     256-row x 64-value tile of quants into a raw ring; eight dequant warps
+//     turn it into the exact two-term fp16 operand of the prefill GEMM: with
+//     the row scaled by 2^-f (row maximum in [2^14, 2^15)) every value
+//     d * q * 2^-f is exactly hi + lo, hi = fp16(d' q), lo = fma(d', q, -hi)
+//     with d' = fp16(d * 2^-f) (exact), computed in packed half arithmetic and
+//     written in the 128-byte-swizzled K-major layout TMA would produce;
+//   * activations: each column (after its RMSNorm) is split into two fp16
+//     planes by the prefill's split kernel and arrives by TMA;
+//   * tcgen05.mma kind::f16, M = 128 weight rows (two per 256-row tile), N =
+//     the columns rounded up to 16, K = 16: W_hi X_hi + W_hi X_lo + W_lo X_hi
+//     accumulate in TMEM (fp32) over the tile's K range;
+//   * split-K where row tiles are few: each split parks its raw sums, the last
+//     CTA of a row tile (completion ticket) adds them in split order -- the
+//     same order whichever CTA finishes last -- and runs the epilogue;
+//   * epilogues: residual add, SwiGLU of interleaved gate/up rows, QKV bias +
+//     RoPE + KV-cache store at each column's (slot, position), logits with a
+//     per-column argmax key (value, first index) combined by atomicMax.
+// Warp roles: 0 TMA, 1 MMA issue, 2-5 epilogue (one TMEM lane quarter each),
+// 6-13 dequant (one weight row each).  Every hand-off is an mbarrier with a
+// bounded wait; a wait that runs out sets a device flag and the CTA unwinds
+// (its own copies in flight land first, TMEM is freed).  Under programmatic
+// dependent launch the weight copies and their dequantization start before the
+// previous kernel has finished; only activation loads and the epilogue wait.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <string>
+
+#include "attention_dev.cuh"
+#include "batch.h"
+#include "common.cuh"
+#include "dqmk.h"
+#include "internal.h"
+#include "tc_dev.cuh"
+
+namespace dqmk {
+namespace {
+
+constexpr int kTileRows = 256;                                 // weight rows per work item
+constexpr int kHalfRows = 128;                                 // rows per MMA (M)
+constexpr int kChunkK = 64;                                    // K values per stage
+constexpr int kOpStages = 2;
+constexpr int kRawStages = 3;
+constexpr int kWHalfBytes = kHalfRows * kChunkK * 2;           // 16 KB
+constexpr int kWPlaneBytes = 2 * kWHalfBytes;                  // 32 KB: one fp16 plane
+constexpr int kXPlaneBytes = kBatchMaxCols * kChunkK * 2;      // 8 KB
+constexpr int kOpStageBytes = 2 * kWPlaneBytes + 2 * kXPlaneBytes;
+constexpr int kEpiWarps = 4, kDeqWarps = 8;
+constexpr int kFirstEpiWarp = 2, kFirstDeqWarp = kFirstEpiWarp + kEpiWarps;
+constexpr int kThreads = (kFirstDeqWarp + kDeqWarps) * 32;
+constexpr int kAccBufs = 2;
+constexpr uint32_t kTmemCols = kAccBufs * 2 * kBatchMaxCols;  // 256
+static_assert(kDeqWarps * 32 == kTileRows, "one dequant thread per tile row");
+
+__device__ unsigned int g_batch_error;  // bit 0: a bounded wait timed out
+
+template <int QT>
+constexpr int raw_row_bytes() {
+  return QT == DQMK_Q80 ? kChunkK : kChunkK / 2;
+}
+template <int QT>
+constexpr int raw_stage_bytes() {
+  return kTileRows * raw_row_bytes<QT>();
+}
+template <int QT>
+constexpr size_t gemm_smem() {
+  return 1024 + (size_t)kOpStages * kOpStageBytes + (size_t)kRawStages * raw_stage_bytes<QT>();
+}
+
+__device__ __forceinline__ bool wait(uint64_t* b, uint32_t parity, volatile int* abort) {
+  return tc::bar_wait(b, parity, abort, &g_batch_error);
+}
+// Bounded wait that ignores the abort flag: a CTA lets its own copies land
+// before it exits.
+__device__ __forceinline__ void wait_landed(uint64_t* b, uint32_t parity) {
+  volatile int never = 0;
+  tc::bar_wait(b, parity, &never, &g_batch_error);
+}
+
+// Work item w -> (row tile, K split, chunk range).  The splits of one tile
+// are consecutive items, so they run at the same time.
+struct Item {
+  int tile, z, c0, c1;
+};
+__device__ __forceinline__ Item item_of(const BatchGemm& p, int w) {
+  Item t;
+  t.tile = w / p.plan.splits;
+  t.z = w % p.plan.splits;
+  const int nb = p.kp / 32;
+  const int kb0 = t.z * p.plan.kb_per;
+  const int kb1 = min(nb, kb0 + p.plan.kb_per);
+  t.c0 = kb0 / 2;
+  t.c1 = (kb1 + 1) / 2;
+  return t;
+}
+
+// The CTA's chunks in order (items blockIdx.x, + gridDim.x, ...).
+struct Walk {
+  int w, c, total;
+  Item t;
+  bool valid;
+  __device__ __forceinline__ void begin(const BatchGemm& p, int n_items) {
+    total = n_items;
+    w = blockIdx.x;
+    valid = w < total;
+    if (valid) {
+      t = item_of(p, w);
+      c = t.c0;
+    }
+  }
+  __device__ __forceinline__ void next(const BatchGemm& p) {
+    if (++c < t.c1) return;
+    w += gridDim.x;
+    valid = w < total;
+    if (valid) {
+      t = item_of(p, w);
+      c = t.c0;
+    }
+  }
+};
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Two exact fp16 terms of t * s (t a small integer held exactly in fp16, s
+// an fp16 power-of-two-scaled block scale): hi rounded, lo the exact rest.
+__device__ __forceinline__ void two_term(__half2 t, __half2 s, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __hmul2_rn(t, s);
+  const __half2 l = __hfma2(t, s, __hneg2(h));
+  hi = h2u(h);
+  lo = h2u(l);
+}
+
+// Stores 16-byte chunk j (8 values) of row rr of a 128-row half tile in the
+// 128-byte swizzle (chunk j of row rr lands at chunk j ^ (rr & 7)).
+__device__ __forceinline__ void put_chunk(unsigned char* half_tile, int rr, int j, uint4 v) {
+  *reinterpret_cast<uint4*>(half_tile + rr * 128 + ((j ^ (rr & 7)) << 4)) = v;
+}
+
+// Q4_0 block (16 bytes: byte i holds value i in its low nibble and value
+// i + 16 in its high nibble, src/quant.cc:160-175) -> 32 values as hi / lo
+// chunks cb .. cb+3 of the row.
+__device__ __forceinline__ void dequant_q4_block(uint4 q, __half2 s, unsigned char* whi,
+                                                 unsigned char* wlo, int rr, int cb) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  const __half2 off = __half2half2(__ushort_as_half(0x6408));  // 1032 = 1024 + 8
+  uint32_t h[16], l[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo4 = w[i] & 0x0F0F0F0Fu, hi4 = (w[i] >> 4) & 0x0F0F0F0Fu;
+    // values 4i, 4i+1 | 4i+2, 4i+3 (low nibbles) and 16+4i .. 16+4i+3 (high)
+    two_term(__hsub2(u2h(prmt(lo4, 0x64646464u, 0x4140u)), off), s, h[2 * i], l[2 * i]);
+    two_term(__hsub2(u2h(prmt(lo4, 0x64646464u, 0x4342u)), off), s, h[2 * i + 1], l[2 * i + 1]);
+    two_term(__hsub2(u2h(prmt(hi4, 0x64646464u, 0x4140u)), off), s, h[8 + 2 * i], l[8 + 2 * i]);
+    two_term(__hsub2(u2h(prmt(hi4, 0x64646464u, 0x4342u)), off), s, h[9 + 2 * i], l[9 + 2 * i]);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    put_chunk(whi, rr, cb + j, make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]));
+    put_chunk(wlo, rr, cb + j, make_uint4(l[4 * j], l[4 * j + 1], l[4 * j + 2], l[4 * j + 3]));
+  }
+}
+
+// 16 Q8_0 values (int8, in order) -> hi / lo chunks cb, cb + 1 of the row.
+__device__ __forceinline__ void dequant_q8_16(uint4 q, __half2 s, unsigned char* whi,
+                                              unsigned char* wlo, int rr, int cb) {
+  const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
+                         q.w ^ 0x80808080u};
+  const __half2 off = __half2half2(__ushort_as_half(0x6480));  // 1152 = 1024 + 128
+  uint32_t h[8], l[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    two_term(__hsub2(u2h(prmt(w[i], 0x64646464u, 0x4140u)), off), s, h[2 * i], l[2 * i]);
+    two_term(__hsub2(u2h(prmt(w[i], 0x64646464u, 0x4342u)), off), s, h[2 * i + 1], l[2 * i + 1]);
+  }
+  put_chunk(whi, rr, cb, make_uint4(h[0], h[1], h[2], h[3]));
+  put_chunk(whi, rr, cb + 1, make_uint4(h[4], h[5], h[6], h[7]));
+  put_chunk(wlo, rr, cb, make_uint4(l[0], l[1], l[2], l[3]));
+  put_chunk(wlo, rr, cb + 1, make_uint4(l[4], l[5], l[6], l[7]));
+}
+
+// fp16 block scale d times the row's 2^-f, as a broadcast half2 (exact: a
+// power-of-two multiple of an fp16 value, at most 2^15 / |q|max).
+__device__ __forceinline__ __half2 block_scale(uint32_t d_bits, float inv_cs) {
+  const float v = __fmul_rn(__half2float(__ushort_as_half((unsigned short)d_bits)), inv_cs);
+  return __half2half2(__float2half_rn(v));
+}
+
+// ------------------------------------------------------------------ epilogue
+// Per-column data of the step, staged once per CTA.
+struct ColInfo {
+  float rs[kBatchMaxCols];
+  int pos[kBatchMaxCols];
+  int slot[kBatchMaxCols];
+};
+
+// Row `row` (this thread's TMEM lane) and columns cb .. cb+31 of finished
+// sums v (raw accumulator values): scale by rs[c] * cs[row] (exact powers of
+// two), then the epilogue.  Every lane of the warp calls this together (the
+// paired epilogues exchange values with the neighbouring lane).
+__device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, int row, int cb,
+                                       float (&v)[32]) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const bool ok = row < p.n;
+  const float c = ok ? __ldg(p.cs + row) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], ci.rs[(cb + j) & 63]), c);
+  const int ncol = min(32, p.cols - cb);  // valid columns of this group
+  if (p.epi == kEpiStore) {
+    if (!ok) return;
+    const float b = p.bias ? __ldg(p.bias + row) : 0.0f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {  // 8 columns at a time: loads first, then stores
+      float r[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = 8 * g + u;
+        r[u] = (p.residual && j < ncol) ? p.residual[(size_t)(cb + j) * p.ldy + row] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = 8 * g + u;
+        if (j < ncol) {
+          float x = p.bias ? __fadd_rn(v[j], b) : v[j];
+          if (p.residual) x = __fadd_rn(r[u], x);
+          p.y[(size_t)(cb + j) * p.ldy + row] = x;
+        }
+      }
+    }
+  } else if (p.epi == kEpiSwiGlu) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float u = __shfl_down_sync(full, v[j], 1);
+      if (ok && !(lane & 1) && j < ncol) {
+        const float g = v[j];
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+        p.y[(size_t)(cb + j) * p.ldy + row / 2] = __fmul_rn(__fmul_rn(g, sig), u);
+      }
+    }
+  } else if (p.epi == kEpiQkv) {
+    const float b = (ok && p.bias) ? __ldg(p.bias + row) : 0.0f;
+    const int half = p.head_dim / 2;
+    const int q_pairs = p.n_heads * half, kv_pairs = p.n_kv_heads * half;
+    const int pp = row / 2;
+    const bool is_q = pp < q_pairs, is_k = !is_q && pp < q_pairs + kv_pairs;
+    const bool rotate = is_q || is_k;
+    const int seg = is_q ? pp : (is_k ? pp - q_pairs : pp - q_pairs - kv_pairs);
+    const int hh = seg / half, i = seg % half;
+    int o0, o1;
+    if (rotate && p.neox) {
+      o0 = hh * p.head_dim + i;
+      o1 = o0 + half;
+    } else {
+      o0 = hh * p.head_dim + 2 * i;
+      o1 = o0 + 1;
+    }
+    const int kvd = p.n_kv_heads * p.head_dim;
+    const bool writer = ok && !(lane & 1);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float a[8], bb[8];
+      float2 rc[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = 8 * g + u;
+        a[u] = p.bias ? __fadd_rn(v[j], b) : v[j];
+        bb[u] = __shfl_down_sync(full, a[u], 1);
+        rc[u] = (writer && rotate && j < ncol)
+                    ? __ldg(p.rope_cs + (size_t)ci.pos[cb + j] * half + i)
+                    : make_float2(1.0f, 0.0f);
+      }
+      if (!writer) continue;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = 8 * g + u;
+        if (j >= ncol) continue;
+        float x0 = a[u], x1 = bb[u];
+        if (rotate) {
+          const float2 cs = rc[u];
+          if (p.neox) {
+            x0 = __fmaf_rn(a[u], cs.x, -__fmul_rn(bb[u], cs.y));
+            x1 = __fmaf_rn(a[u], cs.y, __fmul_rn(bb[u], cs.x));
+          } else {
+            x0 = __fsub_rn(__fmul_rn(a[u], cs.x), __fmul_rn(bb[u], cs.y));
+            x1 = __fadd_rn(__fmul_rn(a[u], cs.y), __fmul_rn(bb[u], cs.x));
+          }
+        }
+        const int col = cb + j;
+        float* dst;
+        if (is_q) {
+          dst = p.q_out + (size_t)col * p.ldq;
+        } else {
+          float* cache = is_k ? p.k_cache : p.v_cache;
+          dst = cache + (size_t)ci.slot[col] * p.slot_stride +
+                ((size_t)p.layer * p.max_seq + ci.pos[col]) * kvd;
+        }
+        dst[o0] = x0;
+        dst[o1] = x1;
+      }
+    }
+  } else {  // kEpiLogits
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (ok && p.y && j < ncol) p.y[(size_t)(cb + j) * p.ldy + row] = v[j];
+      unsigned long long k = ok ? argmax_key(v[j], (uint32_t)(row + p.row_offset)) : 0ull;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(full, k, o);
+        k = other > k ? other : k;
+      }
+      if (lane == 0 && j < ncol) atomicMax(p.keys + cb + j, k);
+    }
+  }
+}
+
+// ------------------------------------------------------------------- kernel
+template <int QT>
+__global__ void __launch_bounds__(kThreads, 1)
+    batch_gemm_kernel(const __grid_constant__ CUtensorMap map_w,
+                      const __grid_constant__ CUtensorMap map_xhi,
+                      const __grid_constant__ CUtensorMap map_xlo, const BatchGemm p) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+  __shared__ __align__(8) uint64_t op_full[kOpStages], x_full[kOpStages], op_empty[kOpStages];
+  __shared__ __align__(8) uint64_t acc_full[kAccBufs], acc_empty[kAccBufs], mma_done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+  __shared__ ColInfo ci;
+
+  constexpr int RB = raw_row_bytes<QT>();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (p.n + kTileRows - 1) / kTileRows;
+  const int n_items = n_tiles * p.plan.splits;
+  const int n_mma = (p.cols + 15) / 16 * 16;
+  unsigned char* ops = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  unsigned char* raws = ops + (size_t)kOpStages * kOpStageBytes;
+
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRawStages; ++s) {
+      tc::bar_init(&raw_full[s], 1);
+      tc::bar_init(&raw_empty[s], kDeqWarps);
+    }
+    for (int s = 0; s < kOpStages; ++s) {
+      tc::bar_init(&op_full[s], kDeqWarps);
+      tc::bar_init(&x_full[s], 1);
+      tc::bar_init(&op_empty[s], 1);
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      tc::bar_init(&acc_full[b], 1);
+      tc::bar_init(&acc_empty[b], kEpiWarps);
+    }
+    tc::bar_init(&mma_done, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tc::tma_prefetch_desc(&map_w);
+    tc::tma_prefetch_desc(&map_xhi);
+    tc::tma_prefetch_desc(&map_xlo);
+  }
+  if (warp == 1) tc::tmem_alloc(&tmem_slot, kTmemCols);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ------------------------------------------- TMA producer
+      Walk rw, xw;
+      rw.begin(p, n_items);
+      xw.begin(p, n_items);
+      int gr = 0, gx = 0;
+      auto issue_raw = [&]() {
+        const int st = gr % kRawStages;
+        tc::bar_expect_tx(&raw_full[st], (uint32_t)raw_stage_bytes<QT>());
+        tc::tma_load_2d(raws + (size_t)st * raw_stage_bytes<QT>(), &map_w, rw.c * RB,
+                        rw.t.tile * kTileRows, &raw_full[st]);
+        rw.next(p);
+        ++gr;
+      };
+      // weight tiles do not depend on the previous kernel: start them first
+      while (rw.valid && gr < kRawStages) issue_raw();
+      pdl_wait();
+      while (xw.valid && !abort_flag) {
+        bool ok = true;
+        while (rw.valid && gr < gx + kRawStages) {
+          if (!wait(&raw_empty[gr % kRawStages], (uint32_t)((gr / kRawStages - 1) & 1),
+                    &abort_flag)) {
+            ok = false;
+            break;
+          }
+          issue_raw();
+        }
+        if (!ok) break;
+        const int os = gx % kOpStages;
+        if (gx >= kOpStages &&
+            !wait(&op_empty[os], (uint32_t)((gx / kOpStages - 1) & 1), &abort_flag))
+          break;
+        unsigned char* st = ops + (size_t)os * kOpStageBytes;
+        tc::bar_expect_tx(&x_full[os], 2u * kXPlaneBytes);
+        tc::tma_load_2d(st + 2 * kWPlaneBytes, &map_xhi, xw.c * kChunkK, 0, &x_full[os]);
+        tc::tma_load_2d(st + 2 * kWPlaneBytes + kXPlaneBytes, &map_xlo, xw.c * kChunkK, 0,
+                        &x_full[os]);
+        xw.next(p);
+        ++gx;
+      }
+      if (abort_flag) {  // let this thread's copies in flight land before exit
+        for (int g = gr - kRawStages < 0 ? 0 : gr - kRawStages; g < gr; ++g)
+          wait_landed(&raw_full[g % kRawStages], (uint32_t)((g / kRawStages) & 1));
+        for (int g = gx - kOpStages < 0 ? 0 : gx - kOpStages; g < gx; ++g)
+          wait_landed(&x_full[g % kOpStages], (uint32_t)((g / kOpStages) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ----------------------------------------------- MMA issue
+      const uint32_t idesc = tc::idesc_f16(kHalfRows, n_mma);
+      int g = 0, tcnt = 0;
+      for (int w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x, ++tcnt) {
+        const Item it = item_of(p, w);
+        const int buf = tcnt % kAccBufs;
+        if (tcnt >= kAccBufs &&
+            !wait(&acc_empty[buf], (uint32_t)((tcnt / kAccBufs - 1) & 1), &abort_flag))
+          break;
+        tc::tc_fence_after();
+        bool ok = true;
+        for (int c = it.c0; c < it.c1; ++c, ++g) {
+          const int os = g % kOpStages;
+          const uint32_t par = (uint32_t)((g / kOpStages) & 1);
+          if (!wait(&op_full[os], par, &abort_flag) || !wait(&x_full[os], par, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc::tc_fence_after();
+          const uint32_t whi = tc::su32(ops + (size_t)os * kOpStageBytes);
+          const uint32_t wlo = whi + kWPlaneBytes, xhi = whi + 2 * kWPlaneBytes,
+                         xlo = xhi + kXPlaneBytes;
+#pragma unroll
+          for (int k = 0; k < kChunkK / 16; ++k) {
+            const uint64_t bhi = tc::smem_desc(xhi + 32 * k), blo = tc::smem_desc(xlo + 32 * k);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t d = tmem + (uint32_t)(buf * 2 * kBatchMaxCols + h * kBatchMaxCols);
+              const uint64_t ahi = tc::smem_desc(whi + h * kWHalfBytes + 32 * k);
+              const uint64_t alo = tc::smem_desc(wlo + h * kWHalfBytes + 32 * k);
+              tc::mma_f16(d, ahi, bhi, idesc, (c > it.c0 || k > 0) ? 1u : 0u);
+              tc::mma_f16(d, ahi, blo, idesc, 1u);
+              tc::mma_f16(d, alo, bhi, idesc, 1u);
+            }
+          }
+          tc::mma_commit(&op_empty[os]);  // the stage is free once these MMAs finish
+        }
+        if (!ok) break;
+        tc::mma_commit(&acc_full[buf]);
+      }
+      // every MMA this thread issued has finished before TMEM is freed
+      tc::mma_commit(&mma_done);
+      wait_landed(&mma_done, 0u);
+    }
+  } else if (warp >= kFirstDeqWarp) {  // ------------------------------- dequant
+    const int t = threadIdx.x - kFirstDeqWarp * 32;  // tile row
+    const int half = t / kHalfRows, rr = t % kHalfRows;
+    const int nb = p.kp / 32;
+    int g = 0;
+    for (int w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x) {
+      const Item it = item_of(p, w);
+      const int row = it.tile * kTileRows + t;
+      const bool ok = row < p.n;
+      const float inv = ok ? __frcp_rn(__ldg(p.cs + row)) : 0.0f;
+      const uint16_t* drow = p.d + (size_t)(ok ? row : 0) * nb;
+      auto scales = [&](int c) -> uint32_t {  // blocks 2c, 2c+1 of this row
+        if (!ok || c >= it.c1) return 0u;
+        const uint32_t a = __ldg(drow + 2 * c);
+        const uint32_t b = 2 * c + 1 < nb ? (uint32_t)__ldg(drow + 2 * c + 1) : 0u;
+        return a | (b << 16);
+      };
+      uint32_t sc0 = scales(it.c0), sc1 = scales(it.c0 + 1), sc2 = scales(it.c0 + 2),
+               sc3 = scales(it.c0 + 3);
+      bool okw = true;
+      for (int c = it.c0; c < it.c1; ++c, ++g) {
+        const uint32_t s2 = sc0;
+        sc0 = sc1;
+        sc1 = sc2;
+        sc2 = sc3;
+        sc3 = scales(c + 4);
+        const int rs_ = g % kRawStages, os = g % kOpStages;
+        if (!wait(&raw_full[rs_], (uint32_t)((g / kRawStages) & 1), &abort_flag) ||
+            (g >= kOpStages &&
+             !wait(&op_empty[os], (uint32_t)((g / kOpStages - 1) & 1), &abort_flag))) {
+          okw = false;
+          break;
+        }
+        const unsigned char* src = raws + (size_t)rs_ * raw_stage_bytes<QT>() + (size_t)t * RB;
+        unsigned char* st = ops + (size_t)os * kOpStageBytes;
+        unsigned char* whi = st + half * kWHalfBytes;
+        unsigned char* wlo = st + kWPlaneBytes + half * kWHalfBytes;
+        const __half2 s_a = block_scale(s2 & 0xffffu, inv), s_b = block_scale(s2 >> 16, inv);
+        if constexpr (QT == DQMK_Q80) {
+          const uint4* q = reinterpret_cast<const uint4*>(src);
+          const uint4 q0 = q[0], q1 = q[1], q2 = q[2], q3 = q[3];
+          dequant_q8_16(q0, s_a, whi, wlo, rr, 0);
+          dequant_q8_16(q1, s_a, whi, wlo, rr, 2);
+          dequant_q8_16(q2, s_b, whi, wlo, rr, 4);
+          dequant_q8_16(q3, s_b, whi, wlo, rr, 6);
+        } else {
+          const uint4* q = reinterpret_cast<const uint4*>(src);
+          const uint4 q0 = q[0], q1 = q[1];
+          dequant_q4_block(q0, s_a, whi, wlo, rr, 0);
+          dequant_q4_block(q1, s_b, whi, wlo, rr, 4);
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tc::bar_arrive(&raw_empty[rs_]);
+          tc::bar_arrive(&op_full[os]);
+        }
+      }
+      if (!okw) break;
+    }
+  } else {  // ---------------------------------------- epilogue warps 2..5
+    const int et = threadIdx.x - kFirstEpiWarp * 32;
+    const int quarter = warp & 3;  // TMEM lanes 32 * quarter ..
+    pdl_wait();
+    for (int c = et; c < kBatchMaxCols; c += kEpiWarps * 32) {
+      const bool v = c < p.cols;
+      ci.rs[c] = v ? p.rs[c] : 0.0f;
+      ci.pos[c] = v && p.col_pos ? p.col_pos[c] : 0;
+      ci.slot[c] = v && p.col_slot ? p.col_slot[c] : 0;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+    int tcnt = 0;
+    for (int w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x, ++tcnt) {
+      const Item it = item_of(p, w);
+      const int buf = tcnt % kAccBufs;
+      if (!wait(&acc_full[buf], (uint32_t)((tcnt / kAccBufs) & 1), &abort_flag)) break;
+      tc::tc_fence_after();
+      const bool split = p.plan.splits > 1;
+      for (int h = 0; h < 2; ++h) {
+        const int row = it.tile * kTileRows + h * kHalfRows + 32 * quarter + lane;
+        for (int cb = 0; cb < n_mma; cb += 32) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + ((uint32_t)(32 * quarter) << 16) +
+                            (uint32_t)(buf * 2 * kBatchMaxCols + h * kBatchMaxCols + cb),
+                        r);
+          tc::tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (split) {
+            if (row < p.n) {
+              float4* dst = reinterpret_cast<float4*>(
+                  p.partial + ((size_t)it.z * p.n + row) * kBatchMaxCols + cb);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                __stcg(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+            }
+          } else {
+            finish(p, ci, row, cb, v);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::bar_arrive(&acc_empty[buf]);
+      if (split) {
+        // this warp's rows of the tile are complete in every split once the
+        // quarter's ticket reaches splits; the last arrival adds them in
+        // split order (no cross-warp barrier after a bounded wait)
+        __threadfence();
+        unsigned int done = 0;
+        unsigned int* ticket = p.tickets + (size_t)it.tile * 4 + quarter;
+        if (lane == 0) done = atomicAdd(ticket, 1u);
+        done = __shfl_sync(0xffffffffu, done, 0);
+        if (done == (unsigned int)p.plan.splits - 1) {
+          __threadfence();
+          for (int h = 0; h < 2; ++h) {
+            const int row = it.tile * kTileRows + h * kHalfRows + 32 * quarter + lane;
+            const int rowc = row < p.n ? row : p.n - 1;
+            for (int cb = 0; cb < n_mma; cb += 32) {
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+              for (int z = 0; z < p.plan.splits; ++z) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    p.partial + ((size_t)z * p.n + rowc) * kBatchMaxCols + cb);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 a = __ldcg(src + j);
+                  v[4 * j] = __fadd_rn(v[4 * j], a.x);
+                  v[4 * j + 1] = __fadd_rn(v[4 * j + 1], a.y);
+                  v[4 * j + 2] = __fadd_rn(v[4 * j + 2], a.z);
+                  v[4 * j + 3] = __fadd_rn(v[4 * j + 3], a.w);
+                }
+              }
+              finish(p, ci, row, cb, v);
+            }
+          }
+          if (lane == 0) *ticket = 0u;
+        }
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tc::tmem_free(tmem, kTmemCols);
+}
+
+// ------------------------------------------------------------- side kernels
+// One CTA per weight row: cs[row] = 2^f with the row's max |d q| 2^-f in
+// [2^14, 2^15) -- the scaling of the prefill's two-term weight planes.
+__global__ void __launch_bounds__(256) row_scales_kernel(int qtype, const uint8_t* __restrict__ qs,
+                                                         const uint16_t* __restrict__ d, int kp,
+                                                         float* __restrict__ cs) {
+  __shared__ float red[8];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int nb = kp / 32;
+  const uint16_t* dr = d + (size_t)row * nb;
+  const uint8_t* qr = qs + (size_t)row * (qtype == DQMK_Q80 ? kp : kp / 2);
+  float mx = 0.0f;
+  for (int e = tid; e < kp; e += 256) {
+    int q;
+    if (qtype == DQMK_Q80) {
+      q = (int)(int8_t)qr[e];
+    } else {
+      const int j = e & 31;
+      const uint8_t byte = qr[(e >> 5) * 16 + (j & 15)];
+      q = (int)(j < 16 ? (byte & 0x0f) : (byte >> 4)) - 8;
+    }
+    mx = fmaxf(mx, fabsf(__fmul_rn(h2f(dr[e >> 5]), (float)q)));
+  }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = red[0];
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+    int ex = 0;
+    if (m > 0.0f && m <= 3.0e38f) {
+      int fe;
+      frexpf(m, &fe);  // m in [2^(fe-1), 2^fe)
+      ex = min(max(fe - 15, -120), 120);
+    }
+    cs[row] = ldexpf(1.0f, ex);
+  }
+}
+
+// Decode attention of column blockIdx.z: the single-sequence body over the
+// column's slot cache and position.
+template <int HD>
+__global__ void __launch_bounds__(256) attention_cols_kernel(const BatchAttn b, int chunk_cap) {
+  extern __shared__ float sm[];
+  pdl_trigger();
+  pdl_wait();
+  const int c = blockIdx.z;
+  const size_t so = (size_t)__ldg(b.col_slot + c) * b.slot_stride;
+  AttnArgs a = {};
+  a.q = b.q + (size_t)c * b.ldq;
+  a.out = b.out + (size_t)c * b.ldq;
+  a.keys = b.keys + so;
+  a.values = b.values + so;
+  a.max_seq = b.max_seq;
+  a.n_kv_heads = b.n_kv_heads;
+  a.head_dim = HD;
+  a.layer = b.layer;
+  a.n_heads = b.n_heads;
+  a.pos_dev = b.col_pos + c;
+  a.partials = b.partials + (size_t)c * b.n_heads * b.max_splits * at::part_stride(HD);
+  a.tickets = b.tickets + (size_t)c * b.n_kv_heads;
+  a.max_splits = b.max_splits;
+  at::attention_hd_body<HD, 256>(a, chunk_cap, blockIdx.x, blockIdx.y, gridDim.y, sm);
+}
+
+__global__ void cols_advance_kernel(unsigned long long* __restrict__ keys, int cols,
+                                    const int* __restrict__ col_slot, int* __restrict__ col_token,
+                                    int* __restrict__ col_pos, int* __restrict__ history,
+                                    int max_seq) {
+  pdl_trigger();
+  pdl_wait();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const unsigned long long key = keys[c];
+  const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+  const int p = col_pos[c];
+  if (history && p >= 0 && p < max_seq) history[(size_t)col_slot[c] * max_seq + p] = idx;
+  col_token[c] = idx;
+  col_pos[c] = p + 1;
+  keys[c] = 0ull;
+}
+
+}  // namespace
+
+// --------------------------------------------------------------------- host
+int batch_row_tiles(int n) { return (n + kTileRows - 1) / kTileRows; }
+
+// K splits so that row tiles x splits covers the SMs, at least 4 scale
+// blocks (two stages) per split, an even block count per split.
+GemmPlan plan_batch_gemm(int n, int kp) {
+  const int nb = kp / 32, tiles = batch_row_tiles(n), sms = sm_count();
+  int splits = 1;
+  if (tiles < sms) splits = std::max(1, std::min(sms / std::max(tiles, 1), nb / 4));
+  int kb_per = (nb + splits - 1) / splits;
+  kb_per = (kb_per + 1) / 2 * 2;
+  splits = (nb + kb_per - 1) / kb_per;
+  return GemmPlan{splits, kb_per};
+}
+
+size_t batch_partial_floats(int n, int kp) {
+  const GemmPlan pl = plan_batch_gemm(n, kp);
+  return pl.splits > 1 ? (size_t)pl.splits * n * kBatchMaxCols : 0;
+}
+
+int make_quant_map(CUtensorMap* map, int qtype, const uint8_t* qs, int rows, int kp) {
+  const uint64_t rb = qtype == DQMK_Q80 ? (uint64_t)kp : (uint64_t)kp / 2;
+  const uint32_t box = qtype == DQMK_Q80 ? kChunkK : kChunkK / 2;
+  return make_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, qs, rb, (uint64_t)rows, rb, box,
+                     kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+int make_cols_map(CUtensorMap* map, const uint16_t* plane, int kp) {
+  return make_f16_tile_map(map, plane, kBatchMaxCols, kp, kBatchMaxCols);
+}
+
+cudaError_t batch_prepare() {
+  static bool done = false;
+  if (done) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(batch_gemm_kernel<DQMK_Q80>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gemm_smem<DQMK_Q80>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(batch_gemm_kernel<DQMK_Q40>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)gemm_smem<DQMK_Q40>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_cols_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_cols_kernel<128>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess) done = true;
+  return e;
+}
+
+cudaError_t launch_batch_gemm(const CUtensorMap& wq, const CUtensorMap& xhi,
+                              const CUtensorMap& xlo, const BatchGemm& p, cudaStream_t s,
+                              bool pdl) {
+  if (p.cols < 1 || p.cols > kBatchMaxCols || p.n < 1 || p.kp < 32 || p.kp % 32 != 0 ||
+      p.plan.splits < 1 || p.plan.kb_per < 2 || p.plan.kb_per % 2 != 0 || !p.rs || !p.cs ||
+      !p.d || (p.plan.splits > 1 && (!p.partial || !p.tickets)))
+    return cudaErrorInvalidValue;
+  if ((p.epi == kEpiSwiGlu || p.epi == kEpiQkv) && (p.n % 2 != 0)) return cudaErrorInvalidValue;
+  if (p.epi == kEpiLogits && !p.keys) return cudaErrorInvalidValue;
+  if (p.epi != kEpiLogits && !p.y && p.epi != kEpiQkv) return cudaErrorInvalidValue;
+  cudaError_t e = batch_prepare();
+  if (e != cudaSuccess) return e;
+  const int items = batch_row_tiles(p.n) * p.plan.splits;
+  const dim3 grid(std::min(items, sm_count()));
+  if (p.qtype == DQMK_Q80)
+    return launch(batch_gemm_kernel<DQMK_Q80>, grid, dim3(kThreads), gemm_smem<DQMK_Q80>(), s,
+                  pdl, wq, xhi, xlo, p);
+  if (p.qtype == DQMK_Q40)
+    return launch(batch_gemm_kernel<DQMK_Q40>, grid, dim3(kThreads), gemm_smem<DQMK_Q40>(), s,
+                  pdl, wq, xhi, xlo, p);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_weight_row_scales(int qtype, const uint8_t* qs, const uint16_t* d, int rows,
+                                     int kp, float* cs, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  row_scales_kernel<<<rows, 256, 0, s>>>(qtype, qs, d, kp, cs);
+  return cudaGetLastError();
+}
+
+// About two CTAs per SM over all (column, KV head) pairs, each split at
+// least kMinChunk positions long.
+int batch_attention_splits(int cols, int n_kv_heads, int max_seq) {
+  const int pairs = std::max(1, cols * n_kv_heads);
+  int sp = (2 * sm_count() + pairs - 1) / pairs;
+  const int by_len = (max_seq + at::kMinChunk - 1) / at::kMinChunk;
+  sp = std::min(sp, by_len);
+  return std::max(1, sp);
+}
+
+size_t batch_attention_partials_floats(int cols, int n_heads, int head_dim, int max_splits) {
+  return (size_t)cols * n_heads * max_splits * at::part_stride(head_dim);
+}
+
+cudaError_t launch_attention_cols(const BatchAttn& a, cudaStream_t s, bool pdl) {
+  if (a.cols < 1 || a.n_kv_heads <= 0 || a.n_heads % a.n_kv_heads != 0 ||
+      a.n_heads / a.n_kv_heads > at::kMaxGroup || a.ldq % 4 != 0 ||
+      ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.out)) & 15u))
+    return cudaErrorInvalidValue;
+  cudaError_t e = batch_prepare();
+  if (e != cudaSuccess) return e;
+  const int cap = attention_chunk_cap(a.max_seq, a.max_splits);
+  const size_t smem = at::smem_bytes_hd(a.head_dim, cap, a.max_splits, 256);
+  const dim3 grid(a.n_kv_heads, a.max_splits, a.cols);
+  if (a.head_dim == 64)
+    return launch(attention_cols_kernel<64>, grid, dim3(256), smem, s, pdl, a, cap);
+  if (a.head_dim == 128)
+    return launch(attention_cols_kernel<128>, grid, dim3(256), smem, s, pdl, a, cap);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_cols_advance(unsigned long long* keys, int cols, const int* col_slot,
+                                int* col_token, int* col_pos, int* history, int max_seq,
+                                cudaStream_t s, bool pdl) {
+  return launch(cols_advance_kernel, dim3(1), dim3(kBatchMaxCols), 0, s, pdl, keys, cols, col_slot,
+                col_token, col_pos, history, max_seq);
+}
+
+cudaError_t read_batch_error(unsigned int* flags, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_batch_error, sizeof(unsigned int));
+  if (e == cudaSuccess && clear && *flags) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_batch_error, &zero, sizeof(unsigned int));
+  }
+  return e;
+}
+
+}  // namespace dqmk
+
+// ------------------------------------------------------------------ C ABI
+using namespace dqmk;
+
+extern "C" int dqmk_linear_cols_packed(int qtype, const float* x, int cols, int in_features,
+                                       const void* packed, int out_features, const float* bias,
+                                       const float* residual, float* y, void* stream) {
+  const char* api = qtype == DQMK_Q40 ? "CudaQ40Linear" : "CudaQ80Linear";
+  if (qtype != DQMK_Q80 && qtype != DQMK_Q40)
+    return fail(DQMK_ERR_UNSUPPORTED, "dqmk_linear_cols_packed: unsupported quant type");
+  if (cols < 1 || cols > kBatchMaxCols || in_features <= 0 || out_features <= 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid shape (1 to 64 columns)");
+  if (!x || !packed || !y) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  if (reinterpret_cast<uintptr_t>(packed) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": packed weight must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int kp = (in_features + 31) / 32 * 32;
+  const uint8_t* qs = static_cast<const uint8_t*>(packed);
+  const size_t qbytes = (size_t)out_features * (qtype == DQMK_Q80 ? kp : kp / 2);
+  const uint16_t* d = reinterpret_cast<const uint16_t*>(qs + qbytes);
+  const GemmPlan plan = plan_batch_gemm(out_features, kp);
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t b_act = up((size_t)kBatchMaxCols * kp * 2), b_rs = up(kBatchMaxCols * 4);
+  const size_t b_cs = up((size_t)out_features * 4);
+  const size_t b_part = up(batch_partial_floats(out_features, kp) * 4);
+  const size_t b_tk = up((size_t)batch_row_tiles(out_features) * 4 * 4);
+  unsigned char* scratch = nullptr;
+  const size_t total = 2 * b_act + b_rs + b_cs + b_part + b_tk + 256;
+  DQMK_CUDA_RET(api, cudaMallocAsync(reinterpret_cast<void**>(&scratch), total, st));
+  unsigned char* cur = scratch;
+  auto take = [&](size_t b) {
+    unsigned char* r = cur;
+    cur += b;
+    return r;
+  };
+  uint16_t* hi = reinterpret_cast<uint16_t*>(take(b_act));
+  uint16_t* lo = reinterpret_cast<uint16_t*>(take(b_act));
+  float* rs = reinterpret_cast<float*>(take(b_rs));
+  float* cs = reinterpret_cast<float*>(take(b_cs));
+  float* part = reinterpret_cast<float*>(take(b_part));
+  unsigned int* tickets = reinterpret_cast<unsigned int*>(take(b_tk));
+  int rc = DQMK_OK;
+  cudaError_t e = cudaSuccess;
+  CUtensorMap mw, mhi, mlo;
+  do {
+    if ((rc = make_quant_map(&mw, qtype, qs, out_features, kp))) break;
+    if ((rc = make_cols_map(&mhi, hi, kp))) break;
+    if ((rc = make_cols_map(&mlo, lo, kp))) break;
+    // unused columns of the planes stay finite (zero); tickets start at zero
+    if ((e = cudaMemsetAsync(scratch, 0, 2 * b_act + b_rs, st)) != cudaSuccess) break;
+    if ((e = cudaMemsetAsync(tickets, 0, b_tk, st)) != cudaSuccess) break;
+    if ((e = launch_weight_row_scales(qtype, qs, d, out_features, kp, cs, st)) != cudaSuccess)
+      break;
+    if ((e = launch_split_rows(x, cols, in_features, kp, in_features, nullptr, 0.0f, hi, lo, rs,
+                               st)) != cudaSuccess)
+      break;
+    BatchGemm g = {};
+    g.qtype = qtype;
+    g.d = d;
+    g.n = out_features;
+    g.kp = kp;
+    g.cols = cols;
+    g.rs = rs;
+    g.cs = cs;
+    g.plan = plan;
+    g.partial = part;
+    g.tickets = tickets;
+    g.epi = kEpiStore;
+    g.bias = bias;
+    g.residual = residual;
+    g.y = y;
+    g.ldy = out_features;
+    e = launch_batch_gemm(mw, mhi, mlo, g, st, false);
+  } while (false);
+  cudaError_t ef = cudaFreeAsync(scratch, st);
+  if (rc) return rc;
+  if (e == cudaSuccess) e = ef;
+  if (e != cudaSuccess) return cuda_fail(api, e);
+  return DQMK_OK;
+}

@@ -26,42 +26,13 @@
 
 #include "dqmk.h"
 #include "internal.h"
+#include "model.h"
 #include "prefill.h"
 #include "tp.h"
 
 using namespace dqmk;
 
 namespace {
-
-struct Packed {
-  int qtype = 0;
-  int rows = 0, k = 0, kp = 0;
-  uint8_t* base = nullptr;  // owns qs plane followed by d plane
-  size_t bytes = 0;
-  const uint8_t* qs() const { return base; }
-  const uint16_t* d() const {
-    const size_t qb = (size_t)rows * (qtype == DQMK_Q80 ? kp : kp / 2);
-    return reinterpret_cast<const uint16_t*>(base + qb);
-  }
-};
-
-struct Raw {
-  int qtype = 0;
-  int rows = 0, cols = 0;
-  void* dev = nullptr;           // quantized blocks on the device
-  std::vector<float> host;       // F32 tensors (small) kept on the host
-};
-
-struct Layer {
-  Packed qkv, wo, gate_up, down;
-  float* qkv_bias = nullptr;  // packed (paired) row order
-  float* attn_norm = nullptr;
-  float* ffn_norm = nullptr;
-  // batched prefill: each weight as two exact fp16 planes (TMA maps {hi, lo})
-  // of its dequantized values scaled per row by 2^-f, and the 2^f
-  float *cs_qkv = nullptr, *cs_o = nullptr, *cs_gu = nullptr, *cs_dn = nullptr;
-  CUtensorMap map_qkv[2], map_o[2], map_gu[2], map_dn[2];
-};
 
 // Per-context buffers of the batched prefill, allocated on first use.
 struct PrefillBufs {
@@ -75,33 +46,6 @@ struct PrefillBufs {
 };
 
 }  // namespace
-
-struct dqmk_model {
-  dqmk_model_config cfg{};
-  int device = 0;
-  int qtype = 0;
-  bool finalized = false;
-  std::map<std::string, Raw> raw;
-  std::vector<Layer> layers;
-  Packed embd, lm_head;
-  bool tied = true;
-  bool prefill_ready = false;  // two-term weight planes and TMA maps built
-  dqmk_tp_plan tp{};           // this model's shard (world 1: everything)
-  void* comm = nullptr;        // NCCL communicator when tp.world > 1
-  float* final_norm = nullptr;
-  float2* rope_cs = nullptr;
-  std::vector<void*> allocs;
-  size_t memory_bytes = 0;
-  dqmk_model_stats stats{};
-
-  ~dqmk_model() {
-    cudaSetDevice(device);
-    for (void* p : allocs) cudaFree(p);
-    for (auto& kv : raw)
-      if (kv.second.dev) cudaFree(kv.second.dev);
-    tp_comm_destroy(comm);
-  }
-};
 
 struct dqmk_context {
   dqmk_model* m = nullptr;
@@ -176,7 +120,9 @@ void rope_table(float theta, int head_dim, int pos_begin, int pos_count, float2*
 
 namespace {
 
-int dev_alloc(std::vector<void*>& owner, size_t bytes, void** out, const char* api) {
+}  // namespace
+
+int dqmk::dev_alloc(std::vector<void*>& owner, size_t bytes, void** out, const char* api) {
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
   if (e != cudaSuccess) return cuda_fail(api, e);
@@ -184,6 +130,8 @@ int dev_alloc(std::vector<void*>& owner, size_t bytes, void** out, const char* a
   *out = p;
   return DQMK_OK;
 }
+
+namespace {
 
 size_t block_bytes(int qtype) { return qtype == DQMK_Q80 ? 34 : 18; }
 
@@ -592,13 +540,17 @@ namespace {
 
 // Programmatic dependent launch between the kernels of a step; DQMK_PDL=0 in
 // the environment launches them plainly instead (diagnostics: same work).
-bool use_pdl() {
+}  // namespace
+
+bool dqmk::use_pdl() {
   static const bool on = [] {
     const char* v = std::getenv("DQMK_PDL");
     return !(v && v[0] == '0');
   }();
   return on;
 }
+
+namespace {
 
 PeerSet peer_set(const dqmk_context* x) {
   PeerSet ps{};

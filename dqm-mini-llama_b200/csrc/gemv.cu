@@ -804,12 +804,13 @@ extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, cons
 }
 
 extern "C" int dqmk_device_error(int clear) {
-  unsigned int flags = 0, prefill_flags = 0, tp_flags = 0, step_flags = 0;
+  unsigned int flags = 0, prefill_flags = 0, tp_flags = 0, step_flags = 0, batch_flags = 0;
   cudaError_t e = read_device_error(&flags, clear != 0);
   if (e == cudaSuccess) e = read_prefill_error(&prefill_flags, clear != 0);
   if (e == cudaSuccess) e = read_tp_error(&tp_flags, clear != 0);
   if (e == cudaSuccess) e = read_step_error(&step_flags, clear != 0);
-  flags |= prefill_flags | tp_flags | step_flags;
+  if (e == cudaSuccess) e = read_batch_error(&batch_flags, clear != 0);
+  flags |= prefill_flags | tp_flags | step_flags | batch_flags;
   if (e != cudaSuccess) {
     cuda_fail("dqmk_device_error", e);
     return -1;

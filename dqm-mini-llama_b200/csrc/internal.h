@@ -159,6 +159,8 @@ cudaError_t launch_tp_argmax_advance(const PeerSet& ps, const unsigned long long
                                      int* token, int* pos, int* history, int cap, cudaStream_t s,
                                      bool pdl);
 cudaError_t read_tp_error(unsigned int* flags, bool clear);
+// Multi-sequence decode GEMM (batch.cu): bounded-wait flag.
+cudaError_t read_batch_error(unsigned int* flags, bool clear);
 cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, int* pos,
                                   int* history, int cap, cudaStream_t s);
 cudaError_t launch_kv_write(float* keys, float* values, int max_seq, int n_kv_heads,

@@ -39,6 +39,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "prefill.h"
+#include "tc_dev.cuh"
 
 namespace dqmk {
 namespace {
@@ -52,114 +53,29 @@ constexpr int kAccBufs = 2;                  // TMEM accumulators (tile t, t+1)
 constexpr uint32_t kTmemCols = kAccBufs * BN;
 constexpr int kEpiWarps = 4;                 // one per TMEM lane quarter, 128 columns each
 constexpr int kGemmThreads = (2 + kEpiWarps) * 32;
-constexpr unsigned long long kWaitNs = 1000000000ull;
 
 __device__ unsigned int g_prefill_error;  // bit 0: a bounded wait timed out
 
-__device__ __forceinline__ uint32_t su32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ unsigned long long now_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void bar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(su32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait; also gives up early once another role has aborted.
+using tc::bar_arrive;
+using tc::bar_expect_tx;
+using tc::bar_init;
+using tc::mma_commit;
+using tc::smem_desc;
+using tc::su32;
+using tc::tc_fence_after;
+using tc::tc_fence_before;
+using tc::tma_load_2d;
+using tc::tmem_ld32;
+using tc::tmem_wait_ld;
+
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
-  if (bar_try(b, parity)) return true;
-  const unsigned long long t0 = now_ns();
-  while (true) {
-    if (bar_try(b, parity)) return true;
-    if (*abort) return false;
-    if (now_ns() - t0 > kWaitNs) {
-      *abort = 1;
-      atomicOr(&g_prefill_error, 1u);
-      return false;
-    }
-  }
+  return tc::bar_wait(b, parity, abort, &g_prefill_error);
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3}], [%4];" ::"r"(su32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
-      : "memory");
-}
-
-// K-major operand in a 128-byte-swizzled tile: rows of 128 bytes, 8-row atoms
-// 1024 bytes apart (stride byte offset), version 1 (sm_100), layout
-// SWIZZLE_128B.  The start address moves by 32 bytes per K=16 fp16 slice.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;            // leading byte offset (unused when swizzled)
-  d |= (uint64_t)(1024u >> 4) << 32;  // stride byte offset: 8 rows x 128 B
-  d |= (uint64_t)1u << 46;            // descriptor version
-  d |= (uint64_t)2u << 61;            // SWIZZLE_128B
-  return d;
-}
-
-// kind::f16 instruction descriptor: f32 accumulate, f16 A and B, both
-// K-major, M = 128, N = 128.
-constexpr uint32_t kIdesc =
-    (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-
+// kind::f16, M = 128 (token rows), N = 128 (weight rows)
+constexpr uint32_t kIdesc = tc::idesc_f16(BM, BN);
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   su32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  tc::mma_f16(tmem_d, a, b, kIdesc, acc);
 }
 
 // QKV epilogue for the pair pp (head hh, pair index i) of token row m, bias
@@ -836,23 +752,34 @@ size_t gemm_smem() {
 
 }  // namespace
 
-// [rows][kp] fp16 plane, 128-row x 64-element (128-byte) boxes, 128-byte swizzle.
-int make_f16_tile_map(CUtensorMap* map, const void* base, int rows, int kp) {
+// 2D tiled tensor map over a row-major [outer][inner] array; the base, the
+// row pitch and the box's inner extent must be 16-byte multiples.
+int make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+                uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
-  if (!fn) return fail(DQMK_ERR_CUDA, "ForwardBatch: cuTensorMapEncodeTiled unavailable");
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (kp % 8) != 0 || rows <= 0)
-    return fail(DQMK_ERR_INVALID, "ForwardBatch: tensor map base or stride not 16-byte aligned");
-  cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)kp * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BKE, (cuuint32_t)BM};
+  if (!fn) return fail(DQMK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (row_bytes % 16) != 0 ||
+      ((uint64_t)box_inner * elem_bytes) % 16 != 0 || inner == 0 || outer == 0)
+    return fail(DQMK_ERR_INVALID, "tensor map base, pitch or box not 16-byte aligned");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
-    return fail(DQMK_ERR_CUDA, "ForwardBatch: cuTensorMapEncodeTiled failed (" +
-                                   std::to_string((int)r) + ")");
+    return fail(DQMK_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return DQMK_OK;
+}
+
+// [rows][kp] fp16 plane, box_rows x 64-element (128-byte) boxes, 128-byte swizzle.
+int make_f16_tile_map(CUtensorMap* map, const void* base, int rows, int kp, int box_rows) {
+  if ((kp % 8) != 0 || rows <= 0)
+    return fail(DQMK_ERR_INVALID, "ForwardBatch: tensor map base or stride not 16-byte aligned");
+  return make_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, (uint64_t)kp, (uint64_t)rows,
+                     (uint64_t)kp * 2, BKE, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Enough work items to cover the SMs, at least 8 scale blocks per split; an

@@ -50,8 +50,14 @@ struct PrefillAttn {
   int m, pos0, layer, max_seq, n_heads, n_kv_heads, head_dim;
 };
 
-// Tensor map of an fp16 [rows][kp] plane in 128 x 64-element boxes.
-int make_f16_tile_map(CUtensorMap* map, const void* base, int rows, int kp);
+// 2D tiled tensor map over a row-major [outer][inner] array (no multicast
+// anywhere); base, row pitch and box inner extent 16-byte multiples.
+int make_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+                uint32_t box_outer, CUtensorMapSwizzle swizzle);
+// Tensor map of an fp16 [rows][kp] plane in box_rows x 64-element boxes with
+// the 128-byte swizzle of the tensor-core operand tiles.
+int make_f16_tile_map(CUtensorMap* map, const void* base, int rows, int kp, int box_rows = 128);
 GemmPlan plan_gemm(int m, int n, int kp);
 // Largest splits * m * n over every m <= m_max (floats of the partial buffer).
 size_t partial_floats_bound(int m_max, int n, int kp);

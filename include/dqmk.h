@@ -114,7 +114,7 @@ int dqmk_gemv_packed(int qtype, const float* x_dev, int in_features, const void*
                      int out_features, const float* bias_dev, const float* residual_dev,
                      float* y_dev, void* stream);
 
-/* Batched (prefill) linear on a packed weight, on the int8 tensor cores:
+/* Batched (prefill) linear on a packed weight, on the tensor cores:
  * y[m][o] = residual[m][o] + bias[o] + sum_k W[o][k] x[m][k] for `m` rows
  * (residual_dev / bias_dev may be NULL; y_dev may equal residual_dev).  The
  * batched form of LinearQ80 / LinearQ40 (src/quant.cc:350-360, rows of x
@@ -130,6 +130,17 @@ int dqmk_gemv_packed(int qtype, const float* x_dev, int in_features, const void*
 int dqmk_linear_batch_packed(int qtype, const float* x_dev, int m, int in_features,
                              const void* packed_dev, int out_features, const float* bias_dev,
                              const float* residual_dev, float* y_dev, void* stream);
+
+/* Multi-sequence decode linear: the same product for 1..64 columns of x
+ * (one per sequence), computed the way a dqmk_batch step runs its
+ * projections -- the packed Q8_0 / Q4_0 blocks are streamed from HBM once and
+ * turned into exact two-term fp16 tensor-core operands on chip (no fp16
+ * weight planes are kept).  y[c][o] = residual[c][o] + bias[o] +
+ * sum_k W[o][k] x[c][k]; results match the F32 product to fp32
+ * summation-order differences.  Scratch is stream-ordered on `stream`. */
+int dqmk_linear_cols_packed(int qtype, const float* x_dev, int cols, int in_features,
+                            const void* packed_dev, int out_features, const float* bias_dev,
+                            const float* residual_dev, float* y_dev, void* stream);
 
 /* Failure detection.  Kernels that wait on asynchronous copies bound every
  * wait (about one second); a wait that runs out records a flag in device
@@ -358,6 +369,46 @@ int dqmk_decode_greedy(dqmk_context* ctx, int token, int pos, int n_steps, int* 
  * synchronizing; returns the context stream for event timing. */
 int dqmk_decode_enqueue(dqmk_context* ctx, int token, int pos, int n_steps);
 void* dqmk_context_stream(dqmk_context* ctx);
+
+/* ---------------------------------------------------- multi-sequence decode
+ * The reference serves one sequence per MiniLlamaContext and one token per
+ * ForwardToken (src/forward.cc:667-754); serving many sequences means many
+ * contexts, each re-reading every weight per token.  A dqmk_batch holds
+ * n_slots independent sequences (each its own KV cache of max_seq
+ * positions, fp32 [layer][pos][kv_head][head_dim] like CudaKvCache) over one
+ * model and runs a step over up to 64 columns at once: column c feeds
+ * tokens[c] at positions[c] of slot slots[c].  Each column computes exactly
+ * what ForwardToken computes for that sequence (within fp32 summation-order
+ * differences); the weights are streamed once per step.  Works on tensor-
+ * parallel models (dqmk_model_set_tp): every rank calls the same functions
+ * with the same arguments.  Head sizes 64 and 128, Q8_0 / Q4_0 weights. */
+typedef struct dqmk_batch dqmk_batch;
+int dqmk_batch_create(dqmk_model* model, int n_slots, int max_seq, dqmk_batch** out);
+int dqmk_batch_destroy(dqmk_batch* batch);
+/* Zeroes every slot's KV cache. */
+int dqmk_batch_reset(dqmk_batch* batch);
+/* One step over n columns (1..64; slots NULL means slot c for column c; a
+ * (slot, position) pair at most once; a slot may take several positions in
+ * one step, e.g. a prompt chunk, since every column's K/V is stored before
+ * attention runs).  logits: NULL or [n][vocab_size] on the host; next: NULL
+ * or the n greedy tokens.  Synchronous. */
+int dqmk_batch_step(dqmk_batch* batch, const int* slots, const int* tokens, const int* positions,
+                    int n, float* logits, int* next);
+/* Greedy decoding of slots 0..n-1 together: slot c starts from tokens[c] at
+ * positions[c]; n_steps steps, each one replay of the captured step graph
+ * with the argmax, token and position advanced on the device.  out:
+ * [n_steps][n], out[i][c] = the token chosen after position positions[c] + i.
+ * Synchronous. */
+int dqmk_batch_decode_greedy(dqmk_batch* batch, const int* tokens, const int* positions, int n,
+                             int n_steps, int* out);
+/* Timing hook: the same steps enqueued without synchronizing, and the batch
+ * stream to time them on. */
+int dqmk_batch_decode_enqueue(dqmk_batch* batch, const int* tokens, const int* positions, int n,
+                              int n_steps);
+void* dqmk_batch_stream(dqmk_batch* batch);
+/* out[i] = the greedy token chosen after position pos0 + i of `slot`.
+ * Synchronous. */
+int dqmk_batch_history(dqmk_batch* batch, int slot, int pos0, int count, int* out);
 
 #ifdef __cplusplus
 }
