@@ -321,21 +321,13 @@ def random_q40_blocks(torch, rows: int, cols: int, gen) -> "torch.Tensor":
     return torch.cat([d.view(torch.uint8).view(nb, 2), q], dim=1).contiguous()
 
 
-def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
-    """Qwen2-7B-architecture Q4_0 (untied lm_head), one sequence, tensor
-    parallel over the ranks (one GPU each): a --ctx-long prompt fills the KV
-    cache, then --steps greedy decode steps are timed (device argmax, captured
-    step graph with the NCCL all-reduces inside)."""
-    S = pkg.synth
-    c = dict(S.QWEN2_7B)
-    n_steps, ctx_len = args.steps, args.ctx
-    nccl_id = None
-    if world > 1:
-        obj = [pkg.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
-    model = pkg.Model(c, ctx_len + n_steps + args.warmup, local)
-    model.set_tp(rank, world, nccl_id)
+def build_7b(pkg, torch, max_seq: int, local: int, tp_rank: int, tp_world: int, nccl_id):
+    """Qwen2-7B-architecture Q4_0 model with random device blocks (uniform
+    nibbles, fp16 scales 0.003-0.006), unit norms, N(0, 0.02) QKV biases,
+    untied lm_head; this rank's tensor-parallel shard."""
+    c = dict(pkg.synth.QWEN2_7B)
+    model = pkg.Model(c, max_seq, local)
+    model.set_tp(tp_rank, tp_world, nccl_id)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(20261205)
     hd = c["dim"] // c["n_heads"]
@@ -360,6 +352,25 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
             model.upload(p + n, pkg.F32, brng.normal(0, 0.02, size).astype(np.float32), 1, size)
         torch.cuda.synchronize()
     model.finalize()
+    return model
+
+
+def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
+    """Qwen2-7B-architecture Q4_0 (untied lm_head), one sequence, tensor
+    parallel over the ranks (one GPU each): a --ctx-long prompt fills the KV
+    cache, then --steps greedy decode steps are timed (device argmax, captured
+    step graph with the NCCL all-reduces inside)."""
+    S = pkg.synth
+    c = dict(S.QWEN2_7B)
+    n_steps, ctx_len = args.steps, args.ctx
+    nccl_id = None
+    if world > 1:
+        obj = [pkg.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    model = build_7b(pkg, torch, ctx_len + n_steps + args.warmup, local, rank, world, nccl_id)
+    hd = c["dim"] // c["n_heads"]
+    qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
     ctx = pkg.Context(model)
     exchange = "none"
     if world > 1:
@@ -415,6 +426,113 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
                    "parallelism": f"tp{world}", "exchange": exchange,
                    "seq_len": ctx_len + args.warmup + n_steps},
         "hbm": {"bytes_per_token_per_gpu": int(per_gpu), "GB_s_per_gpu": round(gbs, 1),
+                "frac_of_peak": round(gbs / peak, 4), "peak_source": peak_kind},
+        "clocks": clk.summary()}))
+
+
+def bench_7b_batch(args, pkg, torch, dist, world, rank, local):
+    """Qwen2-7B-architecture Q4_0, --seqs sequences decoded together
+    (dqmk_batch): tensor parallel over --tp ranks, world / tp independent
+    groups splitting the sequences.  Every slot's KV cache is filled with a
+    --ctx-token random prompt (batched steps of 64 positions of one slot), then
+    --warmup greedy steps run and --steps greedy steps are timed (one captured
+    step graph per step, argmax and position advanced on the device)."""
+    import time
+    S = pkg.synth
+    c = dict(S.QWEN2_7B)
+    tp = args.tp or world
+    if world % tp or args.seqs % (world // tp):
+        raise SystemExit("--gpus must be a multiple of --tp and --seqs of the group count")
+    groups = world // tp
+    group, tp_rank = rank // tp, rank % tp
+    seqs = args.seqs // groups
+    nccl_id = None
+    if tp > 1:
+        mine = pkg.nccl_unique_id() if tp_rank == 0 else None
+        ids = [None] * world
+        dist.all_gather_object(ids, mine)
+        nccl_id = ids[group * tp]
+    ctx_len, n_steps, warm = args.ctx, args.steps, args.warmup
+    max_seq = ctx_len + warm + n_steps + 17  # + the end-to-end steps
+    model = build_7b(pkg, torch, max_seq, local, tp_rank, tp, nccl_id)
+    batch = pkg.Batch(model, seqs, max_seq)
+    stream = torch.cuda.ExternalStream(batch.stream_handle)
+    prompts = [S.prompt_tokens(c["vocab"], ctx_len, 1000 + group * seqs + s) for s in range(seqs)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s in range(seqs):
+        batch.prefill(s, prompts[s][:-1])
+    torch.cuda.synchronize()
+    fill_s = time.perf_counter() - t0
+    last = [int(p[-1]) for p in prompts]
+    batch.decode_enqueue(last, [ctx_len - 1] * seqs, warm)
+    torch.cuda.synchronize()
+    pos0 = ctx_len - 1 + warm
+    cont = [int(batch.history(s, pos0 - 1, 1)[0]) for s in range(seqs)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        batch.decode_enqueue(cont, [pos0] * seqs, n_steps)
+        e1.record(stream)
+        e1.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3
+    # end to end through the public step call: host tokens in, host tokens out
+    pos1 = pos0 + n_steps
+    toks = [int(batch.history(s, pos1 - 1, 1)[0]) for s in range(seqs)]
+    e2e_steps = min(16, max_seq - pos1)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        _, nxt = batch.step(None, toks, [pos1 + i] * seqs, want_logits=False)
+        toks = nxt.tolist()
+    e2e_dt = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([dt, e2e_dt, fill_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt, e2e_dt, fill_s = (float(v) for v in t.tolist())
+    batch.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    hd = c["dim"] // c["n_heads"]
+    qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
+    weights = (c["n_layers"] * (qd + 2 * kvd + qd + 3 * c["hidden"]) * c["dim"] * 18 // 32
+               + c["vocab"] * c["dim"] * 18 // 32)
+    mean_pos = pos0 + n_steps / 2
+    kv = c["n_layers"] * 2 * kvd * 4 * (mean_pos + 1) * seqs
+    per_gpu = (weights + kv) / tp
+    peak, peak_kind = peaks()
+    gbs = per_gpu * n_steps / dt / 1e9
+    launches = 1 + c["n_layers"] * (9 + (4 if tp > 1 else 0)) + 3
+    print(json.dumps({
+        "metric": f"decode tok/s, Qwen2-7B Q4_0, {args.seqs} sequences x {ctx_len} KV",
+        "value": round(args.seqs * n_steps / dt, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": n_steps, "warmup": warm, "ms_per_step": round(dt / n_steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_0xf32",
+        "data": "synthetic: random Q4_0 blocks (uniform nibbles, fp16 scales 0.003-0.006), "
+                "random prompt ids",
+        "config": {"workload": f"qwen2-7b-architecture Q4_0, untied lm_head, {args.seqs} "
+                               f"sequences each with a {ctx_len}-token prompt in its KV cache, "
+                               f"then {n_steps} greedy steps of all sequences together",
+                   "model": "qwen2-7b", "global_batch": args.seqs,
+                   "parallelism": f"{groups}x tp{tp}" if groups > 1 else f"tp{tp}",
+                   "seq_len": max_seq,
+                   "l2": "per-step weight + KV stream far above the 126 MB L2"},
+        "e2e": {"value": round(args.seqs * e2e_steps / e2e_dt, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 3 * 64 * 4, "d2h_bytes_per_step": seqs * 4,
+                "steps": e2e_steps},
+        "kv_fill": {"tokens": args.seqs * (ctx_len - 1), "s": round(fill_s, 3),
+                    "tok_s": round(args.seqs * (ctx_len - 1) / fill_s, 1)},
+        "gpu_launches": n_steps * launches,
+        "hbm": {"bytes_per_step_per_gpu": int(per_gpu), "GB_s_per_gpu": round(gbs, 1),
                 "frac_of_peak": round(gbs / peak, 4), "peak_source": peak_kind},
         "clocks": clk.summary()}))
 
@@ -487,6 +605,12 @@ def main():
     ap.add_argument("--model", default="qwen2-0.5b", choices=["qwen2-0.5b", "qwen2-7b"],
                     help="qwen2-7b: tensor-parallel decode over the --gpus ranks")
     ap.add_argument("--ctx", type=int, default=2048, help="qwen2-7b: KV length before decoding")
+    ap.add_argument("--seqs", type=int, default=1,
+                    help="qwen2-7b: sequences decoded together (64: the multi-sequence "
+                         "configuration; 1: batch-1 decode)")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="qwen2-7b with --seqs > 1: tensor-parallel group size (default: all "
+                         "ranks); --gpus / --tp independent groups split the sequences")
     ap.add_argument("--p2p", action="store_true",
                     help="qwen2-7b under tensor parallelism: exchange partial sums over peer "
                          "memory (IPC-mapped buffers) instead of NCCL all-reduces")
@@ -513,7 +637,10 @@ def main():
     pkg = ge.load_package()
     S = pkg.synth
     if args.model == "qwen2-7b":
-        bench_7b_tp(args, pkg, torch, dist, world, rank, local)
+        if args.seqs > 1:
+            bench_7b_batch(args, pkg, torch, dist, world, rank, local)
+        else:
+            bench_7b_tp(args, pkg, torch, dist, world, rank, local)
         return
     w = build_model(pkg, torch)
     if args.prefill_only:

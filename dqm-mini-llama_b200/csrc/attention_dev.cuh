@@ -166,11 +166,56 @@ __device__ __forceinline__ void attention_hd_body(const AttnArgs& a, int chunk_c
   float* stats = sacc + GROUPS * kMaxGroup * HD;
 
   if (split < sp.n_active) {
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
+    if constexpr (HD == 128) {
+      // Scores with one K row per warp load: lane l holds dims 4l..4l+3 of
+      // the row and of every query head (registers); a warp takes 4
+      // consecutive positions per step, and the 4 x 8 partial dots are
+      // summed across the lanes by a transposed butterfly (31 shuffles) that
+      // leaves lane l with the score of position l / 8, head l % 8.
+      const int lane = tid & 31, wid = tid >> 5;
+      float4 qv[kMaxGroup];
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h)
+        qv[h] = h < G ? __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)(kvh * G + h) * HD) +
+                               lane)
+                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int t0 = 4 * wid; t0 < sp.n; t0 += 4 * (NT / 32)) {
+        float4 kr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          kr[i] = t0 + i < sp.n ? __ldcg(reinterpret_cast<const float4*>(
+                                      kbase + (size_t)(sp.t0 + t0 + i) * row_stride) + lane)
+                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int h = 0; h < kMaxGroup; ++h) {
+            float d = __fmul_rn(qv[h].x, kr[i].x);
+            d = fmaf(qv[h].y, kr[i].y, d);
+            d = fmaf(qv[h].z, kr[i].z, d);
+            d = fmaf(qv[h].w, kr[i].w, d);
+            v[i * kMaxGroup + h] = d;
+          }
+#pragma unroll
+        for (int m = 16, n = 32; m >= 1; m >>= 1, n >>= 1) {
+          const bool upper = (lane & m) != 0;
+#pragma unroll
+          for (int k = 0; k < n / 2; ++k) {
+            const float send = upper ? v[k] : v[k + n / 2];
+            const float keep = upper ? v[k + n / 2] : v[k];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+          }
+        }
+        const int t = t0 + (lane >> 3), h = lane & 7;
+        if (h < G && t < sp.n) ss[h * chunk_cap + t] = __fmul_rn(v[0], scale);
+      }
+    } else {
     for (int i = tid; i < G * D4; i += NT)
       reinterpret_cast<float4*>(sq)[i] =
           __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)(kvh * G) * HD) + i);
     __syncthreads();
-    const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
     const int part = tid % TPT;
     for (int base = 0; base < sp.n; base += 2 * TOK) {
       float4 k4[2][4];
@@ -214,6 +259,7 @@ __device__ __forceinline__ void attention_hd_body(const AttnArgs& a, int chunk_c
             if (h < G) ss[h * chunk_cap + t] = __fmul_rn(dot[h], scale);
         }
       }
+    }
     }
     __syncthreads();
     split_softmax<NT>(ss, chunk_cap, G, sp.n, head_m, head_l);

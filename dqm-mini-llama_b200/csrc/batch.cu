@@ -8,26 +8,30 @@
 // summation-order differences of the F32 reference:
 //
 //   * weights stay in HBM as the packed Q8_0 / Q4_0 blocks of the decode GEMV
-//     (the step streams the same bytes a batch-1 step would).  TMA brings a
-//     256-row x 64-value tile of quants into a raw ring; eight dequant warps
-//     turn it into the exact two-term fp16 operand of the prefill GEMM: with
-//     the row scaled by 2^-f (row maximum in [2^14, 2^15)) every value
-//     d * q * 2^-f is exactly hi + lo, hi = fp16(d' q), lo = fma(d', q, -hi)
-//     with d' = fp16(d * 2^-f) (exact), computed in packed half arithmetic and
-//     written in the 128-byte-swizzled K-major layout TMA would produce;
+//     (the step streams the same bytes a batch-1 step would; the block scales
+//     are read from a copy padded to 16-byte rows).  TMA brings a 256-row x
+//     64-value tile of quants and its scales into a raw ring in shared memory;
+//     eight dequant warps turn it into the exact two-term fp16 operand of the
+//     prefill GEMM: with the row scaled by 2^-f (row maximum in
+//     [2^14, 2^15)) every value d * q * 2^-f is exactly hi + lo,
+//     hi = fp16(d' q), lo = fma(d', q, -hi) with d' = fp16(d * 2^-f) (exact),
+//     computed in packed half arithmetic and stored straight into tensor
+//     memory (tcgen05.st), where the MMA takes it as its A operand -- shared
+//     memory carries only the raw tiles and the activation tiles;
 //   * activations: each column (after its RMSNorm) is split into two fp16
 //     planes by the prefill's split kernel and arrives by TMA;
 //   * tcgen05.mma kind::f16, M = 128 weight rows (two per 256-row tile), N =
 //     the columns rounded up to 16, K = 16: W_hi X_hi + W_hi X_lo + W_lo X_hi
 //     accumulate in TMEM (fp32) over the tile's K range;
-//   * split-K where row tiles are few: each split parks its raw sums, the last
-//     CTA of a row tile (completion ticket) adds them in split order -- the
-//     same order whichever CTA finishes last -- and runs the epilogue;
+//   * split-K where row tiles are few: each split parks its raw sums and a
+//     reduce kernel over the whole grid adds them in split order
+//     (deterministic) and runs the epilogue;
 //   * epilogues: residual add, SwiGLU of interleaved gate/up rows, QKV bias +
 //     RoPE + KV-cache store at each column's (slot, position), logits with a
 //     per-column argmax key (value, first index) combined by atomicMax.
 // Warp roles: 0 TMA, 1 MMA issue, 2-5 epilogue (one TMEM lane quarter each),
-// 6-13 dequant (one weight row each).  Every hand-off is an mbarrier with a
+// 6-13 dequant (one weight row each).  TMEM: two accumulators (256 columns)
+// and two weight-operand stages (256 columns).  Every hand-off is an mbarrier with a
 // bounded wait; a wait that runs out sets a device flag and the CTA unwinds
 // (its own copies in flight land first, TMEM is freed).  Under programmatic
 // dependent launch the weight copies and their dequantization start before the
@@ -47,20 +51,38 @@
 namespace dqmk {
 namespace {
 
-constexpr int kTileRows = 256;                                 // weight rows per work item
-constexpr int kHalfRows = 128;                                 // rows per MMA (M)
-constexpr int kChunkK = 64;                                    // K values per stage
-constexpr int kOpStages = 2;
-constexpr int kRawStages = 3;
-constexpr int kWHalfBytes = kHalfRows * kChunkK * 2;           // 16 KB
-constexpr int kWPlaneBytes = 2 * kWHalfBytes;                  // 32 KB: one fp16 plane
-constexpr int kXPlaneBytes = kBatchMaxCols * kChunkK * 2;      // 8 KB
-constexpr int kOpStageBytes = 2 * kWPlaneBytes + 2 * kXPlaneBytes;
+constexpr int kTileRows = 256;                             // weight rows per work item
+constexpr int kHalfRows = 128;                             // rows per MMA (M)
+constexpr int kChunkK = 64;                                // K values per stage
+#ifndef DQMK_BATCH_RAW_STAGES
+#define DQMK_BATCH_RAW_STAGES 4
+#endif
+#ifndef DQMK_BATCH_A_STAGES
+#define DQMK_BATCH_A_STAGES 2
+#endif
+#ifndef DQMK_BATCH_ACC_BUFS
+#define DQMK_BATCH_ACC_BUFS 2
+#endif
+#ifndef DQMK_BATCH_EPI_SLEEP
+#define DQMK_BATCH_EPI_SLEEP 128
+#endif
+constexpr int kRawStages = DQMK_BATCH_RAW_STAGES;          // quant tiles (shared memory)
+constexpr int kXStages = 4;                                // activation tiles (shared memory)
+constexpr int kAStages = DQMK_BATCH_A_STAGES;              // weight operand tiles (TMEM)
+constexpr int kXPlaneBytes = kBatchMaxCols * kChunkK * 2;  // 8 KB
+constexpr int kXStageBytes = 2 * kXPlaneBytes;             // hi + lo
 constexpr int kEpiWarps = 4, kDeqWarps = 8;
 constexpr int kFirstEpiWarp = 2, kFirstDeqWarp = kFirstEpiWarp + kEpiWarps;
 constexpr int kThreads = (kFirstDeqWarp + kDeqWarps) * 32;
-constexpr int kAccBufs = 2;
-constexpr uint32_t kTmemCols = kAccBufs * 2 * kBatchMaxCols;  // 256
+constexpr int kAccBufs = DQMK_BATCH_ACC_BUFS;
+// TMEM columns: accumulators [buffer][half][64 columns], then the weight
+// operand stages [stage][half][hi 32 | lo 32] (two fp16 per column)
+constexpr uint32_t kAccCols = 2 * kBatchMaxCols;
+constexpr uint32_t kACol0 = kAccBufs * kAccCols;           // 256
+constexpr uint32_t kAStageCols = 2 * 2 * (kChunkK / 2);    // 128
+constexpr uint32_t kTmemNeed = kACol0 + kAStages * kAStageCols;  // 512
+constexpr uint32_t kTmemCols = kTmemNeed <= 256 ? 256 : 512;
+static_assert(kTmemNeed <= 512, "at most the whole tensor memory of the SM");
 static_assert(kDeqWarps * 32 == kTileRows, "one dequant thread per tile row");
 
 __device__ unsigned int g_batch_error;  // bit 0: a bounded wait timed out
@@ -69,17 +91,24 @@ template <int QT>
 constexpr int raw_row_bytes() {
   return QT == DQMK_Q80 ? kChunkK : kChunkK / 2;
 }
+// A raw stage: the quants of 256 rows x 64 values, then each row's group of
+// 8 block scales (16 bytes) that holds the stage's two blocks.
 template <int QT>
-constexpr int raw_stage_bytes() {
+constexpr int raw_scale_off() {
   return kTileRows * raw_row_bytes<QT>();
 }
 template <int QT>
+constexpr int raw_stage_bytes() {
+  return kTileRows * (raw_row_bytes<QT>() + 16);
+}
+template <int QT>
 constexpr size_t gemm_smem() {
-  return 1024 + (size_t)kOpStages * kOpStageBytes + (size_t)kRawStages * raw_stage_bytes<QT>();
+  return 1024 + (size_t)kXStages * kXStageBytes + (size_t)kRawStages * raw_stage_bytes<QT>();
 }
 
-__device__ __forceinline__ bool wait(uint64_t* b, uint32_t parity, volatile int* abort) {
-  return tc::bar_wait(b, parity, abort, &g_batch_error);
+__device__ __forceinline__ bool wait(uint64_t* b, uint32_t parity, volatile int* abort,
+                                     unsigned sleep_ns = 0) {
+  return tc::bar_wait(b, parity, abort, &g_batch_error, sleep_ns);
 }
 // Bounded wait that ignores the abort flag: a CTA lets its own copies land
 // before it exits.
@@ -147,20 +176,12 @@ __device__ __forceinline__ void two_term(__half2 t, __half2 s, uint32_t& hi, uin
   lo = h2u(l);
 }
 
-// Stores 16-byte chunk j (8 values) of row rr of a 128-row half tile in the
-// 128-byte swizzle (chunk j of row rr lands at chunk j ^ (rr & 7)).
-__device__ __forceinline__ void put_chunk(unsigned char* half_tile, int rr, int j, uint4 v) {
-  *reinterpret_cast<uint4*>(half_tile + rr * 128 + ((j ^ (rr & 7)) << 4)) = v;
-}
-
 // Q4_0 block (16 bytes: byte i holds value i in its low nibble and value
-// i + 16 in its high nibble, src/quant.cc:160-175) -> 32 values as hi / lo
-// chunks cb .. cb+3 of the row.
-__device__ __forceinline__ void dequant_q4_block(uint4 q, __half2 s, unsigned char* whi,
-                                                 unsigned char* wlo, int rr, int cb) {
+// i + 16 in its high nibble, src/quant.cc:160-175) -> its 32 values as 16
+// hi / lo pairs in K order (h[m] = values 2m, 2m+1).
+__device__ __forceinline__ void dequant_q4_block(uint4 q, __half2 s, uint32_t* h, uint32_t* l) {
   const uint32_t w[4] = {q.x, q.y, q.z, q.w};
   const __half2 off = __half2half2(__ushort_as_half(0x6408));  // 1032 = 1024 + 8
-  uint32_t h[16], l[16];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t lo4 = w[i] & 0x0F0F0F0Fu, hi4 = (w[i] >> 4) & 0x0F0F0F0Fu;
@@ -170,29 +191,18 @@ __device__ __forceinline__ void dequant_q4_block(uint4 q, __half2 s, unsigned ch
     two_term(__hsub2(u2h(prmt(hi4, 0x64646464u, 0x4140u)), off), s, h[8 + 2 * i], l[8 + 2 * i]);
     two_term(__hsub2(u2h(prmt(hi4, 0x64646464u, 0x4342u)), off), s, h[9 + 2 * i], l[9 + 2 * i]);
   }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    put_chunk(whi, rr, cb + j, make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]));
-    put_chunk(wlo, rr, cb + j, make_uint4(l[4 * j], l[4 * j + 1], l[4 * j + 2], l[4 * j + 3]));
-  }
 }
 
-// 16 Q8_0 values (int8, in order) -> hi / lo chunks cb, cb + 1 of the row.
-__device__ __forceinline__ void dequant_q8_16(uint4 q, __half2 s, unsigned char* whi,
-                                              unsigned char* wlo, int rr, int cb) {
+// 16 Q8_0 values (int8, in order) -> 8 hi / lo pairs in K order.
+__device__ __forceinline__ void dequant_q8_16(uint4 q, __half2 s, uint32_t* h, uint32_t* l) {
   const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u,
                          q.w ^ 0x80808080u};
   const __half2 off = __half2half2(__ushort_as_half(0x6480));  // 1152 = 1024 + 128
-  uint32_t h[8], l[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     two_term(__hsub2(u2h(prmt(w[i], 0x64646464u, 0x4140u)), off), s, h[2 * i], l[2 * i]);
     two_term(__hsub2(u2h(prmt(w[i], 0x64646464u, 0x4342u)), off), s, h[2 * i + 1], l[2 * i + 1]);
   }
-  put_chunk(whi, rr, cb, make_uint4(h[0], h[1], h[2], h[3]));
-  put_chunk(whi, rr, cb + 1, make_uint4(h[4], h[5], h[6], h[7]));
-  put_chunk(wlo, rr, cb, make_uint4(l[0], l[1], l[2], l[3]));
-  put_chunk(wlo, rr, cb + 1, make_uint4(l[4], l[5], l[6], l[7]));
 }
 
 // fp16 block scale d times the row's 2^-f, as a broadcast half2 (exact: a
@@ -210,33 +220,36 @@ struct ColInfo {
   int slot[kBatchMaxCols];
 };
 
-// Row `row` (this thread's TMEM lane) and columns cb .. cb+31 of finished
+// Row `row` (this thread's TMEM lane) and columns cb .. cb+NC-1 of finished
 // sums v (raw accumulator values): scale by rs[c] * cs[row] (exact powers of
-// two), then the epilogue.  Every lane of the warp calls this together (the
-// paired epilogues exchange values with the neighbouring lane).
+// two), then the epilogue.  Every lane of the warp calls this together with
+// consecutive rows on consecutive lanes (the paired epilogues exchange values
+// with the neighbouring lane).
+template <int NC>
 __device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, int row, int cb,
-                                       float (&v)[32]) {
+                                       float (&v)[NC]) {
+  constexpr int G = NC < 8 ? NC : 8;  // columns per load batch
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const bool ok = row < p.n;
   const float c = ok ? __ldg(p.cs + row) : 0.0f;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], ci.rs[(cb + j) & 63]), c);
-  const int ncol = min(32, p.cols - cb);  // valid columns of this group
+  for (int j = 0; j < NC; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], ci.rs[(cb + j) & 63]), c);
+  const int ncol = min(NC, p.cols - cb);  // valid columns of this group
   if (p.epi == kEpiStore) {
     if (!ok) return;
     const float b = p.bias ? __ldg(p.bias + row) : 0.0f;
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {  // 8 columns at a time: loads first, then stores
-      float r[8];
+    for (int g = 0; g < NC / G; ++g) {  // loads of a batch first, then its stores
+      float r[G];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = 8 * g + u;
+      for (int u = 0; u < G; ++u) {
+        const int j = G * g + u;
         r[u] = (p.residual && j < ncol) ? p.residual[(size_t)(cb + j) * p.ldy + row] : 0.0f;
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = 8 * g + u;
+      for (int u = 0; u < G; ++u) {
+        const int j = G * g + u;
         if (j < ncol) {
           float x = p.bias ? __fadd_rn(v[j], b) : v[j];
           if (p.residual) x = __fadd_rn(r[u], x);
@@ -246,7 +259,7 @@ __device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, in
     }
   } else if (p.epi == kEpiSwiGlu) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < NC; ++j) {
       const float u = __shfl_down_sync(full, v[j], 1);
       if (ok && !(lane & 1) && j < ncol) {
         const float g = v[j];
@@ -274,12 +287,12 @@ __device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, in
     const int kvd = p.n_kv_heads * p.head_dim;
     const bool writer = ok && !(lane & 1);
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      float a[8], bb[8];
-      float2 rc[8];
+    for (int g = 0; g < NC / G; ++g) {
+      float a[G], bb[G];
+      float2 rc[G];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = 8 * g + u;
+      for (int u = 0; u < G; ++u) {
+        const int j = G * g + u;
         a[u] = p.bias ? __fadd_rn(v[j], b) : v[j];
         bb[u] = __shfl_down_sync(full, a[u], 1);
         rc[u] = (writer && rotate && j < ncol)
@@ -288,8 +301,8 @@ __device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, in
       }
       if (!writer) continue;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = 8 * g + u;
+      for (int u = 0; u < G; ++u) {
+        const int j = G * g + u;
         if (j >= ncol) continue;
         float x0 = a[u], x1 = bb[u];
         if (rotate) {
@@ -317,7 +330,7 @@ __device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, in
     }
   } else {  // kEpiLogits
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < NC; ++j) {
       if (ok && p.y && j < ncol) p.y[(size_t)(cb + j) * p.ldy + row] = v[j];
       unsigned long long k = ok ? argmax_key(v[j], (uint32_t)(row + p.row_offset)) : 0ull;
 #pragma unroll
@@ -330,15 +343,63 @@ __device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, in
   }
 }
 
+__device__ __forceinline__ void stage_cols(const BatchGemm& p, ColInfo& ci, int tid, int nthreads) {
+  for (int c = tid; c < kBatchMaxCols; c += nthreads) {
+    const bool v = c < p.cols;
+    ci.rs[c] = v ? p.rs[c] : 0.0f;
+    ci.pos[c] = v && p.col_pos ? p.col_pos[c] : 0;
+    ci.slot[c] = v && p.col_slot ? p.col_slot[c] : 0;
+  }
+}
+
+// Split-K: sum of the splits' raw sums (partial[z][column][row]) in split
+// order, then the epilogue.  Thread (row = 32 * blockIdx.x + lane, columns
+// 4 * (8 * blockIdx.y + warp) .. + 3): all splits' loads of a batch of 8 are in
+// flight at once, lanes read consecutive rows (coalesced).
+constexpr int kReduceCols = 4;
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const BatchGemm p) {
+  __shared__ ColInfo ci;
+  pdl_trigger();
+  pdl_wait();
+  stage_cols(p, ci, threadIdx.x, blockDim.x);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 32 + lane;
+  const int c0 = (blockIdx.y * 8 + warp) * kReduceCols;
+  if (c0 >= p.cols) return;  // warp-uniform
+  const int rowc = row < p.n ? row : p.n - 1;
+  float v[kReduceCols];
+#pragma unroll
+  for (int j = 0; j < kReduceCols; ++j) v[j] = 0.0f;
+  for (int z0 = 0; z0 < p.plan.splits; z0 += 8) {
+    float t[8][kReduceCols];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+#pragma unroll
+      for (int j = 0; j < kReduceCols; ++j)
+        t[u][j] = z0 + u < p.plan.splits
+                      ? __ldcg(p.partial + ((size_t)(z0 + u) * kBatchMaxCols + c0 + j) * p.n + rowc)
+                      : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (z0 + u < p.plan.splits)
+#pragma unroll
+        for (int j = 0; j < kReduceCols; ++j) v[j] = __fadd_rn(v[j], t[u][j]);
+  }
+  finish<kReduceCols>(p, ci, row, c0, v);
+}
+
 // ------------------------------------------------------------------- kernel
 template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
     batch_gemm_kernel(const __grid_constant__ CUtensorMap map_w,
+                      const __grid_constant__ CUtensorMap map_d,
                       const __grid_constant__ CUtensorMap map_xhi,
                       const __grid_constant__ CUtensorMap map_xlo, const BatchGemm p) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-  __shared__ __align__(8) uint64_t op_full[kOpStages], x_full[kOpStages], op_empty[kOpStages];
+  __shared__ __align__(8) uint64_t x_full[kXStages], x_empty[kXStages];
+  __shared__ __align__(8) uint64_t a_full[kAStages], a_empty[kAStages];
   __shared__ __align__(8) uint64_t acc_full[kAccBufs], acc_empty[kAccBufs], mma_done;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
@@ -349,9 +410,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_tiles = (p.n + kTileRows - 1) / kTileRows;
   const int n_items = n_tiles * p.plan.splits;
   const int n_mma = (p.cols + 15) / 16 * 16;
-  unsigned char* ops = reinterpret_cast<unsigned char*>(
+  unsigned char* xs = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  unsigned char* raws = ops + (size_t)kOpStages * kOpStageBytes;
+  unsigned char* raws = xs + (size_t)kXStages * kXStageBytes;
 
   pdl_trigger();
   if (threadIdx.x == 0) {
@@ -359,10 +420,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::bar_init(&raw_full[s], 1);
       tc::bar_init(&raw_empty[s], kDeqWarps);
     }
-    for (int s = 0; s < kOpStages; ++s) {
-      tc::bar_init(&op_full[s], kDeqWarps);
+    for (int s = 0; s < kXStages; ++s) {
       tc::bar_init(&x_full[s], 1);
-      tc::bar_init(&op_empty[s], 1);
+      tc::bar_init(&x_empty[s], 1);
+    }
+    for (int s = 0; s < kAStages; ++s) {
+      tc::bar_init(&a_full[s], kDeqWarps);
+      tc::bar_init(&a_empty[s], 1);
     }
     for (int b = 0; b < kAccBufs; ++b) {
       tc::bar_init(&acc_full[b], 1);
@@ -372,6 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tc::tma_prefetch_desc(&map_w);
+    tc::tma_prefetch_desc(&map_d);
     tc::tma_prefetch_desc(&map_xhi);
     tc::tma_prefetch_desc(&map_xlo);
   }
@@ -389,9 +454,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int gr = 0, gx = 0;
       auto issue_raw = [&]() {
         const int st = gr % kRawStages;
+        unsigned char* dst = raws + (size_t)st * raw_stage_bytes<QT>();
         tc::bar_expect_tx(&raw_full[st], (uint32_t)raw_stage_bytes<QT>());
-        tc::tma_load_2d(raws + (size_t)st * raw_stage_bytes<QT>(), &map_w, rw.c * RB,
-                        rw.t.tile * kTileRows, &raw_full[st]);
+        tc::tma_load_2d(dst, &map_w, rw.c * RB, rw.t.tile * kTileRows, &raw_full[st]);
+        tc::tma_load_2d(dst + raw_scale_off<QT>(), &map_d, (2 * rw.c) & ~7, rw.t.tile * kTileRows,
+                        &raw_full[st]);
         rw.next(p);
         ++gr;
       };
@@ -409,23 +476,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_raw();
         }
         if (!ok) break;
-        const int os = gx % kOpStages;
-        if (gx >= kOpStages &&
-            !wait(&op_empty[os], (uint32_t)((gx / kOpStages - 1) & 1), &abort_flag))
+        const int xs_ = gx % kXStages;
+        if (gx >= kXStages &&
+            !wait(&x_empty[xs_], (uint32_t)((gx / kXStages - 1) & 1), &abort_flag))
           break;
-        unsigned char* st = ops + (size_t)os * kOpStageBytes;
-        tc::bar_expect_tx(&x_full[os], 2u * kXPlaneBytes);
-        tc::tma_load_2d(st + 2 * kWPlaneBytes, &map_xhi, xw.c * kChunkK, 0, &x_full[os]);
-        tc::tma_load_2d(st + 2 * kWPlaneBytes + kXPlaneBytes, &map_xlo, xw.c * kChunkK, 0,
-                        &x_full[os]);
+        unsigned char* st = xs + (size_t)xs_ * kXStageBytes;
+        tc::bar_expect_tx(&x_full[xs_], (uint32_t)kXStageBytes);
+        tc::tma_load_2d(st, &map_xhi, xw.c * kChunkK, 0, &x_full[xs_]);
+        tc::tma_load_2d(st + kXPlaneBytes, &map_xlo, xw.c * kChunkK, 0, &x_full[xs_]);
         xw.next(p);
         ++gx;
       }
       if (abort_flag) {  // let this thread's copies in flight land before exit
         for (int g = gr - kRawStages < 0 ? 0 : gr - kRawStages; g < gr; ++g)
           wait_landed(&raw_full[g % kRawStages], (uint32_t)((g / kRawStages) & 1));
-        for (int g = gx - kOpStages < 0 ? 0 : gx - kOpStages; g < gx; ++g)
-          wait_landed(&x_full[g % kOpStages], (uint32_t)((g / kOpStages) & 1));
+        for (int g = gx - kXStages < 0 ? 0 : gx - kXStages; g < gx; ++g)
+          wait_landed(&x_full[g % kXStages], (uint32_t)((g / kXStages) & 1));
       }
     }
   } else if (warp == 1) {
@@ -441,30 +507,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tc_fence_after();
         bool ok = true;
         for (int c = it.c0; c < it.c1; ++c, ++g) {
-          const int os = g % kOpStages;
-          const uint32_t par = (uint32_t)((g / kOpStages) & 1);
-          if (!wait(&op_full[os], par, &abort_flag) || !wait(&x_full[os], par, &abort_flag)) {
+          const int as = g % kAStages, xs_ = g % kXStages;
+          if (!wait(&a_full[as], (uint32_t)((g / kAStages) & 1), &abort_flag) ||
+              !wait(&x_full[xs_], (uint32_t)((g / kXStages) & 1), &abort_flag)) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const uint32_t whi = tc::su32(ops + (size_t)os * kOpStageBytes);
-          const uint32_t wlo = whi + kWPlaneBytes, xhi = whi + 2 * kWPlaneBytes,
-                         xlo = xhi + kXPlaneBytes;
+          const uint32_t xhi = tc::su32(xs + (size_t)xs_ * kXStageBytes);
+          const uint32_t xlo = xhi + kXPlaneBytes;
+          const uint32_t acol = tmem + kACol0 + (uint32_t)as * kAStageCols;
 #pragma unroll
           for (int k = 0; k < kChunkK / 16; ++k) {
             const uint64_t bhi = tc::smem_desc(xhi + 32 * k), blo = tc::smem_desc(xlo + 32 * k);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const uint32_t d = tmem + (uint32_t)(buf * 2 * kBatchMaxCols + h * kBatchMaxCols);
-              const uint64_t ahi = tc::smem_desc(whi + h * kWHalfBytes + 32 * k);
-              const uint64_t alo = tc::smem_desc(wlo + h * kWHalfBytes + 32 * k);
-              tc::mma_f16(d, ahi, bhi, idesc, (c > it.c0 || k > 0) ? 1u : 0u);
-              tc::mma_f16(d, ahi, blo, idesc, 1u);
-              tc::mma_f16(d, alo, bhi, idesc, 1u);
+              const uint32_t d = tmem + (uint32_t)(buf * kAccCols + h * kBatchMaxCols);
+              const uint32_t ahi = acol + (uint32_t)(h * 64 + 8 * k);
+              const uint32_t alo = ahi + 32;
+              tc::mma_f16_ts(d, ahi, bhi, idesc, (c > it.c0 || k > 0) ? 1u : 0u);
+              tc::mma_f16_ts(d, ahi, blo, idesc, 1u);
+              tc::mma_f16_ts(d, alo, bhi, idesc, 1u);
             }
           }
-          tc::mma_commit(&op_empty[os]);  // the stage is free once these MMAs finish
+          // the operand stages are free once these MMAs finish
+          tc::mma_commit(&a_empty[as]);
+          tc::mma_commit(&x_empty[xs_]);
         }
         if (!ok) break;
         tc::mma_commit(&acc_full[buf]);
@@ -474,62 +542,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_landed(&mma_done, 0u);
     }
   } else if (warp >= kFirstDeqWarp) {  // ------------------------------- dequant
-    const int t = threadIdx.x - kFirstDeqWarp * 32;  // tile row
-    const int half = t / kHalfRows, rr = t % kHalfRows;
-    const int nb = p.kp / 32;
+    // one weight row per thread: half (0: warps 6-9, 1: warps 10-13), TMEM
+    // lane quarter warp % 4
+    const int half = (warp - kFirstDeqWarp) / 4, quarter = warp & 3;
+    const int t = half * kHalfRows + 32 * quarter + lane;  // tile row
+    const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
     int g = 0;
     for (int w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x) {
       const Item it = item_of(p, w);
       const int row = it.tile * kTileRows + t;
       const bool ok = row < p.n;
       const float inv = ok ? __frcp_rn(__ldg(p.cs + row)) : 0.0f;
-      const uint16_t* drow = p.d + (size_t)(ok ? row : 0) * nb;
-      auto scales = [&](int c) -> uint32_t {  // blocks 2c, 2c+1 of this row
-        if (!ok || c >= it.c1) return 0u;
-        const uint32_t a = __ldg(drow + 2 * c);
-        const uint32_t b = 2 * c + 1 < nb ? (uint32_t)__ldg(drow + 2 * c + 1) : 0u;
-        return a | (b << 16);
-      };
-      uint32_t sc0 = scales(it.c0), sc1 = scales(it.c0 + 1), sc2 = scales(it.c0 + 2),
-               sc3 = scales(it.c0 + 3);
       bool okw = true;
       for (int c = it.c0; c < it.c1; ++c, ++g) {
-        const uint32_t s2 = sc0;
-        sc0 = sc1;
-        sc1 = sc2;
-        sc2 = sc3;
-        sc3 = scales(c + 4);
-        const int rs_ = g % kRawStages, os = g % kOpStages;
-        if (!wait(&raw_full[rs_], (uint32_t)((g / kRawStages) & 1), &abort_flag) ||
-            (g >= kOpStages &&
-             !wait(&op_empty[os], (uint32_t)((g / kOpStages - 1) & 1), &abort_flag))) {
+        const int rs_ = g % kRawStages, as = g % kAStages;
+        if (!wait(&raw_full[rs_], (uint32_t)((g / kRawStages) & 1), &abort_flag)) {
           okw = false;
           break;
         }
-        const unsigned char* src = raws + (size_t)rs_ * raw_stage_bytes<QT>() + (size_t)t * RB;
-        unsigned char* st = ops + (size_t)os * kOpStageBytes;
-        unsigned char* whi = st + half * kWHalfBytes;
-        unsigned char* wlo = st + kWPlaneBytes + half * kWHalfBytes;
-        const __half2 s_a = block_scale(s2 & 0xffffu, inv), s_b = block_scale(s2 >> 16, inv);
+        const unsigned char* stage = raws + (size_t)rs_ * raw_stage_bytes<QT>();
+        const uint4* q = reinterpret_cast<const uint4*>(stage + (size_t)t * RB);
+        const uint16_t* sr = reinterpret_cast<const uint16_t*>(stage + raw_scale_off<QT>() + t * 16);
+        uint4 qv[RB / 16];
+#pragma unroll
+        for (int i = 0; i < RB / 16; ++i) qv[i] = q[i];
+        const __half2 s_a = block_scale(sr[(2 * c) & 7], inv),
+                      s_b = block_scale(sr[(2 * c + 1) & 7], inv);
+        uint32_t hv[32], lv[32];
         if constexpr (QT == DQMK_Q80) {
-          const uint4* q = reinterpret_cast<const uint4*>(src);
-          const uint4 q0 = q[0], q1 = q[1], q2 = q[2], q3 = q[3];
-          dequant_q8_16(q0, s_a, whi, wlo, rr, 0);
-          dequant_q8_16(q1, s_a, whi, wlo, rr, 2);
-          dequant_q8_16(q2, s_b, whi, wlo, rr, 4);
-          dequant_q8_16(q3, s_b, whi, wlo, rr, 6);
+          dequant_q8_16(qv[0], s_a, hv, lv);
+          dequant_q8_16(qv[1], s_a, hv + 8, lv + 8);
+          dequant_q8_16(qv[2], s_b, hv + 16, lv + 16);
+          dequant_q8_16(qv[3], s_b, hv + 24, lv + 24);
         } else {
-          const uint4* q = reinterpret_cast<const uint4*>(src);
-          const uint4 q0 = q[0], q1 = q[1];
-          dequant_q4_block(q0, s_a, whi, wlo, rr, 0);
-          dequant_q4_block(q1, s_b, whi, wlo, rr, 4);
+          dequant_q4_block(qv[0], s_a, hv, lv);
+          dequant_q4_block(qv[1], s_b, hv + 16, lv + 16);
         }
+        // The raw stage is released only once every lane's reads of it have
+        // returned (the values above depend on them) and are ordered before
+        // the next TMA write into it: a thread read followed by an async-proxy
+        // write of the same shared memory.
         tc::fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          tc::bar_arrive(&raw_empty[rs_]);
-          tc::bar_arrive(&op_full[os]);
+        if (lane == 0) tc::bar_arrive(&raw_empty[rs_]);
+        if (g >= kAStages &&
+            !wait(&a_empty[as], (uint32_t)((g / kAStages - 1) & 1), &abort_flag)) {
+          okw = false;
+          break;
         }
+        tc::tc_fence_after();
+        const uint32_t col = tmem + lane_base + kACol0 + (uint32_t)as * kAStageCols +
+                             (uint32_t)(half * 64);
+        tc::tmem_st32(col, hv);
+        tc::tmem_st32(col + 32, lv);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::bar_arrive(&a_full[as]);
       }
       if (!okw) break;
     }
@@ -537,18 +606,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - kFirstEpiWarp * 32;
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter ..
     pdl_wait();
-    for (int c = et; c < kBatchMaxCols; c += kEpiWarps * 32) {
-      const bool v = c < p.cols;
-      ci.rs[c] = v ? p.rs[c] : 0.0f;
-      ci.pos[c] = v && p.col_pos ? p.col_pos[c] : 0;
-      ci.slot[c] = v && p.col_slot ? p.col_slot[c] : 0;
-    }
+    stage_cols(p, ci, et, kEpiWarps * 32);
     asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
     int tcnt = 0;
     for (int w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x, ++tcnt) {
       const Item it = item_of(p, w);
       const int buf = tcnt % kAccBufs;
-      if (!wait(&acc_full[buf], (uint32_t)((tcnt / kAccBufs) & 1), &abort_flag)) break;
+      if (!wait(&acc_full[buf], (uint32_t)((tcnt / kAccBufs) & 1), &abort_flag, DQMK_BATCH_EPI_SLEEP)) break;
       tc::tc_fence_after();
       const bool split = p.plan.splits > 1;
       for (int h = 0; h < 2; ++h) {
@@ -556,64 +620,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cb = 0; cb < n_mma; cb += 32) {
           uint32_t r[32];
           tc::tmem_ld32(tmem + ((uint32_t)(32 * quarter) << 16) +
-                            (uint32_t)(buf * 2 * kBatchMaxCols + h * kBatchMaxCols + cb),
+                            (uint32_t)(buf * kAccCols + h * kBatchMaxCols + cb),
                         r);
           tc::tmem_wait_ld();
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (split) {
+          if (split) {  // raw sums, column-major [z][column][row]
             if (row < p.n) {
-              float4* dst = reinterpret_cast<float4*>(
-                  p.partial + ((size_t)it.z * p.n + row) * kBatchMaxCols + cb);
+              float* dst = p.partial + ((size_t)it.z * kBatchMaxCols + cb) * p.n + row;
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
-                __stcg(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+              for (int j = 0; j < 32; ++j) __stcg(dst + (size_t)j * p.n, v[j]);
             }
           } else {
-            finish(p, ci, row, cb, v);
+            finish<32>(p, ci, row, cb, v);
           }
         }
       }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::bar_arrive(&acc_empty[buf]);
-      if (split) {
-        // this warp's rows of the tile are complete in every split once the
-        // quarter's ticket reaches splits; the last arrival adds them in
-        // split order (no cross-warp barrier after a bounded wait)
-        __threadfence();
-        unsigned int done = 0;
-        unsigned int* ticket = p.tickets + (size_t)it.tile * 4 + quarter;
-        if (lane == 0) done = atomicAdd(ticket, 1u);
-        done = __shfl_sync(0xffffffffu, done, 0);
-        if (done == (unsigned int)p.plan.splits - 1) {
-          __threadfence();
-          for (int h = 0; h < 2; ++h) {
-            const int row = it.tile * kTileRows + h * kHalfRows + 32 * quarter + lane;
-            const int rowc = row < p.n ? row : p.n - 1;
-            for (int cb = 0; cb < n_mma; cb += 32) {
-              float v[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-              for (int z = 0; z < p.plan.splits; ++z) {
-                const float4* src = reinterpret_cast<const float4*>(
-                    p.partial + ((size_t)z * p.n + rowc) * kBatchMaxCols + cb);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float4 a = __ldcg(src + j);
-                  v[4 * j] = __fadd_rn(v[4 * j], a.x);
-                  v[4 * j + 1] = __fadd_rn(v[4 * j + 1], a.y);
-                  v[4 * j + 2] = __fadd_rn(v[4 * j + 2], a.z);
-                  v[4 * j + 3] = __fadd_rn(v[4 * j + 3], a.w);
-                }
-              }
-              finish(p, ci, row, cb, v);
-            }
-          }
-          if (lane == 0) *ticket = 0u;
-        }
-      }
     }
   }
   tc::tc_fence_before();
@@ -752,16 +778,23 @@ cudaError_t batch_prepare() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attention_cols_kernel<128>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  // the attention CTAs are small: let as many share an SM as registers allow
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_cols_kernel<64>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_cols_kernel<128>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e == cudaSuccess) done = true;
   return e;
 }
 
-cudaError_t launch_batch_gemm(const CUtensorMap& wq, const CUtensorMap& xhi,
-                              const CUtensorMap& xlo, const BatchGemm& p, cudaStream_t s,
-                              bool pdl) {
+cudaError_t launch_batch_gemm(const CUtensorMap& wq, const CUtensorMap& wd,
+                              const CUtensorMap& xhi, const CUtensorMap& xlo, const BatchGemm& p,
+                              cudaStream_t s, bool pdl) {
   if (p.cols < 1 || p.cols > kBatchMaxCols || p.n < 1 || p.kp < 32 || p.kp % 32 != 0 ||
       p.plan.splits < 1 || p.plan.kb_per < 2 || p.plan.kb_per % 2 != 0 || !p.rs || !p.cs ||
-      !p.d || (p.plan.splits > 1 && (!p.partial || !p.tickets)))
+      !p.d || (p.plan.splits > 1 && !p.partial))
     return cudaErrorInvalidValue;
   if ((p.epi == kEpiSwiGlu || p.epi == kEpiQkv) && (p.n % 2 != 0)) return cudaErrorInvalidValue;
   if (p.epi == kEpiLogits && !p.keys) return cudaErrorInvalidValue;
@@ -771,12 +804,32 @@ cudaError_t launch_batch_gemm(const CUtensorMap& wq, const CUtensorMap& xhi,
   const int items = batch_row_tiles(p.n) * p.plan.splits;
   const dim3 grid(std::min(items, sm_count()));
   if (p.qtype == DQMK_Q80)
-    return launch(batch_gemm_kernel<DQMK_Q80>, grid, dim3(kThreads), gemm_smem<DQMK_Q80>(), s,
-                  pdl, wq, xhi, xlo, p);
-  if (p.qtype == DQMK_Q40)
-    return launch(batch_gemm_kernel<DQMK_Q40>, grid, dim3(kThreads), gemm_smem<DQMK_Q40>(), s,
-                  pdl, wq, xhi, xlo, p);
-  return cudaErrorInvalidValue;
+    e = launch(batch_gemm_kernel<DQMK_Q80>, grid, dim3(kThreads), gemm_smem<DQMK_Q80>(), s, pdl,
+               wq, wd, xhi, xlo, p);
+  else if (p.qtype == DQMK_Q40)
+    e = launch(batch_gemm_kernel<DQMK_Q40>, grid, dim3(kThreads), gemm_smem<DQMK_Q40>(), s, pdl,
+               wq, wd, xhi, xlo, p);
+  else
+    return cudaErrorInvalidValue;
+  if (e != cudaSuccess || p.plan.splits == 1) return e;
+  const dim3 rgrid((p.n + 31) / 32, (p.cols + 8 * kReduceCols - 1) / (8 * kReduceCols));
+  return launch(splitk_reduce_kernel, rgrid, dim3(256), 0, s, pdl, p);
+}
+
+int scale_pitch(int kp) { return ((kp / 32) + 7) / 8 * 8; }
+
+int make_scale_map(CUtensorMap* map, const uint16_t* d_pad, int rows, int kp) {
+  const uint64_t nbp = (uint64_t)scale_pitch(kp);
+  return make_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, d_pad, nbp, (uint64_t)rows, nbp * 2,
+                     8, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+cudaError_t copy_scales_padded(const uint16_t* d, int rows, int kp, uint16_t* d_pad,
+                               cudaStream_t s) {
+  const size_t nb = (size_t)kp / 32, nbp = (size_t)scale_pitch(kp);
+  cudaError_t e = cudaMemsetAsync(d_pad, 0, (size_t)rows * nbp * 2, s);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpy2DAsync(d_pad, nbp * 2, d, nb * 2, nb * 2, rows, cudaMemcpyDeviceToDevice, s);
 }
 
 cudaError_t launch_weight_row_scales(int qtype, const uint8_t* qs, const uint16_t* d, int rows,
@@ -786,11 +839,13 @@ cudaError_t launch_weight_row_scales(int qtype, const uint8_t* qs, const uint16_
   return cudaGetLastError();
 }
 
-// About two CTAs per SM over all (column, KV head) pairs, each split at
-// least kMinChunk positions long.
+// Splits per (column, KV head): at least two CTAs per SM over all pairs and
+// at most about 256 positions per split (many short CTAs balance across the
+// SMs; a few long ones leave a ragged last wave), each split at least
+// kMinChunk positions long.
 int batch_attention_splits(int cols, int n_kv_heads, int max_seq) {
   const int pairs = std::max(1, cols * n_kv_heads);
-  int sp = (2 * sm_count() + pairs - 1) / pairs;
+  int sp = std::max((2 * sm_count() + pairs - 1) / pairs, (max_seq + 255) / 256);
   const int by_len = (max_seq + at::kMinChunk - 1) / at::kMinChunk;
   sp = std::min(sp, by_len);
   return std::max(1, sp);
@@ -859,9 +914,9 @@ extern "C" int dqmk_linear_cols_packed(int qtype, const float* x, int cols, int 
   const size_t b_act = up((size_t)kBatchMaxCols * kp * 2), b_rs = up(kBatchMaxCols * 4);
   const size_t b_cs = up((size_t)out_features * 4);
   const size_t b_part = up(batch_partial_floats(out_features, kp) * 4);
-  const size_t b_tk = up((size_t)batch_row_tiles(out_features) * 4 * 4);
+  const size_t b_dp = up((size_t)out_features * scale_pitch(kp) * 2);
   unsigned char* scratch = nullptr;
-  const size_t total = 2 * b_act + b_rs + b_cs + b_part + b_tk + 256;
+  const size_t total = 2 * b_act + b_rs + b_cs + b_part + b_dp + 256;
   DQMK_CUDA_RET(api, cudaMallocAsync(reinterpret_cast<void**>(&scratch), total, st));
   unsigned char* cur = scratch;
   auto take = [&](size_t b) {
@@ -874,17 +929,18 @@ extern "C" int dqmk_linear_cols_packed(int qtype, const float* x, int cols, int 
   float* rs = reinterpret_cast<float*>(take(b_rs));
   float* cs = reinterpret_cast<float*>(take(b_cs));
   float* part = reinterpret_cast<float*>(take(b_part));
-  unsigned int* tickets = reinterpret_cast<unsigned int*>(take(b_tk));
+  uint16_t* d_pad = reinterpret_cast<uint16_t*>(take(b_dp));
   int rc = DQMK_OK;
   cudaError_t e = cudaSuccess;
-  CUtensorMap mw, mhi, mlo;
+  CUtensorMap mw, md, mhi, mlo;
   do {
     if ((rc = make_quant_map(&mw, qtype, qs, out_features, kp))) break;
+    if ((rc = make_scale_map(&md, d_pad, out_features, kp))) break;
     if ((rc = make_cols_map(&mhi, hi, kp))) break;
     if ((rc = make_cols_map(&mlo, lo, kp))) break;
-    // unused columns of the planes stay finite (zero); tickets start at zero
+    // unused columns of the planes stay finite (zero)
     if ((e = cudaMemsetAsync(scratch, 0, 2 * b_act + b_rs, st)) != cudaSuccess) break;
-    if ((e = cudaMemsetAsync(tickets, 0, b_tk, st)) != cudaSuccess) break;
+    if ((e = copy_scales_padded(d, out_features, kp, d_pad, st)) != cudaSuccess) break;
     if ((e = launch_weight_row_scales(qtype, qs, d, out_features, kp, cs, st)) != cudaSuccess)
       break;
     if ((e = launch_split_rows(x, cols, in_features, kp, in_features, nullptr, 0.0f, hi, lo, rs,
@@ -900,13 +956,12 @@ extern "C" int dqmk_linear_cols_packed(int qtype, const float* x, int cols, int 
     g.cs = cs;
     g.plan = plan;
     g.partial = part;
-    g.tickets = tickets;
     g.epi = kEpiStore;
     g.bias = bias;
     g.residual = residual;
     g.y = y;
     g.ldy = out_features;
-    e = launch_batch_gemm(mw, mhi, mlo, g, st, false);
+    e = launch_batch_gemm(mw, md, mhi, mlo, g, st, false);
   } while (false);
   cudaError_t ef = cudaFreeAsync(scratch, st);
   if (rc) return rc;

@@ -29,8 +29,7 @@ struct BatchGemm {
   const float* rs;        // [cols] power-of-two scales of the activation planes
   const float* cs;        // [n] power-of-two row scales of the weight (2^f)
   GemmPlan plan;          // K split; kb_per even
-  float* partial;         // plan.splits > 1: [splits][n][kBatchMaxCols] raw sums
-  unsigned int* tickets;  // plan.splits > 1: [row tiles][4 lane quarters], zero at rest
+  float* partial;         // plan.splits > 1: [splits][kBatchMaxCols][n] raw sums
   int epi;                // kEpiStore / kEpiSwiGlu / kEpiQkv / kEpiLogits
   const float* bias;      // by packed row (may be null)
   const float* residual;  // kEpiStore: [cols][ldy], may alias y
@@ -75,10 +74,17 @@ int batch_row_tiles(int n);
 int make_quant_map(CUtensorMap* map, int qtype, const uint8_t* qs, int rows, int kp);
 // Tensor map of an activation plane [kBatchMaxCols][kp] fp16.
 int make_cols_map(CUtensorMap* map, const uint16_t* plane, int kp);
+// Block scales of a weight copied into rows of scale_pitch(kp) (a multiple
+// of 8, zero-padded) so TMA can fetch them, and the tensor map of the copy.
+int scale_pitch(int kp);
+cudaError_t copy_scales_padded(const uint16_t* d, int rows, int kp, uint16_t* d_pad,
+                               cudaStream_t s);
+int make_scale_map(CUtensorMap* map, const uint16_t* d_pad, int rows, int kp);
 cudaError_t batch_prepare();
-cudaError_t launch_batch_gemm(const CUtensorMap& wq, const CUtensorMap& xhi,
-                              const CUtensorMap& xlo, const BatchGemm& p, cudaStream_t s,
-                              bool pdl);
+// The GEMM, plus the split-K reduce kernel when p.plan.splits > 1.
+cudaError_t launch_batch_gemm(const CUtensorMap& wq, const CUtensorMap& wd,
+                              const CUtensorMap& xhi, const CUtensorMap& xlo, const BatchGemm& p,
+                              cudaStream_t s, bool pdl);
 // cs[row] = 2^f with max |d q| 2^-f of the row in [2^14, 2^15) (1 for a zero row).
 cudaError_t launch_weight_row_scales(int qtype, const uint8_t* qs, const uint16_t* d, int rows,
                                      int kp, float* cs, cudaStream_t s);

@@ -43,7 +43,6 @@ struct dqmk_batch {
   uint16_t *hi = nullptr, *lo = nullptr;  // fp16 activation planes [64][kp]
   float* rs = nullptr;                    // their column scales
   float* partial = nullptr;               // GEMM split-K sums
-  unsigned int* tickets = nullptr;        // GEMM split-K tickets
   float* attn_partials = nullptr;
   unsigned int* attn_tickets = nullptr;
   int* cols = nullptr;                    // device [3][64]: slot, token, pos
@@ -85,7 +84,12 @@ int ensure_batch_weights(dqmk_model* m) {
     out->cs = static_cast<float*>(p);
     DQMK_CUDA_RET(kApi, launch_weight_row_scales(w.qtype, w.qs(), w.d(), w.rows, w.kp, out->cs,
                                                  nullptr));
-    m->memory_bytes += (size_t)w.rows * sizeof(float);
+    const size_t dp_bytes = (size_t)w.rows * scale_pitch(w.kp) * 2;
+    if ((rc = dev_alloc(m->allocs, dp_bytes, &p, kApi))) return rc;
+    out->d_pad = static_cast<uint16_t*>(p);
+    DQMK_CUDA_RET(kApi, copy_scales_padded(w.d(), w.rows, w.kp, out->d_pad, nullptr));
+    m->memory_bytes += (size_t)w.rows * sizeof(float) + dp_bytes;
+    if ((rc = make_scale_map(&out->dmap, out->d_pad, w.rows, w.kp))) return rc;
     return make_quant_map(&out->map, w.qtype, w.qs(), w.rows, w.kp);
   };
   int rc;
@@ -122,7 +126,6 @@ BatchGemm gemm_args(const dqmk_batch* b, const Packed& w, const BatchWeight& bw,
   g.cs = bw.cs;
   g.plan = plan_batch_gemm(w.rows, w.kp);
   g.partial = b->partial;
-  g.tickets = b->tickets;
   g.epi = epi;
   g.col_slot = b->cols;
   g.col_pos = b->cols + 2 * kBatchMaxCols;
@@ -165,7 +168,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     g.n_kv_heads = tp.n_kv_heads;
     g.head_dim = hd;
     g.neox = c.rope_neox;
-    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.qkv.map, b->x_dim[0], b->x_dim[1], g, s, pdl));
+    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.qkv.map, B.qkv.dmap, b->x_dim[0], b->x_dim[1], g, s, pdl));
 
     BatchAttn a = {};
     a.q = b->q;
@@ -193,7 +196,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     o.residual = tpar ? nullptr : b->x;
     o.y = tpar ? b->part : b->x;
     o.ldy = c.dim;
-    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.wo.map, b->x_qd[0], b->x_qd[1], o, s, pdl));
+    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.wo.map, B.wo.dmap, b->x_qd[0], b->x_qd[1], o, s, pdl));
     if (tpar) {  // complete the row-parallel sums, then the residual add
       if ((rc = tp_allreduce_sum(m->comm, b->part, (size_t)n * c.dim, s, kApi))) return rc;
       DQMK_CUDA_RET(kApi, launch_add(b->x, b->part, n * c.dim, b->x, s));
@@ -204,7 +207,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     BatchGemm gu = gemm_args(b, L.gate_up, B.gate_up, n, kEpiSwiGlu);
     gu.y = b->f;
     gu.ldy = tp.hidden;
-    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.gate_up.map, b->x_dim[0], b->x_dim[1], gu, s, pdl));
+    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.gate_up.map, B.gate_up.dmap, b->x_dim[0], b->x_dim[1], gu, s, pdl));
 
     DQMK_CUDA_RET(kApi, launch_split_rows(b->f, n, tp.hidden, L.down.kp, tp.hidden, nullptr, eps,
                                           b->hi, b->lo, b->rs, s));
@@ -212,7 +215,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     dn.residual = tpar ? nullptr : b->x;
     dn.y = tpar ? b->part : b->x;
     dn.ldy = c.dim;
-    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.down.map, b->x_hid[0], b->x_hid[1], dn, s, pdl));
+    DQMK_CUDA_RET(kApi, launch_batch_gemm(B.down.map, B.down.dmap, b->x_hid[0], b->x_hid[1], dn, s, pdl));
     if (tpar) {
       if ((rc = tp_allreduce_sum(m->comm, b->part, (size_t)n * c.dim, s, kApi))) return rc;
       DQMK_CUDA_RET(kApi, launch_add(b->x, b->part, n * c.dim, b->x, s));
@@ -225,7 +228,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
   lg.ldy = tp.vocab_stride;
   lg.keys = b->keys_arg;
   lg.row_offset = tp.vocab0;
-  DQMK_CUDA_RET(kApi, launch_batch_gemm(m->batch_lm.map, b->x_dim[0], b->x_dim[1], lg, s, pdl));
+  DQMK_CUDA_RET(kApi, launch_batch_gemm(m->batch_lm.map, m->batch_lm.dmap, b->x_dim[0], b->x_dim[1], lg, s, pdl));
   if (tpar && (rc = tp_allreduce_max_u64(m->comm, b->keys_arg, n, s, kApi))) return rc;
   DQMK_CUDA_RET(kApi, launch_cols_advance(b->keys_arg, n, b->col_slot(), b->col_token(),
                                           b->col_pos(), b->history, b->max_seq, s, false));
@@ -325,12 +328,8 @@ extern "C" int dqmk_batch_create(dqmk_model* m, int n_slots, int max_seq, dqmk_b
   const int kp_dim = L0.qkv.kp, kp_qd = L0.wo.kp, kp_hid = L0.down.kp;
   const int kp_max = std::max(std::max(kp_dim, kp_qd), std::max(kp_hid, m->lm_head.kp));
   size_t part = 0;
-  int max_tiles = 0;
   const Packed* weights[] = {&L0.qkv, &L0.wo, &L0.gate_up, &L0.down, &m->lm_head};
-  for (const Packed* w : weights) {
-    part = std::max(part, batch_partial_floats(w->rows, w->kp));
-    max_tiles = std::max(max_tiles, batch_row_tiles(w->rows));
-  }
+  for (const Packed* w : weights) part = std::max(part, batch_partial_floats(w->rows, w->kp));
   size_t attn = 0;
   for (int n = 1; n <= kBatchMaxCols; ++n)
     attn = std::max(attn, batch_attention_partials_floats(
@@ -352,7 +351,6 @@ extern "C" int dqmk_batch_create(dqmk_model* m, int n_slots, int max_seq, dqmk_b
               {(void**)&b->lo, C * kp_max * 2},
               {(void**)&b->rs, C * sizeof(float)},
               {(void**)&b->partial, part * sizeof(float)},
-              {(void**)&b->tickets, (size_t)max_tiles * 4 * sizeof(unsigned int)},
               {(void**)&b->attn_partials, attn * sizeof(float)},
               {(void**)&b->attn_tickets, C * tp.n_kv_heads * sizeof(unsigned int)},
               {(void**)&b->cols, 3 * C * sizeof(int)},

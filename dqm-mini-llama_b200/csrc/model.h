@@ -46,11 +46,12 @@ struct Layer {
 };
 
 // Weight-side tables of the multi-sequence decode GEMM (batch.cu), built on
-// the first batch: per weight its power-of-two row scales and the tensor map
-// of its quant plane.
+// the first batch: per weight its power-of-two row scales, a copy of its block
+// scales in 16-byte-padded rows, and the tensor maps of both planes.
 struct BatchWeight {
   float* cs = nullptr;
-  CUtensorMap map;
+  uint16_t* d_pad = nullptr;  // block scales in 16-byte-padded rows
+  CUtensorMap map, dmap;      // quant plane, padded scales
 };
 struct BatchLayer {
   BatchWeight qkv, wo, gate_up, down;

@@ -44,9 +44,11 @@ __device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for phase `parity`; gives up early once another role of the
-// CTA has aborted, and on running out sets *abort and bit 0 of *err.
+// CTA has aborted, and on running out sets *abort and bit 0 of *err.  A
+// nonzero sleep_ns backs off between polls (for waits expected to be long, so
+// the polling warp leaves the issue slots to the warps doing the work).
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
-                                         unsigned int* err) {
+                                         unsigned int* err, unsigned sleep_ns = 0) {
   if (bar_try(b, parity)) return true;
   const unsigned long long t0 = now_ns();
   while (true) {
@@ -57,6 +59,7 @@ __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, volatile 
       atomicOr(err, 1u);
       return false;
     }
+    if (sleep_ns) __nanosleep(sleep_ns);
   }
 }
 
@@ -105,6 +108,17 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b,
       ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
+// A operand from tensor memory (M rows on the TMEM lanes, K along the
+// columns, two fp16 values per 32-bit column), B from shared memory.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                           uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
 // Arrives on the mbarrier once every prior tcgen05 operation of this thread
 // has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -144,6 +158,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// 32 consecutive TMEM columns of this warp's 32 lanes from registers.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 }  // namespace tc
