@@ -67,7 +67,7 @@ constexpr int kChunkK = 64;                                // K values per stage
 #define DQMK_BATCH_EPI_SLEEP 128
 #endif
 constexpr int kRawStages = DQMK_BATCH_RAW_STAGES;          // quant tiles (shared memory)
-constexpr int kXStages = 4;                                // activation tiles (shared memory)
+constexpr int kXStages = 8;                                // activation tiles (shared memory)
 constexpr int kAStages = DQMK_BATCH_A_STAGES;              // weight operand tiles (TMEM)
 constexpr int kXPlaneBytes = kBatchMaxCols * kChunkK * 2;  // 8 KB
 constexpr int kXStageBytes = 2 * kXPlaneBytes;             // hi + lo
@@ -465,27 +465,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       // weight tiles do not depend on the previous kernel: start them first
       while (rw.valid && gr < kRawStages) issue_raw();
       pdl_wait();
-      while (xw.valid && !abort_flag) {
-        bool ok = true;
-        while (rw.valid && gr < gx + kRawStages) {
-          if (!wait(&raw_empty[gr % kRawStages], (uint32_t)((gr / kRawStages - 1) & 1),
-                    &abort_flag)) {
-            ok = false;
-            break;
-          }
+      // Both rings are kept as full as their consumers allow, independently:
+      // the activation tiles (the same for every CTA, so slow to arrive from
+      // L2) run up to kXStages chunks ahead of the MMA, the quant tiles
+      // kRawStages ahead of the dequant warps.  Non-blocking polls; no
+      // progress for about a second records the timeout and unwinds.
+      unsigned long long idle_since = 0;
+      while ((rw.valid || xw.valid) && !abort_flag) {
+        bool progressed = false;
+        if (rw.valid && tc::bar_try(&raw_empty[gr % kRawStages],
+                                    (uint32_t)((gr / kRawStages - 1) & 1))) {
           issue_raw();
+          progressed = true;
         }
-        if (!ok) break;
-        const int xs_ = gx % kXStages;
-        if (gx >= kXStages &&
-            !wait(&x_empty[xs_], (uint32_t)((gx / kXStages - 1) & 1), &abort_flag))
-          break;
-        unsigned char* st = xs + (size_t)xs_ * kXStageBytes;
-        tc::bar_expect_tx(&x_full[xs_], (uint32_t)kXStageBytes);
-        tc::tma_load_2d(st, &map_xhi, xw.c * kChunkK, 0, &x_full[xs_]);
-        tc::tma_load_2d(st + kXPlaneBytes, &map_xlo, xw.c * kChunkK, 0, &x_full[xs_]);
-        xw.next(p);
-        ++gx;
+        if (xw.valid && (gx < kXStages || tc::bar_try(&x_empty[gx % kXStages],
+                                                      (uint32_t)((gx / kXStages - 1) & 1)))) {
+          const int xs_ = gx % kXStages;
+          unsigned char* st = xs + (size_t)xs_ * kXStageBytes;
+          tc::bar_expect_tx(&x_full[xs_], (uint32_t)kXStageBytes);
+          tc::tma_load_2d(st, &map_xhi, xw.c * kChunkK, 0, &x_full[xs_]);
+          tc::tma_load_2d(st + kXPlaneBytes, &map_xlo, xw.c * kChunkK, 0, &x_full[xs_]);
+          xw.next(p);
+          ++gx;
+          progressed = true;
+        }
+        if (progressed) {
+          idle_since = 0;
+        } else if (idle_since == 0) {
+          idle_since = tc::now_ns();
+        } else if (tc::now_ns() - idle_since > tc::kWaitNs) {
+          abort_flag = 1;
+          atomicOr(&g_batch_error, 1u);
+        }
       }
       if (abort_flag) {  // let this thread's copies in flight land before exit
         for (int g = gr - kRawStages < 0 ? 0 : gr - kRawStages; g < gr; ++g)
@@ -494,53 +505,61 @@ __global__ void __launch_bounds__(kThreads, 1)
           wait_landed(&x_full[g % kXStages], (uint32_t)((g / kXStages) & 1));
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {  // ----------------------------------------------- MMA issue
-      const uint32_t idesc = tc::idesc_f16(kHalfRows, n_mma);
-      int g = 0, tcnt = 0;
-      for (int w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x, ++tcnt) {
-        const Item it = item_of(p, w);
-        const int buf = tcnt % kAccBufs;
-        if (tcnt >= kAccBufs &&
-            !wait(&acc_empty[buf], (uint32_t)((tcnt / kAccBufs - 1) & 1), &abort_flag))
-          break;
+  } else if (warp == 1) {  // ------------------------------------------ MMA issue
+    // The whole warp runs the loop (operands stay warp-uniform); one elected
+    // lane issues the tcgen05 instructions; every wait decision is voted so
+    // the warp stays converged.
+    const uint32_t idesc = tc::idesc_f16(kHalfRows, n_mma);
+    int g = 0, tcnt = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++tcnt) {
+      const Item it = item_of(p, w);
+      const int buf = tcnt % kAccBufs;
+      if (tcnt >= kAccBufs)
+        ok = __all_sync(0xffffffffu,
+                        wait(&acc_empty[buf], (uint32_t)((tcnt / kAccBufs - 1) & 1), &abort_flag));
+      if (!ok) break;
+      tc::tc_fence_after();
+      const uint32_t dacc = tmem + (uint32_t)(buf * kAccCols);
+      for (int c = it.c0; c < it.c1; ++c, ++g) {
+        const int as = g % kAStages, xs_ = g % kXStages;
+        ok = __all_sync(0xffffffffu,
+                        wait(&a_full[as], (uint32_t)((g / kAStages) & 1), &abort_flag) &&
+                            wait(&x_full[xs_], (uint32_t)((g / kXStages) & 1), &abort_flag));
+        if (!ok) break;
         tc::tc_fence_after();
-        bool ok = true;
-        for (int c = it.c0; c < it.c1; ++c, ++g) {
-          const int as = g % kAStages, xs_ = g % kXStages;
-          if (!wait(&a_full[as], (uint32_t)((g / kAStages) & 1), &abort_flag) ||
-              !wait(&x_full[xs_], (uint32_t)((g / kXStages) & 1), &abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc::tc_fence_after();
-          const uint32_t xhi = tc::su32(xs + (size_t)xs_ * kXStageBytes);
-          const uint32_t xlo = xhi + kXPlaneBytes;
-          const uint32_t acol = tmem + kACol0 + (uint32_t)as * kAStageCols;
+        const uint64_t bhi0 = tc::smem_desc(tc::su32(xs + (size_t)xs_ * kXStageBytes));
+        const uint64_t blo0 = tc::smem_desc(tc::su32(xs + (size_t)xs_ * kXStageBytes + kXPlaneBytes));
+        const uint32_t acol = tmem + kACol0 + (uint32_t)as * kAStageCols;
+        const uint32_t first = c > it.c0 ? 1u : 0u;
+        if (tc::elect_one()) {
 #pragma unroll
           for (int k = 0; k < kChunkK / 16; ++k) {
-            const uint64_t bhi = tc::smem_desc(xhi + 32 * k), blo = tc::smem_desc(xlo + 32 * k);
+            // a K=16 slice is 32 bytes further: +2 in the descriptor's address field
+            const uint64_t bhi = bhi0 + 2u * k, blo = blo0 + 2u * k;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const uint32_t d = tmem + (uint32_t)(buf * kAccCols + h * kBatchMaxCols);
+              const uint32_t d = dacc + (uint32_t)(h * kBatchMaxCols);
               const uint32_t ahi = acol + (uint32_t)(h * 64 + 8 * k);
-              const uint32_t alo = ahi + 32;
-              tc::mma_f16_ts(d, ahi, bhi, idesc, (c > it.c0 || k > 0) ? 1u : 0u);
+              tc::mma_f16_ts(d, ahi, bhi, idesc, k > 0 ? 1u : first);
               tc::mma_f16_ts(d, ahi, blo, idesc, 1u);
-              tc::mma_f16_ts(d, alo, bhi, idesc, 1u);
+              tc::mma_f16_ts(d, ahi + 32, bhi, idesc, 1u);
             }
           }
           // the operand stages are free once these MMAs finish
           tc::mma_commit(&a_empty[as]);
           tc::mma_commit(&x_empty[xs_]);
         }
-        if (!ok) break;
-        tc::mma_commit(&acc_full[buf]);
+        __syncwarp();
       }
-      // every MMA this thread issued has finished before TMEM is freed
-      tc::mma_commit(&mma_done);
-      wait_landed(&mma_done, 0u);
+      if (!ok) break;
+      if (tc::elect_one()) tc::mma_commit(&acc_full[buf]);
+      __syncwarp();
     }
+    // every MMA this warp issued has finished before TMEM is freed
+    if (tc::elect_one()) tc::mma_commit(&mma_done);
+    __syncwarp();
+    wait_landed(&mma_done, 0u);
   } else if (warp >= kFirstDeqWarp) {  // ------------------------------- dequant
     // one weight row per thread: half (0: warps 6-9, 1: warps 10-13), TMEM
     // lane quarter warp % 4

@@ -63,6 +63,18 @@ __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, volatile 
   }
 }
 
+// One lane of a converged warp (elect.sync): issue tcgen05 instructions from
+// warp-uniform operands under it.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
   asm volatile(
