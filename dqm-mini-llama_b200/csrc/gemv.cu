@@ -20,10 +20,13 @@
 // y[j] = sum_k (d*q_k) * x_k as one sequential FMA chain in k.  Here the sum
 // is split across lanes and the scale is applied per block, so results agree
 // to float rounding (checked against the oracle), not bit for bit.
+#include <algorithm>
+
 #include "common.cuh"
 #include "gemv_dev.cuh"
 #include "internal.h"
 #include "prefill.h"
+#include "tc_dev.cuh"
 
 namespace dqmk {
 namespace {
@@ -96,20 +99,15 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t stream, bool pdl) {
 // Every wait on a stage is bounded (about a second of %globaltimer); on
 // timeout the CTA records DQMK_ERR_TIMEOUT in a device flag, stops issuing,
 // waits (bounded) for its copies still in flight, and exits.
-constexpr int kTmaWarps = 8;
-constexpr int kTmaThreads = kTmaWarps * 32;
+constexpr int kTmaWarps = 8;                        // consumer warps
+constexpr int kTmaConsumers = kTmaWarps * 32;
+constexpr int kTmaThreads = kTmaConsumers + 32;     // + the producer warp
 constexpr int kMaxStages = 4;
-constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 
 __device__ unsigned int g_device_error;  // bit 0: a bounded wait timed out
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
@@ -119,26 +117,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
-// true when the phase completed, false after kWaitLimitNs
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
-  if (mbar_try_wait(bar, phase)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (true) {
-    if (mbar_try_wait(bar, phase)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-  }
 }
 __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t p;
@@ -191,11 +169,13 @@ __device__ __forceinline__ void stage_x_linear(const GemvArgs& a, float* xf, con
                                                bool norm_pref, float* red, float* bcast) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   constexpr int NT = NWARPS * 32;
+  const bool active = tid < NT;  // threads beyond NT only join the barriers
   const int nf4 = a.kp >> 2;
   const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.k & 3) == 0);
   float4* xf4 = reinterpret_cast<float4*>(xf);
   float ss = 0.0f;
-  if (vec) {
+  if (!active) {
+  } else if (vec) {
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     const int k4 = a.k >> 2;
     for (int base = 0; base < nf4; base += 8 * NT) {
@@ -226,7 +206,7 @@ __device__ __forceinline__ void stage_x_linear(const GemvArgs& a, float* xf, con
   }
   if (a.norm_w) {
     ss = warp_sum(ss);
-    if (lane == 0) red[wid] = ss;
+    if (lane == 0 && active) red[wid] = ss;
     __syncthreads();
     if (tid == 0) {
       float t = 0.0f;
@@ -235,7 +215,8 @@ __device__ __forceinline__ void stage_x_linear(const GemvArgs& a, float* xf, con
     }
     __syncthreads();
     const float scale = *bcast;
-    if (vec && norm_pref) {
+    if (!active) {
+    } else if (vec && norm_pref) {
 #pragma unroll
       for (int u = 0; u < NR; ++u) {
         const int i4 = u * NT + tid;
@@ -325,19 +306,33 @@ __host__ __device__ __forceinline__ XLayout x_layout(int kp) {
   return l;
 }
 
+// Warp roles: warps 0..kTmaWarps-1 consume row tiles, warp kTmaWarps (one
+// lane) keeps the ring full.  Each stage has a "full" mbarrier (the copies'
+// bytes) and an "empty" one (one arrival per consumer warp), so a consumer
+// warp moves on to the next tile as soon as its own rows are done and the
+// producer refills a stage as soon as the last warp has left it -- no
+// CTA-wide barrier inside the tile loop.  When x has at most 32 blocks (K <=
+// 1024, the lm_head) lane b keeps block b's three int8 terms in registers
+// for the whole kernel.  The arithmetic (and its order) is per lane and per
+// row exactly that of the per-tile loop, so results do not depend on the
+// schedule.  Every wait is bounded; a wait that runs out sets the device
+// error flag and the CTA's abort flag, every role leaves its loop, and the
+// producer lets the copies it issued land before the CTA exits.
 template <int QT, int RPW>
 __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a, int nstage,
                                                               int skip_tile) {
   constexpr int TR = kTmaWarps * RPW;
-  constexpr int NR = 4;  // float4 of RMSNorm weight prefetched per thread
+  constexpr int NR = 4;  // float4 of RMSNorm weight prefetched per consumer thread
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages];
+  __shared__ __align__(8) uint64_t empty[kMaxStages];
   __shared__ float red[kTmaWarps];
   __shared__ float bcast;
   __shared__ unsigned long long best_w[kTmaWarps];
-  __shared__ int s_err;
+  __shared__ int s_abort;
 
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const bool producer = wid == kTmaWarps;
   TmaGeo g;
   g.chunks = a.kp / Fmt<QT>::kElems;
   g.row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
@@ -354,27 +349,35 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
   float* xsc = reinterpret_cast<float*>(smem + xl.sc);
   int* xsum = reinterpret_cast<int*>(smem + xl.sum);
   unsigned char* stages = smem + xl.stages;
-  const uint64_t policy = evict_first_policy();
+  volatile int* abort = &s_abort;
 
-  if (tid == 0) {
-    for (int s = 0; s < nstage; ++s) mbar_init(&full[s], 1);
+  if (producer && lane == 0) {
+    for (int s = 0; s < nstage; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTmaWarps);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    s_err = 0;
+    s_abort = 0;
   }
   __syncthreads();
-  unsigned pending = 0;  // stages with a copy in flight (thread 0's bookkeeping)
-  if (tid == 0) {
+  // producer bookkeeping (lane 0 of the producer warp): last tile issued into
+  // each stage, -1 for none
+  __shared__ int last_issued[kMaxStages];
+  uint64_t policy = 0;
+  if (producer && lane == 0) {
+    for (int s = 0; s < kMaxStages; ++s) last_issued[s] = -1;
+    policy = evict_first_policy();
     const int pre = min(nstage, g.my_tiles);
     for (int i = 0; i < pre; ++i)
-      if (tma_issue<QT, RPW>(a, g, stages, full, i, i, policy, skip_tile)) pending |= 1u << i;
+      if (tma_issue<QT, RPW>(a, g, stages, full, i, i, policy, skip_tile)) last_issued[i] = i;
   }
   float4 nw[NR];
-  const bool norm_pref = a.norm_w && (a.kp >> 2) <= NR * kTmaThreads && ((a.k & 3) == 0) &&
+  const bool norm_pref = a.norm_w && (a.kp >> 2) <= NR * kTmaConsumers && ((a.k & 3) == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.norm_w) & 15u) == 0);
-  if (norm_pref) {
+  if (norm_pref && !producer) {
 #pragma unroll
     for (int u = 0; u < NR; ++u) {
-      const int i4 = u * kTmaThreads + tid;
+      const int i4 = u * kTmaConsumers + tid;
       nw[u] = i4 < (a.k >> 2) ? __ldg(reinterpret_cast<const float4*>(a.norm_w) + i4)
                               : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -382,119 +385,141 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
   pdl_trigger();
   pdl_wait();
 
+  // x staging by the consumer threads; the producer warp only joins the
+  // CTA barriers inside
   stage_x_linear<kTmaWarps, NR>(a, xf, nw, norm_pref, red, &bcast);
-  quantize_x_terms<kTmaWarps, QT == DQMK_Q40>(xf, g.nbk, xq, xsc, xsum);
+  if (!producer) quantize_x_terms<kTmaWarps, QT == DQMK_Q40>(xf, g.nbk, xq, xsc, xsum);
   __syncthreads();
 
-  int pos = 0;
-  if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
   unsigned long long best = 0ull;
-  int consumed = 0;
-  const int4* xq4 = reinterpret_cast<const int4*>(xq);
-  for (int i = 0; i < g.my_tiles; ++i) {
-    const int s = i % nstage;
-    const uint32_t phase = (uint32_t)(i / nstage) & 1u;
-    if (!mbar_wait_bounded(&full[s], phase)) s_err = 1;
-    __syncthreads();
-    if (s_err) break;
-    consumed = i + 1;
-    const int tile = blockIdx.x + i * gridDim.x;
-    const int r0 = tile * TR;
-    const int rows = min(TR, a.n_rows - r0);
-    const bool d_smem = (((uint32_t)rows * g.nbk * 2) & 15u) == 0;
-    const unsigned char* sq = stages + (size_t)s * g.stage_bytes;
-    const uint16_t* sd = reinterpret_cast<const uint16_t*>(sq + g.q_stage);
-    float acc[RPW];
+  if (producer) {
+    if (lane == 0) {
+      for (int i = nstage; i < g.my_tiles; ++i) {
+        const int s = i % nstage;
+        const uint32_t parity = (uint32_t)(i / nstage - 1) & 1u;
+        if (!tc::bar_wait(&empty[s], parity, abort, &g_device_error, 32)) break;
+        if (tma_issue<QT, RPW>(a, g, stages, full, i, s, policy, skip_tile)) last_issued[s] = i;
+      }
+    }
+    __syncwarp();
+  } else {
+    int pos = 0;
+    if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+    const int4* xq4 = reinterpret_cast<const int4*>(xq);
+    const bool xreg = g.nbk <= 32;
+    int4 xv[6];  // [term][half] of block `lane` when xreg
+    float sc[3];
+    int sm8[3];
+    if (xreg && lane < g.nbk) {
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
-    for (int b = lane; b < g.nbk; b += 32) {
-      int4 xv[6];  // [term][half]
-#pragma unroll
-      for (int t = 0; t < 6; ++t) xv[t] = xq4[(size_t)t * g.nbk + b];
-      float sc[3];
-      int sm8[3];
+      for (int t = 0; t < 6; ++t) xv[t] = xq4[(size_t)t * g.nbk + lane];
 #pragma unroll
       for (int t = 0; t < 3; ++t) {
-        sc[t] = xsc[t * g.nbk + b];
-        sm8[t] = QT == DQMK_Q40 ? 8 * xsum[t * g.nbk + b] : 0;
+        sc[t] = xsc[t * g.nbk + lane];
+        sm8[t] = QT == DQMK_Q40 ? 8 * xsum[t * g.nbk + lane] : 0;
       }
+    }
+    for (int i = 0; i < g.my_tiles; ++i) {
+      const int s = i % nstage;
+      const uint32_t phase = (uint32_t)(i / nstage) & 1u;
+      const bool ok = tc::bar_wait(&full[s], phase, abort, &g_device_error);
+      if (!__all_sync(0xffffffffu, ok)) {
+        *abort = 1;
+        break;
+      }
+      const int tile = blockIdx.x + i * gridDim.x;
+      const int r0 = tile * TR;
+      const int rows = min(TR, a.n_rows - r0);
+      const bool d_smem = (((uint32_t)rows * g.nbk * 2) & 15u) == 0;
+      const unsigned char* sq = stages + (size_t)s * g.stage_bytes;
+      const uint16_t* sd = reinterpret_cast<const uint16_t*>(sq + g.q_stage);
+      float acc[RPW];
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        const int rl = wid * RPW + r;
-        if (rl < rows) {
-          const unsigned char* wrow = sq + (size_t)rl * g.row_bytes;
-          int w[8];
-          if constexpr (QT == DQMK_Q80) {
-            const uint4 w0 = *reinterpret_cast<const uint4*>(wrow + b * 32);
-            const uint4 w1 = *reinterpret_cast<const uint4*>(wrow + b * 32 + 16);
-            w[0] = (int)w0.x; w[1] = (int)w0.y; w[2] = (int)w0.z; w[3] = (int)w0.w;
-            w[4] = (int)w1.x; w[5] = (int)w1.y; w[6] = (int)w1.z; w[7] = (int)w1.w;
-          } else {
-            const uint4 p = *reinterpret_cast<const uint4*>(wrow + b * 16);
-            const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+      for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
+      for (int b = lane; b < g.nbk; b += 32) {
+        if (!xreg) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              w[j] = (int)(pw[j] & 0x0f0f0f0fu);             // values 4j..4j+3
-              w[4 + j] = (int)((pw[j] >> 4) & 0x0f0f0f0fu);  // values 16+4j..
-            }
-          }
-          float blk = 0.0f;
+          for (int t = 0; t < 6; ++t) xv[t] = xq4[(size_t)t * g.nbk + b];
 #pragma unroll
           for (int t = 0; t < 3; ++t) {
-            const int4 lo = xv[t * 2], hi = xv[t * 2 + 1];
-            int S = __dp4a(w[0], lo.x, 0);
-            S = __dp4a(w[1], lo.y, S);
-            S = __dp4a(w[2], lo.z, S);
-            S = __dp4a(w[3], lo.w, S);
-            S = __dp4a(w[4], hi.x, S);
-            S = __dp4a(w[5], hi.y, S);
-            S = __dp4a(w[6], hi.z, S);
-            S = __dp4a(w[7], hi.w, S);
-            blk = __fmaf_rn(sc[t], (float)(S - sm8[t]), blk);
+            sc[t] = xsc[t * g.nbk + b];
+            sm8[t] = QT == DQMK_Q40 ? 8 * xsum[t * g.nbk + b] : 0;
           }
-          const uint16_t dv =
-              d_smem ? sd[rl * g.nbk + b] : __ldg(a.d + (size_t)(r0 + rl) * g.nbk + b);
-          acc[r] = __fmaf_rn(h2f(dv), blk, acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          const int rl = wid * RPW + r;
+          if (rl < rows) {
+            const unsigned char* wrow = sq + (size_t)rl * g.row_bytes;
+            int w[8];
+            if constexpr (QT == DQMK_Q80) {
+              const uint4 w0 = *reinterpret_cast<const uint4*>(wrow + b * 32);
+              const uint4 w1 = *reinterpret_cast<const uint4*>(wrow + b * 32 + 16);
+              w[0] = (int)w0.x; w[1] = (int)w0.y; w[2] = (int)w0.z; w[3] = (int)w0.w;
+              w[4] = (int)w1.x; w[5] = (int)w1.y; w[6] = (int)w1.z; w[7] = (int)w1.w;
+            } else {
+              const uint4 p = *reinterpret_cast<const uint4*>(wrow + b * 16);
+              const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                w[j] = (int)(pw[j] & 0x0f0f0f0fu);             // values 4j..4j+3
+                w[4 + j] = (int)((pw[j] >> 4) & 0x0f0f0f0fu);  // values 16+4j..
+              }
+            }
+            const uint16_t dv =
+                d_smem ? sd[rl * g.nbk + b] : __ldg(a.d + (size_t)(r0 + rl) * g.nbk + b);
+            float blk = 0.0f;
+#pragma unroll
+            for (int t = 0; t < 3; ++t) {
+              const int4 lo = xv[t * 2], hi = xv[t * 2 + 1];
+              int S = __dp4a(w[0], lo.x, 0);
+              S = __dp4a(w[1], lo.y, S);
+              S = __dp4a(w[2], lo.z, S);
+              S = __dp4a(w[3], lo.w, S);
+              S = __dp4a(w[4], hi.x, S);
+              S = __dp4a(w[5], hi.y, S);
+              S = __dp4a(w[6], hi.z, S);
+              S = __dp4a(w[7], hi.w, S);
+              blk = __fmaf_rn(sc[t], (float)(S - sm8[t]), blk);
+            }
+            acc[r] = __fmaf_rn(h2f(dv), blk, acc[r]);
+          }
         }
       }
-    }
+      // every shared-memory read of stage s has returned (its values fed the
+      // sums above): hand the stage back
+      __syncwarp();
+      if (lane == 0) tc::bar_arrive(&empty[s]);
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]);
-    epilogue<RPW, false>(a, tile * kTmaWarps + wid, lane, acc, pos, best);
-    __syncthreads();  // every warp is done reading stage s
-    if (tid == 0) {
-      pending &= ~(1u << s);
-      if (i + nstage < g.my_tiles &&
-          tma_issue<QT, RPW>(a, g, stages, full, i + nstage, s, policy, skip_tile))
-        pending |= 1u << s;
+      for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]);
+      epilogue<RPW, false>(a, tile * kTmaWarps + wid, lane, acc, pos, best);
     }
   }
-
-  if (s_err) {
-    // stop cleanly: record the error and let copies still in flight land
-    if (tid == 0) {
-      atomicOr(&g_device_error, 1u);
-      for (int i = consumed; i < min(consumed + nstage, g.my_tiles); ++i) {
-        const int s = i % nstage;
-        if (pending & (1u << s)) mbar_wait_bounded(&full[s], (uint32_t)(i / nstage) & 1u);
-      }
-    }
-    return;
-  }
-
-  if (a.epi == kEpiLogits) {
+  if (a.epi == kEpiLogits && !producer) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
     if (lane == 0) best_w[wid] = best;
-    __syncthreads();
-    if (tid == 0) {
-      unsigned long long b = 0ull;
-      for (int w = 0; w < kTmaWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
-      logits_finish(a, b, gridDim.x);
+  }
+  __syncthreads();
+  if (*abort) {
+    // every role has stopped; let each copy still in flight land before the
+    // CTA's shared memory goes away
+    if (producer && lane == 0) {
+      volatile int never = 0;
+      for (int s = 0; s < nstage; ++s)
+        if (last_issued[s] >= 0)
+          tc::bar_wait(&full[s], (uint32_t)(last_issued[s] / nstage) & 1u, &never,
+                       &g_device_error);
     }
+    return;
+  }
+  if (a.epi == kEpiLogits && tid == 0) {
+    unsigned long long b = 0ull;
+    for (int w = 0; w < kTmaWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
+    logits_finish(a, b, gridDim.x);
   }
 }
 
@@ -557,8 +582,21 @@ cudaError_t tma_launch(const GemvArgs& a, const TmaPlan& p, cudaStream_t stream,
     if (e != cudaSuccess) return e;
     prepared = true;
   }
-  return launch(gemv_tma_kernel<QT, RPW>, dim3(p.grid), dim3(kTmaThreads), p.smem, stream, pdl,
-                a, p.stages, skip_tile);
+  // the plan counts CTAs per SM by shared memory; registers may allow fewer,
+  // and a grid beyond what is resident at once would run as a second wave
+  static size_t occ_smem = 0;
+  static int occ = 0;
+  if (occ_smem != p.smem) {
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_tma_kernel<QT, RPW>,
+                                                                  kTmaThreads, p.smem);
+    if (e != cudaSuccess) return e;
+    occ = n > 0 ? n : 1;
+    occ_smem = p.smem;
+  }
+  const int grid = std::min(p.grid, sm_count() * occ);
+  return launch(gemv_tma_kernel<QT, RPW>, dim3(grid), dim3(kTmaThreads), p.smem, stream, pdl, a,
+                p.stages, skip_tile);
 }
 
 #define DQMK_TMA_VARIANTS(X) \
