@@ -731,6 +731,241 @@ __global__ void __launch_bounds__(256) attention_cols_kernel(const BatchAttn b, 
   at::attention_hd_body<HD, 256>(a, chunk_cap, blockIdx.x, blockIdx.y, gridDim.y, sm);
 }
 
+// Decode attention of one (column, KV head, split), head_dim 128 and G query
+// heads per KV head, in one pass over the split's positions.  Four warps take
+// 4-position steps in turn (warp w: steps w, w + 4, ...); lane l owns dims
+// 4l..4l+3 of every K / V row.  Each lane streams its own 16-byte slices of
+// the rows into a private ring in shared memory with cp.async (kStreamDepth
+// steps ahead, zero-filled past the split's end), so a warp keeps 16 KB of
+// the cache in flight without holding it in registers.  Per step: the 4 x 8
+// partial dots are summed by a transposed butterfly that leaves lane l with
+// the score of position l / 8, head l % 8; an online softmax per head
+// (running max and sum, the accumulators rescaled when the max moves); p and
+// the rescale factors go through shared memory to every lane for P.V.  The
+// warps' states are merged in the CTA, then across splits by the same
+// last-CTA combine as the other decode attention kernels.
+constexpr int kStreamWarps = 4, kStreamDepth = 4, kStreamPos = 4;
+constexpr size_t kStreamRingBytes =
+    (size_t)kStreamWarps * kStreamDepth * 2 * kStreamPos * 32 * sizeof(float4);  // 64 KB
+constexpr size_t kStreamPBytes = (size_t)kStreamWarps * 48 * sizeof(float);
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStreamWarps * 32, 3)
+    attention_cols_stream_kernel(const BatchAttn b) {
+  constexpr int HD = 128, NW = kStreamWarps, D = kStreamDepth, P = kStreamPos;
+  constexpr int PS = at::part_stride(HD);
+  static_assert(G >= 1 && G <= at::kMaxGroup, "query heads per KV head");
+  extern __shared__ __align__(16) unsigned char smem_s[];
+  float4* ring = reinterpret_cast<float4*>(smem_s);                       // [NW][D][2][P][32]
+  float* pbuf = reinterpret_cast<float*>(smem_s + kStreamRingBytes);      // [NW][48]
+  __shared__ int is_last;
+  pdl_trigger();
+  pdl_wait();
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int c = blockIdx.z, kvh = blockIdx.x, split = blockIdx.y;
+  const size_t so = (size_t)__ldg(b.col_slot + c) * b.slot_stride;
+  AttnArgs a = {};
+  a.q = b.q + (size_t)c * b.ldq;
+  a.out = b.out + (size_t)c * b.ldq;
+  a.keys = b.keys + so;
+  a.values = b.values + so;
+  a.max_seq = b.max_seq;
+  a.n_kv_heads = b.n_kv_heads;
+  a.head_dim = HD;
+  a.layer = b.layer;
+  a.n_heads = b.n_heads;
+  a.pos_dev = b.col_pos + c;
+  a.partials = b.partials + (size_t)c * b.n_heads * b.max_splits * PS;
+  a.tickets = b.tickets + (size_t)c * b.n_kv_heads;
+  a.max_splits = b.max_splits;
+  const int pos = __ldcg(a.pos_dev);
+  const at::Split sp = at::split_of(a, split, pos);
+
+  if (split < sp.n_active) {
+    const size_t row_stride = (size_t)a.n_kv_heads * HD;
+    const size_t lbase = (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD + 4 * lane;
+    const float* kb = a.keys + lbase;
+    const float* vb = a.values + lbase;
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
+    unsigned long long q2[G][2];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float4 qv =
+          __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)(kvh * G + h) * HD) + lane);
+      q2[h][0] = f2_pack(qv.x, qv.y);
+      q2[h][1] = f2_pack(qv.z, qv.w);
+    }
+    const int n_steps = (sp.n + P - 1) / P;
+    const int count = n_steps > w ? (n_steps - w + NW - 1) / NW : 0;
+    const uint32_t ring_u32 = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
+    auto slot_addr = [&](int stage, int kind, int i) -> uint32_t {
+      return ring_u32 + (uint32_t)((((w * D + stage) * 2 + kind) * P + i) * 32 + lane) *
+                            (uint32_t)sizeof(float4);
+    };
+    auto issue = [&](int k, int stage) {
+      const int j = w + k * NW;
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const int t = j * P + i;
+        const bool valid = t < sp.n;
+        const size_t row = (size_t)(sp.t0 + (valid ? t : 0)) * row_stride;
+        cp_async16(slot_addr(stage, 0, i), kb + row, valid ? 16u : 0u);
+        cp_async16(slot_addr(stage, 1, i), vb + row, valid ? 16u : 0u);
+      }
+    };
+#pragma unroll
+    for (int k = 0; k < D; ++k) {
+      if (k < count) issue(k, k);
+      cp_async_commit();
+    }
+    float m_run = -INFINITY, l_run = 0.0f;
+    unsigned long long acc[G][2];
+#pragma unroll
+    for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0ull;
+    float* pb = pbuf + w * 48;
+    const int hs = lane & 7, is = lane >> 3;  // this lane's (head, position) after the butterfly
+    for (int k = 0; k < count; ++k) {
+      const int stage = k % D;
+      cp_async_wait<D - 1>();
+      float4 kr[P], vr[P];
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        kr[i] = ring[(((w * D + stage) * 2 + 0) * P + i) * 32 + lane];
+        vr[i] = ring[(((w * D + stage) * 2 + 1) * P + i) * 32 + lane];
+      }
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const unsigned long long k01 = f2_pack(kr[i].x, kr[i].y), k23 = f2_pack(kr[i].z, kr[i].w);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          if (h < G) {
+            const unsigned long long d2 = ffma2(q2[h][1], k23, fmul2(q2[h][0], k01));
+            v[i * 8 + h] = f2_lo(d2) + f2_hi(d2);
+          } else {
+            v[i * 8 + h] = 0.0f;
+          }
+        }
+      }
+#pragma unroll
+      for (int m = 16, n = 32; m >= 1; m >>= 1, n >>= 1) {
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int u = 0; u < n / 2; ++u) {
+          const float send = upper ? v[u] : v[u + n / 2];
+          const float keep = upper ? v[u + n / 2] : v[u];
+          v[u] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+      }
+      const int t = (w + k * NW) * P + is;
+      const bool valid = t < sp.n && hs < G;
+      const float s = valid ? __fmul_rn(v[0], scale) : -INFINITY;
+      float mx = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float m_new = fmaxf(m_run, mx);
+      const float p = valid ? expf(s - m_new) : 0.0f;
+      const float corr = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);
+      float ps = p + __shfl_xor_sync(0xffffffffu, p, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      l_run = fmaf(l_run, corr, ps);
+      m_run = m_new;
+      pb[lane] = p;
+      if (lane < 8) pb[32 + lane] = corr;
+      __syncwarp();
+      float pr[P][8], cr[8];
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const float4 lo = reinterpret_cast<const float4*>(pb)[2 * i];
+        const float4 hi = reinterpret_cast<const float4*>(pb)[2 * i + 1];
+        pr[i][0] = lo.x; pr[i][1] = lo.y; pr[i][2] = lo.z; pr[i][3] = lo.w;
+        pr[i][4] = hi.x; pr[i][5] = hi.y; pr[i][6] = hi.z; pr[i][7] = hi.w;
+      }
+      {
+        const float4 lo = reinterpret_cast<const float4*>(pb)[8];
+        const float4 hi = reinterpret_cast<const float4*>(pb)[9];
+        cr[0] = lo.x; cr[1] = lo.y; cr[2] = lo.z; cr[3] = lo.w;
+        cr[4] = hi.x; cr[5] = hi.y; cr[6] = hi.z; cr[7] = hi.w;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const unsigned long long c2 = f2_pack(cr[h], cr[h]);
+        unsigned long long a0 = fmul2(acc[h][0], c2), a1 = fmul2(acc[h][1], c2);
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          const unsigned long long p2 = f2_pack(pr[i][h], pr[i][h]);
+          a0 = ffma2(p2, f2_pack(vr[i].x, vr[i].y), a0);
+          a1 = ffma2(p2, f2_pack(vr[i].z, vr[i].w), a1);
+        }
+        acc[h][0] = a0;
+        acc[h][1] = a1;
+      }
+      if (k + D < count) issue(k + D, stage);
+      cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // every warp is done with the ring: reuse it for the merge
+    float* mst = reinterpret_cast<float*>(smem_s);  // [NW][8]
+    float* lst = mst + NW * 8;                      // [NW][8]
+    float* accb = lst + NW * 8;                     // [NW][G][HD]
+    if (lane < 8) {
+      mst[w * 8 + lane] = m_run;
+      lst[w * 8 + lane] = l_run;
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+      reinterpret_cast<float4*>(accb + (size_t)(w * G + h) * HD)[lane] =
+          make_float4(f2_lo(acc[h][0]), f2_hi(acc[h][0]), f2_lo(acc[h][1]), f2_hi(acc[h][1]));
+    __syncthreads();
+    const bool direct = sp.n_active == 1;
+    const int d = tid;  // one output dim per thread
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int ww = 0; ww < NW; ++ww) M = fmaxf(M, mst[ww * 8 + h]);
+      float L = 0.0f, O = 0.0f;
+#pragma unroll
+      for (int ww = 0; ww < NW; ++ww) {
+        const float mw = mst[ww * 8 + h];
+        const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+        L = fmaf(f, lst[ww * 8 + h], L);
+        O = fmaf(f, accb[(size_t)(ww * G + h) * HD + d], O);
+      }
+      if (direct) {
+        a.out[(size_t)(kvh * G + h) * HD + d] = __fdiv_rn(O, L);
+      } else {
+        float* pp = a.partials + ((size_t)(kvh * G + h) * a.max_splits + split) * PS;
+        pp[d] = O;
+        if (d == 0) *reinterpret_cast<float2*>(pp + HD) = make_float2(M, L);
+      }
+    }
+    __syncthreads();  // the merge buffers are free again (the combine reuses them)
+  }
+  if (sp.n_active > 1)
+    at::split_combine_hd<kStreamWarps * 32, HD>(a, kvh, G, sp.n_active, gridDim.y,
+                                                 reinterpret_cast<float*>(smem_s), &is_last);
+}
+
 __global__ void cols_advance_kernel(unsigned long long* __restrict__ keys, int cols,
                                     const int* __restrict__ col_slot, int* __restrict__ col_token,
                                     int* __restrict__ col_pos, int* __restrict__ history,
@@ -803,6 +1038,13 @@ cudaError_t batch_prepare() {
                              cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attention_cols_kernel<128>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_cols_stream_kernel<7>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(kStreamRingBytes + kStreamPBytes));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_cols_stream_kernel<7>,
                              cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e == cudaSuccess) done = true;
   return e;
@@ -881,9 +1123,15 @@ cudaError_t launch_attention_cols(const BatchAttn& a, cudaStream_t s, bool pdl) 
     return cudaErrorInvalidValue;
   cudaError_t e = batch_prepare();
   if (e != cudaSuccess) return e;
+  const dim3 grid(a.n_kv_heads, a.max_splits, a.cols);
+  // head_dim 128 with 7 query heads per KV head (Qwen2-7B): the one-pass
+  // streaming kernel; its merge and split-combine buffers reuse the ring
+  if (a.head_dim == 128 && a.n_heads / a.n_kv_heads == 7 &&
+      (size_t)(2 * a.max_splits + 1) * at::kMaxGroup * sizeof(float) <= kStreamRingBytes)
+    return launch(attention_cols_stream_kernel<7>, grid, dim3(kStreamWarps * 32),
+                  kStreamRingBytes + kStreamPBytes, s, pdl, a);
   const int cap = attention_chunk_cap(a.max_seq, a.max_splits);
   const size_t smem = at::smem_bytes_hd(a.head_dim, cap, a.max_splits, 256);
-  const dim3 grid(a.n_kv_heads, a.max_splits, a.cols);
   if (a.head_dim == 64)
     return launch(attention_cols_kernel<64>, grid, dim3(256), smem, s, pdl, a, cap);
   if (a.head_dim == 128)

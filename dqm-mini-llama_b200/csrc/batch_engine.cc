@@ -153,7 +153,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     const Layer& L = m->layers[l];
     const BatchLayer& B = m->batch_layers[l];
     DQMK_CUDA_RET(kApi, launch_split_rows(b->x, n, c.dim, L.qkv.kp, c.dim, L.attn_norm, eps,
-                                          b->hi, b->lo, b->rs, s));
+                                          b->hi, b->lo, b->rs, s, pdl));
     BatchGemm g = gemm_args(b, L.qkv, B.qkv, n, kEpiQkv);
     g.bias = L.qkv_bias;
     g.rope_cs = m->rope_cs;
@@ -191,7 +191,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     DQMK_CUDA_RET(kApi, launch_attention_cols(a, s, pdl));
 
     DQMK_CUDA_RET(kApi, launch_split_rows(b->att, n, qd, L.wo.kp, qd, nullptr, eps, b->hi, b->lo,
-                                          b->rs, s));
+                                          b->rs, s, pdl));
     BatchGemm o = gemm_args(b, L.wo, B.wo, n, kEpiStore);
     o.residual = tpar ? nullptr : b->x;
     o.y = tpar ? b->part : b->x;
@@ -203,14 +203,14 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     }
 
     DQMK_CUDA_RET(kApi, launch_split_rows(b->x, n, c.dim, L.gate_up.kp, c.dim, L.ffn_norm, eps,
-                                          b->hi, b->lo, b->rs, s));
+                                          b->hi, b->lo, b->rs, s, pdl));
     BatchGemm gu = gemm_args(b, L.gate_up, B.gate_up, n, kEpiSwiGlu);
     gu.y = b->f;
     gu.ldy = tp.hidden;
     DQMK_CUDA_RET(kApi, launch_batch_gemm(B.gate_up.map, B.gate_up.dmap, b->x_dim[0], b->x_dim[1], gu, s, pdl));
 
     DQMK_CUDA_RET(kApi, launch_split_rows(b->f, n, tp.hidden, L.down.kp, tp.hidden, nullptr, eps,
-                                          b->hi, b->lo, b->rs, s));
+                                          b->hi, b->lo, b->rs, s, pdl));
     BatchGemm dn = gemm_args(b, L.down, B.down, n, kEpiStore);
     dn.residual = tpar ? nullptr : b->x;
     dn.y = tpar ? b->part : b->x;
@@ -222,7 +222,7 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
     }
   }
   DQMK_CUDA_RET(kApi, launch_split_rows(b->x, n, c.dim, m->lm_head.kp, c.dim, m->final_norm, eps,
-                                        b->hi, b->lo, b->rs, s));
+                                        b->hi, b->lo, b->rs, s, pdl));
   BatchGemm lg = gemm_args(b, m->lm_head, m->batch_lm, n, kEpiLogits);
   lg.y = with_logits ? b->logits : nullptr;
   lg.ldy = tp.vocab_stride;

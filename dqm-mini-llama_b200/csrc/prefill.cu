@@ -515,6 +515,71 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
   }
 }
 
+// The same split with the row held in registers (J values per thread, element
+// e = tid + 256 j, the order of the loops above): one load pass with every
+// load in flight, instead of a round trip per pass; the sums, the maximum and
+// every written value are those of split_rows_kernel bit for bit.  Launched
+// with programmatic dependent launch in the decode chains: it waits for the
+// producer of x before its first access.
+template <int J>
+__global__ void __launch_bounds__(256) split_rows_reg_kernel(const float* __restrict__ x, int k,
+                                                             int kp, int ldx,
+                                                             const float* __restrict__ norm_w,
+                                                             float eps, uint16_t* __restrict__ hi,
+                                                             uint16_t* __restrict__ lo,
+                                                             float* __restrict__ rs) {
+  __shared__ float red[8];
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const float* xr = x + (size_t)row * ldx;
+  float v[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int e = tid + 256 * j;
+    v[j] = e < k ? xr[e] : 0.0f;
+  }
+  if (norm_w) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+      if (tid + 256 * j < k) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+    const float t = block_sum(ss, red);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float)k), eps)));
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int e = tid + 256 * j;
+      if (e < k) v[j] = __fmul_rn(__fmul_rn(v[j], scale), norm_w[e]);
+    }
+  }
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+    if (tid + 256 * j < k) mx = fmaxf(mx, fabsf(v[j]));
+  mx = block_max(mx, red);
+  int ex = 0;
+  if (mx > 0.0f && mx <= 3.0e38f) {
+    int fe;
+    frexpf(mx, &fe);  // mx in [2^(fe-1), 2^fe)
+    ex = min(max(fe - 15, -120), 120);
+  }
+  const float down = ldexpf(1.0f, -ex);
+  if (tid == 0) rs[row] = ldexpf(1.0f, ex);
+  uint16_t* hr = hi + (size_t)row * kp;
+  uint16_t* lr = lo + (size_t)row * kp;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int e = tid + 256 * j;
+    if (e < kp) {
+      const float t = e < k ? __fmul_rn(v[j], down) : 0.0f;
+      const __half h = __float2half_rn(t);
+      const __half l = __float2half_rn(__fsub_rn(t, __half2float(h)));
+      hr[e] = __half_as_ushort(h);
+      lr[e] = __half_as_ushort(l);
+    }
+  }
+}
+
 // Packed-row gather of M token embeddings (rows of the quantized token_embd).
 __global__ void embed_rows_kernel(int qtype, const uint8_t* __restrict__ qs,
                                   const uint16_t* __restrict__ d, int dim, int kp,
@@ -845,7 +910,18 @@ cudaError_t launch_prefill_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo
 }
 
 cudaError_t launch_split_rows(const float* x, int m, int k, int kp, int ldx, const float* norm_w,
-                              float eps, uint16_t* hi, uint16_t* lo, float* rs, cudaStream_t st) {
+                              float eps, uint16_t* hi, uint16_t* lo, float* rs, cudaStream_t st,
+                              bool pdl) {
+  const dim3 grid(m), block(256);
+  if (kp <= 16 * 256)
+    return launch(split_rows_reg_kernel<16>, grid, block, 0, st, pdl, x, k, kp, ldx, norm_w, eps,
+                  hi, lo, rs);
+  if (kp <= 32 * 256)
+    return launch(split_rows_reg_kernel<32>, grid, block, 0, st, pdl, x, k, kp, ldx, norm_w, eps,
+                  hi, lo, rs);
+  if (kp <= 80 * 256)
+    return launch(split_rows_reg_kernel<80>, grid, block, 0, st, pdl, x, k, kp, ldx, norm_w, eps,
+                  hi, lo, rs);
   split_rows_kernel<<<m, 256, 0, st>>>(x, k, kp, ldx, norm_w, eps, hi, lo, rs);
   return cudaGetLastError();
 }

@@ -67,8 +67,11 @@ cudaError_t launch_prefill_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo
                                 const PrefillGemm& p, cudaStream_t s);
 // x [m][ldx] (optionally RMS-normalised with norm_w) -> fp16 planes hi, lo
 // [m][kp] with x * 2^-e ~= hi + lo, and rs[row] = 2^e.
+// With pdl the launch may start while the previous kernel of the stream
+// drains (programmatic dependent launch); the kernel waits before reading x.
 cudaError_t launch_split_rows(const float* x, int m, int k, int kp, int ldx, const float* norm_w,
-                              float eps, uint16_t* hi, uint16_t* lo, float* rs, cudaStream_t st);
+                              float eps, uint16_t* hi, uint16_t* lo, float* rs, cudaStream_t st,
+                              bool pdl = false);
 cudaError_t launch_embed_rows(int qtype, const uint8_t* qs, const uint16_t* d, int dim, int kp,
                               const int* tokens, int m, float* y, cudaStream_t st);
 cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st);

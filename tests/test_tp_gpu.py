@@ -4,7 +4,9 @@ vocabulary ids; untied lm_head) sharded Megatron-style, one rank per GPU over
 NCCL, and again with the decode step's partial sums exchanged over peer
 memory (IPC-mapped buffers, flags, bounded waits).  The gathered prompt logits
 must sit within 1e-3 x logit range of the oracle, greedy tokens must equal the
-oracle's, and all runs must agree with each other.  Skipped with fewer than 2
+oracle's, and all runs must agree with each other.  On the NCCL runs a
+two-slot multi-sequence batch (dqmk_batch) over the same shards must follow
+the oracle's greedy path in both slots.  Skipped with fewer than 2
 GPUs."""
 import os
 import socket
@@ -68,6 +70,8 @@ def test_tensor_parallel_matches_oracle(cuda, reference, tmp_path):
         err = float(np.abs(got["logits"] - first_logits).max())
         assert err <= 1e-3 * rng, f"TP{world}: prompt logits err {err:.3e}, range {rng:.3f}"
         assert got["tokens"].tolist() == ref_tokens, (got["tokens"].tolist(), ref_tokens, margin)
+        if not p2p:  # the multi-sequence step: both slots follow the oracle's greedy path
+            assert got["batch_tokens"].tolist() == [ref_tokens] * 2, (got["batch_tokens"], ref_tokens)
         srng = float(last_logits.max() - last_logits.min())
         serr = float(np.abs(got["step_logits"] - last_logits).max())
         assert serr <= 1e-3 * srng, f"TP{world}: step logits err {serr:.3e}"

@@ -10,7 +10,9 @@
     ForwardBatch over the prompt and greedy decoding; rank 0 writes the
     gathered logits and the tokens to --out.  With --p2p the contexts
     exchange IPC handles and connect, so the decode step's partial sums
-    travel over peer memory instead of NCCL.
+    travel over peer memory instead of NCCL; without it a two-slot
+    multi-sequence batch (dqmk_batch) also decodes the prompt on the same
+    shards.
 """
 import argparse
 import datetime
@@ -83,13 +85,26 @@ def mode_gpu(pkg, rank, world, local, out, p2p):
     # one more host-visible step: ForwardToken logits after the decoded tokens
     step_logits = ctx.ForwardToken(tokens[-1], r["n_prompt"] + r["n_steps"] - 1)
     ctx.close()
+    batch_tokens = []
+    if not p2p:
+        # the multi-sequence step on the same shards (NCCL all-reduces inside
+        # its captured graph): two slots fed the same prompt must both follow
+        # the single-sequence greedy path
+        batch = pkg.Batch(model, 2, r["n_prompt"] + r["n_steps"])
+        for slot in range(2):
+            batch.prefill(slot, prompt[:-1])
+        _, nxt = batch.step(None, [prompt[-1]] * 2, [r["n_prompt"] - 1] * 2, want_logits=False)
+        seq = batch.decode_greedy(nxt.tolist(), [r["n_prompt"]] * 2, r["n_steps"] - 1)
+        batch_tokens = [[int(nxt[c])] + seq[:, c].tolist() for c in range(2)]
+        batch.close()
     model.close()
     gathered = [None] * world
-    dist.all_gather_object(gathered, tokens)
+    dist.all_gather_object(gathered, (tokens, batch_tokens))
     if rank == 0:
-        assert all(t == tokens for t in gathered), gathered
-        np.savez(out, logits=logits, tokens=np.array(tokens), step_logits=step_logits)
-        print("gpu ok", world, tokens)
+        assert all(t == (tokens, batch_tokens) for t in gathered), gathered
+        np.savez(out, logits=logits, tokens=np.array(tokens), step_logits=step_logits,
+                 batch_tokens=np.array(batch_tokens))
+        print("gpu ok", world, tokens, batch_tokens)
 
 
 def main():
