@@ -476,8 +476,9 @@ def bench_7b_batch(args, pkg, torch, dist, world, rank, local):
     prompts = [S.prompt_tokens(c["vocab"], ctx_len, 1000 + group * seqs + s) for s in range(seqs)]
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for s in range(seqs):
-        batch.prefill(s, prompts[s][:-1])
+    if args.kv_fill == "prompt":
+        for s in range(seqs):
+            batch.prefill(s, prompts[s][:-1])
     torch.cuda.synchronize()
     fill_s = time.perf_counter() - t0
     last = [int(p[-1]) for p in prompts]
@@ -490,10 +491,12 @@ def bench_7b_batch(args, pkg, torch, dist, world, rank, local):
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")  # lets a profiler select the timed steps
         e0.record(stream)
         batch.decode_enqueue(cont, [pos0] * seqs, n_steps)
         e1.record(stream)
         e1.synchronize()
+        torch.cuda.nvtx.range_pop()
     dt = e0.elapsed_time(e1) / 1e3
     # end to end through the public step call: host tokens in, host tokens out
     pos1 = pos0 + n_steps
@@ -545,12 +548,36 @@ def bench_7b_batch(args, pkg, torch, dist, world, rank, local):
         "e2e": {"value": round(args.seqs * e2e_steps / e2e_dt, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": 3 * 64 * 4, "d2h_bytes_per_step": seqs * 4,
                 "steps": e2e_steps},
-        "kv_fill": {"tokens": args.seqs * (ctx_len - 1), "s": round(fill_s, 3),
-                    "tok_s": round(args.seqs * (ctx_len - 1) / fill_s, 1)},
+        "kv_fill": ({"tokens": args.seqs * (ctx_len - 1), "s": round(fill_s, 3),
+                     "tok_s": round(args.seqs * (ctx_len - 1) / fill_s, 1)}
+                    if args.kv_fill == "prompt" else "zero (not filled)"),
         "gpu_launches": n_steps * launches,
         "hbm": {"bytes_per_step_per_gpu": int(per_gpu), "GB_s_per_gpu": round(gbs, 1),
                 "frac_of_peak": round(gbs / peak, 4), "peak_source": peak_kind},
         "clocks": clk.summary()}))
+
+
+def time_cols_gemm(pkg, torch, launches: int = 10):
+    """dqmk_linear_cols_packed at the Qwen2-7B gate/up shape: 64 columns x
+    37888 rows x 3584, Q4_0 (76 MB of blocks), after 3 warm-up calls; CUDA
+    events around `launches` back-to-back calls (each call includes its
+    stream-ordered scratch and side tables)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(3)
+    rows, k = 37888, 3584
+    packed = pkg.pack_weight(pkg.Q40, random_q40_blocks(torch, rows, k, gen), rows, k)
+    x = torch.randn(64, k, device="cuda")
+    y = torch.empty(64, rows, device="cuda")
+    for _ in range(3):
+        pkg.linear_cols_packed(pkg.Q40, x, packed, rows, y=y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(launches):
+        pkg.linear_cols_packed(pkg.Q40, x, packed, rows, y=y)
+    e1.record()
+    e1.synchronize()
+    return {"shape": "64x3584->37888 Q4_0", "us_per_call": round(e0.elapsed_time(e1) / launches * 1e3, 2)}
 
 
 def reference_decode(w, steps: int, warmup: int, threads: int):
@@ -627,6 +654,13 @@ def main():
     ap.add_argument("--tp", type=int, default=0,
                     help="qwen2-7b with --seqs > 1: tensor-parallel group size (default: all "
                          "ranks); --gpus / --tp independent groups split the sequences")
+    ap.add_argument("--kv-fill", default="prompt", choices=["prompt", "zero"],
+                    help="qwen2-7b --seqs > 1: fill every KV cache with a random prompt "
+                         "(prompt) or leave it zero and start decoding at position --ctx - 1 "
+                         "(zero: the step reads the same bytes; for short profiling runs)")
+    ap.add_argument("--cols-gemm", action="store_true",
+                    help="time only the standalone multi-sequence GEMM at the Qwen2-7B gate/up "
+                         "shape (64 columns x 37888 x 3584 Q4_0; profiling)")
     ap.add_argument("--p2p", action="store_true",
                     help="qwen2-7b under tensor parallelism: exchange partial sums over peer "
                          "memory (IPC-mapped buffers) instead of NCCL all-reduces")
@@ -652,6 +686,9 @@ def main():
 
     pkg = ge.load_package()
     S = pkg.synth
+    if args.cols_gemm:
+        print(json.dumps({"cols_gemm": time_cols_gemm(pkg, torch)}))
+        return
     if args.model == "qwen2-7b":
         if args.seqs > 1:
             bench_7b_batch(args, pkg, torch, dist, world, rank, local)

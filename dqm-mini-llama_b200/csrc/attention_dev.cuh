@@ -11,7 +11,7 @@ namespace at {
 
 constexpr int kThreads = 128;
 constexpr int kMaxGroup = 8;  // query heads per KV head
-constexpr int kMinChunk = 32;
+constexpr int kMinChunk = 128;
 
 // Floats per split partial: the head_dim sums, then m and l, padded so every
 // row starts 16-byte aligned (float4 reads in the combine).

@@ -228,7 +228,7 @@ int dqmk_attention_decode(const float* q_dev, const float* keys_dev, const float
  * fixed 2 MiB device buffer compiled into the library (every GPU that loads
  * it holds the 2 MiB until the process exits): n_heads * splits *
  * (head_dim + 4) * 4 bytes + 256 must fit, where splits = min(ceil(max_seq /
- * 32), SM count / n_kv_heads) -- on a 148-SM B200 every supported shape
+ * 128), SM count / n_kv_heads) -- on a 148-SM B200 every supported shape
  * (at most 8 query heads per KV head, head_dim <= 256) needs at most
  * 1.23 MB; on a GPU where a shape does not fit it is rejected with
  * DQMK_ERR_UNSUPPORTED and a message giving both sizes.  All calls share the
