@@ -89,6 +89,29 @@ __global__ void __launch_bounds__(256) attention_hd_kernel(const AttnArgs a, int
   attention_hd_body<HD, 256>(a, chunk_cap, blockIdx.x, blockIdx.y, gridDim.y, sm);
 }
 
+// When the whole context is one split (max_seq <= 128 positions) the grouped
+// kernel would run one CTA per KV head doing all G query heads in turn.
+// Here blockIdx.z picks one query head and the CTA runs the same body as a
+// group of one: K / V rows are read G times, from L2, and each head's
+// arithmetic is exactly that of the grouped kernel (heads are independent in
+// it), so outputs are bit-identical with a G times shorter critical path.
+template <int HD>
+__global__ void __launch_bounds__(256) attention_hd_head_kernel(const AttnArgs a, int chunk_cap) {
+  extern __shared__ float sm[];
+  pdl_trigger();
+  pdl_wait();
+  const int kvh = blockIdx.x, g = blockIdx.z;
+  const int G = a.n_heads / a.n_kv_heads;
+  AttnArgs b = a;
+  b.n_heads = a.n_kv_heads;  // one query head per KV head
+  b.max_splits = 1;
+  // the body addresses query head kvh of b: shift q / out onto head kvh * G + g
+  const size_t shift = (size_t)(kvh * (G - 1) + g) * HD;
+  b.q = a.q + shift;
+  b.out = a.out + shift;
+  attention_hd_body<HD, 256>(b, chunk_cap, kvh, 0, 1, sm);
+}
+
 // Any head_dim that is a multiple of 4 up to 256: one thread per position.
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, int chunk_cap) {
   extern __shared__ float sm[];
@@ -250,6 +273,12 @@ cudaError_t attention_prepare() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attention_hd_kernel<128>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_hd_head_kernel<64>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_hd_head_kernel<128>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -268,6 +297,13 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
   cudaError_t e = attention_prepare();
   if (e != cudaSuccess) return e;
   const dim3 grid(a.n_kv_heads, a.max_splits);
+  const int G = a.n_kv_heads > 0 ? a.n_heads / a.n_kv_heads : 1;
+  if (hd_kernel && a.max_splits == 1 && G > 1) {
+    const dim3 hgrid(a.n_kv_heads, 1, G);
+    if (a.head_dim == 64)
+      return launch(attention_hd_head_kernel<64>, hgrid, dim3(256), smem, stream, pdl, a, cap);
+    return launch(attention_hd_head_kernel<128>, hgrid, dim3(256), smem, stream, pdl, a, cap);
+  }
   if (hd_kernel && a.head_dim == 64)
     return launch(attention_hd_kernel<64>, grid, dim3(256), smem, stream, pdl, a, cap);
   if (hd_kernel && a.head_dim == 128)
