@@ -11,9 +11,12 @@ flush is needed between steps.
 Reported (one JSON line on rank 0):
   value      decode tok/s with weights resident, tokens chosen by the device
              argmax, the step graph replayed back to back (CUDA events);
-  e2e        the same through the C ABI entry point ForwardToken with host
-             buffers: token/pos uploaded, 151936 logits downloaded and argmaxed
-             on the host every step, as the reference engine does;
+  e2e        the same through the public decode entry point with host
+             buffers: each call uploads the token and position, runs one step
+             with the argmax on the device and returns the chosen token
+             (dqmk_decode_greedy, n_steps = 1); e2e.logits_path is the same
+             through ForwardToken with the 151936 logits downloaded and
+             argmaxed on the host every step, as the reference engine does;
   roofline   the dominant kernel (the Q8_0 GEMV) timed live at the lm_head
              shape 151936 x 896 (145.25 MB per launch, two rotating copies);
   cpu_baseline  the reference's own CPU path (compiled from its sources) on
@@ -148,6 +151,21 @@ def time_e2e(ctx, first_token, steps: int):
     for i in range(steps):
         ctx.ForwardToken(tok, N_PROMPT + (i % N_DECODE_POS), logits)
         tok = int(np.argmax(logits))
+    return time.perf_counter() - t0
+
+
+def time_e2e_greedy(ctx, first_token, steps: int):
+    """One greedy token per call of the public decode entry point
+    (dqmk_decode_greedy with n_steps = 1): the token and position go host to
+    device, the step graph runs with the argmax on the device, and the chosen
+    token (4 bytes) comes back to the host, which feeds it to the next call."""
+    tok = first_token
+    for i in range(4):  # warm-up
+        tok = int(ctx.decode_greedy(tok, N_PROMPT + i, 1)[0])
+    tok = first_token
+    t0 = time.perf_counter()
+    for i in range(steps):
+        tok = int(ctx.decode_greedy(tok, N_PROMPT + (i % N_DECODE_POS), 1)[0])
     return time.perf_counter() - t0
 
 
@@ -731,11 +749,12 @@ def main():
 
     # ---- e2e through the C ABI with host buffers
     e2e_steps = min(args.steps, 256)
-    e2e_dt = time_e2e(ctx, first, e2e_steps)
+    e2e_dt = time_e2e_greedy(ctx, first, e2e_steps)
+    e2e_logits_dt = time_e2e(ctx, first, e2e_steps)
     if dist:
-        t = torch.tensor([e2e_dt], device="cuda", dtype=torch.float64)
+        t = torch.tensor([e2e_dt, e2e_logits_dt], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_dt = float(t.item())
+        e2e_dt, e2e_logits_dt = (float(v) for v in t.tolist())
     e2e = world * e2e_steps / e2e_dt
 
     # ---- dominant-kernel roofline (lm_head-shaped Q8_0 GEMV)
@@ -781,7 +800,15 @@ def main():
                    "parallelism": "replicas" if world > 1 else "single",
                    "l2": "per-step weight stream 525 MB > 126 MB L2; no flush needed"},
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                "d2h_bytes_per_step": 151936 * 4},
+                "d2h_bytes_per_step": 4,
+                "path": "dqmk_decode_greedy, one token per call: token and position in, the "
+                        "device argmax's token out",
+                "logits_path": {"value": round(world * e2e_steps / e2e_logits_dt, 2),
+                                "unit": "tok/s", "h2d_bytes_per_step": 8,
+                                "d2h_bytes_per_step": 151936 * 4,
+                                "path": "ForwardToken with the 151936 logits copied to the "
+                                        "host and argmaxed there, as the reference engine "
+                                        "samples"}},
         "gpu_launches": args.steps * launches_per_step,
         "decode_hbm": {"bytes_per_token": bytes_per_token,
                        "GB_s": round(bytes_per_token * value / world / 1e9, 1),
