@@ -140,7 +140,12 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
   const dqmk_model_config& c = m->cfg;
   const dqmk_tp_plan& tp = m->tp;
   const bool tpar = tp.world > 1;
-  const bool pdl = use_pdl();
+  // Under tensor parallelism the step interleaves NCCL kernels with its own;
+  // with programmatic dependent launch there, two ranks decoding the same
+  // prompt in two slots produced diverging greedy tokens on 2 GPUs, with plain
+  // launches they match the oracle in both slots.  Until that race is found
+  // the tensor-parallel step launches every kernel plainly.
+  const bool pdl = use_pdl() && !tpar;
   cudaStream_t s = b->stream;
   const int hd = c.head_dim;
   const int qd = tp.n_q_heads * hd;
