@@ -12,7 +12,7 @@ Each column must compute what ForwardToken computes for its sequence:
     one column, column counts that are not multiples of 16, K tails, row
     counts across the 256-row tile, split-K, bias and an in-place residual;
   * whole models: per-sequence logits within 1e-3 x logit range of the
-    oracle (the BASELINE tolerance), and greedy tokens identical to the
+    oracle (the logit tolerance of the whole path), and greedy tokens identical to the
     oracle's, with sequences at different positions in the same step, one
     slot taking several prompt positions in one step, and the 7B layer
     widths (head_dim 128, K = 3584 / 18944) on a one-layer model.

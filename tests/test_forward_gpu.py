@@ -2,7 +2,7 @@
 reference: ForwardToken logits, ForwardBatch side effects, greedy tokens, and
 the runtime counters the reference's CUDA tests assert.
 
-Logit tolerance (BASELINE north star): max |logit - ref| <= 1e-3 * (max - min
+Logit tolerance: max |logit - ref| <= 1e-3 * (max - min
 of the reference logits).  Greedy decoding must produce identical tokens; the
 smallest top-1/top-2 margin of each run is reported alongside.
 """
