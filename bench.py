@@ -598,6 +598,15 @@ def time_cols_gemm(pkg, torch, launches: int = 10):
     return {"shape": "64x3584->37888 Q4_0", "us_per_call": round(e0.elapsed_time(e1) / launches * 1e3, 2)}
 
 
+def decode_config(world: int) -> dict:
+    """The headline workload, shared by the GPU arm and the reference arm."""
+    return {"workload": "qwen2-0.5b-architecture Q8_0, 32-token prompt then batch-1 greedy "
+                        "decode at positions 32..95 (cycled)",
+            "model": "qwen2-0.5b", "global_batch": world, "seq_len": N_PROMPT + N_DECODE_POS,
+            "parallelism": "replicas" if world > 1 else "single",
+            "l2": "per-step weight stream 525 MB > 126 MB L2; no flush needed"}
+
+
 def reference_decode(w, steps: int, warmup: int, threads: int):
     """The reference's CPU decode (oracle/_ref) on this host: returns s/token."""
     orc = ge.load_oracle()
@@ -606,14 +615,16 @@ def reference_decode(w, steps: int, warmup: int, threads: int):
     rm = orc.RefModel(w, N_PROMPT + N_DECODE_POS, threads=threads)
     S = ge.load_package().synth
     prompt = S.prompt_tokens(w.cfg["vocab"], N_PROMPT, PROMPT_SEED)
-    logits = rm.forward_batch(prompt[:1], 0)  # one prompt token is enough context
+    # the same workload as the GPU arm: the 32-token prompt (untimed, the
+    # reference's per-token ForwardBatch), then greedy steps from position 32
+    logits = rm.forward_batch(prompt, 0)
     tok = int(np.argmax(logits))
     for i in range(warmup):
-        logits = rm.forward_batch([tok], 1 + i)
+        logits = rm.forward_batch([tok], N_PROMPT + i)
         tok = int(np.argmax(logits))
     t0 = time.perf_counter()
     for i in range(steps):
-        logits = rm.forward_batch([tok], 1 + warmup + i)
+        logits = rm.forward_batch([tok], N_PROMPT + warmup + i)
         tok = int(np.argmax(logits))
     dt = time.perf_counter() - t0
     return dt / steps, "ok"
@@ -632,7 +643,7 @@ def reference_arm(args, rank):
     w = S.make_model(S.QWEN2_0_5B, S.Q80, MODEL_SEED,
                      quantize_q80=lambda a: orc.quantize_q80(a, use_ref=True))
     steps = max(1, min(args.steps, 16))
-    warm = max(1, min(args.warmup, 2))
+    warm = max(3, min(args.warmup, 8))
     spt, _ = reference_decode(w, steps, warm, threads)
     v = 1.0 / spt
     print(json.dumps({
@@ -640,9 +651,8 @@ def reference_arm(args, rank):
         "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": round(spt * 1e3, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic random-init weights, random prompt ids",
-        "config": {"workload": "qwen2-0.5b Q8_0 batch-1 greedy decode, reference CPU path "
-                               "(threaded scalar LinearQ80 + AVX2 F32 lm_head)",
-                   "model": "qwen2-0.5b-architecture", "seq": "1 prompt token + decode"},
+        "config": dict(decode_config(1), parallelism="reference CPU path on the host cores "
+                       "(threaded scalar LinearQ80 + AVX2 F32 lm_head)"),
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads,
                          "kind": "reference",
                          "sample": f"{steps} decode steps after {warm} warm-up"},
@@ -776,12 +786,13 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        spt, status = reference_decode(w, 8, 1, threads)
+        spt, status = reference_decode(w, 8, 3, threads)
         if spt is not None:
             cpu = {"value": round(1.0 / spt, 4), "unit": "tok/s", "cores": threads,
                    "kind": "reference",
-                   "sample": "8 decode steps (after 1 warm-up) of the same model on the "
-                             "reference's CPU path, threaded over all host cores"}
+                   "sample": "8 decode steps (after 3 warm-up steps) of the same model and "
+                             "positions on the reference's CPU path, threaded over all host "
+                             "cores"}
 
     if dist:
         dist.barrier()
@@ -794,11 +805,7 @@ def main():
         "ms_per_step": round(dt / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0xf32",
         "data": "synthetic: random-init N(0,0.02) weights quantized to Q8_0, random prompt ids",
-        "config": {"workload": "qwen2-0.5b-architecture Q8_0, 32-token prompt then batch-1 "
-                               "greedy decode at positions 32..95 (cycled)",
-                   "model": "qwen2-0.5b", "global_batch": world, "seq_len": N_PROMPT + N_DECODE_POS,
-                   "parallelism": "replicas" if world > 1 else "single",
-                   "l2": "per-step weight stream 525 MB > 126 MB L2; no flush needed"},
+        "config": decode_config(world),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4,
                 "path": "dqmk_decode_greedy, one token per call: token and position in, the "
