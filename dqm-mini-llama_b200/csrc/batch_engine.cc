@@ -16,6 +16,7 @@
 // once per column count into a CUDA graph; tokens, positions and slots live in
 // device memory, so greedy decoding replays the graph with no host work.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -144,8 +145,14 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
   // with programmatic dependent launch there, two ranks decoding the same
   // prompt in two slots produced diverging greedy tokens on 2 GPUs, with plain
   // launches they match the oracle in both slots.  Until that race is found
-  // the tensor-parallel step launches every kernel plainly.
-  const bool pdl = use_pdl() && !tpar;
+  // the tensor-parallel step launches every kernel plainly
+  // (DQMK_BATCH_TP_PDL=1 in the environment restores the chained launches,
+  // for diagnosing it).
+  static const bool tp_pdl = [] {
+    const char* v = std::getenv("DQMK_BATCH_TP_PDL");
+    return v && v[0] == '1';
+  }();
+  const bool pdl = use_pdl() && (!tpar || tp_pdl);
   cudaStream_t s = b->stream;
   const int hd = c.head_dim;
   const int qd = tp.n_q_heads * hd;
