@@ -65,6 +65,7 @@ SIGNATURES = {
     "dqmk_linear_cols_packed": ([_i, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp], _i),
     "dqmk_device_error": ([_i], _i),
     "dqmk_gemv_packed_withhold_tile": ([_i, _vp, _i, _vp, _i, _vp, _i, _vp], _i),
+    "dqmk_context_withhold_lm_head": ([_vp, _i], _i),
     "dqmk_rmsnorm": ([_vp, _vp, _i, _f, _vp, _vp], _i),
     "dqmk_silu_mul": ([_vp, _vp, _i, _vp, _vp], _i),
     "dqmk_add": ([_vp, _vp, _i, _vp, _vp], _i),

@@ -263,8 +263,8 @@ size_t attention_partials_floats(int n_heads, int head_dim, int max_splits) {
 }
 
 cudaError_t attention_prepare() {
-  static bool attr_set = false;
-  if (!attr_set) {
+  static DeviceOnce once;
+  return once.run([] {
     cudaError_t e = cudaFuncSetAttribute(attention_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e == cudaSuccess)
@@ -279,10 +279,8 @@ cudaError_t attention_prepare() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attention_hd_head_kernel<128>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  return cudaSuccess;
+    return e;
+  });
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {

@@ -1,5 +1,5 @@
 // attention_dev.cuh -- device code of GQA decode attention shared by the
-// standalone kernels (attention.cu) and the persistent decode step (step.cu).
+// batch-1 kernels (attention.cu) and the multi-sequence kernels (batch.cu).
 // See attention.cu for the design.
 #pragma once
 

@@ -85,7 +85,7 @@ constexpr uint32_t kTmemCols = kTmemNeed <= 256 ? 256 : 512;
 static_assert(kTmemNeed <= 512, "at most the whole tensor memory of the SM");
 static_assert(kDeqWarps * 32 == kTileRows, "one dequant thread per tile row");
 
-__device__ unsigned int g_batch_error;  // bit 0: a bounded wait timed out
+__device__ unsigned int g_batch_error;  // kErrTimeout / kErrNoToken
 
 template <int QT>
 constexpr int raw_row_bytes() {
@@ -245,7 +245,8 @@ __device__ __forceinline__ void finish(const BatchGemm& p, const ColInfo& ci, in
 #pragma unroll
       for (int u = 0; u < G; ++u) {
         const int j = G * g + u;
-        r[u] = (p.residual && j < ncol) ? p.residual[(size_t)(cb + j) * p.ldy + row] : 0.0f;
+        // the residual is the previous kernel's output: read through L2
+        r[u] = (p.residual && j < ncol) ? __ldcg(p.residual + (size_t)(cb + j) * p.ldy + row) : 0.0f;
       }
 #pragma unroll
       for (int u = 0; u < G; ++u) {
@@ -966,21 +967,27 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 3)
                                                  reinterpret_cast<float*>(smem_s), &is_last);
 }
 
+// Without a valid key for a column (an lm_head wait ran out) that column
+// keeps its token and position, and kErrNoToken is recorded.
 __global__ void cols_advance_kernel(unsigned long long* __restrict__ keys, int cols,
                                     const int* __restrict__ col_slot, int* __restrict__ col_token,
                                     int* __restrict__ col_pos, int* __restrict__ history,
-                                    int max_seq) {
+                                    int max_seq, int vocab) {
   pdl_trigger();
   pdl_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   const unsigned long long key = keys[c];
-  const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+  keys[c] = 0ull;
+  int idx = 0;
+  if (!argmax_token(key, vocab, &idx)) {
+    atomicOr(&g_batch_error, kErrNoToken);
+    return;
+  }
   const int p = col_pos[c];
   if (history && p >= 0 && p < max_seq) history[(size_t)col_slot[c] * max_seq + p] = idx;
   col_token[c] = idx;
   col_pos[c] = p + 1;
-  keys[c] = 0ull;
 }
 
 }  // namespace
@@ -1016,9 +1023,14 @@ int make_cols_map(CUtensorMap* map, const uint16_t* plane, int kp) {
   return make_f16_tile_map(map, plane, kBatchMaxCols, kp, kBatchMaxCols);
 }
 
+cudaError_t batch_prepare_device();
+
 cudaError_t batch_prepare() {
-  static bool done = false;
-  if (done) return cudaSuccess;
+  static DeviceOnce once;
+  return once.run(batch_prepare_device);
+}
+
+cudaError_t batch_prepare_device() {
   cudaError_t e = cudaFuncSetAttribute(batch_gemm_kernel<DQMK_Q80>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)gemm_smem<DQMK_Q80>());
@@ -1046,7 +1058,6 @@ cudaError_t batch_prepare() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attention_cols_stream_kernel<7>,
                              cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  if (e == cudaSuccess) done = true;
   return e;
 }
 
@@ -1140,10 +1151,10 @@ cudaError_t launch_attention_cols(const BatchAttn& a, cudaStream_t s, bool pdl) 
 }
 
 cudaError_t launch_cols_advance(unsigned long long* keys, int cols, const int* col_slot,
-                                int* col_token, int* col_pos, int* history, int max_seq,
+                                int* col_token, int* col_pos, int* history, int max_seq, int vocab,
                                 cudaStream_t s, bool pdl) {
   return launch(cols_advance_kernel, dim3(1), dim3(kBatchMaxCols), 0, s, pdl, keys, cols, col_slot,
-                col_token, col_pos, history, max_seq);
+                col_token, col_pos, history, max_seq, vocab);
 }
 
 cudaError_t read_batch_error(unsigned int* flags, bool clear) {

@@ -92,9 +92,10 @@ int batch_attention_splits(int cols, int n_kv_heads, int max_seq);
 size_t batch_attention_partials_floats(int cols, int n_heads, int head_dim, int max_splits);
 cudaError_t launch_attention_cols(const BatchAttn& a, cudaStream_t s, bool pdl);
 // Greedy step of every column: token[c] = argmax from keys[c] (keys reset),
-// history[slot][pos] = token, pos[c] += 1.
+// history[slot][pos] = token, pos[c] += 1; a column without a valid key in
+// [0, vocab) keeps its state and the batch error flag records kErrNoToken.
 cudaError_t launch_cols_advance(unsigned long long* keys, int cols, const int* col_slot,
-                                int* col_token, int* col_pos, int* history, int max_seq,
+                                int* col_token, int* col_pos, int* history, int max_seq, int vocab,
                                 cudaStream_t s, bool pdl);
 
 }  // namespace dqmk

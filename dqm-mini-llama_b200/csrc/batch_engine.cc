@@ -108,11 +108,11 @@ int ensure_batch_weights(dqmk_model* m) {
 }
 
 int check_errors(const char* api) {
-  unsigned int f0 = 0, f1 = 0;
+  unsigned int f0 = 0, f1 = 0, f2 = 0;
   DQMK_CUDA_RET(api, read_batch_error(&f0, true));
   DQMK_CUDA_RET(api, read_device_error(&f1, true));
-  if (f0 | f1) return fail(DQMK_ERR_TIMEOUT, std::string(api) + ": a device-side wait timed out");
-  return DQMK_OK;
+  DQMK_CUDA_RET(api, read_prefill_error(&f2, true));
+  return device_flags_status(api, f0 | f1 | f2);
 }
 
 BatchGemm gemm_args(const dqmk_batch* b, const Packed& w, const BatchWeight& bw, int n_cols,
@@ -141,25 +141,14 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
   const dqmk_model_config& c = m->cfg;
   const dqmk_tp_plan& tp = m->tp;
   const bool tpar = tp.world > 1;
-  // Under tensor parallelism the step interleaves NCCL kernels with its own;
-  // with programmatic dependent launch there, two ranks decoding the same
-  // prompt in two slots produced diverging greedy tokens on 2 GPUs, with plain
-  // launches they match the oracle in both slots.  Until that race is found
-  // the tensor-parallel step launches every kernel plainly
-  // (DQMK_BATCH_TP_PDL=1 in the environment restores the chained launches,
-  // for diagnosing it).
-  static const bool tp_pdl = [] {
-    const char* v = std::getenv("DQMK_BATCH_TP_PDL");
-    return v && v[0] == '1';
-  }();
-  const bool pdl = use_pdl() && (!tpar || tp_pdl);
+  const bool pdl = use_pdl();
   cudaStream_t s = b->stream;
   const int hd = c.head_dim;
   const int qd = tp.n_q_heads * hd;
   const float eps = c.rms_norm_eps;
   int rc;
   DQMK_CUDA_RET(kApi, launch_embed_rows(m->embd.qtype, m->embd.qs(), m->embd.d(), c.dim,
-                                        m->embd.kp, b->col_token(), n, b->x, s));
+                                        m->embd.kp, c.vocab_size, b->col_token(), n, b->x, s));
   const int splits = batch_attention_splits(n, tp.n_kv_heads, b->max_seq);
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = m->layers[l];
@@ -243,7 +232,8 @@ int enqueue_batch_step(dqmk_batch* b, int n, bool with_logits) {
   DQMK_CUDA_RET(kApi, launch_batch_gemm(m->batch_lm.map, m->batch_lm.dmap, b->x_dim[0], b->x_dim[1], lg, s, pdl));
   if (tpar && (rc = tp_allreduce_max_u64(m->comm, b->keys_arg, n, s, kApi))) return rc;
   DQMK_CUDA_RET(kApi, launch_cols_advance(b->keys_arg, n, b->col_slot(), b->col_token(),
-                                          b->col_pos(), b->history, b->max_seq, s, false));
+                                          b->col_pos(), b->history, b->max_seq, c.vocab_size, s,
+                                          false));
   return DQMK_OK;
 }
 
@@ -299,10 +289,16 @@ int validate_cols(const dqmk_batch* b, const int* slots, const int* tokens, cons
       return fail(DQMK_ERR_RANGE, std::string(kApi) + ": position out of range");
     seen.emplace_back(sl, positions[i]);
   }
+  // Each column writes KV and history at positions [pos, pos + n_steps) of
+  // its slot; two columns of one slot must not share any of them.
   std::sort(seen.begin(), seen.end());
   for (size_t i = 1; i < seen.size(); ++i)
-    if (seen[i] == seen[i - 1])
-      return fail(DQMK_ERR_INVALID, std::string(kApi) + ": a (slot, position) appears twice");
+    if (seen[i].first == seen[i - 1].first && seen[i].second < seen[i - 1].second + n_steps)
+      return fail(DQMK_ERR_INVALID,
+                  std::string(kApi) + (n_steps > 1
+                                           ? ": two columns of one slot would write the same "
+                                             "positions over the decoded steps"
+                                           : ": a (slot, position) appears twice"));
   return DQMK_OK;
 }
 

@@ -166,4 +166,16 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
   return ((unsigned long long)b << 32) | (0xffffffffu - idx);
 }
 
+// The token id a folded argmax key names; false when nothing was folded in
+// (key 0: the lm_head's bounded wait ran out before its rows were scored) or
+// the id lies outside [0, limit).  Greedy steps keep their state then, so a
+// timed-out step never feeds an invalid id to the next embedding.
+__device__ __forceinline__ bool argmax_token(unsigned long long key, int limit, int* token) {
+  if (key == 0ull) return false;
+  const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+  if (idx < 0 || idx >= limit) return false;
+  *token = idx;
+  return true;
+}
+
 }  // namespace dqmk

@@ -60,13 +60,12 @@ struct dqmk_context {
   char** peer_base = nullptr;
   unsigned int* tp_seq = nullptr;
   bool p2p = false;
+  // a peer wait of this context ran out: the ranks' exchange counters and
+  // parity slots may disagree from then on, so the context refuses to run
+  bool tp_failed = false;
+  // failure-detection hook: lm_head tile withheld in captured steps (-1: none)
+  int lm_withhold = -1;
   std::vector<void*> ipc_opened;
-  // persistent decode step: phase table, grid-barrier words, launch shape
-  StepPhase* step_phases = nullptr;
-  int step_n = 0, step_grid = 0;
-  int step_set[3] = {-1, -1, -1};
-  size_t step_smem = 0;
-  unsigned int* step_sync = nullptr;
   float *keys = nullptr, *values = nullptr, *partials = nullptr;
   // device state block: [argmax u64][lm ticket u32][token i32][pos i32][pad]
   //                     [attention tickets u32 x n_kv] ...
@@ -536,12 +535,8 @@ extern "C" int dqmk_model_stats_reset(dqmk_model* m) {
 extern "C" size_t dqmk_model_memory_bytes(const dqmk_model* m) { return m ? m->memory_bytes : 0; }
 
 // ------------------------------------------------------------------ context
-namespace {
-
 // Programmatic dependent launch between the kernels of a step; DQMK_PDL=0 in
 // the environment launches them plainly instead (diagnostics: same work).
-}  // namespace
-
 bool dqmk::use_pdl() {
   static const bool on = [] {
     const char* v = std::getenv("DQMK_PDL");
@@ -565,10 +560,10 @@ PeerSet peer_set(const dqmk_context* x) {
 
 int enqueue_lm_head(dqmk_context* x);
 
-// The decode step.  With rec set (single-GPU only), the embedding, GEMV and
-// attention operations are recorded as phases of the persistent step kernel
-// instead of being launched, and the lm_head is left to enqueue_lm_head.
-int enqueue_step(dqmk_context* x, std::vector<StepPhase>* rec = nullptr) {
+// The decode step: embedding, per layer QKV GEMV (RMSNorm, bias, RoPE, KV
+// store), attention, O GEMV (+ residual), gate/up GEMV (RMSNorm, SwiGLU),
+// down GEMV (+ residual); then the lm_head with the greedy advance.
+int enqueue_step(dqmk_context* x) {
   const char* api = "ForwardToken";
   const bool pdl = use_pdl();
   dqmk_model* m = x->m;
@@ -579,24 +574,8 @@ int enqueue_step(dqmk_context* x, std::vector<StepPhase>* rec = nullptr) {
   const PeerSet ps = peer_set(x);
   cudaStream_t s = x->stream;
   int rc;
-  auto gemv_op = [&](const GemvArgs& a) -> cudaError_t {
-    if (!rec) return launch_gemv(a, s, pdl);
-    StepPhase p = {};
-    p.kind = kPhaseGemv;
-    p.variant = gemv_variant_id(a);
-    p.g = a;
-    rec->push_back(p);
-    return cudaSuccess;
-  };
-  auto attn_op = [&](const AttnArgs& a) -> cudaError_t {
-    if (!rec) return launch_attention(a, s, pdl);
-    StepPhase p = {};
-    p.kind = kPhaseAttn;
-    p.chunk_cap = attention_chunk_cap(a.max_seq, a.max_splits);
-    p.at = a;
-    rec->push_back(p);
-    return cudaSuccess;
-  };
+  auto gemv_op = [&](const GemvArgs& a) { return launch_gemv(a, s, pdl); };
+  auto attn_op = [&](const AttnArgs& a) { return launch_attention(a, s, pdl); };
   EmbedArgs ea = {};
   ea.qtype = m->embd.qtype;
   ea.qs = m->embd.qs();
@@ -607,14 +586,7 @@ int enqueue_step(dqmk_context* x, std::vector<StepPhase>* rec = nullptr) {
   ea.token_dev = x->token_slot();
   ea.y = x->x;
   ea.argmax_slot = x->argmax_slot();
-  if (rec) {
-    StepPhase p = {};
-    p.kind = kPhaseEmbed;
-    p.e = ea;
-    rec->push_back(p);
-  } else {
-    DQMK_CUDA_RET(api, launch_embed_packed(ea, s));
-  }
+  DQMK_CUDA_RET(api, launch_embed_packed(ea, s));
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = m->layers[l];
     GemvArgs g = {};
@@ -718,7 +690,6 @@ int enqueue_step(dqmk_context* x, std::vector<StepPhase>* rec = nullptr) {
       DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
     }
   }
-  if (rec) return DQMK_OK;
   return enqueue_lm_head(x);
 }
 
@@ -752,15 +723,19 @@ int enqueue_lm_head(dqmk_context* x) {
   lg.pos_slot = x->pos_slot();
   lg.history = x->history_dev;
   lg.history_cap = c.max_seq_len;
-  DQMK_CUDA_RET(api, launch_gemv(lg, s, pdl));
+  if (x->lm_withhold != -1) {  // failure-detection hook (dqmk_context_withhold_lm_head)
+    DQMK_CUDA_RET(api, launch_gemv_tma_skip(lg, s, x->lm_withhold));
+  } else {
+    DQMK_CUDA_RET(api, launch_gemv(lg, s, pdl));
+  }
   if (p2p) {
     DQMK_CUDA_RET(api, launch_tp_argmax_advance(ps, x->argmax_slot(), x->token_slot(),
                                                 x->pos_slot(), x->history_dev, c.max_seq_len,
-                                                s, pdl));
+                                                c.vocab_size, s, pdl));
   } else if (tpar) {  // global greedy choice: max over the ranks' (value, index) keys
     if ((rc = tp_allreduce_max_u64(m->comm, x->argmax_slot(), 1, s, api))) return rc;
     DQMK_CUDA_RET(api, launch_greedy_advance(x->argmax_slot(), x->token_slot(), x->pos_slot(),
-                                             x->history_dev, c.max_seq_len, s));
+                                             x->history_dev, c.max_seq_len, c.vocab_size, s));
   }
   return DQMK_OK;
 }
@@ -783,77 +758,16 @@ int copy_logits(dqmk_context* x, float* logits, const char* api) {
   return DQMK_OK;
 }
 
-// The persistent step kernel (step.cu) runs the embedding and the layers of a
-// single-GPU step as one cooperative launch.  Measured slower than the
-// kernel-per-operation chain under programmatic dependent launch (a grid
-// barrier costs 2.5-3.5 us, one per phase), so it runs only with
-// DQMK_STEP_KERNEL=1 in the environment.  Variant sets without an
-// instantiation, head sizes other than 64 / 128 and tensor parallelism always
-// use the chain.
-bool step_kernel_enabled() {
-  const char* v = std::getenv("DQMK_STEP_KERNEL");
-  return v && v[0] == '1';
-}
-
-int prepare_step_kernel(dqmk_context* x, bool* use) {
-  *use = false;
-  const char* api = "ForwardToken";
-  dqmk_model* m = x->m;
-  const dqmk_model_config& c = m->cfg;
-  if (!step_kernel_enabled() || m->tp.world > 1 || (c.head_dim != 64 && c.head_dim != 128))
-    return DQMK_OK;
-  std::vector<StepPhase> phases;
-  int rc = enqueue_step(x, &phases);
-  if (rc) return rc;
-  size_t smem = 0;
-  std::vector<int> ids;
-  for (const StepPhase& p : phases) {
-    if (p.kind == kPhaseGemv) {
-      ids.push_back(p.variant);
-      smem = std::max(smem, (size_t)p.g.kp * sizeof(float));
-    } else if (p.kind == kPhaseAttn) {
-      smem = std::max(smem, step_attention_smem(c.head_dim, p.chunk_cap, p.at.max_splits));
-    }
-  }
-  if (!step_kernel_variants(ids.data(), (int)ids.size(), x->step_set)) return DQMK_OK;
-  int grid = 0;
-  if (step_kernel_grid(x->step_set, smem, &grid) != cudaSuccess) {
-    cudaGetLastError();
-    return DQMK_OK;  // no resident grid at this shared-memory size: keep the chain
-  }
-  void* p = nullptr;
-  if (!x->step_phases) {
-    if ((rc = dev_alloc(x->allocs, phases.size() * sizeof(StepPhase), &p, api))) return rc;
-    x->step_phases = static_cast<StepPhase*>(p);
-    if ((rc = dev_alloc(x->allocs, 4 * sizeof(unsigned int), &p, api))) return rc;
-    x->step_sync = static_cast<unsigned int*>(p);
-  }
-  DQMK_CUDA_RET(api, cudaMemcpy(x->step_phases, phases.data(), phases.size() * sizeof(StepPhase),
-                                cudaMemcpyHostToDevice));
-  DQMK_CUDA_RET(api, cudaMemset(x->step_sync, 0, 4 * sizeof(unsigned int)));
-  x->step_n = (int)phases.size();
-  x->step_grid = grid;
-  x->step_smem = smem;
-  *use = true;
-  return DQMK_OK;
-}
-
 int ensure_graph(dqmk_context* x) {
-  if (x->graph) return DQMK_OK;
   const char* api = "ForwardToken";
-  bool step = false;
-  int rc = prepare_step_kernel(x, &step);
-  if (rc) return rc;
+  if (x->tp_failed)
+    return fail(DQMK_ERR_TIMEOUT,
+                std::string(api) + ": a peer-memory exchange of this context timed out earlier; "
+                                   "destroy and recreate the contexts of every rank");
+  if (x->graph) return DQMK_OK;
   cudaGraph_t g = nullptr;
   DQMK_CUDA_RET(api, cudaStreamBeginCapture(x->stream, cudaStreamCaptureModeThreadLocal));
-  if (step) {
-    const StepSync sync{x->step_sync, x->step_sync + 1};
-    cudaError_t e = launch_step_kernel(x->step_set, x->step_phases, x->step_n, sync,
-                                       x->step_grid, x->step_smem, x->stream);
-    rc = e == cudaSuccess ? enqueue_lm_head(x) : cuda_fail(api, e);
-  } else {
-    rc = enqueue_step(x);
-  }
+  const int rc = enqueue_step(x);
   cudaError_t e = cudaStreamEndCapture(x->stream, &g);
   if (rc != DQMK_OK) {
     if (g) cudaGraphDestroy(g);
@@ -883,16 +797,12 @@ void count_token(dqmk_context* x, int pos) {
 // After a synchronizing call: a bounded device wait that ran out surfaces as
 // DQMK_ERR_TIMEOUT (the flag is cleared so the context stays usable).
 int check_device_error(const char* api, dqmk_context* x = nullptr) {
-  unsigned int flags = 0, tp_flags = 0, step_flags = 0;
+  unsigned int flags = 0, tp_flags = 0, ops_flags = 0;
   DQMK_CUDA_RET(api, read_device_error(&flags, true));
   DQMK_CUDA_RET(api, read_tp_error(&tp_flags, true));
-  DQMK_CUDA_RET(api, read_step_error(&step_flags, true));
-  // a barrier wait that ran out can leave arrivals counted: start clean
-  if (step_flags && x && x->step_sync)
-    DQMK_CUDA_RET(api, cudaMemset(x->step_sync, 0, 4 * sizeof(unsigned int)));
-  flags |= tp_flags | step_flags;
-  if (flags) return fail(DQMK_ERR_TIMEOUT, std::string(api) + ": a device-side wait timed out");
-  return DQMK_OK;
+  DQMK_CUDA_RET(api, read_ops_error(&ops_flags, true));
+  if ((tp_flags & kErrTimeout) && x && x->p2p) x->tp_failed = true;
+  return device_flags_status(api, flags | tp_flags | ops_flags);
 }
 
 int validate_token(const dqmk_context* x, int token, int pos) {
@@ -994,7 +904,7 @@ int prefill_chunk(dqmk_context* x, const int* tokens, int pos0, int n, bool want
   // a copy from pageable memory is staged by the driver before it returns
   DQMK_CUDA_RET(api, cudaMemcpyAsync(b.tokens, tokens, n * sizeof(int), cudaMemcpyHostToDevice, s));
   DQMK_CUDA_RET(api, launch_embed_rows(m->embd.qtype, m->embd.qs(), m->embd.d(), c.dim,
-                                       m->embd.kp, b.tokens, n, b.x, s));
+                                       m->embd.kp, c.vocab_size, b.tokens, n, b.x, s));
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = m->layers[l];
     // attention block: RMSNorm + fp16 split, fused QKV GEMM (bias, RoPE, cache
@@ -1257,6 +1167,20 @@ extern "C" int dqmk_context_tp_connect(dqmk_context* x, const unsigned char* han
     x->graph = nullptr;
   }
   x->p2p = true;
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_context_withhold_lm_head(dqmk_context* x, int tile) {
+  const char* api = "dqmk_context_withhold_lm_head";
+  if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + ": null context");
+  if (tile < kSkipAllTiles) return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid tile");
+  cudaSetDevice(x->m->device);
+  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  if (x->graph) {  // the step is captured again with (or without) the hook
+    cudaGraphExecDestroy(x->graph);
+    x->graph = nullptr;
+  }
+  x->lm_withhold = tile;
   return DQMK_OK;
 }
 

@@ -33,6 +33,8 @@ namespace {
 
 using namespace gv;
 
+__device__ unsigned int g_device_error;  // kErrTimeout / kErrNoToken
+
 template <int QT, int RPW, int CPL, int GW, bool PEER>
 __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
   extern __shared__ float4 xs[];
@@ -42,7 +44,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
   ph.prefetch(a, blockIdx.x, gridDim.x);
   pdl_trigger();
   pdl_wait();
-  gemv_run<QT, RPW, CPL, GW, PEER>(ph, a, xs, gridDim.x);
+  gemv_run<QT, RPW, CPL, GW, PEER>(ph, a, xs, gridDim.x, &g_device_error);
 }
 
 // ------------------------------------------------------------ launch table
@@ -50,20 +52,27 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
 // case.  Run before any stream capture (context creation does).
 template <int QT, int RPW, int CPL, int GW, bool PEER>
 cudaError_t prepare_t(int* max_ctas_out) {
-  static int max_ctas = -1;
-  if (max_ctas < 0) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<QT, RPW, CPL, GW, PEER>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         200 * 1024);
-    if (e != cudaSuccess) return e;
+  static DeviceOnce once;
+  static int max_ctas[kMaxDevices];  // written under once's lock, per device
+  cudaError_t e = once.run([] {
+    int dev = 0;
+    cudaError_t r = cudaGetDevice(&dev);
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(gemv_kernel<QT, RPW, CPL, GW, PEER>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm,
-                                                      gemv_kernel<QT, RPW, CPL, GW, PEER>,
-                                                      kWarps * 32, 4096 * sizeof(float));
-    if (e != cudaSuccess) return e;
-    max_ctas = (per_sm > 0 ? per_sm : 1) * sm_count();
+    if (r == cudaSuccess)
+      r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &per_sm, gemv_kernel<QT, RPW, CPL, GW, PEER>, kWarps * 32, 4096 * sizeof(float));
+    if (r == cudaSuccess) max_ctas[dev] = (per_sm > 0 ? per_sm : 1) * sm_count();
+    return r;
+  });
+  if (e != cudaSuccess) return e;
+  if (max_ctas_out) {
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    *max_ctas_out = max_ctas[dev];
   }
-  if (max_ctas_out) *max_ctas_out = max_ctas;
   return cudaSuccess;
 }
 
@@ -103,8 +112,6 @@ constexpr int kTmaWarps = 8;                        // consumer warps
 constexpr int kTmaConsumers = kTmaWarps * 32;
 constexpr int kTmaThreads = kTmaConsumers + 32;     // + the producer warp
 constexpr int kMaxStages = 4;
-
-__device__ unsigned int g_device_error;  // bit 0: a bounded wait timed out
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -151,7 +158,8 @@ __device__ __forceinline__ bool tma_issue(const GemvArgs& a, const TmaGeo& g, un
   const uint32_t qbytes = (uint32_t)rows * g.row_bytes;
   const uint32_t dbytes = (uint32_t)rows * g.nbk * 2;
   const uint32_t dbulk = (dbytes & 15u) == 0 ? dbytes : 0u;  // ragged tail: scales read directly
-  if (tile == skip_tile) return false;  // failure-detection hook: nothing arrives
+  // failure-detection hook: nothing arrives for the withheld tile (or tiles)
+  if (tile == skip_tile || skip_tile == kSkipAllTiles) return false;
   unsigned char* st = stages + (size_t)s * g.stage_bytes;
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   mbar_expect_tx(&full[s], qbytes + dbulk);
@@ -504,22 +512,23 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
     if (lane == 0) best_w[wid] = best;
   }
   __syncthreads();
-  if (*abort) {
+  if (*abort && producer && lane == 0) {
     // every role has stopped; let each copy still in flight land before the
     // CTA's shared memory goes away
-    if (producer && lane == 0) {
-      volatile int never = 0;
-      for (int s = 0; s < nstage; ++s)
-        if (last_issued[s] >= 0)
-          tc::bar_wait(&full[s], (uint32_t)(last_issued[s] / nstage) & 1u, &never,
-                       &g_device_error);
-    }
-    return;
+    volatile int never = 0;
+    for (int s = 0; s < nstage; ++s)
+      if (last_issued[s] >= 0)
+        tc::bar_wait(&full[s], (uint32_t)(last_issued[s] / nstage) & 1u, &never,
+                     &g_device_error);
   }
+  // Every CTA, aborted or not, folds in what it scored and takes its
+  // completion ticket exactly once, so the last CTA's greedy step and the
+  // ticket reset always happen (a step whose rows were all withheld finds no
+  // key and keeps the greedy state).
   if (a.epi == kEpiLogits && tid == 0) {
     unsigned long long b = 0ull;
     for (int w = 0; w < kTmaWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
-    logits_finish(a, b, gridDim.x);
+    logits_finish(a, b, gridDim.x, &g_device_error);
   }
 }
 
@@ -569,32 +578,41 @@ TmaPlan tma_plan(const GemvArgs& a) {
 
 template <int QT, int RPW>
 cudaError_t tma_prepare() {
-  return cudaFuncSetAttribute(gemv_tma_kernel<QT, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              210 * 1024);
+  static DeviceOnce once;
+  return once.run([] {
+    return cudaFuncSetAttribute(gemv_tma_kernel<QT, RPW>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
+  });
 }
 
 template <int QT, int RPW>
 cudaError_t tma_launch(const GemvArgs& a, const TmaPlan& p, cudaStream_t stream, bool pdl,
                        int skip_tile) {
-  static bool prepared = false;
-  if (!prepared) {
-    cudaError_t e = tma_prepare<QT, RPW>();
-    if (e != cudaSuccess) return e;
-    prepared = true;
-  }
+  cudaError_t e = tma_prepare<QT, RPW>();
+  if (e != cudaSuccess) return e;
   // the plan counts CTAs per SM by shared memory; registers may allow fewer,
   // and a grid beyond what is resident at once would run as a second wave
-  static size_t occ_smem = 0;
-  static int occ = 0;
-  if (occ_smem != p.smem) {
-    int n = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_tma_kernel<QT, RPW>,
-                                                                  kTmaThreads, p.smem);
-    if (e != cudaSuccess) return e;
-    occ = n > 0 ? n : 1;
-    occ_smem = p.smem;
+  // (the figure is cached per device and shared-memory size)
+  static std::mutex mu;
+  static size_t occ_smem[kMaxDevices];
+  static int occ[kMaxDevices];
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  int resident = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (occ_smem[dev] != p.smem) {
+      int n = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_tma_kernel<QT, RPW>,
+                                                        kTmaThreads, p.smem);
+      if (e != cudaSuccess) return e;
+      occ[dev] = n > 0 ? n : 1;
+      occ_smem[dev] = p.smem;
+    }
+    resident = occ[dev];
   }
-  const int grid = std::min(p.grid, sm_count() * occ);
+  const int grid = std::min(p.grid, sm_count() * resident);
   return launch(gemv_tma_kernel<QT, RPW>, dim3(grid), dim3(kTmaThreads), p.smem, stream, pdl, a,
                 p.stages, skip_tile);
 }
@@ -842,13 +860,13 @@ extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, cons
 }
 
 extern "C" int dqmk_device_error(int clear) {
-  unsigned int flags = 0, prefill_flags = 0, tp_flags = 0, step_flags = 0, batch_flags = 0;
+  unsigned int flags = 0, prefill_flags = 0, tp_flags = 0, ops_flags = 0, batch_flags = 0;
   cudaError_t e = read_device_error(&flags, clear != 0);
   if (e == cudaSuccess) e = read_prefill_error(&prefill_flags, clear != 0);
   if (e == cudaSuccess) e = read_tp_error(&tp_flags, clear != 0);
-  if (e == cudaSuccess) e = read_step_error(&step_flags, clear != 0);
+  if (e == cudaSuccess) e = read_ops_error(&ops_flags, clear != 0);
   if (e == cudaSuccess) e = read_batch_error(&batch_flags, clear != 0);
-  flags |= prefill_flags | tp_flags | step_flags | batch_flags;
+  flags |= prefill_flags | tp_flags | ops_flags | batch_flags;
   if (e != cudaSuccess) {
     cuda_fail("dqmk_device_error", e);
     return -1;

@@ -1,6 +1,6 @@
 // gemv_dev.cuh -- device code of the batch-1 decode GEMV over Q8_0 / Q4_0
-// weights, shared by the standalone kernels (gemv.cu) and the persistent
-// decode step (step.cu).  See gemv.cu for the design.
+// weights, instantiated by the kernels of gemv.cu.  See gemv.cu for the
+// design.
 #pragma once
 
 #include "common.cuh"
@@ -8,8 +8,7 @@
 
 // Every register-GEMV instantiation the dispatcher (gemv.cu, gemv_variant_id)
 // can pick, with its id: X(id, quant type, rows per group, chunks per lane,
-// warps per row group).  The persistent decode step instantiates the per-layer
-// ones of one quant type (the wide lm_head forms stay out of it).
+// warps per row group).
 #define DQMK_GEMV_VARIANT_IDS_Q80(X)                                                        \
   X(0, DQMK_Q80, 2, 1, 1) X(1, DQMK_Q80, 2, 2, 1) X(2, DQMK_Q80, 4, 2, 1)                  \
   X(3, DQMK_Q80, 2, 2, 4) X(4, DQMK_Q80, 2, 3, 4) X(5, DQMK_Q80, 2, 4, 4)
@@ -373,9 +372,11 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const flo
 // Thread 0 of each CTA with the CTA's best (value, index) key: fold it into
 // the device argmax; the last CTA then advances the greedy state (token,
 // position, history) unless ticket is null (tensor parallel: the ranks' keys
-// are combined by a later kernel).
+// are combined by a later kernel).  Without a valid key (a CTA's bounded wait
+// ran out before its rows were scored) the state is kept and kErrNoToken
+// recorded in *err.
 __device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long long b,
-                                              int n_ctas) {
+                                              int n_ctas, unsigned int* err) {
   if (!a.argmax_slot) return;
   atomicMax(a.argmax_slot, b);
   if (!a.ticket) return;
@@ -385,7 +386,11 @@ __device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long l
   __threadfence();
   const unsigned long long key = atomicAdd(a.argmax_slot, 0ull);
   *a.ticket = 0u;
-  const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+  int idx = 0;
+  if (!argmax_token(key, a.row_offset + a.n_rows, &idx)) {
+    atomicOr(err, kErrNoToken);
+    return;
+  }
   const int p = *a.pos_slot;
   if (a.history && p >= 0 && p < a.history_cap) a.history[p] = idx;
   *a.token_slot = idx;
@@ -395,9 +400,8 @@ __device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long l
 // One GEMV on one CTA of a grid of n_ctas, in two parts: prefetch() computes
 // the CTA's share of row groups and loads its first weight tile and the
 // RMSNorm weight into registers -- none of it depends on the previous step of
-// the chain, so callers issue it before waiting (griddepcontrol.wait in the
-// kernel, a grid barrier in the persistent decode step); run() stages x and
-// does the math and the epilogue.
+// the chain, so callers issue it before griddepcontrol.wait; run() stages x
+// and does the math and the epilogue.
 template <int QT, int RPW, int CPL, int GW>
 struct GemvPhase {
   static_assert(GW == 1 || GW == kWarps, "a row group is one warp or the whole CTA");
@@ -438,7 +442,7 @@ struct GemvPhase {
 
 template <int QT, int RPW, int CPL, int GW, bool PEER>
 __device__ __forceinline__ void gemv_run(GemvPhase<QT, RPW, CPL, GW>& ph, const GemvArgs& a,
-                                         float4* xs, int n_ctas) {
+                                         float4* xs, int n_ctas, unsigned int* err) {
   constexpr int GT = GW * 32;
   __shared__ float red[kWarps];
   __shared__ float red_rows[kWarps][RPW];
@@ -514,7 +518,7 @@ __device__ __forceinline__ void gemv_run(GemvPhase<QT, RPW, CPL, GW>& ph, const 
     if (tid == 0) {
       unsigned long long b = 0ull;
       for (int w = 0; w < kWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
-      logits_finish(a, b, n_ctas);
+      logits_finish(a, b, n_ctas, err);
     }
   }
   if constexpr (PEER) peer_signal(a.peer, 0, a.peer.seq[0] + 1, n_ctas);

@@ -3,8 +3,10 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 // Returns the dqmk status of a failed CUDA call from the enclosing function.
@@ -21,7 +23,41 @@ void set_error(const std::string& msg);
 int fail(int status, const std::string& msg);
 int cuda_fail(const char* api, cudaError_t err);
 const char* last_error_cstr();
+// SM count of the current device (cached per device).
 int sm_count();
+
+// Kernel attributes (cudaFuncSetAttribute) and occupancy figures belong to
+// the device that is current when they are set or queried, so every one-time
+// set-up runs once per device: fn() with that device current.
+constexpr int kMaxDevices = 64;
+class DeviceOnce {
+ public:
+  template <typename F>
+  cudaError_t run(F fn) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (done_[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (done_[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+    e = fn();
+    if (e == cudaSuccess) done_[dev].store(true, std::memory_order_release);
+    return e;
+  }
+
+ private:
+  std::mutex mu_;
+  std::atomic<bool> done_[kMaxDevices] = {};
+};
+
+// Device error flags, per kernel family; every flag word uses the same bits.
+constexpr unsigned int kErrTimeout = 1u;   // a bounded wait ran out
+constexpr unsigned int kErrNoToken = 2u;   // greedy step without a valid argmax (state kept)
+constexpr unsigned int kErrBadToken = 4u;  // embedding of a token id outside [0, vocab)
+// DQMK_OK when no flag is set, else DQMK_ERR_TIMEOUT with a message prefixed
+// by `api` that names what the flags record.
+int device_flags_status(const char* api, unsigned int flags);
 // Library-owned per-device scratch (grown on demand, zero-filled when
 // (re)allocated).  Callers that use it from several streams at once race.
 cudaError_t device_scratch(size_t bytes, void** out);
@@ -113,8 +149,10 @@ int gemv_variant_id(const GemvArgs& a);
 // Sets kernel attributes of every GEMV / attention instantiation; call
 // outside stream capture.
 cudaError_t gemv_prepare();
-// Failure-detection hook: the TMA GEMV with the copies of one tile withheld,
-// so that tile's bounded wait runs out and sets the device error flag.
+// Failure-detection hook: the TMA GEMV with the copies of one tile withheld
+// (skip_tile >= 0) or of every tile (kSkipAllTiles), so those bounded waits
+// run out and set the device error flag.
+constexpr int kSkipAllTiles = -2;
 cudaError_t launch_gemv_tma_skip(const GemvArgs& a, cudaStream_t stream, int skip_tile);
 // Device error flags set by bounded waits (bit 0: timeout); optionally cleared.
 cudaError_t read_device_error(unsigned int* flags, bool clear);
@@ -151,18 +189,20 @@ cudaError_t launch_embed_blocks(int qtype, const void* blocks, int dim, int toke
                                 cudaStream_t s);
 cudaError_t launch_argmax(const float* x, int n, unsigned long long* slot, int* index,
                           cudaStream_t s);
+// Flags of the embedding and greedy-advance kernels (ops.cu).
+cudaError_t read_ops_error(unsigned int* flags, bool clear);
 // Peer-memory tensor parallelism (tp_p2p.cu): wait for every rank's partial
 // of exchange seq[0] + 1, x += their sum (fixed rank order); and the greedy
 // step after a vocabulary-parallel lm_head (max over the ranks' keys).
 cudaError_t launch_tp_reduce(float* x, const PeerSet& ps, cudaStream_t s, bool pdl);
 cudaError_t launch_tp_argmax_advance(const PeerSet& ps, const unsigned long long* local_key,
-                                     int* token, int* pos, int* history, int cap, cudaStream_t s,
-                                     bool pdl);
+                                     int* token, int* pos, int* history, int cap, int vocab,
+                                     cudaStream_t s, bool pdl);
 cudaError_t read_tp_error(unsigned int* flags, bool clear);
 // Multi-sequence decode GEMM (batch.cu): bounded-wait flag.
 cudaError_t read_batch_error(unsigned int* flags, bool clear);
 cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, int* pos,
-                                  int* history, int cap, cudaStream_t s);
+                                  int* history, int cap, int vocab, cudaStream_t s);
 cudaError_t launch_kv_write(float* keys, float* values, int max_seq, int n_kv_heads,
                             int head_dim, int layer, int pos, const float* k, const float* v,
                             cudaStream_t s);
@@ -185,30 +225,6 @@ int attention_splits(int max_seq, int n_kv_heads);
 size_t attention_partials_floats(int n_heads, int head_dim, int max_splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl);
 int attention_chunk_cap(int max_seq, int max_splits);
-
-// ------------------------------------------------------ persistent decode step
-enum StepPhaseKind : int { kPhaseEmbed = 0, kPhaseGemv = 1, kPhaseAttn = 2 };
-struct StepPhase {
-  int kind;
-  int variant;    // kPhaseGemv: gemv_variant_id of g
-  int chunk_cap;  // kPhaseAttn
-  GemvArgs g;
-  AttnArgs at;
-  EmbedArgs e;
-};
-struct StepSync {
-  unsigned int* count;  // grid-barrier arrivals
-  unsigned int* gen;    // grid-barrier generation
-};
-// The step kernel is instantiated per set of GEMV variants (at most three);
-// true with the set (ordered as instantiated) when one covers ids[0..n).
-bool step_kernel_variants(const int* ids, int n, int out[3]);
-// Dynamic shared memory -> the cooperative grid (resident CTAs x SMs).
-cudaError_t step_kernel_grid(const int set[3], size_t smem, int* grid);
-cudaError_t launch_step_kernel(const int set[3], const StepPhase* phases, int n_phases,
-                               const StepSync& sync, int grid, size_t smem, cudaStream_t s);
-size_t step_attention_smem(int head_dim, int chunk_cap, int max_splits);
-cudaError_t read_step_error(unsigned int* flags, bool clear);
 
 // host-side RoPE table in the reference's float arithmetic (src/ops.cc:18-23,
 // :40-45): entry [p][i] = (cos, sin) of p * 1/theta^(2i/head_dim).

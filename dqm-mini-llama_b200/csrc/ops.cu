@@ -30,18 +30,31 @@ int cuda_fail(const char* api, cudaError_t err) {
   return err == cudaErrorMemoryAllocation ? DQMK_ERR_NOMEM : DQMK_ERR_CUDA;
 }
 
+int device_flags_status(const char* api, unsigned int flags) {
+  if (!flags) return DQMK_OK;
+  std::string msg = std::string(api) + ": a device-side wait timed out";
+  if (flags & kErrNoToken) msg += "; a greedy step found no scored token and kept its state";
+  if (flags & kErrBadToken) msg += "; an embedding was asked for a token id outside the vocabulary";
+  return fail(DQMK_ERR_TIMEOUT, msg);
+}
+
 int sm_count() {
-  static int n = 0;
+  static std::atomic<int> cached[kMaxDevices];  // zero-initialized: not yet queried
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  int n = cached[dev].load(std::memory_order_relaxed);
   if (n == 0) {
-    int dev = 0, v = 0;
-    cudaGetDevice(&dev);
+    int v = 0;
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
     n = v > 0 ? v : 148;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }
 
 namespace {
+
+__device__ unsigned int g_ops_error;  // kErrNoToken / kErrBadToken
 
 constexpr int kMaxRopeHalf = 128;
 
@@ -110,9 +123,20 @@ __global__ void embed_f32_kernel(const float* __restrict__ table, int dim, int t
 }
 
 // Packed (planar) table row gather; also clears the greedy argmax slot for
-// the step this kernel opens.
+// the step this kernel opens.  A token id outside [0, vocab) (possible only
+// on the device, where the host cannot validate it) gathers nothing: the row
+// is zeroed and kErrBadToken recorded.
 __global__ void embed_packed_kernel(const EmbedArgs a) {
   const int token = a.token_dev ? *a.token_dev : a.token;
+  if (token < 0 || token >= a.vocab) {
+    for (int i = threadIdx.x; i < a.dim; i += blockDim.x) a.y[i] = 0.0f;
+    if (threadIdx.x == 0) {
+      atomicOr(&g_ops_error, kErrBadToken);
+      if (a.argmax_slot) *a.argmax_slot = 0ull;
+    }
+    pdl_trigger();
+    return;
+  }
   const int nbk = a.kp / 32;
   const size_t row_bytes = a.qtype == DQMK_Q80 ? (size_t)a.kp : (size_t)a.kp / 2;
   const uint8_t* q = a.qs + (size_t)token * row_bytes;
@@ -165,9 +189,10 @@ __global__ void argmax_kernel(const float* __restrict__ x, int n, unsigned long 
   if ((threadIdx.x & 31) == 0) atomicMax(slot, best);
 }
 
-__global__ void argmax_finish_kernel(unsigned long long* slot, int* index) {
-  const unsigned long long key = *slot;
-  *index = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+__global__ void argmax_finish_kernel(unsigned long long* slot, int n, int* index) {
+  int idx = 0;
+  if (!argmax_token(*slot, n, &idx)) atomicOr(&g_ops_error, kErrNoToken);
+  *index = idx;
   *slot = 0ull;
 }
 
@@ -235,16 +260,21 @@ cudaError_t launch_embed_blocks(int qtype, const void* blocks, int dim, int toke
 cudaError_t launch_argmax(const float* x, int n, unsigned long long* slot, int* index,
                           cudaStream_t s) {
   argmax_kernel<<<grid1d(n, 256), 256, 0, s>>>(x, n, slot);
-  argmax_finish_kernel<<<1, 1, 0, s>>>(slot, index);
+  argmax_finish_kernel<<<1, 1, 0, s>>>(slot, n, index);
   return cudaGetLastError();
 }
 
 // Greedy decode state after a tensor-parallel lm_head: the all-reduced
 // (value, index) key names the next token; record it, advance the position.
+// Without a valid key (an lm_head wait ran out) the state is kept and
+// kErrNoToken recorded.
 __global__ void greedy_advance_kernel(const unsigned long long* slot, int* token, int* pos,
-                                      int* history, int cap) {
-  const unsigned long long key = *slot;
-  const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+                                      int* history, int cap, int vocab) {
+  int idx = 0;
+  if (!argmax_token(*slot, vocab, &idx)) {
+    atomicOr(&g_ops_error, kErrNoToken);
+    return;
+  }
   const int p = *pos;
   if (history && p >= 0 && p < cap) history[p] = idx;
   *token = idx;
@@ -252,9 +282,18 @@ __global__ void greedy_advance_kernel(const unsigned long long* slot, int* token
 }
 
 cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, int* pos,
-                                  int* history, int cap, cudaStream_t s) {
-  greedy_advance_kernel<<<1, 1, 0, s>>>(slot, token, pos, history, cap);
+                                  int* history, int cap, int vocab, cudaStream_t s) {
+  greedy_advance_kernel<<<1, 1, 0, s>>>(slot, token, pos, history, cap, vocab);
   return cudaGetLastError();
+}
+
+cudaError_t read_ops_error(unsigned int* flags, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_ops_error, sizeof(unsigned int));
+  if (e == cudaSuccess && clear && *flags) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_ops_error, &zero, sizeof(unsigned int));
+  }
+  return e;
 }
 
 cudaError_t launch_kv_write(float* keys, float* values, int max_seq, int n_kv_heads,

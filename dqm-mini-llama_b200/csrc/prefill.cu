@@ -54,7 +54,7 @@ constexpr uint32_t kTmemCols = kAccBufs * BN;
 constexpr int kEpiWarps = 4;                 // one per TMEM lane quarter, 128 columns each
 constexpr int kGemmThreads = (2 + kEpiWarps) * 32;
 
-__device__ unsigned int g_prefill_error;  // bit 0: a bounded wait timed out
+__device__ unsigned int g_prefill_error;  // kErrTimeout / kErrBadToken
 
 using tc::bar_arrive;
 using tc::bar_expect_tx;
@@ -520,9 +520,16 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 // load in flight, instead of a round trip per pass; the sums, the maximum and
 // every written value are those of split_rows_kernel bit for bit.  Launched
 // with programmatic dependent launch in the decode chains: it waits for the
-// producer of x before its first access.
+// producer of x before its first access, and reads x through L2 with
+// ld.global.cg.  x is written by the previous kernel while this one may
+// already be resident, so it is not read-only for this kernel's lifetime: a
+// load the compiler turned into a read-only-path (.nc) load -- which a
+// const __restrict__ pointer invites -- may be scheduled ahead of
+// griddepcontrol.wait or hit a stale copy.  (Under tensor parallelism that
+// corrupted the multi-sequence step's activations; the explicit .cg load,
+// an asm volatile like griddepcontrol.wait, stays after it.)
 template <int J>
-__global__ void __launch_bounds__(256) split_rows_reg_kernel(const float* __restrict__ x, int k,
+__global__ void __launch_bounds__(256) split_rows_reg_kernel(const float* x, int k,
                                                              int kp, int ldx,
                                                              const float* __restrict__ norm_w,
                                                              float eps, uint16_t* __restrict__ hi,
@@ -537,7 +544,7 @@ __global__ void __launch_bounds__(256) split_rows_reg_kernel(const float* __rest
 #pragma unroll
   for (int j = 0; j < J; ++j) {
     const int e = tid + 256 * j;
-    v[j] = e < k ? xr[e] : 0.0f;
+    v[j] = e < k ? __ldcg(xr + e) : 0.0f;
   }
   if (norm_w) {
     float ss = 0.0f;
@@ -581,11 +588,19 @@ __global__ void __launch_bounds__(256) split_rows_reg_kernel(const float* __rest
 }
 
 // Packed-row gather of M token embeddings (rows of the quantized token_embd).
+// A token id outside [0, vocab) -- possible only when it comes from device
+// state the host did not validate -- gathers nothing: the row is zeroed and
+// kErrBadToken recorded.
 __global__ void embed_rows_kernel(int qtype, const uint8_t* __restrict__ qs,
-                                  const uint16_t* __restrict__ d, int dim, int kp,
+                                  const uint16_t* __restrict__ d, int dim, int kp, int vocab,
                                   const int* __restrict__ tokens, float* __restrict__ y) {
   const int row = blockIdx.x;
   const int token = tokens[row];
+  if (token < 0 || token >= vocab) {
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) y[(size_t)row * dim + i] = 0.0f;
+    if (threadIdx.x == 0) atomicOr(&g_prefill_error, kErrBadToken);
+    return;
+  }
   const int nbk = kp / 32;
   const size_t row_bytes = qtype == DQMK_Q80 ? (size_t)kp : (size_t)kp / 2;
   const uint8_t* qr = qs + (size_t)token * row_bytes;
@@ -870,20 +885,20 @@ size_t partial_floats_bound(int m_max, int n, int kp) {
 }
 
 cudaError_t prefill_prepare() {
-  static bool done = false;
-  if (done) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)gemm_smem());
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attention_prefill_kernel<64>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attention_prefill_smem<64>());
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attention_prefill_kernel<128>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attention_prefill_smem<128>());
-  if (e == cudaSuccess) done = true;
-  return e;
+  static DeviceOnce once;
+  return once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(
+        gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_prefill_kernel<64>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)attention_prefill_smem<64>());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_prefill_kernel<128>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)attention_prefill_smem<128>());
+    return e;
+  });
 }
 
 cudaError_t launch_prefill_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo,
@@ -927,8 +942,8 @@ cudaError_t launch_split_rows(const float* x, int m, int k, int kp, int ldx, con
 }
 
 cudaError_t launch_embed_rows(int qtype, const uint8_t* qs, const uint16_t* d, int dim, int kp,
-                              const int* tokens, int m, float* y, cudaStream_t st) {
-  embed_rows_kernel<<<m, 256, 0, st>>>(qtype, qs, d, dim, kp, tokens, y);
+                              int vocab, const int* tokens, int m, float* y, cudaStream_t st) {
+  embed_rows_kernel<<<m, 256, 0, st>>>(qtype, qs, d, dim, kp, vocab, tokens, y);
   return cudaGetLastError();
 }
 

@@ -72,8 +72,9 @@ cudaError_t launch_prefill_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo
 cudaError_t launch_split_rows(const float* x, int m, int k, int kp, int ldx, const float* norm_w,
                               float eps, uint16_t* hi, uint16_t* lo, float* rs, cudaStream_t st,
                               bool pdl = false);
+// Token ids outside [0, vocab) gather a zero row and set kErrBadToken.
 cudaError_t launch_embed_rows(int qtype, const uint8_t* qs, const uint16_t* d, int dim, int kp,
-                              const int* tokens, int m, float* y, cudaStream_t st);
+                              int vocab, const int* tokens, int m, float* y, cudaStream_t st);
 cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st);
 // Packed Q8_0 / Q4_0 weight [rows][kp] -> exact two-term fp16 planes of
 // d * q * 2^-f and the row scales cs[row] = 2^f.

@@ -19,7 +19,7 @@ namespace {
 
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;
 
-__device__ unsigned int g_tp_error;  // bit 0: a peer wait timed out
+__device__ unsigned int g_tp_error;  // kErrTimeout: a peer wait ran out; kErrNoToken
 
 __device__ __forceinline__ unsigned long long now_ns() {
   unsigned long long t;
@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(256) tp_reduce_kernel(float* __restrict__ x, c
 // lm_head) to every rank, wait for all ranks' keys, take the max -- first
 // maximum wins through the packed index -- and advance the greedy state.
 __global__ void tp_argmax_advance_kernel(const PeerSet ps, const unsigned long long* local_key,
-                                         int* token, int* pos, int* history, int cap) {
+                                         int* token, int* pos, int* history, int cap, int vocab) {
   pdl_trigger();
   pdl_wait();
   const unsigned int s = ps.seq[1] + 1;
@@ -100,12 +100,17 @@ __global__ void tp_argmax_advance_kernel(const PeerSet ps, const unsigned long l
       best = k > best ? k : best;
     }
   }
-  const int idx = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
+  ps.seq[1] = s;
+  // no valid key (a wait ran out here or in the lm_head): keep the state
+  int idx = 0;
+  if (!argmax_token(best, vocab, &idx)) {
+    atomicOr(&g_tp_error, kErrNoToken);
+    return;
+  }
   const int p = *pos;
   if (history && p >= 0 && p < cap) history[p] = idx;
   *token = idx;
   *pos = p + 1;
-  ps.seq[1] = s;
 }
 
 }  // namespace
@@ -116,10 +121,10 @@ cudaError_t launch_tp_reduce(float* x, const PeerSet& ps, cudaStream_t s, bool p
 }
 
 cudaError_t launch_tp_argmax_advance(const PeerSet& ps, const unsigned long long* local_key,
-                                     int* token, int* pos, int* history, int cap, cudaStream_t s,
-                                     bool pdl) {
+                                     int* token, int* pos, int* history, int cap, int vocab,
+                                     cudaStream_t s, bool pdl) {
   return launch(tp_argmax_advance_kernel, dim3(1), dim3(1), 0, s, pdl, ps, local_key, token, pos,
-                history, cap);
+                history, cap, vocab);
 }
 
 cudaError_t read_tp_error(unsigned int* flags, bool clear) {

@@ -331,6 +331,15 @@ int dqmk_model_set_tp(dqmk_model* model, int rank, int world, const unsigned cha
  * Every rank connects its context before the next step. */
 int dqmk_context_tp_ipc_handle(dqmk_context* ctx, unsigned char* handle_out);
 int dqmk_context_tp_connect(dqmk_context* ctx, const unsigned char* handles);
+
+/* Test hook for the decode step: the context's lm_head runs as the
+ * TMA-staged GEMV with row tile `tile` withheld (tile >= 0), every tile
+ * withheld (tile == -2) or nothing withheld (tile == -1, the default); the
+ * step is captured again.  A step whose lm_head rows were all withheld finds
+ * no scored token: the greedy state (token, position, history) is kept and the
+ * call returns DQMK_ERR_TIMEOUT, so no invalid token id reaches the next
+ * embedding.  No reference counterpart. */
+int dqmk_context_withhold_lm_head(dqmk_context* ctx, int tile);
 int dqmk_model_stats_get(const dqmk_model* model, dqmk_model_stats* out);
 int dqmk_model_stats_reset(dqmk_model* model);
 /* ModelCudaMemoryBytes (include/dqm_llama/model.h:119). */

@@ -36,3 +36,37 @@ def test_bounded_wait_times_out_and_context_survives(pkg, orc, S, cuda):
     ref = orc.linear(pkg.Q80, x, blocks, 64)
     assert np.abs(y2 - ref).max() <= 1e-3 * max(1.0, np.abs(ref).max())
     assert L.dqmk_device_error(0) == 0
+
+
+def test_lm_head_timeout_keeps_greedy_state(pkg, orc, S, cuda):
+    """Every row tile of the decode step's lm_head withheld for two greedy
+    steps: each CTA's bounded wait runs out, no row is scored, so no token id
+    exists for the step.  The greedy state (token, position, history) must be
+    kept -- never an invalid id fed to the next step's embedding -- and the call
+    must report the timeout.  With the hook removed, the same context decodes
+    the reference context's greedy tokens from the same token and position.
+    The model is Qwen2-shaped with a 40960-id vocabulary so its tied lm_head is
+    the TMA-staged (bounded-wait) GEMV."""
+    L = pkg.lib()
+    assert L.dqmk_device_error(1) == 0
+    cfg = dict(S.QWEN2_MINI, vocab=40960, n_layers=1)
+    w = S.make_model(cfg, S.Q80, 21, quantize_q80=orc.quantize_q80)
+    model = pkg.Model.from_synth(w, max_seq_len=16)
+    ref = pkg.Context(model)
+    tok = int(np.argmax(ref.ForwardToken(5, 0)))
+    ref_tokens = ref.decode_greedy(tok, 1, 4).tolist()
+    ref.close()
+
+    ctx = pkg.Context(model)
+    ctx.ForwardToken(5, 0)
+    pkg.check(L.dqmk_context_withhold_lm_head(ctx.h, -2))
+    t0 = time.time()
+    with pytest.raises(pkg.CudaError, match="no scored token"):
+        ctx.decode_greedy(tok, 1, 2)
+    assert time.time() - t0 < 60
+    assert L.dqmk_device_error(0) == 0  # the call read and cleared the flags
+    pkg.check(L.dqmk_context_withhold_lm_head(ctx.h, -1))
+    assert ctx.decode_greedy(tok, 1, 4).tolist() == ref_tokens
+    assert L.dqmk_device_error(0) == 0
+    ctx.close()
+    model.close()

@@ -150,28 +150,3 @@ def test_qwen2_0_5b_q8_0_greedy_64_matches_reference(pkg, S, cuda):
     assert tokens == g["greedy_tokens"], (
         f"first divergence at {next(i for i, (a, b) in enumerate(zip(tokens, g['greedy_tokens'])) if a != b)}"
         f", reference min margin {min(g['top1_top2_margin']):.3e}")
-
-
-def test_persistent_step_kernel_matches_chain(pkg, mini, cuda):
-    """DQMK_STEP_KERNEL=1: the decode step as one cooperative kernel (grid
-    barriers between phases) gives the chain's logits within tolerance (the
-    attention phase runs with 128 threads instead of 256) and the same greedy
-    tokens."""
-    for qt in (pkg.Q80, pkg.Q40):
-        w = mini[qt]
-        toks = [3, 14, 15, 92, 65, 35]
-        model = pkg.Model.from_synth(w, max_seq_len=64)
-        chain = pkg.Context(model)
-        for i, t in enumerate(toks):  # ForwardToken replays the step graph
-            ref = chain.ForwardToken(t, i)
-        ref_greedy = chain.decode_greedy(int(np.argmax(ref)), len(toks), 12).tolist()
-        os.environ["DQMK_STEP_KERNEL"] = "1"
-        try:
-            step = pkg.Context(model)
-            for i, t in enumerate(toks):
-                got = step.ForwardToken(t, i)
-            got_greedy = step.decode_greedy(int(np.argmax(got)), len(toks), 12).tolist()
-        finally:
-            del os.environ["DQMK_STEP_KERNEL"]
-        check_logits(got, ref, f"q{qt} step kernel")
-        assert got_greedy == ref_greedy
