@@ -47,6 +47,15 @@ MODEL_SEED = 20261201
 PROMPT_SEED = 1
 LM_HEAD_BYTES = 151936 * 28 * 34 + 896 * 4 + 151936 * 4  # blocks + x + logits
 METRIC = "decode tok/s, Qwen2-0.5B Q8_0, batch 1"
+SWEEP_SHAPES = ((896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896))
+ROTATE_BYTES = 1_050_000_000  # rotating weight copies per timed shape: > 8 x the 126 MB L2
+REF_MAX_STEPS = 512           # reference arm: at ~12 tokens/s, under a minute of host time
+
+
+def decode_launches_per_step(n_layers: int) -> int:
+    """Kernels of one batch-1 decode step: embedding, per layer QKV GEMV,
+    attention, O GEMV, gate/up GEMV, down GEMV, then the lm_head GEMV."""
+    return 1 + 5 * n_layers + 1
 
 
 def peaks():
@@ -200,43 +209,57 @@ def graph_time(torch, launch, n: int, reps: int = 3):
     return best
 
 
-def time_gemv(pkg, torch, w, launches: int = 40):
-    """Packed Q8_0 GEMV at the lm_head shape, two rotating weight copies
-    (290 MB > L2), launches back to back in a CUDA graph, CUDA events."""
+def time_gemv(pkg, torch, w):
+    """The lm_head GEMV (151936 x 896 Q8_0, 145.25 MB per launch: the largest
+    single kernel by bytes, 5% of the step) standalone: rotating weight copies
+    (> 8 x L2) back to back in a CUDA graph, CUDA events."""
     blocks = torch.from_numpy(w.token_embd).cuda()
-    packs = [pkg.pack_weight(pkg.Q80, blocks, 151936, 896) for _ in range(2)]
+    copies = -(-ROTATE_BYTES // w.token_embd.nbytes)
+    packs = [pkg.pack_weight(pkg.Q80, blocks, 151936, 896) for _ in range(copies)]
     x = torch.randn(896, device="cuda")
     y = torch.empty(151936, device="cuda")
-    return graph_time(torch, lambda i: pkg.gemv_packed(pkg.Q80, x, packs[i % 2], 151936, y=y),
-                      launches)
+    dt = graph_time(torch, lambda i: pkg.gemv_packed(pkg.Q80, x, packs[i % copies], 151936, y=y),
+                    4 * copies)
+    del packs
+    torch.cuda.empty_cache()
+    peak, _ = peaks()
+    gbs = LM_HEAD_BYTES / dt / 1e9
+    return {"kernel": "gemv_tma_kernel<Q8_0> 151936x896", "us_per_launch": round(dt * 1e6, 2),
+            "GB_s": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "algorithmic_bytes": LM_HEAD_BYTES, "traffic": profile_traffic()}
 
 
 def gemv_sweep(pkg, torch, S):
-    """Config 2 shapes: GB/s per launch, rotating weight copies (> 300 MB in
-    total, so every launch reads its weight from HBM), launches back to back in
-    a CUDA graph (device time, no host launch overhead)."""
-    out = {}
-    for o, i in ((896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896)):
+    """Configuration 2 (Q8_0 GEMV sweep): per shape, rotating weight copies
+    totalling more than 8 x L2 (so every launch reads its weight from HBM),
+    one launch per copy back to back in a CUDA graph (device time, no host
+    launch overhead); GB/s and fraction of the measured HBM peak."""
+    peak, kind = peaks()
+    out = {"rotating_bytes_per_shape": ROTATE_BYTES, "peak_GB_s": peak, "peak_source": kind}
+    for o, i in SWEEP_SHAPES:
         blocks, x = S.gemv_case(o, i, 7)
         bd = torch.from_numpy(blocks).cuda()
         nbytes = blocks.nbytes + 4 * (i + o)
-        copies = max(2, int(300e6 // blocks.nbytes) + 1)
+        copies = max(2, -(-ROTATE_BYTES // blocks.nbytes))
         packs = [pkg.pack_weight(pkg.Q80, bd, o, i) for _ in range(copies)]
         xd = torch.from_numpy(x).cuda()
         y = torch.empty(o, device="cuda")
-        n = max(copies, 20)
-        dt = graph_time(torch, lambda k: pkg.gemv_packed(pkg.Q80, xd, packs[k % copies], o, y=y), n)
-        out[f"{o}x{i}"] = {"us": round(dt * 1e6, 2), "GB_s": round(nbytes / dt / 1e9, 1)}
+        dt = graph_time(torch, lambda k: pkg.gemv_packed(pkg.Q80, xd, packs[k % copies], o, y=y),
+                        copies)
+        gbs = nbytes / dt / 1e9
+        out[f"{o}x{i}"] = {"us": round(dt * 1e6, 2), "GB_s": round(gbs, 1),
+                           "frac": round(gbs / peak, 4), "copies": copies}
         del packs
+        torch.cuda.empty_cache()
     return out
 
 
-def profile_traffic():
-    """DRAM bytes per launch of the lm_head GEMV from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "gemv_q8_0_lm_head_151936x896.md")
+def profile_traffic(name="gemv_q8_0_lm_head_151936x896.md", key="dram_bytes_per_launch:"):
+    """DRAM bytes per launch of a kernel from its committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         for ln in open(path):
-            if ln.startswith("dram_bytes_per_launch:"):
+            if ln.startswith(key):
                 return int(float(ln.split(":")[1].strip()))
     except OSError:
         pass
@@ -389,27 +412,34 @@ def build_7b(pkg, torch, max_seq: int, local: int, tp_rank: int, tp_world: int, 
     return model
 
 
-def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
+def seven_b_bytes(c: dict):
+    hd = c["dim"] // c["n_heads"]
+    qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
+    weights = (c["n_layers"] * (qd + 2 * kvd + qd + 3 * c["hidden"]) * c["dim"] * 18 // 32
+               + c["vocab"] * c["dim"] * 18 // 32)
+    return weights, kvd
+
+
+def block_7b_tp(pkg, torch, dist, world, rank, local, ctx_len=2048, n_steps=64, warm=8,
+                p2p=False):
     """Qwen2-7B-architecture Q4_0 (untied lm_head), one sequence, tensor
-    parallel over the ranks (one GPU each): a --ctx-long prompt fills the KV
-    cache, then --steps greedy decode steps are timed (device argmax, captured
-    step graph with the NCCL all-reduces inside)."""
+    parallel over the ranks (one GPU each): a ctx_len prompt through
+    ForwardBatch fills the KV cache, then n_steps greedy decode steps are timed
+    (device argmax, captured step graph with the NCCL all-reduces inside).
+    Returns the result dict on rank 0."""
     S = pkg.synth
     c = dict(S.QWEN2_7B)
-    n_steps, ctx_len = args.steps, args.ctx
     nccl_id = None
     if world > 1:
         obj = [pkg.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
-    model = build_7b(pkg, torch, ctx_len + n_steps + args.warmup, local, rank, world, nccl_id)
-    hd = c["dim"] // c["n_heads"]
-    qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
+    model = build_7b(pkg, torch, ctx_len + n_steps + warm, local, rank, world, nccl_id)
     ctx = pkg.Context(model)
     exchange = "none"
     if world > 1:
         exchange = "nccl"
-        if args.p2p:
+        if p2p:
             handles = [None] * world
             dist.all_gather_object(handles, ctx.tp_ipc_handle())
             ctx.tp_connect(handles)
@@ -419,7 +449,7 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
     prompt = S.prompt_tokens(c["vocab"], ctx_len, 11).tolist()
     logits = ctx.ForwardBatch(prompt, 0)
     first = int(np.argmax(logits))
-    ctx.decode_enqueue(first, ctx_len, args.warmup)
+    ctx.decode_enqueue(first, ctx_len, warm)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -427,7 +457,7 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
     with ClockSampler(local) as clk:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        ctx.decode_enqueue(first, ctx_len + args.warmup, n_steps)
+        ctx.decode_enqueue(first, ctx_len + warm, n_steps)
         e1.record(stream)
         e1.synchronize()
     dt = e0.elapsed_time(e1) / 1e3
@@ -437,73 +467,69 @@ def bench_7b_tp(args, pkg, torch, dist, world, rank, local):
         dt = float(t.item())
     ctx.close()
     model.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    torch.cuda.synchronize()
     if rank != 0:
-        return
-    weights = (c["n_layers"] * (qd + 2 * kvd + qd + 3 * c["hidden"]) * c["dim"] * 18 // 32
-               + c["vocab"] * c["dim"] * 18 // 32)
-    kv = c["n_layers"] * 2 * kvd * 4 * (ctx_len + args.warmup + n_steps // 2)
+        return None
+    weights, kvd = seven_b_bytes(c)
+    kv = c["n_layers"] * 2 * kvd * 4 * (ctx_len + warm + n_steps // 2)
     per_gpu = (weights + kv) / world
     peak, peak_kind = peaks()
     gbs = per_gpu * n_steps / dt / 1e9
-    print(json.dumps({
-        "metric": "decode tok/s, Qwen2-7B Q4_0, batch 1, tensor parallel",
-        "value": round(n_steps / dt, 2), "unit": "tok/s", "n_gpus": world, "steps": n_steps,
-        "warmup": args.warmup, "ms_per_step": round(dt / n_steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_0xf32",
-        "data": "synthetic: random Q4_0 blocks (uniform nibbles, fp16 scales 0.003-0.006), "
-                "random prompt ids",
-        "config": {"workload": f"qwen2-7b-architecture Q4_0, untied lm_head, {ctx_len}-token "
-                               f"prompt then batch-1 greedy decode", "model": "qwen2-7b",
-                   "parallelism": f"tp{world}", "exchange": exchange,
-                   "seq_len": ctx_len + args.warmup + n_steps},
+    return {
+        "workload": f"qwen2-7b-architecture Q4_0, untied lm_head, {ctx_len}-token prompt then "
+                    f"batch-1 greedy decode ({n_steps} timed steps after {warm})",
+        "value": round(n_steps / dt, 2), "unit": "tok/s", "ms_per_step": round(dt / n_steps * 1e3, 4),
+        "parallelism": f"tp{world}", "exchange": exchange,
         "hbm": {"bytes_per_token_per_gpu": int(per_gpu), "GB_s_per_gpu": round(gbs, 1),
                 "frac_of_peak": round(gbs / peak, 4), "peak_source": peak_kind},
-        "clocks": clk.summary()}))
+        "clocks": clk.summary()}
 
 
-def bench_7b_batch(args, pkg, torch, dist, world, rank, local):
-    """Qwen2-7B-architecture Q4_0, --seqs sequences decoded together
-    (dqmk_batch): tensor parallel over --tp ranks, world / tp independent
-    groups splitting the sequences.  Every slot's KV cache is filled with a
-    --ctx-token random prompt (batched steps of 64 positions of one slot), then
-    --warmup greedy steps run and --steps greedy steps are timed (one captured
-    step graph per step, argmax and position advanced on the device)."""
-    import time
+def block_7b_batch(pkg, torch, dist, world, rank, local, seqs=64, ctx_len=2048, n_steps=32,
+                   warm=8, tp=0, kv_fill="zero", e2e_steps=8):
+    """Configuration 5: Qwen2-7B-architecture Q4_0, `seqs` sequences decoded
+    together (dqmk_batch), tensor parallel over `tp` ranks (default min(world,
+    4)), world / tp independent groups splitting the sequences (2 x TP4 at 8
+    GPUs).  Every slot's KV cache holds ctx_len positions -- filled by a
+    random prompt (kv_fill "prompt", batched steps of 64 positions of one slot)
+    or left zero (kv_fill "zero": the step reads the same bytes) -- then `warm`
+    greedy steps run and n_steps are timed (one captured step graph per step,
+    argmax and position advanced on the device), max over ranks.  Then
+    e2e_steps through the public step call with host tokens.  Returns the
+    result dict on rank 0."""
     S = pkg.synth
     c = dict(S.QWEN2_7B)
-    tp = args.tp or world
-    if world % tp or args.seqs % (world // tp):
-        raise SystemExit("--gpus must be a multiple of --tp and --seqs of the group count")
+    tp = tp or min(world, 4)
+    if world % tp or seqs % (world // tp):
+        raise SystemExit("the GPU count must be a multiple of the TP size and the sequences of "
+                         "the group count")
     groups = world // tp
     group, tp_rank = rank // tp, rank % tp
-    seqs = args.seqs // groups
+    my_seqs = seqs // groups
     nccl_id = None
     if tp > 1:
         mine = pkg.nccl_unique_id() if tp_rank == 0 else None
         ids = [None] * world
         dist.all_gather_object(ids, mine)
         nccl_id = ids[group * tp]
-    ctx_len, n_steps, warm = args.ctx, args.steps, args.warmup
-    max_seq = ctx_len + warm + n_steps + 17  # + the end-to-end steps
+    max_seq = ctx_len + warm + n_steps + e2e_steps + 1
     model = build_7b(pkg, torch, max_seq, local, tp_rank, tp, nccl_id)
-    batch = pkg.Batch(model, seqs, max_seq)
+    batch = pkg.Batch(model, my_seqs, max_seq)
     stream = torch.cuda.ExternalStream(batch.stream_handle)
-    prompts = [S.prompt_tokens(c["vocab"], ctx_len, 1000 + group * seqs + s) for s in range(seqs)]
+    prompts = [S.prompt_tokens(c["vocab"], ctx_len, 1000 + group * my_seqs + i)
+               for i in range(my_seqs)]
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    if args.kv_fill == "prompt":
-        for s in range(seqs):
-            batch.prefill(s, prompts[s][:-1])
+    if kv_fill == "prompt":
+        for i in range(my_seqs):
+            batch.prefill(i, prompts[i][:-1])
     torch.cuda.synchronize()
     fill_s = time.perf_counter() - t0
     last = [int(p[-1]) for p in prompts]
-    batch.decode_enqueue(last, [ctx_len - 1] * seqs, warm)
+    batch.decode_enqueue(last, [ctx_len - 1] * my_seqs, warm)
     torch.cuda.synchronize()
     pos0 = ctx_len - 1 + warm
-    cont = [int(batch.history(s, pos0 - 1, 1)[0]) for s in range(seqs)]
+    cont = [int(batch.history(i, pos0 - 1, 1)[0]) for i in range(my_seqs)]
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -511,21 +537,20 @@ def bench_7b_batch(args, pkg, torch, dist, world, rank, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.nvtx.range_push("timed")  # lets a profiler select the timed steps
         e0.record(stream)
-        batch.decode_enqueue(cont, [pos0] * seqs, n_steps)
+        batch.decode_enqueue(cont, [pos0] * my_seqs, n_steps)
         e1.record(stream)
         e1.synchronize()
         torch.cuda.nvtx.range_pop()
     dt = e0.elapsed_time(e1) / 1e3
     # end to end through the public step call: host tokens in, host tokens out
     pos1 = pos0 + n_steps
-    toks = [int(batch.history(s, pos1 - 1, 1)[0]) for s in range(seqs)]
-    e2e_steps = min(16, max_seq - pos1)
+    toks = [int(batch.history(i, pos1 - 1, 1)[0]) for i in range(my_seqs)]
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
-        _, nxt = batch.step(None, toks, [pos1 + i] * seqs, want_logits=False)
+        _, nxt = batch.step(None, toks, [pos1 + i] * my_seqs, want_logits=False)
         toks = nxt.tolist()
     e2e_dt = time.perf_counter() - t0
     if dist:
@@ -534,45 +559,35 @@ def bench_7b_batch(args, pkg, torch, dist, world, rank, local):
         dt, e2e_dt, fill_s = (float(v) for v in t.tolist())
     batch.close()
     model.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    torch.cuda.synchronize()
     if rank != 0:
-        return
-    hd = c["dim"] // c["n_heads"]
-    qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
-    weights = (c["n_layers"] * (qd + 2 * kvd + qd + 3 * c["hidden"]) * c["dim"] * 18 // 32
-               + c["vocab"] * c["dim"] * 18 // 32)
+        return None
+    weights, kvd = seven_b_bytes(c)
     mean_pos = pos0 + n_steps / 2
-    kv = c["n_layers"] * 2 * kvd * 4 * (mean_pos + 1) * seqs
+    kv = c["n_layers"] * 2 * kvd * 4 * (mean_pos + 1) * my_seqs
     per_gpu = (weights + kv) / tp
     peak, peak_kind = peaks()
     gbs = per_gpu * n_steps / dt / 1e9
-    launches = 1 + c["n_layers"] * (9 + (4 if tp > 1 else 0)) + 3
-    print(json.dumps({
-        "metric": f"decode tok/s, Qwen2-7B Q4_0, {args.seqs} sequences x {ctx_len} KV",
-        "value": round(args.seqs * n_steps / dt, 1), "unit": "tok/s", "n_gpus": world,
-        "steps": n_steps, "warmup": warm, "ms_per_step": round(dt / n_steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_0xf32",
-        "data": "synthetic: random Q4_0 blocks (uniform nibbles, fp16 scales 0.003-0.006), "
-                "random prompt ids",
-        "config": {"workload": f"qwen2-7b-architecture Q4_0, untied lm_head, {args.seqs} "
-                               f"sequences each with a {ctx_len}-token prompt in its KV cache, "
-                               f"then {n_steps} greedy steps of all sequences together",
-                   "model": "qwen2-7b", "global_batch": args.seqs,
-                   "parallelism": f"{groups}x tp{tp}" if groups > 1 else f"tp{tp}",
-                   "seq_len": max_seq,
-                   "l2": "per-step weight + KV stream far above the 126 MB L2"},
-        "e2e": {"value": round(args.seqs * e2e_steps / e2e_dt, 1), "unit": "tok/s",
-                "h2d_bytes_per_step": 3 * 64 * 4, "d2h_bytes_per_step": seqs * 4,
-                "steps": e2e_steps},
-        "kv_fill": ({"tokens": args.seqs * (ctx_len - 1), "s": round(fill_s, 3),
-                     "tok_s": round(args.seqs * (ctx_len - 1) / fill_s, 1)}
-                    if args.kv_fill == "prompt" else "zero (not filled)"),
-        "gpu_launches": n_steps * launches,
+    per_layer = 9 + (4 if tp > 1 else 0)
+    return {
+        "workload": f"qwen2-7b-architecture Q4_0, untied lm_head, {seqs} sequences each with "
+                    f"{ctx_len} positions in its KV cache, greedy steps of all sequences "
+                    f"together ({n_steps} timed after {warm})",
+        "value": round(seqs * n_steps / dt, 1), "unit": "tok/s",
+        "ms_per_step": round(dt / n_steps * 1e3, 4),
+        "parallelism": f"{groups}x tp{tp}" if groups > 1 else f"tp{tp}",
+        "tp": tp, "groups": groups, "nccl_ranks_per_communicator": tp,
+        "collectives_per_step": (2 * c["n_layers"] + 1) if tp > 1 else 0,
+        "allreduce_bytes": my_seqs * c["dim"] * 4 if tp > 1 else 0,
+        "kv_fill": ({"tokens": seqs * (ctx_len - 1), "s": round(fill_s, 3)}
+                    if kv_fill == "prompt" else "zero (not filled; the step reads the same bytes)"),
         "hbm": {"bytes_per_step_per_gpu": int(per_gpu), "GB_s_per_gpu": round(gbs, 1),
                 "frac_of_peak": round(gbs / peak, 4), "peak_source": peak_kind},
-        "clocks": clk.summary()}))
+        "e2e": {"value": round(seqs * e2e_steps / e2e_dt, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 3 * 64 * 4, "d2h_bytes_per_step": my_seqs * 4,
+                "steps": e2e_steps},
+        "gpu_launches": n_steps * (1 + c["n_layers"] * per_layer + 3),
+        "clocks": clk.summary()}
 
 
 def time_cols_gemm(pkg, torch, launches: int = 10):
@@ -607,6 +622,16 @@ def decode_config(world: int) -> dict:
             "l2": "per-step weight stream 525 MB > 126 MB L2; no flush needed"}
 
 
+def cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def reference_decode(w, steps: int, warmup: int, threads: int):
     """The reference's CPU decode (oracle/_ref) on this host: returns s/token."""
     orc = ge.load_oracle()
@@ -624,10 +649,44 @@ def reference_decode(w, steps: int, warmup: int, threads: int):
         tok = int(np.argmax(logits))
     t0 = time.perf_counter()
     for i in range(steps):
-        logits = rm.forward_batch([tok], N_PROMPT + warmup + i)
+        logits = rm.forward_batch([tok], N_PROMPT + (warmup + i) % N_DECODE_POS)
         tok = int(np.argmax(logits))
     dt = time.perf_counter() - t0
     return dt / steps, "ok"
+
+
+def reference_prefill_sample(w, threads: int, n_tokens: int = 96):
+    """The reference's ForwardBatch (src/batch.cc:26-42, a per-token
+    ForwardToken loop) over the first n_tokens of the 602-token prefill prompt,
+    on this host: tokens/s of the per-token loop."""
+    orc = ge.load_oracle()
+    S = ge.load_package().synth
+    rm = orc.RefModel(w, n_tokens, threads=threads)
+    prompt = S.prompt_tokens(w.cfg["vocab"], 602, 4)[:n_tokens]
+    t0 = time.perf_counter()
+    rm.forward_batch(prompt, 0)
+    return n_tokens / (time.perf_counter() - t0)
+
+
+def reference_linear_sweep(S, threads: int):
+    """The reference's LinearQ80 / LinearQ40 (src/quant.cc:350-366) at the
+    GEMV-sweep shapes on this host: median of 3 calls after one warm-up."""
+    orc = ge.load_oracle()
+    orc.ref_set_threads(threads)
+    out = {}
+    for qt, name in ((S.Q80, "q8_0"), (S.Q40, "q4_0")):
+        for o, i in SWEEP_SHAPES:
+            blocks, x = S.gemv_case(o, i, 7, qt)
+            orc.linear(qt, x, blocks, o, use_ref=True)
+            ts = []
+            for _ in range(3):
+                t0 = time.perf_counter()
+                orc.linear(qt, x, blocks, o, use_ref=True)
+                ts.append(time.perf_counter() - t0)
+            t = statistics.median(ts)
+            nbytes = blocks.nbytes + 4 * (i + o)
+            out[f"{name} {o}x{i}"] = {"ms": round(t * 1e3, 3), "GB_s": round(nbytes / t / 1e9, 2)}
+    return out
 
 
 def reference_arm(args, rank):
@@ -642,23 +701,29 @@ def reference_arm(args, rank):
     threads = os.cpu_count() or 1
     w = S.make_model(S.QWEN2_0_5B, S.Q80, MODEL_SEED,
                      quantize_q80=lambda a: orc.quantize_q80(a, use_ref=True))
-    steps = max(1, min(args.steps, 16))
+    # every timed step is one decode token of the same workload; the run is
+    # kept to a few minutes on the host cores (about 12 tokens/s)
+    steps = max(1, min(args.steps, REF_MAX_STEPS))
     warm = max(3, min(args.warmup, 8))
     spt, _ = reference_decode(w, steps, warm, threads)
     v = 1.0 / spt
-    print(json.dumps({
+    line = {
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s",
         "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": round(spt * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic random-init weights, random prompt ids",
-        "config": dict(decode_config(1), parallelism="reference CPU path on the host cores "
-                       "(threaded scalar LinearQ80 + AVX2 F32 lm_head)"),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0xf32",
+        "data": "synthetic: random-init N(0,0.02) weights quantized to Q8_0, random prompt ids",
+        "config": decode_config(args.gpus),
+        "path": "the reference's CPU ForwardBatch / ForwardToken (compiled from its sources: "
+                "threaded scalar LinearQ80, AVX2 F32 lm_head) on the host cores",
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads,
-                         "kind": "reference",
+                         "kind": "reference", "cpu": cpu_model(),
                          "sample": f"{steps} decode steps after {warm} warm-up"},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }))
+    }
+    if steps < args.steps:
+        line["steps_note"] = f"{args.steps} steps asked; {steps} run (bounded CPU sample)"
+    print(json.dumps(line))
 
 
 def main():
@@ -669,29 +734,30 @@ def main():
     ap.add_argument("--impl", default="dqmk", choices=["dqmk", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-7b", action="store_true", help="skip the Qwen2-7B blocks")
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the decode steps (small runs for profiling)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="time only the 602-token prefill and the batched linear (profiling)")
     ap.add_argument("--model", default="qwen2-0.5b", choices=["qwen2-0.5b", "qwen2-7b"],
-                    help="qwen2-7b: tensor-parallel decode over the --gpus ranks")
+                    help="qwen2-7b: only the 7B workload, as its own line")
     ap.add_argument("--ctx", type=int, default=2048, help="qwen2-7b: KV length before decoding")
-    ap.add_argument("--seqs", type=int, default=1,
-                    help="qwen2-7b: sequences decoded together (64: the multi-sequence "
-                         "configuration; 1: batch-1 decode)")
+    ap.add_argument("--seqs", type=int, default=64,
+                    help="qwen2-7b: sequences decoded together (64: configuration 5; 1: "
+                         "batch-1 decode)")
     ap.add_argument("--tp", type=int, default=0,
-                    help="qwen2-7b with --seqs > 1: tensor-parallel group size (default: all "
-                         "ranks); --gpus / --tp independent groups split the sequences")
-    ap.add_argument("--kv-fill", default="prompt", choices=["prompt", "zero"],
+                    help="qwen2-7b with --seqs > 1: tensor-parallel group size (default: "
+                         "min(ranks, 4)); ranks / tp independent groups split the sequences")
+    ap.add_argument("--kv-fill", default="zero", choices=["prompt", "zero"],
                     help="qwen2-7b --seqs > 1: fill every KV cache with a random prompt "
                          "(prompt) or leave it zero and start decoding at position --ctx - 1 "
-                         "(zero: the step reads the same bytes; for short profiling runs)")
+                         "(zero: the step reads the same bytes)")
     ap.add_argument("--cols-gemm", action="store_true",
                     help="time only the standalone multi-sequence GEMM at the Qwen2-7B gate/up "
                          "shape (64 columns x 37888 x 3584 Q4_0; profiling)")
     ap.add_argument("--p2p", action="store_true",
-                    help="qwen2-7b under tensor parallelism: exchange partial sums over peer "
-                         "memory (IPC-mapped buffers) instead of NCCL all-reduces")
+                    help="qwen2-7b batch 1 under tensor parallelism: exchange partial sums over "
+                         "peer memory instead of NCCL all-reduces")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -719,9 +785,17 @@ def main():
         return
     if args.model == "qwen2-7b":
         if args.seqs > 1:
-            bench_7b_batch(args, pkg, torch, dist, world, rank, local)
+            r = block_7b_batch(pkg, torch, dist, world, rank, local, seqs=args.seqs,
+                               ctx_len=args.ctx, n_steps=args.steps, warm=args.warmup, tp=args.tp,
+                               kv_fill=args.kv_fill)
         else:
-            bench_7b_tp(args, pkg, torch, dist, world, rank, local)
+            r = block_7b_tp(pkg, torch, dist, world, rank, local, ctx_len=args.ctx,
+                            n_steps=args.steps, warm=args.warmup, p2p=args.p2p)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=world, steps=args.steps, warmup=args.warmup)))
         return
     w = build_model(pkg, torch)
     if args.prefill_only:
@@ -732,8 +806,7 @@ def main():
     prompt = S.prompt_tokens(w.cfg["vocab"], N_PROMPT, PROMPT_SEED)
     logits = ctx.ForwardBatch(prompt, 0)
     first = int(np.argmax(logits))
-    n_layers = w.cfg["n_layers"]
-    launches_per_step = 1 + 5 * n_layers + 1
+    launches_per_step = decode_launches_per_step(w.cfg["n_layers"])
 
     # ---- timed region: K device-resident decode steps
     if dist:
@@ -767,32 +840,46 @@ def main():
         e2e_dt, e2e_logits_dt = (float(v) for v in t.tolist())
     e2e = world * e2e_steps / e2e_dt
 
-    # ---- dominant-kernel roofline (lm_head-shaped Q8_0 GEMV)
-    gemv_s = time_gemv(pkg, torch, w)
+    # ---- the dominant kernel of the step, timed in its in-graph (chained) form
     peak, peak_kind = peaks()
-    achieved = LM_HEAD_BYTES / gemv_s / 1e9
+    dom = time_dominant(pkg, torch, ctx)
     bytes_per_token = (sum(getattr(L, n).nbytes for L in w.layers
                            for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))
                        + w.token_embd.nbytes + 896 * 4 * 2)
+    ctx.close()
+    model.close()
+    lm = time_gemv(pkg, torch, w) if rank == 0 else None
     sweep = None if (args.no_sweep or rank != 0) else gemv_sweep(pkg, torch, S)
 
     # ---- prefill (ForwardBatch) of a 602-token prompt: the batched path
-    # (tensor-core GEMMs + causal attention), events on the context stream
-    ctx.close()
-    model.close()
     prefill = time_prefill(pkg, torch, S, w) if rank == 0 else None
     q4_ctx2048 = time_q4_ctx2048(pkg, torch, S) if rank == 0 else None
+    torch.cuda.synchronize()
+
+    # ---- Qwen2-7B: configuration 5 (64 sequences) on every run; batch 1 at N=1
+    seven_b = None
+    if not args.no_7b:
+        seven_b = {"config5": block_7b_batch(pkg, torch, dist, world, rank, local)}
+        if world == 1:
+            seven_b["batch1_tp1"] = block_7b_tp(pkg, torch, dist, world, rank, local)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         spt, status = reference_decode(w, 8, 3, threads)
         if spt is not None:
+            pre_tok_s = reference_prefill_sample(w, threads)
             cpu = {"value": round(1.0 / spt, 4), "unit": "tok/s", "cores": threads,
-                   "kind": "reference",
+                   "kind": "reference", "cpu": cpu_model(),
                    "sample": "8 decode steps (after 3 warm-up steps) of the same model and "
                              "positions on the reference's CPU path, threaded over all host "
-                             "cores"}
+                             "cores",
+                   "prefill_per_token_loop": {
+                       "tok_s": round(pre_tok_s, 3), "sample": "the reference's ForwardBatch "
+                       "(per-token loop) over the first 96 ids of the 602-token prompt",
+                       "gpu_batched_over_reference": (round(prefill["tok_s"] / pre_tok_s, 1)
+                                                      if prefill else None)},
+                   "linear_sweep": reference_linear_sweep(S, threads)}
 
     if dist:
         dist.barrier()
@@ -819,15 +906,16 @@ def main():
         "gpu_launches": args.steps * launches_per_step,
         "decode_hbm": {"bytes_per_token": bytes_per_token,
                        "GB_s": round(bytes_per_token * value / world / 1e9, 1),
-                       "frac_of_peak": round(bytes_per_token * value / world / 1e9 / peak, 4)},
-        "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel<Q8_0> lm_head 151936x896",
-                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": profile_traffic(), "algorithmic_bytes": LM_HEAD_BYTES,
-                     "us_per_launch": round(gemv_s * 1e6, 2)},
+                       "frac_of_peak": round(bytes_per_token * value / world / 1e9 / peak, 4),
+                       "peak_source": peak_kind},
+        "roofline": dict(dom, bound="hbm", peak=peak, unit="GB/s",
+                         frac=round(dom["achieved"] / peak, 4),
+                         peak_source=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"),
+        "lm_head_gemv": lm,
         "gemv_sweep": sweep,
         "prefill": prefill,
         "q4_0_ctx2048": q4_ctx2048,
+        "qwen2_7b": seven_b,
         "cpu_baseline": cpu,
         "clocks": clocks,
     }

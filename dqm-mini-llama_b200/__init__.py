@@ -171,6 +171,16 @@ def gemv_packed(qtype: int, x, packed, out_features: int, bias=None, residual=No
     return y
 
 
+def gemv_packed_chained(qtype: int, x, packed, out_features: int, y, norm=None, eps=1e-6,
+                        swiglu=False, stream=None):
+    """The decode step's GEMV launched as the step chains it (programmatic
+    dependent launch), with optional RMSNorm prologue and SwiGLU epilogue."""
+    check(lib().dqmk_gemv_packed_chained(qtype, _ptr(x), x.shape[-1], _ptr(packed), out_features,
+                                         _ptr(norm), float(eps), 1 if swiglu else 0, _ptr(y),
+                                         _stream(stream)))
+    return y
+
+
 def linear_batch_packed(qtype: int, x, packed, out_features: int, bias=None, residual=None,
                         y=None, stream=None):
     """x [m, in] (device, float32) times a packed weight on the tensor cores."""

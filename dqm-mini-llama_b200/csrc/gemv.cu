@@ -297,6 +297,48 @@ __device__ __forceinline__ void quantize_x_terms(const float* xf, int nbk, int8_
   }
 }
 
+// The 32 weights of block b of a packed row as eight int8x4 words in the
+// order of the x-term planes: Q8_0 bytes as stored (signed); Q4_0 nibbles
+// unpacked to unsigned bytes 0..15, words 0-3 the low nibbles (values
+// 4j..4j+3), words 4-7 the high nibbles (values 16+4j..).
+template <int QT>
+__device__ __forceinline__ void block_words(const unsigned char* row, int b, int (&w)[8]) {
+  if constexpr (QT == DQMK_Q80) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(row + b * 32);
+    const uint4 w1 = *reinterpret_cast<const uint4*>(row + b * 32 + 16);
+    w[0] = (int)w0.x; w[1] = (int)w0.y; w[2] = (int)w0.z; w[3] = (int)w0.w;
+    w[4] = (int)w1.x; w[5] = (int)w1.y; w[6] = (int)w1.z; w[7] = (int)w1.w;
+  } else {
+    const uint4 p = *reinterpret_cast<const uint4*>(row + b * 16);
+    const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      w[j] = (int)(pw[j] & 0x0f0f0f0fu);
+      w[4 + j] = (int)((pw[j] >> 4) & 0x0f0f0f0fu);
+    }
+  }
+}
+
+// Exact int32 sums of one block against the three x terms:
+// S[t] = sum_j q_w[j] q_t[j] (Q4_0: nibbles minus 8, via sm8[t] = 8 sum_j q_t[j]).
+// xv[2t], xv[2t+1]: values 0-15 and 16-31 of term t as int8x4 words.
+__device__ __forceinline__ void block_term_sums(const int (&w)[8], const int4 (&xv)[6],
+                                                const int (&sm8)[3], int (&S)[3]) {
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    const int4 lo = xv[t * 2], hi = xv[t * 2 + 1];
+    int v = __dp4a(w[0], lo.x, 0);
+    v = __dp4a(w[1], lo.y, v);
+    v = __dp4a(w[2], lo.z, v);
+    v = __dp4a(w[3], lo.w, v);
+    v = __dp4a(w[4], hi.x, v);
+    v = __dp4a(w[5], hi.y, v);
+    v = __dp4a(w[6], hi.z, v);
+    v = __dp4a(w[7], hi.w, v);
+    S[t] = v - sm8[t];
+  }
+}
+
 __device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
 
 // Shared-memory layout of the staged x: fp32 copy, int8 term planes, term
@@ -458,38 +500,15 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
         for (int r = 0; r < RPW; ++r) {
           const int rl = wid * RPW + r;
           if (rl < rows) {
-            const unsigned char* wrow = sq + (size_t)rl * g.row_bytes;
             int w[8];
-            if constexpr (QT == DQMK_Q80) {
-              const uint4 w0 = *reinterpret_cast<const uint4*>(wrow + b * 32);
-              const uint4 w1 = *reinterpret_cast<const uint4*>(wrow + b * 32 + 16);
-              w[0] = (int)w0.x; w[1] = (int)w0.y; w[2] = (int)w0.z; w[3] = (int)w0.w;
-              w[4] = (int)w1.x; w[5] = (int)w1.y; w[6] = (int)w1.z; w[7] = (int)w1.w;
-            } else {
-              const uint4 p = *reinterpret_cast<const uint4*>(wrow + b * 16);
-              const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                w[j] = (int)(pw[j] & 0x0f0f0f0fu);             // values 4j..4j+3
-                w[4 + j] = (int)((pw[j] >> 4) & 0x0f0f0f0fu);  // values 16+4j..
-              }
-            }
+            block_words<QT>(sq + (size_t)rl * g.row_bytes, b, w);
             const uint16_t dv =
                 d_smem ? sd[rl * g.nbk + b] : __ldg(a.d + (size_t)(r0 + rl) * g.nbk + b);
+            int S[3];
+            block_term_sums(w, xv, sm8, S);
             float blk = 0.0f;
 #pragma unroll
-            for (int t = 0; t < 3; ++t) {
-              const int4 lo = xv[t * 2], hi = xv[t * 2 + 1];
-              int S = __dp4a(w[0], lo.x, 0);
-              S = __dp4a(w[1], lo.y, S);
-              S = __dp4a(w[2], lo.z, S);
-              S = __dp4a(w[3], lo.w, S);
-              S = __dp4a(w[4], hi.x, S);
-              S = __dp4a(w[5], hi.y, S);
-              S = __dp4a(w[6], hi.z, S);
-              S = __dp4a(w[7], hi.w, S);
-              blk = __fmaf_rn(sc[t], (float)(S - sm8[t]), blk);
-            }
+            for (int t = 0; t < 3; ++t) blk = __fmaf_rn(sc[t], (float)S[t], blk);
             acc[r] = __fmaf_rn(h2f(dv), blk, acc[r]);
           }
         }
@@ -529,6 +548,50 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
     unsigned long long b = 0ull;
     for (int w = 0; w < kTmaWarps; ++w) b = best_w[w] > b ? best_w[w] : b;
     logits_finish(a, b, gridDim.x, &g_device_error);
+  }
+}
+
+// Test hook behind dqmk_lm_head_block_sums: x (k floats) split into the three
+// int8 terms by quantize_x_terms, then every (row, block) of a packed weight
+// summed against them with block_term_sums -- the integer arithmetic of
+// gemv_tma_kernel, exposed so it can be checked exactly.  One CTA of
+// kTmaConsumers threads; x staged in shared memory (zero past k).
+template <int QT>
+__global__ void __launch_bounds__(kTmaConsumers) block_sums_kernel(
+    const float* __restrict__ x, int k, int kp, const uint8_t* __restrict__ qs, int n_rows,
+    int8_t* __restrict__ q_terms, float* __restrict__ scales, int* __restrict__ sums) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int nbk = kp / 32;
+  float* xf = reinterpret_cast<float*>(smem);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + (size_t)kp * 4);
+  float* xsc = reinterpret_cast<float*>(smem + (size_t)kp * 4 + (size_t)3 * kp);
+  int* xsum = reinterpret_cast<int*>(xsc + 3 * nbk);
+  for (int e = threadIdx.x; e < kp; e += blockDim.x) xf[e] = e < k ? x[e] : 0.0f;
+  __syncthreads();
+  quantize_x_terms<kTmaWarps, QT == DQMK_Q40>(xf, nbk, xq, xsc, xsum);
+  __syncthreads();
+  // terms out as [term][block][32 values]: plane [t][half][block][16 bytes]
+  for (int i = threadIdx.x; i < 3 * nbk * 32; i += blockDim.x) {
+    const int t = i / (nbk * 32), b = (i / 32) % nbk, j = i % 32;
+    q_terms[i] = xq[((size_t)(t * 2 + j / 16) * nbk + b) * 16 + (j % 16)];
+  }
+  for (int i = threadIdx.x; i < 3 * nbk; i += blockDim.x) scales[i] = xsc[i];
+  const int4* xq4 = reinterpret_cast<const int4*>(xq);
+  const size_t row_bytes = QT == DQMK_Q80 ? (size_t)kp : (size_t)kp / 2;
+  for (int i = threadIdx.x; i < n_rows * nbk; i += blockDim.x) {
+    const int row = i / nbk, b = i % nbk;
+    int4 xv[6];
+    int sm8[3];
+#pragma unroll
+    for (int t = 0; t < 6; ++t) xv[t] = xq4[(size_t)t * nbk + b];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) sm8[t] = QT == DQMK_Q40 ? 8 * xsum[t * nbk + b] : 0;
+    int w[8];
+    block_words<QT>(qs + (size_t)row * row_bytes, b, w);
+    int S[3];
+    block_term_sums(w, xv, sm8, S);
+#pragma unroll
+    for (int t = 0; t < 3; ++t) sums[((size_t)row * 3 + t) * nbk + b] = S[t];
   }
 }
 
@@ -859,6 +922,37 @@ extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, cons
   return DQMK_OK;
 }
 
+extern "C" int dqmk_gemv_packed_chained(int qtype, const float* x, int in_features,
+                                        const void* packed, int out_features, const float* norm_w,
+                                        float eps, int swiglu, float* y, void* stream) {
+  const char* api = "dqmk_gemv_packed_chained";
+  if (qtype != DQMK_Q80 && qtype != DQMK_Q40)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": unsupported quant type");
+  if (in_features <= 0 || out_features <= 0 || (swiglu && out_features % 2))
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid shape");
+  if (!x || !packed || !y) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  if (reinterpret_cast<uintptr_t>(packed) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": packed weight must be 16-byte aligned");
+  const int kp = (in_features + 31) / 32 * 32;
+  if (kp > 48 * 1024)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": in_features too large");
+  GemvArgs a = {};
+  a.qtype = qtype;
+  a.qs = static_cast<const uint8_t*>(packed);
+  a.d = reinterpret_cast<const uint16_t*>(a.qs + (size_t)out_features *
+                                                     (qtype == DQMK_Q80 ? kp : kp / 2));
+  a.n_rows = out_features;
+  a.k = in_features;
+  a.kp = kp;
+  a.x = x;
+  a.norm_w = norm_w;
+  a.eps = eps;
+  a.epi = swiglu ? kEpiSwiGlu : kEpiStore;
+  a.y = y;
+  DQMK_CUDA_RET(api, launch_gemv(a, static_cast<cudaStream_t>(stream), use_pdl()));
+  return DQMK_OK;
+}
+
 extern "C" int dqmk_device_error(int clear) {
   unsigned int flags = 0, prefill_flags = 0, tp_flags = 0, ops_flags = 0, batch_flags = 0;
   cudaError_t e = read_device_error(&flags, clear != 0);
@@ -897,5 +991,38 @@ extern "C" int dqmk_gemv_packed_withhold_tile(int qtype, const float* x, int in_
   a.epi = kEpiStore;
   a.y = y;
   DQMK_CUDA_RET(api, launch_gemv_tma_skip(a, static_cast<cudaStream_t>(stream), tile));
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_lm_head_block_sums(int qtype, const float* x, int in_features,
+                                       const void* packed, int out_features, int8_t* q_terms,
+                                       float* scales, int32_t* sums, void* stream) {
+  const char* api = "dqmk_lm_head_block_sums";
+  if (qtype != DQMK_Q80 && qtype != DQMK_Q40)
+    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": unsupported quant type");
+  if (in_features <= 0 || out_features <= 0 || !x || !packed || !q_terms || !scales || !sums)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid argument");
+  if (reinterpret_cast<uintptr_t>(packed) & 15u)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": packed weight must be 16-byte aligned");
+  const int kp = (in_features + 31) / 32 * 32;
+  if (kp > 8192) return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": in_features too large");
+  const int nbk = kp / 32;
+  const size_t smem = (size_t)kp * 4 + (size_t)3 * kp + (size_t)3 * nbk * 4 * 2;
+  const uint8_t* qs = static_cast<const uint8_t*>(packed);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (qtype == DQMK_Q80) {
+    DQMK_CUDA_RET(api, cudaFuncSetAttribute(block_sums_kernel<DQMK_Q80>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)smem));
+    block_sums_kernel<DQMK_Q80><<<1, kTmaConsumers, smem, st>>>(
+        x, in_features, kp, qs, out_features, q_terms, scales, sums);
+  } else {
+    DQMK_CUDA_RET(api, cudaFuncSetAttribute(block_sums_kernel<DQMK_Q40>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)smem));
+    block_sums_kernel<DQMK_Q40><<<1, kTmaConsumers, smem, st>>>(
+        x, in_features, kp, qs, out_features, q_terms, scales, sums);
+  }
+  DQMK_CUDA_RET(api, cudaGetLastError());
   return DQMK_OK;
 }

@@ -25,6 +25,8 @@ int cuda_fail(const char* api, cudaError_t err);
 const char* last_error_cstr();
 // SM count of the current device (cached per device).
 int sm_count();
+// Programmatic dependent launch between chained kernels (off with DQMK_PDL=0).
+bool use_pdl();
 
 // Kernel attributes (cudaFuncSetAttribute) and occupancy figures belong to
 // the device that is current when they are set or queried, so every one-time

@@ -114,6 +114,15 @@ int dqmk_gemv_packed(int qtype, const float* x_dev, int in_features, const void*
                      int out_features, const float* bias_dev, const float* residual_dev,
                      float* y_dev, void* stream);
 
+/* The decode step's GEMV as the step launches it, for measurement: RMSNorm
+ * of x by norm_dev (NULL: none) in the prologue, y = W x (swiglu == 0) or the
+ * SwiGLU of interleaved gate/up rows (swiglu != 0; y has out_features / 2
+ * values), launched with programmatic dependent launch so back-to-back calls
+ * overlap like the kernels of the captured step.  No reference counterpart. */
+int dqmk_gemv_packed_chained(int qtype, const float* x_dev, int in_features,
+                             const void* packed_dev, int out_features, const float* norm_dev,
+                             float eps, int swiglu, float* y_dev, void* stream);
+
 /* Batched (prefill) linear on a packed weight, on the tensor cores:
  * y[m][o] = residual[m][o] + bias[o] + sum_k W[o][k] x[m][k] for `m` rows
  * (residual_dev / bias_dev may be NULL; y_dev may equal residual_dev).  The
@@ -157,6 +166,19 @@ int dqmk_device_error(int clear);
 int dqmk_gemv_packed_withhold_tile(int qtype, const float* x_dev, int in_features,
                                    const void* packed_dev, int out_features, float* y_dev,
                                    int tile, void* stream);
+
+/* Test hook exposing the integer arithmetic of the TMA-staged GEMV (the
+ * lm_head form): x_dev (in_features floats) is split into three int8 terms
+ * per 32-value block, x ~= s1 q1 + s2 q2 + s3 q3, and every block b of every
+ * row of the packed weight is summed exactly against each term with dp4a:
+ * sums_dev[row][t][b] = sum_j w_j q_t[j] (Q4_0: nibble - 8).  Outputs:
+ * q_terms_dev [3][nb][32] int8, scales_dev [3][nb] float, sums_dev
+ * [out_features][3][nb] int32 (nb = ceil(in_features/32)).  One CTA; for
+ * checking against an integer restatement on the host, not for speed.  No
+ * reference counterpart: the reference's Linear has no integer dot product. */
+int dqmk_lm_head_block_sums(int qtype, const float* x_dev, int in_features,
+                            const void* packed_dev, int out_features, int8_t* q_terms_dev,
+                            float* scales_dev, int32_t* sums_dev, void* stream);
 
 /* ------------------------------------------------------------------ */
 /* Memory-bound ops                                                     */

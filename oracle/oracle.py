@@ -121,6 +121,11 @@ def ref():
     return _ref
 
 
+def ref_set_threads(n: int) -> None:
+    """SetThreadCount of the reference's CPU thread pool (src/thread_pool.cc:186)."""
+    ref().ref_set_threads(int(n))
+
+
 def _check_ref(rc: int) -> None:
     if rc != 0:
         raise RuntimeError(ref().ref_last_error().decode())
@@ -199,6 +204,54 @@ def linear(qtype: int, x: np.ndarray, w: np.ndarray, out_features: int,
         assert rows == 1
         lib().orc_linear_f32_simd(_f(x), inf, w.ctypes.data_as(_fp), out_features, _f(y))
     return y[0] if x.ndim == 1 else y
+
+
+# ---- integer restatement of the decode GEMV's int8 path (numpy) ----------
+# The reference's Linear has no integer dot product; the TMA-staged decode
+# GEMV (the lm_head form) quantizes x per 32-value block into three int8 terms
+# and sums int8 x int8 products exactly in int32.  These functions restate
+# that arithmetic on the host so its terms, scales and block sums can be
+# compared bit for bit.
+
+def x_terms(x: np.ndarray):
+    """x [k] -> (q [3, nb, 32] int8, s [3, nb] float32), x ~= sum_t s_t q_t per
+    block.  s_1 = absmax / 127 (0 for a zero block); term t: inv = 1 / s_t,
+    q_t = clamp(round-half-even(r * inv), -127, 127), r <- fl(r - s_t q_t)
+    (one rounding: s_t q_t is exact in float64, so the float64 difference is
+    exact and rounds once to float32), s_{t+1} = s_t * fl(1 / 254)."""
+    x = np.asarray(x, dtype=np.float32)
+    nb = (x.size + 31) // 32
+    r = np.zeros((nb, 32), np.float32)
+    r.reshape(-1)[: x.size] = x
+    m = np.abs(r).max(axis=1)
+    s = np.where(m > 0, m / np.float32(127.0), np.float32(0.0)).astype(np.float32)
+    step = np.float32(1.0) / np.float32(254.0)
+    q = np.zeros((3, nb, 32), np.int8)
+    sc = np.zeros((3, nb), np.float32)
+    for t in range(3):
+        with np.errstate(divide="ignore"):
+            inv = np.where(s > 0, np.float32(1.0) / s, np.float32(0.0)).astype(np.float32)
+        qq = np.clip(np.rint((r * inv[:, None]).astype(np.float32)), -127, 127)
+        r = (r.astype(np.float64) - s.astype(np.float64)[:, None] * qq).astype(np.float32)
+        q[t] = qq.astype(np.int8)
+        sc[t] = s
+        s = (s * step).astype(np.float32)
+    return q, sc
+
+
+def block_term_sums(qtype: int, blocks: np.ndarray, rows: int, cols: int,
+                    q: np.ndarray) -> np.ndarray:
+    """Exact sums[row, t, b] = sum_j w[row, 32 b + j] q[t, b, j] with the
+    block's integer weights (Q8_0: int8; Q4_0: nibble - 8), int64."""
+    nb = (cols + 31) // 32
+    bl = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(rows, nb, -1)
+    if qtype == Q80:
+        w = bl[:, :, 2:34].view(np.int8).astype(np.int64)
+    else:
+        lo = (bl[:, :, 2:18] & 0x0F).astype(np.int64) - 8
+        hi = (bl[:, :, 2:18] >> 4).astype(np.int64) - 8
+        w = np.concatenate([lo, hi], axis=2)
+    return np.einsum("rbj,tbj->rtb", w, q.astype(np.int64))
 
 
 def rmsnorm(x, w, eps, use_ref=False):

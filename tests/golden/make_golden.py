@@ -17,7 +17,15 @@ tests and bench.py regenerate on any machine, and stores its outputs:
                         Q4_0 weights: a 2048-id random prompt fills the KV cache,
                         then 128 greedy steps (same fields).
 
-Usage: python tests/golden/make_golden.py [--skip-full] [--q4-long]
+  qwen2_0_5b_q8_0_logits.npz  Whole logit vectors of the full-size Q8_0 model:
+                        after the 32-id prompt (step 0), after 16 further
+                        greedy tokens (step 16), and after a 602-id prompt run
+                        through the reference's per-token ForwardBatch (the
+                        batched-prefill workload), with that prompt's digest.
+  qwen2_0_5b_q4_0_ctx2048_logits.npz  Whole logit vectors of the Q4_0 model
+                        after its 2048-id prompt (step 0) and at step 64.
+
+Usage: python tests/golden/make_golden.py [--skip-full] [--q4-long] [--logits] [--q4-logits]
 """
 from __future__ import annotations
 
@@ -157,12 +165,61 @@ def make_q4_long(threads: int):
     print(json.dumps(res["seconds"]))
 
 
+def make_full_logits(threads: int):
+    t0 = time.time()
+    seed, prompt_seed = 20261201, 1
+    w = S.make_model(S.QWEN2_0_5B, S.Q80, seed, quantize_q80=lambda a: O.quantize_q80(a, True))
+    rm = O.RefModel(w, 602, threads=threads)
+    prompt = S.prompt_tokens(w.cfg["vocab"], 32, prompt_seed)
+    logits = rm.forward_batch(prompt, 0)
+    out = {"step0": logits.astype(np.float32)}
+    pos, steps = 32, 16
+    for _ in range(steps):
+        tok = int(O.argmax(logits, use_ref=True))
+        logits = rm.forward_batch([tok], pos)
+        pos += 1
+    out["step16"] = logits.astype(np.float32)
+    t1 = time.time()
+    rm.reset()
+    p602 = S.prompt_tokens(w.cfg["vocab"], 602, 4)
+    out["prefill602"] = rm.forward_batch(p602, 0).astype(np.float32)
+    t2 = time.time()
+    out["prefill602_prompt_sha256"] = np.frombuffer(digest(p602).encode(), np.uint8)
+    out["prefill602_seconds"] = np.array([t2 - t1, threads], np.float64)
+    np.savez_compressed(os.path.join(HERE, "qwen2_0_5b_q8_0_logits.npz"), **out)
+    print(json.dumps({"decode_s": t1 - t0, "prefill602_s": t2 - t1, "threads": threads}))
+
+
+def make_q4_logits(threads: int):
+    seed, prompt_seed, n_prompt = 20261202, 3, 2048
+    w = S.make_model(S.QWEN2_0_5B, S.Q40, seed)
+    rm = O.RefModel(w, n_prompt + 65, threads=threads)
+    prompt = S.prompt_tokens(w.cfg["vocab"], n_prompt, prompt_seed)
+    logits = rm.forward_batch(prompt, 0)
+    out = {"step0": logits.astype(np.float32)}
+    pos = n_prompt
+    for _ in range(64):
+        tok = int(np.argmax(logits))
+        logits = rm.forward_batch([tok], pos)
+        pos += 1
+    out["step64"] = logits.astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "qwen2_0_5b_q4_0_ctx2048_logits.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-full", action="store_true")
     ap.add_argument("--q4-long", action="store_true")
     ap.add_argument("--threads", type=int, default=os.cpu_count())
+    ap.add_argument("--logits", action="store_true")
+    ap.add_argument("--q4-logits", action="store_true")
     args = ap.parse_args()
+    if args.logits:
+        make_full_logits(args.threads)
+        return
+    if args.q4_logits:
+        make_q4_logits(args.threads)
+        return
     if args.q4_long:
         make_q4_long(args.threads)
         return

@@ -245,3 +245,36 @@ def test_attention_decode(pkg, orc, cuda, cfg):
     assert np.array_equal(bits(out), bits(exp))
     with pytest.raises(pkg.OutOfRange):
         pkg.CudaAttentionDecodeDeviceInput(qd, kv, 2, 0, n_heads, n_kv, hd)
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_lm_head_block_sums_exact(pkg, orc, S, cuda, qt):
+    """The TMA-staged GEMV's integer path, bit for bit: x split into three int8
+    terms per 32-value block (terms and scales equal to the host integer
+    restatement), and the int32 dp4a sums of every block of every row against
+    each term equal to exact integer sums -- at the five Qwen2-0.5B GEMV
+    shapes.  The terms also reconstruct x to within 1e-7 of each block's
+    largest magnitude."""
+    torch = cuda
+    L = pkg.lib()
+    for o, i in ((896, 896), (128, 896), (4864, 896), (896, 4864), (151936, 896)):
+        blocks, x = S.gemv_case(o, i, 5 + o % 97, qt)
+        packed = pkg.pack_weight(qt, blocks, o, i)
+        nb = (i + 31) // 32
+        q = torch.empty(3 * nb * 32, dtype=torch.int8, device="cuda")
+        sc = torch.empty(3 * nb, dtype=torch.float32, device="cuda")
+        sums = torch.empty(o * 3 * nb, dtype=torch.int32, device="cuda")
+        xd = torch.from_numpy(x).cuda()
+        pkg.check(L.dqmk_lm_head_block_sums(qt, xd.data_ptr(), i, packed.data_ptr(), o,
+                                            q.data_ptr(), sc.data_ptr(), sums.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        rq, rsc = orc.x_terms(x)
+        assert np.array_equal(q.cpu().numpy().reshape(3, nb, 32), rq), (o, i)
+        assert np.array_equal(sc.cpu().numpy().view(np.uint32), rsc.reshape(-1).view(np.uint32))
+        ref = orc.block_term_sums(qt, blocks, o, i, rq)
+        assert np.array_equal(sums.cpu().numpy().reshape(o, 3, nb).astype(np.int64), ref), (o, i)
+        recon = np.einsum("tbj,tb->bj", rq.astype(np.float64), rsc.astype(np.float64))
+        xb = np.zeros((nb, 32))
+        xb.reshape(-1)[:i] = x
+        assert np.all(np.abs(recon - xb) <= 1e-7 * np.abs(xb).max(axis=1, keepdims=True) + 1e-30)

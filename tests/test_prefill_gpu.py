@@ -154,3 +154,28 @@ def test_qwen2_0_5b_q4_0_ctx2048_prefill_then_128_greedy(pkg, S, cuda):
     assert tokens == g["greedy_tokens"], (
         f"first divergence at {next(i for i, (a, b) in enumerate(zip(tokens, g['greedy_tokens'])) if a != b)}"
         f", reference min margin {min(g['top1_top2_margin']):.3e}")
+
+
+def test_qwen2_0_5b_q8_0_prefill_602_whole_logits(pkg, S, cuda):
+    """Configuration 4 at full size: the Qwen2-0.5B-architecture Q8_0 model
+    (reference-quantized weights) runs one 602-id prompt as a single batched
+    ForwardBatch (tensor-core GEMMs, causal attention); its whole 151936-entry
+    logit vector must sit within 1e-3 x logit range of the reference's own
+    per-token ForwardBatch loop over the same prompt."""
+    import hashlib
+
+    g = np.load(golden_path("qwen2_0_5b_q8_0_logits.npz"))
+    w = S.make_model(S.QWEN2_0_5B, S.Q80, 20261201,
+                     quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+    prompt = S.prompt_tokens(w.cfg["vocab"], 602, 4)
+    sha = hashlib.sha256(np.ascontiguousarray(prompt).tobytes()).hexdigest()
+    assert sha == bytes(g["prefill602_prompt_sha256"]).decode()
+    model = pkg.Model.from_synth(w, max_seq_len=602)
+    ctx = pkg.Context(model)
+    logits = ctx.ForwardBatch(prompt.tolist(), 0)
+    err = check_logits(logits, g["prefill602"], "602-token batched prefill")
+    print(f"602-token prefill: relative logit error {err:.2e}")
+    assert int(np.argmax(logits)) == int(np.argmax(g["prefill602"]))
+    ctx.close()
+    model.close()
+
