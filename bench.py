@@ -266,6 +266,32 @@ def profile_traffic(name="gemv_q8_0_lm_head_151936x896.md", key="dram_bytes_per_
     return None
 
 
+def int8_peak(torch):
+    """Dense int8 tensor-core throughput measured here: torch._int_mm (cuBLASLt
+    int8 x int8 -> int32) at 8192^3, best of 10 after warm-up, CUDA events;
+    None where the call is unavailable."""
+    try:
+        n = 8192
+        a = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda").t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = None
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            e1.synchronize()
+            t = e0.elapsed_time(e1) / 1e3
+            best = t if best is None else min(best, t)
+        del a, b
+        torch.cuda.empty_cache()
+        return round(2.0 * n ** 3 / best / 1e12, 1)
+    except Exception:
+        return None
+
+
 def tensor_peak():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -320,8 +346,22 @@ def time_prefill(pkg, torch, S, w, n_tokens: int = 602):
     # three fp16 products per weight: A_hi B_hi, A_hi B_lo, A_lo B_hi
     issued = 2.0 * 3 * (m_tiles * 128) * kp64 * (n_tiles * 128) / t / 1e12
     peak, src = tensor_peak()
+    i8 = int8_peak(torch)
+    # useful work of the whole prefill: every linear over all rows, the
+    # lm_head on the last row, causal attention (QK^T and PV)
+    hd = c["dim"] // c["n_heads"]
+    per_layer = (c["dim"] + 2 * c["n_kv_heads"] * hd) * c["dim"] + c["dim"] * c["dim"] \
+        + 2 * c["hidden"] * c["dim"] + c["dim"] * c["hidden"]
+    attn = 4 * hd * c["n_heads"] * (n_tokens * (n_tokens + 1) // 2) * c["n_layers"]
+    ops = 2 * n_tokens * per_layer * c["n_layers"] + 2 * c["vocab"] * c["dim"] + attn
+    whole = ops / dev / 1e12
     return {
         "tokens": n_tokens, "tok_s": round(n_tokens / wall, 1),
+        "useful_tops": round(whole, 2), "useful_ops": ops,
+        "frac_of_int8_peak": round(whole / i8, 4) if i8 else None,
+        "int8_peak_tops": i8, "int8_peak_source": "measured here: torch._int_mm (cuBLASLt "
+                                                   "int8) at 8192^3, best of 10",
+        "frac_of_bf16_peak": round(whole / peak, 4), "bf16_peak_source": src,
         "device_tok_s": round(n_tokens / dev, 1), "ms": round(wall * 1e3, 3),
         "device_ms": round(dev * 1e3, 3),
         "path": "ForwardBatch: per layer RMSNorm + two-term fp16 split, persistent tcgen05 "
@@ -330,7 +370,8 @@ def time_prefill(pkg, torch, S, w, n_tokens: int = 602):
         "linear_batch": {"shape": f"{m}x{k}->{o}", "us_per_call": round(t * 1e6, 2),
                          "useful_tflops": round(useful, 1), "issued_tflops": round(issued, 1),
                          "peak_tflops": peak, "peak_source": src,
-                         "frac_issued_of_peak": round(issued / peak, 4),
+                         "frac_useful_of_bf16_peak": round(useful / peak, 4),
+                         "frac_useful_of_int8_peak": round(useful / i8, 4) if i8 else None,
                          "note": "standalone op per call: activation split and weight "
                                  "two-term split launches included"},
     }

@@ -462,42 +462,10 @@ extern "C" int dqmk_model_finalize(dqmk_model* m) {
       if ((rc = upload_f32(m, perm, &L.qkv_bias, api))) return rc;
     }
   }
-  // batched-prefill side tables (see prefill.cu); skipped for head sizes the
-  // prefill attention kernel does not take, which then prefill token by token
-  if ((hd == 64 || hd == 128) && tp.world == 1) {
-    // the decode path keeps streaming the packed quants; the tensor cores
-    // take the same values as two exact fp16 planes per weight
-    auto side = [&](const Packed& w, float** cs, CUtensorMap* maps) -> int {
-      void* p = nullptr;
-      int r = dev_alloc(m->allocs, (size_t)w.rows * sizeof(float), &p, api);
-      if (r) return r;
-      *cs = static_cast<float*>(p);
-      void* planes[2];
-      for (int t = 0; t < 2; ++t) {
-        if ((r = dev_alloc(m->allocs, (size_t)w.rows * w.kp * 2, &planes[t], api))) return r;
-        if ((r = make_f16_tile_map(&maps[t], planes[t], w.rows, w.kp))) return r;
-      }
-      cudaError_t e = launch_weights_split(w.qtype, w.qs(), w.d(), w.rows, w.kp,
-                                           static_cast<uint16_t*>(planes[0]),
-                                           static_cast<uint16_t*>(planes[1]), *cs, nullptr);
-      if (e != cudaSuccess) return cuda_fail(api, e);
-      return DQMK_OK;
-    };
-    // the lm_head GEMV reads the last activation row with 16-byte vectors
-    bool ok = c.dim % 4 == 0;
-    for (int l = 0; ok && l < c.n_layers; ++l) {
-      Layer& L = m->layers[l];
-      if ((rc = side(L.qkv, &L.cs_qkv, L.map_qkv))) return rc;
-      if ((rc = side(L.wo, &L.cs_o, L.map_o))) return rc;
-      if ((rc = side(L.gate_up, &L.cs_gu, L.map_gu))) return rc;
-      if ((rc = side(L.down, &L.cs_dn, L.map_dn))) return rc;
-    }
-    if (ok) {
-      cudaError_t e = cudaDeviceSynchronize();
-      if (e != cudaSuccess) return cuda_fail(api, e);
-    }
-    m->prefill_ready = ok;
-  }
+  // batched-prefill side tables (see prefill.cu) are built on the first
+  // batched ForwardBatch; head sizes the prefill attention kernel does not
+  // take, and tensor-parallel shards, prefill token by token
+  m->prefill_eligible = (hd == 64 || hd == 128) && tp.world == 1 && c.dim % 4 == 0;
 
   // RoPE table for every cache position
   std::vector<float2> cs((size_t)c.max_seq_len * (hd / 2));
@@ -514,6 +482,46 @@ extern "C" int dqmk_model_finalize(dqmk_model* m) {
       kv.second.dev = nullptr;
     }
   m->finalized = true;
+  return DQMK_OK;
+}
+
+// The batched prefill's side tables: per projection the exact two-term fp16
+// planes of the dequantized weight (4 bytes per weight) and the per-row
+// power-of-two scales.  Built once, on the first batched ForwardBatch, and
+// counted in memory_bytes from then on, so an engine that only decodes holds
+// (and reports) the block bytes plus the resident F32 tensors, the
+// reference's accounting (src/model.cc:227-260).
+int ensure_prefill_weights(dqmk_model* m, const char* api) {
+  if (m->prefill_ready) return DQMK_OK;
+  if (!m->prefill_eligible) return fail(DQMK_ERR_UNSUPPORTED, std::string(api) +
+                                                                  ": no batched prefill for this model");
+  auto side = [&](const Packed& w, float** cs, CUtensorMap* maps) -> int {
+    void* p = nullptr;
+    int r = dev_alloc(m->allocs, (size_t)w.rows * sizeof(float), &p, api);
+    if (r) return r;
+    *cs = static_cast<float*>(p);
+    void* planes[2];
+    for (int t = 0; t < 2; ++t) {
+      if ((r = dev_alloc(m->allocs, (size_t)w.rows * w.kp * 2, &planes[t], api))) return r;
+      if ((r = make_f16_tile_map(&maps[t], planes[t], w.rows, w.kp))) return r;
+    }
+    m->memory_bytes += (size_t)w.rows * sizeof(float) + (size_t)2 * w.rows * w.kp * 2;
+    cudaError_t e = launch_weights_split(w.qtype, w.qs(), w.d(), w.rows, w.kp,
+                                         static_cast<uint16_t*>(planes[0]),
+                                         static_cast<uint16_t*>(planes[1]), *cs, nullptr);
+    if (e != cudaSuccess) return cuda_fail(api, e);
+    return DQMK_OK;
+  };
+  int rc;
+  for (int l = 0; l < m->cfg.n_layers; ++l) {
+    Layer& L = m->layers[l];
+    if ((rc = side(L.qkv, &L.cs_qkv, L.map_qkv))) return rc;
+    if ((rc = side(L.wo, &L.cs_o, L.map_o))) return rc;
+    if ((rc = side(L.gate_up, &L.cs_gu, L.map_gu))) return rc;
+    if ((rc = side(L.down, &L.cs_dn, L.map_dn))) return rc;
+  }
+  DQMK_CUDA_RET(api, cudaDeviceSynchronize());
+  m->prefill_ready = true;
   return DQMK_OK;
 }
 
@@ -1209,7 +1217,8 @@ extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int*
   cudaSetDevice(x->m->device);
   bool consecutive = true;
   for (int i = 1; i < n && consecutive; ++i) consecutive = positions[i] == positions[0] + i;
-  if (n > 1 && consecutive && x->m->prefill_ready && prefill_enabled()) {
+  if (n > 1 && consecutive && x->m->prefill_eligible && prefill_enabled()) {
+    if ((rc = ensure_prefill_weights(x->m, api))) return rc;
     if ((rc = ensure_prefill(x))) return rc;
     for (int i0 = 0; i0 < n; i0 += x->pf.m_max) {
       const int cnt = std::min(x->pf.m_max, n - i0);

@@ -72,7 +72,8 @@ struct dqmk_model {
   std::vector<dqmk::Layer> layers;
   dqmk::Packed embd, lm_head;
   bool tied = true;
-  bool prefill_ready = false;  // two-term weight planes and TMA maps built
+  bool prefill_eligible = false;  // batched prefill possible (head size, no TP)
+  bool prefill_ready = false;     // its two-term weight planes and TMA maps built
   bool batch_ready = false;    // multi-sequence GEMM tables built
   std::vector<dqmk::BatchLayer> batch_layers;
   dqmk::BatchWeight batch_lm;

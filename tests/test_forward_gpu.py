@@ -104,6 +104,15 @@ def test_runtime_counters(pkg, mini, cuda):
                                        for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))
     f32 = 4 * (c["dim"] + L * (2 * c["dim"] + c["n_heads"] * hd + 2 * c["n_kv_heads"] * hd))
     assert model.memory_bytes() == blocks + f32
+    # the first batched ForwardBatch builds the tensor-core side tables --
+    # two fp16 planes per weight (4 bytes per weight, rows padded to 32
+    # values) and a float scale per row -- and the accounting grows by them
+    ctx.ForwardBatch([3, 4, 5, 6], 3)
+    kp = lambda k: (k + 31) // 32 * 32
+    rows_k = [(c["dim"] + 2 * c["n_kv_heads"] * hd, c["dim"]), (c["dim"], c["n_heads"] * hd),
+              (2 * c["hidden"], c["dim"]), (c["dim"], c["hidden"])]
+    planes = L * sum(r * 4 + 4 * r * kp(k) for r, k in rows_k)
+    assert model.memory_bytes() == blocks + f32 + planes
 
 
 @pytest.mark.parametrize("qt", [1, 2])
