@@ -15,20 +15,21 @@ from typing import Optional, Sequence
 import numpy as np
 
 from . import synth
-from ._lib import (F32, Q40, Q80, CudaError, ModelConfig, ModelStats, OutOfRange, TpPlan, build,
-                   check, lib)
+from ._lib import (F32, Q40, Q41, Q80, CudaError, ModelConfig, ModelStats, OutOfRange, TpPlan,
+                   build, check, lib)
 
 __all__ = [
-    "F32", "Q80", "Q40", "OutOfRange", "CudaError", "build", "lib", "synth",
+    "F32", "Q80", "Q40", "Q41", "OutOfRange", "CudaError", "build", "lib", "synth",
     "QuantizeToQ80", "QuantizeToQ40", "DequantizeFromQ80", "DequantizeFromQ40",
     "CudaQ80Linear", "CudaQ40Linear", "CudaQ80LinearDeviceInput", "CudaQ40LinearDeviceInput",
     "pack_weight", "gemv_packed", "CudaRmsNormDeviceWeight", "CudaSiluMulDeviceInput",
     "CudaElementwiseAddDeviceInput", "CudaRopeDeviceInput", "CudaEmbeddingLookupDeviceWeight",
     "embedding_lookup_blocks", "argmax", "CudaKvCache", "CudaAttentionDecodeDeviceInput",
     "Model", "Context", "Batch", "BLOCK_BYTES", "linear_batch_packed", "linear_cols_packed",
+    "CudaQ41Linear", "CudaQ41LinearDeviceInput", "CudaLinear", "CudaLinearDeviceInput",
 ]
 
-BLOCK_BYTES = {Q80: 34, Q40: 18}
+BLOCK_BYTES = {Q80: 34, Q40: 18, Q41: 20}
 
 
 def _torch():
@@ -110,13 +111,14 @@ def _linear_device(qtype, x, blocks, block_count, weight_shape, bias=None):
     if len(weight_shape) != 2:
         raise RuntimeError("LinearQuantized: expected 2D weight shape")
     out_f, in_f = weight_shape
+    name = {Q80: "CudaQ80Linear", Q40: "CudaQ40Linear", Q41: "CudaQ41Linear"}[qtype]
     if x.shape[-1] != in_f:
-        raise RuntimeError(("CudaQ80Linear" if qtype == Q80 else "CudaQ40Linear") +
-                           ": dimension mismatch")
+        raise RuntimeError(name + ": dimension mismatch")
     rows = 1 if x.dim() == 1 else x.shape[0]
     y = torch.empty((out_f,) if x.dim() == 1 else (rows, out_f), dtype=torch.float32,
                     device=x.device)
-    fn = lib().dqmk_q80_linear if qtype == Q80 else lib().dqmk_q40_linear
+    fn = {Q80: lib().dqmk_q80_linear, Q40: lib().dqmk_q40_linear,
+          Q41: lib().dqmk_q41_linear}[qtype]
     check(fn(_ptr(x), rows, in_f, _ptr(blocks), block_count, out_f, _ptr(bias), _ptr(y),
              _stream()))
     return y
@@ -129,6 +131,35 @@ def CudaQ80LinearDeviceInput(x, q8_0_device, block_count: int, weight_shape):
 
 def CudaQ40LinearDeviceInput(x, q4_0_device, block_count: int, weight_shape):
     return _linear_device(Q40, x, q4_0_device, block_count, weight_shape)
+
+
+def CudaQ41LinearDeviceInput(x, q4_1_device, block_count: int, weight_shape):
+    """include/dqm_llama/cuda_quant.h:59-63."""
+    return _linear_device(Q41, x, q4_1_device, block_count, weight_shape)
+
+
+def CudaLinearDeviceInput(x, w_device, weight_shape, bias=None):
+    """include/dqm_llama/cuda_matmul.h:35-41: F32 weight [out, in] on the device."""
+    torch = _torch()
+    out_f, in_f = weight_shape
+    if x.shape[-1] != in_f:
+        raise RuntimeError("CudaLinear: dimension mismatch")
+    rows = 1 if x.dim() == 1 else x.shape[0]
+    y = torch.empty((out_f,) if x.dim() == 1 else (rows, out_f), dtype=torch.float32,
+                    device=x.device)
+    check(lib().dqmk_f32_linear(_ptr(x), rows, in_f, _ptr(w_device), out_f, _ptr(bias), _ptr(y),
+                                _stream()))
+    return y
+
+
+def CudaLinear(x, weight, bias=None):
+    """include/dqm_llama/cuda_matmul.h:25-27: host x and F32 weight [out, in]."""
+    torch = _torch()
+    w = _dev(weight, torch.float32)
+    y = CudaLinearDeviceInput(_dev(x, torch.float32), w, tuple(w.shape),
+                              None if bias is None else _dev(bias, torch.float32))
+    torch.cuda.current_stream().synchronize()
+    return y.cpu().numpy()
 
 
 def _linear_host(qtype, x, blocks, weight_shape, bias=None):
@@ -148,6 +179,11 @@ def CudaQ80Linear(x, weight_blocks, weight_shape, bias=None):
 
 def CudaQ40Linear(x, weight_blocks, weight_shape, bias=None):
     return _linear_host(Q40, x, weight_blocks, weight_shape, bias)
+
+
+def CudaQ41Linear(x, weight_blocks, weight_shape, bias=None):
+    """include/dqm_llama/cuda_quant.h:49-51."""
+    return _linear_host(Q41, x, weight_blocks, weight_shape, bias)
 
 
 def pack_weight(qtype: int, blocks, out_features: int, in_features: int):

@@ -20,7 +20,7 @@ DQMK_ERR_TIMEOUT = 4
 DQMK_ERR_UNSUPPORTED = 5
 DQMK_ERR_NOMEM = 6
 
-F32, Q80, Q40 = 0, 1, 2
+F32, Q80, Q40, Q41 = 0, 1, 2, 3
 
 # Every symbol include/dqmk.h declares, with its ctypes signature.
 _vp, _i, _i64, _sz, _f = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
@@ -58,6 +58,8 @@ SIGNATURES = {
     "dqmk_dequantize_q40": ([_vp, _i64, _i64, _vp, _vp], _i),
     "dqmk_q80_linear": ([_vp, _i, _i, _vp, _sz, _i, _vp, _vp, _vp], _i),
     "dqmk_q40_linear": ([_vp, _i, _i, _vp, _sz, _i, _vp, _vp, _vp], _i),
+    "dqmk_q41_linear": ([_vp, _i, _i, _vp, _sz, _i, _vp, _vp, _vp], _i),
+    "dqmk_f32_linear": ([_vp, _i, _i, _vp, _i, _vp, _vp, _vp], _i),
     "dqmk_packed_bytes": ([_i, _i, _i], _sz),
     "dqmk_pack_weight": ([_i, _vp, _sz, _i, _i, _vp, _vp], _i),
     "dqmk_gemv_packed": ([_i, _vp, _i, _vp, _i, _vp, _vp, _vp, _vp], _i),

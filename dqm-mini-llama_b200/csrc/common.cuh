@@ -111,6 +111,13 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return r;
 }
 
+// 128-bit streaming load of four floats (read once, no L1 allocation).
+__device__ __forceinline__ float4 ldg_f4_stream(const float* p) {
+  const uint4 r = ldg_stream(p);
+  return make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z),
+                     __uint_as_float(r.w));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -704,14 +704,16 @@ bool tma_eligible(const GemvArgs& a) {
 }
 
 // ------------------------------------------------ ggml-layout compatibility
-// One warp per weight row, blocks read in place (34 / 18 bytes, 2-byte
+// One warp per weight row, blocks read in place (34 / 18 / 20 bytes, 2-byte
 // aligned), up to 8 input rows per pass.  Serves the drop-in entry points
 // that receive raw ggml blocks (CudaQ80LinearDeviceInput and friends).
+// Q4_1 (d * q + m): per block d * sum(q x) + m * sum(x).
 template <int QT>
 __global__ void linear_blocks_kernel(const float* __restrict__ x, int rows, int in_features,
                                      const uint8_t* __restrict__ blocks, int out_features,
                                      const float* __restrict__ bias, float* __restrict__ y) {
-  constexpr int BYTES = QT == DQMK_Q80 ? 34 : 18;
+  constexpr int BYTES = QT == DQMK_Q80 ? 34 : (QT == DQMK_Q40 ? 18 : 20);
+  constexpr int QS = QT == DQMK_Q41 ? 2 : 1;  // first 16-bit word of the quants
   const int lane = threadIdx.x & 31;
   const int nb = (in_features + 31) / 32;
   const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -725,18 +727,20 @@ __global__ void linear_blocks_kernel(const float* __restrict__ x, int rows, int 
         const uint8_t* p = blocks + ((size_t)o * nb + b) * BYTES;
         const uint16_t* p16 = reinterpret_cast<const uint16_t*>(p);
         const float d = h2f(__ldg(p16));
+        const float mn = QT == DQMK_Q41 ? h2f(__ldg(p16 + 1)) : 0.0f;
         float w[32];
 #pragma unroll
         for (int j = 0; j < (QT == DQMK_Q80 ? 16 : 8); ++j) {
-          const uint16_t v = __ldg(p16 + 1 + j);
+          const uint16_t v = __ldg(p16 + QS + j);
           if constexpr (QT == DQMK_Q80) {
             w[2 * j] = (float)(int8_t)(v & 0xff);
             w[2 * j + 1] = (float)(int8_t)(v >> 8);
           } else {
-            w[2 * j] = (float)((v & 0x0f) - 8);
-            w[2 * j + 16] = (float)(((v >> 4) & 0x0f) - 8);
-            w[2 * j + 1] = (float)(((v >> 8) & 0x0f) - 8);
-            w[2 * j + 17] = (float)((v >> 12) - 8);
+            constexpr int off = QT == DQMK_Q40 ? 8 : 0;
+            w[2 * j] = (float)((v & 0x0f) - off);
+            w[2 * j + 16] = (float)(((v >> 4) & 0x0f) - off);
+            w[2 * j + 1] = (float)(((v >> 8) & 0x0f) - off);
+            w[2 * j + 17] = (float)((v >> 12) - off);
           }
         }
         const int valid = min(32, in_features - b * 32);
@@ -744,12 +748,68 @@ __global__ void linear_blocks_kernel(const float* __restrict__ x, int rows, int 
         for (int i = 0; i < 8; ++i) {
           if (r0 + i < rows) {
             const float* xr = x + (size_t)(r0 + i) * in_features + b * 32;
-            float s = 0.0f;
+            float s = 0.0f, sx = 0.0f;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (j < valid) s = fmaf(w[j], xr[j], s);
+              if (j < valid) {
+                s = fmaf(w[j], xr[j], s);
+                if constexpr (QT == DQMK_Q41) sx += xr[j];
+              }
             acc[i] = fmaf(d, s, acc[i]);
+            if constexpr (QT == DQMK_Q41) acc[i] = fmaf(mn, sx, acc[i]);
           }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float v = warp_sum(acc[i]);
+        if (lane == 0 && r0 + i < rows)
+          y[(size_t)(r0 + i) * out_features + o] = bias ? __fadd_rn(v, bias[o]) : v;
+      }
+    }
+  }
+}
+
+// F32 weights (the reference's cuBLAS SGEMM path, src/cuda_matmul.cc:60-64,
+// 181-216, which creates a cuBLAS handle per call): one warp per output row,
+// the row streamed with 16-byte loads when in_features % 4 == 0 (otherwise
+// scalar), up to 8 input rows per pass, warp-shuffle reduction.
+__global__ void linear_f32_kernel(const float* __restrict__ x, int rows, int in_features,
+                                  const float* __restrict__ w, int out_features,
+                                  const float* __restrict__ bias, float* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  const bool vec = (in_features & 3) == 0 && ((reinterpret_cast<uintptr_t>(w) |
+                                               reinterpret_cast<uintptr_t>(x)) & 15u) == 0;
+  for (int o = warp; o < out_features; o += nwarps) {
+    const float* wr = w + (size_t)o * in_features;
+    for (int r0 = 0; r0 < rows; r0 += 8) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+      if (vec) {
+        const int k4 = in_features >> 2;
+        for (int c = lane; c < k4; c += 32) {
+          const float4 wv = ldg_f4_stream(wr + 4 * c);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (r0 + i < rows) {
+              const float4 xv =
+                  *reinterpret_cast<const float4*>(x + (size_t)(r0 + i) * in_features + 4 * c);
+              acc[i] = fmaf(wv.x, xv.x, acc[i]);
+              acc[i] = fmaf(wv.y, xv.y, acc[i]);
+              acc[i] = fmaf(wv.z, xv.z, acc[i]);
+              acc[i] = fmaf(wv.w, xv.w, acc[i]);
+            }
+          }
+        }
+      } else {
+        for (int k = lane; k < in_features; k += 32) {
+          const float wv = __ldg(wr + k);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (r0 + i < rows) acc[i] = fmaf(wv, x[(size_t)(r0 + i) * in_features + k], acc[i]);
         }
       }
 #pragma unroll
@@ -844,9 +904,15 @@ cudaError_t launch_linear_blocks(int qtype, const float* x, int rows, int in_fea
   if (qtype == DQMK_Q80)
     linear_blocks_kernel<DQMK_Q80><<<grid, warps_per_cta * 32, 0, stream>>>(
         x, rows, in_features, b, out_features, bias, y);
-  else
+  else if (qtype == DQMK_Q40)
     linear_blocks_kernel<DQMK_Q40><<<grid, warps_per_cta * 32, 0, stream>>>(
         x, rows, in_features, b, out_features, bias, y);
+  else if (qtype == DQMK_Q41)
+    linear_blocks_kernel<DQMK_Q41><<<grid, warps_per_cta * 32, 0, stream>>>(
+        x, rows, in_features, b, out_features, bias, y);
+  else
+    linear_f32_kernel<<<grid, warps_per_cta * 32, 0, stream>>>(
+        x, rows, in_features, static_cast<const float*>(blocks), out_features, bias, y);
   return cudaGetLastError();
 }
 
@@ -889,6 +955,24 @@ extern "C" int dqmk_q40_linear(const float* x, int rows, int in_features, const 
                                float* y, void* stream) {
   return linear_common("CudaQ40Linear", DQMK_Q40, x, rows, in_features, blocks, block_count,
                        out_features, bias, y, stream);
+}
+
+extern "C" int dqmk_q41_linear(const float* x, int rows, int in_features, const void* blocks,
+                               size_t block_count, int out_features, const float* bias,
+                               float* y, void* stream) {
+  return linear_common("CudaQ41Linear", DQMK_Q41, x, rows, in_features, blocks, block_count,
+                       out_features, bias, y, stream);
+}
+
+extern "C" int dqmk_f32_linear(const float* x, int rows, int in_features, const float* w,
+                               int out_features, const float* bias, float* y, void* stream) {
+  const char* api = "CudaLinear";
+  if (rows <= 0 || in_features <= 0 || out_features <= 0)
+    return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid shape");
+  if (!x || !w || !y) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
+  DQMK_CUDA_RET(api, launch_linear_blocks(DQMK_F32, x, rows, in_features, w, out_features, bias,
+                                          y, static_cast<cudaStream_t>(stream)));
+  return DQMK_OK;
 }
 
 extern "C" int dqmk_gemv_packed(int qtype, const float* x, int in_features, const void* packed,

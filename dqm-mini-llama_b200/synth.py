@@ -24,8 +24,8 @@ from typing import Callable, List, Optional
 
 import numpy as np
 
-Q80, Q40 = 1, 2
-BLOCK_BYTES = {Q80: 34, Q40: 18}
+Q80, Q40, Q41 = 1, 2, 3
+BLOCK_BYTES = {Q80: 34, Q40: 18, Q41: 20}
 
 QWEN2_0_5B = dict(name="qwen2-0.5b", vocab=151936, dim=896, hidden=4864, n_layers=24,
                   n_heads=14, n_kv_heads=2, rope_theta=1e6, eps=1e-6, bias=True, tied=True)
@@ -147,8 +147,9 @@ def prompt_tokens(vocab: int, n: int, seed: int) -> np.ndarray:
 
 
 def gemv_case(out_features: int, in_features: int, seed: int, qtype: int = Q80):
-    """Standalone GEMV inputs: int8 values uniform in [-127, 127] (Q4_0: nibbles
-    uniform in [0, 15]), fp16 scales uniform in [1e-4, 1e-2], x ~ N(0, 1).
+    """Standalone GEMV inputs: int8 values uniform in [-127, 127] (Q4_0 / Q4_1:
+    nibbles uniform in [0, 15]; Q4_1 minima uniform in [-0.08, 0]), fp16 scales
+    uniform in [1e-4, 1e-2], x ~ N(0, 1).
     Returns (blocks uint8, x float32)."""
     g = rng_for(seed, 7000 + qtype)
     nb = (in_features + 31) // 32
@@ -157,6 +158,10 @@ def gemv_case(out_features: int, in_features: int, seed: int, qtype: int = Q80):
     if qtype == Q80:
         qs = g.integers(-127, 128, size=(n, 32), dtype=np.int16).astype(np.int8).view(np.uint8)
         blocks = np.concatenate([d, qs], axis=1)
+    elif qtype == Q41:
+        m = g.uniform(-0.08, 0.0, size=n).astype(np.float16).view(np.uint8).reshape(n, 2)
+        qs = g.integers(0, 256, size=(n, 16), dtype=np.int16).astype(np.uint8)
+        blocks = np.concatenate([d, m, qs], axis=1)
     else:
         qs = g.integers(0, 256, size=(n, 16), dtype=np.int16).astype(np.uint8)
         blocks = np.concatenate([d, qs], axis=1)

@@ -42,7 +42,7 @@ typedef enum dqmk_status {
   DQMK_ERR_NOMEM = 6        /* device allocation failed */
 } dqmk_status;
 
-enum { DQMK_F32 = 0, DQMK_Q80 = 1, DQMK_Q40 = 2 };
+enum { DQMK_F32 = 0, DQMK_Q80 = 1, DQMK_Q40 = 2, DQMK_Q41 = 3 };
 
 /* Message of the last failed call on this host thread ("" if none). */
 const char* dqmk_last_error(void);
@@ -92,6 +92,22 @@ int dqmk_q80_linear(const float* x_dev, int rows, int in_features, const void* b
 int dqmk_q40_linear(const float* x_dev, int rows, int in_features, const void* blocks_dev,
                     size_t block_count, int out_features, const float* bias_dev,
                     float* y_dev, void* stream);
+
+/* Q4_1 twin (20-byte blocks { fp16 d; fp16 m; uint8 qs[16] }, value d * q + m
+ * with an unsigned nibble q): CudaQ41LinearDeviceInput / CudaQ41Linear
+ * (DeviceWeight) (include/dqm_llama/cuda_quant.h:49-63; src/cuda_quant.cu:
+ * 105-127). */
+int dqmk_q41_linear(const float* x_dev, int rows, int in_features, const void* blocks_dev,
+                    size_t block_count, int out_features, const float* bias_dev,
+                    float* y_dev, void* stream);
+
+/* F32-weight Linear: y_dev[rows, out] = x_dev[rows, in] * W^T (+ bias) for
+ * W_dev [out_features, in_features] float.  Replaces CudaLinear /
+ * CudaLinearDeviceWeight / CudaLinearDeviceInput (include/dqm_llama/
+ * cuda_matmul.h:25-41; src/cuda_matmul.cc:60-64,167,209,251: a cuBLAS SGEMM
+ * with a handle created per call).  A bandwidth-bound warp-per-row kernel. */
+int dqmk_f32_linear(const float* x_dev, int rows, int in_features, const float* w_dev,
+                    int out_features, const float* bias_dev, float* y_dev, void* stream);
 
 /* ------------------------------------------------------------------ */
 /* Planar ("packed") weights: the layout the engine keeps in HBM        */

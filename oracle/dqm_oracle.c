@@ -238,6 +238,41 @@ void orc_linear_q40(const float* x, int rows, int in_features,
   }
 }
 
+/* src/quant.cc:256-262 (DequantQ41, d * q + m: contracted to one fused
+ * multiply-add in the -O3 -mfma build) and :326-344 (the k loop) */
+static float dequant_q41(const orc_block_q41* blk, int i) {
+  const int q = i < 16 ? (blk->qs[i] & 0x0f) : (blk->qs[i - 16] >> 4);
+  return fmaf(orc_fp16_to_fp32(blk->d), (float)q, orc_fp16_to_fp32(blk->m));
+}
+
+void orc_linear_q41(const float* x, int rows, int in_features,
+                    const orc_block_q41* w, int out_features, float* y) {
+  const int nb = (int)blocks_per_row(in_features);
+  for (int64_t flat = 0; flat < (int64_t)rows * out_features; ++flat) {
+    const int r = (int)(flat / out_features);
+    const int j = (int)(flat % out_features);
+    const float* xr = x + (int64_t)r * in_features;
+    float sum = 0.0f;
+    for (int b = 0; b < nb; ++b) {
+      const orc_block_q41* blk = w + (int64_t)j * nb + b;
+      const int k0 = b * 32;
+      const int k1 = k0 + 32 < in_features ? k0 + 32 : in_features;
+      for (int k = k0; k < k1; ++k) sum = fmaf(dequant_q41(blk, k - k0), xr[k], sum);
+    }
+    y[flat] = sum;
+  }
+}
+
+/* src/quant.cc:192-235 (DequantizeFromQ41): the same d * q + m per value as
+ * the Linear's dequantization, low nibbles values 0-15, high 16-31 */
+void orc_dequantize_q41(const orc_block_q41* blocks, int64_t n_rows, int64_t row_size,
+                        float* dst) {
+  const int64_t nb = blocks_per_row(row_size);
+  for (int64_t r = 0; r < n_rows; ++r)
+    for (int64_t k = 0; k < row_size; ++k)
+      dst[r * row_size + k] = dequant_q41(blocks + r * nb + k / 32, (int)(k % 32));
+}
+
 /* F32 Linear in the reference's default "threaded-simd" mode:
  * src/matmul_dispatch.cc:208-222 (LinearThreadedSimd) over
  * src/matmul_dispatch.cc:153-173 (DotSimdAvx2).  Eight lane accumulators

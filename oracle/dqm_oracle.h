@@ -23,6 +23,12 @@ typedef struct {
   uint8_t qs[16];
 } orc_block_q40; /* 18 bytes */
 
+typedef struct {
+  uint16_t d;
+  uint16_t m;
+  uint8_t qs[16];
+} orc_block_q41; /* 20 bytes: x = d * q + m, q an unsigned nibble */
+
 enum { ORC_F32 = 0, ORC_Q80 = 1, ORC_Q40 = 2 };
 
 float orc_fp16_to_fp32(uint16_t h);
@@ -41,6 +47,10 @@ void orc_linear_q80(const float* x, int rows, int in_features,
                     const orc_block_q80* w, int out_features, float* y);
 void orc_linear_q40(const float* x, int rows, int in_features,
                     const orc_block_q40* w, int out_features, float* y);
+void orc_dequantize_q41(const orc_block_q41* blocks, int64_t n_rows,
+                        int64_t row_size, float* dst);
+void orc_linear_q41(const float* x, int rows, int in_features,
+                    const orc_block_q41* w, int out_features, float* y);
 void orc_linear_f32_simd(const float* x, int in_features, const float* w,
                          int out_features, float* y);
 

@@ -23,7 +23,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 Q80_BYTES = 34
 Q40_BYTES = 18
-F32, Q80, Q40 = 0, 1, 2
+Q41_BYTES = 20
+F32, Q80, Q40, Q41 = 0, 1, 2, 3
 
 _fp = C.POINTER(C.c_float)
 _vp = C.c_void_p
@@ -59,9 +60,9 @@ def lib():
         L.orc_fp32_to_fp16.restype = C.c_uint16
         for n in ("orc_quantize_q80", "orc_quantize_q40"):
             getattr(L, n).argtypes = [_fp, C.c_int64, C.c_int64, _vp]
-        for n in ("orc_dequantize_q80", "orc_dequantize_q40"):
+        for n in ("orc_dequantize_q80", "orc_dequantize_q40", "orc_dequantize_q41"):
             getattr(L, n).argtypes = [_vp, C.c_int64, C.c_int64, _fp]
-        for n in ("orc_linear_q80", "orc_linear_q40"):
+        for n in ("orc_linear_q80", "orc_linear_q40", "orc_linear_q41"):
             getattr(L, n).argtypes = [_fp, C.c_int, C.c_int, _vp, C.c_int, _fp]
         L.orc_linear_f32_simd.argtypes = [_fp, C.c_int, _fp, C.c_int, _fp]
         L.orc_rmsnorm.argtypes = [_fp, _fp, C.c_int, C.c_float, _fp]
@@ -96,7 +97,7 @@ def ref():
         R.ref_get_threads.restype = C.c_int
         for n in ("ref_quantize_q80", "ref_quantize_q40"):
             getattr(R, n).argtypes = [_fp, C.c_int, C.c_int, _vp]
-        for n in ("ref_dequantize_q80", "ref_dequantize_q40"):
+        for n in ("ref_dequantize_q80", "ref_dequantize_q40", "ref_dequantize_q41"):
             getattr(R, n).argtypes = [_vp, C.c_int, C.c_int, _fp]
         R.ref_linear.argtypes = [C.c_int, _fp, C.c_int, C.c_int, _vp, C.c_int, _fp]
         R.ref_rmsnorm.argtypes = [_fp, _fp, C.c_int, C.c_float, _fp]
@@ -177,11 +178,12 @@ def dequantize(qtype: int, blocks: np.ndarray, rows: int, cols: int,
                use_ref: bool = False) -> np.ndarray:
     blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
     out = np.zeros((rows, cols), dtype=np.float32)
+    names = {Q80: "q80", Q40: "q40", Q41: "q41"}
     if use_ref:
-        fn = ref().ref_dequantize_q80 if qtype == Q80 else ref().ref_dequantize_q40
+        fn = getattr(ref(), "ref_dequantize_" + names[qtype])
         _check_ref(fn(_v(blocks), rows, cols, _f(out)))
     else:
-        fn = lib().orc_dequantize_q80 if qtype == Q80 else lib().orc_dequantize_q40
+        fn = getattr(lib(), "orc_dequantize_" + names[qtype])
         fn(_v(blocks), rows, cols, _f(out))
     return out
 
@@ -200,6 +202,8 @@ def linear(qtype: int, x: np.ndarray, w: np.ndarray, out_features: int,
         lib().orc_linear_q80(_f(x), rows, inf, _v(w), out_features, _f(y))
     elif qtype == Q40:
         lib().orc_linear_q40(_f(x), rows, inf, _v(w), out_features, _f(y))
+    elif qtype == Q41:
+        lib().orc_linear_q41(_f(x), rows, inf, _v(w), out_features, _f(y))
     else:
         assert rows == 1
         lib().orc_linear_f32_simd(_f(x), inf, w.ctypes.data_as(_fp), out_features, _f(y))

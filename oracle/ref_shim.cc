@@ -53,6 +53,10 @@ QuantizedTensor MakeQuant(int qtype, const void* p, int rows, int cols) {
     q.type = QuantType::kQ40;
     q.q4_0_data.resize(nb);
     std::memcpy(q.q4_0_data.data(), p, nb * sizeof(BlockQ40));
+  } else if (qtype == 3) {
+    q.type = QuantType::kQ41;
+    q.q4_1_data.resize(nb);
+    std::memcpy(q.q4_1_data.data(), p, nb * sizeof(BlockQ41));
   } else {
     q.type = QuantType::kF32;
     q.f32_data.resize(static_cast<size_t>(rows) * cols);
@@ -116,6 +120,15 @@ int ref_dequantize_q40(const void* blocks, int rows, int cols, float* out) {
   return Guard([&] {
     QuantizedTensor q = MakeQuant(2, blocks, rows, cols);
     Tensor t = DequantizeFromQ40(q.q4_0_data, rows <= 1 ? std::vector<int>{cols}
+                                                        : std::vector<int>{rows, cols});
+    std::memcpy(out, t.data.data(), t.data.size() * sizeof(float));
+  });
+}
+
+int ref_dequantize_q41(const void* blocks, int rows, int cols, float* out) {
+  return Guard([&] {
+    QuantizedTensor q = MakeQuant(3, blocks, rows, cols);
+    Tensor t = DequantizeFromQ41(q.q4_1_data, rows <= 1 ? std::vector<int>{cols}
                                                         : std::vector<int>{rows, cols});
     std::memcpy(out, t.data.data(), t.data.size() * sizeof(float));
   });

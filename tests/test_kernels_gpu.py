@@ -125,6 +125,48 @@ def test_linear_reference_cases(pkg, orc, cuda, qt):
         lin(x3, q3[:-34], (17, 65))
 
 
+def test_q41_linear_reference_cases(pkg, orc, S, cuda):
+    """The Q4_1 cases of tests/test_cuda_quant.cc:373-411 (pattern shapes
+    5x13 with and without bias, 32x64 with 3 input rows, 17x65 device input)
+    against the reference's LinearQ41, abs/rel tolerance 1e-3."""
+    for (o, i), rows in (((5, 13), 1), ((32, 64), 3), ((17, 65), 3), ((896, 896), 1)):
+        blocks, _ = S.gemv_case(o, i, 300 + o, S.Q41)
+        x = pattern((rows, i) if rows > 1 else (i,), 0.029, -0.06)
+        ref = orc.linear(orc.Q41, x, blocks, o, use_ref=True)
+        assert_close(pkg.CudaQ41Linear(x, blocks, (o, i)), ref.reshape(-1, o).squeeze(0)
+                     if rows == 1 else ref, f"q4_1 {o}x{i}")
+    b = pattern((5,), 0.013, -0.02)
+    blocks, _ = S.gemv_case(5, 13, 305, S.Q41)
+    x = pattern((13,), 0.071, 0.03)
+    assert_close(pkg.CudaQ41Linear(x, blocks, (5, 13), bias=b),
+                 orc.linear(orc.Q41, x, blocks, 5, use_ref=True)[0] + b, "q4_1 bias")
+    dev = pkg.CudaQ41LinearDeviceInput(cuda.zeros(3, 65, device="cuda"),
+                                       cuda.from_numpy(S.gemv_case(17, 65, 1, S.Q41)[0]).cuda(),
+                                       17 * 3, (17, 65))
+    assert float(dev.abs().max()) == 0.0
+    with pytest.raises(RuntimeError, match="CudaQ41Linear: block count mismatch"):
+        pkg.CudaQ41Linear(x, blocks[:-20], (5, 13))
+
+
+@pytest.mark.parametrize("shape", [(64, 13), (896, 896), (17, 65), (151936, 896)])
+def test_f32_linear_matches_reference(pkg, orc, cuda, shape):
+    """F32-weight Linear (the reference's cuBLAS path, tests/test_cuda_matmul.cc:
+    112-163) against the reference's threaded-simd LinearDispatch, abs/rel
+    tolerance 1e-3; 1 and 3 input rows, bias on one case; the 151936 x 896
+    shape is the reference's tied F32 lm_head."""
+    o, i = shape
+    rng = np.random.default_rng(o + i)
+    w = (rng.standard_normal((o, i)) * 0.02).astype(np.float32)
+    x = rng.standard_normal(i).astype(np.float32)
+    ref = orc.linear(orc.F32, x, w, o, use_ref=True)[0]
+    assert_close(pkg.CudaLinear(x, w), ref, f"f32 {o}x{i}")
+    if o <= 896:
+        x3 = rng.standard_normal((3, i)).astype(np.float32)
+        ref3 = np.stack([orc.linear(orc.F32, r, w, o, use_ref=True)[0] for r in x3])
+        bias = rng.standard_normal(o).astype(np.float32)
+        assert_close(pkg.CudaLinear(x3, w, bias=bias), ref3 + bias, f"f32 {o}x{i} x3 bias")
+
+
 def gemv_cases():
     import importlib.util
     spec = importlib.util.spec_from_file_location("make_golden", golden_path("make_golden.py"))

@@ -218,3 +218,20 @@ def test_full_model_golden_is_consistent():
     assert len(d["prompt"]) == 32 and len(d["greedy_tokens"]) == 64
     assert all(t[0][0] == tok for t, tok in zip(d["top5"], d["greedy_tokens"]))
     assert min(d["top1_top2_margin"]) > 0
+
+
+@needs_ref
+@pytest.mark.parametrize("shape", [(5, 13), (32, 64), (17, 65), (64, 896)])
+def test_q41_dequant_and_linear_match_reference(orc, S, shape):
+    """Q4_1 (20-byte blocks, d * q + m): the restatement's dequantization and
+    Linear equal the reference's DequantizeFromQ41 / LinearQ41
+    (src/quant.cc:192-235, 256-262, 362-366) bit for bit."""
+    o, i = shape
+    blocks, _ = S.gemv_case(o, i, 91 + o, S.Q41)
+    assert np.array_equal(bits(orc.dequantize(orc.Q41, blocks, o, i)),
+                          bits(orc.dequantize(orc.Q41, blocks, o, i, use_ref=True)))
+    rng = np.random.default_rng(o * i)
+    for rows in (1, 3):
+        x = rng.standard_normal((rows, i)).astype(np.float32)
+        assert np.array_equal(bits(orc.linear(orc.Q41, x, blocks, o)),
+                              bits(orc.linear(orc.Q41, x, blocks, o, use_ref=True)))
