@@ -391,6 +391,31 @@ class Model:
     def finalize(self) -> None:
         check(lib().dqmk_model_finalize(self.h))
 
+    @staticmethod
+    def gguf_config(path: str) -> dict:
+        """The model configuration a GGUF file's metadata gives (BuildConfig,
+        src/gguf_loader.cc:202-273), without touching a device."""
+        c = ModelConfig()
+        check(lib().dqmk_gguf_read_config(path.encode(), C.byref(c)))
+        return {"vocab": c.vocab_size, "dim": c.dim, "hidden": c.hidden_dim,
+                "n_layers": c.n_layers, "n_heads": c.n_heads, "n_kv_heads": c.n_kv_heads,
+                "head_dim": c.head_dim, "max_seq_len": c.max_seq_len,
+                "rope_theta": c.rope_theta, "eps": c.rms_norm_eps, "rope_neox": c.rope_neox}
+
+    @classmethod
+    def from_gguf(cls, path: str, max_seq_len: int = 0, device: int = 0) -> "Model":
+        """LoadGgufModel + UploadModelWeightsToCuda: a finalized model from a
+        GGUF v3 file (quantized tensors kept as stored)."""
+        cfg = cls.gguf_config(path)
+        m = cls.__new__(cls)
+        m.cfg = {k: cfg[k] for k in ("vocab", "dim", "hidden", "n_layers", "n_heads",
+                                     "n_kv_heads", "rope_theta", "eps")}
+        m.max_seq_len = max_seq_len or cfg["max_seq_len"]
+        h = C.c_void_p()
+        check(lib().dqmk_model_load_gguf(path.encode(), int(max_seq_len), device, C.byref(h)))
+        m.h = h
+        return m
+
     @classmethod
     def from_synth(cls, w: "synth.SynthModel", max_seq_len: int, device: int = 0,
                    tp: Optional[tuple] = None) -> "Model":

@@ -19,12 +19,13 @@ which is what GGUF files carry; the forward pass reads any valid Q4_0 block.
 """
 from __future__ import annotations
 
+import struct
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional
 
 import numpy as np
 
-Q80, Q40, Q41 = 1, 2, 3
+F32, Q80, Q40, Q41 = 0, 1, 2, 3
 BLOCK_BYTES = {Q80: 34, Q40: 18, Q41: 20}
 
 QWEN2_0_5B = dict(name="qwen2-0.5b", vocab=151936, dim=896, hidden=4864, n_layers=24,
@@ -167,3 +168,92 @@ def gemv_case(out_features: int, in_features: int, seed: int, qtype: int = Q80):
         blocks = np.concatenate([d, qs], axis=1)
     x = g.standard_normal(in_features, dtype=np.float32)
     return np.ascontiguousarray(blocks.reshape(-1)), x
+
+
+# ---------------------------------------------------------------- GGUF files
+# GGUF version 3 (the llama.cpp model container, the input format of every
+# workload here): header "GGUF", u32 version, u64 tensor count, u64 metadata
+# count; metadata as (string key, u32 type, value); tensor infos as (string
+# name, u32 n_dims, u64 dims innermost first, u32 ggml type, u64 offset into
+# the data section); the data section starts at the next multiple of
+# general.alignment (32 here).  Strings are u64 length + bytes, little endian.
+GGUF_U32, GGUF_F32, GGUF_STRING, GGUF_ARRAY = 4, 6, 8, 9
+GGML_TYPE = {F32: 0, Q40: 2, Q41: 3, Q80: 8}
+
+
+def _gguf_str(s: str) -> bytes:
+    b = s.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def gguf_tensors(w: SynthModel):
+    """(GGUF name, ggml qtype, data bytes, [rows, cols] or [n]) of a model, in
+    the llama.cpp naming the reference's loader maps (src/gguf_loader.cc:21-59)."""
+    c = w.cfg
+    hd = c["dim"] // c["n_heads"]
+    qd, kvd = c["n_heads"] * hd, c["n_kv_heads"] * hd
+    out = [("token_embd.weight", w.qtype, w.token_embd, [c["vocab"], c["dim"]]),
+           ("output_norm.weight", F32, w.final_norm, [c["dim"]])]
+    if w.lm_head is not None:
+        out.append(("output.weight", w.qtype, w.lm_head, [c["vocab"], c["dim"]]))
+    for i, L in enumerate(w.layers):
+        p = f"blk.{i}."
+        out += [(p + "attn_norm.weight", F32, L.attention_norm, [c["dim"]]),
+                (p + "attn_q.weight", w.qtype, L.wq, [qd, c["dim"]]),
+                (p + "attn_k.weight", w.qtype, L.wk, [kvd, c["dim"]]),
+                (p + "attn_v.weight", w.qtype, L.wv, [kvd, c["dim"]])]
+        for nm, b, n in (("attn_q.bias", L.bq, qd), ("attn_k.bias", L.bk, kvd),
+                         ("attn_v.bias", L.bv, kvd)):
+            if b is not None:
+                out.append((p + nm, F32, b, [n]))
+        out += [(p + "attn_output.weight", w.qtype, L.wo, [c["dim"], qd]),
+                (p + "ffn_norm.weight", F32, L.ffn_norm, [c["dim"]]),
+                (p + "ffn_gate.weight", w.qtype, L.w_gate, [c["hidden"], c["dim"]]),
+                (p + "ffn_up.weight", w.qtype, L.w_up, [c["hidden"], c["dim"]]),
+                (p + "ffn_down.weight", w.qtype, L.w_down, [c["dim"], c["hidden"]])]
+    return out
+
+
+def write_gguf(path: str, w: SynthModel, context_length: int, alignment: int = 32) -> None:
+    """Write a model as a GGUF v3 file with qwen2 metadata: block count,
+    widths, head counts, context length, RoPE base, RMSNorm epsilon and a
+    tokenizer.ggml.tokens array whose length is the vocabulary."""
+    c = w.cfg
+    kv = [("general.architecture", GGUF_STRING, "qwen2"),
+          ("general.alignment", GGUF_U32, alignment),
+          ("qwen2.block_count", GGUF_U32, c["n_layers"]),
+          ("qwen2.context_length", GGUF_U32, context_length),
+          ("qwen2.embedding_length", GGUF_U32, c["dim"]),
+          ("qwen2.feed_forward_length", GGUF_U32, c["hidden"]),
+          ("qwen2.attention.head_count", GGUF_U32, c["n_heads"]),
+          ("qwen2.attention.head_count_kv", GGUF_U32, c["n_kv_heads"]),
+          ("qwen2.rope.freq_base", GGUF_F32, c["rope_theta"]),
+          ("qwen2.attention.layer_norm_rms_epsilon", GGUF_F32, c["eps"])]
+    tensors = gguf_tensors(w)
+    head = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kv) + 1))
+    for key, t, v in kv:
+        head += _gguf_str(key) + struct.pack("<I", t)
+        if t == GGUF_STRING:
+            head += _gguf_str(v)
+        elif t == GGUF_U32:
+            head += struct.pack("<I", int(v))
+        else:
+            head += struct.pack("<f", float(v))
+    head += _gguf_str("tokenizer.ggml.tokens") + struct.pack("<IIQ", GGUF_ARRAY, GGUF_STRING,
+                                                            c["vocab"])
+    head += b"".join(_gguf_str(f"tok_{i}") for i in range(c["vocab"]))
+    offset, blobs = 0, []
+    for name, qt, data, shape in tensors:
+        raw = np.ascontiguousarray(data).view(np.uint8).tobytes()
+        dims = list(reversed(shape))  # innermost first: [in, out]
+        head += _gguf_str(name) + struct.pack("<I", len(dims))
+        head += b"".join(struct.pack("<Q", d) for d in dims)
+        head += struct.pack("<IQ", GGML_TYPE[qt], offset)
+        pad = (-len(raw)) % alignment
+        blobs.append(raw + b"\0" * pad)
+        offset += len(raw) + pad
+    head += b"\0" * ((-len(head)) % alignment)
+    with open(path, "wb") as f:
+        f.write(head)
+        for b in blobs:
+            f.write(b)

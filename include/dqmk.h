@@ -334,6 +334,18 @@ int dqmk_model_upload(dqmk_model* model, const char* name, int qtype, const void
 /* Validates that every tensor is present and builds the fused layouts. */
 int dqmk_model_finalize(dqmk_model* model);
 
+/* GGUF v3 model files (LoadGgufModel, src/gguf_loader.cc:279-364, with the
+ * configuration rules of BuildConfig, :202-273).  dqmk_gguf_read_config
+ * parses the metadata only (no device work).  dqmk_model_load_gguf creates,
+ * uploads and finalizes a model on device_id: quantized tensors (Q8_0,
+ * Q4_0) are uploaded as stored -- the token embedding stays quantized and a
+ * file without output.weight gets the tied lm_head over those blocks, where
+ * the reference expands both to F32 (:313-326, 356-360) -- and F32 norms and
+ * biases as F32.  max_seq_len > 0 overrides the file's context length.
+ * Other ggml types fail with DQMK_ERR_UNSUPPORTED. */
+int dqmk_gguf_read_config(const char* path, dqmk_model_config* out);
+int dqmk_model_load_gguf(const char* path, int max_seq_len, int device_id, dqmk_model** out);
+
 /* Tensor parallelism (Megatron split; no reference counterpart -- the
  * reference runs one device).  A rank's share of the model: */
 typedef struct dqmk_tp_plan {

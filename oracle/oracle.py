@@ -455,3 +455,55 @@ class RefModel:
         out = np.zeros(max(n, 1), np.int32)
         ref().ref_context_history(self.h, out.ctypes.data_as(_ip), n)
         return out[:n]
+
+
+_GGUF_CHILD = r"""
+import ctypes as C, struct, sys
+path, out, threads = sys.argv[1], sys.argv[2], int(sys.argv[3])
+toks = [int(t) for t in sys.argv[4].split(",")]
+R = C.CDLL(sys.argv[5])
+R.ref_last_error.restype = C.c_char_p
+R.ref_set_threads.argtypes = [C.c_int]
+R.ref_model_load_gguf.argtypes = [C.c_char_p, C.c_void_p]
+R.ref_model_load_gguf.restype = C.c_void_p
+R.ref_forward_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+if threads:
+    R.ref_set_threads(threads)
+cfg = (C.c_int * 8)()
+h = R.ref_model_load_gguf(path.encode(), cfg)
+if not h:
+    sys.stderr.write(R.ref_last_error().decode())
+    sys.exit(2)
+arr = (C.c_int * len(toks))(*toks)
+logits = (C.c_float * cfg[0])()
+if R.ref_forward_batch(h, arr, len(toks), 0, logits):
+    sys.stderr.write(R.ref_last_error().decode())
+    sys.exit(3)
+with open(out, "wb") as f:
+    f.write(struct.pack("<8i", *cfg))
+    f.write(bytes(logits))
+"""
+
+
+def ref_gguf_forward(path: str, tokens, threads: int = 0):
+    """The reference's own LoadGgufModel (src/gguf_loader.cc:279-364) over a
+    GGUF file, then its ForwardBatch over `tokens` from position 0: returns
+    (config dict, last-token logits).  Runs in a child interpreter that loads
+    only ctypes: inside a process that has imported numpy, the reference's
+    reader faulted in its console output (std::cout), while plain hosts read
+    the same files cleanly."""
+    import subprocess
+    import sys
+    import tempfile
+    with tempfile.NamedTemporaryFile(suffix=".bin") as tf:
+        r = subprocess.run([sys.executable, "-c", _GGUF_CHILD, path, tf.name, str(threads),
+                            ",".join(str(int(t)) for t in tokens),
+                            os.path.join(HERE, "_ref", "libdqmref.so")],
+                           capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("reference GGUF load failed: " + r.stderr[-2000:])
+        raw = open(tf.name, "rb").read()
+    cfg = np.frombuffer(raw[:32], np.int32)
+    keys = ("vocab", "dim", "hidden", "n_layers", "n_heads", "n_kv_heads", "max_seq", "neox")
+    return dict(zip(keys, (int(v) for v in cfg))), np.frombuffer(raw[32:], np.float32).copy()
+

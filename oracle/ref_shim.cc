@@ -16,12 +16,14 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
 #include "dqm_llama/batch.h"
 #include "dqm_llama/context.h"
 #include "dqm_llama/forward.h"
+#include "dqm_llama/gguf_loader.h"
 #include "dqm_llama/matmul_dispatch.h"
 #include "dqm_llama/model.h"
 #include "dqm_llama/ops.h"
@@ -272,6 +274,30 @@ int ref_model_finish(void* h) {
     s->model.loaded = true;
     s->ctx = std::make_unique<MiniLlamaContext>(&s->model);
   });
+}
+
+// The reference's own GGUF path (src/gguf_loader.cc:279-364, LoadGgufModel):
+// returns a session over the loaded model, or NULL with ref_last_error set.
+// cfg_out (optional): vocab, dim, hidden, layers, heads, kv heads, max_seq,
+// rope neox.
+void* ref_model_load_gguf(const char* path, int* cfg_out) {
+  auto* s = new RefSession();
+  int rc = Guard([&] {
+    s->model = LoadGgufModel(path);
+    if (!s->model.loaded) throw std::runtime_error("LoadGgufModel: " + s->model.load_error);
+    const ModelConfig& c = s->model.config;
+    if (cfg_out) {
+      const int v[8] = {c.vocab_size, c.dim, c.hidden_dim, c.n_layers, c.n_heads,
+                        c.n_kv_heads, c.max_seq_len, c.rope_type == RopeType::kNeoX ? 1 : 0};
+      std::memcpy(cfg_out, v, sizeof(v));
+    }
+    s->ctx = std::make_unique<MiniLlamaContext>(&s->model);
+  });
+  if (rc != 0) {
+    delete s;
+    return nullptr;
+  }
+  return s;
 }
 
 // Fresh context (empty KV cache, pos 0, empty history).

@@ -167,3 +167,33 @@ def test_qwen2_0_5b_q8_0_greedy_64_matches_reference(pkg, S, cuda):
     assert tokens == g["greedy_tokens"], (
         f"first divergence at {next(i for i, (a, b) in enumerate(zip(tokens, g['greedy_tokens'])) if a != b)}"
         f", reference min margin {min(g['top1_top2_margin']):.3e}")
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_gguf_model_matches_reference_gguf_load(pkg, orc, S, cuda, tmp_path, qt):
+    """A model loaded from a GGUF v3 file by the library (dqmk_model_load_gguf)
+    against the reference's own LoadGgufModel of the same file: the prompt's
+    logits within 1e-3 x logit range, and the library keeps the token
+    embedding quantized (memory = block bytes + F32 norms and biases, where the
+    reference holds the embedding -- and a tied lm_head -- as F32)."""
+    w = S.make_model(dict(S.QWEN2_MINI, tied=qt == 1), qt, 41,
+                     quantize_q80=lambda a: orc.quantize_q80(a, True))
+    path = str(tmp_path / "mini.gguf")
+    S.write_gguf(path, w, context_length=64)
+    c = w.cfg
+    toks = S.prompt_tokens(c["vocab"], 9, 5)
+    _, ref = orc.ref_gguf_forward(path, toks)
+    model = pkg.Model.from_gguf(path)
+    ctx = pkg.Context(model)
+    got = ctx.ForwardBatch(toks.tolist(), 0)
+    check_logits(got, ref, f"gguf q{qt}")
+    hd = c["dim"] // c["n_heads"]
+    blocks = w.token_embd.nbytes + (0 if w.lm_head is None else w.lm_head.nbytes) + sum(
+        getattr(Ly, n).nbytes for Ly in w.layers
+        for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"))
+    L = c["n_layers"]
+    f32 = 4 * (c["dim"] + L * (2 * c["dim"] + c["n_heads"] * hd + 2 * c["n_kv_heads"] * hd))
+    planes = model.memory_bytes() - blocks - f32  # the batched prefill's side tables
+    assert planes >= 0 and planes % 4 == 0
+    ctx.close()
+    model.close()

@@ -235,3 +235,48 @@ def test_q41_dequant_and_linear_match_reference(orc, S, shape):
         x = rng.standard_normal((rows, i)).astype(np.float32)
         assert np.array_equal(bits(orc.linear(orc.Q41, x, blocks, o)),
                               bits(orc.linear(orc.Q41, x, blocks, o, use_ref=True)))
+
+
+@needs_ref
+@pytest.mark.parametrize("qt", [1, 2])
+def test_gguf_writer_read_by_reference(orc, S, tmp_path, qt):
+    """The synthetic GGUF v3 writer (synth.write_gguf) produces files the
+    reference's own reader and LoadGgufModel accept (src/gguf.cc,
+    src/gguf_loader.cc:279-364): the configuration comes back from the
+    metadata and the loaded model's ForwardBatch logits equal, bit for bit,
+    those of the same weights handed to the reference directly."""
+    w = S.make_model(dict(S.QWEN2_MINI, tied=qt == 1), qt, 31,
+                     quantize_q80=lambda a: orc.quantize_q80(a, True))
+    path = str(tmp_path / "mini.gguf")
+    S.write_gguf(path, w, context_length=64)
+    c = w.cfg
+    toks = S.prompt_tokens(c["vocab"], 7, 3)
+    cfg, logits = orc.ref_gguf_forward(path, toks)
+    assert cfg == {"vocab": c["vocab"], "dim": c["dim"], "hidden": c["hidden"],
+                   "n_layers": c["n_layers"], "n_heads": c["n_heads"],
+                   "n_kv_heads": c["n_kv_heads"], "max_seq": 64, "neox": 1}
+    direct = orc.RefModel(w, 64)
+    assert np.array_equal(bits(logits), bits(direct.forward_batch(toks, 0)))
+
+
+@pytest.mark.parametrize("qt", [1, 2])
+def test_gguf_config_read_by_library(pkg, orc, S, tmp_path, qt):
+    """The library's own GGUF reader (dqmk_gguf_read_config, no device work)
+    builds the configuration the reference's BuildConfig does from the same
+    file: qwen2 => NeoX RoPE, vocabulary = tokenizer.ggml.tokens length,
+    head_dim = dim / n_heads."""
+    w = S.make_model(dict(S.QWEN2_MINI, tied=qt == 1), qt, 31,
+                     quantize_q80=lambda a: orc.quantize_q80(a))
+    path = str(tmp_path / "mini.gguf")
+    S.write_gguf(path, w, context_length=96)
+    c = w.cfg
+    got = pkg.Model.gguf_config(path)
+    assert got == {"vocab": c["vocab"], "dim": c["dim"], "hidden": c["hidden"],
+                   "n_layers": c["n_layers"], "n_heads": c["n_heads"],
+                   "n_kv_heads": c["n_kv_heads"], "head_dim": c["dim"] // c["n_heads"],
+                   "max_seq_len": 96, "rope_theta": np.float32(c["rope_theta"]),
+                   "eps": np.float32(c["eps"]), "rope_neox": 1}
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGUF\x02\x00\x00\x00" + b"\x00" * 16)
+    with pytest.raises(RuntimeError, match="LoadGgufModel: GGUF version 3 expected"):
+        pkg.Model.gguf_config(str(bad))
