@@ -514,6 +514,18 @@ class Context:
                                        toks.size, out.ctypes.data_as(C.POINTER(C.c_float))))
         return out
 
+    def ForwardBatchReuse(self, tokens: Sequence[int]):
+        """A new prompt on this context, reusing the longest common prefix
+        of its token history (dqmk_forward_batch_prefix); returns (logits,
+        number of prompt tokens whose KV entries were kept)."""
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        out = np.empty(self.vocab, np.float32)
+        reused = C.c_int(0)
+        check(lib().dqmk_forward_batch_prefix(self.h, toks.ctypes.data_as(C.POINTER(C.c_int)),
+                                              toks.size, out.ctypes.data_as(C.POINTER(C.c_float)),
+                                              C.byref(reused)))
+        return out, reused.value
+
     def decode_greedy(self, token: int, pos: int, n_steps: int) -> np.ndarray:
         out = np.zeros(n_steps, np.int32)
         check(lib().dqmk_decode_greedy(self.h, int(token), int(pos), int(n_steps),

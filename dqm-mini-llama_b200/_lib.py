@@ -68,6 +68,7 @@ SIGNATURES = {
     "dqmk_device_error": ([_i], _i),
     "dqmk_gemv_packed_withhold_tile": ([_i, _vp, _i, _vp, _i, _vp, _i, _vp], _i),
     "dqmk_context_withhold_lm_head": ([_vp, _i], _i),
+    "dqmk_forward_batch_prefix": ([_vp, _vp, _i, _vp, _vp], _i),
     "dqmk_gguf_read_config": ([C.c_char_p, _vp], _i),
     "dqmk_model_load_gguf": ([C.c_char_p, _i, _i, _vp], _i),
     "dqmk_gemv_packed_chained": ([_i, _vp, _i, _vp, _i, _vp, _f, _i, _vp, _vp], _i),

@@ -1243,6 +1243,31 @@ extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int*
   return check_device_error(api, x);
 }
 
+// Prefix reuse for a new prompt on a context that already holds a sequence
+// (the chat path's reuse, src/main.cc:887-913, with the context's own token
+// history as the source of truth): p = the longest common prefix of the
+// history and the prompt.  p == 0 or p == n (nothing left to compute logits
+// from) recomputes the whole prompt from position 0; otherwise the history
+// is cut to p tokens, pos rolls back to p - 1, and only tokens[p..n) run,
+// at positions p.. -- one batched prefill when the model has one.  KV rows
+// past the kept prefix are simply overwritten as positions advance;
+// attention never reads beyond the current position.
+extern "C" int dqmk_forward_batch_prefix(dqmk_context* x, const int* tokens, int n,
+                                         float* logits, int* reused) {
+  const char* api = "ForwardBatch";
+  if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + ": null context");
+  if (n <= 0 || !tokens) return fail(DQMK_ERR_INVALID, "ForwardBatch: empty token");
+  size_t p = 0;
+  while (p < x->history.size() && p < (size_t)n && x->history[p] == tokens[p]) ++p;
+  if (p >= (size_t)n) p = 0;
+  x->history.resize(p);
+  x->pos = p ? (int)p - 1 : 0;
+  std::vector<int> positions(n - p);
+  for (size_t i = 0; i < positions.size(); ++i) positions[i] = (int)(p + i);
+  if (reused) *reused = (int)p;
+  return dqmk_forward_batch(x, tokens + p, positions.data(), (int)positions.size(), logits);
+}
+
 extern "C" int dqmk_decode_enqueue(dqmk_context* x, int token, int pos, int n_steps) {
   const char* api = "DecodeGreedy";
   if (!x) return fail(DQMK_ERR_INVALID, std::string(api) + ": null context");

@@ -418,6 +418,17 @@ int dqmk_forward_token(dqmk_context* ctx, int token, int pos, float* logits);
 int dqmk_forward_batch(dqmk_context* ctx, const int* tokens, const int* positions, int n,
                        float* logits);
 
+/* ForwardBatch with prefix reuse, the reference chat loop's step before its
+ * prefill (src/main.cc:887-913): the longest common prefix p of the
+ * context's token history and `tokens` is kept (history cut to p tokens, pos
+ * rolled back to p - 1) and only tokens[p..n) run, from position p, as a
+ * batched prefill.  p == 0, or p == n (no token left to give logits), runs
+ * the whole prompt from position 0.  *reused (if non-NULL) receives p.  The
+ * reference intersects this with its RadixTree registry of cached prompts;
+ * here the context's own history is the registry.  Synchronous. */
+int dqmk_forward_batch_prefix(dqmk_context* ctx, const int* tokens, int n, float* logits,
+                              int* reused);
+
 /* Greedy decode on the device: feeds `token` at `pos`, then n_steps-1 more
  * tokens chosen by the device argmax, replaying the captured decode graph
  * with no host round trip per step.  tokens_out[i] receives the argmax after

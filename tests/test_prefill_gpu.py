@@ -179,3 +179,38 @@ def test_qwen2_0_5b_q8_0_prefill_602_whole_logits(pkg, S, cuda):
     ctx.close()
     model.close()
 
+
+
+def test_prefix_reuse_matches_full_prefill(pkg, S, minis, cuda):
+    """Prefix reuse (dqmk_forward_batch_prefix, the reference chat loop's
+    reuse at src/main.cc:887-913): after a 300-token prompt and 6 greedy
+    tokens, a second prompt that shares the first 200 tokens keeps those 200
+    positions and batched-prefills only the rest; its logits and next greedy
+    tokens equal a fresh context's full prefill of the second prompt (logits
+    within 1e-3 x range).  The same prompt again, or one sharing nothing,
+    recomputes from position 0."""
+    w = minis[pkg.Q80]
+    vocab = w.cfg["vocab"]
+    p1 = S.prompt_tokens(vocab, 300, 21).tolist()
+    p2 = p1[:200] + S.prompt_tokens(vocab, 150, 22).tolist()
+    model = pkg.Model.from_synth(w, max_seq_len=512)
+    ctx = pkg.Context(model)
+    first = int(np.argmax(ctx.ForwardBatch(p1, 0)))
+    ctx.decode_greedy(first, 300, 6)
+    got, reused = ctx.ForwardBatchReuse(p2)
+    assert reused == 200
+    assert ctx.pos == len(p2) - 1
+    fresh = pkg.Context(model)
+    ref = fresh.ForwardBatch(p2, 0)
+    check_logits(got, ref, "prefix reuse")
+    nxt = int(np.argmax(got))
+    assert ctx.decode_greedy(nxt, len(p2), 4).tolist() == fresh.decode_greedy(nxt, len(p2), 4).tolist()
+    again, reused = ctx.ForwardBatchReuse(p2)
+    assert reused == 0
+    check_logits(again, ref, "same prompt, recomputed")
+    other = S.prompt_tokens(vocab, 40, 23).tolist()
+    _, reused = ctx.ForwardBatchReuse(other)
+    assert reused == 0 and ctx.pos == 39
+    ctx.close()
+    fresh.close()
+    model.close()
