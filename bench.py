@@ -229,6 +229,36 @@ def time_gemv(pkg, torch, w):
             "algorithmic_bytes": LM_HEAD_BYTES, "traffic": profile_traffic()}
 
 
+def time_dominant(pkg, torch, ctx):
+    """The decode step's largest kernel by share of the step (the fused gate/up
+    GEMV: RMSNorm of x, 9728 interleaved gate/up rows x 896 Q8_0, SwiGLU
+    epilogue) in its in-graph form: launched with programmatic dependent launch
+    back to back, each launch on the next of rotating weight copies totalling
+    > 8 x L2, captured in a CUDA graph; CUDA events around the replay."""
+    rows, k = 9728, 896
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(9)
+    nb = rows * k // 32
+    one = torch.cat([(torch.rand(nb, device="cuda", generator=gen) * 0.01 + 1e-4).half()
+                     .view(torch.uint8).view(nb, 2),
+                     torch.randint(0, 256, (nb, 32), dtype=torch.uint8, device="cuda",
+                                   generator=gen)], dim=1).contiguous()
+    copies = -(-ROTATE_BYTES // one.numel())
+    packs = [pkg.pack_weight(pkg.Q80, one, rows, k) for _ in range(copies)]
+    x = torch.randn(k, device="cuda")
+    nw = torch.ones(k, device="cuda")
+    y = torch.empty(rows // 2, device="cuda")
+    dt = graph_time(torch, lambda i: pkg.gemv_packed_chained(pkg.Q80, x, packs[i % copies], rows,
+                                                               y, norm=nw, swiglu=True), copies)
+    nbytes = rows * k // 32 * 34 + 4 * k * 2 + 4 * rows // 2
+    del packs
+    torch.cuda.empty_cache()
+    return {"kernel": "gemv_kernel<Q8_0> gate/up 9728x896 (RMSNorm + SwiGLU), chained",
+            "achieved": round(nbytes / dt / 1e9, 1), "algorithmic_bytes": nbytes,
+            "us_per_launch": round(dt * 1e6, 3), "launches": copies,
+            "traffic": profile_traffic("gemv_q8_0_layer_projections.md", "gate_up_dram_bytes:")}
+
+
 def gemv_sweep(pkg, torch, S):
     """Configuration 2 (Q8_0 GEMV sweep): per shape, rotating weight copies
     totalling more than 8 x L2 (so every launch reads its weight from HBM),

@@ -76,6 +76,9 @@ SIGNATURES = {
     "dqmk_rmsnorm": ([_vp, _vp, _i, _f, _vp, _vp], _i),
     "dqmk_silu_mul": ([_vp, _vp, _i, _vp, _vp], _i),
     "dqmk_add": ([_vp, _vp, _i, _vp, _vp], _i),
+    "dqmk_silu": ([_vp, _i, _vp, _vp], _i),
+    "dqmk_mul": ([_vp, _vp, _i, _vp, _vp], _i),
+    "dqmk_softmax": ([_vp, _i, _vp, _vp], _i),
     "dqmk_rope": ([_vp, _vp, _i, _i, _i, _i, _f, _i, _vp], _i),
     "dqmk_embedding_lookup": ([_vp, _i, _i, _i, _vp, _vp], _i),
     "dqmk_embedding_lookup_blocks": ([_i, _vp, _i, _i, _i, _vp, _vp], _i),

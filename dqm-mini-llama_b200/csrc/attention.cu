@@ -112,6 +112,123 @@ __global__ void __launch_bounds__(256) attention_hd_head_kernel(const AttnArgs a
   attention_hd_body<HD, 256>(b, chunk_cap, kvh, 0, 1, sm);
 }
 
+// Short caches (max_seq <= kShortMax, the whole cache one split): one CTA
+// per query head, every global load issued at once right after the
+// dependency wait -- the thread's 16 dims of q, the K rows of its score
+// positions and the V rows of its P.V positions -- so the kernel pays one L2
+// round trip instead of three (q, then K, then V).  Scores: HD/16 threads
+// per position; softmax statistics computed redundantly by every warp from
+// the scores in shared memory (no extra barrier); P.V: thread (d4, group)
+// owns 4 dims and every NG-th position; the NG group sums are added in
+// shared memory.  Same arithmetic per term as attention_hd_body (fp32,
+// expf(s - m), divide by l), different summation order.
+constexpr int kShortMax = 128;
+
+template <int HD>
+__global__ void __launch_bounds__(256) attention_short_kernel(const AttnArgs a) {
+  constexpr int NT = 256;
+  constexpr int TPP = HD / 16;          // threads per score position (16 dims each)
+  constexpr int PPASS = NT / TPP;       // positions per score pass
+  constexpr int NPASS = kShortMax / PPASS;
+  constexpr int D4 = HD / 4;            // float4 columns of a row
+  constexpr int NG = NT / D4;           // position groups in P.V
+  constexpr int NPV = kShortMax / NG;   // positions per thread in P.V
+  __shared__ float ss[kShortMax];
+  __shared__ float4 red[NG][D4];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int kvh = blockIdx.x, G = a.n_heads / a.n_kv_heads;
+  const int head = kvh * G + blockIdx.z;
+  const int pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+  const int T = pos + 1;
+  const size_t row_stride = (size_t)a.n_kv_heads * HD;
+  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
+  const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
+  const int part = tid % TPP, p0 = tid / TPP;
+  const int d4 = tid % D4, grp = tid / D4;
+  // ---- every load in flight together
+  float4 qv[4], kr[NPASS][4], vr[NPV];
+  const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)head * HD) + part * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qv[i] = __ldcg(q4 + i);
+#pragma unroll
+  for (int u = 0; u < NPASS; ++u) {
+    const int t = p0 + u * PPASS;
+    const float4* kp = reinterpret_cast<const float4*>(kbase + (size_t)t * row_stride) + part * 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      kr[u][i] = t < T ? __ldcg(kp + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < NPV; ++j) {
+    const int t = grp + j * NG;
+    vr[j] = t < T ? __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)t * row_stride) + d4)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // ---- scores
+  const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
+#pragma unroll
+  for (int u = 0; u < NPASS; ++u) {
+    float d = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      d = fmaf(qv[i].x, kr[u][i].x, d);
+      d = fmaf(qv[i].y, kr[u][i].y, d);
+      d = fmaf(qv[i].z, kr[u][i].z, d);
+      d = fmaf(qv[i].w, kr[u][i].w, d);
+    }
+#pragma unroll
+    for (int o = TPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    const int t = p0 + u * PPASS;
+    if (part == 0 && t < T) ss[t] = __fmul_rn(d, scale);
+  }
+  __syncthreads();
+  // ---- softmax statistics (every warp alike)
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < kShortMax / 32; ++k) {
+    const int t = lane + 32 * k;
+    if (t < T) m = fmaxf(m, ss[t]);
+  }
+  m = warp_max(m);
+  float l = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kShortMax / 32; ++k) {
+    const int t = lane + 32 * k;
+    if (t < T) l += expf(ss[t] - m);
+  }
+  l = warp_sum(l);
+  // ---- P.V over this thread's positions
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < NPV; ++j) {
+    const int t = grp + j * NG;
+    if (t < T) {
+      const float pr = expf(ss[t] - m);
+      acc.x = fmaf(pr, vr[j].x, acc.x);
+      acc.y = fmaf(pr, vr[j].y, acc.y);
+      acc.z = fmaf(pr, vr[j].z, acc.z);
+      acc.w = fmaf(pr, vr[j].w, acc.w);
+    }
+  }
+  red[grp][d4] = acc;
+  __syncthreads();
+  if (tid < D4) {
+    float4 o = red[0][tid];
+#pragma unroll
+    for (int g2 = 1; g2 < NG; ++g2) {
+      const float4 x = red[g2][tid];
+      o.x += x.x;
+      o.y += x.y;
+      o.z += x.z;
+      o.w += x.w;
+    }
+    reinterpret_cast<float4*>(a.out + (size_t)head * HD)[tid] =
+        make_float4(__fdiv_rn(o.x, l), __fdiv_rn(o.y, l), __fdiv_rn(o.z, l), __fdiv_rn(o.w, l));
+  }
+}
+
 // Any head_dim that is a multiple of 4 up to 256: one thread per position.
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, int chunk_cap) {
   extern __shared__ float sm[];
@@ -296,6 +413,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
   if (e != cudaSuccess) return e;
   const dim3 grid(a.n_kv_heads, a.max_splits);
   const int G = a.n_kv_heads > 0 ? a.n_heads / a.n_kv_heads : 1;
+  if (hd_kernel && a.max_splits == 1 && a.max_seq <= kShortMax) {
+    const dim3 hgrid(a.n_kv_heads, 1, G);
+    if (a.head_dim == 64)
+      return launch(attention_short_kernel<64>, hgrid, dim3(256), 0, stream, pdl, a);
+    return launch(attention_short_kernel<128>, hgrid, dim3(256), 0, stream, pdl, a);
+  }
   if (hd_kernel && a.max_splits == 1 && G > 1) {
     const dim3 hgrid(a.n_kv_heads, 1, G);
     if (a.head_dim == 64)

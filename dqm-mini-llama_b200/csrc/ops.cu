@@ -207,6 +207,55 @@ __global__ void kv_write_kernel(float* keys, float* values, int max_seq, int n_k
   }
 }
 
+// y = x * sigmoid(x) (SiluKernel, src/cuda_ops.cu:52-58) and y = a * b
+// (ElementwiseMulKernel, :60-66): the standalone forms of the SwiGLU pieces.
+__global__ void silu_kernel(const float* __restrict__ x, int n, float* __restrict__ y) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float v = x[i];
+    y[i] = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+  }
+}
+
+__global__ void mul_kernel(const float* __restrict__ a, const float* __restrict__ b, int n,
+                           float* __restrict__ y) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    y[i] = __fmul_rn(a[i], b[i]);
+}
+
+// One-dimensional softmax (src/ops.cc:92-118; the reference's three-kernel
+// CUDA form, src/cuda_ops.cu:84-136): one CTA, max, sum of exp(x - max),
+// divide.
+__global__ void softmax_kernel(const float* __restrict__ x, int n, float* __restrict__ y) {
+  __shared__ float red[32];
+  __shared__ float bc;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = fmaxf(t, red[w]);
+    bc = t;
+  }
+  __syncthreads();
+  m = bc;
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += expf(x[i] - m);
+  s = warp_sum(s);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    bc = t;
+  }
+  __syncthreads();
+  const float inv = bc;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fdiv_rn(expf(x[i] - m), inv);
+}
+
 int grid1d(int n, int threads) {
   int g = (n + threads - 1) / threads;
   const int cap = sm_count() * 8;
@@ -364,6 +413,32 @@ extern "C" int dqmk_silu_mul(const float* g, const float* u, int n, float* y, vo
   if (n == 0) return DQMK_OK;
   if (!g || !u || !y) return fail(DQMK_ERR_INVALID, "SwiGlu: null pointer");
   DQMK_CUDA_RET("CudaSilu", launch_silu_mul(g, u, n, y, (cudaStream_t)stream));
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_silu(const float* x, int n, float* y, void* stream) {
+  if (n < 0) return fail(DQMK_ERR_INVALID, "CudaSilu: shape mismatch");
+  if (n == 0) return DQMK_OK;
+  if (!x || !y) return fail(DQMK_ERR_INVALID, "CudaSilu: null pointer");
+  silu_kernel<<<grid1d(n, 256), 256, 0, (cudaStream_t)stream>>>(x, n, y);
+  DQMK_CUDA_RET("CudaSilu", cudaGetLastError());
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_mul(const float* a, const float* b, int n, float* y, void* stream) {
+  if (n < 0) return fail(DQMK_ERR_INVALID, "CudaElementwiseMul: shape mismatch");
+  if (n == 0) return DQMK_OK;
+  if (!a || !b || !y) return fail(DQMK_ERR_INVALID, "CudaElementwiseMul: null pointer");
+  mul_kernel<<<grid1d(n, 256), 256, 0, (cudaStream_t)stream>>>(a, b, n, y);
+  DQMK_CUDA_RET("CudaElementwiseMul", cudaGetLastError());
+  return DQMK_OK;
+}
+
+extern "C" int dqmk_softmax(const float* x, int n, float* y, void* stream) {
+  if (n <= 0) return fail(DQMK_ERR_INVALID, "CudaSoftmax: empty input");
+  if (!x || !y) return fail(DQMK_ERR_INVALID, "CudaSoftmax: null pointer");
+  softmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, n, y);
+  DQMK_CUDA_RET("CudaSoftmax", cudaGetLastError());
   return DQMK_OK;
 }
 

@@ -209,6 +209,14 @@ int dqmk_rmsnorm(const float* x_dev, const float* w_dev, int dim, float eps, flo
  * reference SwiGlu (src/ops.cc:140-151): y = silu(gate) * up. */
 int dqmk_silu_mul(const float* gate_dev, const float* up_dev, int n, float* y_dev, void* stream);
 
+/* CudaSiluDeviceInput (cuda_ops.h:39-40): y = x * sigmoid(x);
+ * CudaElementwiseMulDeviceInput (cuda_ops.h:41-44): y = a * b;
+ * CudaSoftmax (cuda_ops.h:24): y = softmax(x) over n values.  The decode step
+ * fuses these into its kernels; the standalone forms serve the per-op API. */
+int dqmk_silu(const float* x_dev, int n, float* y_dev, void* stream);
+int dqmk_mul(const float* a_dev, const float* b_dev, int n, float* y_dev, void* stream);
+int dqmk_softmax(const float* x_dev, int n, float* y_dev, void* stream);
+
 /* CudaElementwiseAddDeviceInput / DeviceWeight (cuda_ops.h:45-53): y = a + b. */
 int dqmk_add(const float* a_dev, const float* b_dev, int n, float* y_dev, void* stream);
 
