@@ -415,6 +415,7 @@ struct GemvPhase {
 
   __device__ __forceinline__ void prefetch(const GemvArgs& a, int cta, int n_ctas) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    if (a.l2.n) l2_prefetch_share(a.l2, cta, n_ctas);
     gt = (wid % GW) * 32 + lane;
     g.chunks = a.kp / Fmt<QT>::kElems;
     g.row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
