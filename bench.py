@@ -684,6 +684,51 @@ def time_cols_gemm(pkg, torch, launches: int = 10):
     return {"shape": "64x3584->37888 Q4_0", "us_per_call": round(e0.elapsed_time(e1) / launches * 1e3, 2)}
 
 
+def kernel_sample(pkg, torch):
+    """One small launch of every kernel kind of the library, for profiling
+    runs (ncu -k regex:... on this mode): quantize / dequantize / pack, the
+    ggml-layout Linears (Q8_0, Q4_0, Q4_1, F32), the packed GEMV and the
+    TMA-staged lm_head GEMV, one Qwen2-0.5B-architecture decode step (embed,
+    QKV / O / gate-up / down GEMVs, short-cache attention, lm_head), a
+    128-token batched prefill (activation split, tensor-core GEMM, split-K
+    epilogue, causal attention, weight split), and one 64-column step of a
+    one-layer Qwen2-7B-shaped multi-sequence batch over a 2048-position cache
+    (split, batch GEMM, split-K reduce, streaming attention, greedy
+    advance)."""
+    S = pkg.synth
+    x = torch.randn(4096, 4096, device="cuda")
+    for qt in (pkg.Q80, pkg.Q40):
+        q = pkg.QuantizeToQ80(x) if qt == pkg.Q80 else pkg.QuantizeToQ40(x)
+        (pkg.DequantizeFromQ80 if qt == pkg.Q80 else pkg.DequantizeFromQ40)(q, (4096, 4096))
+        pkg.pack_weight(qt, q, 4096, 4096)
+    del x
+    for qt in (pkg.Q80, pkg.Q40, pkg.Q41):
+        blocks, xs = S.gemv_case(4864, 896, 3, qt)
+        fn = {pkg.Q80: pkg.CudaQ80Linear, pkg.Q40: pkg.CudaQ40Linear, pkg.Q41: pkg.CudaQ41Linear}
+        fn[qt](xs, blocks, (4864, 896))
+    pkg.CudaLinear(np.random.default_rng(0).standard_normal(896).astype(np.float32),
+                   np.random.default_rng(1).standard_normal((4864, 896)).astype(np.float32))
+    w = S.make_model(S.QWEN2_0_5B, S.Q80, MODEL_SEED,
+                     quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+    model = pkg.Model.from_synth(w, max_seq_len=N_PROMPT + N_DECODE_POS)
+    ctx = pkg.Context(model)
+    prompt = S.prompt_tokens(w.cfg["vocab"], 128, 5).tolist()
+    first = int(np.argmax(ctx.ForwardBatch(prompt[:N_PROMPT], 0)))
+    ctx.decode_enqueue(first, N_PROMPT, 1)
+    torch.cuda.synchronize()
+    ctx.close()
+    model.close()
+    c7 = dict(S.QWEN2_7B, vocab=8192)
+    w7 = S.make_model(c7, S.Q40, 77, n_layers=1)
+    m7 = pkg.Model.from_synth(w7, max_seq_len=2048 + 4)
+    b7 = pkg.Batch(m7, 64, 2048 + 4)
+    b7.decode_enqueue([3] * 64, [2047] * 64, 1)
+    torch.cuda.synchronize()
+    b7.close()
+    m7.close()
+    return {"kernel_sample": "done"}
+
+
 def decode_config(world: int) -> dict:
     """The headline workload, shared by the GPU arm and the reference arm."""
     return {"workload": "qwen2-0.5b-architecture Q8_0, 32-token prompt then batch-1 greedy "
@@ -823,6 +868,8 @@ def main():
                     help="qwen2-7b --seqs > 1: fill every KV cache with a random prompt "
                          "(prompt) or leave it zero and start decoding at position --ctx - 1 "
                          "(zero: the step reads the same bytes)")
+    ap.add_argument("--kernel-sample", action="store_true",
+                    help="one small launch of every kernel kind (for profiling)")
     ap.add_argument("--cols-gemm", action="store_true",
                     help="time only the standalone multi-sequence GEMM at the Qwen2-7B gate/up "
                          "shape (64 columns x 37888 x 3584 Q4_0; profiling)")
@@ -853,6 +900,9 @@ def main():
     S = pkg.synth
     if args.cols_gemm:
         print(json.dumps({"cols_gemm": time_cols_gemm(pkg, torch)}))
+        return
+    if args.kernel_sample:
+        print(json.dumps(kernel_sample(pkg, torch)))
         return
     if args.model == "qwen2-7b":
         if args.seqs > 1:

@@ -118,26 +118,6 @@ __device__ __forceinline__ float4 ldg_f4_stream(const float* p) {
                      __uint_as_float(r.w));
 }
 
-// This CTA's share of each L2Prefetch range, as bulk prefetches of at most
-// 64 KB (one thread issues them; nothing waits on them).
-__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int cta, int n_ctas) {
-  if (threadIdx.x != 0) return;
-  for (int r = 0; r < pf.n; ++r) {
-    const unsigned long long total = pf.bytes[r] & ~15ull;
-    unsigned long long per = (total + n_ctas - 1) / n_ctas;
-    per = (per + 15) & ~15ull;
-    const unsigned long long begin = (unsigned long long)cta * per;
-    if (begin >= total) continue;
-    const unsigned long long end = begin + per < total ? begin + per : total;
-    const char* base = static_cast<const char*>(pf.base[r]);
-    for (unsigned long long o = begin; o < end; o += 65536ull) {
-      const unsigned int n = (unsigned int)(end - o < 65536ull ? end - o : 65536ull);
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + o), "r"(n)
-                   : "memory");
-    }
-  }
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -539,16 +539,6 @@ extern "C" int dqmk_model_stats_reset(dqmk_model* m) {
 extern "C" size_t dqmk_model_memory_bytes(const dqmk_model* m) { return m ? m->memory_bytes : 0; }
 
 // ------------------------------------------------------------------ context
-// L2 staging of a layer's later weights by its QKV GEMV; DQMK_L2_PREFETCH=0
-// in the environment leaves it out (diagnostics: same results).
-static bool l2_prefetch_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("DQMK_L2_PREFETCH");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 // Programmatic dependent launch between the kernels of a step; DQMK_PDL=0 in
 // the environment launches them plainly instead (diagnostics: same work).
 bool dqmk::use_pdl() {
@@ -626,19 +616,6 @@ int enqueue_step(dqmk_context* x) {
     g.n_kv_heads = tp.n_kv_heads;
     g.head_dim = c.head_dim;
     g.neox = c.rope_neox;
-    // The layer's O, gate/up and down weights and the next layer's QKV
-    // stream into L2 while the QKV GEMV and attention run (latency-bound
-    // links of the chain that leave HBM idle); those GEMVs then read L2.
-    if (l2_prefetch_enabled()) {
-      const Packed* later[] = {&L.wo, &L.gate_up, &L.down,
-                               l + 1 < c.n_layers ? &m->layers[l + 1].qkv : nullptr};
-      for (const Packed* w : later)
-        if (w) {
-          g.l2.base[g.l2.n] = w->base;
-          g.l2.bytes[g.l2.n] = w->bytes;
-          ++g.l2.n;
-        }
-    }
     DQMK_CUDA_RET(api, gemv_op(g));
 
     AttnArgs at = {};

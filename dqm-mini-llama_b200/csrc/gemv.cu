@@ -21,6 +21,7 @@
 // is split across lanes and the scale is applied per block, so results agree
 // to float rounding (checked against the oracle), not bit for bit.
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "gemv_dev.cuh"
@@ -41,7 +42,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
   // Weights and norm weights do not depend on the previous kernel: fetch
   // them before the programmatic-dependency wait.
   GemvPhase<QT, RPW, CPL, GW> ph;
-  ph.prefetch(a, blockIdx.x, gridDim.x);
+  ph.prefetch(a, blockIdx.x, gridDim.x, xs + (a.kp >> 2));
   pdl_trigger();
   pdl_wait();
   gemv_run<QT, RPW, CPL, GW, PEER>(ph, a, xs, gridDim.x, &g_device_error);
@@ -50,6 +51,8 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
 // ------------------------------------------------------------ launch table
 // One-time kernel attributes and the resident-CTA cap for the grid-stride
 // case.  Run before any stream capture (context creation does).
+constexpr int kDefaultCtasPerSm = 0;
+
 template <int QT, int RPW, int CPL, int GW, bool PEER>
 cudaError_t prepare_t(int* max_ctas_out) {
   static DeviceOnce once;
@@ -76,16 +79,30 @@ cudaError_t prepare_t(int* max_ctas_out) {
   return cudaSuccess;
 }
 
+// CTAs per SM a chained GEMV may take (0: as many as fit).  A grid that fills
+// every SM's registers keeps the next kernel of the chain from becoming
+// resident -- and prefetching its weights -- until it drains.
+int gemv_ctas_per_sm_cap() {
+  static const int cap = [] {
+    const char* v = std::getenv("DQMK_GEMV_CTAS_PER_SM");
+    return v ? std::atoi(v) : kDefaultCtasPerSm;
+  }();
+  return cap;
+}
+
 template <int QT, int RPW, int CPL, int GW, bool PEER>
 cudaError_t launch_impl(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   int max_ctas = 0;
   cudaError_t e = prepare_t<QT, RPW, CPL, GW, PEER>(&max_ctas);
   if (e != cudaSuccess) return e;
-  const size_t smem = (size_t)a.kp * sizeof(float);
+  // x, then (RMSNorm kernels) the norm weight
+  const size_t smem = (size_t)a.kp * sizeof(float) * (a.norm_w ? 2 : 1);
   const int n_groups = (a.n_rows + RPW - 1) / RPW;
   constexpr int GPC = kWarps / GW;
   int grid = (n_groups + GPC - 1) / GPC;
   if (grid > max_ctas) grid = max_ctas;
+  const int cap = gemv_ctas_per_sm_cap();
+  if (pdl && cap > 0 && grid > cap * sm_count()) grid = cap * sm_count();
   if (grid < 1) grid = 1;
   return launch(gemv_kernel<QT, RPW, CPL, GW, PEER>, dim3(grid), dim3(kWarps * 32), smem,
                 stream, pdl, a);

@@ -274,12 +274,22 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
 
 constexpr int kNormRegs = 8;  // float4 of RMSNorm weight prefetched per thread
 
+// 16-byte global -> shared copy that does not go through registers.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(src)
+               : "memory");
+}
+
 // Stage x (k floats, zero-padded to kp) into swizzled shared memory, RMS-
 // normalised when norm_w is set.  One global round trip: every thread issues
 // all of its loads before using any.  Activations come from the previous
 // kernel of the chain, so they are read through L2 (ld.global.cg).
+// nws: the RMSNorm weight, copied into shared memory by the prefetch phase
+// (each thread reads back exactly the float4s it copied).
 template <int QT, int NWARPS, int NR>
-__device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const float4 (&nw)[NR],
+__device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const float4* nws,
                                         bool norm_pref, float* red, float* bcast) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   constexpr int NT = NWARPS * 32;
@@ -329,6 +339,9 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const flo
     }
     __syncthreads();
     const float scale = *bcast;
+    // the prefetch phase's copies of the norm weight (none in flight when it
+    // issued none) land before any use and before the kernel can exit
+    asm volatile("cp.async.wait_all;" ::: "memory");
     if (vec && norm_pref) {
 #pragma unroll
       for (int u = 0; u < NR; ++u) {
@@ -337,10 +350,11 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, const flo
           const int e = i4 * 4;
           float4* p = &xs[xslot<QT>(e / Fmt<QT>::kElems, (e % Fmt<QT>::kElems) >> 2)];
           float4 v = *p;
-          v.x = __fmul_rn(__fmul_rn(v.x, scale), nw[u].x);
-          v.y = __fmul_rn(__fmul_rn(v.y, scale), nw[u].y);
-          v.z = __fmul_rn(__fmul_rn(v.z, scale), nw[u].z);
-          v.w = __fmul_rn(__fmul_rn(v.w, scale), nw[u].w);
+          const float4 nw = nws[i4];
+          v.x = __fmul_rn(__fmul_rn(v.x, scale), nw.x);
+          v.y = __fmul_rn(__fmul_rn(v.y, scale), nw.y);
+          v.z = __fmul_rn(__fmul_rn(v.z, scale), nw.z);
+          v.w = __fmul_rn(__fmul_rn(v.w, scale), nw.w);
           *p = v;
         }
       }
@@ -410,12 +424,11 @@ struct GemvPhase {
   Geo g;
   int total, gt;
   Tile<QT, RPW, CPL> ta, tb;
-  float4 nw[kNormRegs];
   bool norm_pref;
 
-  __device__ __forceinline__ void prefetch(const GemvArgs& a, int cta, int n_ctas) {
+  // nws: shared memory for the RMSNorm weight (kp floats, after x's).
+  __device__ __forceinline__ void prefetch(const GemvArgs& a, int cta, int n_ctas, float4* nws) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    if (a.l2.n) l2_prefetch_share(a.l2, cta, n_ctas);
     gt = (wid % GW) * 32 + lane;
     g.chunks = a.kp / Fmt<QT>::kElems;
     g.row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
@@ -434,9 +447,9 @@ struct GemvPhase {
 #pragma unroll
       for (int u = 0; u < kNormRegs; ++u) {
         const int i4 = u * kWarps * 32 + tid;
-        nw[u] = i4 < (a.k >> 2) ? __ldg(reinterpret_cast<const float4*>(a.norm_w) + i4)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i4 < (a.k >> 2)) cp_async16(nws + i4, reinterpret_cast<const float4*>(a.norm_w) + i4);
       }
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
   }
 };
@@ -457,7 +470,7 @@ __device__ __forceinline__ void gemv_run(GemvPhase<QT, RPW, CPL, GW>& ph, const 
   Tile<QT, RPW, CPL>& ta = ph.ta;
   Tile<QT, RPW, CPL>& tb = ph.tb;
 
-  stage_x<QT, kWarps, kNormRegs>(a, xs, ph.nw, ph.norm_pref, red, &bcast);
+  stage_x<QT, kWarps, kNormRegs>(a, xs, xs + (a.kp >> 2), ph.norm_pref, red, &bcast);
 
   int pos = 0;
   if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;

@@ -110,18 +110,6 @@ __host__ __device__ __forceinline__ size_t tp_buf_bytes(int world, int dim) {
   return tp_flags_off(world, dim) + tp_round256((size_t)2 * world * 4);
 }
 
-// Byte ranges a kernel asks the memory system to bring into L2 ahead of the
-// kernels that read them (cp.async.bulk.prefetch.L2; a hint, no data moves
-// into the kernel).  Each CTA takes an equal 16-byte-aligned share of every
-// range.  Used by the decode step to stream a layer's later weights while
-// its latency-bound first kernels run.
-struct L2Prefetch {
-  static constexpr int kMax = 4;
-  const void* base[kMax];
-  unsigned long long bytes[kMax];
-  int n;
-};
-
 struct GemvArgs {
   int qtype;
   const uint8_t* qs;    // quant plane
@@ -155,8 +143,6 @@ struct GemvArgs {
   int history_cap;
   // kEpiPeer: where the partial rows go
   PeerSet peer;
-  // weights of later kernels to stage into L2 (issued before the wait)
-  L2Prefetch l2;
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);

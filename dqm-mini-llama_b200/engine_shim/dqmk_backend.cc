@@ -292,7 +292,8 @@ CudaTensor CudaAttentionDecodeDeviceInput(const CudaTensor& q, const CudaKvCache
   if (q.size() != static_cast<size_t>(n_heads) * head_dim)
     throw std::runtime_error("CudaAttentionDecode: q shape mismatch");
   SetDevice(device_id, "CudaAttentionDecode");
-  CudaTensor out({n_heads, head_dim}, device_id);
+  // The device-resident result is flat [n_heads * head_dim], ready for the O projection.
+  CudaTensor out({n_heads * head_dim}, device_id);
   Check(dqmk_attention_decode(F(q), static_cast<const float*>(kv_cache.keys_data()),
                               static_cast<const float*>(kv_cache.values_data()),
                               kv_cache.n_layers(), kv_cache.max_seq_len(), n_kv_heads, head_dim,
@@ -305,7 +306,7 @@ Tensor CudaAttentionDecode(const Tensor& q, const CudaKvCache& kv_cache, int lay
   Tensor out = CudaAttentionDecodeDeviceInput(qd, kv_cache, layer, pos, n_heads, n_kv_heads,
                                               head_dim, device_id)
                    .Download();
-  out.shape = q.shape;
+  out.shape = {n_heads, head_dim};
   return out;
 }
 
