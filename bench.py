@@ -688,7 +688,8 @@ def kernel_sample(pkg, torch):
     """One small launch of every kernel kind of the library, for profiling
     runs (ncu -k regex:... on this mode): quantize / dequantize / pack, the
     ggml-layout Linears (Q8_0, Q4_0, Q4_1, F32), the packed GEMV and the
-    TMA-staged lm_head GEMV, one Qwen2-0.5B-architecture decode step (embed,
+    TMA-staged lm_head GEMV, decode attention over a 2048-position cache and
+    over an odd head shape, one Qwen2-0.5B-architecture decode step (embed,
     QKV / O / gate-up / down GEMVs, short-cache attention, lm_head), a
     128-token batched prefill (activation split, tensor-core GEMM, split-K
     epilogue, causal attention, weight split), and one 64-column step of a
@@ -708,6 +709,15 @@ def kernel_sample(pkg, torch):
         fn[qt](xs, blocks, (4864, 896))
     pkg.CudaLinear(np.random.default_rng(0).standard_normal(896).astype(np.float32),
                    np.random.default_rng(1).standard_normal((4864, 896)).astype(np.float32))
+    # decode attention outside the chain: a 2048-position cache (split over
+    # the SMs, merged by the last CTA) and a head shape only the general
+    # kernel takes
+    for n_heads, n_kv, hd, max_seq, pos in ((14, 2, 64, 2048, 2047), (2, 1, 3, 4, 1)):
+        kv = pkg.CudaKvCache(1, max_seq, n_kv, hd)
+        kv.keys.normal_()
+        kv.values.normal_()
+        q = torch.randn(n_heads * hd, device="cuda")
+        pkg.CudaAttentionDecodeDeviceInput(q, kv, 0, pos, n_heads, n_kv, hd)
     w = S.make_model(S.QWEN2_0_5B, S.Q80, MODEL_SEED,
                      quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
     model = pkg.Model.from_synth(w, max_seq_len=N_PROMPT + N_DECODE_POS)

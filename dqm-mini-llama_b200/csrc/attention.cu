@@ -400,7 +400,94 @@ cudaError_t attention_prepare() {
   });
 }
 
+// Any head configuration the fast kernels do not take (head_dim not a
+// multiple of 4 or above 256, more than 8 query heads per KV head): one CTA
+// per query head, plain float loads.  Pass 1 keeps a running (max, sum) of
+// the scaled scores per thread and merges them across the CTA; pass 2 turns
+// 1024 positions at a time into probabilities in shared memory and
+// accumulates P.V with one thread per output dimension.  Drop-in entry
+// points only (the decode step's shapes all have a fast kernel).
+constexpr int kAnyThreads = 256;
+constexpr int kAnyChunk = 1024;
+
+__global__ void __launch_bounds__(kAnyThreads) attention_any_kernel(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float w[kAnyChunk];
+  __shared__ float red_m[kAnyThreads / 32], red_l[kAnyThreads / 32];
+  __shared__ float stat[2];
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int hd = a.head_dim;
+  const int G = a.n_heads / a.n_kv_heads;
+  const int kvh = h / G;
+  const int pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+  const size_t row_stride = (size_t)a.n_kv_heads * hd;
+  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * hd;
+  const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * hd;
+  const float* qh = a.q + (size_t)h * hd;
+  const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
+  auto score = [&](int t) {
+    const float* kr = kbase + (size_t)t * row_stride;
+    float d = 0.0f;
+    for (int i = 0; i < hd; ++i) d = fmaf(__ldcg(qh + i), __ldcg(kr + i), d);
+    return __fmul_rn(d, scale);
+  };
+  float m = -INFINITY, l = 0.0f;
+  for (int t = tid; t <= pos; t += kAnyThreads) {
+    const float sc = score(t);
+    const float nm = fmaxf(m, sc);
+    l = l * expf(m - nm) + expf(sc - nm);
+    m = nm;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float ol = __shfl_xor_sync(0xffffffffu, l, o);
+    const float nm = fmaxf(m, om);
+    l = (m == -INFINITY ? 0.0f : l * expf(m - nm)) + (om == -INFINITY ? 0.0f : ol * expf(om - nm));
+    m = nm;
+  }
+  if (lane == 0) {
+    red_m[wid] = m;
+    red_l[wid] = l;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float M = -INFINITY, L = 0.0f;
+    for (int i = 0; i < kAnyThreads / 32; ++i) {
+      const float nm = fmaxf(M, red_m[i]);
+      L = (M == -INFINITY ? 0.0f : L * expf(M - nm)) +
+          (red_m[i] == -INFINITY ? 0.0f : red_l[i] * expf(red_m[i] - nm));
+      M = nm;
+    }
+    stat[0] = M;
+    stat[1] = L;
+  }
+  __syncthreads();
+  const float M = stat[0], L = stat[1];
+  for (int d0 = 0; d0 < hd; d0 += kAnyThreads) {
+    const int d = d0 + tid;
+    float acc = 0.0f;
+    for (int c0 = 0; c0 <= pos; c0 += kAnyChunk) {
+      const int n = min(kAnyChunk, pos + 1 - c0);
+      __syncthreads();
+      for (int t = tid; t < n; t += kAnyThreads) w[t] = expf(score(c0 + t) - M);
+      __syncthreads();
+      if (d < hd)
+        for (int t = 0; t < n; ++t)
+          acc = fmaf(w[t], __ldcg(vbase + (size_t)(c0 + t) * row_stride + d), acc);
+    }
+    if (d < hd) a.out[(size_t)h * hd + d] = __fdiv_rn(acc, L);
+  }
+}
+
+bool attention_fast_shape(int head_dim, int n_heads, int n_kv_heads) {
+  return head_dim % 4 == 0 && head_dim <= 256 && n_heads / n_kv_heads <= kMaxGroup;
+}
+
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
+  if (!attention_fast_shape(a.head_dim, a.n_heads, a.n_kv_heads))
+    return launch(attention_any_kernel, dim3(a.n_heads), dim3(kAnyThreads), 0, stream, pdl, a);
   const int cap = chunk_cap_for(a.max_seq, a.max_splits);
   // the templated kernel reads q and writes out with 16-byte vectors
   const bool aligned =
@@ -446,12 +533,11 @@ extern "C" int dqmk_attention_decode(const float* q, const float* keys, const fl
   if (pos < 0 || pos >= max_seq) return fail(DQMK_ERR_RANGE, std::string(api) + ": pos out of range");
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || n_heads % n_kv_heads != 0)
     return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid head configuration");
-  if (n_heads / n_kv_heads > 8)
-    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": more than 8 query heads per KV head");
-  if (head_dim % 4 != 0 || head_dim > 256)
-    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": head_dim must be a multiple of 4, <= 256");
   if (!q || !keys || !values || !out) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
-  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15u)
+  // the fast kernels read the cache with 16-byte vectors; other shapes take
+  // the general kernel
+  if (attention_fast_shape(head_dim, n_heads, n_kv_heads) &&
+      ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15u))
     return fail(DQMK_ERR_INVALID, std::string(api) + ": KV cache must be 16-byte aligned");
   const int splits = attention_splits(max_seq, n_kv_heads);
   const size_t tickets_bytes = 256;
@@ -528,12 +614,11 @@ extern "C" int dqmk_attention_decode_noalloc(const float* q, const float* keys,
   if (pos < 0 || pos >= max_seq) return fail(DQMK_ERR_RANGE, std::string(api) + ": pos out of range");
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || n_heads % n_kv_heads != 0)
     return fail(DQMK_ERR_INVALID, std::string(api) + ": invalid head configuration");
-  if (n_heads / n_kv_heads > 8)
-    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": more than 8 query heads per KV head");
-  if (head_dim % 4 != 0 || head_dim > 256)
-    return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": head_dim must be a multiple of 4, <= 256");
   if (!q || !keys || !values || !out) return fail(DQMK_ERR_INVALID, std::string(api) + ": null pointer");
-  if ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15u)
+  // the fast kernels read the cache with 16-byte vectors; other shapes take
+  // the general kernel
+  if (attention_fast_shape(head_dim, n_heads, n_kv_heads) &&
+      ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(values)) & 15u))
     return fail(DQMK_ERR_INVALID, std::string(api) + ": KV cache must be 16-byte aligned");
   if (n_kv_heads * sizeof(unsigned int) > kNoAllocTicketBytes)
     return fail(DQMK_ERR_UNSUPPORTED, std::string(api) + ": too many KV heads");

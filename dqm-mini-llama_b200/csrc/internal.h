@@ -146,7 +146,8 @@ struct GemvArgs {
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
-// Register-GEMV variant the dispatcher picks for a shape (-1: the TMA form).
+// Register-GEMV variant the dispatcher picks for a shape (-1: the TMA form,
+// -2: the slice-resident form).
 int gemv_variant_id(const GemvArgs& a);
 // Sets kernel attributes of every GEMV / attention instantiation; call
 // outside stream capture.

@@ -313,6 +313,32 @@ def test_attention_decode_short_cache(pkg, orc, cuda, cfg):
     assert np.array_equal(bits(out), bits(exp))
 
 
+@pytest.mark.parametrize("cfg", [(2, 1, 3, 4), (12, 1, 6, 300), (4, 2, 260, 40), (18, 1, 64, 64)])
+def test_attention_decode_any_shape(pkg, orc, cuda, cfg):
+    """Head configurations outside the fast kernels (head_dim not a multiple
+    of 4 or above 256, more than 8 query heads per KV head -- the reference's
+    CUDA attention takes any): the general kernel, within the CUDA tests'
+    tolerance of the oracle, exactly V at position 0.  (2, 1, 3) is the
+    reference test's own GQA case (tests/test_cuda_attention.cc:106-145)."""
+    n_heads, n_kv, hd, max_seq = cfg
+    n_layers = 2
+    rng = np.random.default_rng(n_heads * hd + max_seq)
+    kv = pkg.CudaKvCache(n_layers, max_seq, n_kv, hd)
+    keys = rng.standard_normal((n_layers, max_seq, n_kv, hd)).astype(np.float32)
+    vals = rng.standard_normal((n_layers, max_seq, n_kv, hd)).astype(np.float32)
+    kv.keys.copy_(cuda.from_numpy(keys))
+    kv.values.copy_(cuda.from_numpy(vals))
+    q = rng.standard_normal(n_heads * hd).astype(np.float32)
+    qd = cuda.from_numpy(q).cuda()
+    for layer, pos in ((0, 1), (1, max_seq // 2), (1, max_seq - 1)):
+        out = pkg.CudaAttentionDecodeDeviceInput(qd, kv, layer, pos, n_heads, n_kv, hd)
+        ref = orc.attention(q, keys, vals, layer, pos, n_heads)
+        assert_close(out.cpu().numpy(), ref, f"layer {layer} pos {pos}")
+    out = pkg.CudaAttentionDecodeDeviceInput(qd, kv, 1, 0, n_heads, n_kv, hd).cpu().numpy()
+    exp = np.concatenate([vals[1, 0, h // (n_heads // n_kv)] for h in range(n_heads)])
+    assert np.array_equal(bits(out), bits(exp))
+
+
 @pytest.mark.parametrize("qt", [1, 2])
 def test_lm_head_block_sums_exact(pkg, orc, S, cuda, qt):
     """The TMA-staged GEMV's integer path, bit for bit: x split into three int8
