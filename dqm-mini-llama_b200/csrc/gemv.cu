@@ -21,7 +21,6 @@
 // is split across lanes and the scale is applied per block, so results agree
 // to float rounding (checked against the oracle), not bit for bit.
 #include <algorithm>
-#include <cstdlib>
 
 #include "common.cuh"
 #include "gemv_dev.cuh"
@@ -705,270 +704,6 @@ bool tma_eligible(const GemvArgs& a) {
   return a.qtype == DQMK_Q80 && a.kp <= 8192 && a.n_rows >= 32768 && a.epi != kEpiPeer;
 }
 
-// ====================================================== slice-resident GEMV
-// For the per-layer projections of the decode chain.  Each CTA owns one
-// contiguous slice of rows (at most one CTA per SM) and, before
-// griddepcontrol.wait, requests the whole slice -- quants, scales and the
-// RMSNorm weight -- with bulk asynchronous copies into shared memory.  The
-// CTA is small in registers (256 threads, at most 64 registers each), so
-// under programmatic dependent launch the next kernels of the chain become
-// resident next to the running one and their weights stream in while it
-// works: after the dependency resolves a CTA only stages x, splits it into
-// three int8 terms per 32-block and runs the exact dp4a block sums of the
-// TMA form against shared memory.  The single wait on the copies is bounded
-// like the TMA form's; on timeout the CTA records kErrTimeout, skips the
-// math, lets its copies land and exits.
-constexpr int kSliceWarps = 8;
-constexpr int kSliceThreads = kSliceWarps * 32;
-constexpr size_t kSliceSmemMax = 120 * 1024;
-
-struct SlicePlan {
-  int rows_per_cta, grid;
-  size_t norm_off, w_off, d_off, smem;
-};
-
-int gcd_int(int a, int b) { return b ? gcd_int(b, a % b) : a; }
-
-// Rows per CTA: an even share of the rows over the SMs, rounded up so every
-// slice starts a whole number of 16-byte units into the scale plane
-// (rows x nbk x 2 bytes) and holds whole row groups.
-SlicePlan slice_plan(const GemvArgs& a, int rpw) {
-  SlicePlan p = {};
-  const int nbk = a.kp / 32;
-  const size_t row_bytes = a.qtype == DQMK_Q80 ? (size_t)a.kp : (size_t)a.kp / 2;
-  const int gran0 = 8 / gcd_int(nbk, 8);
-  const int gran = gran0 * rpw / gcd_int(gran0, rpw);
-  const int sms = sm_count();
-  int r = (a.n_rows + sms - 1) / sms;
-  r = (r + gran - 1) / gran * gran;
-  p.rows_per_cta = r;
-  p.grid = (a.n_rows + r - 1) / r;
-  auto up16 = [](size_t v) { return (v + 15) & ~(size_t)15; };
-  p.norm_off = x_layout(a.kp).stages;
-  p.w_off = p.norm_off + (a.norm_w ? up16((size_t)a.kp * 4) : 0);
-  p.d_off = p.w_off + up16((size_t)r * row_bytes);
-  p.smem = p.d_off + up16((size_t)r * nbk * 2);
-  return p;
-}
-
-template <int QT, int RPW>
-__global__ void __launch_bounds__(kSliceThreads, 4) gemv_slice_kernel(const GemvArgs a,
-                                                                     int rows_per_cta,
-                                                                     unsigned norm_off,
-                                                                     unsigned w_off,
-                                                                     unsigned d_off) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ float red[kSliceWarps];
-  __shared__ float bcast;
-  __shared__ int s_abort;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int nbk = a.kp / 32;
-  const int row_bytes = QT == DQMK_Q80 ? a.kp : a.kp / 2;
-  const int r0 = blockIdx.x * rows_per_cta;
-  const int rows = min(rows_per_cta, a.n_rows - r0);
-  const XLayout xl = x_layout(a.kp);
-  float* xf = reinterpret_cast<float*>(smem);
-  int8_t* xq = reinterpret_cast<int8_t*>(smem + xl.q);
-  float* xsc = reinterpret_cast<float*>(smem + xl.sc);
-  int* xsum = reinterpret_cast<int*>(smem + xl.sum);
-  float* nws = reinterpret_cast<float*>(smem + norm_off);
-  const unsigned char* wq = smem + w_off;
-  const uint16_t* wd = reinterpret_cast<const uint16_t*>(smem + d_off);
-  volatile int* abort = &s_abort;
-  const bool norm_bulk = a.norm_w && (a.k & 3) == 0 &&
-                         (reinterpret_cast<uintptr_t>(a.norm_w) & 15u) == 0;
-
-  // ---- before the dependency: the slice's bytes (constant for the step)
-  if (tid == 0) {
-    s_abort = 0;
-    mbar_init(&bar, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    const uint32_t qbytes = (uint32_t)(rows * row_bytes);
-    const uint32_t dbytes = (uint32_t)(rows * nbk * 2);
-    const uint32_t nbytes = norm_bulk ? (uint32_t)a.k * 4u : 0u;
-    const uint64_t policy = evict_first_policy();
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_expect_tx(&bar, qbytes + dbytes + nbytes);
-    bulk_g2s(smem + w_off, a.qs + (size_t)r0 * row_bytes, qbytes, &bar, policy);
-    bulk_g2s(smem + d_off, a.d + (size_t)r0 * nbk, dbytes, &bar, policy);
-    if (nbytes) bulk_g2s(nws, a.norm_w, nbytes, &bar, policy);
-  }
-  __syncthreads();
-  pdl_trigger();
-  pdl_wait();
-
-  // ---- x: one round trip, RMSNorm statistics on the way
-  const bool vec = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0) && ((a.k & 3) == 0);
-  float ss = 0.0f;
-  if (vec) {
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    float4* xf4 = reinterpret_cast<float4*>(xf);
-    const int k4 = a.k >> 2, nf4 = a.kp >> 2;
-    for (int base = 0; base < nf4; base += 8 * kSliceThreads) {
-      float4 v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i4 = base + u * kSliceThreads + tid;
-        v[u] = i4 < k4 ? __ldcg(x4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i4 = base + u * kSliceThreads + tid;
-        if (i4 < nf4) {
-          ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
-          ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
-          ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
-          ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
-          xf4[i4] = v[u];
-        }
-      }
-    }
-  } else {
-    for (int e = tid; e < a.kp; e += kSliceThreads) {
-      const float v = e < a.k ? __ldcg(a.x + e) : 0.0f;
-      xf[e] = v;
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
-    }
-  }
-  if (a.norm_w) {
-    ss = warp_sum(ss);
-    if (lane == 0) red[wid] = ss;
-  }
-  // every thread waits for the slice (and the norm weight) here; lanes of a
-  // warp agree on the outcome
-  const bool ok = rows <= 0 || tc::bar_wait(&bar, 0, abort, &g_device_error);
-  __syncthreads();
-  const bool run = !*abort && ok;
-  if (a.norm_w) {
-    if (tid == 0) {
-      float t = 0.0f;
-      for (int w = 0; w < kSliceWarps; ++w) t += red[w];
-      bcast = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(t, (float)a.k), a.eps)));
-    }
-    __syncthreads();
-    const float scale = bcast;
-    for (int e = tid; e < a.k; e += kSliceThreads) {
-      const float w = (norm_bulk && run) ? nws[e] : __ldg(a.norm_w + e);
-      xf[e] = __fmul_rn(__fmul_rn(xf[e], scale), w);
-    }
-    __syncthreads();
-  }
-  quantize_x_terms<kSliceWarps, QT == DQMK_Q40>(xf, nbk, xq, xsc, xsum);
-  __syncthreads();
-
-  if (run) {
-    int pos = 0;
-    if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
-    const int4* xq4 = reinterpret_cast<const int4*>(xq);
-    const bool xreg = nbk <= 32;
-    int4 xv[6];
-    float sc[3];
-    int sm8[3];
-    if (xreg && lane < nbk) {
-#pragma unroll
-      for (int t = 0; t < 6; ++t) xv[t] = xq4[(size_t)t * nbk + lane];
-#pragma unroll
-      for (int t = 0; t < 3; ++t) {
-        sc[t] = xsc[t * nbk + lane];
-        sm8[t] = QT == DQMK_Q40 ? 8 * xsum[t * nbk + lane] : 0;
-      }
-    }
-    unsigned long long best = 0ull;  // logits are not served here
-    const int n_groups = (rows + RPW - 1) / RPW;
-    for (int gl = wid; gl < n_groups; gl += kSliceWarps) {
-      float acc[RPW];
-#pragma unroll
-      for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
-      for (int b = lane; b < nbk; b += 32) {
-        if (!xreg) {
-#pragma unroll
-          for (int t = 0; t < 6; ++t) xv[t] = xq4[(size_t)t * nbk + b];
-#pragma unroll
-          for (int t = 0; t < 3; ++t) {
-            sc[t] = xsc[t * nbk + b];
-            sm8[t] = QT == DQMK_Q40 ? 8 * xsum[t * nbk + b] : 0;
-          }
-        }
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          const int rl = gl * RPW + r;
-          if (rl < rows) {
-            int w[8];
-            block_words<QT>(wq + (size_t)rl * row_bytes, b, w);
-            int S[3];
-            block_term_sums(w, xv, sm8, S);
-            float blk = 0.0f;
-#pragma unroll
-            for (int t = 0; t < 3; ++t) blk = __fmaf_rn(sc[t], (float)S[t], blk);
-            acc[r] = __fmaf_rn(h2f(wd[rl * nbk + b]), blk, acc[r]);
-          }
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < RPW; ++r) acc[r] = warp_sum(acc[r]);
-      epilogue<RPW, false>(a, r0 / RPW + gl, lane, acc, pos, best);
-    }
-  } else if (tid == 0 && rows > 0) {
-    // the copies this CTA issued land before its shared memory goes away
-    volatile int never = 0;
-    tc::bar_wait(&bar, 0, &never, &g_device_error);
-  }
-}
-
-#define DQMK_SLICE_VARIANTS(X) X(DQMK_Q80, 1) X(DQMK_Q80, 2) X(DQMK_Q40, 1) X(DQMK_Q40, 2)
-
-template <int QT, int RPW>
-cudaError_t slice_prepare() {
-  static DeviceOnce once;
-  return once.run([] {
-    return cudaFuncSetAttribute(gemv_slice_kernel<QT, RPW>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSliceSmemMax);
-  });
-}
-
-int slice_rpw(const GemvArgs& a) {
-  return (a.epi == kEpiSwiGlu || a.epi == kEpiQkv) ? 2 : 1;
-}
-
-cudaError_t slice_dispatch(const GemvArgs& a, cudaStream_t stream, bool pdl) {
-  const int rpw = slice_rpw(a);
-  const SlicePlan p = slice_plan(a, rpw);
-#define DQMK_SLICE_CASE(QT, RPW)                                                          \
-  if (a.qtype == QT && rpw == RPW) {                                                      \
-    cudaError_t e = slice_prepare<QT, RPW>();                                             \
-    if (e != cudaSuccess) return e;                                                       \
-    return launch(gemv_slice_kernel<QT, RPW>, dim3(p.grid), dim3(kSliceThreads), p.smem, \
-                  stream, pdl, a, p.rows_per_cta, (unsigned)p.norm_off, (unsigned)p.w_off, \
-                  (unsigned)p.d_off);                                                     \
-  }
-  DQMK_SLICE_VARIANTS(DQMK_SLICE_CASE)
-#undef DQMK_SLICE_CASE
-  return cudaErrorInvalidValue;
-}
-
-// The slice form serves the per-layer projections whose whole slice fits
-// the shared-memory budget; DQMK_GEMV_SLICE=0 in the environment keeps them
-// on the register form (A/B comparisons).
-bool slice_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("DQMK_GEMV_SLICE");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
-bool slice_eligible(const GemvArgs& a) {
-  if (!slice_enabled()) return false;
-  if (a.qtype != DQMK_Q80 && a.qtype != DQMK_Q40) return false;
-  if (a.epi != kEpiStore && a.epi != kEpiSwiGlu && a.epi != kEpiQkv) return false;
-  if (a.kp > 8192 || a.n_rows <= 0) return false;
-  if ((reinterpret_cast<uintptr_t>(a.qs) | reinterpret_cast<uintptr_t>(a.d)) & 15u) return false;
-  // the last slice's scales end on a 16-byte boundary too
-  if (((size_t)a.n_rows * (a.kp / 32) * 2) & 15u) return false;
-  return slice_plan(a, slice_rpw(a)).smem <= kSliceSmemMax;
-}
-
 // ------------------------------------------------ ggml-layout compatibility
 // One warp per weight row, blocks read in place (34 / 18 / 20 bytes, 2-byte
 // aligned), up to 8 input rows per pass.  Serves the drop-in entry points
@@ -1101,10 +836,6 @@ cudaError_t gemv_prepare() {
   if (e == cudaSuccess) e = tma_prepare<QT, RPW>();
   DQMK_TMA_VARIANTS(DQMK_TMA_PREP)
 #undef DQMK_TMA_PREP
-#define DQMK_SLICE_PREP(QT, RPW) \
-  if (e == cudaSuccess) e = slice_prepare<QT, RPW>();
-  DQMK_SLICE_VARIANTS(DQMK_SLICE_PREP)
-#undef DQMK_SLICE_PREP
   return e;
 }
 
@@ -1131,7 +862,6 @@ cudaError_t read_device_error(unsigned int* flags, bool clear) {
 // reads of x.
 int gemv_variant_id(const GemvArgs& a) {
   if (tma_eligible(a)) return -1;
-  if (slice_eligible(a)) return -2;
   const bool wide = a.n_rows >= 32768 && a.epi != kEpiSwiGlu && a.epi != kEpiQkv;
   const int chunks = a.qtype == DQMK_Q80 ? a.kp / 16 : a.kp / 32;
   if (a.qtype == DQMK_Q80) {
@@ -1159,8 +889,6 @@ cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     return launch_t<QT, RPW, CPL, GW>(a, stream, pdl);
     DQMK_GEMV_VARIANT_IDS(DQMK_LAUNCH_CASE)
 #undef DQMK_LAUNCH_CASE
-    case -2:
-      return slice_dispatch(a, stream, pdl);
     default:
       return tma_dispatch(a, stream, pdl, -1);
   }

@@ -412,8 +412,9 @@ __device__ __forceinline__ void logits_finish(const GemvArgs& a, unsigned long l
 }
 
 // One GEMV on one CTA of a grid of n_ctas, in two parts: prefetch() computes
-// the CTA's share of row groups and loads its first weight tile and the
-// RMSNorm weight into registers -- none of it depends on the previous step of
+// the CTA's share of row groups and loads its first two weight tiles into
+// registers and the RMSNorm weight into shared memory -- none of it depends
+// on the previous step of
 // the chain, so callers issue it before griddepcontrol.wait; run() stages x
 // and does the math and the epilogue.
 template <int QT, int RPW, int CPL, int GW>
@@ -440,7 +441,10 @@ struct GemvPhase {
     const int n_groups = (a.n_rows + RPW - 1) / RPW;
     const int my_groups = g.gw < n_groups ? (n_groups - g.gw + g.nw - 1) / g.nw : 0;
     total = my_groups * g.nseg;
+    // the warp's first two tiles: both are in flight before the dependency
+    // resolves (the tile registers exist for the two-stage pipeline anyway)
     if (total > 0) load_step<QT, RPW, CPL, GT>(ta, a, g, 0, gt);
+    if (total > 1) load_step<QT, RPW, CPL, GT>(tb, a, g, 1, gt);
     norm_pref = a.norm_w && (a.kp >> 2) <= kNormRegs * kWarps * 32 && ((a.k & 3) == 0) &&
                 ((reinterpret_cast<uintptr_t>(a.norm_w) & 15u) == 0);
     if (norm_pref) {
@@ -509,7 +513,7 @@ __device__ __forceinline__ void gemv_run(GemvPhase<QT, RPW, CPL, GW>& ph, const 
 
   // two-stage register pipeline: load step s+1 while step s computes
   for (int s = 0; s < total; s += 2) {
-    if (s + 1 < total) load_step<QT, RPW, CPL, GT>(tb, a, g, s + 1, gt);
+    if (s + 1 < total && s > 0) load_step<QT, RPW, CPL, GT>(tb, a, g, s + 1, gt);
     compute_step<QT, RPW, CPL, GT>(ta, g, s, gt, xs, acc);
     finish(s);
     if (s + 1 < total) {
