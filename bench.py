@@ -688,8 +688,9 @@ def kernel_sample(pkg, torch):
     """One small launch of every kernel kind of the library, for profiling
     runs (ncu -k regex:... on this mode): quantize / dequantize / pack, the
     ggml-layout Linears (Q8_0, Q4_0, Q4_1, F32), the packed GEMV and the
-    TMA-staged lm_head GEMV, decode attention over a 2048-position cache and
-    over an odd head shape, one Qwen2-0.5B-architecture decode step (embed,
+    TMA-staged lm_head GEMV, the standalone ops (RMSNorm, SiLU, SwiGLU, add,
+    multiply, softmax, argmax, RoPE, embedding lookup, KV write), decode
+    attention over a 2048-position cache and over an odd head shape, one Qwen2-0.5B-architecture decode step (embed,
     QKV / O / gate-up / down GEMVs, short-cache attention, lm_head), a
     128-token batched prefill (activation split, tensor-core GEMM, split-K
     epilogue, causal attention, weight split), and one 64-column step of a
@@ -709,6 +710,21 @@ def kernel_sample(pkg, torch):
         fn[qt](xs, blocks, (4864, 896))
     pkg.CudaLinear(np.random.default_rng(0).standard_normal(896).astype(np.float32),
                    np.random.default_rng(1).standard_normal((4864, 896)).astype(np.float32))
+    # the standalone ops of the drop-in boundary
+    v = torch.randn(4864, device="cuda")
+    w = torch.randn(4864, device="cuda")
+    pkg.CudaRmsNormDeviceWeight(v, w, 1e-6)
+    pkg.CudaSiluMulDeviceInput(v, w)
+    pkg.CudaElementwiseAddDeviceInput(v, w)
+    out = torch.empty_like(v)
+    for name, args in (("dqmk_silu", (v.data_ptr(), v.numel(), out.data_ptr(), None)),
+                       ("dqmk_mul", (v.data_ptr(), w.data_ptr(), v.numel(), out.data_ptr(), None)),
+                       ("dqmk_softmax", (v.data_ptr(), v.numel(), out.data_ptr(), None))):
+        pkg.check(getattr(pkg.lib(), name)(*args))
+    pkg.argmax(v)
+    q, k = torch.randn(14 * 64, device="cuda"), torch.randn(2 * 64, device="cuda")
+    pkg.CudaRopeDeviceInput(q, k, 14, 2, 64, 5, 1e6)
+    pkg.CudaEmbeddingLookupDeviceWeight(torch.randn(1024, 896, device="cuda"), 7)
     # decode attention outside the chain: a 2048-position cache (split over
     # the SMs, merged by the last CTA) and a head shape only the general
     # kernel takes
@@ -718,6 +734,8 @@ def kernel_sample(pkg, torch):
         kv.values.normal_()
         q = torch.randn(n_heads * hd, device="cuda")
         pkg.CudaAttentionDecodeDeviceInput(q, kv, 0, pos, n_heads, n_kv, hd)
+        kv.WriteDevice(0, 0, torch.randn(n_kv * hd, device="cuda"),
+                       torch.randn(n_kv * hd, device="cuda"))
     w = S.make_model(S.QWEN2_0_5B, S.Q80, MODEL_SEED,
                      quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
     model = pkg.Model.from_synth(w, max_seq_len=N_PROMPT + N_DECODE_POS)

@@ -17,7 +17,6 @@
 
 #include "attention_dev.cuh"
 #include "common.cuh"
-#include "gemv_dev.cuh"
 #include "internal.h"
 
 namespace dqmk {
@@ -248,113 +247,6 @@ __global__ void __launch_bounds__(256) attention_short_kernel(const AttnArgs a) 
   short_head<HD>(a, kvh, head, reinterpret_cast<float4*>(a.out + (size_t)head * HD), ss, red);
 }
 
-// ============================================ attention fused with the O GEMV
-// Decode step over a short cache (at most kShortMax positions): one CTA per
-// query head computes the head's attention (short_head) and right away its
-// share of the O projection, out_h = Wo[:, head columns] . attn_h, from the
-// Wo column slice it copied into shared memory (cp.async, before the
-// dependency wait: weights are constant across the step).  The per-head
-// partial rows go to part[head][rows]; the CTA that takes the last ticket
-// sums them in head order, adds the residual in place and resets the
-// ticket.  One launch replaces attention + O GEMV, so the step loses one
-// dependent link per layer.
-//
-// Reference: src/forward.cc:461-506 (attention), :344-366 (O projection and
-// residual).  The O sum is taken per head and then across heads, a different
-// float summation order from the reference's single chain over
-// n_heads * head_dim (agreement to rounding, as for every GEMV here).
-__device__ __forceinline__ void cp_async4(void* smem_dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
-               "l"(src)
-               : "memory");
-}
-
-template <int HD, int QT>
-struct OSlice {
-  static constexpr int SEG = QT == DQMK_Q80 ? HD : HD / 2;  // bytes of a row's head columns
-  static constexpr int CPR = SEG / 16;                      // 16-byte chunks per row slice
-  static constexpr int RPL = CPR >= 8 ? 1 : 8 / CPR;        // rows per 128-byte line
-  static constexpr int NBH = HD / 32;                       // scale blocks per row slice
-  // chunk c of row r sits in slot c ^ f(r): the 8 lanes of a 16-byte shared
-  // load phase (consecutive rows, same chunk) hit 8 distinct 16-byte banks
-  __host__ __device__ static int slot(int r, int c) { return c ^ ((r / RPL) & (CPR - 1)); }
-  static size_t smem(int rows) {
-    return (size_t)rows * SEG + (((size_t)rows * NBH * 2 + 15) & ~(size_t)15);
-  }
-};
-
-template <int HD, int QT>
-__global__ void __launch_bounds__(256) attention_o_kernel(const AttnOArgs o) {
-  using SS = ShortShape<HD>;
-  using OS = OSlice<HD, QT>;
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ float ss[kShortMax];
-  __shared__ float4 red[SS::NG][SS::D4];
-  __shared__ __align__(16) float sa[HD];
-  __shared__ int s_last;
-  const AttnArgs& a = o.at;
-  const int tid = threadIdx.x;
-  const int head = blockIdx.x, G = a.n_heads / a.n_kv_heads;
-  const int kvh = head / G;
-  const int rows = o.rows;
-  const int row_bytes = QT == DQMK_Q80 ? o.kp : o.kp / 2;
-  const int nbk = o.kp / 32;
-  unsigned char* wq = smem;
-  uint16_t* wd = reinterpret_cast<uint16_t*>(smem + (size_t)rows * OS::SEG);
-
-  // ---- before the dependency: this head's Wo columns and their scales
-  for (int i = tid; i < rows * OS::CPR; i += 256) {
-    const int r = i / OS::CPR, c = i % OS::CPR;
-    gv::cp_async16(wq + (size_t)r * OS::SEG + OS::slot(r, c) * 16,
-                   o.qs + (size_t)r * row_bytes + (size_t)head * OS::SEG + c * 16);
-  }
-  for (int i = tid; i < rows * (OS::NBH / 2); i += 256) {
-    const int r = i / (OS::NBH / 2), u = i % (OS::NBH / 2);
-    cp_async4(wd + (size_t)r * OS::NBH + 2 * u, o.d + (size_t)r * nbk + (size_t)head * OS::NBH + 2 * u);
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  pdl_trigger();
-  pdl_wait();
-
-  short_head<HD>(a, kvh, head, reinterpret_cast<float4*>(sa), ss, red);
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-
-  // ---- this head's share of every O row
-  const float4* sa4 = reinterpret_cast<const float4*>(sa);
-  for (int r = tid; r < rows; r += 256) {
-    float acc = 0.0f;
-#pragma unroll
-    for (int c = 0; c < OS::CPR; ++c) {
-      const uint4 w = *reinterpret_cast<const uint4*>(wq + (size_t)r * OS::SEG + OS::slot(r, c) * 16);
-      float4 xv[8];
-      if constexpr (QT == DQMK_Q80) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) xv[i] = sa4[c * 4 + i];
-        acc = fmaf(h2f(wd[r * OS::NBH + (c >> 1)]), gv::dot_q8(w, xv), acc);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xv[i] = sa4[c * 8 + i];
-        acc = fmaf(h2f(wd[r * OS::NBH + c]), gv::dot_q4(w, xv), acc);
-      }
-    }
-    o.part[(size_t)head * rows + r] = acc;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(o.ticket, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = tid; i < rows; i += 256) {
-    float sum = 0.0f;
-    for (int h = 0; h < (int)gridDim.x; ++h) sum += __ldcg(o.part + (size_t)h * rows + i);
-    o.x[i] = __fadd_rn(__ldcg(o.x + i), sum);
-  }
-  if (tid == 0) *o.ticket = 0u;
-}
-
 // Any head_dim that is a multiple of 4 up to 256: one thread per position.
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a, int chunk_cap) {
   extern __shared__ float sm[];
@@ -505,14 +397,6 @@ size_t attention_partials_floats(int n_heads, int head_dim, int max_splits) {
   return (size_t)n_heads * max_splits * part_stride(head_dim);
 }
 
-constexpr size_t kAttnOSmemMax = 160 * 1024;
-
-size_t attention_o_smem(int head_dim, int qtype, int rows) {
-  if (head_dim == 64)
-    return qtype == DQMK_Q80 ? OSlice<64, DQMK_Q80>::smem(rows) : OSlice<64, DQMK_Q40>::smem(rows);
-  return qtype == DQMK_Q80 ? OSlice<128, DQMK_Q80>::smem(rows) : OSlice<128, DQMK_Q40>::smem(rows);
-}
-
 cudaError_t attention_prepare() {
   static DeviceOnce once;
   return once.run([] {
@@ -530,13 +414,6 @@ cudaError_t attention_prepare() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attention_hd_head_kernel<128>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-#define DQMK_AO_ATTR(HD, QT)                                                              \
-    if (e == cudaSuccess)                                                                 \
-      e = cudaFuncSetAttribute(attention_o_kernel<HD, QT>,                                \
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnOSmemMax);
-    DQMK_AO_ATTR(64, DQMK_Q80) DQMK_AO_ATTR(64, DQMK_Q40) DQMK_AO_ATTR(128, DQMK_Q80)
-    DQMK_AO_ATTR(128, DQMK_Q40)
-#undef DQMK_AO_ATTR
     return e;
   });
 }
@@ -658,30 +535,6 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
   if (hd_kernel && a.head_dim == 128)
     return launch(attention_hd_kernel<128>, grid, dim3(256), smem, stream, pdl, a, cap);
   return launch(attention_kernel, grid, dim3(kThreads), smem, stream, pdl, a, cap);
-}
-
-bool attention_o_supported(int head_dim, int n_heads, int n_kv_heads, int max_seq, int wo_qtype,
-                           int rows, int kp) {
-  if (head_dim != 64 && head_dim != 128) return false;
-  if (n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || max_seq > kShortMax) return false;
-  if (attention_splits(max_seq, n_kv_heads) != 1) return false;
-  if (wo_qtype != DQMK_Q80 && wo_qtype != DQMK_Q40) return false;
-  if (kp != n_heads * head_dim || (kp / 32) % 2 != 0) return false;
-  return attention_o_smem(head_dim, wo_qtype, rows) <= kAttnOSmemMax;
-}
-
-cudaError_t launch_attention_o(const AttnOArgs& o, cudaStream_t stream, bool pdl) {
-  cudaError_t e = attention_prepare();
-  if (e != cudaSuccess) return e;
-  const size_t smem = attention_o_smem(o.at.head_dim, o.qtype, o.rows);
-  const dim3 grid(o.at.n_heads);
-  if (o.at.head_dim == 64)
-    return o.qtype == DQMK_Q80
-               ? launch(attention_o_kernel<64, DQMK_Q80>, grid, dim3(256), smem, stream, pdl, o)
-               : launch(attention_o_kernel<64, DQMK_Q40>, grid, dim3(256), smem, stream, pdl, o);
-  return o.qtype == DQMK_Q80
-             ? launch(attention_o_kernel<128, DQMK_Q80>, grid, dim3(256), smem, stream, pdl, o)
-             : launch(attention_o_kernel<128, DQMK_Q40>, grid, dim3(256), smem, stream, pdl, o);
 }
 
 }  // namespace dqmk

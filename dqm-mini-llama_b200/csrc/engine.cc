@@ -68,17 +68,12 @@ struct dqmk_context {
   std::vector<void*> ipc_opened;
   float *keys = nullptr, *values = nullptr, *partials = nullptr;
   // device state block: [argmax u64][lm ticket u32][token i32][pos i32][pad]
-  //                     [attention tickets u32 x n_kv][attention-O ticket u32][pad]
+  //                     [attention tickets u32 x n_kv][pad]
   unsigned char* state = nullptr;
   int* history_dev = nullptr;
   int* pinned = nullptr;  // host staging: [token, pos]
   cudaEvent_t staged = nullptr;  // recorded after the last copy out of `pinned`
   int attn_splits = 1;
-  // decode step over a short cache: attention fused with the O GEMV
-  // (attention_o_kernel), its per-head partial rows and completion ticket
-  bool attn_o = false;
-  float* o_part = nullptr;
-  unsigned int* o_ticket = nullptr;
   PrefillBufs pf;
   cudaGraphExec_t graph = nullptr;
   int pos = 0;
@@ -544,16 +539,6 @@ extern "C" int dqmk_model_stats_reset(dqmk_model* m) {
 extern "C" size_t dqmk_model_memory_bytes(const dqmk_model* m) { return m ? m->memory_bytes : 0; }
 
 // ------------------------------------------------------------------ context
-// Attention fused with the O GEMV in the decode step where the shapes allow;
-// DQMK_ATTN_O=0 in the environment keeps the two launches (A/B comparisons).
-static bool attention_o_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("DQMK_ATTN_O");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 // Programmatic dependent launch between the kernels of a step; DQMK_PDL=0 in
 // the environment launches them plainly instead (diagnostics: same work).
 bool dqmk::use_pdl() {
@@ -647,43 +632,29 @@ int enqueue_step(dqmk_context* x) {
     at.partials = x->partials;
     at.tickets = x->attn_tickets();
     at.max_splits = x->attn_splits;
-    if (x->attn_o) {  // attention, O projection and residual add in one launch
-      AttnOArgs ao = {};
-      ao.at = at;
-      ao.qtype = L.wo.qtype;
-      ao.qs = L.wo.qs();
-      ao.d = L.wo.d();
-      ao.rows = L.wo.rows;
-      ao.kp = L.wo.kp;
-      ao.part = x->o_part;
-      ao.ticket = x->o_ticket;
-      ao.x = x->x;
-      DQMK_CUDA_RET(api, launch_attention_o(ao, s, pdl));
-    } else {
-      DQMK_CUDA_RET(api, attn_op(at));
+    DQMK_CUDA_RET(api, attn_op(at));
 
-      GemvArgs o = {};
-      o.qtype = L.wo.qtype;
-      o.qs = L.wo.qs();
-      o.d = L.wo.d();
-      o.n_rows = L.wo.rows;
-      o.k = L.wo.k;
-      o.kp = L.wo.kp;
-      o.x = x->att;
-      o.epi = kEpiStore;
-      o.residual = tpar ? nullptr : x->x;
-      o.y = tpar ? x->part : x->x;
-      if (p2p) {  // partial rows straight into every rank's slot
-        o.epi = kEpiPeer;
-        o.peer = ps;
-      }
-      DQMK_CUDA_RET(api, gemv_op(o));
-      if (p2p) {
-        DQMK_CUDA_RET(api, launch_tp_reduce(x->x, ps, s, pdl));
-      } else if (tpar) {  // complete the row-parallel sum, then the residual add
-        if ((rc = tp_allreduce_sum(m->comm, x->part, c.dim, s, api))) return rc;
-        DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
-      }
+    GemvArgs o = {};
+    o.qtype = L.wo.qtype;
+    o.qs = L.wo.qs();
+    o.d = L.wo.d();
+    o.n_rows = L.wo.rows;
+    o.k = L.wo.k;
+    o.kp = L.wo.kp;
+    o.x = x->att;
+    o.epi = kEpiStore;
+    o.residual = tpar ? nullptr : x->x;
+    o.y = tpar ? x->part : x->x;
+    if (p2p) {  // partial rows straight into every rank's slot
+      o.epi = kEpiPeer;
+      o.peer = ps;
+    }
+    DQMK_CUDA_RET(api, gemv_op(o));
+    if (p2p) {
+      DQMK_CUDA_RET(api, launch_tp_reduce(x->x, ps, s, pdl));
+    } else if (tpar) {  // complete the row-parallel sum, then the residual add
+      if ((rc = tp_allreduce_sum(m->comm, x->part, c.dim, s, api))) return rc;
+      DQMK_CUDA_RET(api, launch_add(x->x, x->part, c.dim, x->x, s));
     }
 
     GemvArgs gu = {};
@@ -1086,12 +1057,6 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
   const dqmk_tp_plan& tp = m->tp;
   const size_t kv = (size_t)c.n_layers * c.max_seq_len * tp.n_kv_heads * c.head_dim;
   x->attn_splits = attention_splits(c.max_seq_len, tp.n_kv_heads);
-  x->attn_o = attention_o_enabled() && tp.world == 1;
-  for (int l = 0; l < c.n_layers && x->attn_o; ++l) {
-    const Packed& wo = m->layers[l].wo;
-    x->attn_o = attention_o_supported(c.head_dim, tp.n_q_heads, tp.n_kv_heads, c.max_seq_len,
-                                      wo.qtype, wo.rows, wo.kp);
-  }
   void* p = nullptr;
   int rc;
   const int hd = c.head_dim;
@@ -1107,7 +1072,6 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
               {&x->values, kv},
               {&x->partials, attention_partials_floats(tp.n_q_heads, hd, x->attn_splits)},
               {&x->part, (size_t)c.dim},
-              {&x->o_part, x->attn_o ? (size_t)tp.n_q_heads * c.dim : 1},
               {&x->logits_all, tp.world > 1 ? (size_t)tp.vocab_stride * tp.world : 1}};
   for (auto& b : bufs) {
     if ((rc = dev_alloc(x->allocs, b.n * sizeof(float), &p, api))) return rc;
@@ -1126,7 +1090,6 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
   }
   if ((rc = dev_alloc(x->allocs, 64 + 4 * (size_t)tp.n_kv_heads + 64, &p, api))) return rc;
   x->state = static_cast<unsigned char*>(p);
-  x->o_ticket = reinterpret_cast<unsigned int*>(x->state + 64 + 4 * (size_t)tp.n_kv_heads);
   if ((rc = dev_alloc(x->allocs, (size_t)c.max_seq_len * sizeof(int), &p, api))) return rc;
   x->history_dev = static_cast<int*>(p);
   DQMK_CUDA_RET(api, cudaMemset(x->state, 0, 64 + 4 * (size_t)tp.n_kv_heads + 64));

@@ -222,24 +222,6 @@ struct AttnArgs {
   unsigned int* tickets; // [n_kv_heads], zero at rest
   int max_splits;        // gridDim.y
 };
-// Attention of every query head fused with the O projection and the
-// residual add (decode step, caches of at most 128 positions): one CTA per
-// head writes part[head][rows] = Wo[:, head columns] . attn_head; the last
-// CTA sums the heads in order into x (in place).
-struct AttnOArgs {
-  AttnArgs at;           // out / partials / tickets unused
-  int qtype;             // Wo: DQMK_Q80 or DQMK_Q40, packed
-  const uint8_t* qs;
-  const uint16_t* d;
-  int rows;              // Wo rows (dim)
-  int kp;                // Wo columns = n_heads * head_dim
-  float* part;           // [n_heads][rows]
-  unsigned int* ticket;  // zero at rest
-  float* x;              // residual stream, updated in place
-};
-bool attention_o_supported(int head_dim, int n_heads, int n_kv_heads, int max_seq, int wo_qtype,
-                           int rows, int kp);
-cudaError_t launch_attention_o(const AttnOArgs& o, cudaStream_t stream, bool pdl);
 // Splits (CTAs per KV head along the sequence) used for a cache of max_seq.
 int attention_splits(int max_seq, int n_kv_heads);
 size_t attention_partials_floats(int n_heads, int head_dim, int max_splits);
