@@ -81,9 +81,30 @@ __device__ __forceinline__ void split_combine(const AttnArgs& a, int kvh, int G,
   if (threadIdx.x == 0) a.tickets[kvh] = 0u;
 }
 
+// Rows t0..min(t0 + n, pos) - 1 of this KV head's K and V in the split: those
+// earlier steps wrote, requested into L2 before the dependency wait so the
+// body's loads after it hit L2 (128-byte lines, every thread of the CTA).
+template <int HD>
+__device__ __forceinline__ void prefetch_split_l2(const AttnArgs& a, int kvh, int split, int pos) {
+  const Split sp = split_of(a, split, pos);
+  const int n = min(sp.n, pos - sp.t0);
+  if (n <= 0) return;
+  constexpr int LPR = HD * 4 / 128;  // 128-byte lines per row
+  const size_t row_stride = (size_t)a.n_kv_heads * HD;
+  const size_t base = (size_t)a.layer * a.max_seq * row_stride + (size_t)sp.t0 * row_stride +
+                      (size_t)kvh * HD;
+  for (int i = threadIdx.x; i < 2 * n * LPR; i += blockDim.x) {
+    const int kv = i / (n * LPR), r = (i / LPR) % n, l = i % LPR;
+    const float* p = (kv ? a.values : a.keys) + base + (size_t)r * row_stride + l * 32;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(256) attention_hd_kernel(const AttnArgs a, int chunk_cap) {
   extern __shared__ float sm[];
+  // the position is advanced only between steps: stable across this one
+  prefetch_split_l2<HD>(a, blockIdx.x, blockIdx.y, a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg);
   pdl_trigger();
   pdl_wait();
   attention_hd_body<HD, 256>(a, chunk_cap, blockIdx.x, blockIdx.y, gridDim.y, sm);
@@ -98,6 +119,7 @@ __global__ void __launch_bounds__(256) attention_hd_kernel(const AttnArgs a, int
 template <int HD>
 __global__ void __launch_bounds__(256) attention_hd_head_kernel(const AttnArgs a, int chunk_cap) {
   extern __shared__ float sm[];
+  prefetch_split_l2<HD>(a, blockIdx.x, 0, a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg);
   pdl_trigger();
   pdl_wait();
   const int kvh = blockIdx.x, g = blockIdx.z;
@@ -125,9 +147,12 @@ __global__ void __launch_bounds__(256) attention_hd_head_kernel(const AttnArgs a
 constexpr int kShortMax = 128;
 
 // One query head over a cache of at most kShortMax positions, by a CTA of
-// 256 threads: every load in flight together, scores to shared memory,
-// softmax statistics per warp, P.V in position groups, and the head's output
-// as HD/4 float4 to out4 (global or shared memory).
+// 256 threads.  Rows 0..pos-1 of the cache were written by earlier steps, so
+// they are loaded before the dependency wait (under programmatic dependent
+// launch they arrive while the QKV GEMV that this kernel waits on still
+// runs); after the wait only q and row pos (written by that GEMV) are read.
+// Then scores to shared memory, softmax statistics per warp, P.V in position
+// groups, and the head's output.
 template <int HD>
 struct ShortShape {
   static constexpr int NT = 256;
@@ -140,12 +165,16 @@ struct ShortShape {
 };
 
 template <int HD>
-__device__ __forceinline__ void short_head(const AttnArgs& a, int kvh, int head, float4* out4,
-                                           float* ss, float4 (*red)[ShortShape<HD>::D4]) {
+__global__ void __launch_bounds__(256) attention_short_kernel(const AttnArgs a) {
   using SS = ShortShape<HD>;
   constexpr int TPP = SS::TPP, PPASS = SS::PPASS, NPASS = SS::NPASS, D4 = SS::D4, NG = SS::NG,
                 NPV = SS::NPV;
+  __shared__ float ss[kShortMax];
+  __shared__ float4 red[NG][D4];
+  const int kvh = blockIdx.x, G = a.n_heads / a.n_kv_heads;
+  const int head = kvh * G + blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31;
+  // the position is advanced only between steps: stable across this one
   const int pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
   const int T = pos + 1;
   const size_t row_stride = (size_t)a.n_kv_heads * HD;
@@ -153,25 +182,41 @@ __device__ __forceinline__ void short_head(const AttnArgs& a, int kvh, int head,
   const float* vbase = a.values + (size_t)a.layer * a.max_seq * row_stride + (size_t)kvh * HD;
   const int part = tid % TPP, p0 = tid / TPP;
   const int d4 = tid % D4, grp = tid / D4;
-  // ---- every load in flight together
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  // ---- before the dependency: the rows earlier steps wrote (t < pos)
   float4 qv[4], kr[NPASS][4], vr[NPV];
-  const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)head * HD) + part * 4;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) qv[i] = __ldcg(q4 + i);
 #pragma unroll
   for (int u = 0; u < NPASS; ++u) {
     const int t = p0 + u * PPASS;
     const float4* kp = reinterpret_cast<const float4*>(kbase + (size_t)t * row_stride) + part * 4;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      kr[u][i] = t < T ? __ldcg(kp + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < 4; ++i) kr[u][i] = t < pos ? __ldcg(kp + i) : zero;
   }
 #pragma unroll
   for (int j = 0; j < NPV; ++j) {
     const int t = grp + j * NG;
-    vr[j] = t < T ? __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)t * row_stride) + d4)
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    vr[j] = t < pos ? __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)t * row_stride) + d4)
+                    : zero;
   }
+  pdl_trigger();
+  pdl_wait();
+  // ---- after it: q and row pos
+  const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)head * HD) + part * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qv[i] = __ldcg(q4 + i);
+#pragma unroll
+  for (int u = 0; u < NPASS; ++u) {
+    if (p0 + u * PPASS == pos) {
+      const float4* kp =
+          reinterpret_cast<const float4*>(kbase + (size_t)pos * row_stride) + part * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) kr[u][i] = __ldcg(kp + i);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NPV; ++j)
+    if (grp + j * NG == pos)
+      vr[j] = __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)pos * row_stride) + d4);
   // ---- scores
   const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
 #pragma unroll
@@ -206,7 +251,7 @@ __device__ __forceinline__ void short_head(const AttnArgs& a, int kvh, int head,
   }
   l = warp_sum(l);
   // ---- P.V over this thread's positions
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 acc = zero;
 #pragma unroll
   for (int j = 0; j < NPV; ++j) {
     const int t = grp + j * NG;
@@ -230,21 +275,9 @@ __device__ __forceinline__ void short_head(const AttnArgs& a, int kvh, int head,
       o.z += x.z;
       o.w += x.w;
     }
-    out4[tid] =
+    reinterpret_cast<float4*>(a.out + (size_t)head * HD)[tid] =
         make_float4(__fdiv_rn(o.x, l), __fdiv_rn(o.y, l), __fdiv_rn(o.z, l), __fdiv_rn(o.w, l));
   }
-}
-
-template <int HD>
-__global__ void __launch_bounds__(256) attention_short_kernel(const AttnArgs a) {
-  using SS = ShortShape<HD>;
-  __shared__ float ss[kShortMax];
-  __shared__ float4 red[SS::NG][SS::D4];
-  pdl_trigger();
-  pdl_wait();
-  const int kvh = blockIdx.x, G = a.n_heads / a.n_kv_heads;
-  const int head = kvh * G + blockIdx.z;
-  short_head<HD>(a, kvh, head, reinterpret_cast<float4*>(a.out + (size_t)head * HD), ss, red);
 }
 
 // Any head_dim that is a multiple of 4 up to 256: one thread per position.

@@ -340,7 +340,7 @@ __device__ __forceinline__ void block_term_sums(const int (&w)[8], const int4 (&
   }
 }
 
-__device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+__host__ __device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
 
 // Shared-memory layout of the staged x: fp32 copy, int8 term planes, term
 // scales, term sums; the weight stages follow.
@@ -552,6 +552,348 @@ __global__ void __launch_bounds__(kTmaThreads) gemv_tma_kernel(const GemvArgs a,
   }
 }
 
+// ============================================================= ring GEMV
+// Wide rows (K >= 2048: the Qwen2-7B-class projections).  Two things decide
+// the bandwidth there: bytes in flight per SM and instructions per block.
+//  * Row tiles of TR rows arrive by cp.async.bulk in a ring of up to six
+//    shared-memory stages filled by one producer lane (full / empty
+//    mbarriers, as in gemv_tma_kernel); the first stages are requested
+//    before griddepcontrol.wait, and 100-170 KB stay in flight per SM.
+//  * x stays in registers: consumer warp w owns the 32-block chunk
+//    c = w % nch for the whole kernel (lane l: block 32c + l) and row set
+//    w / nch of every tile.  Each lane loads its block of x once, applies the
+//    fused RMSNorm (one CTA reduction of sum(x^2)), and splits it into the
+//    three int8 terms of quantize_x_terms (same arithmetic, same terms).  A
+//    (row, block) product is then the exact int32 dp4a sums of
+//    block_term_sums scaled by the term scales: no per-row x traffic.
+// Per tile each warp sums its rows over its lanes, the chunk partials meet
+// in shared memory (double-buffered by tile parity, one named barrier of the
+// consumer warps per tile) and are added in chunk order, and the group's
+// epilogue runs on the totals.  Every wait is bounded (as in
+// gemv_tma_kernel); a consumer that gives up marks the tile in a flag that the
+// consumers read after that tile's barrier, so they all leave together.
+constexpr int kRingMaxStages = 6;
+
+// Barrier `id` (1..15) over the first n threads that reach it (n a multiple
+// of 32): the consumer warps of a CTA without its producer warp.
+__device__ __forceinline__ void named_bar(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+struct RingDims {
+  int W;         // consumer warps
+  int nch;       // 32-block chunks of a row
+  int TR;        // rows per tile = row sets x RW
+  int nstage;    // ring stages
+  int rows_cap;  // rows a CTA holds partial sums for: TR x its most tiles
+};
+
+// Sums R per-lane values of R rows over the 32 lanes of a warp with 31
+// fewer shuffles than R separate reductions: each halving stage trades half
+// of the values with the partner lane, so lane l ends with the total of row
+// (l >> (5 - log2 R)) & (R - 1) (every lane of that row alike).
+template <int R>
+__device__ __forceinline__ float transpose_sum(float (&v)[R], int lane) {
+#pragma unroll
+  for (int m = 16, n = R; n > 1; m >>= 1, n >>= 1) {
+    const bool upper = (lane & m) != 0;
+#pragma unroll
+    for (int k = 0; k < n / 2; ++k) {
+      const float send = upper ? v[k] : v[k + n / 2];
+      const float keep = upper ? v[k + n / 2] : v[k];
+      v[k] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+    }
+  }
+#pragma unroll
+  for (int m = 32 / R / 2; m >= 1; m >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+  return v[0];
+}
+template <int R>
+__host__ __device__ constexpr int log2i() {
+  return R <= 1 ? 0 : 1 + log2i<R / 2>();
+}
+
+// The three int8 terms of one 32-value block of x, as quantize_x_terms
+// computes them, by one thread: xv[2t], xv[2t+1] = values 0-15 / 16-31 of
+// term t; sc[t] its scale; sm8[t] = 8 * sum of its values (Q4_0 offset).
+__device__ __forceinline__ void block_x_terms(const float (&v)[32], int4 (&xv)[6], float (&sc)[3],
+                                              int (&sm8)[3]) {
+  float m = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(v[e]));
+  float r[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) r[e] = v[e];
+  float s = m > 0.0f ? __fdiv_rn(m, 127.0f) : 0.0f;
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+    uint32_t wd[8];
+    int tsum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int qq = __float2int_rn(__fmul_rn(r[4 * j + e], inv));
+        qq = qq > 127 ? 127 : (qq < -127 ? -127 : qq);
+        r[4 * j + e] = __fmaf_rn(-s, (float)qq, r[4 * j + e]);
+        packed |= ((uint32_t)qq & 0xffu) << (8 * e);
+        tsum += qq;
+      }
+      wd[j] = packed;
+    }
+    xv[2 * t] = make_int4((int)wd[0], (int)wd[1], (int)wd[2], (int)wd[3]);
+    xv[2 * t + 1] = make_int4((int)wd[4], (int)wd[5], (int)wd[6], (int)wd[7]);
+    sc[t] = s;
+    sm8[t] = 8 * tsum;
+    s = __fmul_rn(s, 1.0f / 254.0f);
+  }
+}
+
+template <int QT, int RW, int WMAX, bool PEER>
+__global__ void __launch_bounds__((WMAX + 1) * 32) gemv_ring_kernel(const GemvArgs a,
+                                                                   const RingDims dm) {
+  constexpr int EG = RW >= 8 ? 8 : 4;  // rows per epilogue group
+  constexpr int BB = QT == DQMK_Q80 ? 32 : 16;  // quant bytes of a block
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) uint64_t full[kRingMaxStages];
+  __shared__ __align__(8) uint64_t empty[kRingMaxStages];
+  __shared__ int last_issued[kRingMaxStages];
+  __shared__ float red_norm[WMAX];
+  __shared__ unsigned long long best_w[WMAX];
+  __shared__ int s_abort;
+  __shared__ int c_abort[2];
+
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int W = dm.W, nch = dm.nch, TR = dm.TR, nstage = dm.nstage;
+  const bool producer = wid == W;
+  const int nbk = a.kp / 32;
+  const size_t row_bytes = (size_t)nbk * BB;
+  const size_t q_stage = (size_t)TR * row_bytes;
+  const size_t stage_bytes = q_stage + align16((size_t)TR * nbk * 2);
+  const int n_tiles = (a.n_rows + TR - 1) / TR;
+  const int my_tiles =
+      (int)blockIdx.x < n_tiles ? (n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                                : 0;
+  float* red = reinterpret_cast<float*>(smem);  // [nch][rows_cap] partial row sums
+  unsigned char* stages = smem + align16((size_t)nch * dm.rows_cap * 4);
+  volatile int* abort = &s_abort;
+
+  if (producer && lane == 0) {
+    for (int s = 0; s < nstage; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], W);
+      last_issued[s] = -1;
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_abort = 0;
+    c_abort[0] = c_abort[1] = 0;
+  }
+  __syncthreads();
+
+  // Issue the copies of local tile i into stage s (producer lane 0).
+  auto issue = [&](int i, int s, uint64_t policy) {
+    const int tile = blockIdx.x + i * gridDim.x;
+    const int r0 = tile * TR;
+    const int rows = min(TR, a.n_rows - r0);
+    const uint32_t qbytes = (uint32_t)((size_t)rows * row_bytes);
+    const uint32_t dbytes = (uint32_t)rows * nbk * 2;
+    const uint32_t dbulk = (dbytes & 15u) == 0 ? dbytes : 0u;  // ragged: read in place
+    unsigned char* st = stages + (size_t)s * stage_bytes;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(&full[s], qbytes + dbulk);
+    bulk_g2s(st, a.qs + (size_t)r0 * row_bytes, qbytes, &full[s], policy);
+    if (dbulk)
+      bulk_g2s(st + q_stage, reinterpret_cast<const unsigned char*>(a.d) + (size_t)r0 * nbk * 2,
+               dbulk, &full[s], policy);
+    last_issued[s] = i;
+  };
+
+  uint64_t policy = 0;
+  if (producer && lane == 0) {
+    policy = evict_first_policy();
+    const int pre = min(nstage, my_tiles);
+    for (int i = 0; i < pre; ++i) issue(i, i, policy);
+  }
+  // consumer lane: its block of x, and of the RMSNorm weight (constant:
+  // fetched before the dependency wait)
+  const int c = producer ? 0 : wid % nch, rs = producer ? 0 : wid / nch;
+  const int b = c * 32 + lane;
+  const bool bok = !producer && b < nbk;
+  float4 nw[8];
+  if (a.norm_w && bok) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) nw[u] = __ldg(reinterpret_cast<const float4*>(a.norm_w) + b * 8 + u);
+  }
+  pdl_trigger();
+  pdl_wait();
+
+  unsigned long long best = 0ull;
+  if (producer) {
+    if (lane == 0) {
+      for (int i = nstage; i < my_tiles; ++i) {
+        const int s = i % nstage;
+        const uint32_t parity = (uint32_t)(i / nstage - 1) & 1u;
+        if (!tc::bar_wait(&empty[s], parity, abort, &g_device_error, 32)) break;
+        issue(i, s, policy);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- x: this lane's block, RMS-normalised, as three int8 terms
+    float v[32];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float4 t4 = bok ? __ldcg(reinterpret_cast<const float4*>(a.x) + b * 8 + u)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * u] = t4.x;
+      v[4 * u + 1] = t4.y;
+      v[4 * u + 2] = t4.z;
+      v[4 * u + 3] = t4.w;
+    }
+    if (a.norm_w) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) ss = __fadd_rn(ss, __fmul_rn(v[e], v[e]));
+      ss = warp_sum(ss);
+      if (rs == 0 && lane == 0) red_norm[c] = ss;
+      named_bar(1, W * 32);
+      float tot = 0.0f;
+      for (int k = 0; k < nch; ++k) tot += red_norm[k];
+      const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)a.k), a.eps)));
+      if (bok) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          v[4 * u] = __fmul_rn(__fmul_rn(v[4 * u], scale), nw[u].x);
+          v[4 * u + 1] = __fmul_rn(__fmul_rn(v[4 * u + 1], scale), nw[u].y);
+          v[4 * u + 2] = __fmul_rn(__fmul_rn(v[4 * u + 2], scale), nw[u].z);
+          v[4 * u + 3] = __fmul_rn(__fmul_rn(v[4 * u + 3], scale), nw[u].w);
+        }
+      }
+    }
+    int4 xv[6];
+    float sc[3];
+    int sm8[3];
+    block_x_terms(v, xv, sc, sm8);
+    if constexpr (QT == DQMK_Q80) sm8[0] = sm8[1] = sm8[2] = 0;
+    int pos = 0;
+    if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+
+    for (int i = 0; i < my_tiles; ++i) {
+      const int s = i % nstage;
+      const uint32_t phase = (uint32_t)(i / nstage) & 1u;
+      bool ok = tc::bar_wait(&full[s], phase, abort, &g_device_error);
+      ok = __all_sync(0xffffffffu, ok);
+      const int tile = blockIdx.x + i * gridDim.x;
+      const int r0 = tile * TR;
+      const int rows = min(TR, a.n_rows - r0);
+      float acc[RW];
+#pragma unroll
+      for (int j = 0; j < RW; ++j) acc[j] = 0.0f;
+      if (ok && bok) {
+        const unsigned char* sq = stages + (size_t)s * stage_bytes;
+        const uint16_t* sd = reinterpret_cast<const uint16_t*>(sq + q_stage);
+        const bool d_smem = (((uint32_t)rows * nbk * 2) & 15u) == 0;
+#pragma unroll
+        for (int j = 0; j < RW; ++j) {
+          const int rl = rs * RW + j;
+          if (rl < rows) {
+            const unsigned char* p = sq + (size_t)rl * row_bytes + (size_t)b * BB;
+            int w[8];
+            if constexpr (QT == DQMK_Q80) {
+              const uint4 w0 = *reinterpret_cast<const uint4*>(p);
+              const uint4 w1 = *reinterpret_cast<const uint4*>(p + 16);
+              w[0] = (int)w0.x; w[1] = (int)w0.y; w[2] = (int)w0.z; w[3] = (int)w0.w;
+              w[4] = (int)w1.x; w[5] = (int)w1.y; w[6] = (int)w1.z; w[7] = (int)w1.w;
+            } else {
+              const uint4 pq = *reinterpret_cast<const uint4*>(p);
+              const uint32_t pw[4] = {pq.x, pq.y, pq.z, pq.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                w[k] = (int)(pw[k] & 0x0f0f0f0fu);
+                w[4 + k] = (int)((pw[k] >> 4) & 0x0f0f0f0fu);
+              }
+            }
+            const uint16_t dv =
+                d_smem ? sd[rl * nbk + b] : __ldg(a.d + (size_t)(r0 + rl) * nbk + b);
+            // the three terms' sums as six independent dp4a chains of four
+            // (values 0-15 and 16-31 apart), the integer results of
+            // block_term_sums
+            int lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+#pragma unroll
+              for (int k = 0; k < 3; ++k) {
+                const int4 xl = xv[2 * k], xh = xv[2 * k + 1];
+                lo[k] = __dp4a(w[q], q == 0 ? xl.x : q == 1 ? xl.y : q == 2 ? xl.z : xl.w, lo[k]);
+                hi[k] = __dp4a(w[4 + q], q == 0 ? xh.x : q == 1 ? xh.y : q == 2 ? xh.z : xh.w,
+                               hi[k]);
+              }
+            }
+            float blk = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 3; ++k) blk = __fmaf_rn(sc[k], (float)(lo[k] + hi[k] - sm8[k]), blk);
+            acc[j] = __fmaf_rn(h2f(dv), blk, acc[j]);
+          }
+        }
+      }
+      // every shared-memory read of stage s has returned: hand it back
+      __syncwarp();
+      if (!ok) {
+        if (lane == 0) c_abort[0] = 1;
+        break;
+      }
+      if (lane == 0) tc::bar_arrive(&empty[s]);
+      // this warp's chunk of the tile's rows: lane l ends with row j(l)
+      const float tot = transpose_sum<RW>(acc, lane);
+      if ((lane & (32 / RW - 1)) == 0) {
+        const int j = (lane >> (5 - log2i<RW>())) & (RW - 1);
+        red[(size_t)c * dm.rows_cap + i * TR + rs * RW + j] = tot;
+      }
+    }
+    // ---- every partial is in: chunks added in order, epilogues by groups
+    named_bar(1, W * 32);
+    if (!c_abort[0]) {
+      for (int gg = wid; gg < my_tiles * TR / EG; gg += W) {
+        const int i = gg * EG / TR;
+        const int row0 = (blockIdx.x + i * gridDim.x) * TR + (gg * EG) % TR;
+        float e8[EG];
+#pragma unroll
+        for (int r = 0; r < EG; ++r) {
+          float t = 0.0f;
+          for (int k = 0; k < nch; ++k) t += red[(size_t)k * dm.rows_cap + gg * EG + r];
+          e8[r] = t;
+        }
+        epilogue<EG, PEER>(a, row0 / EG, lane, e8, pos, best);
+      }
+    }
+  }
+  if (a.epi == kEpiLogits && !producer) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) best_w[wid] = best;
+  }
+  __syncthreads();
+  if (*abort && producer && lane == 0) {
+    // every role has stopped; let each copy still in flight land before the
+    // CTA's shared memory goes away
+    volatile int never = 0;
+    for (int s = 0; s < nstage; ++s)
+      if (last_issued[s] >= 0)
+        tc::bar_wait(&full[s], (uint32_t)(last_issued[s] / nstage) & 1u, &never,
+                     &g_device_error);
+  }
+  if (a.epi == kEpiLogits && tid == 0) {
+    unsigned long long bb = 0ull;
+    for (int w = 0; w < W; ++w) bb = best_w[w] > bb ? best_w[w] : bb;
+    logits_finish(a, bb, gridDim.x, &g_device_error);
+  }
+}
+
 // Test hook behind dqmk_lm_head_block_sums: x (k floats) split into the three
 // int8 terms by quantize_x_terms, then every (row, block) of a packed weight
 // summed against them with block_term_sums -- the integer arithmetic of
@@ -704,6 +1046,123 @@ bool tma_eligible(const GemvArgs& a) {
   return a.qtype == DQMK_Q80 && a.kp <= 8192 && a.n_rows >= 32768 && a.epi != kEpiPeer;
 }
 
+// ------------------------------------------------------ ring GEMV launches
+// Every instantiation: X(quant type, rows per warp and tile, max consumer warps).
+#define DQMK_RING_VARIANTS(X) \
+  X(DQMK_Q40, 8, 16) X(DQMK_Q40, 8, 24) X(DQMK_Q80, 4, 16) X(DQMK_Q80, 4, 24)
+
+struct RingPlan {
+  RingDims dm{};
+  int rw = 0, wmax = 0;
+  size_t smem = 0;
+  bool ok = false;
+};
+
+// Consumer warps: one per 32-block chunk, times as many row sets as fit in
+// the target warp count, or one per chunk up to 24 chunks.  Stages:
+// as many as fit 200 KB of shared memory, up to six.
+RingPlan ring_plan(const GemvArgs& a, int rw, int wt) {
+  RingPlan p;
+  const int nbk = a.kp / 32, nch = (nbk + 31) / 32;
+  const int rs = nch <= wt ? wt / nch : 1;
+  const int W = rs * nch;
+  if (W > 24) return p;
+  const size_t row_bytes = (size_t)nbk * (a.qtype == DQMK_Q80 ? 32 : 16);
+  const int TR = rs * rw;
+  const size_t stage = (size_t)TR * row_bytes + align16((size_t)TR * nbk * 2);
+  // partial row sums of a CTA's rows: at most ceil(tiles / grid) tiles each,
+  // the grid being at least min(tiles, SM count)
+  const int n_tiles = (a.n_rows + TR - 1) / TR;
+  const int min_grid = std::min(n_tiles, sm_count());
+  const int rows_cap = (n_tiles + min_grid - 1) / min_grid * TR;
+  const size_t red = align16((size_t)nch * rows_cap * 4);
+  const size_t budget = 200 * 1024;
+  if (red + 2 * stage > budget) return p;
+  int ns = (int)((budget - red) / stage);
+  if (ns > kRingMaxStages) ns = kRingMaxStages;
+  p.dm = RingDims{W, nch, TR, ns, rows_cap};
+  p.rw = rw;
+  p.wmax = W <= 16 ? 16 : 24;
+  p.smem = red + (size_t)ns * stage;
+  p.ok = true;
+  return p;
+}
+
+// Rows per warp and tile, and consumer warps aimed at (16: enough warps per
+// SM to hide the dp4a and shared-memory latencies of one CTA per SM), from a
+// sweep of 8/16/24 warps and 4/8 rows at the Qwen2-7B shapes.
+int ring_rw(const GemvArgs& a) { return a.qtype == DQMK_Q40 ? 8 : 4; }
+int ring_wt(const GemvArgs&) { return 16; }
+
+template <int QT, int RW, int WMAX, bool PEER>
+cudaError_t ring_prepare(const RingPlan* p, int* resident_out) {
+  static DeviceOnce once;
+  cudaError_t e = once.run([] {
+    return cudaFuncSetAttribute(gemv_ring_kernel<QT, RW, WMAX, PEER>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (e != cudaSuccess || !p) return e;
+  static std::mutex mu;
+  static size_t occ_key[kMaxDevices];
+  static int occ[kMaxDevices];
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  const size_t key = p->smem * 64 + (size_t)p->dm.W;
+  std::lock_guard<std::mutex> lock(mu);
+  if (occ_key[dev] != key) {
+    int n = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_ring_kernel<QT, RW, WMAX, PEER>,
+                                                      (p->dm.W + 1) * 32, p->smem);
+    if (e != cudaSuccess) return e;
+    occ[dev] = n > 0 ? n : 1;
+    occ_key[dev] = key;
+  }
+  *resident_out = occ[dev];
+  return cudaSuccess;
+}
+
+template <int QT, int RW, int WMAX, bool PEER>
+cudaError_t ring_launch(const GemvArgs& a, const RingPlan& p, cudaStream_t stream, bool pdl) {
+  int resident = 1;
+  cudaError_t e = ring_prepare<QT, RW, WMAX, PEER>(&p, &resident);
+  if (e != cudaSuccess) return e;
+  const int n_tiles = (a.n_rows + p.dm.TR - 1) / p.dm.TR;
+  const int grid = std::min(n_tiles, sm_count() * resident);
+  return launch(gemv_ring_kernel<QT, RW, WMAX, PEER>, dim3(grid), dim3((p.dm.W + 1) * 32),
+                p.smem, stream, pdl, a, p.dm);
+}
+
+// Shapes the ring form takes, where it measured faster than the register and
+// TMA forms (HBM-cold weights, back-to-back launches on a B200): Q4_0 with at
+// least 65536 rows (a Qwen2-7B-class lm_head: 0.54 vs 0.41 of HBM) and Q8_0
+// rows of at least 8192 values on fewer than 32768 rows (3584 x 18944: 0.55 vs
+// 0.39).  The Qwen2-7B QKV / O / gate-up shapes stay with the register and
+// TMA forms (ring 0.12 / 0.38 / 0.60 vs 0.24 / 0.38 / 0.67).  Further: whole
+// 32-value blocks of x (k == kp), rows of at most 24576 values, 16-byte
+// aligned x and RMSNorm weight, not the peer-memory epilogue.
+bool ring_eligible(const GemvArgs& a) {
+  if (a.epi == kEpiPeer) return false;
+  const bool tall_q4 = a.qtype == DQMK_Q40 && a.n_rows >= 65536;
+  const bool wide_q8 = a.qtype == DQMK_Q80 && a.kp >= 8192 && a.n_rows < 32768;
+  if (!tall_q4 && !wide_q8) return false;
+  if (a.kp < 2048 || a.kp > 24576 || a.k != a.kp) return false;
+  if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.norm_w)) & 15u)
+    return false;
+  return ring_plan(a, ring_rw(a), ring_wt(a)).ok;
+}
+
+cudaError_t ring_dispatch(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  const RingPlan p = ring_plan(a, ring_rw(a), ring_wt(a));
+  if (!p.ok) return cudaErrorInvalidValue;
+#define DQMK_RING_CASE(QT, RW, WMAX)                 \
+  if (a.qtype == QT && p.rw == RW && p.wmax == WMAX) \
+    return ring_launch<QT, RW, WMAX, false>(a, p, stream, pdl);
+  DQMK_RING_VARIANTS(DQMK_RING_CASE)
+#undef DQMK_RING_CASE
+  return cudaErrorInvalidValue;
+}
+
 // ------------------------------------------------ ggml-layout compatibility
 // One warp per weight row, blocks read in place (34 / 18 / 20 bytes, 2-byte
 // aligned), up to 8 input rows per pass.  Serves the drop-in entry points
@@ -836,6 +1295,10 @@ cudaError_t gemv_prepare() {
   if (e == cudaSuccess) e = tma_prepare<QT, RPW>();
   DQMK_TMA_VARIANTS(DQMK_TMA_PREP)
 #undef DQMK_TMA_PREP
+#define DQMK_RING_PREP(QT, RW, WMAX)                                              \
+  if (e == cudaSuccess) e = ring_prepare<QT, RW, WMAX, false>(nullptr, nullptr);
+  DQMK_RING_VARIANTS(DQMK_RING_PREP)
+#undef DQMK_RING_PREP
   return e;
 }
 
@@ -883,6 +1346,7 @@ int gemv_variant_id(const GemvArgs& a) {
 }
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  if (ring_eligible(a)) return ring_dispatch(a, stream, pdl);
   switch (gemv_variant_id(a)) {
 #define DQMK_LAUNCH_CASE(ID, QT, RPW, CPL, GW) \
   case ID:                                     \

@@ -198,6 +198,31 @@ def test_gemv_sweep_vs_golden_and_oracle(pkg, orc, S, cuda, case):
         assert_close(y_packed, ref, key + " packed vs oracle")
 
 
+@pytest.mark.parametrize("qt", [1, 2], ids=["q8_0", "q4_0"])
+@pytest.mark.parametrize("rows,k", [(4100, 3584), (1000, 18944), (520, 2048), (65600, 2048)])
+def test_gemv_wide_rows_vs_oracle(pkg, orc, S, cuda, qt, rows, k):
+    """Rows of 2048 values and more (the Qwen2-7B widths; ragged row counts that
+    leave a partial tile; a tall Q4_0 weight and wide Q8_0 rows, which take
+    the shared-memory ring form): packed GEMV with a residual add, and the
+    chained form with RMSNorm and SwiGLU over interleaved gate/up rows, both
+    against the oracle within the reference's CUDA-test tolerance (1e-3
+    absolute or relative)."""
+    blocks, x = S.gemv_case(rows, k, 40 + rows % 7, qt)
+    rng = np.random.default_rng(rows)
+    res = rng.standard_normal(rows).astype(np.float32)
+    packed = pkg.pack_weight(qt, cuda.from_numpy(blocks).cuda(), rows, k)
+    xd = cuda.from_numpy(x).cuda()
+    rd = cuda.from_numpy(res).cuda()
+    y = pkg.gemv_packed(qt, xd, packed, rows, residual=rd, y=rd).cpu().numpy()
+    assert_close(y, res + orc.linear(qt, x, blocks, rows), f"q{qt} {rows}x{k} residual")
+    nw = (1 + 0.02 * rng.standard_normal(k)).astype(np.float32)
+    yo = cuda.empty(rows // 2, dtype=cuda.float32, device="cuda")
+    pkg.gemv_packed_chained(qt, xd, packed, rows, yo, norm=cuda.from_numpy(nw).cuda(),
+                            swiglu=True)
+    lin = orc.linear(qt, orc.rmsnorm(x, nw, 1e-6), blocks, rows)
+    assert_close(yo.cpu().numpy(), orc.swiglu(lin[0::2], lin[1::2]), f"q{qt} {rows}x{k} swiglu")
+
+
 def test_gemv_residual_and_bias(pkg, orc, S, cuda):
     blocks, x = S.gemv_case(300, 896, 9)
     rng = np.random.default_rng(1)

@@ -82,3 +82,32 @@ def test_tensor_parallel_matches_oracle(cuda, reference, tmp_path):
         for (wb, pb), b in results.items():
             assert float(np.abs(a["logits"] - b["logits"]).max()) <= 1e-3 * rng
             assert a["tokens"].tolist() == b["tokens"].tolist()
+
+
+def test_reduced_7b_one_gpu_matches_oracle(pkg, cuda, reference):
+    """The same reduced Qwen2-7B-shaped model on one GPU (no sharding): its
+    batch-1 decode runs every projection at the 7B widths (QKV 4608x3584 with
+    bias, RoPE and KV store; O 3584x3584; gate/up 37888x3584 with RMSNorm and
+    SwiGLU; down 3584x18944 with the residual; lm_head 8192x3584 with the
+    device argmax).  Prompt logits within 1e-3 x logit range of the oracle,
+    greedy tokens equal to the oracle's, and a later step's logits within
+    1e-3 x range."""
+    S = pkg.synth
+    first_logits, ref_tokens, last_logits, margin = reference
+    w, prompt = tp_worker.reduced_7b(S)
+    r = tp_worker.REDUCED_7B
+    model = pkg.Model.from_synth(w, max_seq_len=r["n_prompt"] + r["n_steps"])
+    ctx = pkg.Context(model)
+    logits = ctx.ForwardBatch(prompt, 0)
+    rng = float(first_logits.max() - first_logits.min())
+    err = float(np.abs(logits - first_logits).max())
+    assert err <= 1e-3 * rng, f"prompt logits err {err:.3e}, range {rng:.3f}"
+    first = int(np.argmax(logits))
+    tokens = [first] + ctx.decode_greedy(first, r["n_prompt"], r["n_steps"] - 1).tolist()
+    assert tokens == ref_tokens, (tokens, ref_tokens, margin)
+    step_logits = ctx.ForwardToken(tokens[-1], r["n_prompt"] + r["n_steps"] - 1)
+    srng = float(last_logits.max() - last_logits.min())
+    serr = float(np.abs(step_logits - last_logits).max())
+    assert serr <= 1e-3 * srng, f"step logits err {serr:.3e}, range {srng:.3f}"
+    ctx.close()
+    model.close()
