@@ -687,8 +687,8 @@ def time_cols_gemm(pkg, torch, launches: int = 10):
 def kernel_sample(pkg, torch):
     """One small launch of every kernel kind of the library, for profiling
     runs (ncu -k regex:... on this mode): quantize / dequantize / pack, the
-    ggml-layout Linears (Q8_0, Q4_0, Q4_1, F32), the packed GEMV and the
-    TMA-staged lm_head GEMV, the standalone ops (RMSNorm, SiLU, SwiGLU, add,
+    ggml-layout Linears (Q8_0, Q4_0, Q4_1, F32), the packed GEMV, the
+    TMA-staged lm_head GEMV and the shared-memory ring GEMV, the standalone ops (RMSNorm, SiLU, SwiGLU, add,
     multiply, softmax, argmax, RoPE, embedding lookup, KV write), decode
     attention over a 2048-position cache and over an odd head shape, one Qwen2-0.5B-architecture decode step (embed,
     QKV / O / gate-up / down GEMVs, short-cache attention, lm_head), a
@@ -710,6 +710,10 @@ def kernel_sample(pkg, torch):
         fn[qt](xs, blocks, (4864, 896))
     pkg.CudaLinear(np.random.default_rng(0).standard_normal(896).astype(np.float32),
                    np.random.default_rng(1).standard_normal((4864, 896)).astype(np.float32))
+    # the shared-memory ring GEMV: a tall Q4_0 weight (65600 x 2048, 75 MB)
+    blocks, xs = S.gemv_case(65600, 2048, 5, pkg.Q40)
+    pkg.gemv_packed(pkg.Q40, torch.from_numpy(xs).cuda(),
+                    pkg.pack_weight(pkg.Q40, torch.from_numpy(blocks).cuda(), 65600, 2048), 65600)
     # the standalone ops of the drop-in boundary
     v = torch.randn(4864, device="cuda")
     w = torch.randn(4864, device="cuda")

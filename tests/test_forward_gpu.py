@@ -138,6 +138,40 @@ def test_greedy_decode_matches_oracle(pkg, orc, mini, cuda, qt):
     assert got.tolist() == ref_tokens
 
 
+def test_long_cache_head_dim_128_matches_oracle(pkg, orc, S, cuda):
+    """Decode attention over a cache longer than 128 positions at the Qwen2-7B
+    head shape (head_dim 128, 7 query heads per KV head; the split kernel with
+    its cache rows requested into L2 before the dependency wait, and the
+    last-CTA merge of the splits): a two-layer Q4_0 model with that head shape
+    (dim 896, 7 / 1 heads), a 200-id prompt through ForwardBatch, then 16
+    greedy steps.  Prompt logits within 1e-3 x logit range of the oracle and
+    greedy tokens equal to the oracle's."""
+    cfg = dict(S.QWEN2_7B, name="qwen2-7b-heads", vocab=2048, dim=896, hidden=1216, n_layers=2,
+               n_heads=7, n_kv_heads=1)
+    w = S.make_model(cfg, S.Q40, 31)
+    prompt = S.prompt_tokens(cfg["vocab"], 200, 4).tolist()
+    n_steps = 16
+    om = orc.OracleModel(w, 224)
+    for i, t in enumerate(prompt):
+        lg = om.forward_token(t, i)
+    first = lg.copy()
+    tok, ref_tokens = orc.argmax(lg), []
+    for i in range(n_steps):
+        ref_tokens.append(tok)
+        lg = om.forward_token(tok, len(prompt) + i)
+        tok = orc.argmax(lg)
+    model = pkg.Model.from_synth(w, max_seq_len=224)
+    ctx = pkg.Context(model)
+    logits = ctx.ForwardBatch(prompt, 0)
+    rng = float(first.max() - first.min())
+    assert float(np.abs(logits - first).max()) <= 1e-3 * rng
+    got = [int(np.argmax(logits))] + ctx.decode_greedy(int(np.argmax(logits)), len(prompt),
+                                                       n_steps - 1).tolist()
+    assert got == ref_tokens
+    ctx.close()
+    model.close()
+
+
 def test_qwen2_0_5b_q8_0_greedy_64_matches_reference(pkg, S, cuda):
     """Full-size Qwen2-0.5B-architecture Q8_0 (configuration 1): 32 random prompt
     ids, 64 greedy steps; tokens must equal the reference's, and the whole
