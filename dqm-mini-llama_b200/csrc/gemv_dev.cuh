@@ -170,10 +170,61 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, float c, float s
   }
 }
 
+// Epilogue operands of one row group fetched ahead of the arithmetic: the
+// bias and the RoPE (cos, sin) of the QKV rows do not depend on the previous
+// kernel (the position is advanced only between steps), so they are loaded
+// before the dependency wait; the residual is loaded right after it, beside
+// the staging of x, instead of after the dot products.  Lane r holds what
+// the epilogue's writer of row r (kEpiStore) or of pair r (kEpiQkv) needs.
+struct EpiPre {
+  int grp = -1;  // row group these belong to (-1: none)
+  float b0 = 0.0f, b1 = 0.0f, res = 0.0f;
+  float2 cs = make_float2(1.0f, 0.0f);
+};
+
+// Position of a QKV pair's rotation in the RoPE table, and whether it rotates.
+__device__ __forceinline__ bool qkv_pair_rope(const GemvArgs& a, int pp, int* i) {
+  const int half = a.head_dim / 2;
+  const int q_pairs = a.n_heads * half, kv_pairs = a.n_kv_heads * half;
+  const int seg_pair = pp < q_pairs ? pp : (pp < q_pairs + kv_pairs ? pp - q_pairs : pp - q_pairs - kv_pairs);
+  *i = seg_pair % half;
+  return pp < q_pairs + kv_pairs;
+}
+
+template <int RPW>
+__device__ __forceinline__ void epi_prefetch_const(const GemvArgs& a, int grp, int lane, int pos,
+                                                   EpiPre& e) {
+  if (a.epi == kEpiStore) {
+    const int row = grp * RPW + lane;
+    if (lane < RPW && row < a.n_rows && a.bias) e.b0 = __ldg(a.bias + row);
+    e.grp = grp;
+  } else if (a.epi == kEpiQkv) {
+    const int pp = (grp * RPW) / 2 + lane;
+    if (lane < RPW / 2 && 2 * pp + 1 < a.n_rows) {
+      if (a.bias) {
+        e.b0 = __ldg(a.bias + 2 * pp);
+        e.b1 = __ldg(a.bias + 2 * pp + 1);
+      }
+      int i = 0;
+      if (qkv_pair_rope(a, pp, &i)) e.cs = __ldg(a.rope_cs + (size_t)pos * (a.head_dim / 2) + i);
+    }
+    e.grp = grp;
+  }
+}
+
+template <int RPW>
+__device__ __forceinline__ void epi_prefetch_res(const GemvArgs& a, int lane, EpiPre& e) {
+  if (a.epi == kEpiStore && a.residual && e.grp >= 0) {
+    const int row = e.grp * RPW + lane;
+    if (lane < RPW && row < a.n_rows) e.res = __ldcg(a.residual + row);
+  }
+}
+
 template <int RPW, bool PEER>
 __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
                                          const float (&acc)[RPW], int pos,
-                                         unsigned long long& best) {
+                                         unsigned long long& best, const EpiPre* pre = nullptr) {
+  const bool have = pre && pre->grp == grp;
   if constexpr (PEER) {
     // row-parallel partial sum (kEpiPeer): to slot [parity][own rank] of every
     // rank.  A separate instantiation, so the other kernels' code is untouched.
@@ -196,8 +247,8 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
       const int row = grp * RPW + r;
       if (lane == r && row < a.n_rows) {
         float v = acc[r];
-        if (a.bias) v = __fadd_rn(v, a.bias[row]);
-        if (a.residual) v = __fadd_rn(__ldcg(a.residual + row), v);
+        if (a.bias) v = __fadd_rn(v, have ? pre->b0 : a.bias[row]);
+        if (a.residual) v = __fadd_rn(have ? pre->res : __ldcg(a.residual + row), v);
         a.y[row] = v;
       }
     }
@@ -232,8 +283,8 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
       if (lane == p && 2 * pp + 1 < a.n_rows) {
         float x0 = acc[2 * p], x1 = acc[2 * p + 1];
         if (a.bias) {
-          x0 = __fadd_rn(x0, a.bias[2 * pp]);
-          x1 = __fadd_rn(x1, a.bias[2 * pp + 1]);
+          x0 = __fadd_rn(x0, have ? pre->b0 : a.bias[2 * pp]);
+          x1 = __fadd_rn(x1, have ? pre->b1 : a.bias[2 * pp + 1]);
         }
         int seg_pair, nh;
         float* dst;
@@ -262,7 +313,7 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int grp, int lane,
           o1 = o0 + 1;
         }
         if (rotate) {
-          const float2 cs = a.rope_cs[(size_t)pos * half + i];
+          const float2 cs = have ? pre->cs : a.rope_cs[(size_t)pos * half + i];
           rope_pair(x0, x1, cs.x, cs.y, a.neox);
         }
         dst[o0] = x0;
@@ -423,9 +474,10 @@ struct GemvPhase {
   static constexpr int GT = GW * 32;       // threads per row group
   static constexpr int GPC = kWarps / GW;  // row groups per CTA
   Geo g;
-  int total, gt;
+  int total, gt, pos;
   Tile<QT, RPW, CPL> ta, tb;
   bool norm_pref;
+  EpiPre pre;
 
   // nws: shared memory for the RMSNorm weight (kp floats, after x's).
   __device__ __forceinline__ void prefetch(const GemvArgs& a, int cta, int n_ctas, float4* nws) {
@@ -445,6 +497,10 @@ struct GemvPhase {
     // resolves (the tile registers exist for the two-stage pipeline anyway)
     if (total > 0) load_step<QT, RPW, CPL, GT>(ta, a, g, 0, gt);
     if (total > 1) load_step<QT, RPW, CPL, GT>(tb, a, g, 1, gt);
+    // the position is advanced only between steps: stable across this one
+    pos = 0;
+    if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+    if (total > 0) epi_prefetch_const<RPW>(a, g.gw, lane, pos, pre);
     norm_pref = a.norm_w && (a.kp >> 2) <= kNormRegs * kWarps * 32 && ((a.k & 3) == 0) &&
                 ((reinterpret_cast<uintptr_t>(a.norm_w) & 15u) == 0);
     if (norm_pref) {
@@ -474,10 +530,10 @@ __device__ __forceinline__ void gemv_run(GemvPhase<QT, RPW, CPL, GW>& ph, const 
   Tile<QT, RPW, CPL>& ta = ph.ta;
   Tile<QT, RPW, CPL>& tb = ph.tb;
 
+  epi_prefetch_res<RPW>(a, lane, ph.pre);
   stage_x<QT, kWarps, kNormRegs>(a, xs, xs + (a.kp >> 2), ph.norm_pref, red, &bcast);
 
-  int pos = 0;
-  if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+  const int pos = ph.pos;
   unsigned long long best = 0ull;
   float acc[RPW];
 #pragma unroll
@@ -503,9 +559,9 @@ __device__ __forceinline__ void gemv_run(GemvPhase<QT, RPW, CPL, GW>& ph, const 
         acc[r] = t;
       }
       __syncthreads();
-      if (wid == 0) epilogue<RPW, PEER>(a, grp, lane, acc, pos, best);
+      if (wid == 0) epilogue<RPW, PEER>(a, grp, lane, acc, pos, best, &ph.pre);
     } else {
-      epilogue<RPW, PEER>(a, grp, lane, acc, pos, best);
+      epilogue<RPW, PEER>(a, grp, lane, acc, pos, best, &ph.pre);
     }
 #pragma unroll
     for (int r = 0; r < RPW; ++r) acc[r] = 0.0f;
