@@ -72,6 +72,10 @@ struct dqmk_context {
   unsigned char* state = nullptr;
   int* history_dev = nullptr;
   int* pinned = nullptr;  // host staging: [token, pos]
+  // host landing area of a greedy call: [max_seq tokens][3 error flag words],
+  // and the device addresses of those flag words
+  int* pinned_out = nullptr;
+  unsigned int* flag_dev[3] = {nullptr, nullptr, nullptr};
   cudaEvent_t staged = nullptr;  // recorded after the last copy out of `pinned`
   int attn_splits = 1;
   PrefillBufs pf;
@@ -94,6 +98,7 @@ struct dqmk_context {
     if (stream) cudaStreamDestroy(stream);
     for (void* p : allocs) cudaFree(p);
     if (pinned) cudaFreeHost(pinned);
+    if (pinned_out) cudaFreeHost(pinned_out);
   }
 };
 
@@ -809,6 +814,20 @@ int check_device_error(const char* api, dqmk_context* x = nullptr) {
   return device_flags_status(api, flags | tp_flags | ops_flags);
 }
 
+// Synchronise the context's stream with the three error flag words read
+// back behind the work already enqueued (asynchronous copies into pinned
+// memory), then report: only a raised flag costs check_device_error's
+// synchronous read-and-clear.
+int sync_and_check(const char* api, dqmk_context* x) {
+  unsigned int* flags = reinterpret_cast<unsigned int*>(x->pinned_out + x->m->cfg.max_seq_len);
+  for (int i = 0; i < 3; ++i)
+    DQMK_CUDA_RET(api, cudaMemcpyAsync(flags + i, x->flag_dev[i], sizeof(unsigned int),
+                                       cudaMemcpyDeviceToHost, x->stream));
+  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  if (flags[0] | flags[1] | flags[2]) return check_device_error(api, x);
+  return DQMK_OK;
+}
+
 int validate_token(const dqmk_context* x, int token, int pos) {
   const dqmk_model_config& c = x->m->cfg;
   if (token < 0 || token >= c.vocab_size)
@@ -1053,6 +1072,11 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
   x->m = m;
   DQMK_CUDA_RET(api, cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking));
   DQMK_CUDA_RET(api, cudaMallocHost(&x->pinned, 64));
+  DQMK_CUDA_RET(api, cudaMallocHost(&x->pinned_out,
+                                    ((size_t)m->cfg.max_seq_len + 4) * sizeof(int)));
+  DQMK_CUDA_RET(api, device_error_address(&x->flag_dev[0]));
+  DQMK_CUDA_RET(api, tp_error_address(&x->flag_dev[1]));
+  DQMK_CUDA_RET(api, ops_error_address(&x->flag_dev[2]));
   DQMK_CUDA_RET(api, cudaEventCreateWithFlags(&x->staged, cudaEventDisableTiming));
   const dqmk_tp_plan& tp = m->tp;
   const size_t kv = (size_t)c.n_layers * c.max_seq_len * tp.n_kv_heads * c.head_dim;
@@ -1197,8 +1221,7 @@ extern "C" int dqmk_forward_token(dqmk_context* x, int token, int pos, float* lo
   if ((rc = ensure_graph(x))) return rc;
   if ((rc = launch_token(x, token, pos))) return rc;
   if (logits && (rc = copy_logits(x, logits, api))) return rc;
-  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
-  return check_device_error(api, x);
+  return sync_and_check(api, x);
 }
 
 extern "C" int dqmk_forward_batch(dqmk_context* x, const int* tokens, const int* positions, int n,
@@ -1287,13 +1310,17 @@ extern "C" int dqmk_decode_greedy(dqmk_context* x, int token, int pos, int n_ste
   const char* api = "DecodeGreedy";
   int rc = dqmk_decode_enqueue(x, token, pos, n_steps);
   if (rc) return rc;
+  // the tokens come back with the steps into pinned memory, behind the one
+  // synchronisation of sync_and_check
+  int* out = x->pinned_out;
   if (tokens_out) {
-    DQMK_CUDA_RET(api, cudaMemcpyAsync(tokens_out, x->history_dev + pos, n_steps * sizeof(int),
+    DQMK_CUDA_RET(api, cudaMemcpyAsync(out, x->history_dev + pos, n_steps * sizeof(int),
                                        cudaMemcpyDeviceToHost, x->stream));
   }
-  DQMK_CUDA_RET(api, cudaStreamSynchronize(x->stream));
+  rc = sync_and_check(api, x);
+  if (tokens_out) std::memcpy(tokens_out, out, n_steps * sizeof(int));
   x->history.push_back(token);
   for (int i = 0; i + 1 < n_steps && tokens_out; ++i) x->history.push_back(tokens_out[i]);
   x->pos = pos + n_steps - 1;
-  return check_device_error(api, x);
+  return rc;
 }

@@ -1306,6 +1306,10 @@ cudaError_t launch_gemv_tma_skip(const GemvArgs& a, cudaStream_t stream, int ski
   return tma_dispatch(a, stream, false, skip_tile);
 }
 
+cudaError_t device_error_address(unsigned int** p) {
+  return cudaGetSymbolAddress(reinterpret_cast<void**>(p), g_device_error);
+}
+
 cudaError_t read_device_error(unsigned int* flags, bool clear) {
   cudaError_t e = cudaMemcpyFromSymbol(flags, g_device_error, sizeof(unsigned int));
   if (e == cudaSuccess && clear && *flags) {

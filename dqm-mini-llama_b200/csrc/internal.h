@@ -158,6 +158,12 @@ constexpr int kSkipAllTiles = -2;
 cudaError_t launch_gemv_tma_skip(const GemvArgs& a, cudaStream_t stream, int skip_tile);
 // Device error flags set by bounded waits (bit 0: timeout); optionally cleared.
 cudaError_t read_device_error(unsigned int* flags, bool clear);
+// Device addresses (current device) of the three error flag words -- this
+// file's, the peer exchange's and the standalone ops' -- for asynchronous
+// reads of all three with a step's results.
+cudaError_t device_error_address(unsigned int** p);
+cudaError_t tp_error_address(unsigned int** p);
+cudaError_t ops_error_address(unsigned int** p);
 cudaError_t attention_prepare();
 
 // ggml-layout Linear (compatibility entry point), rows >= 1.

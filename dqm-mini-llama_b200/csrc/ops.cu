@@ -336,6 +336,10 @@ cudaError_t launch_greedy_advance(const unsigned long long* slot, int* token, in
   return cudaGetLastError();
 }
 
+cudaError_t ops_error_address(unsigned int** p) {
+  return cudaGetSymbolAddress(reinterpret_cast<void**>(p), g_ops_error);
+}
+
 cudaError_t read_ops_error(unsigned int* flags, bool clear) {
   cudaError_t e = cudaMemcpyFromSymbol(flags, g_ops_error, sizeof(unsigned int));
   if (e == cudaSuccess && clear && *flags) {

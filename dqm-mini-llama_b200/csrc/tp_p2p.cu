@@ -127,6 +127,10 @@ cudaError_t launch_tp_argmax_advance(const PeerSet& ps, const unsigned long long
                 history, cap, vocab);
 }
 
+cudaError_t tp_error_address(unsigned int** p) {
+  return cudaGetSymbolAddress(reinterpret_cast<void**>(p), g_tp_error);
+}
+
 cudaError_t read_tp_error(unsigned int* flags, bool clear) {
   cudaError_t e = cudaMemcpyFromSymbol(flags, g_tp_error, sizeof(unsigned int));
   if (e == cudaSuccess && clear && *flags) {
