@@ -894,6 +894,401 @@ __global__ void __launch_bounds__((WMAX + 1) * 32) gemv_ring_kernel(const GemvAr
   }
 }
 
+// ====================================================== tensor-core GEMV
+// Tall weights with rows of 2048-4096 values (the Qwen2-7B gate/up and
+// lm_head shapes).  The per-block integer dot products that cost the other
+// forms ~90-160 instructions per (row, 32-value block) run on the tensor
+// cores: tcgen05.mma kind::i8 with A = 128 weight rows x one block (Q8_0:
+// the bytes as TMA brought them; Q4_0: nibbles unpacked to bytes by the row
+// threads into tensor memory), B = the three int8 terms of x's block
+// (quantize_x_terms' arithmetic) as N = 16 columns (only 0-2 are read), and
+// one D slot of 16 s32 columns per block in tensor memory.  One thread per
+// weight row then reads its three sums per block (tcgen05.ld) and applies
+// the term scales and the block scale -- the exact int32 sums of
+// block_term_sums, combined in the same order per block, and added over the
+// blocks in order by one thread per row.
+//
+// Warp roles: 0 TMA producer (one lane), 1 MMA issuer (one elected lane;
+// also allocates tensor memory), 2-5 row warps (row 32 * (warp % 4) + lane
+// of the tile: the tensor-memory lane quarter the warp may access).  Raw
+// tiles of 128 rows x 8 blocks (quants, 128-byte swizzle, and their scales)
+// stream through kTcStages shared-memory stages filled before the
+// dependency wait; the row threads build x's terms for all of K once per
+// CTA.  Per chunk of 8 blocks the row threads unpack (Q4_0) and read the
+// scales, the MMA warp issues 8 MMAs into one of two D buffers, and the row
+// threads fold the previous chunk's D.  Every wait is bounded (an abort flag
+// unwinds every role; the producer lets its copies land before exit).
+constexpr int kTcRows = 128;                        // M: weight rows per tile
+constexpr int kTcKB = 8;                            // 32-value blocks per chunk
+constexpr int kTcStages = 4;
+constexpr int kTcRowWarps = 4;
+constexpr int kTcThreads = (2 + kTcRowWarps) * 32;
+constexpr uint32_t kTcDCols = kTcKB * 16;           // D columns of one chunk
+constexpr uint32_t kTcACols = kTcKB * 8;            // A columns of one chunk (Q4_0)
+constexpr uint32_t kTcTmemCols = 512;               // 2 x (128 + 64) used
+
+template <int QT>
+struct TcLayout {
+  static constexpr int QB = QT == DQMK_Q80 ? 32 : 16;          // quant bytes per block
+  static constexpr size_t kQuant = (size_t)kTcRows * kTcKB * QB;  // 32 / 16 KB
+  static constexpr size_t kScale = (size_t)kTcRows * kTcKB * 2;   // 2 KB
+  static constexpr size_t kStage = kQuant + kScale;
+  // B operand: one 1 KB 128-byte-swizzled atom (8 rows x 128 K bytes, only
+  // rows 0-2 meaningful) per 4 blocks, plus one more for the last atom's
+  // rows 8-15; per block the three term scales and 8 x the three term sums
+  __host__ __device__ static size_t b_bytes(int nbk) { return ((size_t)nbk / 4 + 1) * 1024; }
+  __host__ __device__ static size_t c_bytes(int nbk) { return (size_t)nbk * 32; }
+  static size_t smem(int nbk) {
+    return 1024 + kTcStages * kStage + b_bytes(nbk) + c_bytes(nbk);
+  }
+};
+
+// x (k = kp floats, 16-byte aligned), RMS-normalised when norm_w is set,
+// as the three int8 terms of each 32-value block written into the B atoms
+// (term t = row t; block b at K bytes 32 (b % 4).. of atom b / 4, 16-byte
+// chunks XOR-swizzled by the row as TMA's 128-byte swizzle lays them out),
+// and per block the term scales {s0, s1, s2} and, for Q4_0 (nibbles offset
+// by 8), {8 sum(q0), 8 sum(q1), 8 sum(q2)}.  The 128 row threads; eight
+// threads per block, four values each (quantize_x_terms' arithmetic).
+template <int QT>
+__device__ __forceinline__ void tc_build_x(const GemvArgs& a, int t, int nbk, unsigned char* batoms,
+                                           float4* scales, int4* sums8, float* red, float* bcast,
+                                           const float4 (&nw)[8]) {
+  constexpr int NT = kTcRowWarps * 32;
+  const int lane = t & 31, w = t >> 5;
+  const float4* x4 = reinterpret_cast<const float4*>(a.x);
+  const int nf4 = a.kp >> 2;
+  float4 v[8];  // float4 i4 = t + u * NT (8 * NT >= kp / 4: kp <= 4096)
+  float ss = 0.0f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int i4 = t + u * NT;
+    v[u] = i4 < nf4 ? __ldcg(x4 + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
+    ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
+    ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
+    ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
+  }
+  if (a.norm_w) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[w] = ss;
+    named_bar(1, NT);
+    if (t == 0) {
+      float tot = 0.0f;
+      for (int i = 0; i < kTcRowWarps; ++i) tot += red[i];
+      *bcast = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)a.k), a.eps)));
+    }
+    named_bar(1, NT);
+    const float scale = *bcast;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      v[u].x = __fmul_rn(__fmul_rn(v[u].x, scale), nw[u].x);
+      v[u].y = __fmul_rn(__fmul_rn(v[u].y, scale), nw[u].y);
+      v[u].z = __fmul_rn(__fmul_rn(v[u].z, scale), nw[u].z);
+      v[u].w = __fmul_rn(__fmul_rn(v[u].w, scale), nw[u].w);
+    }
+  }
+  const int sub = t & 7;  // which 4 values of the block
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int i4 = t + u * NT;
+    const int b = i4 >> 3;
+    const bool valid = i4 < nf4;  // uniform per group of 8 lanes
+    float m = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    float r[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+    float s = m > 0.0f ? __fdiv_rn(m, 127.0f) : 0.0f;
+    float sc[3];
+    int s8[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const float inv = s > 0.0f ? __frcp_rn(s) : 0.0f;
+      uint32_t packed = 0;
+      int tsum = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int qq = __float2int_rn(__fmul_rn(r[e], inv));
+        qq = qq > 127 ? 127 : (qq < -127 ? -127 : qq);
+        r[e] = __fmaf_rn(-s, (float)qq, r[e]);
+        packed |= ((uint32_t)qq & 0xffu) << (8 * e);
+        tsum += qq;
+      }
+      tsum += __shfl_xor_sync(0xffffffffu, tsum, 1);
+      tsum += __shfl_xor_sync(0xffffffffu, tsum, 2);
+      tsum += __shfl_xor_sync(0xffffffffu, tsum, 4);
+      if (valid) {
+        // row k, K byte 32 (b % 4) + 4 sub of atom b / 4, 128-byte swizzle
+        const int kb = 32 * (b & 3) + 4 * sub;
+        unsigned char* atom = batoms + (size_t)(b >> 2) * 1024;
+        *reinterpret_cast<uint32_t*>(atom + k * 128 + (((kb >> 4) ^ k) << 4) + (kb & 15)) = packed;
+      }
+      sc[k] = s;
+      s8[k] = QT == DQMK_Q40 ? 8 * tsum : 0;
+      s = __fmul_rn(s, 1.0f / 254.0f);
+    }
+    if (valid && sub == 0) {
+      scales[b] = make_float4(sc[0], sc[1], sc[2], 0.0f);
+      sums8[b] = make_int4(s8[0], s8[1], s8[2], 0);
+    }
+  }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap map_q,
+                   const __grid_constant__ CUtensorMap map_d, const GemvArgs a) {
+  using L = TcLayout<QT>;
+  extern __shared__ unsigned char smem_tc[];
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages];
+  __shared__ __align__(8) uint64_t a_full[2], a_empty[2], d_full[2], d_empty[2];
+  __shared__ __align__(8) uint64_t b_ready, mma_done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int s_abort;
+  __shared__ int last_issued[kTcStages];
+  __shared__ float red[kTcRowWarps];
+  __shared__ float bcast;
+  __shared__ unsigned long long best_w[kTcRowWarps];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nbk = a.kp / 32;
+  const int nch = nbk / kTcKB;  // chunks per tile
+  const int n_tiles = (a.n_rows + kTcRows - 1) / kTcRows;
+  const int my_tiles = (int)blockIdx.x < n_tiles
+                           ? (n_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                           : 0;
+  const int total = my_tiles * nch;  // chunks of this CTA
+  unsigned char* stages = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_tc) + 1023) & ~(uintptr_t)1023);
+  unsigned char* batoms = stages + (size_t)kTcStages * L::kStage;
+  float4* scales = reinterpret_cast<float4*>(batoms + L::b_bytes(nbk));
+  int4* sums8 = reinterpret_cast<int4*>(scales + nbk);
+  volatile int* abort = &s_abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      tc::bar_init(&full[s], 1);
+      tc::bar_init(&empty[s], QT == DQMK_Q80 ? kTcRowWarps + 1 : kTcRowWarps);
+      last_issued[s] = -1;
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&a_full[b], kTcRowWarps);
+      tc::bar_init(&a_empty[b], 1);
+      tc::bar_init(&d_full[b], 1);
+      tc::bar_init(&d_empty[b], kTcRowWarps);
+    }
+    tc::bar_init(&b_ready, kTcRowWarps);
+    tc::bar_init(&mma_done, 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tc::tma_prefetch_desc(&map_q);
+    tc::tma_prefetch_desc(&map_d);
+  }
+  if (warp == 1) tc::tmem_alloc(&tmem_slot, kTcTmemCols);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  // weights are read once: evict them from L2 first
+  uint64_t policy = 0;
+  if (warp == 0 && lane == 0) policy = evict_first_policy();
+  // chunk g of this CTA into stage s (producer lane)
+  auto issue = [&](int g, int s) {
+    const int tile = (int)blockIdx.x + (g / nch) * (int)gridDim.x, c = g % nch;
+    unsigned char* st = stages + (size_t)s * L::kStage;
+    tc::bar_expect_tx(&full[s], (uint32_t)L::kStage);
+    if constexpr (QT == DQMK_Q80) {
+      tc::tma_load_2d_hint(st, &map_q, c * 256, tile * kTcRows, &full[s], policy);
+      tc::tma_load_2d_hint(st + 16384, &map_q, c * 256 + 128, tile * kTcRows, &full[s], policy);
+    } else {
+      tc::tma_load_2d_hint(st, &map_q, c * 128, tile * kTcRows, &full[s], policy);
+    }
+    tc::tma_load_2d_hint(st + L::kQuant, &map_d, c * kTcKB, tile * kTcRows, &full[s], policy);
+    last_issued[s] = g;
+  };
+  // before the dependency: the first stages of weights (constant), the
+  // row threads' RMSNorm weights
+  if (warp == 0 && lane == 0)
+    for (int g = 0; g < total && g < kTcStages; ++g) issue(g, g);
+  const int t = 32 * (warp & 3) + lane;  // row of the tile (row warps)
+  float4 nw[8];
+  if (warp >= 2) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i4 = t + u * kTcRowWarps * 32;
+      nw[u] = a.norm_w && i4 < (a.kp >> 2)
+                  ? __ldg(reinterpret_cast<const float4*>(a.norm_w) + i4)
+                  : make_float4(1.f, 1.f, 1.f, 1.f);
+    }
+  }
+  pdl_trigger();
+  pdl_wait();
+
+  unsigned long long best = 0ull;
+  if (warp == 0) {  // ----------------------------------------- TMA producer
+    if (lane == 0) {
+      for (int g = kTcStages; g < total; ++g) {
+        const int s = g % kTcStages;
+        if (!tc::bar_wait(&empty[s], (uint32_t)((g / kTcStages - 1) & 1), abort, &g_device_error,
+                          32))
+          break;
+        issue(g, s);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {  // ------------------------------------ MMA issue
+    const uint32_t idesc = tc::idesc_i8(kTcRows, 16, QT == DQMK_Q80 ? 1 : 0, 1);
+    bool ok = __all_sync(0xffffffffu, tc::bar_wait(&b_ready, 0u, abort, &g_device_error));
+    for (int g = 0; g < total && ok; ++g) {
+      const int s = g % kTcStages, buf = g & 1;
+      bool w = QT == DQMK_Q80
+                   ? tc::bar_wait(&full[s], (uint32_t)((g / kTcStages) & 1), abort, &g_device_error)
+                   : tc::bar_wait(&a_full[buf], (uint32_t)((g >> 1) & 1), abort, &g_device_error);
+      if (w && g >= 2)
+        w = tc::bar_wait(&d_empty[buf], (uint32_t)(((g >> 1) - 1) & 1), abort, &g_device_error);
+      ok = __all_sync(0xffffffffu, w);
+      if (!ok) break;
+      tc::tc_fence_after();
+      if (tc::elect_one()) {
+        const unsigned char* st = stages + (size_t)s * L::kStage;
+#pragma unroll
+        for (int j = 0; j < kTcKB; ++j) {
+          const int b = (g % nch) * kTcKB + j;  // block of the row
+          const uint64_t bdesc = tc::smem_desc(tc::su32(batoms + (size_t)(b >> 2) * 1024)) +
+                                 2u * (uint32_t)(b & 3);
+          const uint32_t d = tmem + (uint32_t)buf * kTcDCols + 16u * (uint32_t)j;
+          if constexpr (QT == DQMK_Q80) {
+            const uint64_t adesc = tc::smem_desc(tc::su32(st + (j >> 2) * 16384)) +
+                                   2u * (uint32_t)(j & 3);
+            tc::mma_i8(d, adesc, bdesc, idesc, 0u);
+          } else {
+            tc::mma_i8_ts(d, tmem + 2u * kTcDCols + (uint32_t)buf * kTcACols + 8u * (uint32_t)j,
+                          bdesc, idesc, 0u);
+          }
+        }
+        tc::mma_commit(&d_full[buf]);
+        tc::mma_commit(QT == DQMK_Q80 ? &empty[s] : &a_empty[buf]);
+      }
+      __syncwarp();
+    }
+    // every MMA issued has finished before tensor memory is freed
+    if (tc::elect_one()) tc::mma_commit(&mma_done);
+    __syncwarp();
+    volatile int never = 0;
+    tc::bar_wait(&mma_done, 0u, &never, &g_device_error);
+  } else {  // ------------------------------------------------- row warps
+    tc_build_x<QT>(a, t, nbk, batoms, scales, sums8, red, &bcast, nw);
+    tc::fence_proxy_async_smem();  // the B atoms are read by the tensor core
+    named_bar(1, kTcRowWarps * 32);
+    if (lane == 0) tc::bar_arrive(&b_ready);
+    int pos = 0;
+    if (a.epi == kEpiQkv) pos = a.pos_dev ? __ldcg(a.pos_dev) : a.pos_arg;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    uint4 dsw[2];  // the 8 block scales (fp16) of the two chunks in flight
+    float acc = 0.0f;
+    for (int g = 0; g <= total; ++g) {
+      if (g < total) {  // ---- chunk g: scales, and the Q4_0 expansion
+        const int s = g % kTcStages, buf = g & 1;
+        if (!tc::bar_wait(&full[s], (uint32_t)((g / kTcStages) & 1), abort, &g_device_error))
+          break;
+        const unsigned char* st = stages + (size_t)s * L::kStage;
+        dsw[buf] = *reinterpret_cast<const uint4*>(st + L::kQuant + (size_t)t * 16);
+        if constexpr (QT == DQMK_Q40) {
+          uint32_t r[64];
+#pragma unroll
+          for (int c = 0; c < kTcKB; ++c) {
+            const uint4 p = *reinterpret_cast<const uint4*>(st + (size_t)t * 128 +
+                                                            (((c ^ (t & 7))) << 4));
+            const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              r[8 * c + k] = pw[k] & 0x0f0f0f0fu;
+              r[8 * c + 4 + k] = (pw[k] >> 4) & 0x0f0f0f0fu;
+            }
+          }
+          if (g >= 2 && !tc::bar_wait(&a_empty[buf], (uint32_t)(((g >> 1) - 1) & 1), abort,
+                                      &g_device_error))
+            break;
+          tc::tc_fence_after();
+          const uint32_t acol = tmem + lane_base + 2u * kTcDCols + (uint32_t)buf * kTcACols;
+          uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+          uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+          tc::tmem_st32(acol, r0);
+          tc::tmem_st32(acol + 32, r1);
+          tc::tmem_wait_st();
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::bar_arrive(&a_full[buf]);
+        }
+        // this thread's reads of stage s are done before the next TMA write
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::bar_arrive(&empty[s]);
+      }
+      if (g >= 1) {  // ---- chunk g - 1: fold its D into the row's sum
+        const int pg = g - 1, pb = pg & 1;
+        if (!tc::bar_wait(&d_full[pb], (uint32_t)((pg >> 1) & 1), abort, &g_device_error)) break;
+        tc::tc_fence_after();
+        uint32_t dv[kTcKB][4];
+#pragma unroll
+        for (int j = 0; j < kTcKB; ++j)
+          tc::tmem_ld4(tmem + lane_base + (uint32_t)pb * kTcDCols + 16u * (uint32_t)j, dv[j]);
+        tc::tmem_wait_ld();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::bar_arrive(&d_empty[pb]);
+        const int cg = pg % nch;
+        const uint32_t hw[4] = {dsw[pb].x, dsw[pb].y, dsw[pb].z, dsw[pb].w};
+#pragma unroll
+        for (int j = 0; j < kTcKB; ++j) {
+          const int b = cg * kTcKB + j;
+          const float4 sc = scales[b];
+          const int4 s8 = sums8[b];
+          float blk = __fmul_rn(sc.x, (float)((int)dv[j][0] - s8.x));
+          blk = __fmaf_rn(sc.y, (float)((int)dv[j][1] - s8.y), blk);
+          blk = __fmaf_rn(sc.z, (float)((int)dv[j][2] - s8.z), blk);
+          const uint16_t h = (uint16_t)((hw[j >> 1] >> (16 * (j & 1))) & 0xffffu);
+          acc = __fmaf_rn(h2f(h), blk, acc);
+        }
+        if (cg == nch - 1) {  // the tile's rows are complete
+          const int row = ((int)blockIdx.x + (pg / nch) * (int)gridDim.x) * kTcRows + t;
+          const float other = __shfl_xor_sync(0xffffffffu, acc, 1);
+          const float pr[2] = {(lane & 1) ? other : acc, (lane & 1) ? acc : other};
+          epilogue<2, false>(a, row >> 1, lane & 1, pr, pos, best);
+          acc = 0.0f;
+        }
+      }
+    }
+    if (a.epi == kEpiLogits) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      if (lane == 0) best_w[warp - 2] = best;
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (*abort && warp == 0 && lane == 0) {
+    // every role has stopped; let each copy still in flight land before the
+    // CTA's shared memory goes away
+    volatile int never = 0;
+    for (int s = 0; s < kTcStages; ++s)
+      if (last_issued[s] >= 0)
+        tc::bar_wait(&full[s], (uint32_t)((last_issued[s] / kTcStages) & 1), &never,
+                     &g_device_error);
+  }
+  if (a.epi == kEpiLogits && threadIdx.x == 64) {
+    unsigned long long bb = 0ull;
+    for (int w = 0; w < kTcRowWarps; ++w) bb = best_w[w] > bb ? best_w[w] : bb;
+    logits_finish(a, bb, gridDim.x, &g_device_error);
+  }
+  if (warp == 1) tc::tmem_free(tmem, kTcTmemCols);
+}
+
 // Test hook behind dqmk_lm_head_block_sums: x (k floats) split into the three
 // int8 terms by quantize_x_terms, then every (row, block) of a packed weight
 // summed against them with block_term_sums -- the integer arithmetic of
@@ -1044,6 +1439,59 @@ cudaError_t tma_dispatch(const GemvArgs& a, cudaStream_t stream, bool pdl, int s
 // resolves, finishes sooner.
 bool tma_eligible(const GemvArgs& a) {
   return a.qtype == DQMK_Q80 && a.kp <= 8192 && a.n_rows >= 32768 && a.epi != kEpiPeer;
+}
+
+// ------------------------------------------------ tensor-core GEMV launches
+template <int QT>
+cudaError_t tc_prepare() {
+  static DeviceOnce once;
+  return once.run([] {
+    return cudaFuncSetAttribute(gemv_tc_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                200 * 1024);
+  });
+}
+
+// Tall Q8_0 weights (16384 rows or more) with rows of 2048-4096 values in
+// whole 256-value chunks, x and the RMSNorm weight 16-byte aligned; not the
+// peer-memory epilogue.  Measured on a B200 at the Qwen2-7B shapes, weights
+// HBM-cold: Q8_0 gate/up 37888 x 3584 0.74 of HBM (TMA form 0.66), and the
+// Qwen2-7B Q8_0 batch-1 decode step 2.60 vs 2.69 ms.  Q4_0 stays with the
+// register / ring forms: the kernel is faster there alone (gate/up 0.42 vs
+// 0.37) but made the Q4_0 decode step slower (3.2-3.4 vs 2.62 ms), where one
+// 24k-register, 108 KB CTA per SM leaves room for a single CTA of the down
+// projection's register GEMV to start early instead of three.
+bool tc_eligible(const GemvArgs& a) {
+  if (a.epi == kEpiPeer || a.qtype != DQMK_Q80) return false;
+  if (a.n_rows < 16384 || a.k != a.kp || a.kp % 256 != 0 || a.kp < 2048 || a.kp > 4096)
+    return false;
+  if (a.qtype == DQMK_Q80 ? TcLayout<DQMK_Q80>::smem(a.kp / 32) > 200 * 1024
+                          : TcLayout<DQMK_Q40>::smem(a.kp / 32) > 200 * 1024)
+    return false;
+  return ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.norm_w) |
+           reinterpret_cast<uintptr_t>(a.qs) | reinterpret_cast<uintptr_t>(a.d)) & 15u) == 0;
+}
+
+template <int QT>
+cudaError_t tc_launch(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  cudaError_t e = tc_prepare<QT>();
+  if (e != cudaSuccess) return e;
+  const int nbk = a.kp / 32;
+  const uint64_t row_bytes = QT == DQMK_Q80 ? (uint64_t)a.kp : (uint64_t)a.kp / 2;
+  CUtensorMap mq, md;
+  if (make_map_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.qs, row_bytes, (uint64_t)a.n_rows,
+                  row_bytes, 128, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B) != DQMK_OK ||
+      make_map_2d(&md, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.d, (uint64_t)nbk, (uint64_t)a.n_rows,
+                  (uint64_t)nbk * 2, kTcKB, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE) != DQMK_OK)
+    return cudaErrorInvalidValue;
+  const int n_tiles = (a.n_rows + kTcRows - 1) / kTcRows;
+  const int grid = std::min(n_tiles, sm_count());
+  return launch(gemv_tc_kernel<QT>, dim3(grid), dim3(kTcThreads), TcLayout<QT>::smem(nbk), stream,
+                pdl, mq, md, a);
+}
+
+cudaError_t tc_dispatch(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  return a.qtype == DQMK_Q80 ? tc_launch<DQMK_Q80>(a, stream, pdl)
+                             : tc_launch<DQMK_Q40>(a, stream, pdl);
 }
 
 // ------------------------------------------------------ ring GEMV launches
@@ -1295,6 +1743,8 @@ cudaError_t gemv_prepare() {
   if (e == cudaSuccess) e = tma_prepare<QT, RPW>();
   DQMK_TMA_VARIANTS(DQMK_TMA_PREP)
 #undef DQMK_TMA_PREP
+  if (e == cudaSuccess) e = tc_prepare<DQMK_Q80>();
+  if (e == cudaSuccess) e = tc_prepare<DQMK_Q40>();
 #define DQMK_RING_PREP(QT, RW, WMAX)                                              \
   if (e == cudaSuccess) e = ring_prepare<QT, RW, WMAX, false>(nullptr, nullptr);
   DQMK_RING_VARIANTS(DQMK_RING_PREP)
@@ -1350,6 +1800,7 @@ int gemv_variant_id(const GemvArgs& a) {
 }
 
 cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl) {
+  if (tc_eligible(a)) return tc_dispatch(a, stream, pdl);
   if (ring_eligible(a)) return ring_dispatch(a, stream, pdl);
   switch (gemv_variant_id(a)) {
 #define DQMK_LAUNCH_CASE(ID, QT, RPW, CPL, GW) \

@@ -138,6 +138,41 @@ def test_greedy_decode_matches_oracle(pkg, orc, mini, cuda, qt):
     assert got.tolist() == ref_tokens
 
 
+@pytest.mark.parametrize("qt", [1, 2], ids=["q8_0", "q4_0"])
+def test_tall_weights_match_oracle(pkg, orc, S, cuda, qt):
+    """A model with tall gate/up (16384 rows x 2048) and lm_head (16384 x
+    2048) weights: in Q8_0 both take the tensor-core GEMV (tcgen05 kind::i8,
+    per-block sums in tensor memory) with its fused RMSNorm + SwiGLU and final
+    RMSNorm + logits + device argmax epilogues; Q4_0 runs the same model on
+    the register GEMV.  One layer; an 8-id prompt through ForwardBatch, then 8 greedy
+    steps.  Prompt logits within 1e-3 x logit range of the oracle, greedy
+    tokens equal to the oracle's."""
+    cfg = dict(S.QWEN2_7B, name="tall", vocab=16384, dim=2048, hidden=8192, n_layers=1,
+               n_heads=16, n_kv_heads=2)
+    w = S.make_model(cfg, qt, 41, quantize_q80=lambda a: pkg.QuantizeToQ80(a).cpu().numpy())
+    prompt = S.prompt_tokens(cfg["vocab"], 8, 6).tolist()
+    n_steps = 8
+    om = orc.OracleModel(w, 32)
+    for i, t in enumerate(prompt):
+        lg = om.forward_token(t, i)
+    first = lg.copy()
+    tok, ref_tokens = orc.argmax(lg), []
+    for i in range(n_steps):
+        ref_tokens.append(tok)
+        lg = om.forward_token(tok, len(prompt) + i)
+        tok = orc.argmax(lg)
+    model = pkg.Model.from_synth(w, max_seq_len=32)
+    ctx = pkg.Context(model)
+    logits = ctx.ForwardBatch(prompt, 0)
+    rng = float(first.max() - first.min())
+    assert float(np.abs(logits - first).max()) <= 1e-3 * rng
+    got = [int(np.argmax(logits))] + ctx.decode_greedy(int(np.argmax(logits)), len(prompt),
+                                                       n_steps - 1).tolist()
+    assert got == ref_tokens
+    ctx.close()
+    model.close()
+
+
 def test_long_cache_head_dim_128_matches_oracle(pkg, orc, S, cuda):
     """Decode attention over a cache longer than 128 positions at the Qwen2-7B
     head shape (head_dim 128, 7 query heads per KV head; the split kernel with

@@ -202,8 +202,9 @@ def test_gemv_sweep_vs_golden_and_oracle(pkg, orc, S, cuda, case):
 @pytest.mark.parametrize("rows,k", [(4100, 3584), (1000, 18944), (520, 2048), (65600, 2048)])
 def test_gemv_wide_rows_vs_oracle(pkg, orc, S, cuda, qt, rows, k):
     """Rows of 2048 values and more (the Qwen2-7B widths; ragged row counts that
-    leave a partial tile; a tall Q4_0 weight and wide Q8_0 rows, which take
-    the shared-memory ring form): packed GEMV with a residual add, and the
+    leave a partial tile; a tall Q8_0 weight, which takes the tensor-core
+    GEMV, and a tall Q4_0 weight and wide Q8_0 rows, which take the
+    shared-memory ring form): packed GEMV with a residual add, and the
     chained form with RMSNorm and SwiGLU over interleaved gate/up rows, both
     against the oracle within the reference's CUDA-test tolerance (1e-3
     absolute or relative)."""
