@@ -684,6 +684,33 @@ def time_cols_gemm(pkg, torch, launches: int = 10):
     return {"shape": "64x3584->37888 Q4_0", "us_per_call": round(e0.elapsed_time(e1) / launches * 1e3, 2)}
 
 
+def gemv_sample(pkg, torch, spec: str):
+    """A few launches of one decode GEMV for profiling: spec "q8_0:37888x3584"
+    (quant type, rows x in_features); random blocks (int8 / nibbles uniform,
+    fp16 scales in [1e-4, 1e-2]), RMSNorm prologue and SwiGLU epilogue as in
+    the decode step's gate/up projection, a 256 MB buffer written between
+    launches so the weight is read from HBM."""
+    name, shape = spec.split(":")
+    qt = {"q8_0": pkg.Q80, "q4_0": pkg.Q40}[name]
+    rows, k = (int(v) for v in shape.split("x"))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    nb = rows * k // 32
+    d = (torch.rand(nb, device="cuda", generator=gen) * 0.01 + 1e-4).half().view(torch.uint8)
+    q = torch.randint(0, 256, (nb, 32 if qt == pkg.Q80 else 16), dtype=torch.uint8, device="cuda",
+                      generator=gen)
+    packed = pkg.pack_weight(qt, torch.cat([d.view(nb, 2), q], dim=1).contiguous(), rows, k)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    x = torch.randn(k, device="cuda")
+    nw = torch.ones(k, device="cuda")
+    y = torch.empty(rows // 2, device="cuda")
+    for _ in range(3):
+        flush.fill_(1)
+        pkg.gemv_packed_chained(qt, x, packed, rows, y, norm=nw, swiglu=True)
+    torch.cuda.synchronize()
+    return {"gemv_sample": spec, "y0": float(y[0])}
+
+
 def kernel_sample(pkg, torch):
     """One small launch of every kernel kind of the library, for profiling
     runs (ncu -k regex:... on this mode): quantize / dequantize / pack, the
@@ -710,6 +737,10 @@ def kernel_sample(pkg, torch):
         fn[qt](xs, blocks, (4864, 896))
     pkg.CudaLinear(np.random.default_rng(0).standard_normal(896).astype(np.float32),
                    np.random.default_rng(1).standard_normal((4864, 896)).astype(np.float32))
+    # the tensor-core GEMV: a tall Q8_0 weight (16384 x 2048, 35 MB)
+    blocks, xs = S.gemv_case(16384, 2048, 5, pkg.Q80)
+    pkg.gemv_packed(pkg.Q80, torch.from_numpy(xs).cuda(),
+                    pkg.pack_weight(pkg.Q80, torch.from_numpy(blocks).cuda(), 16384, 2048), 16384)
     # the shared-memory ring GEMV: a tall Q4_0 weight (65600 x 2048, 75 MB)
     blocks, xs = S.gemv_case(65600, 2048, 5, pkg.Q40)
     pkg.gemv_packed(pkg.Q40, torch.from_numpy(xs).cuda(),
@@ -902,6 +933,8 @@ def main():
                          "(zero: the step reads the same bytes)")
     ap.add_argument("--kernel-sample", action="store_true",
                     help="one small launch of every kernel kind (for profiling)")
+    ap.add_argument("--gemv-sample", default="",
+                    help="a few launches of one decode GEMV (profiling), e.g. q8_0:37888x3584")
     ap.add_argument("--cols-gemm", action="store_true",
                     help="time only the standalone multi-sequence GEMM at the Qwen2-7B gate/up "
                          "shape (64 columns x 37888 x 3584 Q4_0; profiling)")
@@ -930,6 +963,9 @@ def main():
 
     pkg = ge.load_package()
     S = pkg.synth
+    if args.gemv_sample:
+        print(json.dumps(gemv_sample(pkg, torch, args.gemv_sample)))
+        return
     if args.cols_gemm:
         print(json.dumps({"cols_gemm": time_cols_gemm(pkg, torch)}))
         return
