@@ -1457,9 +1457,10 @@ cudaError_t tc_prepare() {
 // HBM-cold: Q8_0 gate/up 37888 x 3584 0.74 of HBM (TMA form 0.66), and the
 // Qwen2-7B Q8_0 batch-1 decode step 2.60 vs 2.69 ms.  Q4_0 stays with the
 // register / ring forms: the kernel is faster there alone (gate/up 0.42 vs
-// 0.37) but made the Q4_0 decode step slower (3.2-3.4 vs 2.62 ms), where one
-// 24k-register, 108 KB CTA per SM leaves room for a single CTA of the down
-// projection's register GEMV to start early instead of three.
+// 0.37) but made the Q4_0 decode step slower (3.2-3.4 vs 2.62 ms), with the
+// down projection on the register or on the ring form alike, under early or
+// late dependent-launch triggers, and with evict-first weight copies; the
+// cause is not found.
 bool tc_eligible(const GemvArgs& a) {
   if (a.epi == kEpiPeer || a.qtype != DQMK_Q80) return false;
   if (a.n_rows < 16384 || a.k != a.kp || a.kp % 256 != 0 || a.kp < 2048 || a.kp > 4096)
