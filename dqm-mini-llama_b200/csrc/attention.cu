@@ -403,10 +403,11 @@ int attention_chunk_cap(int max_seq, int max_splits) {
 
 namespace {
 
-int chunk_cap_for(int max_seq, int max_splits) {
+int chunk_cap_for(int max_seq, int max_splits, int min_chunk) {
   int c = (max_seq + max_splits - 1) / max_splits;
   c = (c + 31) & ~31;
-  return c < kMinChunk ? kMinChunk : c;
+  const int mc = min_chunk > 0 ? min_chunk : kMinChunk;
+  return c < mc ? mc : c;
 }
 
 size_t smem_bytes(int threads, int head_dim, int chunk_cap, int max_splits) {
@@ -418,8 +419,11 @@ size_t smem_bytes(int threads, int head_dim, int chunk_cap, int max_splits) {
 
 }  // namespace
 
-int attention_splits(int max_seq, int n_kv_heads) {
-  int s = (max_seq + kMinChunk - 1) / kMinChunk;
+int decode_min_chunk(int head_dim) { return head_dim >= 128 ? 64 : kMinChunk; }
+
+int attention_splits(int max_seq, int n_kv_heads, int min_chunk) {
+  const int mc = min_chunk > 0 ? min_chunk : kMinChunk;
+  int s = (max_seq + mc - 1) / mc;
   int cap = sm_count() / (n_kv_heads > 0 ? n_kv_heads : 1);
   if (cap < 1) cap = 1;
   if (s > cap) s = cap;
@@ -539,7 +543,7 @@ bool attention_fast_shape(int head_dim, int n_heads, int n_kv_heads) {
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl) {
   if (!attention_fast_shape(a.head_dim, a.n_heads, a.n_kv_heads))
     return launch(attention_any_kernel, dim3(a.n_heads), dim3(kAnyThreads), 0, stream, pdl, a);
-  const int cap = chunk_cap_for(a.max_seq, a.max_splits);
+  const int cap = chunk_cap_for(a.max_seq, a.max_splits, a.min_chunk);
   // the templated kernel reads q and writes out with 16-byte vectors
   const bool aligned =
       ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.out) |

@@ -28,7 +28,8 @@ __device__ __forceinline__ Split split_of(const AttnArgs& a, int split, int pos)
   Split s;
   s.T = pos + 1;
   s.chunk = round_up32((s.T + a.max_splits - 1) / a.max_splits);
-  if (s.chunk < kMinChunk) s.chunk = kMinChunk;
+  const int mc = a.min_chunk > 0 ? a.min_chunk : kMinChunk;
+  if (s.chunk < mc) s.chunk = mc;
   s.n_active = (s.T + s.chunk - 1) / s.chunk;
   s.t0 = split * s.chunk;
   s.n = max(0, min(s.T, s.t0 + s.chunk) - s.t0);

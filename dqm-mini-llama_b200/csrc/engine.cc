@@ -637,6 +637,7 @@ int enqueue_step(dqmk_context* x) {
     at.partials = x->partials;
     at.tickets = x->attn_tickets();
     at.max_splits = x->attn_splits;
+    at.min_chunk = decode_min_chunk(c.head_dim);
     DQMK_CUDA_RET(api, attn_op(at));
 
     GemvArgs o = {};
@@ -1080,7 +1081,7 @@ extern "C" int dqmk_context_create(dqmk_model* m, dqmk_context** out) {
   DQMK_CUDA_RET(api, cudaEventCreateWithFlags(&x->staged, cudaEventDisableTiming));
   const dqmk_tp_plan& tp = m->tp;
   const size_t kv = (size_t)c.n_layers * c.max_seq_len * tp.n_kv_heads * c.head_dim;
-  x->attn_splits = attention_splits(c.max_seq_len, tp.n_kv_heads);
+  x->attn_splits = attention_splits(c.max_seq_len, tp.n_kv_heads, decode_min_chunk(c.head_dim));
   void* p = nullptr;
   int rc;
   const int hd = c.head_dim;

@@ -227,9 +227,14 @@ struct AttnArgs {
   float* partials;       // [n_heads][max_splits][hd + 4]: sums, m, l, pad
   unsigned int* tickets; // [n_kv_heads], zero at rest
   int max_splits;        // gridDim.y
+  int min_chunk;         // shortest split in positions (0: 128)
 };
+// Shortest split of the batch-1 decode attention for a head size: 64
+// positions at head_dim 128 (Qwen2-7B batch-1 step 2.62 -> 2.56 ms against
+// 128), 128 below it (Qwen2-0.5B at 2048 positions: 0.714 vs 0.743 ms at 64).
+int decode_min_chunk(int head_dim);
 // Splits (CTAs per KV head along the sequence) used for a cache of max_seq.
-int attention_splits(int max_seq, int n_kv_heads);
+int attention_splits(int max_seq, int n_kv_heads, int min_chunk = 128);
 size_t attention_partials_floats(int n_heads, int head_dim, int max_splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t stream, bool pdl);
 int attention_chunk_cap(int max_seq, int max_splits);
