@@ -576,7 +576,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool okw = true;
       for (int c = it.c0; c < it.c1; ++c, ++g) {
         const int rs_ = g % kRawStages, as = g % kAStages;
-        if (!wait(&raw_full[rs_], (uint32_t)((g / kRawStages) & 1), &abort_flag)) {
+        // waits are voted: the tcgen05 stores below are warp-wide
+        if (!__all_sync(0xffffffffu,
+                        wait(&raw_full[rs_], (uint32_t)((g / kRawStages) & 1), &abort_flag))) {
           okw = false;
           break;
         }
@@ -606,7 +608,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) tc::bar_arrive(&raw_empty[rs_]);
         if (g >= kAStages &&
-            !wait(&a_empty[as], (uint32_t)((g / kAStages - 1) & 1), &abort_flag)) {
+            !__all_sync(0xffffffffu,
+                        wait(&a_empty[as], (uint32_t)((g / kAStages - 1) & 1), &abort_flag))) {
           okw = false;
           break;
         }
@@ -632,7 +635,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < n_items && !abort_flag; w += gridDim.x, ++tcnt) {
       const Item it = item_of(p, w);
       const int buf = tcnt % kAccBufs;
-      if (!wait(&acc_full[buf], (uint32_t)((tcnt / kAccBufs) & 1), &abort_flag, DQMK_BATCH_EPI_SLEEP)) break;
+      // voted: the tensor-memory loads below are warp-wide
+      if (!__all_sync(0xffffffffu, wait(&acc_full[buf], (uint32_t)((tcnt / kAccBufs) & 1),
+                                        &abort_flag, DQMK_BATCH_EPI_SLEEP)))
+        break;
       tc::tc_fence_after();
       const bool split = p.plan.splits > 1;
       for (int h = 0; h < 2; ++h) {

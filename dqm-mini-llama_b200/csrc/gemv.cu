@@ -1191,7 +1191,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int g = 0; g <= total; ++g) {
       if (g < total) {  // ---- chunk g: scales, and the Q4_0 expansion
         const int s = g % kTcStages, buf = g & 1;
-        if (!tc::bar_wait(&full[s], (uint32_t)((g / kTcStages) & 1), abort, &g_device_error))
+        // waits are voted: the tcgen05 loads and stores below are warp-wide
+        if (!__all_sync(0xffffffffu, tc::bar_wait(&full[s], (uint32_t)((g / kTcStages) & 1),
+                                                  abort, &g_device_error)))
           break;
         const unsigned char* st = stages + (size_t)s * L::kStage;
         dsw[buf] = *reinterpret_cast<const uint4*>(st + L::kQuant + (size_t)t * 16);
@@ -1208,8 +1210,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               r[8 * c + 4 + k] = (pw[k] >> 4) & 0x0f0f0f0fu;
             }
           }
-          if (g >= 2 && !tc::bar_wait(&a_empty[buf], (uint32_t)(((g >> 1) - 1) & 1), abort,
-                                      &g_device_error))
+          if (g >= 2 && !__all_sync(0xffffffffu,
+                                    tc::bar_wait(&a_empty[buf], (uint32_t)(((g >> 1) - 1) & 1),
+                                                 abort, &g_device_error)))
             break;
           tc::tc_fence_after();
           const uint32_t acol = tmem + lane_base + 2u * kTcDCols + (uint32_t)buf * kTcACols;
@@ -1229,7 +1232,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (g >= 1) {  // ---- chunk g - 1: fold its D into the row's sum
         const int pg = g - 1, pb = pg & 1;
-        if (!tc::bar_wait(&d_full[pb], (uint32_t)((pg >> 1) & 1), abort, &g_device_error)) break;
+        if (!__all_sync(0xffffffffu, tc::bar_wait(&d_full[pb], (uint32_t)((pg >> 1) & 1), abort,
+                                                  &g_device_error)))
+          break;
         tc::tc_fence_after();
         uint32_t dv[kTcKB][4];
 #pragma unroll
