@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -812,6 +813,357 @@ constexpr size_t attention_prefill_smem() {
   return sizeof(float) * (2 * 64 * (HD + 4) + 64 * HD + 64 * 65);
 }
 
+// ------------------------------------------- causal attention, tensor cores
+// The same attention at head_dim 64 on tcgen05.  A CTA takes 128 query rows
+// of one head (row r on TMEM lane r) and walks the cache in 64-position tiles
+// with both contractions as kind::f16 MMAs over the two-term operands of the
+// projections: each Q row, each K row (cache position) and each V column (one
+// head dimension within a tile) is scaled by a power of two to a maximum in
+// [2^14, 2^15) and split into fp16 hi + lo, and A_hi B_hi + A_hi B_lo +
+// A_lo B_hi accumulate in fp32 tensor memory (about 2^-22 relative per
+// product, as in the GEMMs):
+//   S' = Q' K'^T   A = Q' (TMEM, once per CTA), B = K' tile [position][hd]
+//   S  = S' 2^(eq + ek) / sqrt(64); masked online softmax in registers, in
+//        the base-2 domain (scores times log2 e, exp2f)
+//   O' = P V'      A = P in [0, 1], two-term (TMEM), B = V'^T tile [hd][position]
+//   O  = O corr + O' 2^ev per tile in registers; O / l at the end.
+// Eight warps: warps w and w + 4 read the same 32 TMEM lanes (rows) and take
+// 32 of the 64 columns each, in the softmax and in the O update, exchanging
+// row maxima through shared memory.  All 256 threads read the next tile's K
+// and V from global memory (L2: the QKV epilogue just wrote them) and write
+// it into the other shared-memory buffer while the score MMAs run.  Every
+// wait is bounded and decided for the whole CTA (__syncthreads_and), so all
+// threads leave the tile loop together.
+namespace atc {
+constexpr int kRows = 128, kKv = 64, kHd = 64, kThreads = 256;
+constexpr int kPlane = kKv * 128;      // 64 rows of 64 fp16, 128-byte swizzle
+constexpr int kBufBytes = 4 * kPlane;  // K hi, K lo, V^T hi, V^T lo
+// two buffers + alignment, padded so that at most two CTAs (2 x 256 TMEM
+// columns) share an SM
+constexpr int kSmem = 80 * 1024;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0, kColO = 64, kColQ = 128, kColP = 192;
+constexpr uint32_t kIdesc = tc::idesc_f16(kRows, 64);
+constexpr float kLog2e = 1.44269504088896341f;
+static_assert(2 * kBufBytes + 1024 <= kSmem && 3 * kSmem > 227 * 1024, "smem plan");
+
+// Byte offset of 16-byte chunk c (8 fp16) of row r in a 128-byte-swizzled
+// K-major operand tile (8-row atoms of 1024 bytes).
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+// ex such that mx 2^-ex lies in [2^14, 2^15) for a normal mx > 0, read from
+// the exponent field (mx in [2^(fe-1), 2^fe)); 0 for mx == 0; clamped to
+// [-120, 120].
+__device__ __forceinline__ int pow2_ex(float mx) {
+  const int fe = ((__float_as_int(mx) >> 23) & 0xff) - 126;
+  return mx > 0.0f ? min(max(fe - 15, -120), 120) : 0;
+}
+// 2^e for |e| <= 126, built from its exponent field.
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+// Two values to packed fp16 pairs hi and lo with x = hi + lo + r,
+// |r| <= 2^-22 |x| (element 0 in the low half).
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const float2 back = __half22float2(h);
+  const __half2 l = __floats2half2_rn(__fsub_rn(x0, back.x), __fsub_rn(x1, back.y));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// One 64-position tile of K and V (positions kt.., zero past `last`) into a
+// shared-memory buffer, with the per-position K scales 2^ek (sk) and the
+// per-dimension V scales 2^ev (sv); 256 threads.
+//   K: thread -> position j = tid / 4; its float4 i holds dimensions
+//      16 i + 4 (tid % 4) .. +3 (a warp reads 8 rows x 64 contiguous bytes
+//      per load), stored as 8-byte halves of the swizzled chunks;
+//   V: thread -> dimensions 4 (tid / 16) .. +3 at positions kt + 4 (tid % 16)
+//      .. +3, stored as 8-byte halves of its four B rows' chunks.
+__device__ __forceinline__ void load_tile(const float* kbase, const float* vbase, size_t rstride,
+                                          int kt, int last, unsigned char* buf, float* sk,
+                                          float* sv, int tid) {
+  {
+    const int j = tid >> 2, p = tid & 3, pos = kt + j;
+    float4 v[4];
+    if (pos <= last) {
+      const float4* src = reinterpret_cast<const float4*>(kbase + (size_t)pos * rstride) + p;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __ldcg(src + 4 * i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const int ex = pow2_ex(mx);
+    const float down = pow2f(-ex);
+    if (p == 0) sk[j] = pow2f(ex);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint2 hi, lo;
+      split2(__fmul_rn(v[i].x, down), __fmul_rn(v[i].y, down), hi.x, lo.x);
+      split2(__fmul_rn(v[i].z, down), __fmul_rn(v[i].w, down), hi.y, lo.y);
+      const uint32_t off = sw128(j, 2 * i + (p >> 1)) + (uint32_t)(p & 1) * 8;
+      *reinterpret_cast<uint2*>(buf + off) = hi;
+      *reinterpret_cast<uint2*>(buf + kPlane + off) = lo;
+    }
+  }
+  {
+    const int dg = tid >> 4, pg = tid & 15;
+    float4 v[4];  // v[i] = V[kt + 4 pg + i][4 dg .. 4 dg + 3]
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pos = kt + 4 * pg + i;
+      v[i] = pos <= last
+                 ? __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)pos * rstride + 4 * dg))
+                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float mx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      mx[0] = fmaxf(mx[0], fabsf(v[i].x));
+      mx[1] = fmaxf(mx[1], fabsf(v[i].y));
+      mx[2] = fmaxf(mx[2], fabsf(v[i].z));
+      mx[3] = fmaxf(mx[3], fabsf(v[i].w));
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1)
+        mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], off));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int ex = pow2_ex(mx[e]);
+      const float down = pow2f(-ex);
+      if (pg == 0) sv[4 * dg + e] = pow2f(ex);
+      float x[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float val = e == 0 ? v[i].x : e == 1 ? v[i].y : e == 2 ? v[i].z : v[i].w;
+        x[i] = __fmul_rn(val, down);
+      }
+      uint2 hi, lo;
+      split2(x[0], x[1], hi.x, lo.x);
+      split2(x[2], x[3], hi.y, lo.y);
+      const uint32_t off = sw128(4 * dg + e, pg >> 1) + (uint32_t)(pg & 1) * 8;
+      *reinterpret_cast<uint2*>(buf + 2 * kPlane + off) = hi;
+      *reinterpret_cast<uint2*>(buf + 3 * kPlane + off) = lo;
+    }
+  }
+}
+}  // namespace atc
+
+__global__ void __launch_bounds__(atc::kThreads) attention_prefill_tc_kernel(PrefillAttn a) {
+  using namespace atc;
+  extern __shared__ unsigned char atc_raw[];
+  __shared__ __align__(8) uint64_t bar_s, bar_o, bar_fin;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+  // scales of three tiles: the one being read, the one being written, and the
+  // one whose last readers may still be in their O update
+  __shared__ float sk[3][kKv], sv[3][kHd];
+  __shared__ float red[2][kRows];  // per row and column half: maxima, then partial sums
+  __shared__ float qf[kRows];      // per row: 2^eq log2(e) / sqrt(64)
+  unsigned char* bufs = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(atc_raw) + 1023) & ~(uintptr_t)1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;  // TMEM lanes 32 quarter.., columns 32 half..
+  const int row = 32 * quarter + lane;
+  const int h = blockIdx.x;
+  const int q0 = (int)(gridDim.y - 1 - blockIdx.y) * kRows;  // longest blocks first
+  const int kvh = h / (a.n_heads / a.n_kv_heads);
+  const size_t rstride = (size_t)a.n_kv_heads * kHd;
+  const float* kbase = a.keys + (size_t)a.layer * a.max_seq * rstride + (size_t)kvh * kHd;
+  const float* vbase = a.values + (size_t)a.layer * a.max_seq * rstride + (size_t)kvh * kHd;
+  const int nq = min(kRows, a.m - q0);
+  const int qmin = a.pos0 + q0;           // the first query's position
+  const int last = qmin + nq - 1;         // the last position any row here sees
+  const int nt = last / kKv + 1;
+  const bool valid = row < nq;
+  const int qpos = qmin + row;
+
+  if (tid == 0) {
+    tc::bar_init(&bar_s, 1);
+    tc::bar_init(&bar_o, 1);
+    tc::bar_init(&bar_fin, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, atc::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+
+  if (half == 0) {  // warps 0-3: this row of Q, scaled and split, into TMEM
+    float4 v[16];
+    const float4* src =
+        reinterpret_cast<const float4*>(a.q + (size_t)(q0 + row) * a.ldq + (size_t)h * kHd);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = valid ? src[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float mx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    const int ex = pow2_ex(mx);
+    const float down = pow2f(-ex);
+    // 2^eq / sqrt(64) is exact; one rounding for log2(e)
+    qf[row] = __fmul_rn(__fmul_rn(pow2f(ex), __fdiv_rn(1.0f, sqrtf((float)kHd))), kLog2e);
+    uint32_t hi[32], lo[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      split2(__fmul_rn(v[i].x, down), __fmul_rn(v[i].y, down), hi[2 * i], lo[2 * i]);
+      split2(__fmul_rn(v[i].z, down), __fmul_rn(v[i].w, down), hi[2 * i + 1], lo[2 * i + 1]);
+    }
+    tc::tmem_st32(tmem + lane_base + kColQ, hi);
+    tc::tmem_st32(tmem + lane_base + kColQ + 32, lo);
+    tc::tmem_wait_st();
+  }
+  load_tile(kbase, vbase, rstride, 0, last, bufs, sk[0], sv[0], tid);
+  tc::fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const float fq = qf[row];
+  float o[32];
+#pragma unroll
+  for (int d = 0; d < 32; ++d) o[d] = 0.0f;
+  float mrow = -INFINITY, lpart = 0.0f;
+  bool ok = true;
+  for (int t = 0; t < nt; ++t) {
+    const int kt = t * kKv, set = t % 3;
+    unsigned char* buf = bufs + (size_t)(t & 1) * kBufBytes;
+    if (warp == 0) {  // S' = Q' K'^T
+      if (tc::elect_one()) {
+        const uint64_t khi = smem_desc(su32(buf)), klo = smem_desc(su32(buf + kPlane));
+#pragma unroll
+        for (int k = 0; k < kHd / 16; ++k) {
+          // a K=16 slice: 8 TMEM columns of A, 32 bytes (+2) of the B descriptor
+          const uint32_t qa = tmem + kColQ + 8u * k;
+          tc::mma_f16_ts(tmem + kColS, qa, khi + 2u * k, atc::kIdesc, k > 0 ? 1u : 0u);
+          tc::mma_f16_ts(tmem + kColS, qa, klo + 2u * k, atc::kIdesc, 1u);
+          tc::mma_f16_ts(tmem + kColS, qa + 32, khi + 2u * k, atc::kIdesc, 1u);
+        }
+        mma_commit(&bar_s);
+      }
+      __syncwarp();
+    }
+    if (t + 1 < nt) {  // the next tile into the other buffer, under the MMAs
+      load_tile(kbase, vbase, rstride, kt + kKv, last, bufs + (size_t)((t + 1) & 1) * kBufBytes,
+                sk[(t + 1) % 3], sv[(t + 1) % 3], tid);
+      tc::fence_proxy_async_smem();
+    }
+    ok = __syncthreads_and(bar_wait(&bar_s, (uint32_t)(t & 1), &abort_flag));
+    if (!ok) break;
+    tc_fence_after();
+
+    uint32_t r[32];
+    tmem_ld32(tmem + lane_base + kColS + 32u * half, r);
+    tmem_wait_ld();
+    const float* skp = sk[set] + 32 * half;
+    float s[32];
+    float tmax = -INFINITY;
+    if (kt + kKv - 1 <= qmin) {  // every position of the tile is visible to every row
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        s[j] = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), fq), skp[j]);
+        tmax = fmaxf(tmax, s[j]);
+      }
+    } else {
+      const int first = kt + 32 * half;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float v = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), fq), skp[j]);
+        s[j] = valid && first + j <= qpos ? v : -INFINITY;
+        tmax = fmaxf(tmax, s[j]);
+      }
+    }
+    red[half][row] = tmax;
+    __syncthreads();
+    const float mnew = fmaxf(mrow, fmaxf(red[0][row], red[1][row]));
+    const float mref = mnew == -INFINITY ? 0.0f : mnew;  // rows with nothing visible yet
+    const float corr = exp2f(mrow - mref);
+    float psum = 0.0f;
+    uint32_t ph[16], pl[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float p0 = exp2f(s[2 * j] - mref), p1 = exp2f(s[2 * j + 1] - mref);
+      psum += p0;
+      psum += p1;
+      split2(p0, p1, ph[j], pl[j]);
+    }
+    lpart = fmaf(lpart, corr, psum);
+    mrow = mnew;
+    // P's columns are free: the previous tile's P V MMAs have completed
+    tc::tmem_st16(tmem + lane_base + kColP + 16u * half, ph);
+    tc::tmem_st16(tmem + lane_base + kColP + 32u + 16u * half, pl);
+    tc::tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) {  // O' = P V'
+      if (tc::elect_one()) {
+        const uint64_t vhi = smem_desc(su32(buf + 2 * kPlane)),
+                       vlo = smem_desc(su32(buf + 3 * kPlane));
+#pragma unroll
+        for (int k = 0; k < kKv / 16; ++k) {
+          const uint32_t pa = tmem + kColP + 8u * k;
+          tc::mma_f16_ts(tmem + kColO, pa, vhi + 2u * k, atc::kIdesc, k > 0 ? 1u : 0u);
+          tc::mma_f16_ts(tmem + kColO, pa, vlo + 2u * k, atc::kIdesc, 1u);
+          tc::mma_f16_ts(tmem + kColO, pa + 32, vhi + 2u * k, atc::kIdesc, 1u);
+        }
+        mma_commit(&bar_o);
+      }
+      __syncwarp();
+    }
+    ok = __syncthreads_and(bar_wait(&bar_o, (uint32_t)(t & 1), &abort_flag));
+    if (!ok) break;
+    tc_fence_after();
+    tmem_ld32(tmem + lane_base + kColO + 32u * half, r);
+    tmem_wait_ld();
+    const float* svp = sv[set] + 32 * half;
+#pragma unroll
+    for (int d = 0; d < 32; ++d)
+      o[d] = __fmaf_rn(o[d], corr, __fmul_rn(__uint_as_float(r[d]), svp[d]));
+    tc_fence_before();
+  }
+
+  // every MMA issued here has completed before TMEM is freed
+  if (warp == 0) {
+    if (tc::elect_one()) mma_commit(&bar_fin);
+    __syncwarp();
+  }
+  {
+    const unsigned long long t0 = tc::now_ns();
+    while (!tc::bar_try(&bar_fin, 0u)) {
+      if (tc::now_ns() - t0 > tc::kWaitNs) {
+        atomicOr(&g_prefill_error, kErrTimeout);
+        break;
+      }
+    }
+  }
+  red[half][row] = lpart;  // the last reads of red came before the tile loop's last barriers
+  __syncthreads();
+  if (ok && valid) {
+    const float l = red[0][row] + red[1][row];
+    float4* out = reinterpret_cast<float4*>(a.out + (size_t)(q0 + row) * a.ldo +
+                                            (size_t)h * kHd + 32 * half);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      out[i] = make_float4(__fdiv_rn(o[4 * i], l), __fdiv_rn(o[4 * i + 1], l),
+                           __fdiv_rn(o[4 * i + 2], l), __fdiv_rn(o[4 * i + 3], l));
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_free(tmem, atc::kTmemCols);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -897,6 +1249,9 @@ cudaError_t prefill_prepare() {
       e = cudaFuncSetAttribute(attention_prefill_kernel<128>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)attention_prefill_smem<128>());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_prefill_tc_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, atc::kSmem);
     return e;
   });
 }
@@ -953,6 +1308,14 @@ cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st) {
   if (a.m <= 0 || a.n_kv_heads <= 0 || a.n_heads % a.n_kv_heads != 0 || a.ldq % 4 != 0 ||
       a.ldo % 4 != 0)
     return cudaErrorInvalidValue;
+  // head_dim 64 on the tensor cores unless DQMK_PREFILL_ATTN=fma asks for the
+  // fp32 kernel (kept for head_dim 128 and for comparisons)
+  const char* mode = std::getenv("DQMK_PREFILL_ATTN");
+  if (a.head_dim == 64 && !(mode && std::string(mode) == "fma")) {
+    const dim3 tgrid(a.n_heads, (a.m + atc::kRows - 1) / atc::kRows);
+    attention_prefill_tc_kernel<<<tgrid, atc::kThreads, atc::kSmem, st>>>(a);
+    return cudaGetLastError();
+  }
   dim3 grid(a.n_heads, (a.m + 63) / 64);
   if (a.head_dim == 64) {
     attention_prefill_kernel<64><<<grid, 256, attention_prefill_smem<64>(), st>>>(a);

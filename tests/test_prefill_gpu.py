@@ -39,6 +39,23 @@ def mini_q8(minis, pkg):
     return minis[pkg.Q80]
 
 
+class env_var:
+    """Sets one environment variable for the duration of a block."""
+
+    def __init__(self, name, value):
+        self.name, self.value = name, value
+
+    def __enter__(self):
+        self.old = os.environ.get(self.name)
+        os.environ[self.name] = self.value
+
+    def __exit__(self, *exc):
+        if self.old is None:
+            del os.environ[self.name]
+        else:
+            os.environ[self.name] = self.old
+
+
 class per_token_path:
     """DQMK_PREFILL=0: ForwardBatch replays the decode graph per token."""
 
@@ -103,10 +120,12 @@ def test_prefill_offset_start_and_second_batch(pkg, mini_q8, orc, cuda):
     check_logits(ctx.ForwardBatch(toks[9:], 9), ref, "three batches")
 
 
-def test_prefill_chunked_long_prompt_matches_reference(pkg, orc, S, mini_q8, cuda):
-    """1100 tokens: two chunks (1024 + 76 rows) of the batched path; last
-    logits against the reference's own ForwardBatch, then 16 greedy steps
-    must equal the reference's."""
+@pytest.mark.parametrize("attn", ["tc", "fma"])
+def test_prefill_chunked_long_prompt_matches_reference(pkg, orc, S, mini_q8, cuda, attn):
+    """1100 tokens: two chunks (1024 + 76 rows, the second starting at cache
+    position 1024) of the batched path under either causal attention kernel;
+    last logits against the reference's own ForwardBatch, then 16 greedy
+    steps must equal the reference's."""
     n, steps = 1100, 16
     prompt = S.prompt_tokens(mini_q8.cfg["vocab"], n, 5).tolist()
     rm = orc.RefModel(mini_q8, n + steps)
@@ -121,8 +140,9 @@ def test_prefill_chunked_long_prompt_matches_reference(pkg, orc, S, mini_q8, cud
         if i + 1 < steps:
             lg = rm.forward_batch([tok], n + i)
     ctx = pkg.Context(pkg.Model.from_synth(mini_q8, max_seq_len=n + steps))
-    got = ctx.ForwardBatch(prompt, 0)
-    print(f"relative logit error {check_logits(got, ref, 'chunked prefill'):.2e}, "
+    with env_var("DQMK_PREFILL_ATTN", attn):
+        got = ctx.ForwardBatch(prompt, 0)
+    print(f"{attn} attention: relative logit error {check_logits(got, ref, 'chunked prefill'):.2e}, "
           f"min margin {min(margins):.2e}")
     first = int(np.argmax(got))
     assert first == ref_tokens[0]
@@ -163,12 +183,15 @@ def test_qwen2_0_5b_q4_0_ctx2048_prefill_then_128_greedy(pkg, S, cuda):
         f", reference min margin {min(g['top1_top2_margin']):.3e}")
 
 
-def test_qwen2_0_5b_q8_0_prefill_602_whole_logits(pkg, S, cuda):
+@pytest.mark.parametrize("attn", ["tc", "fma"])
+def test_qwen2_0_5b_q8_0_prefill_602_whole_logits(pkg, S, cuda, attn):
     """Configuration 4 at full size: the Qwen2-0.5B-architecture Q8_0 model
     (reference-quantized weights) runs one 602-id prompt as a single batched
     ForwardBatch (tensor-core GEMMs, causal attention); its whole 151936-entry
     logit vector must sit within 1e-3 x logit range of the reference's own
-    per-token ForwardBatch loop over the same prompt."""
+    per-token ForwardBatch loop over the same prompt.  Both causal attention
+    kernels: tcgen05 (the default at head_dim 64) and fp32 FMA
+    (DQMK_PREFILL_ATTN=fma)."""
     import hashlib
 
     g = np.load(golden_path("qwen2_0_5b_q8_0_logits.npz"))
@@ -179,9 +202,10 @@ def test_qwen2_0_5b_q8_0_prefill_602_whole_logits(pkg, S, cuda):
     assert sha == bytes(g["prefill602_prompt_sha256"]).decode()
     model = pkg.Model.from_synth(w, max_seq_len=602)
     ctx = pkg.Context(model)
-    logits = ctx.ForwardBatch(prompt.tolist(), 0)
-    err = check_logits(logits, g["prefill602"], "602-token batched prefill")
-    print(f"602-token prefill: relative logit error {err:.2e}")
+    with env_var("DQMK_PREFILL_ATTN", attn):
+        logits = ctx.ForwardBatch(prompt.tolist(), 0)
+    err = check_logits(logits, g["prefill602"], f"602-token batched prefill ({attn} attention)")
+    print(f"602-token prefill, {attn} attention: relative logit error {err:.2e}")
     assert int(np.argmax(logits)) == int(np.argmax(g["prefill602"]))
     ctx.close()
     model.close()
