@@ -41,6 +41,8 @@ struct PrefillBufs {
   uint16_t *hi = nullptr, *lo = nullptr;  // fp16 activation planes [m_max][kp]
   float* rs = nullptr;                    // their row scales [m_max]
   float* partial = nullptr;               // split-K partial sums
+  float* attn_part = nullptr;             // split causal attention: partial rows
+  unsigned int* attn_tickets = nullptr;   // and per-block tickets (left zero by every launch)
   int* tokens = nullptr;
   CUtensorMap a_dim[2], a_qd[2], a_hid[2];  // {hi, lo} per K
 };
@@ -881,6 +883,7 @@ int ensure_prefill(dqmk_context* x) {
   const int kp_max = std::max(kp_dim, std::max(kp_qd, kp_hid));
   const int m_max = std::min(1024, c.max_seq_len);
   size_t part = 0;
+  const bool split_attn = c.head_dim == 64;  // the tensor-core attention's scratch
   for (const Packed* w : {&L0.qkv, &L0.wo, &L0.gate_up, &L0.down})
     part = std::max(part, partial_floats_bound(m_max, w->rows, w->kp));
   void* p = nullptr;
@@ -896,6 +899,8 @@ int ensure_prefill(dqmk_context* x) {
               {(void**)&b.lo, (size_t)m_max * kp_max * 2},
               {(void**)&b.rs, (size_t)m_max * sizeof(float)},
               {(void**)&b.partial, part * sizeof(float)},
+              {(void**)&b.attn_part, split_attn ? prefill_attn_part_floats(m_max, c.n_heads) * sizeof(float) : 0},
+              {(void**)&b.attn_tickets, split_attn ? prefill_attn_tickets(m_max, c.n_heads) * sizeof(unsigned) : 0},
               {(void**)&b.tokens, (size_t)m_max * sizeof(int)}};
   for (auto& e : bufs) {
     if ((rc = dev_alloc(x->allocs, e.bytes, &p, api))) return rc;
@@ -973,6 +978,10 @@ int prefill_chunk(dqmk_context* x, const int* tokens, int pos0, int n, bool want
     a.n_heads = c.n_heads;
     a.n_kv_heads = c.n_kv_heads;
     a.head_dim = c.head_dim;
+    if (c.head_dim == 64) {
+      a.part = b.attn_part;
+      a.tickets = b.attn_tickets;
+    }
     DQMK_CUDA_RET(api, launch_attention_prefill(a, s));
 
     DQMK_CUDA_RET(api, launch_split_rows(b.att, n, qd, L.wo.kp, qd, nullptr, eps, b.hi, b.lo,

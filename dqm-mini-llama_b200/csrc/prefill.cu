@@ -846,6 +846,25 @@ constexpr uint32_t kColS = 0, kColO = 64, kColQ = 128, kColP = 192;
 constexpr uint32_t kIdesc = tc::idesc_f16(kRows, 64);
 constexpr float kLog2e = 1.44269504088896341f;
 static_assert(2 * kBufBytes + 1024 <= kSmem && 3 * kSmem > 227 * 1024, "smem plan");
+// A query block's cache tiles split across at most kMaxSplits CTAs; each
+// writes O (unnormalised), the running maximum m (base 2) and the sum l of
+// its rows: kPartFloats per split.
+constexpr int kMaxSplits = 8;
+constexpr int kPartFloats = kRows * (kHd + 2);
+
+// Tiles per split and number of splits of a query block with nt tiles, for
+// a target of `target` tiles per split (0: no split); every split non-empty.
+__host__ __device__ inline void split_plan(int nt, int target, int* per, int* splits) {
+  if (target <= 0) {
+    *per = nt;
+    *splits = 1;
+    return;
+  }
+  int sp = (nt + target - 1) / target;
+  sp = sp < kMaxSplits ? sp : kMaxSplits;
+  *per = (nt + sp - 1) / sp;
+  *splits = (nt + *per - 1) / *per;
+}
 
 // Byte offset of 16-byte chunk c (8 fp16) of row r in a 128-byte-swizzled
 // K-major operand tile (8-row atoms of 1024 bytes).
@@ -957,7 +976,7 @@ __device__ __forceinline__ void load_tile(const float* kbase, const float* vbase
 }
 }  // namespace atc
 
-__global__ void __launch_bounds__(atc::kThreads) attention_prefill_tc_kernel(PrefillAttn a) {
+__global__ void __launch_bounds__(atc::kThreads, 2) attention_prefill_tc_kernel(PrefillAttn a) {
   using namespace atc;
   extern __shared__ unsigned char atc_raw[];
   __shared__ __align__(8) uint64_t bar_s, bar_o, bar_fin;
@@ -974,7 +993,8 @@ __global__ void __launch_bounds__(atc::kThreads) attention_prefill_tc_kernel(Pre
   const int quarter = warp & 3, half = warp >> 2;  // TMEM lanes 32 quarter.., columns 32 half..
   const int row = 32 * quarter + lane;
   const int h = blockIdx.x;
-  const int q0 = (int)(gridDim.y - 1 - blockIdx.y) * kRows;  // longest blocks first
+  const int qb = (int)(gridDim.y - 1 - blockIdx.y);  // longest blocks first
+  const int q0 = qb * kRows;
   const int kvh = h / (a.n_heads / a.n_kv_heads);
   const size_t rstride = (size_t)a.n_kv_heads * kHd;
   const float* kbase = a.keys + (size_t)a.layer * a.max_seq * rstride + (size_t)kvh * kHd;
@@ -982,7 +1002,12 @@ __global__ void __launch_bounds__(atc::kThreads) attention_prefill_tc_kernel(Pre
   const int nq = min(kRows, a.m - q0);
   const int qmin = a.pos0 + q0;           // the first query's position
   const int last = qmin + nq - 1;         // the last position any row here sees
-  const int nt = last / kKv + 1;
+  int per, splits;
+  split_plan(last / kKv + 1, a.part ? a.tiles_per_split : 0, &per, &splits);
+  const int split = blockIdx.z;
+  if (split >= splits) return;  // this block needs fewer splits than the grid has
+  const int t0 = split * per;
+  const int nt = min(last / kKv + 1 - t0, per);  // tiles t0 .. t0 + nt - 1
   const bool valid = row < nq;
   const int qpos = qmin + row;
 
@@ -1024,7 +1049,7 @@ __global__ void __launch_bounds__(atc::kThreads) attention_prefill_tc_kernel(Pre
     tc::tmem_st32(tmem + lane_base + kColQ + 32, lo);
     tc::tmem_wait_st();
   }
-  load_tile(kbase, vbase, rstride, 0, last, bufs, sk[0], sv[0], tid);
+  load_tile(kbase, vbase, rstride, t0 * kKv, last, bufs, sk[0], sv[0], tid);
   tc::fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -1036,8 +1061,8 @@ __global__ void __launch_bounds__(atc::kThreads) attention_prefill_tc_kernel(Pre
   for (int d = 0; d < 32; ++d) o[d] = 0.0f;
   float mrow = -INFINITY, lpart = 0.0f;
   bool ok = true;
-  for (int t = 0; t < nt; ++t) {
-    const int kt = t * kKv, set = t % 3;
+  for (int t = 0; t < nt; ++t) {  // t: tile index within this split
+    const int kt = (t0 + t) * kKv, set = t % 3;
     unsigned char* buf = bufs + (size_t)(t & 1) * kBufBytes;
     if (warp == 0) {  // S' = Q' K'^T
       if (tc::elect_one()) {
@@ -1149,20 +1174,74 @@ __global__ void __launch_bounds__(atc::kThreads) attention_prefill_tc_kernel(Pre
     }
   }
   red[half][row] = lpart;  // the last reads of red came before the tile loop's last barriers
-  __syncthreads();
-  if (ok && valid) {
-    const float l = red[0][row] + red[1][row];
-    float4* out = reinterpret_cast<float4*>(a.out + (size_t)(q0 + row) * a.ldo +
-                                            (size_t)h * kHd + 32 * half);
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      out[i] = make_float4(__fdiv_rn(o[4 * i], l), __fdiv_rn(o[4 * i + 1], l),
-                           __fdiv_rn(o[4 * i + 2], l), __fdiv_rn(o[4 * i + 3], l));
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tc::tmem_free(tmem, atc::kTmemCols);
+  const float l = red[0][row] + red[1][row];
+  float4* out =
+      reinterpret_cast<float4*>(a.out + (size_t)(q0 + row) * a.ldo + (size_t)h * kHd + 32 * half);
+  if (splits == 1) {
+    if (ok && valid) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        out[i] = make_float4(__fdiv_rn(o[4 * i], l), __fdiv_rn(o[4 * i + 1], l),
+                             __fdiv_rn(o[4 * i + 2], l), __fdiv_rn(o[4 * i + 3], l));
+    }
+    return;
+  }
+
+  // Split block: this split's O, m and l to the scratch; the last of the
+  // block's splits to arrive combines them in split order (deterministic)
+  // and leaves the block's ticket at zero for the next launch.  Every split
+  // takes its ticket, also after a timeout (the error flag is set then).
+  const size_t blk = (size_t)h * gridDim.y + qb;
+  float* part = a.part + blk * kMaxSplits * kPartFloats;
+  if (valid) {
+    float4* po = reinterpret_cast<float4*>(part + (size_t)split * kPartFloats + row * kHd + 32 * half);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) po[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    if (half == 0) {
+      part[(size_t)split * kPartFloats + kRows * kHd + row] = mrow;
+      part[(size_t)split * kPartFloats + kRows * kHd + kRows + row] = l;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ unsigned int ticket;
+  if (tid == 0) ticket = atomicAdd(&a.tickets[blk], 1u);
+  __syncthreads();
+  if (ticket != (unsigned int)(splits - 1)) return;
+  __threadfence();
+  if (tid == 0) a.tickets[blk] = 0u;
+  if (!valid) return;
+  // every valid row sees position 0 in split 0, so mx is finite
+  float mx = -INFINITY;
+  for (int sp = 0; sp < splits; ++sp)
+    mx = fmaxf(mx, __ldcg(part + (size_t)sp * kPartFloats + kRows * kHd + row));
+  float lt = 0.0f;
+  float* acc = o;  // this split's O is in the scratch now
+#pragma unroll
+  for (int d = 0; d < 32; ++d) acc[d] = 0.0f;
+  for (int sp = 0; sp < splits; ++sp) {
+    const float* ps = part + (size_t)sp * kPartFloats;
+    const float w = exp2f(__ldcg(ps + kRows * kHd + row) - mx);  // 0 for a split with nothing visible
+    lt = fmaf(__ldcg(ps + kRows * kHd + kRows + row), w, lt);
+    const float4* po = reinterpret_cast<const float4*>(ps + row * kHd + 32 * half);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = __ldcg(po + i);
+      acc[4 * i] = fmaf(v.x, w, acc[4 * i]);
+      acc[4 * i + 1] = fmaf(v.y, w, acc[4 * i + 1]);
+      acc[4 * i + 2] = fmaf(v.z, w, acc[4 * i + 2]);
+      acc[4 * i + 3] = fmaf(v.w, w, acc[4 * i + 3]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    out[i] = make_float4(__fdiv_rn(acc[4 * i], lt), __fdiv_rn(acc[4 * i + 1], lt),
+                         __fdiv_rn(acc[4 * i + 2], lt), __fdiv_rn(acc[4 * i + 3], lt));
 }
+
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1302,6 +1381,14 @@ cudaError_t launch_embed_rows(int qtype, const uint8_t* qs, const uint16_t* d, i
   return cudaGetLastError();
 }
 
+size_t prefill_attn_part_floats(int m_max, int n_heads) {
+  return (size_t)n_heads * ((m_max + atc::kRows - 1) / atc::kRows) * atc::kMaxSplits *
+         atc::kPartFloats;
+}
+size_t prefill_attn_tickets(int m_max, int n_heads) {
+  return (size_t)n_heads * ((m_max + atc::kRows - 1) / atc::kRows);
+}
+
 cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st) {
   cudaError_t e = prefill_prepare();
   if (e != cudaSuccess) return e;
@@ -1312,8 +1399,30 @@ cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st) {
   // fp32 kernel (kept for head_dim 128 and for comparisons)
   const char* mode = std::getenv("DQMK_PREFILL_ATTN");
   if (a.head_dim == 64 && !(mode && std::string(mode) == "fma")) {
-    const dim3 tgrid(a.n_heads, (a.m + atc::kRows - 1) / atc::kRows);
-    attention_prefill_tc_kernel<<<tgrid, atc::kThreads, atc::kSmem, st>>>(a);
+    // Split the query blocks' cache ranges so that about two CTAs per SM
+    // share the work (at least two 64-position tiles per CTA).
+    const int nqb = (a.m + atc::kRows - 1) / atc::kRows;
+    auto tiles_of = [&](int b) {
+      const int nq = std::min(atc::kRows, a.m - b * atc::kRows);
+      return (a.pos0 + b * atc::kRows + nq - 1) / atc::kKv + 1;
+    };
+    PrefillAttn t = a;
+    int zmax = 1;
+    t.tiles_per_split = 0;
+    if (a.part && a.tickets) {
+      long long total = 0;
+      for (int b = 0; b < nqb; ++b) total += tiles_of(b);
+      total *= a.n_heads;
+      const long long slots = 2ll * sm_count();
+      t.tiles_per_split = (int)std::max(2ll, (total + slots - 1) / slots);
+      for (int b = 0; b < nqb; ++b) {
+        int per, splits;
+        atc::split_plan(tiles_of(b), t.tiles_per_split, &per, &splits);
+        zmax = std::max(zmax, splits);
+      }
+    }
+    const dim3 tgrid(a.n_heads, nqb, zmax);
+    attention_prefill_tc_kernel<<<tgrid, atc::kThreads, atc::kSmem, st>>>(t);
     return cudaGetLastError();
   }
   dim3 grid(a.n_heads, (a.m + 63) / 64);

@@ -48,6 +48,13 @@ struct PrefillAttn {
   float* out;  // [m][ldo]
   int ldo;
   int m, pos0, layer, max_seq, n_heads, n_kv_heads, head_dim;
+  // Tensor-core kernel (head_dim 64): scratch that lets several CTAs share
+  // one 128-row query block's cache range (prefill_attn_part_floats and
+  // prefill_attn_tickets entries for the chunk size; tickets zeroed once,
+  // every launch leaves them zero).  Null: one CTA per query block.
+  float* part;
+  unsigned int* tickets;
+  int tiles_per_split;  // target 64-position tiles per CTA (set by the launcher)
 };
 
 // 2D tiled tensor map over a row-major [outer][inner] array (no multicast
@@ -61,6 +68,9 @@ int make_f16_tile_map(CUtensorMap* map, const void* base, int rows, int kp, int 
 GemmPlan plan_gemm(int m, int n, int kp);
 // Largest splits * m * n over every m <= m_max (floats of the partial buffer).
 size_t partial_floats_bound(int m_max, int n, int kp);
+// Scratch of the split causal attention for chunks of up to m_max rows.
+size_t prefill_attn_part_floats(int m_max, int n_heads);
+size_t prefill_attn_tickets(int m_max, int n_heads);
 cudaError_t prefill_prepare();
 cudaError_t launch_prefill_gemm(const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                                 const CUtensorMap& b_hi, const CUtensorMap& b_lo,
