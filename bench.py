@@ -396,7 +396,8 @@ def time_prefill(pkg, torch, S, w, n_tokens: int = 602):
         "device_ms": round(dev * 1e3, 3),
         "path": "ForwardBatch: per layer RMSNorm + two-term fp16 split, persistent tcgen05 "
                 "kind::f16 GEMM over two-term fp16 weights (QKV, O, gate/up, down; split-K where "
-                "output tiles are few) + causal attention; lm_head GEMV on the last row",
+                "output tiles are few) + causal attention (tcgen05 kind::f16, two-term Q/K/V/P, "
+                "cache range split across CTAs); lm_head GEMV on the last row",
         "linear_batch": {"shape": f"{m}x{k}->{o}", "us_per_call": round(t * 1e6, 2),
                          "useful_tflops": round(useful, 1), "issued_tflops": round(issued, 1),
                          "peak_tflops": peak, "peak_source": src,
