@@ -1399,8 +1399,9 @@ cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st) {
   // fp32 kernel (kept for head_dim 128 and for comparisons)
   const char* mode = std::getenv("DQMK_PREFILL_ATTN");
   if (a.head_dim == 64 && !(mode && std::string(mode) == "fma")) {
-    // Split the query blocks' cache ranges so that about two CTAs per SM
-    // share the work (at least two 64-position tiles per CTA).
+    // Split the query blocks' cache ranges for about one CTA per SM, with at
+    // least four 64-position tiles per CTA: at 602 and 2048 tokens this beat
+    // two CTAs per SM with two tiles each (per-CTA set-up is a large share).
     const int nqb = (a.m + atc::kRows - 1) / atc::kRows;
     auto tiles_of = [&](int b) {
       const int nq = std::min(atc::kRows, a.m - b * atc::kRows);
@@ -1413,8 +1414,8 @@ cudaError_t launch_attention_prefill(const PrefillAttn& a, cudaStream_t st) {
       long long total = 0;
       for (int b = 0; b < nqb; ++b) total += tiles_of(b);
       total *= a.n_heads;
-      const long long slots = 2ll * sm_count();
-      t.tiles_per_split = (int)std::max(2ll, (total + slots - 1) / slots);
+      const long long slots = sm_count();
+      t.tiles_per_split = (int)std::max(4ll, (total + slots - 1) / slots);
       for (int b = 0; b < nqb; ++b) {
         int per, splits;
         atc::split_plan(tiles_of(b), t.tiles_per_split, &per, &splits);
